@@ -1,0 +1,348 @@
+"""Benchmark of the sm_100a attention path (one JSON line on rank 0).
+
+Default workload: BASELINE config 3 -- batched ragged GQA decode, Llama-3-8B
+attention shape (32 q / 8 kv heads, head_dim 128, 32 layers), 64 sequences
+with seeded context lengths in [1024, 8192], fp16 KV cache.  One step = one
+decode step of attention: 32 per-layer launches over all sequences, as the
+engine calls it layer by layer.  Sharded by sequence over N GPUs (no
+collective in the data path); value = total tokens/s of the whole job.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+    torchrun --nproc-per-node N bench.py --gpus N ...
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+
+
+def log(*a):
+    print(*a, file=sys.stderr, flush=True)
+
+
+def load_peaks() -> tuple[dict, str]:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        return json.loads(p.read_text()), "measured"
+    return dict(PEAKS_FALLBACK), "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi sampling of SM clocks / throttle reasons during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.lines: list[str] = []
+        self.thread = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except (FileNotFoundError, OSError):
+            self.proc = None
+            return
+        self.thread = threading.Thread(target=self._read, daemon=True)
+        self.thread.start()
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"], "samples": 0}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        if self.thread:
+            self.thread.join(timeout=2)
+        sm, smax, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [x.strip() for x in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                smax.append(float(parts[2]))
+            except ValueError:
+                continue
+            for name, val in zip(names, parts[5:9]):
+                if val.lower().startswith("active"):
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(smax) if smax else None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# --------------------------------------------------------------- CPU side
+
+class CpuReference:
+    """The reference's CPU attention for the workload: oracle/_ref (the
+    reference's matvec.c/platform.c under the restated engine.c:1074-1096
+    loop, OpenMP over query heads), or the port if _ref is absent.  The
+    sample is one layer of every sequence (same seeded bytes as the GPU
+    arm); a full step is that layer's time x the number of layers."""
+
+    def __init__(self, cfg, seqs: list, layer: int = 0):
+        sys.path.insert(0, str(ROOT / "tests"))
+        import oracle
+
+        self.oracle = oracle
+        self.kind = "reference" if oracle.has_ref() else "port"
+        self.lib = oracle.load("ref" if self.kind == "reference" else "port")
+        self.cores = int(self.lib.orc_max_threads())
+        self.cfg, self.seqs = cfg, seqs
+        self.fx = [oracle.decode_fixture(cfg, layer, s, lib=self.lib) for s in seqs]
+
+    def time_layer(self) -> float:
+        c = self.cfg
+        t0 = time.perf_counter()
+        for f in self.fx:
+            self.oracle.attn_decode(f["q"], f["k"], f["v"], f["pos"], c.n_heads, c.n_kv_heads, c.head_dim,
+                                    c.kv_dim, lib=self.lib)
+        return time.perf_counter() - t0
+
+    def rate(self, budget_s: float) -> dict:
+        times = []
+        while not times or (sum(times) < budget_s and len(times) < 8):
+            times.append(self.time_layer())
+        step_s = statistics.median(times) * self.cfg.layers
+        return {"value": round(len(self.seqs) / step_s, 4), "unit": "tok/s", "cores": self.cores,
+                "kind": self.kind,
+                "sample": f"layer 0 of {len(self.seqs)} seqs ({sum(self.fx[i]['pos'] + 1 for i in range(len(self.fx)))}"
+                          f" keys), timed {len(times)}x ({sum(times):.1f} s), x{self.cfg.layers} layers per step",
+                "step_s": step_s}
+
+
+# --------------------------------------------------------------- GPU side
+
+def run_ours(args) -> None:
+    import torch
+    import torch.distributed as dist
+
+    from yllm_b200 import attn, dist as ydist, fixtures
+    from yllm_b200.configs import CFG3 as cfg
+
+    rank, world, local = ydist.init("nccl" if args.gpus > 1 else "gloo")
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    ctx_all = cfg.ctx()
+    shards = ydist.shard_by_length(ctx_all, world)
+    seqs = shards[rank]
+    log(f"[rank {rank}] {len(seqs)} seqs, {sum(ctx_all[s] for s in seqs)} keys/layer")
+
+    d = fixtures.decode_inputs(cfg, seqs=seqs, device=dev)
+    torch.cuda.synchronize()
+    plan = attn.DecodePlan.build([c - 1 for c in d.ctx], cfg.n_heads, cfg.n_kv_heads, cfg.head_dim, cfg.kv_dim,
+                                 device=dev)
+    items = [attn.make_items([(d.q[l, i], d.out[l, i], d.k_ptr(l, i), d.v_ptr(l, i), None, d.ctx[i] - 1)
+                              for i in range(len(seqs))], device=dev) for l in range(cfg.layers)]
+    stream = torch.cuda.current_stream()
+
+    def step():
+        for l in range(cfg.layers):
+            plan.run(items[l], stream)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    # ---- device-resident timing ----
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    barrier()
+    torch.cuda.synchronize()
+    clocks = ClockSampler(local)
+    clocks.start()
+    time.sleep(0.3)
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+          for _ in range(args.steps * cfg.layers)]
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    t0.record(stream)
+    k = 0
+    for _ in range(args.steps):
+        for l in range(cfg.layers):
+            ev[k][0].record(stream)
+            plan.run(items[l], stream)
+            ev[k][1].record(stream)
+            k += 1
+    t1.record(stream)
+    torch.cuda.synchronize()
+    clk = clocks.stop()
+    barrier()
+    elapsed_ms = t0.elapsed_time(t1)
+    launch_ms = sum(a.elapsed_time(b) for a, b in ev) / len(ev)
+    t = torch.tensor([elapsed_ms], device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    elapsed_ms = float(t.item())
+    ms_per_step = elapsed_ms / args.steps
+    value = cfg.n_seqs / (ms_per_step / 1e3)
+
+    # ---- end to end: pinned host q in, host out back, every step ----
+    n_q = d.q.numel()
+    q_host = torch.empty(n_q, dtype=torch.float32, pin_memory=True)
+    q_host.copy_(d.q.reshape(-1).cpu())
+    out_host = torch.empty(n_q, dtype=torch.float32, pin_memory=True)
+
+    def e2e_step():
+        d.q.view(-1).copy_(q_host, non_blocking=True)
+        step()
+        out_host.copy_(d.out.view(-1), non_blocking=True)
+
+    for _ in range(max(1, args.warmup)):
+        e2e_step()
+    torch.cuda.synchronize()
+    barrier()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        e2e_step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    te = torch.tensor([e0.elapsed_time(e1)], device=dev)
+    if world > 1:
+        dist.all_reduce(te, op=dist.ReduceOp.MAX)
+    e2e_value = cfg.n_seqs / (float(te.item()) / args.steps / 1e3)
+
+    # ---- roofline of the decode kernel (per launch = one layer of this rank's seqs) ----
+    bytes_per_launch = sum(d.ctx) * cfg.kv_dim * 2 * 2 + len(seqs) * cfg.n_heads * cfg.head_dim * 4 * 2
+    achieved = bytes_per_launch / (launch_ms / 1e3) / 1e9
+    peaks, peak_src = load_peaks()
+    st = attn.device_status()
+    if st != 0:
+        raise RuntimeError(f"device status {st}: a kernel gave up waiting")
+
+    if rank == 0:
+        cpu = None
+        if not args.no_cpu_baseline and world == 1:
+            cpu = CpuReference(cfg, list(range(cfg.n_seqs))).rate(args.cpu_budget)
+            cpu.pop("step_s", None)
+        line = {
+            "metric": "attn decode tok/s (batched ragged GQA decode, all layers)",
+            "value": round(value, 2),
+            "unit": "tok/s",
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": round(ms_per_step, 4),
+            "higher_is_better": True,
+            "scaling": "strong",
+            "vs_baseline": None,
+            "dtype": "f32 math, fp16 KV",
+            "data": "synthetic (seeded splitmix64 + Box-Muller, N(0,1) fp16 KV cache)",
+            "config": {
+                "workload": cfg.name,
+                "n_heads": cfg.n_heads, "n_kv_heads": cfg.n_kv_heads, "head_dim": cfg.head_dim,
+                "layers": cfg.layers, "n_seqs": cfg.n_seqs, "ctx_range": [cfg.ctx_lo, cfg.ctx_hi],
+                "total_keys_per_layer": sum(ctx_all),
+                "kv_bytes_per_step": cfg.kv_bytes_per_step(),
+                "parallelism": f"sequence-sharded x{world}",
+                "l2": "inputs larger than L2 (KV per GPU >> 126 MB)",
+            },
+            "e2e": {"value": round(e2e_value, 2), "unit": "tok/s",
+                    "h2d_bytes_per_step": int(n_q * 4 * world), "d2h_bytes_per_step": int(n_q * 4 * world)},
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"],
+                         "unit": "GB/s", "frac": round(achieved / peaks["hbm_gbs"], 4),
+                         "traffic": None, "kernel": "k_decode<128,4>", "peak_source": peak_src,
+                         "bytes_per_launch": bytes_per_launch, "launch_ms": round(launch_ms, 5)},
+            "gpu_launches": args.steps * cfg.layers,
+            "clocks": {"sm_mhz": clk["sm_mhz"], "sm_max_mhz": clk["sm_max_mhz"], "reasons": clk["reasons"]},
+        }
+        if cpu is not None:
+            line["cpu_baseline"] = cpu
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def run_reference(args) -> None:
+    """The reference's own CPU attention for the same workload (rank 0 only)."""
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    from yllm_b200.configs import CFG3 as cfg
+
+    ref = CpuReference(cfg, list(range(cfg.n_seqs)))
+    per_step = []
+    t_start = time.perf_counter()
+    for i in range(args.warmup + args.steps):
+        t = ref.time_layer()
+        if i >= args.warmup:
+            per_step.append(t * cfg.layers)
+        if time.perf_counter() - t_start > args.cpu_budget * 6 and len(per_step) >= 1:
+            break   # keep the whole run within a few minutes
+    step_s = statistics.median(per_step)
+    value = cfg.n_seqs / step_s
+    res = {"cores": ref.cores, "kind": ref.kind,
+           "sample": f"layer 0 of all {cfg.n_seqs} seqs per step (x{cfg.layers} layers), "
+                     f"{len(per_step)} timed steps"}
+    line = {
+        "impl": "reference",
+        "metric": "attn decode tok/s (batched ragged GQA decode, all layers)",
+        "value": round(value, 4),
+        "unit": "tok/s",
+        "n_gpus": 0,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(step_s * 1e3, 2),
+        "higher_is_better": True,
+        "scaling": "strong",
+        "vs_baseline": None,
+        "dtype": "f32 math, fp16 KV",
+        "data": "synthetic (seeded splitmix64 + Box-Muller, N(0,1) fp16 KV cache)",
+        "config": {"workload": cfg.name, "n_heads": cfg.n_heads, "n_kv_heads": cfg.n_kv_heads,
+                   "head_dim": cfg.head_dim, "layers": cfg.layers, "n_seqs": cfg.n_seqs,
+                   "ctx_range": [cfg.ctx_lo, cfg.ctx_hi], "parallelism": "host cores (OpenMP over q heads)"},
+        "cpu_baseline": {"value": round(value, 4), "unit": "tok/s", "cores": res["cores"], "kind": res["kind"],
+                         "sample": res["sample"]},
+        "e2e": {"value": round(value, 4), "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-budget", type=float, default=20.0, help="seconds of CPU attention in the baseline")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        log("warmup raised to 3 (timing rule)")
+        args.warmup = 3
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

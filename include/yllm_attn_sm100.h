@@ -1,0 +1,203 @@
+/* yllm_attn_sm100.h -- C ABI of the sm_100a (B200) attention path for the yllm engine.
+ *
+ * Plain pointers and sizes only.  Every q/k/v/out/state pointer is a DEVICE
+ * pointer unless the comment says "host".  Streams are passed as void*
+ * (a cudaStream_t; NULL = the legacy default stream the reference launches on).
+ *
+ * Two families of entry points:
+ *   1. Drop-in replacements for the reference's CUDA launchers, same names and
+ *      signatures as inference/cuda/cuda_kernels.h (void, legacy default
+ *      stream).  A failure is kept in yattn_last_error() instead of silently
+ *      launching nothing.
+ *   2. yattn_* entry points that return 0 / -1 and fill (err, errlen), the
+ *      cuda_k_gemv_f16 convention (inference/cuda/cuda_kernels.cu:53-87), and
+ *      take an explicit stream and caller-owned workspace.
+ *
+ * KV cache layout (engine.c:261, 1066-1067; device_cuda.c:396-398): fp16 bits
+ * (uint16_t), one region per layer, row t of a layer at base + t*kv_dim, the
+ * kv_head slice at + kv_head*head_dim.  q and out are fp32, heads contiguous.
+ * Query head hh reads kv head hh*n_kv_heads/n_heads (engine.c:1079).
+ */
+#ifndef YLLM_ATTN_SM100_H
+#define YLLM_ATTN_SM100_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ------------------------------------------------------------------ status */
+
+/* Library version (major*10000 + minor*100 + patch). */
+int yattn_version(void);
+
+/* Message of the last failure of a void drop-in entry point on this host
+ * thread ("" if none).  Replaces the reference's silent early return
+ * (cuda_kernels.cu:594, 651). */
+const char* yattn_last_error(void);
+
+/* Clears yattn_last_error() for this host thread. */
+void yattn_clear_error(void);
+
+/* Reads (and with clear != 0 resets) the device-side status word of the
+ * current device: 0 = no kernel gave up; otherwise the code of the first
+ * bounded wait that timed out (a kernel that times out returns early instead
+ * of hanging).  Synchronises the legacy default stream. */
+int yattn_device_status(int* status_out, int clear, char* err, size_t errlen);
+
+/* ------------------------------------------------ drop-in replacements
+ * Same names and signatures as the reference's inference/cuda/cuda_kernels.h. */
+
+/* Replaces cuda_k_attn_decode (cuda_kernels.h:55-58; kernel cuda_kernels.cu:543-600).
+ * One query token at position pos attends to keys 0..pos of one layer.
+ * Split-KV over the sequence with a log-sum-exp merge; the split partials live
+ * in a per-device workspace that the first call (or yattn_reserve) allocates. */
+void cuda_k_attn_decode(float* att_out,
+                        const float* q, const uint16_t* kcache, const uint16_t* vcache,
+                        uint32_t pos, uint32_t n_heads, uint32_t n_kv_heads, uint32_t head_dim,
+                        uint32_t kv_dim);
+
+/* Replaces cuda_k_store_kv (cuda_kernels.h:50-51; kernel cuda_kernels.cu:494-507).
+ * Unlike the reference kernel (__float2half_rn, round-to-nearest-even) this
+ * rounds with the engine's own f32_to_f16 (platform.c:340-379: half-up, f32
+ * subnormals to zero), so the device cache bytes equal the CPU engine's. */
+void cuda_k_store_kv(uint16_t* kcache, uint16_t* vcache, const float* k, const float* v,
+                     uint32_t pos, uint32_t kv_dim);
+
+/* Replaces cuda_k_store_kv_batch (cuda_kernels.h:52-53; cuda_kernels.cu:509-528), same rounding. */
+void cuda_k_store_kv_batch(uint16_t* kcache, uint16_t* vcache, const float* k, const float* v,
+                           uint32_t pos_start, uint32_t B, uint32_t kv_dim);
+
+/* ---------------------------------------------- batched / split-KV decode */
+
+/* One decode query: the attention of one sequence at one layer.
+ * k, v: that layer's cache base (row t at k + t*kv_dim).  gate: NULL, or
+ * [n_heads*head_dim] fp32 for the qwen35 output gate out *= sigmoid(gate)
+ * (engine.c:958-960).  Keys 0..pos are attended. */
+typedef struct YattnDecodeItem {
+    const float* q;
+    float* out;
+    const uint16_t* k;
+    const uint16_t* v;
+    const float* gate;
+    uint32_t pos;
+    uint32_t reserved;
+} YattnDecodeItem;
+
+/* One CTA of work: keys [t_begin, t_end) of one (item, kv_head).  Filled by
+ * yattn_decode_plan; opaque to callers apart from its size. */
+typedef struct YattnDecodeWork {
+    uint32_t item;
+    uint16_t kv_head;
+    uint16_t n_splits;
+    uint32_t split;
+    uint32_t t_begin;
+    uint32_t t_end;
+    uint32_t part_base;   /* first partial slot of this (item, kv_head); unused if n_splits == 1 */
+    uint32_t group;       /* merge counter of this (item, kv_head); unused if n_splits == 1 */
+    uint32_t reserved;
+} YattnDecodeWork;
+
+/* Host-side schedule.  pos_host[n_items] are the items' query positions.
+ * split_tokens = 0 picks a split length that gives about target_ctas work
+ * units (target_ctas = 0: 4 per SM of the current device).  Writes up to
+ * work_cap entries to work_host (host memory).  The schedule depends only on
+ * the positions, so one plan serves every layer of a decode step. */
+int yattn_decode_plan(const uint32_t* pos_host, uint32_t n_items, uint32_t n_kv_heads,
+                      uint32_t split_tokens, uint32_t target_ctas,
+                      YattnDecodeWork* work_host, uint32_t work_cap,
+                      uint32_t* n_work, uint32_t* n_parts, uint32_t* n_groups,
+                      char* err, size_t errlen);
+
+/* Workspace bytes for a plan (split partials + merge counters). */
+size_t yattn_decode_workspace_bytes(uint32_t n_parts, uint32_t n_groups,
+                                    uint32_t n_heads, uint32_t n_kv_heads, uint32_t head_dim);
+
+/* Zeroes the merge counters of a new workspace (runs leave them at zero). */
+int yattn_decode_workspace_init(void* workspace, size_t ws_bytes, void* stream,
+                                char* err, size_t errlen);
+
+/* Runs a plan: items_dev[] and work_dev[] are device copies of the items and
+ * of yattn_decode_plan's output.  Supported: head_dim 64/128/256, up to 8
+ * query heads per kv head, kv_dim % 8 == 0, 16-byte aligned k/v bases. */
+int yattn_decode_run(const YattnDecodeItem* items_dev, const YattnDecodeWork* work_dev,
+                     uint32_t n_work, uint32_t n_parts, uint32_t n_groups,
+                     uint32_t n_heads, uint32_t n_kv_heads, uint32_t head_dim, uint32_t kv_dim,
+                     void* workspace, size_t ws_bytes, void* stream, char* err, size_t errlen);
+
+/* Split-KV partials without the final merge (long-context decode sharded over
+ * GPUs).  Keys [t_begin, t_end) of one layer; writes per query head
+ * ml[2*hh] = (m, l) and o[hh*head_dim ..] = unnormalised sum, where
+ * m = max_t(score_t * log2(e)), l = sum_t 2^(score_t*log2(e) - m),
+ * o = sum_t 2^(...) * v_t.  workspace as for yattn_decode_run with the plan
+ * of a single item of t_end - t_begin keys (yattn_decode_partial_workspace_bytes). */
+size_t yattn_decode_partial_workspace_bytes(uint32_t n_tokens, uint32_t n_heads,
+                                            uint32_t n_kv_heads, uint32_t head_dim);
+int yattn_decode_partial(float* ml, float* o, const float* q, const uint16_t* kcache,
+                         const uint16_t* vcache, uint32_t t_begin, uint32_t t_end,
+                         uint32_t n_heads, uint32_t n_kv_heads, uint32_t head_dim, uint32_t kv_dim,
+                         void* workspace, size_t ws_bytes, void* stream, char* err, size_t errlen);
+
+/* Merges n_parts partial sets laid out [n_parts][n_heads] (ml: 2 floats each,
+ * o: head_dim floats each) into out[n_heads*head_dim]; gate as in
+ * YattnDecodeItem.  Parts with l == 0 (empty shards) are skipped. */
+int yattn_merge_partials(float* out, const float* ml, const float* o, uint32_t n_parts,
+                         uint32_t n_heads, uint32_t head_dim, const float* gate,
+                         void* stream, char* err, size_t errlen);
+
+/* Error-returning form of cuda_k_attn_decode with an explicit stream and gate. */
+int yattn_attn_decode(float* att_out, const float* q, const uint16_t* kcache,
+                      const uint16_t* vcache, const float* gate, uint32_t pos,
+                      uint32_t n_heads, uint32_t n_kv_heads, uint32_t head_dim, uint32_t kv_dim,
+                      void* stream, char* err, size_t errlen);
+
+/* Pre-allocates the per-device workspace the drop-in entry points use, so no
+ * allocation happens inside a decode step (the shim's bind-time workspace). */
+int yattn_reserve(size_t bytes, char* err, size_t errlen);
+
+/* Error-returning KV store (engine f32_to_f16 rounding), B rows at pos_start. */
+int yattn_store_kv(uint16_t* kcache, uint16_t* vcache, const float* k, const float* v,
+                   uint32_t pos_start, uint32_t B, uint32_t kv_dim, void* stream,
+                   char* err, size_t errlen);
+
+/* ------------------------------------------------ seeded input generator
+ * Deterministic on every device and bit-identical to the CPU restatement in
+ * the test oracle: splitmix64 (platform.c:411-417) draws, Box-Muller with
+ * IEEE-exact double arithmetic, the engine's f32_to_f16. */
+
+enum { YATTN_GEN_F32 = 0,        /* float out */
+       YATTN_GEN_F16 = 1,        /* uint16 fp16 bits (engine rounding) */
+       YATTN_GEN_F32_F16 = 2,    /* float out, value rounded through fp16 */
+       YATTN_GEN_F32_BF16 = 3 }; /* float out, value truncated to bf16 */
+
+/* n_rows rows of n_heads*head_dim values: value j of row r is the
+ * ((first_row + r)*n_heads*head_dim + j)-th N(0,1) draw of stream `seed`,
+ * times scale; with rope != 0 the qwen half-split rotation at position
+ * pos0 + r (angle (pos0+r)*theta^(-2i/head_dim)) is applied; then converted
+ * per out_kind and stored at dst + r*row_stride elements. */
+int yattn_gen_rows(void* dst, int out_kind, size_t row_stride, size_t n_rows,
+                   uint32_t n_heads, uint32_t head_dim, uint64_t seed, uint64_t first_row,
+                   double scale, int rope, uint32_t pos0, double theta,
+                   void* stream, char* err, size_t errlen);
+
+/* GDN gates: gate[i] = -softplus(z_a), beta[i] = sigmoid(z_b), z the
+ * (first+i)-th draws of streams seed_a / seed_b. */
+int yattn_gen_gdn_gates(float* gate, float* beta, uint64_t seed_a, uint64_t seed_b,
+                        uint64_t first, size_t n, void* stream, char* err, size_t errlen);
+
+/* GDN q/k rows: bf16(N(0,1)) then l2norm_inplace (matvec.c:942-949) per head. */
+int yattn_gen_gdn_qk(float* dst, uint64_t seed, uint64_t first_row, size_t n_rows,
+                     uint32_t n_heads, uint32_t head_dim, float eps,
+                     void* stream, char* err, size_t errlen);
+
+/* FNV-1a 64 over n bytes of device memory, computed in 1 MiB blocks
+ * (a checksum of block checksums; equals the oracle's blockwise hash). */
+int yattn_checksum(const void* data, size_t n, uint64_t* out_host, void* stream,
+                   char* err, size_t errlen);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* YLLM_ATTN_SM100_H */

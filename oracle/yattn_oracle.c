@@ -1,0 +1,650 @@
+/* yattn_oracle.c -- CPU oracle for the sm_100a attention path (TEST INFRASTRUCTURE).
+ *
+ * Only tests/, __graft_entry__.smoke() and bench.py's CPU-baseline leg use this
+ * file, as the checker.  The product (yllm_b200/) never links or calls it.
+ *
+ * Build with the reference's own flags (Makefile:122,165):
+ *   -O2 -std=c99 -mavx2 -mfma -mf16c -fopenmp
+ * In ISO C mode gcc does not contract a*b+c into FMA, exactly as when the
+ * reference itself is built, so the restated loops round like engine.c.
+ *
+ * ORACLE_LINK_REF: the helper functions come from the reference's
+ * inference/core/matvec.c and platform.c (compiled unmodified by
+ * oracle/Makefile into oracle/_ref/); otherwise they are restated below.
+ * The attention loops live inline in engine.c and are restated in both builds.
+ *
+ * Parity anchors (tests/test_oracle.py):
+ *   - f16 conversion, softmax and rope known answers from tests/test_matvec.c:32-55,
+ *     213-239 (copied as numbers into tests/golden/);
+ *   - port build == reference build, bit for bit, on every helper and loop.
+ */
+#include "yattn_oracle.h"
+
+#include <math.h>
+#include <stdlib.h>
+#include <string.h>
+#ifdef _OPENMP
+#include <omp.h>
+#endif
+
+#ifdef ORACLE_LINK_REF
+/* --- helpers from the reference (matvec.h / yllm.h declarations) --- */
+float    f16_to_f32(uint16_t h);
+uint16_t f32_to_f16(float f);
+uint64_t yrng(uint64_t* s);
+void     softmax(float* v, uint32_t n);
+void     rope_inplace(float* v, uint32_t d, uint32_t pos, float theta);
+void     rope_inplace_qwen(float* v, uint32_t d, uint32_t pos, float theta);
+void     rope_inplace_mrope(float* v, uint32_t head_dim, uint32_t n_dims, uint32_t pos, float theta);
+void     l2norm_inplace(float* v, uint32_t n, float eps);
+void     gdn_state_update(float* S, float* out, const float* q, const float* k,
+                          const float* v, const float* gate, const float* beta,
+                          uint32_t num_k_heads, uint32_t hk, uint32_t n_vheads, uint32_t hv);
+void     rmsnorm_gated(float* y, const float* x, const uint8_t* w, const float* z,
+                       uint32_t n, float eps, uint32_t dtype);
+#define REF_DT_F32 1u   /* DT_F32, inference/include/llf.h:15 */
+
+int orc_build_kind(void) { return 1; }
+float    orc_f16_to_f32(uint16_t h) { return f16_to_f32(h); }
+uint16_t orc_f32_to_f16(float f) { return f32_to_f16(f); }
+uint64_t orc_yrng(uint64_t* s) { return yrng(s); }
+void orc_softmax(float* v, uint32_t n) { softmax(v, n); }
+void orc_rope_inplace(float* v, uint32_t d, uint32_t pos, float theta) { rope_inplace(v, d, pos, theta); }
+void orc_rope_inplace_qwen(float* v, uint32_t d, uint32_t pos, float theta) { rope_inplace_qwen(v, d, pos, theta); }
+void orc_rope_inplace_mrope(float* v, uint32_t hd, uint32_t n_dims, uint32_t pos, float theta)
+{ rope_inplace_mrope(v, hd, n_dims, pos, theta); }
+void orc_l2norm_inplace(float* v, uint32_t n, float eps) { l2norm_inplace(v, n, eps); }
+void orc_gdn_state_update(float* S, float* out, const float* q, const float* k,
+                          const float* v, const float* gate, const float* beta,
+                          uint32_t num_k_heads, uint32_t hk, uint32_t n_vheads, uint32_t hv)
+{ gdn_state_update(S, out, q, k, v, gate, beta, num_k_heads, hk, n_vheads, hv); }
+void orc_rmsnorm_gated_f32(float* y, const float* x, const float* w, const float* z, uint32_t n, float eps)
+{ rmsnorm_gated(y, x, (const uint8_t*)w, z, n, eps, REF_DT_F32); }
+
+#else  /* ---------------- restated helpers ("port") ---------------- */
+
+int orc_build_kind(void) { return 0; }
+
+/* platform.c:316-338: exact fp16 -> fp32, subnormals renormalised.  Like the
+ * reference, both zeros (0x0000 and 0x8000) come back as +0.0f. */
+float orc_f16_to_f32(uint16_t h)
+{
+    uint32_t sign = (uint32_t)(h & 0x8000u) << 16;
+    uint32_t ex = (h >> 10) & 0x1fu;
+    uint32_t man = h & 0x3ffu;
+    uint32_t bits;
+    if (ex == 0) {
+        if (man == 0) {
+            bits = 0;
+        } else {
+            int shift = 0;
+            while ((man & 0x400u) == 0) { man <<= 1; shift++; }
+            bits = sign | ((uint32_t)(113 - shift) << 23) | ((man & 0x3ffu) << 13);
+        }
+    } else if (ex == 0x1f) {
+        bits = sign | 0x7f800000u | (man ? 0x7fc000u : 0u);
+    } else {
+        bits = sign | ((ex + 112u) << 23) | (man << 13);
+    }
+    float f;
+    memcpy(&f, &bits, 4);
+    return f;
+}
+
+/* platform.c:340-379: fp32 -> fp16 the engine's way: f32 subnormals flush to
+ * zero, the normal range rounds half-up on the dropped 13 bits (+0x1000),
+ * the fp16-subnormal range rounds half-up at its own shift, overflow -> inf,
+ * NaN keeps a quiet payload bit. */
+uint16_t orc_f32_to_f16(float f)
+{
+    uint32_t x;
+    memcpy(&x, &f, 4);
+    uint32_t sign = (x >> 16) & 0x8000u;
+    uint32_t fexp = (x >> 23) & 0xffu;
+    uint32_t man = x & 0x7fffffu;
+    int e = (int)fexp - 112;   /* rebias 127 -> 15 */
+    if (fexp == 0) return (uint16_t)sign;
+    if (fexp == 0xff) return (uint16_t)(sign | 0x7c00u | (man ? 0x200u : 0u));
+    if (e >= 31) return (uint16_t)(sign | 0x7c00u);
+    if (e <= 0) {
+        if (e < -10) return (uint16_t)sign;
+        uint32_t full = man | 0x800000u;
+        uint32_t sh = (uint32_t)(14 - e);
+        return (uint16_t)(sign | ((full + (1u << (sh - 1))) >> sh));
+    }
+    man += 0x1000u;
+    if (man & 0x800000u) {         /* mantissa carried into the exponent */
+        e += 1;
+        if (e >= 31) return (uint16_t)(sign | 0x7c00u);
+        return (uint16_t)(sign | ((uint32_t)e << 10));
+    }
+    return (uint16_t)(sign | ((uint32_t)e << 10) | (man >> 13));
+}
+
+/* platform.c:411-417: splitmix64. */
+uint64_t orc_yrng(uint64_t* s)
+{
+    uint64_t z = (*s += 0x9e3779b97f4a7c15ull);
+    z = (z ^ (z >> 30)) * 0xbf58476d1ce4e5b9ull;
+    z = (z ^ (z >> 27)) * 0x94d049bb133111ebull;
+    return z ^ (z >> 31);
+}
+
+/* matvec.c:1023-1031: max pass, exp+sum pass, divide pass. */
+void orc_softmax(float* v, uint32_t n)
+{
+    float mx = v[0];
+    uint32_t i;
+    for (i = 1; i < n; i++)
+        if (v[i] > mx) mx = v[i];
+    float sum = 0.0f;
+    for (i = 0; i < n; i++) {
+        v[i] = expf(v[i] - mx);
+        sum += v[i];
+    }
+    for (i = 0; i < n; i++) v[i] /= sum;
+}
+
+/* matvec.c:890-904: LLaMA pairs (2j, 2j+1). */
+void orc_rope_inplace(float* v, uint32_t d, uint32_t pos, float theta)
+{
+    uint32_t j;
+    for (j = 0; j < d / 2; j++) {
+        float fr = powf(theta, -2.0f * (float)j / (float)d);
+        float ang = fr * (float)pos;
+        float c = cosf(ang), s = sinf(ang);
+        float a = v[2 * j], b = v[2 * j + 1];
+        v[2 * j] = a * c - b * s;
+        v[2 * j + 1] = a * s + b * c;
+    }
+}
+
+/* matvec.c:907-921: qwen2 pairs (j, j + d/2). */
+void orc_rope_inplace_qwen(float* v, uint32_t d, uint32_t pos, float theta)
+{
+    uint32_t half = d / 2, j;
+    for (j = 0; j < half; j++) {
+        float fr = powf(theta, -2.0f * (float)j / (float)d);
+        float ang = fr * (float)pos;
+        float c = cosf(ang), s = sinf(ang);
+        float a = v[j], b = v[j + half];
+        v[j] = a * c - b * s;
+        v[j + half] = a * s + b * c;
+    }
+}
+
+/* matvec.c:924-939: qwen35 M-RoPE on the first n_dims dims, pairs (j, j + n_dims/2). */
+void orc_rope_inplace_mrope(float* v, uint32_t hd, uint32_t n_dims, uint32_t pos, float theta)
+{
+    uint32_t half = n_dims / 2, j;
+    (void)hd;
+    for (j = 0; j < half; j++) {
+        float fr = powf(theta, -2.0f * (float)j / (float)n_dims);
+        float ang = fr * (float)pos;
+        float c = cosf(ang), s = sinf(ang);
+        float a = v[j], b = v[j + half];
+        v[j] = a * c - b * s;
+        v[j + half] = a * s + b * c;
+    }
+}
+
+/* matvec.c:942-949: x / max(||x||, eps). */
+void orc_l2norm_inplace(float* v, uint32_t n, float eps)
+{
+    float ss = 0.0f;
+    uint32_t i;
+    for (i = 0; i < n; i++) ss += v[i] * v[i];
+    float scale = 1.0f / fmaxf(sqrtf(ss), eps);
+    for (i = 0; i < n; i++) v[i] *= scale;
+}
+
+/* matvec.c:975-1004: per v-head h (k-head h % num_k_heads), rows j of the
+ * transposed state: decay, delta against k, rank-1 update; then out = S q / sqrt(hv). */
+void orc_gdn_state_update(float* S, float* out, const float* q, const float* k,
+                          const float* v, const float* gate, const float* beta,
+                          uint32_t num_k_heads, uint32_t hk, uint32_t n_vheads, uint32_t hv)
+{
+    const float scale = 1.0f / sqrtf((float)hv);
+    uint32_t h, j, i;
+    for (h = 0; h < n_vheads; h++) {
+        uint32_t kh = h % num_k_heads;
+        const float* qh = q + (size_t)kh * hk;
+        const float* kk = k + (size_t)kh * hk;
+        const float* vh = v + (size_t)h * hv;
+        float* Sh = S + (size_t)h * hk * hv;
+        float* oh = out + (size_t)h * hv;
+        float g = expf(gate[h]);
+        float b = beta[h];
+        for (j = 0; j < hv; j++) {
+            float* row = Sh + (size_t)j * hv;
+            float dot = 0.0f;
+            for (i = 0; i < hk; i++) {
+                row[i] *= g;
+                dot += row[i] * kk[i];
+            }
+            float del = (vh[j] - dot) * b;
+            for (i = 0; i < hk; i++) row[i] += kk[i] * del;
+        }
+        for (j = 0; j < hv; j++) {
+            const float* row = Sh + (size_t)j * hv;
+            float dot = 0.0f;
+            for (i = 0; i < hk; i++) dot += row[i] * qh[i];
+            oh[j] = dot * scale;
+        }
+    }
+}
+
+/* matvec.c:1007-1021 with DT_F32 weights: x * w / sqrt(mean(x^2)+eps) * silu(z). */
+void orc_rmsnorm_gated_f32(float* y, const float* x, const float* w, const float* z, uint32_t n, float eps)
+{
+    float ss = 0.0f;
+    uint32_t i;
+    for (i = 0; i < n; i++) ss += x[i] * x[i];
+    float inv = 1.0f / sqrtf(ss / (float)n + eps);
+    for (i = 0; i < n; i++) {
+        float zg = z[i];
+        y[i] = x[i] * w[i] * inv * (zg / (1.0f + expf(-zg)));
+    }
+}
+#endif /* ORACLE_LINK_REF */
+
+int orc_max_threads(void)
+{
+#ifdef _OPENMP
+    return omp_get_max_threads();
+#else
+    return 1;
+#endif
+}
+
+void orc_f32_to_f16_buf(const float* src, uint16_t* dst, size_t n)
+{
+    size_t i;
+    for (i = 0; i < n; i++) dst[i] = orc_f32_to_f16(src[i]);
+}
+
+void orc_f16_to_f32_buf(const uint16_t* src, float* dst, size_t n)
+{
+    size_t i;
+    for (i = 0; i < n; i++) dst[i] = orc_f16_to_f32(src[i]);
+}
+
+/* ---------------- attention loops (engine.c, operation order kept) ---------------- */
+
+/* One head of the engine's decode/prefill inner body: scores over keys
+ * 0..pos (acc over head_dim, then * inv_d), softmax, then the PV sum.
+ * engine.c:1078-1095 and 541-561 are the same body. */
+static void head_attend(float* out, const float* qh, const uint16_t* kcache, const uint16_t* vcache,
+                        uint32_t pos, uint32_t kv_head, uint32_t hd, uint32_t kv_dim, float* att_h)
+{
+    float inv_d = 1.0f / sqrtf((float)hd);
+    uint32_t s, jj;
+    for (s = 0; s <= pos; s++) {
+        const uint16_t* kh = kcache + (size_t)s * kv_dim + (size_t)kv_head * hd;
+        float acc = 0.0f;
+        for (jj = 0; jj < hd; jj++) acc += qh[jj] * orc_f16_to_f32(kh[jj]);
+        att_h[s] = acc * inv_d;
+    }
+    orc_softmax(att_h, pos + 1);
+    memset(out, 0, (size_t)hd * 4);
+    for (s = 0; s <= pos; s++) {
+        const uint16_t* vh = vcache + (size_t)s * kv_dim + (size_t)kv_head * hd;
+        float a = att_h[s];
+        for (jj = 0; jj < hd; jj++) out[jj] += a * orc_f16_to_f32(vh[jj]);
+    }
+}
+
+void orc_attn_decode(float* att_out, const float* q, const uint16_t* kcache, const uint16_t* vcache,
+                     uint32_t pos, uint32_t n_heads, uint32_t n_kv_heads, uint32_t head_dim,
+                     uint32_t kv_dim)
+{
+    float* att = (float*)malloc((size_t)n_heads * (pos + 1) * sizeof(float));
+    int hh;
+    #pragma omp parallel for schedule(static)
+    for (hh = 0; hh < (int)n_heads; hh++) {
+        uint32_t kv_head = (uint32_t)hh * n_kv_heads / n_heads;
+        head_attend(att_out + (size_t)hh * head_dim, q + (size_t)hh * head_dim, kcache, vcache,
+                    pos, kv_head, head_dim, kv_dim, att + (size_t)hh * (pos + 1));
+    }
+    free(att);
+}
+
+void orc_attn_prefill(float* att_out, const float* q, const uint16_t* kcache, const uint16_t* vcache,
+                      uint32_t pos_start, uint32_t B, uint32_t n_heads, uint32_t n_kv_heads,
+                      uint32_t head_dim, uint32_t kv_dim, uint32_t q_stride)
+{
+    uint32_t maxlen = pos_start + B;
+    int nth = orc_max_threads();
+    float* att = (float*)malloc((size_t)nth * maxlen * sizeof(float));
+    int hh;
+    #pragma omp parallel for schedule(static)
+    for (hh = 0; hh < (int)n_heads; hh++) {
+        int tid = 0;
+#ifdef _OPENMP
+        tid = omp_get_thread_num();
+#endif
+        uint32_t kv_head = (uint32_t)hh * n_kv_heads / n_heads;
+        uint32_t bb;
+        for (bb = 0; bb < B; bb++) {
+            head_attend(att_out + (size_t)bb * q_stride + (size_t)hh * head_dim,
+                        q + (size_t)bb * q_stride + (size_t)hh * head_dim, kcache, vcache,
+                        pos_start + bb, kv_head, head_dim, kv_dim, att + (size_t)tid * maxlen);
+        }
+    }
+    free(att);
+}
+
+/* engine.c:958-960: the gate pass runs after every head's attention. */
+static void sigmoid_gate(float* att_out, const float* gate, size_t n)
+{
+    size_t i;
+    for (i = 0; i < n; i++) att_out[i] *= 1.0f / (1.0f + expf(-gate[i]));
+}
+
+void orc_attn_decode_gated(float* att_out, const float* q, const float* gate,
+                           const uint16_t* kcache, const uint16_t* vcache,
+                           uint32_t pos, uint32_t n_heads, uint32_t n_kv_heads, uint32_t head_dim,
+                           uint32_t kv_dim)
+{
+    orc_attn_decode(att_out, q, kcache, vcache, pos, n_heads, n_kv_heads, head_dim, kv_dim);
+    sigmoid_gate(att_out, gate, (size_t)n_heads * head_dim);
+}
+
+void orc_attn_prefill_gated(float* att_out, const float* q, const float* gate,
+                            const uint16_t* kcache, const uint16_t* vcache,
+                            uint32_t pos_start, uint32_t B, uint32_t n_heads, uint32_t n_kv_heads,
+                            uint32_t head_dim, uint32_t kv_dim, uint32_t q_stride)
+{
+    uint32_t bb;
+    orc_attn_prefill(att_out, q, kcache, vcache, pos_start, B, n_heads, n_kv_heads, head_dim,
+                     kv_dim, q_stride);
+    for (bb = 0; bb < B; bb++)
+        sigmoid_gate(att_out + (size_t)bb * q_stride, gate + (size_t)bb * q_stride,
+                     (size_t)n_heads * head_dim);
+}
+
+void orc_gdn_step(float* S, float* out, const float* q, const float* k, const float* v,
+                  const float* gate, const float* beta, uint32_t num_k_heads, uint32_t hk,
+                  uint32_t n_vheads, uint32_t hv, const float* norm_w, const float* z, float eps)
+{
+    int h;
+    /* One reference call per head (num_k_heads = n_vheads = 1 on offset
+     * pointers) does exactly the arithmetic of the all-heads call. */
+    #pragma omp parallel for schedule(static)
+    for (h = 0; h < (int)n_vheads; h++) {
+        uint32_t kh = (uint32_t)h % num_k_heads;
+        orc_gdn_state_update(S + (size_t)h * hk * hv, out + (size_t)h * hv, q + (size_t)kh * hk,
+                             k + (size_t)kh * hk, v + (size_t)h * hv, gate + h, beta + h, 1, hk, 1, hv);
+        if (norm_w && z)
+            orc_rmsnorm_gated_f32(out + (size_t)h * hv, out + (size_t)h * hv, norm_w,
+                                  z + (size_t)h * hv, hv, eps);
+    }
+}
+
+void orc_gdn_prefill(float* S, float* out, const float* q, const float* k, const float* v,
+                     const float* gate, const float* beta, uint32_t T, uint32_t num_k_heads,
+                     uint32_t hk, uint32_t n_vheads, uint32_t hv,
+                     const float* norm_w, const float* z, float eps)
+{
+    int h;
+    size_t qk_row = (size_t)num_k_heads * hk, v_row = (size_t)n_vheads * hv;
+    #pragma omp parallel for schedule(dynamic, 1)
+    for (h = 0; h < (int)n_vheads; h++) {
+        uint32_t kh = (uint32_t)h % num_k_heads;
+        uint32_t t;
+        for (t = 0; t < T; t++) {
+            float* oh = out + t * v_row + (size_t)h * hv;
+            orc_gdn_state_update(S + (size_t)h * hk * hv, oh, q + t * qk_row + (size_t)kh * hk,
+                                 k + t * qk_row + (size_t)kh * hk, v + t * v_row + (size_t)h * hv,
+                                 gate + (size_t)t * n_vheads + h, beta + (size_t)t * n_vheads + h,
+                                 1, hk, 1, hv);
+            if (norm_w && z)
+                orc_rmsnorm_gated_f32(oh, oh, norm_w, z + t * v_row + (size_t)h * hv, hv, eps);
+        }
+    }
+}
+
+/* ---------------- deterministic seeded inputs ----------------
+ * The GPU generator in yllm_b200/csrc/fixture.cu performs this exact sequence
+ * of IEEE operations.  Literals are the nearest doubles of the named values. */
+
+#define D_SQRT2    1.4142135623730951      /* sqrt(2) */
+#define D_LN2      0.6931471805599453      /* ln 2 */
+#define D_LN2_HI   0.6931471803691238      /* ln 2 to 32 bits */
+#define D_LN2_LO   1.9082149292705877e-10  /* ln 2 - D_LN2_HI */
+#define D_INV_LN2  1.4426950408889634
+#define D_2_PI     0.6366197723675814      /* 2/pi */
+#define D_PIO2_1   1.5707963267341256      /* pi/2 to 33 bits */
+#define D_PIO2_2   6.077100506303966e-11   /* next 33 bits */
+#define D_PIO2_3   2.0222662487959506e-21  /* remainder */
+#define D_2PI      6.283185307179586
+
+/* ln x = e ln2 + 2 atanh((m-1)/(m+1)), m in [sqrt(2)/2, sqrt(2)];
+ * atanh series s + s^3/3 + ... + s^23/23 (|s| <= 0.1716). */
+double orc_det_log(double x)
+{
+    uint64_t b;
+    memcpy(&b, &x, 8);
+    int e = (int)((b >> 52) & 0x7ff) - 1023;
+    b = (b & 0x000fffffffffffffull) | 0x3ff0000000000000ull;
+    double m;
+    memcpy(&m, &b, 8);
+    if (m > D_SQRT2) { m = m * 0.5; e += 1; }
+    double s = (m - 1.0) / (m + 1.0);
+    double s2 = s * s;
+    double p = 0.043478260869565216;           /* 1/23 */
+    p = fma(p, s2, 0.047619047619047616);      /* 1/21 */
+    p = fma(p, s2, 0.05263157894736842);       /* 1/19 */
+    p = fma(p, s2, 0.058823529411764705);      /* 1/17 */
+    p = fma(p, s2, 0.06666666666666667);       /* 1/15 */
+    p = fma(p, s2, 0.07692307692307693);       /* 1/13 */
+    p = fma(p, s2, 0.09090909090909091);       /* 1/11 */
+    p = fma(p, s2, 0.1111111111111111);        /* 1/9 */
+    p = fma(p, s2, 0.14285714285714285);       /* 1/7 */
+    p = fma(p, s2, 0.2);                       /* 1/5 */
+    p = fma(p, s2, 0.3333333333333333);        /* 1/3 */
+    double t = (s * s2) * p;
+    double lm = fma(2.0, t, 2.0 * s);
+    return fma((double)e, D_LN2, lm);
+}
+
+/* e^x = 2^k e^r, k = rint(x/ln2), r by a two-part ln2; Taylor series to r^13. */
+double orc_det_exp(double x)
+{
+    double k = rint(x * D_INV_LN2);
+    double r = fma(-k, D_LN2_HI, x);
+    r = fma(-k, D_LN2_LO, r);
+    double p = 1.6059043836821613e-10;         /* 1/13! */
+    p = fma(p, r, 2.08767569878681e-09);       /* 1/12! */
+    p = fma(p, r, 2.505210838544172e-08);      /* 1/11! */
+    p = fma(p, r, 2.755731922398589e-07);      /* 1/10! */
+    p = fma(p, r, 2.7557319223985893e-06);     /* 1/9! */
+    p = fma(p, r, 2.48015873015873e-05);       /* 1/8! */
+    p = fma(p, r, 0.0001984126984126984);      /* 1/7! */
+    p = fma(p, r, 0.001388888888888889);       /* 1/6! */
+    p = fma(p, r, 0.008333333333333333);       /* 1/5! */
+    p = fma(p, r, 0.041666666666666664);       /* 1/4! */
+    p = fma(p, r, 0.16666666666666666);        /* 1/3! */
+    p = fma(p, r, 0.5);
+    p = fma(p, r, 1.0);
+    p = fma(p, r, 1.0);
+    int64_t ki = (int64_t)k;
+    uint64_t sb = (uint64_t)(ki + 1023) << 52;
+    double sc;
+    memcpy(&sc, &sb, 8);
+    return p * sc;
+}
+
+/* Cody-Waite reduction by pi/2 (three parts), then Taylor series on |r| <= pi/4:
+ * sin to r^17, cos to r^18. */
+void orc_det_sincos(double x, double* s_out, double* c_out)
+{
+    double k = rint(x * D_2_PI);
+    double r = fma(-k, D_PIO2_1, x);
+    r = fma(-k, D_PIO2_2, r);
+    r = fma(-k, D_PIO2_3, r);
+    double r2 = r * r;
+    double ps = 2.8114572543455206e-15;        /* 1/17! */
+    ps = fma(ps, r2, -7.647163731819816e-13);  /* -1/15! */
+    ps = fma(ps, r2, 1.6059043836821613e-10);  /* 1/13! */
+    ps = fma(ps, r2, -2.505210838544172e-08);  /* -1/11! */
+    ps = fma(ps, r2, 2.7557319223985893e-06);  /* 1/9! */
+    ps = fma(ps, r2, -0.0001984126984126984);  /* -1/7! */
+    ps = fma(ps, r2, 0.008333333333333333);    /* 1/5! */
+    ps = fma(ps, r2, -0.16666666666666666);    /* -1/3! */
+    double sn = fma(r * r2, ps, r);
+    double pc = -1.5619206968586225e-16;       /* -1/18! */
+    pc = fma(pc, r2, 4.779477332387385e-14);   /* 1/16! */
+    pc = fma(pc, r2, -1.1470745597729725e-11); /* -1/14! */
+    pc = fma(pc, r2, 2.08767569878681e-09);    /* 1/12! */
+    pc = fma(pc, r2, -2.755731922398589e-07);  /* -1/10! */
+    pc = fma(pc, r2, 2.48015873015873e-05);    /* 1/8! */
+    pc = fma(pc, r2, -0.001388888888888889);   /* -1/6! */
+    pc = fma(pc, r2, 0.041666666666666664);    /* 1/4! */
+    pc = fma(pc, r2, -0.5);
+    double cs = fma(pc, r2, 1.0);
+    int64_t q = ((int64_t)k) & 3;
+    if (q == 0)      { *s_out = sn;  *c_out = cs;  }
+    else if (q == 1) { *s_out = cs;  *c_out = -sn; }
+    else if (q == 2) { *s_out = -sn; *c_out = -cs; }
+    else             { *s_out = -cs; *c_out = sn;  }
+}
+
+/* The k-th (0-based) yrng() output of a stream whose state starts at `seed`
+ * (ysrand maps 0 to the golden-ratio constant, platform.c:405-409). */
+uint64_t orc_stream_draw(uint64_t seed, uint64_t k)
+{
+    if (seed == 0) seed = 0x9e3779b97f4a7c15ull;
+    uint64_t st = seed + k * 0x9e3779b97f4a7c15ull;
+    return orc_yrng(&st);
+}
+
+/* Box-Muller on draw i/2: u1 = (top 24 bits + 1) / 2^24 in (0,1] (the engine's
+ * uniform, engine.c:1649, shifted off zero), u2 = next 24 bits / 2^24;
+ * even i -> r cos(2 pi u2), odd i -> r sin(2 pi u2). */
+double orc_normal_d(uint64_t seed, uint64_t i)
+{
+    uint64_t v = orc_stream_draw(seed, i >> 1);
+    double u1 = (double)((v >> 40) + 1) * 5.9604644775390625e-08;       /* 2^-24 */
+    double u2 = (double)((v >> 16) & 0xffffffull) * 5.9604644775390625e-08;
+    double r = sqrt(-2.0 * orc_det_log(u1));
+    double sn, cs;
+    orc_det_sincos(D_2PI * u2, &sn, &cs);
+    return (i & 1) ? r * sn : r * cs;
+}
+
+void orc_fill_normal(uint64_t seed, uint64_t first, size_t n, double scale, float* out)
+{
+    long long i;
+    #pragma omp parallel for schedule(static)
+    for (i = 0; i < (long long)n; i++)
+        out[i] = (float)(orc_normal_d(seed, first + (uint64_t)i) * scale);
+}
+
+void orc_rope_rows(float* x, size_t n_rows, uint32_t n_heads, uint32_t hd, uint32_t pos0, double theta)
+{
+    double lt = orc_det_log(theta);
+    uint32_t half = hd / 2;
+    long long r;
+    #pragma omp parallel for schedule(static)
+    for (r = 0; r < (long long)n_rows; r++) {
+        double pos = (double)(pos0 + (uint32_t)r);
+        uint32_t h, j;
+        for (j = 0; j < half; j++) {
+            double t = (double)(2 * j) / (double)hd;
+            double fr = orc_det_exp(-(t * lt));
+            double sn, cs;
+            orc_det_sincos(pos * fr, &sn, &cs);
+            for (h = 0; h < n_heads; h++) {
+                float* v = x + (size_t)r * n_heads * hd + (size_t)h * hd;
+                double a = (double)v[j], b = (double)v[j + half];
+                v[j] = (float)fma(a, cs, -(b * sn));
+                v[j + half] = (float)fma(a, sn, b * cs);
+            }
+        }
+    }
+}
+
+void orc_round_f16(const float* x, size_t n, uint16_t* out)
+{
+    long long i;
+    #pragma omp parallel for schedule(static)
+    for (i = 0; i < (long long)n; i++) out[i] = orc_f32_to_f16(x[i]);
+}
+
+void orc_round_f16_inplace(float* x, size_t n)
+{
+    long long i;
+    #pragma omp parallel for schedule(static)
+    for (i = 0; i < (long long)n; i++) x[i] = orc_f16_to_f32(orc_f32_to_f16(x[i]));
+}
+
+void orc_round_bf16_inplace(float* x, size_t n)
+{
+    size_t i;
+    for (i = 0; i < n; i++) {
+        uint32_t b;
+        memcpy(&b, &x[i], 4);
+        b &= 0xffff0000u;
+        memcpy(&x[i], &b, 4);
+    }
+}
+
+/* gate = -softplus(z_a) = -ln(1 + e^z_a), so e^gate is the decay alpha;
+ * beta = 1 / (1 + e^-z_b). */
+void orc_gdn_gates(uint64_t seed_a, uint64_t seed_b, uint64_t first, size_t n, float* gate, float* beta)
+{
+    size_t i;
+    for (i = 0; i < n; i++) {
+        double za = orc_normal_d(seed_a, first + i);
+        double zb = orc_normal_d(seed_b, first + i);
+        gate[i] = (float)(-orc_det_log(1.0 + orc_det_exp(za)));
+        beta[i] = (float)(1.0 / (1.0 + orc_det_exp(-zb)));
+    }
+}
+
+void orc_gdn_qk(uint64_t seed, uint64_t first_row, size_t n_rows, uint32_t n_heads, uint32_t hd,
+                float eps, float* out)
+{
+    size_t row = (size_t)n_heads * hd;
+    orc_fill_normal(seed, first_row * row, n_rows * row, 1.0, out);
+    orc_round_bf16_inplace(out, n_rows * row);
+    size_t i;
+    for (i = 0; i < n_rows * n_heads; i++) orc_l2norm_inplace(out + i * hd, hd, eps);
+}
+
+uint32_t orc_ctx_len(uint64_t seed, uint32_t i, uint32_t lo, uint32_t hi)
+{
+    uint64_t v = orc_stream_draw(seed, i);
+    return lo + (uint32_t)(v % (uint64_t)(hi - lo + 1));
+}
+
+uint64_t orc_fnv1a(const void* p, size_t n)
+{
+    const unsigned char* c = (const unsigned char*)p;
+    uint64_t h = 0xcbf29ce484222325ull;
+    size_t i;
+    for (i = 0; i < n; i++) { h ^= c[i]; h *= 0x100000001b3ull; }
+    return h;
+}
+
+uint64_t orc_checksum64(const void* p, size_t n)
+{
+    const uint64_t* w = (const uint64_t*)p;
+    size_t n_words = n / 8, per = 65536 / 8;
+    size_t n_blocks = (n + 65535) / 65536;
+    uint64_t* hb = (uint64_t*)malloc((n_blocks ? n_blocks : 1) * sizeof(uint64_t));
+    long long b;
+    #pragma omp parallel for schedule(static)
+    for (b = 0; b < (long long)n_blocks; b++) {
+        size_t i0 = (size_t)b * per, i1 = i0 + per < n_words ? i0 + per : n_words, i;
+        uint64_t h = 0xcbf29ce484222325ull;
+        for (i = i0; i < i1; i++) { h ^= w[i]; h *= 0x100000001b3ull; }
+        hb[b] = h;
+    }
+    uint64_t h = 0xcbf29ce484222325ull;
+    size_t j;
+    for (j = 0; j < n_blocks; j++) { h ^= hb[j]; h *= 0x100000001b3ull; }
+    free(hb);
+    return h;
+}

@@ -1,0 +1,127 @@
+"""Host-side checks of the C ABI library that need no GPU."""
+import ctypes as C
+import re
+import subprocess
+from pathlib import Path
+
+import numpy as np
+import pytest
+
+ROOT = Path(__file__).resolve().parent.parent
+HEADER = ROOT / "include" / "yllm_attn_sm100.h"
+
+
+def declared_functions() -> list:
+    text = HEADER.read_text()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    names = re.findall(r"^[A-Za-z_][\w\s\*]*?\b([a-z_][a-z0-9_]*)\s*\(", text, flags=re.M)
+    return sorted(set(n for n in names if n not in ("if", "defined")))
+
+
+def test_library_exports_every_declared_symbol():
+    from yllm_b200 import _lib
+
+    names = declared_functions()
+    assert "cuda_k_attn_decode" in names and "yattn_decode_run" in names
+    out = subprocess.run(["nm", "-D", "--defined-only", str(_lib.LIB_PATH)], capture_output=True, text=True,
+                         check=True).stdout
+    exported = set(line.split()[-1] for line in out.splitlines() if " T " in line)
+    missing = [n for n in names if n not in exported]
+    assert not missing, f"declared but not exported: {missing}"
+    for n in names:
+        assert hasattr(_lib.lib, n)
+
+
+def test_struct_layout_matches_header(tmp_path):
+    from yllm_b200._lib import YattnDecodeItem, YattnDecodeWork
+
+    src = tmp_path / "s.c"
+    src.write_text('#include "yllm_attn_sm100.h"\n#include <stdio.h>\n#include <stddef.h>\n'
+                   'int main(void){printf("%zu %zu %zu %zu\\n", sizeof(YattnDecodeItem), sizeof(YattnDecodeWork),'
+                   ' offsetof(YattnDecodeItem,pos), offsetof(YattnDecodeWork,part_base));return 0;}\n')
+    exe = tmp_path / "s"
+    subprocess.run(["gcc", "-I", str(ROOT / "include"), str(src), "-o", str(exe)], check=True)
+    a, b, c, d = (int(x) for x in subprocess.run([str(exe)], capture_output=True, text=True).stdout.split())
+    assert a == C.sizeof(YattnDecodeItem) and b == C.sizeof(YattnDecodeWork)
+    assert c == YattnDecodeItem.pos.offset and d == YattnDecodeWork.part_base.offset
+
+
+def _plan(pos, n_kv, split=0, target=592):
+    from yllm_b200._lib import YattnDecodeWork, lib
+
+    pos = np.asarray(pos, dtype=np.uint32)
+    cap = 200000
+    work = (YattnDecodeWork * cap)()
+    nw, npart, ng = C.c_uint32(), C.c_uint32(), C.c_uint32()
+    err = C.create_string_buffer(256)
+    rc = lib.yattn_decode_plan(pos.ctypes.data_as(C.POINTER(C.c_uint32)), pos.size, n_kv, split, target, work,
+                               cap, C.byref(nw), C.byref(npart), C.byref(ng), err, 256)
+    assert rc == 0, err.value
+    return [work[i] for i in range(nw.value)], npart.value, ng.value
+
+
+@pytest.mark.parametrize("pos,n_kv,split", [
+    ([511], 2, 0), ([0], 8, 0), ([131071], 8, 0), ([4095] * 32, 2, 0),
+    ([1023, 8191, 5000, 1, 77], 8, 0), ([300, 301, 5], 4, 64),
+])
+def test_decode_plan_covers_every_key_once(pos, n_kv, split):
+    work, n_parts, n_groups = _plan(pos, n_kv, split)
+    seen = {}
+    parts, groups = set(), set()
+    for w in work:
+        key = (w.item, w.kv_head)
+        assert 0 <= w.t_begin < w.t_end <= pos[w.item] + 1
+        seen.setdefault(key, []).append((w.t_begin, w.t_end, w.split, w.n_splits))
+        if w.n_splits > 1:
+            parts.add(w.part_base + w.split)
+            groups.add(w.group)
+    for i, p in enumerate(pos):
+        for h in range(n_kv):
+            segs = sorted(seen[(i, h)])
+            assert segs[0][0] == 0 and segs[-1][1] == p + 1
+            for a, b in zip(segs, segs[1:]):
+                assert a[1] == b[0]
+            assert sorted(s[2] for s in segs) == list(range(len(segs)))
+            assert all(s[3] == len(segs) for s in segs)
+    assert parts == set(range(n_parts)) and groups == set(range(n_groups))
+    lens = [w.t_end - w.t_begin for w in work]
+    assert lens == sorted(lens, reverse=True)
+
+
+def test_plan_rejects_bad_args():
+    from yllm_b200._lib import YattnDecodeWork, lib
+
+    err = C.create_string_buffer(256)
+    nw, npart, ng = C.c_uint32(), C.c_uint32(), C.c_uint32()
+    pos = (C.c_uint32 * 1)(10)
+    work = (YattnDecodeWork * 1)()
+    rc = lib.yattn_decode_plan(pos, 1, 0, 0, 1, work, 1, C.byref(nw), C.byref(npart), C.byref(ng), err, 256)
+    assert rc == -1 and b"bad arguments" in err.value
+    pos = (C.c_uint32 * 1)(100000)
+    rc = lib.yattn_decode_plan(pos, 1, 8, 64, 1, work, 1, C.byref(nw), C.byref(npart), C.byref(ng), err, 256)
+    assert rc == -1 and b"work_cap" in err.value and nw.value > 1
+
+
+def test_error_paths_before_any_device_work():
+    from yllm_b200._lib import YattnError, call, call_void, lib
+
+    with pytest.raises(YattnError, match="head_dim 96"):
+        call("yattn_attn_decode", 0, 0, 0, 0, None, 10, 8, 2, 96, 192, None)
+    with pytest.raises(YattnError, match="query heads per kv head"):
+        call("yattn_decode_run", 1, 1, 1, 0, 0, 64, 2, 128, 256, None, 0, None)
+    with pytest.raises(YattnError, match="kv_dim"):
+        call("yattn_attn_decode", 0, 0, 0, 0, None, 10, 8, 2, 128, 100, None)
+    with pytest.raises(YattnError, match="head_dim 96"):
+        call_void("cuda_k_attn_decode", 0, 0, 0, 0, 10, 8, 2, 96, 192)
+    lib.yattn_clear_error()
+    assert lib.yattn_last_error() == b""
+    assert lib.yattn_version() >= 10000
+
+
+def test_workspace_size_formula():
+    from yllm_b200._lib import lib
+
+    # counters (256-aligned) + (m,l) (256-aligned) + o
+    n = lib.yattn_decode_workspace_bytes(10, 3, 32, 8, 128)
+    assert n == 256 + 512 + 10 * 4 * 128 * 4
+    assert lib.yattn_decode_workspace_bytes(0, 0, 32, 8, 128) == 0

@@ -1,0 +1,196 @@
+"""Pins the CPU oracle: reference known answers, reference-build golden vectors,
+port == reference bit for bit, and the deterministic input generator."""
+import ctypes as C
+import json
+import math
+from pathlib import Path
+
+import numpy as np
+import pytest
+
+import oracle
+
+GOLD = Path(__file__).resolve().parent / "golden"
+
+
+@pytest.fixture(scope="module")
+def gold():
+    return dict(np.load(GOLD / "golden_ref.npz"))
+
+
+def test_reference_known_answers(orc):
+    kat = json.loads((GOLD / "reference_kat.json").read_text())
+    for hx, want, tol in kat["f16_to_f32"]:
+        got = orc.orc_f16_to_f32(int(hx, 16))
+        if isinstance(want, str):
+            assert math.isinf(got) and (got < 0) == want.startswith("-"), hx
+        else:
+            assert abs(got - want) <= tol, (hx, got, want)   # CHECK_NEAR semantics
+    for hx in kat["f16_round_trip"]:
+        h = int(hx, 16)
+        assert orc.orc_f32_to_f16(orc.orc_f16_to_f32(h)) == h, hx
+    for v, d, pos, theta, want, tol in kat["rope_inplace"]:
+        x = np.array(v, dtype=np.float32)
+        orc.orc_rope_inplace(x, d, pos, theta)
+        assert np.all(np.abs(x[:len(want)] - np.array(want)) <= tol)
+    for v, want, tol in kat["softmax"]:
+        x = np.array(v, dtype=np.float32)
+        orc.orc_softmax(x, x.size)
+        assert np.all(np.abs(x - np.array(want)) <= tol)
+        assert abs(float(x.sum()) - 1.0) <= tol
+
+
+def test_port_matches_reference_golden_helpers(orc, gold):
+    f = gold["f32_bits"].view(np.float32)
+    assert np.array_equal(oracle.f32_to_f16(f, lib=orc), gold["f32_to_f16"])
+    h = np.arange(65536, dtype=np.uint16)
+    got = oracle.f16_to_f32(h, lib=orc)
+    want = gold["f16_to_f32_all"]
+    finite = np.isfinite(want)
+    assert np.array_equal(got[finite].view(np.uint32), want[finite].view(np.uint32))
+    assert np.array_equal(np.isnan(got), np.isnan(want))
+    x = gold["softmax_in"].copy()
+    orc.orc_softmax(x, x.size)
+    assert np.array_equal(x, gold["softmax_out"])
+    for name in ("rope_inplace", "rope_inplace_qwen"):
+        x = gold[name + "_in"].copy()
+        getattr(orc, "orc_" + name)(x, 128, 777, 1e6)
+        assert np.array_equal(x, gold[name + "_out"]), name
+    x = gold["rope_mrope_in"].copy()
+    orc.orc_rope_inplace_mrope(x, 256, 64, 1234, 1e7)
+    assert np.array_equal(x, gold["rope_mrope_out"])
+    x = gold["l2norm_in"].copy()
+    orc.orc_l2norm_inplace(x, 128, 1e-6)
+    assert np.array_equal(x, gold["l2norm_out"])
+
+
+def test_port_matches_reference_golden_attention(orc, gold):
+    for tag in ("dec", "gdec"):
+        H, KV, hd, T = (int(v) for v in gold[tag + "_geom"])
+        gate = gold.get(tag + "_gate")
+        out = oracle.attn_decode(gold[tag + "_q"], gold[tag + "_k"], gold[tag + "_v"], T - 1, H, KV, hd, KV * hd,
+                                 gate=gate, lib=orc)
+        assert np.array_equal(out, gold[tag + "_out"]), tag
+    H, KV, hd, S, P0 = (int(v) for v in gold["pre_geom"])
+    out = oracle.attn_prefill(gold["pre_q"], gold["pre_k"], gold["pre_v"], P0, S, H, KV, hd, KV * hd, H * hd,
+                              lib=orc)
+    assert np.array_equal(out, gold["pre_out"])
+
+
+def test_port_matches_reference_golden_gdn(orc, gold):
+    T, NK, NV, D = (int(v) for v in gold["gdn_geom"])
+    S = gold["gdn_S0"].copy()
+    out = np.zeros((T, NV * D), dtype=np.float32)
+    w, z = gold["gdn_w"], gold["gdn_z"]
+    orc.orc_gdn_prefill(S, out.ravel(), gold["gdn_q"].ravel(), gold["gdn_k"].ravel(), gold["gdn_v"].ravel(),
+                        gold["gdn_gate"].ravel(), gold["gdn_beta"].ravel(), T, NK, D, NV, D, w.ctypes.data,
+                        z.ctypes.data, 1e-6)
+    assert np.array_equal(S, gold["gdn_S1"])
+    assert np.array_equal(out, gold["gdn_out"])
+
+
+def test_port_equals_reference_build_live(orc, orc_ref):
+    """Where the reference tree is present, compare the two builds directly."""
+    assert orc.orc_build_kind() == 0 and orc_ref.orc_build_kind() == 1
+    hi = np.arange(65536, dtype=np.uint64) << np.uint64(16)
+    lows = np.array([0, 1, 0x0FFF, 0x1000, 0x1001, 0x1FFF, 0x2000, 0x7FFF, 0x8000, 0xFFFF, 0x2FFF, 0x3000],
+                    dtype=np.uint64)
+    f = (hi[:, None] | lows[None, :]).ravel().astype(np.uint32).view(np.float32)
+    assert np.array_equal(oracle.f32_to_f16(f, lib=orc), oracle.f32_to_f16(f, lib=orc_ref))
+    rng = np.random.default_rng(5)
+    H, KV, hd, T = 32, 8, 128, 300
+    kd = KV * hd
+    q = rng.standard_normal(H * hd).astype(np.float32)
+    k = oracle.f32_to_f16(rng.standard_normal(T * kd).astype(np.float32))
+    v = oracle.f32_to_f16(rng.standard_normal(T * kd).astype(np.float32))
+    a = oracle.attn_decode(q, k, v, T - 1, H, KV, hd, kd, lib=orc)
+    b = oracle.attn_decode(q, k, v, T - 1, H, KV, hd, kd, lib=orc_ref)
+    assert np.array_equal(a, b)
+    # GDN, full qwen3.5 head geometry, a few steps
+    NK, NV, D, steps = 16, 32, 128, 3
+    Sa = (rng.standard_normal(NV * D * D) * 0.1).astype(np.float32)
+    Sb = Sa.copy()
+    for _ in range(steps):
+        qg = rng.standard_normal(NK * D).astype(np.float32)
+        kg = rng.standard_normal(NK * D).astype(np.float32)
+        for hh in range(NK):
+            orc.orc_l2norm_inplace(qg[hh * D:(hh + 1) * D], D, 1e-6)
+            orc.orc_l2norm_inplace(kg[hh * D:(hh + 1) * D], D, 1e-6)
+        vg = rng.standard_normal(NV * D).astype(np.float32)
+        gt = rng.uniform(-3, 0, NV).astype(np.float32)
+        bt = rng.uniform(0, 1, NV).astype(np.float32)
+        oa = np.zeros(NV * D, np.float32)
+        ob = np.zeros(NV * D, np.float32)
+        orc.orc_gdn_step(Sa, oa, qg, kg, vg, gt, bt, NK, D, NV, D, None, None, 1e-6)
+        orc_ref.orc_gdn_step(Sb, ob, qg, kg, vg, gt, bt, NK, D, NV, D, None, None, 1e-6)
+        assert np.array_equal(oa, ob) and np.array_equal(Sa, Sb)
+
+
+def test_per_head_gdn_call_equals_all_heads_call(orc):
+    """orc_gdn_step splits the reference call per head; same bits as one call."""
+    rng = np.random.default_rng(9)
+    NK, NV, D = 4, 8, 32
+    S1 = (rng.standard_normal(NV * D * D) * 0.1).astype(np.float32)
+    S2 = S1.copy()
+    q = rng.standard_normal(NK * D).astype(np.float32)
+    k = rng.standard_normal(NK * D).astype(np.float32)
+    v = rng.standard_normal(NV * D).astype(np.float32)
+    g = rng.uniform(-2, 0, NV).astype(np.float32)
+    b = rng.uniform(0, 1, NV).astype(np.float32)
+    o1 = np.zeros(NV * D, np.float32)
+    o2 = np.zeros(NV * D, np.float32)
+    orc.orc_gdn_state_update(S1, o1, q, k, v, g, b, NK, D, NV, D)
+    orc.orc_gdn_step(S2, o2, q, k, v, g, b, NK, D, NV, D, None, None, 1e-6)
+    assert np.array_equal(o1, o2) and np.array_equal(S1, S2)
+
+
+def test_det_math_accuracy(orc):
+    rng = np.random.default_rng(1)
+    for x in rng.uniform(1e-7, 1, 2000):
+        assert abs(orc.orc_det_log(x) - math.log(x)) < 4e-15
+    for x in rng.uniform(-40, 40, 2000):
+        assert abs(orc.orc_det_exp(x) / math.exp(x) - 1) < 4e-16
+    s, c = C.c_double(), C.c_double()
+    for x in rng.uniform(-3e5, 3e5, 2000):
+        orc.orc_det_sincos(x, C.byref(s), C.byref(c))
+        assert abs(s.value - math.sin(x)) < 1e-10 and abs(c.value - math.cos(x)) < 1e-10
+
+
+def test_normal_stream_statistics(orc):
+    x = np.empty(400000, dtype=np.float32)
+    orc.orc_fill_normal(12345, 0, x.size, 1.0, x)
+    assert abs(float(x.mean())) < 0.01
+    assert abs(float(x.std()) - 1.0) < 0.01
+    kurt = float(((x - x.mean()) ** 4).mean() / x.var() ** 2)
+    assert abs(kurt - 3.0) < 0.05
+    # draws are the reference's splitmix64 (yrng) sequence
+    st = C.c_uint64(777)
+    lib_yrng = orc.orc_yrng if hasattr(orc, "orc_yrng") else None
+    if lib_yrng is not None:
+        lib_yrng.restype = C.c_uint64
+        lib_yrng.argtypes = [C.POINTER(C.c_uint64)]
+        for kk in range(5):
+            assert lib_yrng(C.byref(st)) == orc.orc_stream_draw(777, kk)
+
+
+def test_fixture_rope_matches_reference_rope(orc, orc_ref):
+    """The generator's double-precision rotation agrees with the engine's float
+    rope_inplace_qwen (matvec.c:907-921) to float accuracy."""
+    H, hd, pos = 2, 128, 511
+    rows = oracle.gen_rows(oracle.GEN_F32, 1, H, hd, 99, rope=False, lib=orc)[0]
+    rot = oracle.gen_rows(oracle.GEN_F32, 1, H, hd, 99, rope=True, pos0=pos, theta=1e6, lib=orc)[0]
+    ref = rows.copy()
+    for h in range(H):
+        orc_ref.orc_rope_inplace_qwen(ref[h * hd:(h + 1) * hd], hd, pos, 1e6)
+    assert np.max(np.abs(rot - ref)) < 2e-4 * max(1.0, float(np.max(np.abs(ref))))
+
+
+def test_config_seeds_and_ctx(orc):
+    from yllm_b200.configs import CFG3, ctx_lengths, seed_of, splitmix_draw
+
+    seed = seed_of(3, "ctx")
+    for i in range(64):
+        assert splitmix_draw(seed, i) == orc.orc_stream_draw(seed, i)
+    lens = ctx_lengths(64, 1024, 8192, seed)
+    assert lens == [orc.orc_ctx_len(seed, i, 1024, 8192) for i in range(64)]
+    assert CFG3.ctx() == lens and min(lens) >= 1024 and max(lens) <= 8192

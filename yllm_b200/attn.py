@@ -1,0 +1,191 @@
+"""Host-side mirror of the engine's attention entry points on torch tensors.
+
+Each function forwards to the C ABI (include/yllm_attn_sm100.h) with the
+tensors' device pointers and the current torch stream.  Names and argument
+meaning follow the reference's CUDA launchers (inference/cuda/cuda_kernels.h):
+cuda_k_attn_decode, cuda_k_attn_prefill, cuda_k_store_kv(_batch), plus the
+batched / split-KV / gated / GDN entry points the engine lacks today.
+Nothing here computes attention on the host: every path launches the CUDA
+library, and a missing library fails at import.
+"""
+from __future__ import annotations
+
+import ctypes as C
+from dataclasses import dataclass
+from typing import Optional, Sequence
+
+import numpy as np
+import torch
+
+from . import _lib
+from ._lib import YattnDecodeItem, YattnDecodeWork, call, call_void, lib
+
+
+def _ptr(t: Optional[torch.Tensor]) -> Optional[int]:
+    return None if t is None else t.data_ptr()
+
+
+def _stream(stream: Optional[torch.cuda.Stream] = None) -> int:
+    s = stream if stream is not None else torch.cuda.current_stream()
+    return s.cuda_stream
+
+
+def _need(t: torch.Tensor, dtype: torch.dtype, name: str) -> None:
+    if not t.is_cuda:
+        raise ValueError(f"{name} must be a CUDA tensor")
+    if t.dtype != dtype:
+        raise ValueError(f"{name} must be {dtype}, got {t.dtype}")
+    if not t.is_contiguous():
+        raise ValueError(f"{name} must be contiguous")
+
+
+def _kv_tensor(t: torch.Tensor, name: str) -> None:
+    if not t.is_cuda or t.dtype not in (torch.uint16, torch.float16, torch.int16):
+        raise ValueError(f"{name} must be a CUDA fp16-bits tensor (uint16/float16/int16)")
+
+
+# ----------------------------------------------------------------- drop-ins
+
+def cuda_k_attn_decode(att_out: torch.Tensor, q: torch.Tensor, kcache: torch.Tensor, vcache: torch.Tensor,
+                       pos: int, n_heads: int, n_kv_heads: int, head_dim: int, kv_dim: int) -> None:
+    """Same contract as the reference launcher (cuda_kernels.h:55-58), legacy default stream."""
+    _need(att_out, torch.float32, "att_out")
+    _need(q, torch.float32, "q")
+    _kv_tensor(kcache, "kcache")
+    _kv_tensor(vcache, "vcache")
+    call_void("cuda_k_attn_decode", att_out.data_ptr(), q.data_ptr(), kcache.data_ptr(), vcache.data_ptr(),
+              pos, n_heads, n_kv_heads, head_dim, kv_dim)
+
+
+def cuda_k_store_kv(kcache: torch.Tensor, vcache: torch.Tensor, k: torch.Tensor, v: torch.Tensor, pos: int,
+                    kv_dim: int) -> None:
+    call_void("cuda_k_store_kv", kcache.data_ptr(), vcache.data_ptr(), k.data_ptr(), v.data_ptr(), pos, kv_dim)
+
+
+def cuda_k_store_kv_batch(kcache: torch.Tensor, vcache: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
+                          pos_start: int, B: int, kv_dim: int) -> None:
+    call_void("cuda_k_store_kv_batch", kcache.data_ptr(), vcache.data_ptr(), k.data_ptr(), v.data_ptr(),
+              pos_start, B, kv_dim)
+
+
+# ------------------------------------------------------- error-returning API
+
+def attn_decode(att_out: torch.Tensor, q: torch.Tensor, kcache: torch.Tensor, vcache: torch.Tensor, pos: int,
+                n_heads: int, n_kv_heads: int, head_dim: int, kv_dim: int, gate: Optional[torch.Tensor] = None,
+                stream=None) -> None:
+    """One decode query (keys 0..pos) of one layer; optional qwen35 sigmoid gate."""
+    _need(att_out, torch.float32, "att_out")
+    _need(q, torch.float32, "q")
+    if gate is not None:
+        _need(gate, torch.float32, "gate")
+    call("yattn_attn_decode", att_out.data_ptr(), q.data_ptr(), kcache.data_ptr(), vcache.data_ptr(), _ptr(gate),
+         pos, n_heads, n_kv_heads, head_dim, kv_dim, _stream(stream))
+
+
+def store_kv(kcache: torch.Tensor, vcache: torch.Tensor, k: torch.Tensor, v: torch.Tensor, pos_start: int,
+             kv_dim: int, stream=None) -> None:
+    """fp32 rows -> fp16 cache rows pos_start.. with the engine's f32_to_f16 rounding."""
+    _need(k, torch.float32, "k")
+    _need(v, torch.float32, "v")
+    B = k.numel() // kv_dim
+    call("yattn_store_kv", kcache.data_ptr(), vcache.data_ptr(), k.data_ptr(), v.data_ptr(), pos_start, B, kv_dim,
+         _stream(stream))
+
+
+@dataclass
+class DecodePlan:
+    """A split schedule for a batch of decode queries (one per item).
+
+    The schedule depends only on the query positions, so one plan serves every
+    layer of a decode step: run() takes a device array of items per call.
+    """
+
+    n_items: int
+    n_heads: int
+    n_kv_heads: int
+    head_dim: int
+    kv_dim: int
+    work: torch.Tensor        # device bytes of YattnDecodeWork[n_work]
+    n_work: int
+    n_parts: int
+    n_groups: int
+    workspace: Optional[torch.Tensor]
+
+    @staticmethod
+    def build(positions: Sequence[int], n_heads: int, n_kv_heads: int, head_dim: int, kv_dim: int,
+              split_tokens: int = 0, target_ctas: int = 0, device=None) -> "DecodePlan":
+        pos = np.ascontiguousarray(np.asarray(positions, dtype=np.uint32))
+        n = int(pos.size)
+        cap = max(1, n * n_kv_heads * 64)
+        while True:
+            work = (YattnDecodeWork * cap)()
+            n_work, n_parts, n_groups = C.c_uint32(), C.c_uint32(), C.c_uint32()
+            err = C.create_string_buffer(512)
+            rc = lib.yattn_decode_plan(pos.ctypes.data_as(C.POINTER(C.c_uint32)), n, n_kv_heads, split_tokens,
+                                       target_ctas, work, cap, C.byref(n_work), C.byref(n_parts),
+                                       C.byref(n_groups), err, 512)
+            if rc == 0:
+                break
+            if n_work.value > cap:
+                cap = n_work.value
+                continue
+            raise _lib.YattnError("yattn_decode_plan: " + err.value.decode())
+        nbytes = n_work.value * C.sizeof(YattnDecodeWork)
+        host = torch.frombuffer(bytearray(C.string_at(work, nbytes)), dtype=torch.uint8)
+        dev = host.to(device or "cuda")
+        ws_bytes = lib.yattn_decode_workspace_bytes(n_parts.value, n_groups.value, n_heads, n_kv_heads, head_dim)
+        ws = None
+        if ws_bytes:
+            ws = torch.zeros(ws_bytes, dtype=torch.uint8, device=device or "cuda")
+        return DecodePlan(n, n_heads, n_kv_heads, head_dim, kv_dim, dev, n_work.value, n_parts.value,
+                          n_groups.value, ws)
+
+    def run(self, items_dev: torch.Tensor, stream=None) -> None:
+        ws_ptr = self.workspace.data_ptr() if self.workspace is not None else None
+        ws_len = self.workspace.numel() if self.workspace is not None else 0
+        call("yattn_decode_run", items_dev.data_ptr(), self.work.data_ptr(), self.n_work, self.n_parts,
+             self.n_groups, self.n_heads, self.n_kv_heads, self.head_dim, self.kv_dim, ws_ptr, ws_len,
+             _stream(stream))
+
+
+def make_items(entries: Sequence[tuple], device=None) -> torch.Tensor:
+    """Device array of YattnDecodeItem from (q, out, k, v, gate_or_None, pos) tuples of tensors."""
+    arr = (YattnDecodeItem * len(entries))()
+    for i, (q, out, k, v, gate, pos) in enumerate(entries):
+        arr[i].q = q.data_ptr()
+        arr[i].out = out.data_ptr()
+        arr[i].k = k.data_ptr() if isinstance(k, torch.Tensor) else int(k)
+        arr[i].v = v.data_ptr() if isinstance(v, torch.Tensor) else int(v)
+        arr[i].gate = gate.data_ptr() if gate is not None else 0
+        arr[i].pos = int(pos)
+    raw = bytearray(C.string_at(arr, C.sizeof(arr)))
+    return torch.frombuffer(raw, dtype=torch.uint8).to(device or "cuda")
+
+
+def decode_partial(ml: torch.Tensor, o: torch.Tensor, q: torch.Tensor, kcache: torch.Tensor, vcache: torch.Tensor,
+                   t_begin: int, t_end: int, n_heads: int, n_kv_heads: int, head_dim: int, kv_dim: int,
+                   stream=None) -> None:
+    """Unmerged (m, l, o) over keys [t_begin, t_end): m in log2 units (score*log2 e)."""
+    call("yattn_decode_partial", ml.data_ptr(), o.data_ptr(), q.data_ptr(), kcache.data_ptr(), vcache.data_ptr(),
+         t_begin, t_end, n_heads, n_kv_heads, head_dim, kv_dim, None, 0, _stream(stream))
+
+
+def merge_partials(out: torch.Tensor, ml: torch.Tensor, o: torch.Tensor, n_parts: int, n_heads: int,
+                   head_dim: int, gate: Optional[torch.Tensor] = None, stream=None) -> None:
+    """Log-sum-exp merge of [n_parts][n_heads] partials into out[n_heads*head_dim]."""
+    call("yattn_merge_partials", out.data_ptr(), ml.data_ptr(), o.data_ptr(), n_parts, n_heads, head_dim,
+         _ptr(gate), _stream(stream))
+
+
+def device_status(clear: bool = True) -> int:
+    st = C.c_int(0)
+    call("yattn_device_status", C.byref(st), 1 if clear else 0)
+    return st.value
+
+
+def reserve(nbytes: int) -> None:
+    call("yattn_reserve", nbytes)
+
+
+def version() -> int:
+    return lib.yattn_version()
