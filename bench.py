@@ -147,21 +147,25 @@ def run_ours(args) -> None:
     rank, world, local = ydist.init("nccl" if args.gpus > 1 else "gloo")
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
-    ctx_all = cfg.ctx()
+    # --seqs / --layers shrink the workload for profiler captures only; the
+    # default (and every reported number) is the full config.
+    n_layers = args.layers or cfg.layers
+    n_total = args.seqs or cfg.n_seqs
+    ctx_all = cfg.ctx()[:n_total]
     shards = ydist.shard_by_length(ctx_all, world)
     seqs = shards[rank]
-    log(f"[rank {rank}] {len(seqs)} seqs, {sum(ctx_all[s] for s in seqs)} keys/layer")
+    log(f"[rank {rank}] {len(seqs)} seqs, {sum(ctx_all[s] for s in seqs)} keys/layer, {n_layers} layers")
 
-    d = fixtures.decode_inputs(cfg, seqs=seqs, device=dev)
+    d = fixtures.decode_inputs(cfg, layers=list(range(n_layers)), seqs=seqs, device=dev)
     torch.cuda.synchronize()
     plan = attn.DecodePlan.build([c - 1 for c in d.ctx], cfg.n_heads, cfg.n_kv_heads, cfg.head_dim, cfg.kv_dim,
                                  device=dev)
     items = [attn.make_items([(d.q[l, i], d.out[l, i], d.k_ptr(l, i), d.v_ptr(l, i), None, d.ctx[i] - 1)
-                              for i in range(len(seqs))], device=dev) for l in range(cfg.layers)]
+                              for i in range(len(seqs))], device=dev) for l in range(n_layers)]
     stream = torch.cuda.current_stream()
 
     def step():
-        for l in range(cfg.layers):
+        for l in range(n_layers):
             plan.run(items[l], stream)
 
     def barrier():
@@ -178,13 +182,13 @@ def run_ours(args) -> None:
     clocks.start()
     time.sleep(0.3)
     ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
-          for _ in range(args.steps * cfg.layers)]
+          for _ in range(args.steps * n_layers)]
     t0 = torch.cuda.Event(enable_timing=True)
     t1 = torch.cuda.Event(enable_timing=True)
     t0.record(stream)
     k = 0
     for _ in range(args.steps):
-        for l in range(cfg.layers):
+        for l in range(n_layers):
             ev[k][0].record(stream)
             plan.run(items[l], stream)
             ev[k][1].record(stream)
@@ -200,7 +204,7 @@ def run_ours(args) -> None:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     elapsed_ms = float(t.item())
     ms_per_step = elapsed_ms / args.steps
-    value = cfg.n_seqs / (ms_per_step / 1e3)
+    value = n_total / (ms_per_step / 1e3)
 
     # ---- end to end: pinned host q in, host out back, every step ----
     n_q = d.q.numel()
@@ -213,21 +217,23 @@ def run_ours(args) -> None:
         step()
         out_host.copy_(d.out.view(-1), non_blocking=True)
 
-    for _ in range(max(1, args.warmup)):
-        e2e_step()
-    torch.cuda.synchronize()
-    barrier()
-    e0 = torch.cuda.Event(enable_timing=True)
-    e1 = torch.cuda.Event(enable_timing=True)
-    e0.record(stream)
-    for _ in range(args.steps):
-        e2e_step()
-    e1.record(stream)
-    torch.cuda.synchronize()
-    te = torch.tensor([e0.elapsed_time(e1)], device=dev)
-    if world > 1:
-        dist.all_reduce(te, op=dist.ReduceOp.MAX)
-    e2e_value = cfg.n_seqs / (float(te.item()) / args.steps / 1e3)
+    e2e_value = None
+    if not args.no_e2e:
+        for _ in range(max(1, args.warmup)):
+            e2e_step()
+        torch.cuda.synchronize()
+        barrier()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(args.steps):
+            e2e_step()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        te = torch.tensor([e0.elapsed_time(e1)], device=dev)
+        if world > 1:
+            dist.all_reduce(te, op=dist.ReduceOp.MAX)
+        e2e_value = n_total / (float(te.item()) / args.steps / 1e3)
 
     # ---- roofline of the decode kernel (per launch = one layer of this rank's seqs) ----
     bytes_per_launch = sum(d.ctx) * cfg.kv_dim * 2 * 2 + len(seqs) * cfg.n_heads * cfg.head_dim * 4 * 2
@@ -239,7 +245,7 @@ def run_ours(args) -> None:
 
     if rank == 0:
         cpu = None
-        if not args.no_cpu_baseline and world == 1:
+        if not args.no_cpu_baseline and world == 1 and not (args.seqs or args.layers):
             cpu = CpuReference(cfg, list(range(cfg.n_seqs))).rate(args.cpu_budget)
             cpu.pop("step_s", None)
         line = {
@@ -256,21 +262,22 @@ def run_ours(args) -> None:
             "dtype": "f32 math, fp16 KV",
             "data": "synthetic (seeded splitmix64 + Box-Muller, N(0,1) fp16 KV cache)",
             "config": {
-                "workload": cfg.name,
+                "workload": cfg.name + ("" if not (args.seqs or args.layers) else f"-profile-{n_total}seq-{n_layers}layer"),
                 "n_heads": cfg.n_heads, "n_kv_heads": cfg.n_kv_heads, "head_dim": cfg.head_dim,
-                "layers": cfg.layers, "n_seqs": cfg.n_seqs, "ctx_range": [cfg.ctx_lo, cfg.ctx_hi],
+                "layers": n_layers, "n_seqs": n_total, "ctx_range": [cfg.ctx_lo, cfg.ctx_hi],
                 "total_keys_per_layer": sum(ctx_all),
                 "kv_bytes_per_step": cfg.kv_bytes_per_step(),
                 "parallelism": f"sequence-sharded x{world}",
                 "l2": "inputs larger than L2 (KV per GPU >> 126 MB)",
             },
-            "e2e": {"value": round(e2e_value, 2), "unit": "tok/s",
-                    "h2d_bytes_per_step": int(n_q * 4 * world), "d2h_bytes_per_step": int(n_q * 4 * world)},
+            "e2e": None if e2e_value is None else {
+                "value": round(e2e_value, 2), "unit": "tok/s",
+                "h2d_bytes_per_step": int(n_q * 4 * world), "d2h_bytes_per_step": int(n_q * 4 * world)},
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"],
                          "unit": "GB/s", "frac": round(achieved / peaks["hbm_gbs"], 4),
                          "traffic": None, "kernel": "k_decode<128,4>", "peak_source": peak_src,
                          "bytes_per_launch": bytes_per_launch, "launch_ms": round(launch_ms, 5)},
-            "gpu_launches": args.steps * cfg.layers,
+            "gpu_launches": args.steps * n_layers,
             "clocks": {"sm_mhz": clk["sm_mhz"], "sm_max_mhz": clk["sm_max_mhz"], "reasons": clk["reasons"]},
         }
         if cpu is not None:
@@ -333,6 +340,9 @@ def main() -> None:
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--seqs", type=int, default=0, help="profiling only: first N sequences")
+    ap.add_argument("--layers", type=int, default=0, help="profiling only: first L layers")
     ap.add_argument("--cpu-budget", type=float, default=20.0, help="seconds of CPU attention in the baseline")
     args = ap.parse_args()
     if args.warmup < 3:

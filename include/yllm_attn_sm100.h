@@ -59,6 +59,17 @@ void cuda_k_attn_decode(float* att_out,
                         uint32_t pos, uint32_t n_heads, uint32_t n_kv_heads, uint32_t head_dim,
                         uint32_t kv_dim);
 
+/* Replaces cuda_k_attn_prefill (cuda_kernels.h:60-63; kernel cuda_kernels.cu:602-655).
+ * B query tokens at positions pos_start..pos_start+B-1 (q row b at
+ * q + b*q_stride); token b attends keys 0..pos_start+b.  Any B (the reference
+ * caps a chunk at 64).  Flash attention on tcgen05 tensor cores: q is rounded
+ * to fp16 on load, P is fp16, accumulation fp32.  Needs 16-byte aligned
+ * pointers, q_stride % 4 == 0, kv_dim % 8 == 0, head_dim 64/128/256. */
+void cuda_k_attn_prefill(float* att_out,
+                         const float* q, const uint16_t* kcache, const uint16_t* vcache,
+                         uint32_t pos_start, uint32_t B, uint32_t n_heads, uint32_t n_kv_heads,
+                         uint32_t head_dim, uint32_t kv_dim, uint32_t q_stride);
+
 /* Replaces cuda_k_store_kv (cuda_kernels.h:50-51; kernel cuda_kernels.cu:494-507).
  * Unlike the reference kernel (__float2half_rn, round-to-nearest-even) this
  * rounds with the engine's own f32_to_f16 (platform.c:340-379: half-up, f32
@@ -153,6 +164,13 @@ int yattn_attn_decode(float* att_out, const float* q, const uint16_t* kcache,
                       uint32_t n_heads, uint32_t n_kv_heads, uint32_t head_dim, uint32_t kv_dim,
                       void* stream, char* err, size_t errlen);
 
+/* Error-returning form of cuda_k_attn_prefill with an explicit stream and the
+ * qwen35 output gate (gate rows laid out like q, or NULL; engine.c:958-960). */
+int yattn_attn_prefill(float* att_out, const float* q, const uint16_t* kcache,
+                       const uint16_t* vcache, const float* gate, uint32_t pos_start, uint32_t B,
+                       uint32_t n_heads, uint32_t n_kv_heads, uint32_t head_dim, uint32_t kv_dim,
+                       uint32_t q_stride, void* stream, char* err, size_t errlen);
+
 /* Pre-allocates the per-device workspace the drop-in entry points use, so no
  * allocation happens inside a decode step (the shim's bind-time workspace). */
 int yattn_reserve(size_t bytes, char* err, size_t errlen);
@@ -161,6 +179,36 @@ int yattn_reserve(size_t bytes, char* err, size_t errlen);
 int yattn_store_kv(uint16_t* kcache, uint16_t* vcache, const float* k, const float* v,
                    uint32_t pos_start, uint32_t B, uint32_t kv_dim, void* stream,
                    char* err, size_t errlen);
+
+/* -------------------------------------------- Gated DeltaNet (qwen35)
+ * State S: fp32 [n_vheads][hv][hk] per sequence (row j = v index, row stride
+ * hv), updated in place.  v-head h reads k-head h % num_k_heads.  Supported:
+ * hk == hv == 128; 16-byte aligned S, q, k, v, out, norm_w, z. */
+
+/* Same argument order and meaning as gdn_state_update (inference/include/matvec.h:35-37,
+ * inference/core/matvec.c:975-1004), on device pointers, legacy default stream:
+ * one token, decay e^gate[h], delta rule with beta[h], out = S q / sqrt(hv). */
+void cuda_k_gdn_state_update(float* S, float* out, const float* q, const float* k,
+                             const float* v, const float* gate, const float* beta,
+                             uint32_t num_k_heads, uint32_t hk, uint32_t n_vheads, uint32_t hv);
+
+/* Batched single-token update of n_seqs independent sequences (engine.c:826-852):
+ * S [n_seqs][n_vheads][hv][hk]; q,k [n_seqs][num_k_heads*hk]; v,out,z
+ * [n_seqs][n_vheads*hv]; gate,beta [n_seqs][n_vheads].  With norm_w ([hv])
+ * and z, out gets the rmsnorm_gated epilogue (matvec.c:1007-1021) per v-head. */
+int yattn_gdn_decode(float* S, float* out, const float* q, const float* k, const float* v,
+                     const float* gate, const float* beta, uint32_t n_seqs, uint32_t num_k_heads,
+                     uint32_t hk, uint32_t n_vheads, uint32_t hv, const float* norm_w,
+                     const float* z, float eps, void* stream, char* err, size_t errlen);
+
+/* T tokens of each of n_seqs sequences in order (the engine's qwen35 prefill,
+ * engine.c:723-734, calls gdn_state_update once per token).  Per-token rows as
+ * in yattn_gdn_decode, token t of sequence s at row s*T + t. */
+int yattn_gdn_prefill(float* S, float* out, const float* q, const float* k, const float* v,
+                      const float* gate, const float* beta, uint32_t n_seqs, uint32_t T,
+                      uint32_t num_k_heads, uint32_t hk, uint32_t n_vheads, uint32_t hv,
+                      const float* norm_w, const float* z, float eps, void* stream,
+                      char* err, size_t errlen);
 
 /* ------------------------------------------------ seeded input generator
  * Deterministic on every device and bit-identical to the CPU restatement in

@@ -153,6 +153,52 @@ def prefill_fixture(cfg, seq_len: Optional[int] = None, lib=None) -> dict:
     return {"q": q, "k": k, "v": v, "gate": gate}
 
 
+def gdn_fixture(cfg, n_seqs: int, T: int, seeded_state: bool, lib=None) -> dict:
+    """CPU restatement of yllm_b200.fixtures.gdn_inputs (same bits)."""
+    from yllm_b200.configs import seed_of
+
+    lib = lib or load()
+    D, NK, NV, c = cfg.head_dim, cfg.num_k_heads, cfg.n_v_heads, cfg.cfg
+    rows = n_seqs * T
+    S = np.zeros(n_seqs * NV * D * D, dtype=np.float32)
+    if seeded_state:
+        S = gen_rows(GEN_F32, n_seqs * NV * D, 1, D, seed_of(c, "state"), scale=cfg.state_scale, lib=lib).ravel()
+    q = np.empty(rows * NK * D, np.float32)
+    k = np.empty(rows * NK * D, np.float32)
+    lib.orc_gdn_qk(seed_of(c, "gdn_q"), 0, rows, NK, D, cfg.eps, q)
+    lib.orc_gdn_qk(seed_of(c, "gdn_k"), 0, rows, NK, D, cfg.eps, k)
+    v = gen_rows(GEN_F32_BF16, rows, NV, D, seed_of(c, "gdn_v"), lib=lib).ravel()
+    z = gen_rows(GEN_F32_BF16, rows, NV, D, seed_of(c, "z"), lib=lib).ravel()
+    gate = np.empty(rows * NV, np.float32)
+    beta = np.empty(rows * NV, np.float32)
+    lib.orc_gdn_gates(seed_of(c, "gdn_a"), seed_of(c, "gdn_b"), 0, rows * NV, gate, beta)
+    w = gen_rows(GEN_F32, 1, 1, D, seed_of(c, "norm_w"), scale=0.1, lib=lib).ravel()
+    w = (w + np.float32(1.0)).astype(np.float32)
+    return dict(S=S, q=q, k=k, v=v, z=z, gate=gate, beta=beta, norm_w=w)
+
+
+def gdn_run(fx: dict, cfg, n_seqs: int, T: int, epilogue: bool, lib=None) -> tuple:
+    """engine.c:723-734 + 826-852: token-by-token gdn_state_update (+ rmsnorm_gated)
+    per sequence.  Returns (final state, outputs [n_seqs*T, n_vheads*128])."""
+    lib = lib or load()
+    D, NK, NV = cfg.head_dim, cfg.num_k_heads, cfg.n_v_heads
+    S = fx["S"].copy()
+    out = np.zeros(n_seqs * T * NV * D, np.float32)
+    per_state = NV * D * D
+    for s in range(n_seqs):
+        Ss = S[s * per_state:(s + 1) * per_state]   # view: updated in place
+        r0 = s * T
+        sl = lambda a, width: np.ascontiguousarray(a[r0 * width:(r0 + T) * width])
+        os_ = np.zeros(T * NV * D, np.float32)
+        zs = sl(fx["z"], NV * D)
+        w = fx["norm_w"]
+        lib.orc_gdn_prefill(Ss, os_, sl(fx["q"], NK * D), sl(fx["k"], NK * D), sl(fx["v"], NV * D),
+                            sl(fx["gate"], NV), sl(fx["beta"], NV), T, NK, D, NV, D,
+                            w.ctypes.data if epilogue else None, zs.ctypes.data if epilogue else None, cfg.eps)
+        out[r0 * NV * D:(r0 + T) * NV * D] = os_
+    return S, out
+
+
 # ------------------------------------------------------------ attention
 
 def attn_decode(q, k, v, pos, n_heads, n_kv, hd, kv_dim, gate=None, lib=None) -> np.ndarray:

@@ -1,0 +1,142 @@
+"""GPU parity of the tcgen05 prefill path against the CPU oracle (engine.c:533-563).
+
+Tolerance: oracle.REL_TOL = 2e-3 relative to max(|cpu|, rms(cpu)) per element.
+The kernel rounds q to fp16 (the fixtures' q are fp16-exact) and holds P in
+fp16 with fp32 accumulation.
+"""
+import numpy as np
+import pytest
+import torch
+
+import oracle
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def dev():
+    assert torch.cuda.is_available(), "GPU tests need a CUDA device"
+    torch.cuda.set_device(0)
+    import yllm_b200.attn  # noqa: F401
+
+    return torch.device("cuda:0")
+
+
+def _case(dev, H, KV, hd, P0, B, seed, kv_extra=0, q_extra=0, gated=False):
+    rng = np.random.default_rng(seed)
+    kd = KV * hd + kv_extra
+    qs = H * hd + q_extra
+    lib = oracle.load()
+    q = (rng.standard_normal((B, qs)) * 0.5).astype(np.float32)
+    q = oracle.f16_to_f32(oracle.f32_to_f16(q, lib=lib), lib=lib).reshape(B, qs)   # fp16-exact q
+    n = P0 + B
+    k = oracle.f32_to_f16((rng.standard_normal(n * kd) * 0.5).astype(np.float32), lib=lib)
+    v = oracle.f32_to_f16((rng.standard_normal(n * kd) * 0.5).astype(np.float32), lib=lib)
+    gate = rng.standard_normal((B, qs)).astype(np.float32) if gated else None
+    t = lambda a: torch.from_numpy(a).to(dev)
+    tk = t(k.view(np.int16)).view(torch.uint16)
+    tv = t(v.view(np.int16)).view(torch.uint16)
+    return dict(q=q, k=k, v=v, kd=kd, qs=qs, gate=gate, tq=t(q), tk=tk, tv=tv,
+                tg=t(gate) if gated else None)
+
+
+@pytest.mark.parametrize("H,KV,hd,P0,B", [
+    (16, 8, 128, 0, 200), (16, 8, 128, 37, 100), (16, 8, 128, 0, 1), (16, 8, 128, 5, 129),
+    (14, 2, 64, 0, 300), (32, 8, 64, 300, 64), (16, 2, 256, 0, 200), (8, 1, 256, 130, 70),
+    (12, 4, 128, 0, 256), (4, 4, 128, 1000, 40),
+])
+def test_prefill_matches_oracle(dev, H, KV, hd, P0, B):
+    from yllm_b200 import attn
+
+    c = _case(dev, H, KV, hd, P0, B, seed=H + hd + P0 + B)
+    out = torch.zeros(B, c["qs"], device=dev)
+    attn.attn_prefill(out, c["tq"], c["tk"], c["tv"], P0, B, H, KV, hd, c["kd"], c["qs"])
+    want = oracle.attn_prefill(c["q"], c["k"], c["v"], P0, B, H, KV, hd, c["kd"], c["qs"])
+    torch.cuda.synchronize()
+    oracle.assert_close(out.cpu().numpy()[:, :H * hd], want[:, :H * hd], what=f"prefill H{H} KV{KV} hd{hd} P0{P0} B{B}")
+    assert attn.device_status() == 0
+
+
+def test_prefill_strides_and_dropin(dev):
+    """q_stride > n_heads*head_dim (the engine passes hidden) and padded kv rows."""
+    from yllm_b200 import attn
+
+    H, KV, hd, P0, B = 8, 2, 128, 17, 150
+    c = _case(dev, H, KV, hd, P0, B, seed=11, kv_extra=128, q_extra=64)
+    out = torch.full((B, c["qs"]), 7.0, device=dev)
+    attn.cuda_k_attn_prefill(out, c["tq"], c["tk"], c["tv"], P0, B, H, KV, hd, c["kd"], c["qs"])
+    torch.cuda.synchronize()
+    want = oracle.attn_prefill(c["q"], c["k"], c["v"], P0, B, H, KV, hd, c["kd"], c["qs"])
+    got = out.cpu().numpy()
+    oracle.assert_close(got[:, :H * hd], want[:, :H * hd], what="strided prefill")
+    assert np.all(got[:, H * hd:] == 7.0), "columns past n_heads*head_dim must be untouched"
+
+
+def test_prefill_gated(dev):
+    from yllm_b200 import attn
+
+    H, KV, hd, P0, B = 16, 2, 256, 0, 300
+    c = _case(dev, H, KV, hd, P0, B, seed=5, gated=True)
+    out = torch.zeros(B, c["qs"], device=dev)
+    attn.attn_prefill(out, c["tq"], c["tk"], c["tv"], P0, B, H, KV, hd, c["kd"], c["qs"], gate=c["tg"])
+    want = oracle.attn_prefill(c["q"], c["k"], c["v"], P0, B, H, KV, hd, c["kd"], c["qs"], gate=c["gate"])
+    torch.cuda.synchronize()
+    oracle.assert_close(out.cpu().numpy(), want, what="gated prefill")
+
+
+def test_prefill_config2_full(dev):
+    """Qwen3-0.6B shape, 2048 tokens, one call."""
+    from yllm_b200 import attn, fixtures
+    from yllm_b200.configs import CFG2 as c
+
+    p = fixtures.prefill_inputs(c, device=dev)
+    attn.attn_prefill(p.out, p.q, p.k, p.v, 0, c.seq_len, c.n_heads, c.n_kv_heads, c.head_dim, c.kv_dim,
+                      c.n_heads * c.head_dim)
+    torch.cuda.synchronize()
+    f = oracle.prefill_fixture(c)
+    want = oracle.attn_prefill(f["q"], f["k"], f["v"], 0, c.seq_len, c.n_heads, c.n_kv_heads, c.head_dim, c.kv_dim,
+                               c.n_heads * c.head_dim)
+    oracle.assert_close(p.out.cpu().numpy(), want, what="config2 prefill")
+
+
+def test_prefill_config5_gated_last_chunk(dev):
+    """BASELINE config 5 gated attention prefill (4096 tokens, hd 256).  The
+    oracle runs the engine's chunked form on the last 64 tokens (keys 0..4095);
+    the full-sequence GPU call must give the same rows."""
+    from yllm_b200 import attn, fixtures
+    from yllm_b200.configs import CFG5_GATED_PREFILL as c
+
+    S, H, hd = c.seq_len, c.n_heads, c.head_dim
+    p = fixtures.prefill_inputs(c, device=dev)
+    attn.attn_prefill(p.out, p.q, p.k, p.v, 0, S, H, c.n_kv_heads, hd, c.kv_dim, H * hd, gate=p.gate)
+    torch.cuda.synchronize()
+    f = oracle.prefill_fixture(c)
+    B = 64
+    want = oracle.attn_prefill(f["q"][S - B:], f["k"], f["v"], S - B, B, H, c.n_kv_heads, hd, c.kv_dim, H * hd,
+                               gate=f["gate"][S - B:])
+    oracle.assert_close(p.out.cpu().numpy()[S - B:], want, what="config5 gated prefill (last chunk)")
+
+
+def test_prefill_last_row_equals_decode(dev):
+    """The last prefill row and a decode at the same position agree (two kernels)."""
+    from yllm_b200 import attn
+
+    H, KV, hd, B = 32, 8, 128, 777
+    c = _case(dev, H, KV, hd, 0, B, seed=3)
+    out = torch.zeros(B, c["qs"], device=dev)
+    attn.attn_prefill(out, c["tq"], c["tk"], c["tv"], 0, B, H, KV, hd, c["kd"], c["qs"])
+    dec = torch.zeros(H * hd, device=dev)
+    attn.attn_decode(dec, c["tq"][B - 1].contiguous(), c["tk"], c["tv"], B - 1, H, KV, hd, c["kd"])
+    torch.cuda.synchronize()
+    oracle.assert_close(out[B - 1].cpu().numpy(), dec.cpu().numpy(), what="prefill vs decode")
+
+
+def test_prefill_rejects_bad_geometry(dev):
+    from yllm_b200 import _lib, attn
+
+    c = _case(dev, 8, 2, 128, 0, 10, seed=1)
+    out = torch.zeros(10, c["qs"], device=dev)
+    with pytest.raises(_lib.YattnError, match="head_dim"):
+        attn.attn_prefill(out, c["tq"], c["tk"], c["tv"], 0, 10, 8, 2, 96, c["kd"], c["qs"])
+    with pytest.raises(_lib.YattnError, match="q_stride"):
+        attn.attn_prefill(out, c["tq"], c["tk"], c["tv"], 0, 10, 8, 2, 128, c["kd"], 1022)

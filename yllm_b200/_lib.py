@@ -68,6 +68,8 @@ PROTOS = {
     "yattn_clear_error": (None, []),
     "yattn_device_status": (C.c_int, [C.POINTER(C.c_int), C.c_int, *E]),
     "cuda_k_attn_decode": (None, [vp, vp, vp, vp, u32, u32, u32, u32, u32]),
+    "cuda_k_attn_prefill": (None, [vp, vp, vp, vp, u32, u32, u32, u32, u32, u32, u32]),
+    "yattn_attn_prefill": (C.c_int, [vp, vp, vp, vp, vp, u32, u32, u32, u32, u32, u32, u32, vp, *E]),
     "cuda_k_store_kv": (None, [vp, vp, vp, vp, u32, u32]),
     "cuda_k_store_kv_batch": (None, [vp, vp, vp, vp, u32, u32, u32]),
     "yattn_decode_plan": (
@@ -84,6 +86,10 @@ PROTOS = {
     "yattn_attn_decode": (C.c_int, [vp, vp, vp, vp, vp, u32, u32, u32, u32, u32, vp, *E]),
     "yattn_reserve": (C.c_int, [sz, *E]),
     "yattn_store_kv": (C.c_int, [vp, vp, vp, vp, u32, u32, u32, vp, *E]),
+    "cuda_k_gdn_state_update": (None, [vp, vp, vp, vp, vp, vp, vp, u32, u32, u32, u32]),
+    "yattn_gdn_decode": (C.c_int, [vp, vp, vp, vp, vp, vp, vp, u32, u32, u32, u32, u32, vp, vp, C.c_float, vp, *E]),
+    "yattn_gdn_prefill": (
+        C.c_int, [vp, vp, vp, vp, vp, vp, vp, u32, u32, u32, u32, u32, u32, vp, vp, C.c_float, vp, *E]),
     "yattn_gen_rows": (
         C.c_int,
         [vp, C.c_int, sz, sz, u32, u32, u64, u64, C.c_double, C.c_int, u32, C.c_double, vp, *E],

@@ -57,6 +57,30 @@ def cuda_k_attn_decode(att_out: torch.Tensor, q: torch.Tensor, kcache: torch.Ten
               pos, n_heads, n_kv_heads, head_dim, kv_dim)
 
 
+def cuda_k_attn_prefill(att_out: torch.Tensor, q: torch.Tensor, kcache: torch.Tensor, vcache: torch.Tensor,
+                        pos_start: int, B: int, n_heads: int, n_kv_heads: int, head_dim: int, kv_dim: int,
+                        q_stride: int) -> None:
+    """Same contract as the reference launcher (cuda_kernels.h:60-63), legacy default stream."""
+    _need(att_out, torch.float32, "att_out")
+    _need(q, torch.float32, "q")
+    _kv_tensor(kcache, "kcache")
+    _kv_tensor(vcache, "vcache")
+    call_void("cuda_k_attn_prefill", att_out.data_ptr(), q.data_ptr(), kcache.data_ptr(), vcache.data_ptr(),
+              pos_start, B, n_heads, n_kv_heads, head_dim, kv_dim, q_stride)
+
+
+def attn_prefill(att_out: torch.Tensor, q: torch.Tensor, kcache: torch.Tensor, vcache: torch.Tensor,
+                 pos_start: int, B: int, n_heads: int, n_kv_heads: int, head_dim: int, kv_dim: int, q_stride: int,
+                 gate: Optional[torch.Tensor] = None, stream=None) -> None:
+    """Causal prefill of B tokens at pos_start (keys 0..pos_start+b), optional qwen35 gate."""
+    _need(att_out, torch.float32, "att_out")
+    _need(q, torch.float32, "q")
+    if gate is not None:
+        _need(gate, torch.float32, "gate")
+    call("yattn_attn_prefill", att_out.data_ptr(), q.data_ptr(), kcache.data_ptr(), vcache.data_ptr(), _ptr(gate),
+         pos_start, B, n_heads, n_kv_heads, head_dim, kv_dim, q_stride, _stream(stream))
+
+
 def cuda_k_store_kv(kcache: torch.Tensor, vcache: torch.Tensor, k: torch.Tensor, v: torch.Tensor, pos: int,
                     kv_dim: int) -> None:
     call_void("cuda_k_store_kv", kcache.data_ptr(), vcache.data_ptr(), k.data_ptr(), v.data_ptr(), pos, kv_dim)
@@ -175,6 +199,36 @@ def merge_partials(out: torch.Tensor, ml: torch.Tensor, o: torch.Tensor, n_parts
     """Log-sum-exp merge of [n_parts][n_heads] partials into out[n_heads*head_dim]."""
     call("yattn_merge_partials", out.data_ptr(), ml.data_ptr(), o.data_ptr(), n_parts, n_heads, head_dim,
          _ptr(gate), _stream(stream))
+
+
+def cuda_k_gdn_state_update(S: torch.Tensor, out: torch.Tensor, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
+                            gate: torch.Tensor, beta: torch.Tensor, num_k_heads: int, hk: int, n_vheads: int,
+                            hv: int) -> None:
+    """gdn_state_update (matvec.h:35-37) on device tensors, legacy default stream."""
+    call_void("cuda_k_gdn_state_update", S.data_ptr(), out.data_ptr(), q.data_ptr(), k.data_ptr(), v.data_ptr(),
+              gate.data_ptr(), beta.data_ptr(), num_k_heads, hk, n_vheads, hv)
+
+
+def gdn_decode(S, out, q, k, v, gate, beta, n_seqs: int, num_k_heads: int, hk: int, n_vheads: int, hv: int,
+               norm_w: Optional[torch.Tensor] = None, z: Optional[torch.Tensor] = None, eps: float = 1e-6,
+               stream=None) -> None:
+    """One GDN token for each of n_seqs sequences (state updated in place)."""
+    for name, t in (("S", S), ("out", out), ("q", q), ("k", k), ("v", v), ("gate", gate), ("beta", beta)):
+        _need(t, torch.float32, name)
+    call("yattn_gdn_decode", S.data_ptr(), out.data_ptr(), q.data_ptr(), k.data_ptr(), v.data_ptr(),
+         gate.data_ptr(), beta.data_ptr(), n_seqs, num_k_heads, hk, n_vheads, hv, _ptr(norm_w), _ptr(z), float(eps),
+         _stream(stream))
+
+
+def gdn_prefill(S, out, q, k, v, gate, beta, n_seqs: int, T: int, num_k_heads: int, hk: int, n_vheads: int,
+                hv: int, norm_w: Optional[torch.Tensor] = None, z: Optional[torch.Tensor] = None,
+                eps: float = 1e-6, stream=None) -> None:
+    """T GDN tokens per sequence in order (state updated in place)."""
+    for name, t in (("S", S), ("out", out), ("q", q), ("k", k), ("v", v), ("gate", gate), ("beta", beta)):
+        _need(t, torch.float32, name)
+    call("yattn_gdn_prefill", S.data_ptr(), out.data_ptr(), q.data_ptr(), k.data_ptr(), v.data_ptr(),
+         gate.data_ptr(), beta.data_ptr(), n_seqs, T, num_k_heads, hk, n_vheads, hv, _ptr(norm_w), _ptr(z),
+         float(eps), _stream(stream))
 
 
 def device_status(clear: bool = True) -> int:

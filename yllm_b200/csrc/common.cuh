@@ -113,6 +113,14 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity
     }
 }
 
+// Warp-uniform form: every lane waits, the warp proceeds only if all lanes saw
+// the phase complete (so a timeout never splits a warp before warp-collective code).
+__device__ __forceinline__ bool warp_wait_bounded(uint64_t* bar, uint32_t parity, int* status, int code,
+                                                  volatile int* abort_flag) {
+    const bool ok = mbar_wait_bounded(bar, parity, status, code, abort_flag);
+    return __all_sync(0xffffffffu, ok);
+}
+
 // One bulk global->shared copy completing on an mbarrier (TMA, non-tensor form).
 // dst/src 16-byte aligned, bytes a multiple of 16.
 __device__ __forceinline__ void bulk_g2s(void* dst_smem, const void* src_gmem, uint32_t bytes, uint64_t* bar) {

@@ -162,7 +162,7 @@ __global__ void __launch_bounds__(kThreads, 2) k_decode(const DecodeParams p) {
         for (uint32_t i = 0; i < ntiles; ++i) {
             const int s = i % C::NST;
             if (i >= static_cast<uint32_t>(C::NST)) {
-                if (!mbar_wait_bounded(&empty[s], ((i / C::NST) & 1u) ^ 1u, p.status, ST_DECODE_EMPTY_TIMEOUT,
+                if (!warp_wait_bounded(&empty[s], ((i / C::NST) & 1u) ^ 1u, p.status, ST_DECODE_EMPTY_TIMEOUT,
                                        abort_flag))
                     break;
             }
@@ -226,7 +226,7 @@ __global__ void __launch_bounds__(kThreads, 2) k_decode(const DecodeParams p) {
 
     for (uint32_t i = 0; i < ntiles; ++i) {
         const int s = i % C::NST;
-        if (!mbar_wait_bounded(&full[s], (i / C::NST) & 1u, p.status, ST_DECODE_FULL_TIMEOUT, abort_flag)) break;
+        if (!warp_wait_bounded(&full[s], (i / C::NST) & 1u, p.status, ST_DECODE_FULL_TIMEOUT, abort_flag)) break;
         const uint32_t nrows = min(static_cast<uint32_t>(kTok), t1 - (t0 + i * kTok));
         const int nvalid = max(0, min(8, static_cast<int>(nrows) - warp * 8));
         const uint8_t* kt = stages + s * C::STAGEB + warp * 8 * C::ROWB;

@@ -1,0 +1,497 @@
+// prefill.cu -- causal batched prefill attention on tcgen05 / TMEM / TMA (sm_100a).
+//
+// Reference semantics: engine.c:533-563 (CPU batched prefill) and the
+// reference GPU kernel k_attn_flash_prefill (inference/cuda/cuda_kernels.cu:602-655):
+// B query tokens at positions pos_start..pos_start+B-1; token b (q row
+// q + b*q_stride + hh*head_dim) attends keys 0..pos_start+b of kv head
+// hh*n_kv/n_heads; out has q's layout.  Optional qwen35 sigmoid output gate
+// (engine.c:958-960).
+//
+// One CTA = one (query head, 128-row query tile).  Warps:
+//   0-3  softmax: thread i owns query row i = TMEM lane i.  Loads the fp32 Q
+//        tile once (-> fp16, SWIZZLE_128B K-major in smem), then per key block
+//        reads S from TMEM, applies the causal mask and the online softmax
+//        (log2 domain; the running max only moves when it grows by more than
+//        2^8, so O in TMEM is rarely rescaled), and writes P to smem as two
+//        fp16 planes P_hi + P_lo (P_lo = fp16(p - P_hi)), which keeps P to
+//        ~22 bits instead of fp16's 11.
+//   4    TMA for K blocks, 6 TMA for V blocks: separate two-stage rings, so K
+//        of block j+2 loads as soon as S(j) is done (not after PV(j)).
+//   5    MMA: one thread issues S(j) = Q K(j)^T into two alternating TMEM S
+//        buffers (the tensor core computes S(j+1) while softmax works on S(j))
+//        and O += P_hi V + P_lo V into one TMEM accumulator; tcgen05.commit
+//        signals the mbarriers.
+// Keys past the end of the cache are zero-filled by TMA and masked.
+#include "common.cuh"
+#include "tcgen05.cuh"
+
+#include <cudaTypedefs.h>
+
+namespace yattn {
+namespace {
+
+constexpr int BM = 128;
+constexpr int KST = 2;
+constexpr int kPThreads = 224;
+
+template <int HD> struct PCfg {
+    static constexpr int BN = (HD >= 256) ? 64 : 128;
+    static constexpr int Q_BYTES = BM * HD * 2;
+    static constexpr int KV_BYTES = BN * HD * 2;            // one K (or V) block
+    static constexpr int P_BYTES = BM * BN * 2;             // one P plane
+    static constexpr int OFF_Q = 0;
+    static constexpr int OFF_K = OFF_Q + Q_BYTES;
+    static constexpr int OFF_V = OFF_K + KST * KV_BYTES;
+    static constexpr int OFF_P = OFF_V + KST * KV_BYTES;    // P_hi, then P_lo
+    static constexpr int OFF_BAR = OFF_P + 2 * P_BYTES;
+    static constexpr int SMEM = OFF_BAR + 256 + 1024;        // + barriers, + alignment slack
+    static constexpr uint32_t TMEM_COLS = 512;
+    static constexpr uint32_t COL_S = 0;                     // two S buffers: [0, BN), [BN, 2BN)
+    static constexpr uint32_t COL_O = 2 * BN;
+    static_assert(2 * BN + HD <= 512, "TMEM columns");
+    static_assert(SMEM <= 232448, "shared memory");
+};
+
+struct PrefillParams {
+    const float* q;
+    float* out;
+    const float* gate;
+    uint32_t q_stride, pos_start, B, n_heads, n_kv;
+    float scale_log2;
+    int* status;
+};
+
+struct Bars {
+    uint64_t k_full[KST], k_empty[KST], v_full[KST], v_empty[KST];
+    uint64_t s_full[2], s_free[2], p_full, pv_done, q_full, mma_drain;
+    uint32_t tmem_base;
+    int abort_flag;
+};
+
+// One TMA producer: block j of a K or V stream into a KST-deep ring.
+template <int HD>
+__device__ __forceinline__ void produce(const CUtensorMap* map, uint8_t* ring, uint64_t* full, uint64_t* empty,
+                                        uint32_t kvh, uint32_t nkb, int* status, volatile int* abort_flag) {
+    using C = PCfg<HD>;
+    constexpr int BN = C::BN;
+    prefetch_tensormap(map);
+    uint32_t issued = 0;
+    for (uint32_t j = 0; j < nkb; ++j) {
+        const int s = j % KST;
+        if (j >= static_cast<uint32_t>(KST) &&
+            !mbar_wait_bounded(&empty[s], ((j / KST) & 1u) ^ 1u, status, ST_PREFILL_TIMEOUT, abort_flag))
+            break;
+        mbar_arrive_expect_tx(&full[s], C::KV_BYTES);
+#pragma unroll
+        for (int c = 0; c < HD / 64; ++c)
+            tma_load_2d(ring + s * C::KV_BYTES + c * BN * 128, map, static_cast<int32_t>(kvh * HD + c * 64),
+                        static_cast<int32_t>(j * BN), &full[s]);
+        issued = j + 1;
+    }
+    // no load may still be landing when the CTA exits
+    volatile int dummy = 0;
+    for (uint32_t j = (issued > static_cast<uint32_t>(KST) ? issued - KST : 0); j < issued; ++j)
+        mbar_wait_bounded(&full[j % KST], (j / KST) & 1u, status, ST_PREFILL_TIMEOUT, &dummy);
+}
+
+__device__ __forceinline__ uint32_t h2_bits(__half2 h) { return *reinterpret_cast<uint32_t*>(&h); }
+
+template <int HD>
+__global__ void __launch_bounds__(kPThreads, 1)
+    k_prefill(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV, const PrefillParams p) {
+    using C = PCfg<HD>;
+    constexpr int BN = C::BN;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t* sQ = smem + C::OFF_Q;
+    uint8_t* sK = smem + C::OFF_K;
+    uint8_t* sV = smem + C::OFF_V;
+    uint8_t* sPh = smem + C::OFF_P;
+    uint8_t* sPl = sPh + C::P_BYTES;
+    Bars* bars = reinterpret_cast<Bars*>(smem + C::OFF_BAR);
+    volatile int* abort_flag = &bars->abort_flag;
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const uint32_t hh = blockIdx.x;
+    const uint32_t qt = gridDim.y - 1 - blockIdx.y;          // heaviest tiles first
+    const uint32_t kvh = hh * p.n_kv / p.n_heads;
+    const uint32_t row0 = qt * BM;
+    const uint32_t rows_valid = min(static_cast<uint32_t>(BM), p.B - row0);
+    const uint32_t qpos0 = p.pos_start + row0;
+    const uint32_t kmax = qpos0 + rows_valid - 1;
+    const uint32_t nkb = kmax / BN + 1;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < KST; ++s) {
+            mbar_init(&bars->k_full[s], 1);
+            mbar_init(&bars->k_empty[s], 1);
+            mbar_init(&bars->v_full[s], 1);
+            mbar_init(&bars->v_empty[s], 1);
+        }
+        for (int s = 0; s < 2; ++s) {
+            mbar_init(&bars->s_full[s], 1);
+            mbar_init(&bars->s_free[s], 4);
+        }
+        mbar_init(&bars->p_full, 4);
+        mbar_init(&bars->pv_done, 1);
+        mbar_init(&bars->q_full, 4);
+        mbar_init(&bars->mma_drain, 1);
+        bars->abort_flag = 0;
+        fence_mbar_init();
+    }
+    if (warp == 0) tmem_alloc(&bars->tmem_base, C::TMEM_COLS);
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = bars->tmem_base;
+
+    if (warp == 4) {
+        if (lane == 0) produce<HD>(&tmK, sK, bars->k_full, bars->k_empty, kvh, nkb, p.status, abort_flag);
+    } else if (warp == 6) {
+        if (lane == 0) produce<HD>(&tmV, sV, bars->v_full, bars->v_empty, kvh, nkb, p.status, abort_flag);
+    } else if (warp == 5) {
+        // ================= MMA issuer =================
+        if (lane == 0) {
+            constexpr uint32_t IDESC_QK = idesc_f16(BM, BN, 0);
+            constexpr uint32_t IDESC_PV = idesc_f16(BM, HD, 1);
+            bool ok = mbar_wait_bounded(&bars->q_full, 0, p.status, ST_PREFILL_TIMEOUT, abort_flag);
+            tc_fence_after();
+            auto do_pv = [&](uint32_t jj) -> bool {
+                const int s = jj % KST;
+                if (!mbar_wait_bounded(&bars->p_full, jj & 1u, p.status, ST_PREFILL_TIMEOUT, abort_flag) ||
+                    !mbar_wait_bounded(&bars->v_full[s], (jj / KST) & 1u, p.status, ST_PREFILL_TIMEOUT, abort_flag))
+                    return false;
+                tc_fence_after();
+#pragma unroll
+                for (int plane = 0; plane < 2; ++plane) {
+                    const uint8_t* sP = plane ? sPl : sPh;
+#pragma unroll
+                    for (int kk = 0; kk < BN / 16; ++kk) {
+                        const uint64_t a = sdesc_sw128(sP + (kk >> 2) * (BM * 128) + (kk & 3) * 32, 16, 1024);
+                        const uint64_t b = sdesc_sw128(sV + s * C::KV_BYTES + kk * 16 * 128, BN * 128, 1024);
+                        umma_f16(tmem + C::COL_O, a, b, IDESC_PV, (jj > 0 || plane > 0 || kk > 0) ? 1u : 0u);
+                    }
+                }
+                umma_commit(&bars->v_empty[s]);
+                umma_commit(&bars->pv_done);
+                return true;
+            };
+            for (uint32_t j = 0; ok && j < nkb; ++j) {
+                const int s = j % KST;
+                if (!mbar_wait_bounded(&bars->k_full[s], (j / KST) & 1u, p.status, ST_PREFILL_TIMEOUT, abort_flag))
+                    break;
+                const uint32_t sb = j & 1u;
+                if (j >= 2 &&
+                    !mbar_wait_bounded(&bars->s_free[sb], ((j >> 1) & 1u) ^ 1u, p.status, ST_PREFILL_TIMEOUT,
+                                       abort_flag))
+                    break;
+                tc_fence_after();
+#pragma unroll
+                for (int kk = 0; kk < HD / 16; ++kk) {
+                    const uint64_t a = sdesc_sw128(sQ + (kk >> 2) * (BM * 128) + (kk & 3) * 32, 16, 1024);
+                    const uint64_t b = sdesc_sw128(sK + s * C::KV_BYTES + (kk >> 2) * (BN * 128) + (kk & 3) * 32, 16,
+                                                   1024);
+                    umma_f16(tmem + C::COL_S + sb * BN, a, b, IDESC_QK, kk > 0 ? 1u : 0u);
+                }
+                umma_commit(&bars->s_full[sb]);
+                umma_commit(&bars->k_empty[s]);
+                if (j >= 1 && !do_pv(j - 1)) {
+                    ok = false;
+                    break;
+                }
+            }
+            if (ok && !*abort_flag) do_pv(nkb - 1);
+            // drain: every MMA issued so far completes before TMEM is freed
+            umma_commit(&bars->mma_drain);
+            volatile int dummy = 0;
+            mbar_wait_bounded(&bars->mma_drain, 0, p.status, ST_PREFILL_TIMEOUT, &dummy);
+        }
+    } else {
+        // ================= softmax warps 0-3 =================
+        const int r = threadIdx.x;                                   // row of the tile
+        // ---- Q tile: fp32 -> fp16, swizzled K-major ----
+        constexpr int C4 = HD / 4;
+        for (int idx = threadIdx.x; idx < BM * C4; idx += 128) {
+            const int row = idx / C4, col = (idx % C4) * 4;
+            const uint32_t b = row0 + row;
+            float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (b < p.B)
+                v = *reinterpret_cast<const float4*>(p.q + static_cast<size_t>(b) * p.q_stride +
+                                                     static_cast<size_t>(hh) * HD + col);
+            uint2 pk;
+            pk.x = h2_bits(__floats2half2_rn(v.x, v.y));
+            pk.y = h2_bits(__floats2half2_rn(v.z, v.w));
+            *reinterpret_cast<uint2*>(sQ + sw128_offset(row, col, BM)) = pk;
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bars->q_full);
+
+        const uint32_t trow = tmem + (static_cast<uint32_t>(warp * 32) << 16);
+        const uint32_t qpos = qpos0 + r;
+        float m_run = -INFINITY, l_run = 0.f;
+        bool ok = true;
+        for (uint32_t j = 0; j < nkb; ++j) {
+            const uint32_t sb = j & 1u;
+            if (!warp_wait_bounded(&bars->s_full[sb], (j >> 1) & 1u, p.status, ST_PREFILL_TIMEOUT, abort_flag)) {
+                ok = false;
+                break;
+            }
+            tc_fence_after();
+            float sv[BN];
+#pragma unroll
+            for (int c = 0; c < BN / 32; ++c) {
+                uint32_t rr[32];
+                tmem_ld32(trow + C::COL_S + sb * BN + c * 32, rr);
+                tmem_wait_ld();
+#pragma unroll
+                for (int i = 0; i < 32; ++i) sv[c * 32 + i] = __uint_as_float(rr[i]);
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&bars->s_free[sb]);
+            // ---- mask, scale, row max ----
+            const uint32_t kbase = j * BN;
+            const bool diag = kbase + BN - 1 > qpos0;
+            float mx = -INFINITY;
+#pragma unroll
+            for (int c = 0; c < BN; ++c) {
+                float x = sv[c] * p.scale_log2;
+                if (diag && kbase + c > qpos) x = -INFINITY;
+                sv[c] = x;
+                mx = fmaxf(mx, x);
+            }
+            const float m_new = fmaxf(m_run, mx);
+            const bool grow = m_new > m_run + 8.0f;                  // keep a stale max up to 2^8 headroom
+            const float m_use = grow ? m_new : m_run;
+            const float alpha = grow ? ex2_approx(m_run - m_use) : 1.0f;
+            float rs = 0.f;
+#pragma unroll
+            for (int c = 0; c < BN; ++c) {
+                sv[c] = ex2_approx(sv[c] - m_use);
+                rs += sv[c];
+            }
+            l_run = l_run * alpha + rs;
+            m_run = m_use;
+            // ---- PV(j-1) must be finished before P is overwritten and O rescaled ----
+            if (j >= 1) {
+                if (!warp_wait_bounded(&bars->pv_done, (j - 1) & 1u, p.status, ST_PREFILL_TIMEOUT, abort_flag)) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                if (__any_sync(0xffffffffu, grow)) {
+#pragma unroll 1
+                    for (int c = 0; c < HD / 32; ++c) {
+                        uint32_t rr[32];
+                        tmem_ld32(trow + C::COL_O + c * 32, rr);
+                        tmem_wait_ld();
+#pragma unroll
+                        for (int i = 0; i < 32; ++i) rr[i] = __float_as_uint(__uint_as_float(rr[i]) * alpha);
+                        tmem_st32(trow + C::COL_O + c * 32, rr);
+                    }
+                    tmem_wait_st();
+                }
+            }
+            // ---- P row -> smem as P_hi + P_lo (fp16 each, swizzled K-major) ----
+#pragma unroll
+            for (int c = 0; c < BN; c += 8) {
+                uint4 hi, lo;
+                uint32_t* hp = &hi.x;
+                uint32_t* lp = &lo.x;
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    const float a = sv[c + 2 * e], b = sv[c + 2 * e + 1];
+                    const __half2 h = __floats2half2_rn(a, b);
+                    const float2 hf = __half22float2(h);
+                    hp[e] = h2_bits(h);
+                    lp[e] = h2_bits(__floats2half2_rn(a - hf.x, b - hf.y));
+                }
+                const uint32_t off = sw128_offset(r, c, BM);
+                *reinterpret_cast<uint4*>(sPh + off) = hi;
+                *reinterpret_cast<uint4*>(sPl + off) = lo;
+            }
+            fence_proxy_async_smem();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&bars->p_full);
+        }
+        // ---- epilogue: O / l (x sigmoid(gate)) -> out ----
+        if (ok && warp_wait_bounded(&bars->pv_done, (nkb - 1) & 1u, p.status, ST_PREFILL_TIMEOUT, abort_flag)) {
+            tc_fence_after();
+            const uint32_t b = row0 + r;
+            const float inv_l = 1.0f / l_run;
+#pragma unroll 1
+            for (int c = 0; c < HD / 32; ++c) {
+                uint32_t rr[32];
+                tmem_ld32(trow + C::COL_O + c * 32, rr);
+                tmem_wait_ld();
+                if (b < p.B) {
+                    float* dst = p.out + static_cast<size_t>(b) * p.q_stride + static_cast<size_t>(hh) * HD + c * 32;
+                    const float* g = p.gate ? p.gate + static_cast<size_t>(b) * p.q_stride +
+                                                   static_cast<size_t>(hh) * HD + c * 32
+                                            : nullptr;
+#pragma unroll
+                    for (int i = 0; i < 32; i += 4) {
+                        float4 o;
+                        o.x = __uint_as_float(rr[i]) * inv_l;
+                        o.y = __uint_as_float(rr[i + 1]) * inv_l;
+                        o.z = __uint_as_float(rr[i + 2]) * inv_l;
+                        o.w = __uint_as_float(rr[i + 3]) * inv_l;
+                        if (g) {
+                            o.x *= 1.0f / (1.0f + __expf(-g[i]));
+                            o.y *= 1.0f / (1.0f + __expf(-g[i + 1]));
+                            o.z *= 1.0f / (1.0f + __expf(-g[i + 2]));
+                            o.w *= 1.0f / (1.0f + __expf(-g[i + 3]));
+                        }
+                        *reinterpret_cast<float4*>(dst + i) = o;
+                    }
+                }
+            }
+        }
+        tc_fence_before();
+    }
+    __syncthreads();
+    tc_fence_after();
+    if (warp == 0) tmem_dealloc(tmem, C::TMEM_COLS);
+}
+
+// ------------------------------------------------------------------ host side
+
+PFN_cuTensorMapEncodeTiled_v12000 get_encode(char* err, size_t errlen) {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    if (fn) return fn;
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q{};
+    cudaError_t e = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q);
+    if (e != cudaSuccess || q != cudaDriverEntryPointSuccess || !ptr) {
+        set_err(err, errlen, "prefill: cuTensorMapEncodeTiled unavailable (%s)", cudaGetErrorString(e));
+        return nullptr;
+    }
+    fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+    return fn;
+}
+
+// 2-D map over a cache layer: rows of kv_dim fp16, n_rows rows; box 64 x box_rows, 128B swizzle.
+int make_kv_map(CUtensorMap* map, const void* base, uint32_t kv_dim, uint32_t n_rows, uint32_t box_rows, char* err,
+                size_t errlen) {
+    auto enc = get_encode(err, errlen);
+    if (!enc) return -1;
+    cuuint64_t dims[2] = {kv_dim, n_rows};
+    cuuint64_t strides[1] = {static_cast<cuuint64_t>(kv_dim) * 2};
+    cuuint32_t box[2] = {64, box_rows};
+    cuuint32_t estr[2] = {1, 1};
+    CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) {
+        set_err(err, errlen, "prefill: cuTensorMapEncodeTiled failed (%d)", static_cast<int>(r));
+        return -1;
+    }
+    return 0;
+}
+
+template <int HD>
+int launch_prefill(const CUtensorMap& mk, const CUtensorMap& mv, const PrefillParams& p, uint32_t n_qtiles,
+                   cudaStream_t st, char* err, size_t errlen) {
+    using C = PCfg<HD>;
+    static bool attr_done[64] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev >= 0 && dev < 64 && !attr_done[dev]) {
+        cudaError_t e = cudaFuncSetAttribute(k_prefill<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
+        if (e != cudaSuccess) {
+            set_err(err, errlen, "prefill: smem attribute (%d bytes): %s", C::SMEM, cudaGetErrorString(e));
+            return -1;
+        }
+        attr_done[dev] = true;
+    }
+    dim3 grid(p.n_heads, n_qtiles);
+    k_prefill<HD><<<grid, kPThreads, C::SMEM, st>>>(mk, mv, p);
+    YATTN_CHECK_LAUNCH(err, errlen, "prefill");
+    return 0;
+}
+
+}  // namespace
+
+int prefill(float* out, const float* q, const uint16_t* kc, const uint16_t* vc, const float* gate,
+            uint32_t pos_start, uint32_t B, uint32_t n_heads, uint32_t n_kv, uint32_t hd, uint32_t kv_dim,
+            uint32_t q_stride, cudaStream_t st, char* err, size_t errlen) {
+    if (!out || !q || !kc || !vc) {
+        set_err(err, errlen, "prefill: null pointer argument");
+        return -1;
+    }
+    if (B == 0) return 0;
+    if (n_heads == 0 || n_kv == 0 || n_kv > n_heads) {
+        set_err(err, errlen, "prefill: bad head counts n_heads=%u n_kv_heads=%u", n_heads, n_kv);
+        return -1;
+    }
+    if (hd != 64 && hd != 128 && hd != 256) {
+        set_err(err, errlen, "prefill: head_dim %u not supported (64/128/256)", hd);
+        return -1;
+    }
+    if (kv_dim < n_kv * hd || (kv_dim % 8) != 0) {
+        set_err(err, errlen, "prefill: kv_dim %u must be >= n_kv_heads*head_dim and a multiple of 8", kv_dim);
+        return -1;
+    }
+    if (q_stride < n_heads * hd || (q_stride % 4) != 0) {
+        set_err(err, errlen, "prefill: q_stride %u must be >= n_heads*head_dim and a multiple of 4", q_stride);
+        return -1;
+    }
+    if ((reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(out) | reinterpret_cast<uintptr_t>(kc) |
+         reinterpret_cast<uintptr_t>(vc)) & 15u) {
+        set_err(err, errlen, "prefill: q, out, kcache and vcache must be 16-byte aligned");
+        return -1;
+    }
+    if (static_cast<uint64_t>(pos_start) + B > 0x7fffffffull) {
+        set_err(err, errlen, "prefill: pos_start + B too large");
+        return -1;
+    }
+    DevCtx* ctx = dev_ctx(err, errlen);
+    if (!ctx) return -1;
+    const uint32_t n_keys = pos_start + B;
+    const uint32_t bn = (hd >= 256) ? 64u : 128u;
+    CUtensorMap mk, mv;
+    if (make_kv_map(&mk, kc, kv_dim, n_keys, bn, err, errlen) || make_kv_map(&mv, vc, kv_dim, n_keys, bn, err, errlen))
+        return -1;
+    PrefillParams p{};
+    p.q = q;
+    p.out = out;
+    p.gate = gate;
+    p.q_stride = q_stride;
+    p.pos_start = pos_start;
+    p.B = B;
+    p.n_heads = n_heads;
+    p.n_kv = n_kv;
+    p.scale_log2 = 1.4426950408889634f / sqrtf(static_cast<float>(hd));
+    p.status = ctx->status;
+    const uint32_t n_qtiles = (B + BM - 1) / BM;
+    switch (hd) {
+        case 64: return launch_prefill<64>(mk, mv, p, n_qtiles, st, err, errlen);
+        case 128: return launch_prefill<128>(mk, mv, p, n_qtiles, st, err, errlen);
+        default: return launch_prefill<256>(mk, mv, p, n_qtiles, st, err, errlen);
+    }
+}
+
+}  // namespace yattn
+
+using namespace yattn;
+
+extern "C" int yattn_attn_prefill(float* att_out, const float* q, const uint16_t* kcache, const uint16_t* vcache,
+                                  const float* gate, uint32_t pos_start, uint32_t B, uint32_t n_heads,
+                                  uint32_t n_kv_heads, uint32_t head_dim, uint32_t kv_dim, uint32_t q_stride,
+                                  void* stream, char* err, size_t errlen) {
+    return prefill(att_out, q, kcache, vcache, gate, pos_start, B, n_heads, n_kv_heads, head_dim, kv_dim, q_stride,
+                   static_cast<cudaStream_t>(stream), err, errlen);
+}
+
+extern "C" void cuda_k_attn_prefill(float* att_out, const float* q, const uint16_t* kcache, const uint16_t* vcache,
+                                    uint32_t pos_start, uint32_t B, uint32_t n_heads, uint32_t n_kv_heads,
+                                    uint32_t head_dim, uint32_t kv_dim, uint32_t q_stride) {
+    char err[256];
+    err[0] = 0;
+    if (prefill(att_out, q, kcache, vcache, nullptr, pos_start, B, n_heads, n_kv_heads, head_dim, kv_dim, q_stride,
+                nullptr, err, sizeof(err)) != 0)
+        set_last_error(err);
+}

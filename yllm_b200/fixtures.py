@@ -12,7 +12,7 @@ import torch
 
 from ._lib import call
 from .attn import _stream
-from .configs import DecodeCfg, PrefillCfg, seed_of
+from .configs import DecodeCfg, GdnCfg, PrefillCfg, seed_of
 
 GEN_F32, GEN_F16, GEN_F32_F16, GEN_F32_BF16 = 0, 1, 2, 3
 
@@ -51,8 +51,9 @@ class DecodeInputs:
     q: torch.Tensor          # [layers, n_seqs, n_heads*hd] f32
     out: torch.Tensor        # same shape
     gate: Optional[torch.Tensor]
-    kv_pool: torch.Tensor    # uint16, per sequence one engine blob [2*layers][ctx_i][kv_dim]
+    kv_pool: torch.Tensor    # uint16, per sequence one engine blob [2*n_layers][ctx_i][kv_dim]
     seq_off: list            # element offset of each sequence's blob in kv_pool
+    n_layers: int            # layers actually built (K regions 0..n-1, V regions n..2n-1)
 
     def k_ptr(self, layer: int, seq: int) -> int:
         c = self.ctx[seq]
@@ -60,7 +61,7 @@ class DecodeInputs:
 
     def v_ptr(self, layer: int, seq: int) -> int:
         c = self.ctx[seq]
-        return self.kv_pool.data_ptr() + 2 * (self.seq_off[seq] + (self.cfg.layers + layer) * c * self.cfg.kv_dim)
+        return self.kv_pool.data_ptr() + 2 * (self.seq_off[seq] + (self.n_layers + layer) * c * self.cfg.kv_dim)
 
     def k_view(self, layer: int, seq: int) -> torch.Tensor:
         c, kd = self.ctx[seq], self.cfg.kv_dim
@@ -69,7 +70,7 @@ class DecodeInputs:
 
     def v_view(self, layer: int, seq: int) -> torch.Tensor:
         c, kd = self.ctx[seq], self.cfg.kv_dim
-        o = self.seq_off[seq] + (self.cfg.layers + layer) * c * kd
+        o = self.seq_off[seq] + (self.n_layers + layer) * c * kd
         return self.kv_pool[o:o + c * kd].view(c, kd)
 
 
@@ -103,7 +104,51 @@ def decode_inputs(cfg: DecodeCfg, layers: Optional[list] = None, seqs: Optional[
             if gate is not None:
                 gen_rows(gate[li, si], GEN_F32_BF16, H * hd, 1, H, hd, seed_of(cfg.cfg, "gate", l, s))
     out = torch.zeros_like(q)
-    return DecodeInputs(cfg, ctx, q, out, gate, pool, offs)
+    return DecodeInputs(cfg, ctx, q, out, gate, pool, offs, L)
+
+
+@dataclass
+class GdnInputs:
+    cfg: GdnCfg
+    n_seqs: int
+    T: int
+    S: torch.Tensor       # [n_seqs, n_vheads, 128, 128] f32
+    q: torch.Tensor       # [n_seqs*T, num_k_heads*128]
+    k: torch.Tensor
+    v: torch.Tensor       # [n_seqs*T, n_vheads*128]
+    gate: torch.Tensor    # [n_seqs*T, n_vheads]
+    beta: torch.Tensor
+    z: torch.Tensor       # [n_seqs*T, n_vheads*128]
+    norm_w: torch.Tensor  # [128]
+    out: torch.Tensor
+
+
+def gdn_inputs(cfg: GdnCfg, n_seqs: int, T: int, seeded_state: bool, device="cuda") -> GdnInputs:
+    """GDN token inputs for n_seqs sequences of T tokens (rows seq*T + t):
+    q,k = l2norm(bf16(N(0,1))), v,z = bf16(N(0,1)), gate = -softplus(N(0,1)),
+    beta = sigmoid(N(0,1)), norm weight 1 + 0.1 N(0,1); state zero or N(0,1)*state_scale."""
+    D, NK, NV = cfg.head_dim, cfg.num_k_heads, cfg.n_v_heads
+    rows = n_seqs * T
+    c = cfg.cfg
+    S = torch.zeros(n_seqs, NV, D, D, dtype=torch.float32, device=device)
+    if seeded_state:
+        gen_rows(S, GEN_F32, D, n_seqs * NV * D, 1, D, seed_of(c, "state"), scale=cfg.state_scale)
+    q = torch.empty(rows, NK * D, dtype=torch.float32, device=device)
+    k = torch.empty_like(q)
+    gen_gdn_qk(q, seed_of(c, "gdn_q"), rows, NK, D, cfg.eps)
+    gen_gdn_qk(k, seed_of(c, "gdn_k"), rows, NK, D, cfg.eps)
+    v = torch.empty(rows, NV * D, dtype=torch.float32, device=device)
+    gen_rows(v, GEN_F32_BF16, NV * D, rows, NV, D, seed_of(c, "gdn_v"))
+    z = torch.empty_like(v)
+    gen_rows(z, GEN_F32_BF16, NV * D, rows, NV, D, seed_of(c, "z"))
+    gate = torch.empty(rows, NV, dtype=torch.float32, device=device)
+    beta = torch.empty_like(gate)
+    gen_gdn_gates(gate, beta, seed_of(c, "gdn_a"), seed_of(c, "gdn_b"))
+    w = torch.empty(D, dtype=torch.float32, device=device)
+    gen_rows(w, GEN_F32, D, 1, 1, D, seed_of(c, "norm_w"), scale=0.1)
+    w += 1.0
+    out = torch.zeros_like(v)
+    return GdnInputs(cfg, n_seqs, T, S, q, k, v, gate, beta, z, w, out)
 
 
 @dataclass
