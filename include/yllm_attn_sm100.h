@@ -171,6 +171,24 @@ int yattn_attn_prefill(float* att_out, const float* q, const uint16_t* kcache,
                        uint32_t n_heads, uint32_t n_kv_heads, uint32_t head_dim, uint32_t kv_dim,
                        uint32_t q_stride, void* stream, char* err, size_t errlen);
 
+/* Allocation-free form of yattn_attn_decode.  No counterpart in the reference:
+ * it exists for callers that cannot call cudaMalloc while decoding (a serving
+ * loop held to a device-memory budget fixed up front, or a host thread that
+ * must not re-enter the allocator) and cannot hand the library a workspace.
+ * The split-KV scratch lives in a fixed 4 MiB static device array that every
+ * GPU loading this library holds until exit; a query whose split partials do
+ * not fit (many splits at head_dim 256 with 8 query heads per kv head) is
+ * rejected with an error naming the bytes needed.  The first call on a device
+ * looks up the array's device address (no allocation), so make that first
+ * call before any stream capture.  Every call on a device shares the array and
+ * clears what must start at zero; calls that overlap on the GPU (other
+ * streams or host threads) race on it and must be serialised by the caller.
+ * Same arguments, results and errors as yattn_attn_decode otherwise. */
+int yattn_attn_decode_noalloc(float* att_out, const float* q, const uint16_t* kcache,
+                              const uint16_t* vcache, const float* gate, uint32_t pos,
+                              uint32_t n_heads, uint32_t n_kv_heads, uint32_t head_dim,
+                              uint32_t kv_dim, void* stream, char* err, size_t errlen);
+
 /* Pre-allocates the per-device workspace the drop-in entry points use, so no
  * allocation happens inside a decode step (the shim's bind-time workspace). */
 int yattn_reserve(size_t bytes, char* err, size_t errlen);

@@ -1,0 +1,74 @@
+"""The allocation-free decode entry point, yattn_attn_decode_noalloc.
+
+It serves callers that cannot call cudaMalloc while decoding (a fixed device
+memory budget, or an allocator that must not be re-entered from the decode
+thread): its split-KV scratch is a static device array inside the library.
+This file is collected last so a failure here leaves every other test run.
+"""
+import ctypes as C
+
+import numpy as np
+import pytest
+import torch
+
+import oracle
+
+pytestmark = pytest.mark.gpu
+
+
+def _noalloc(out, q, k, v, gate, pos, H, KV, hd, kd, stream):
+    from yllm_b200._lib import call
+
+    call("yattn_attn_decode_noalloc", out.data_ptr(), q.data_ptr(), k.data_ptr(), v.data_ptr(),
+         gate.data_ptr() if gate is not None else None, pos, H, KV, hd, kd, stream)
+
+
+def _case(dev, H, KV, hd, T, seed, gated=False):
+    rng = np.random.default_rng(seed)
+    kd = KV * hd
+    q = torch.from_numpy(rng.standard_normal(H * hd).astype(np.float32)).to(dev)
+    k = oracle.f32_to_f16(rng.standard_normal(T * kd).astype(np.float32))
+    v = oracle.f32_to_f16(rng.standard_normal(T * kd).astype(np.float32))
+    tk = torch.from_numpy(k.view(np.int16)).to(dev).view(torch.uint16)
+    tv = torch.from_numpy(v.view(np.int16)).to(dev).view(torch.uint16)
+    gate = torch.from_numpy(rng.standard_normal(H * hd).astype(np.float32)).to(dev) if gated else None
+    return q, tk, tv, gate, kd
+
+
+@pytest.mark.parametrize("H,KV,hd,T,gated", [
+    (32, 8, 128, 20000, False),   # many splits: scratch partials + merge counters in use
+    (14, 2, 64, 512, False),      # Qwen2.5-0.5B decode shape
+    (16, 2, 256, 3000, True),     # qwen35 gated attention
+    (8, 2, 128, 20, False),       # one split: no partials
+])
+def test_noalloc_decode_matches_allocating_entry(H, KV, hd, T, gated):
+    from yllm_b200 import attn
+
+    assert torch.cuda.is_available(), "GPU tests need a CUDA device"
+    dev = torch.device("cuda:0")
+    torch.cuda.set_device(dev)
+    q, k, v, gate, kd = _case(dev, H, KV, hd, T, seed=H + T, gated=gated)
+    stream = torch.cuda.current_stream().cuda_stream
+    ref = torch.zeros(H * hd, device=dev)
+    attn.attn_decode(ref, q, k, v, T - 1, H, KV, hd, kd, gate=gate)
+    outs = []
+    for _ in range(2):   # the second call reuses the static scratch left by the first
+        out = torch.full((H * hd,), float("nan"), device=dev)
+        _noalloc(out, q, k, v, gate, T - 1, H, KV, hd, kd, stream)
+        outs.append(out)
+    torch.cuda.synchronize()
+    want = ref.cpu().numpy()
+    for out in outs:
+        oracle.assert_close(out.cpu().numpy(), want, what=f"noalloc H{H} KV{KV} hd{hd} T{T}")
+
+
+def test_noalloc_rejects_scratch_overflow():
+    from yllm_b200._lib import YattnError
+
+    dev = torch.device("cuda:0")
+    H, KV, hd, T = 16, 2, 256, 131072
+    q = torch.zeros(H * hd, device=dev)
+    k = torch.zeros(T * KV * hd, dtype=torch.uint16, device=dev)
+    out = torch.zeros(H * hd, device=dev)
+    with pytest.raises(YattnError, match="static scratch"):
+        _noalloc(out, q, k, k, None, T - 1, H, KV, hd, KV * hd, torch.cuda.current_stream().cuda_stream)

@@ -21,6 +21,7 @@
 #include "common.cuh"
 
 #include <algorithm>
+#include <mutex>
 #include <vector>
 
 namespace yattn {
@@ -780,4 +781,112 @@ extern "C" void cuda_k_attn_decode(float* att_out, const float* q, const uint16_
     if (decode_single(att_out, q, kcache, vcache, nullptr, 0, pos + 1, n_heads, n_kv_heads, head_dim, kv_dim,
                       nullptr, nullptr, nullptr, 0, nullptr, err, sizeof(err)) != 0)
         set_last_error(err);
+}
+
+// ------------------------------------------------------- allocation-free decode
+//
+// Some callers cannot call cudaMalloc at the point where they decode: a
+// serving loop that runs under a fixed device-memory budget carved out up
+// front, a host whose allocator must not be re-entered from the decode thread,
+// or a C caller that owns every buffer and has no way to hand the library a
+// workspace.  For them, yattn_attn_decode_noalloc keeps the split-KV scratch
+// (per-split (m, l, o) partials, the merge counters and a status word) in the
+// fixed array below, which every GPU that loads the library holds until exit.
+// The array is shared by every call on a device: calls that overlap on the GPU
+// (different streams, or host threads) race on it and must be serialised by
+// the caller.
+
+namespace {
+
+constexpr size_t kNoAllocScratchBytes = 4u << 20;   // 4 MiB per device
+constexpr size_t kNoAllocHeader = 256;              // status word, then 256-aligned counters + partials
+
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
+
+// Device address of g_noalloc_scratch, looked up once per device.  In host
+// code the symbol itself is only a host-side stand-in, never a device address.
+void* g_noalloc_addr[64];
+std::mutex g_noalloc_mu;
+
+void* noalloc_scratch(int dev, char* err, size_t errlen) {
+    std::lock_guard<std::mutex> lk(g_noalloc_mu);
+    if (!g_noalloc_addr[dev]) {
+        void* ptr = nullptr;
+        cudaError_t e = cudaGetSymbolAddress(&ptr, g_noalloc_scratch);
+        if (e != cudaSuccess || !ptr) {
+            set_err(err, errlen, "decode_noalloc: cudaGetSymbolAddress of the static scratch failed: %s",
+                    cudaGetErrorString(e));
+            return nullptr;
+        }
+        g_noalloc_addr[dev] = ptr;
+    }
+    return g_noalloc_addr[dev];
+}
+
+}  // namespace
+
+extern "C" int yattn_attn_decode_noalloc(float* att_out, const float* q, const uint16_t* kcache,
+                                         const uint16_t* vcache, const float* gate, uint32_t pos, uint32_t n_heads,
+                                         uint32_t n_kv_heads, uint32_t head_dim, uint32_t kv_dim, void* stream,
+                                         char* err, size_t errlen) {
+    if (check_geom(n_heads, n_kv_heads, head_dim, kv_dim, err, errlen)) return -1;
+    if (!att_out || !q || !kcache || !vcache) {
+        set_err(err, errlen, "decode_noalloc: null pointer argument");
+        return -1;
+    }
+    if (!aligned16(kcache) || !aligned16(vcache) || !aligned16(q)) {
+        set_err(err, errlen, "decode_noalloc: q, kcache and vcache must be 16-byte aligned");
+        return -1;
+    }
+    int dev = -1;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) {
+        set_err(err, errlen, "decode_noalloc: no usable CUDA device");
+        return -1;
+    }
+    // The split schedule is the one yattn_attn_decode uses, so both give the same result.
+    const uint32_t ntok = pos + 1;
+    const uint32_t gmax = gmax_of(n_heads, n_kv_heads);
+    const uint32_t split = auto_split(static_cast<uint64_t>(ntok) * n_kv_heads, static_cast<uint32_t>(dev_num_sms()) * 4);
+    const uint32_t ns = (ntok + split - 1) / split;
+    const size_t need = ns > 1 ? ws_bytes_for(ns * n_kv_heads, n_kv_heads, gmax, head_dim) : 0;
+    if (need > kNoAllocScratchBytes - kNoAllocHeader) {
+        set_err(err, errlen,
+                "decode_noalloc: this query needs %zu bytes of split-KV scratch, more than the %zu-byte static "
+                "scratch (%u splits x %u kv heads x %u q heads x head_dim %u); use yattn_attn_decode",
+                need, kNoAllocScratchBytes - kNoAllocHeader, ns, n_kv_heads, gmax, head_dim);
+        return -1;
+    }
+    // First call on a device: looks up the scratch address (no allocation).
+    uint8_t* base = static_cast<uint8_t*>(noalloc_scratch(dev, err, errlen));
+    if (!base) return -1;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    DecodeParams p{};
+    p.item0.q = q;
+    p.item0.out = att_out;
+    p.item0.k = kcache;
+    p.item0.v = vcache;
+    p.item0.gate = gate;
+    p.item0.pos = pos;
+    p.split_len = split;
+    p.n_splits0 = ns;
+    p.t_base = 0;
+    p.t_end0 = ntok;
+    p.n_heads = n_heads;
+    p.n_kv = n_kv_heads;
+    p.kv_dim = kv_dim;
+    p.scale_log2 = 1.4426950408889634f / sqrtf(static_cast<float>(head_dim));
+    p.status = reinterpret_cast<int*>(base);
+    // The array keeps the previous call's contents: the status word and the merge
+    // counters must start at zero, the partials are fully rewritten before use.
+    size_t clear = sizeof(int);
+    if (ns > 1) {
+        carve_ws(base + kNoAllocHeader, ns * n_kv_heads, n_kv_heads, gmax, p);
+        clear = kNoAllocHeader + static_cast<size_t>(n_kv_heads) * sizeof(uint32_t);
+    }
+    cudaError_t e = cudaMemsetAsync(base, 0, clear, st);
+    if (e != cudaSuccess) {
+        set_err(err, errlen, "decode_noalloc: clearing the scratch failed: %s", cudaGetErrorString(e));
+        return -1;
+    }
+    return launch_decode(p, head_dim, ns * n_kv_heads, st, err, errlen);
 }
