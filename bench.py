@@ -333,9 +333,258 @@ def run_reference(args) -> None:
     print(json.dumps(line), flush=True)
 
 
+# ------------------------------------------------------- other workloads
+#
+# `--workload` selects one of the other BASELINE configs.  Each prints one line
+# of the same shape; the driver's default (no flag) is config 3 above.
+
+def _timed(fn, args, stream, world, dist, local):
+    """Warm-up, then args.steps calls of fn between CUDA events on the stream
+    (one event pair per call), clocks sampled meanwhile; max over ranks."""
+    import torch
+
+    for _ in range(args.warmup):
+        fn()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    clocks = ClockSampler(local)
+    clocks.start()
+    time.sleep(0.3)
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0.record(stream)
+    for a, b in ev:
+        a.record(stream)
+        fn()
+        b.record(stream)
+    t1.record(stream)
+    torch.cuda.synchronize()
+    clk = clocks.stop()
+    total = torch.tensor([t0.elapsed_time(t1)], device=f"cuda:{local}")
+    if world > 1:
+        dist.all_reduce(total, op=dist.ReduceOp.MAX)
+    per_call = sum(a.elapsed_time(b) for a, b in ev) / len(ev)
+    return float(total.item()) / args.steps, per_call, clk
+
+
+def _line(args, world, metric, value, unit, ms, cfg_dict, roofline, launches, clk, e2e=None, cpu=None,
+          higher=True, scaling="strong"):
+    line = {"metric": metric, "value": round(value, 4), "unit": unit, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(ms, 5), "higher_is_better": higher, "scaling": scaling,
+            "vs_baseline": None, "dtype": "f32 math, fp16 Q/K/V/P hi+lo", "data": "synthetic (seeded)",
+            "config": cfg_dict, "e2e": e2e, "roofline": roofline, "gpu_launches": launches,
+            "clocks": {"sm_mhz": clk["sm_mhz"], "sm_max_mhz": clk["sm_max_mhz"], "reasons": clk["reasons"]}}
+    if cpu is not None:
+        line["cpu_baseline"] = cpu
+    return line
+
+
+def run_prefill(args, gated: bool) -> None:
+    import torch
+    import torch.distributed as dist
+
+    from yllm_b200 import attn, dist as ydist, fixtures
+    from yllm_b200.configs import CFG2, CFG5_GATED_PREFILL
+
+    cfg = CFG5_GATED_PREFILL if gated else CFG2
+    rank, world, local = ydist.init("nccl" if args.gpus > 1 else "gloo")
+    torch.cuda.set_device(local)
+    stream = torch.cuda.current_stream()
+    S, H, hd = cfg.seq_len, cfg.n_heads, cfg.head_dim
+    p = fixtures.prefill_inputs(cfg)
+    r0, r1 = ydist.causal_row_split(S, world, rank)
+    B = r1 - r0
+    qs = H * hd
+
+    def step():
+        if B > 0:
+            attn.attn_prefill(p.out[r0:r1], p.q[r0:r1], p.k, p.v, r0, B, H, cfg.n_kv_heads, hd, cfg.kv_dim, qs,
+                              gate=p.gate[r0:r1] if p.gate is not None else None, stream=stream)
+
+    ms, per_call, clk = _timed(step, args, stream, world, dist, local)
+    flops = cfg.causal_flops()
+    my_flops = 4.0 * hd * H * sum(r + 1 for r in range(r0, r1))
+    e2e = None
+    if not args.no_e2e:
+        qh = torch.empty(B * qs, dtype=torch.float32, pin_memory=True)
+        qh.copy_(p.q[r0:r1].reshape(-1).cpu())
+        kh = torch.empty(r1 * cfg.kv_dim, dtype=torch.uint16, pin_memory=True)
+        kh.copy_(p.k[:r1].reshape(-1).cpu())
+        vh = torch.empty_like(kh)
+        vh.copy_(p.v[:r1].reshape(-1).cpu())
+        oh = torch.empty(B * qs, dtype=torch.float32, pin_memory=True)
+
+        def e2e_step():
+            p.q[r0:r1].view(-1).copy_(qh, non_blocking=True)
+            p.k[:r1].view(-1).copy_(kh, non_blocking=True)
+            p.v[:r1].view(-1).copy_(vh, non_blocking=True)
+            step()
+            oh.copy_(p.out[r0:r1].view(-1), non_blocking=True)
+
+        ems, _, _ = _timed(e2e_step, args, stream, world, dist, local)
+        nb = B * qs * 4
+        e2e = {"value": round(flops / (ems / 1e3) / 1e12, 3), "unit": "TFLOP/s",
+               "h2d_bytes_per_step": int((nb + 2 * r1 * cfg.kv_dim * 2) * world), "d2h_bytes_per_step": int(nb * world)}
+    peaks, src = load_peaks()
+    achieved = my_flops / (per_call / 1e3) / 1e12
+    roof = {"bound": "tensor", "achieved": round(achieved, 1), "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
+            "frac": round(achieved / peaks["bf16_tflops"], 4), "traffic": None,
+            "kernel": f"k_prefill<{hd}>", "peak_source": src + " (dense bf16 burst)"}
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu = cpu_prefill_rate(cfg, args.cpu_budget)
+    if rank == 0:
+        print(json.dumps(_line(args, world, "prefill attn TFLOP/s (causal, counted causal FLOPs)",
+                               flops / (ms / 1e3) / 1e12, "TFLOP/s", ms,
+                               {"workload": cfg.name, "seq_len": S, "n_heads": H, "n_kv_heads": cfg.n_kv_heads,
+                                "head_dim": hd, "gated": gated, "flops": flops,
+                                "parallelism": f"query rows split x{world} (equal causal work)",
+                                "l2": "whole working set fits L2 (config size); no flush"},
+                               roof, args.steps, clk, e2e, cpu)), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def cpu_prefill_rate(cfg, budget_s: float) -> dict:
+    """Reference CPU prefill (oracle/_ref) on the last 128 query rows, scaled to
+    the whole causal prefill by FLOP count."""
+    sys.path.insert(0, str(ROOT / "tests"))
+    import oracle
+
+    kind = "reference" if oracle.has_ref() else "port"
+    lib = oracle.load("ref" if kind == "reference" else "port")
+    f = oracle.prefill_fixture(cfg, lib=lib)
+    S, H, hd, B = cfg.seq_len, cfg.n_heads, cfg.head_dim, 128
+    times = []
+    while not times or (sum(times) < budget_s and len(times) < 5):
+        t0 = time.perf_counter()
+        oracle.attn_prefill(f["q"][S - B:], f["k"], f["v"], S - B, B, H, cfg.n_kv_heads, hd, cfg.kv_dim, H * hd,
+                            gate=None if f["gate"] is None else f["gate"][S - B:], lib=lib)
+        times.append(time.perf_counter() - t0)
+    sample_flops = 4.0 * hd * H * sum(r + 1 for r in range(S - B, S))
+    rate = sample_flops / statistics.median(times)
+    return {"value": round(rate / 1e12, 6), "unit": "TFLOP/s", "cores": int(lib.orc_max_threads()), "kind": kind,
+            "sample": f"last {B} rows of the {S}-token prefill (keys 0..{S - 1}), {len(times)} runs; "
+                      f"rate = sample FLOPs / time"}
+
+
+def run_gdn(args, decode: bool) -> None:
+    import torch
+    import torch.distributed as dist
+
+    from yllm_b200 import attn, dist as ydist, fixtures
+    from yllm_b200.configs import CFG5_GDN as c
+
+    rank, world, local = ydist.init("nccl" if args.gpus > 1 else "gloo")
+    torch.cuda.set_device(local)
+    stream = torch.cuda.current_stream()
+    D, NK, NV = c.head_dim, c.num_k_heads, c.n_v_heads
+    if decode:
+        s0, s1 = ydist.split_range(c.batch, world, rank)
+        n = s1 - s0
+        g = fixtures.gdn_inputs(c, c.batch, 1, seeded_state=True)
+        S, q, k, v, o = g.S[s0:s1], g.q[s0:s1], g.k[s0:s1], g.v[s0:s1], g.out[s0:s1]
+        gt, bt, z = g.gate[s0:s1], g.beta[s0:s1], g.z[s0:s1]
+
+        def step():
+            if n:
+                attn.gdn_decode(S, o, q, k, v, gt, bt, n, NK, D, NV, D, norm_w=g.norm_w, z=z, eps=c.eps,
+                                stream=stream)
+        ms, per_call, clk = _timed(step, args, stream, world, dist, local)
+        nbytes = c.batch * NV * D * D * 4 * 2
+        mine = n * NV * D * D * 4 * 2
+        peaks, src = load_peaks()
+        ach = mine / (per_call / 1e3) / 1e9
+        roof = {"bound": "hbm", "achieved": round(ach, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                "frac": round(ach / peaks["hbm_gbs"], 4), "traffic": None, "kernel": "k_gdn_decode",
+                "peak_source": src}
+        if rank == 0:
+            print(json.dumps(_line(args, world, "GDN batch-32 decode tok/s (state read+write)",
+                                   c.batch / (ms / 1e3), "tok/s", ms,
+                                   {"workload": c.name + "-decode-b32", "n_v_heads": NV, "num_k_heads": NK,
+                                    "head_dim": D, "batch": c.batch, "state_bytes_per_step": nbytes,
+                                    "parallelism": f"sequences x{world}", "l2": "state 134 MB > L2"},
+                                   roof, args.steps, clk)), flush=True)
+    else:
+        T = c.tokens
+        g = fixtures.gdn_inputs(c, 1, T, seeded_state=False)
+
+        def step():
+            attn.gdn_prefill(g.S, g.out, g.q, g.k, g.v, g.gate, g.beta, 1, T, NK, D, NV, D, norm_w=g.norm_w,
+                             z=g.z, eps=c.eps, stream=stream)
+        ms, per_call, clk = _timed(step, args, stream, world, dist, local)
+        flops = T * NV * 7.0 * D * D
+        peaks, src = load_peaks()
+        ach = flops / (per_call / 1e3) / 1e12
+        roof = {"bound": "tensor", "achieved": round(ach, 2), "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
+                "frac": round(ach / peaks["bf16_tflops"], 4), "traffic": None, "kernel": "k_gdn_prefill",
+                "peak_source": src + " (dense bf16 burst)"}
+        if rank == 0:
+            print(json.dumps(_line(args, world, "GDN 4096-token prefill TFLOP/s (recurrent-equivalent FLOPs)",
+                                   flops / (ms / 1e3) / 1e12, "TFLOP/s", ms,
+                                   {"workload": c.name + "-prefill-4096", "n_v_heads": NV, "num_k_heads": NK,
+                                    "head_dim": D, "tokens": T, "flops": flops, "parallelism": "1 GPU"},
+                                   roof, args.steps, clk)), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def run_long_decode(args) -> None:
+    """Config 4: one 131072-key decode, key range split over the ranks, per-rank
+    (m, l, o) partials all-gathered over NCCL and merged on every GPU."""
+    import torch
+    import torch.distributed as dist
+
+    from yllm_b200 import attn, dist as ydist, fixtures
+    from yllm_b200.configs import CFG4 as c
+
+    rank, world, local = ydist.init("nccl" if args.gpus > 1 else "gloo")
+    torch.cuda.set_device(local)
+    stream = torch.cuda.current_stream()
+    d = fixtures.decode_inputs(c)
+    n = d.ctx[0]
+    k0, k1 = ydist.split_range(n, world, rank)
+    H, hd = c.n_heads, c.head_dim
+    ml = torch.zeros(H, 2, device=f"cuda:{local}")
+    o = torch.zeros(H, hd, device=f"cuda:{local}")
+    out = d.out[0, 0]
+    kv, vv = d.k_view(0, 0), d.v_view(0, 0)
+
+    def step():
+        if world == 1:
+            attn.attn_decode(out, d.q[0, 0], kv, vv, n - 1, H, c.n_kv_heads, hd, c.kv_dim, stream=stream)
+        else:
+            attn.decode_partial(ml, o, d.q[0, 0], kv, vv, k0, k1, H, c.n_kv_heads, hd, c.kv_dim, stream=stream)
+            ydist.allgather_merge_partials(ml, o, out, H, hd)
+
+    ms, per_call, clk = _timed(step, args, stream, world, dist, local)
+    nbytes = n * c.kv_dim * 2 * 2
+    peaks, src = load_peaks()
+    ach = nbytes / (ms / 1e3) / 1e9
+    roof = {"bound": "hbm", "achieved": round(ach, 1), "peak": peaks["hbm_gbs"] * world, "unit": "GB/s",
+            "frac": round(ach / (peaks["hbm_gbs"] * world), 4), "traffic": None,
+            "kernel": "k_decode<128,4> (+ NCCL all-gather + merge at N>1)", "peak_source": src + f" x{world} GPUs"}
+    if rank == 0:
+        print(json.dumps(_line(args, world, "long-context decode GB/s (131072 keys, one layer)", ach, "GB/s", ms,
+                               {"workload": c.name, "ctx": n, "n_heads": H, "n_kv_heads": c.n_kv_heads,
+                                "head_dim": hd, "kv_bytes": nbytes,
+                                "parallelism": f"split-KV x{world}, NCCL all-gather of (m,l,o) + LSE merge",
+                                "l2": "KV 537 MB > L2"},
+                               roof, args.steps, clk)), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--workload", default="decode",
+                    choices=["decode", "prefill", "gated_prefill", "gdn_prefill", "gdn_decode", "long_decode"],
+                    help="decode = BASELINE config 3 (the default bench line)")
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
@@ -350,8 +599,14 @@ def main() -> None:
         args.warmup = 3
     if args.impl == "reference":
         run_reference(args)
-    else:
+    elif args.workload == "decode":
         run_ours(args)
+    elif args.workload in ("prefill", "gated_prefill"):
+        run_prefill(args, gated=args.workload == "gated_prefill")
+    elif args.workload in ("gdn_prefill", "gdn_decode"):
+        run_gdn(args, decode=args.workload == "gdn_decode")
+    else:
+        run_long_decode(args)
 
 
 if __name__ == "__main__":

@@ -97,8 +97,11 @@ typedef struct YattnDecodeItem {
     uint32_t reserved;
 } YattnDecodeItem;
 
-/* One CTA of work: keys [t_begin, t_end) of one (item, kv_head).  Filled by
- * yattn_decode_plan; opaque to callers apart from its size. */
+/* One CTA of work: keys [t_begin, t_end) of one item for a group of kv heads
+ * (kv_head is the group's first head; a group is the largest of 8/4/2/1 heads
+ * dividing n_kv_heads, at most 4 for head_dim 256, so one token's K row of the
+ * group is one contiguous copy).  Filled by yattn_decode_plan; opaque to
+ * callers apart from its size. */
 typedef struct YattnDecodeWork {
     uint32_t item;
     uint16_t kv_head;
@@ -106,18 +109,19 @@ typedef struct YattnDecodeWork {
     uint32_t split;
     uint32_t t_begin;
     uint32_t t_end;
-    uint32_t part_base;   /* first partial slot of this (item, kv_head); unused if n_splits == 1 */
-    uint32_t group;       /* merge counter of this (item, kv_head); unused if n_splits == 1 */
+    uint32_t part_base;   /* first partial slot of this (item, head group); unused if n_splits == 1 */
+    uint32_t group;       /* merge counter of this (item, head group); unused if n_splits == 1 */
     uint32_t reserved;
 } YattnDecodeWork;
 
 /* Host-side schedule.  pos_host[n_items] are the items' query positions.
  * split_tokens = 0 picks a split length that gives about target_ctas work
- * units (target_ctas = 0: 4 per SM of the current device).  Writes up to
+ * units (target_ctas = 0: one per SM of the current device).  Writes up to
  * work_cap entries to work_host (host memory).  The schedule depends only on
- * the positions, so one plan serves every layer of a decode step. */
+ * the positions and the head geometry, so one plan serves every layer of a
+ * decode step. */
 int yattn_decode_plan(const uint32_t* pos_host, uint32_t n_items, uint32_t n_kv_heads,
-                      uint32_t split_tokens, uint32_t target_ctas,
+                      uint32_t head_dim, uint32_t split_tokens, uint32_t target_ctas,
                       YattnDecodeWork* work_host, uint32_t work_cap,
                       uint32_t* n_work, uint32_t* n_parts, uint32_t* n_groups,
                       char* err, size_t errlen);

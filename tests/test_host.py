@@ -46,7 +46,16 @@ def test_struct_layout_matches_header(tmp_path):
     assert c == YattnDecodeItem.pos.offset and d == YattnDecodeWork.part_base.offset
 
 
-def _plan(pos, n_kv, split=0, target=592):
+def heads_per_cta(n_kv, hd):
+    """The library's kv-head grouping: largest of 8/4/2/1 (4 at head_dim 256) dividing n_kv."""
+    cap = 4 if hd >= 256 else 8
+    hc = cap
+    while hc > 1 and n_kv % hc:
+        hc //= 2
+    return hc
+
+
+def _plan(pos, n_kv, hd=128, split=0, target=592):
     from yllm_b200._lib import YattnDecodeWork, lib
 
     pos = np.asarray(pos, dtype=np.uint32)
@@ -54,36 +63,40 @@ def _plan(pos, n_kv, split=0, target=592):
     work = (YattnDecodeWork * cap)()
     nw, npart, ng = C.c_uint32(), C.c_uint32(), C.c_uint32()
     err = C.create_string_buffer(256)
-    rc = lib.yattn_decode_plan(pos.ctypes.data_as(C.POINTER(C.c_uint32)), pos.size, n_kv, split, target, work,
-                               cap, C.byref(nw), C.byref(npart), C.byref(ng), err, 256)
+    rc = lib.yattn_decode_plan(pos.ctypes.data_as(C.POINTER(C.c_uint32)), pos.size, n_kv, hd, split, target,
+                               work, cap, C.byref(nw), C.byref(npart), C.byref(ng), err, 256)
     assert rc == 0, err.value
     return [work[i] for i in range(nw.value)], npart.value, ng.value
 
 
-@pytest.mark.parametrize("pos,n_kv,split", [
-    ([511], 2, 0), ([0], 8, 0), ([131071], 8, 0), ([4095] * 32, 2, 0),
-    ([1023, 8191, 5000, 1, 77], 8, 0), ([300, 301, 5], 4, 64),
+@pytest.mark.parametrize("pos,n_kv,hd,split", [
+    ([511], 2, 64, 0), ([0], 8, 128, 0), ([131071], 8, 128, 0), ([4095] * 32, 2, 256, 0),
+    ([1023, 8191, 5000, 1, 77], 8, 128, 0), ([300, 301, 5], 4, 128, 64), ([700, 9], 6, 128, 128),
+    ([1000], 8, 256, 0), ([2000, 5], 3, 64, 0),
 ])
-def test_decode_plan_covers_every_key_once(pos, n_kv, split):
-    work, n_parts, n_groups = _plan(pos, n_kv, split)
+def test_decode_plan_covers_every_key_once(pos, n_kv, hd, split):
+    hc = heads_per_cta(n_kv, hd)
+    work, n_parts, n_groups = _plan(pos, n_kv, hd, split)
     seen = {}
-    parts, groups = set(), set()
+    parts, groups = [], set()
     for w in work:
+        assert w.kv_head % hc == 0
         key = (w.item, w.kv_head)
         assert 0 <= w.t_begin < w.t_end <= pos[w.item] + 1
         seen.setdefault(key, []).append((w.t_begin, w.t_end, w.split, w.n_splits))
         if w.n_splits > 1:
-            parts.add(w.part_base + w.split)
+            for h in range(hc):   # one partial slot per (kv head of the group, split)
+                parts.append(w.part_base + h * w.n_splits + w.split)
             groups.add(w.group)
     for i, p in enumerate(pos):
-        for h in range(n_kv):
-            segs = sorted(seen[(i, h)])
+        for kg in range(n_kv // hc):
+            segs = sorted(seen[(i, kg * hc)])
             assert segs[0][0] == 0 and segs[-1][1] == p + 1
             for a, b in zip(segs, segs[1:]):
                 assert a[1] == b[0]
             assert sorted(s[2] for s in segs) == list(range(len(segs)))
             assert all(s[3] == len(segs) for s in segs)
-    assert parts == set(range(n_parts)) and groups == set(range(n_groups))
+    assert sorted(parts) == list(range(n_parts)) and groups == set(range(n_groups))
     lens = [w.t_end - w.t_begin for w in work]
     assert lens == sorted(lens, reverse=True)
 
@@ -95,10 +108,12 @@ def test_plan_rejects_bad_args():
     nw, npart, ng = C.c_uint32(), C.c_uint32(), C.c_uint32()
     pos = (C.c_uint32 * 1)(10)
     work = (YattnDecodeWork * 1)()
-    rc = lib.yattn_decode_plan(pos, 1, 0, 0, 1, work, 1, C.byref(nw), C.byref(npart), C.byref(ng), err, 256)
+    rc = lib.yattn_decode_plan(pos, 1, 0, 128, 0, 1, work, 1, C.byref(nw), C.byref(npart), C.byref(ng), err, 256)
     assert rc == -1 and b"bad arguments" in err.value
+    rc = lib.yattn_decode_plan(pos, 1, 8, 96, 0, 1, work, 1, C.byref(nw), C.byref(npart), C.byref(ng), err, 256)
+    assert rc == -1 and b"head_dim 96" in err.value
     pos = (C.c_uint32 * 1)(100000)
-    rc = lib.yattn_decode_plan(pos, 1, 8, 64, 1, work, 1, C.byref(nw), C.byref(npart), C.byref(ng), err, 256)
+    rc = lib.yattn_decode_plan(pos, 1, 8, 128, 64, 1, work, 1, C.byref(nw), C.byref(npart), C.byref(ng), err, 256)
     assert rc == -1 and b"work_cap" in err.value and nw.value > 1
 
 

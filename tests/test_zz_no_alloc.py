@@ -66,7 +66,8 @@ def test_noalloc_rejects_scratch_overflow():
     from yllm_b200._lib import YattnError
 
     dev = torch.device("cuda:0")
-    H, KV, hd, T = 16, 2, 256, 131072
+    # head_dim 256, 8 query heads per kv head, 8 kv heads: ~74 splits x 8 heads of 8 KB partials > 4 MiB
+    H, KV, hd, T = 64, 8, 256, 32768
     q = torch.zeros(H * hd, device=dev)
     k = torch.zeros(T * KV * hd, dtype=torch.uint16, device=dev)
     out = torch.zeros(H * hd, device=dev)

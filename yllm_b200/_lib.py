@@ -74,7 +74,7 @@ PROTOS = {
     "cuda_k_store_kv_batch": (None, [vp, vp, vp, vp, u32, u32, u32]),
     "yattn_decode_plan": (
         C.c_int,
-        [C.POINTER(u32), u32, u32, u32, u32, C.POINTER(YattnDecodeWork), u32,
+        [C.POINTER(u32), u32, u32, u32, u32, u32, C.POINTER(YattnDecodeWork), u32,
          C.POINTER(u32), C.POINTER(u32), C.POINTER(u32), *E],
     ),
     "yattn_decode_workspace_bytes": (sz, [u32, u32, u32, u32, u32]),

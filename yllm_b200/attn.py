@@ -145,8 +145,8 @@ class DecodePlan:
             work = (YattnDecodeWork * cap)()
             n_work, n_parts, n_groups = C.c_uint32(), C.c_uint32(), C.c_uint32()
             err = C.create_string_buffer(512)
-            rc = lib.yattn_decode_plan(pos.ctypes.data_as(C.POINTER(C.c_uint32)), n, n_kv_heads, split_tokens,
-                                       target_ctas, work, cap, C.byref(n_work), C.byref(n_parts),
+            rc = lib.yattn_decode_plan(pos.ctypes.data_as(C.POINTER(C.c_uint32)), n, n_kv_heads, head_dim,
+                                       split_tokens, target_ctas, work, cap, C.byref(n_work), C.byref(n_parts),
                                        C.byref(n_groups), err, 512)
             if rc == 0:
                 break

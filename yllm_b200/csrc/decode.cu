@@ -5,19 +5,21 @@
 // query head hh, kv head hh*n_kv/n_heads, scores q.k_t / sqrt(d) over t=0..pos,
 // softmax, out = sum p_t v_t.
 //
-// Design (B200): one CTA = one (item, kv_head, key split).
-//   * warp 4 (producer) streams the split's K and V rows into a 4-stage shared
-//     memory ring with cp.async.bulk (TMA, non-tensor) completing on mbarriers;
-//   * warps 0-3 (consumers) each take 8 of the 32 tokens of a stage.  The kv
-//     head's query group (<= 8 heads) sits in registers, each lane owning
-//     head_dim/32 dims.  Per-lane partial dot products for (token, head) pairs
-//     are summed across the warp with a transpose-reduce (31 shuffles per 32
-//     sums, lane l ends with sum l), the online softmax runs in the log2
-//     domain, and p.V accumulates in registers with packed fp32 FMAs;
-//   * the 4 warps' (m, l, o) are merged in shared memory; a split writes its
-//     partial to the workspace and the last split of a (item, kv_head) to
+// Design (B200): one CTA = one (item, group of HC kv heads, key split).
+//   * the producer warp streams the split's K and V rows into a shared-memory
+//     ring with cp.async.bulk (TMA, non-tensor), one bulk copy per token row
+//     covering the HC kv heads' contiguous slices (2 KB for Llama-3-8B), rows
+//     padded by 16 B in shared memory for conflict-free ldmatrix;
+//   * each consumer warp owns one kv head of the group and 16 tokens of every
+//     stage and runs both products on the tensor cores with mma.sync m16n8k16
+//     in the transposed form S^T = K Q^T and O^T += V^T P^T (tokens / dims on
+//     M, the <= 8 query heads of the kv head on N).  q and p are split into
+//     fp16 hi + lo parts, so the products keep ~22 bits against the engine's
+//     fp32 loop; K and V are the cache's fp16 values, exact.  The online
+//     softmax runs in the log2 domain with warp-shuffle max/sum;
+//   * the warps' (m, l, o) are merged in shared memory; a split writes its
+//     partials to the workspace and the last split of an (item, head group) to
 //     arrive (atomic counter) merges all splits with log-sum-exp weights.
-// All math is fp32 (fp16 K/V converted exactly), like the reference.
 #include "common.cuh"
 
 #include <algorithm>
@@ -27,38 +29,47 @@
 namespace yattn {
 namespace {
 
-constexpr int kTok = 32;            // tokens per stage
-constexpr int kConsumers = 4;       // consumer warps
-constexpr int kThreads = 32 * (kConsumers + 1);
+constexpr int kSplitQuant = 64;     // split lengths are multiples of this
 
+// Per head_dim: NCW consumer warps, ring of NST stages sized for the worst case (HC = 1).
 template <int HD> struct DecodeCfg {
-    static constexpr int DPL = HD / 32;                    // dims per lane
-    static constexpr int ROWB = HD * 2;                    // bytes of one K (or V) row slice
-    static constexpr int NST = (HD >= 256) ? 3 : 4;        // pipeline stages
-    static constexpr int STAGEB = 2 * kTok * ROWB;         // K tile + V tile
+    static constexpr int NCW = (HD >= 256) ? 4 : 8;
+    static constexpr int THREADS = 32 * (NCW + 1);
+    static constexpr int STAGE_MAX = 2 * 16 * NCW * (HD * 2 + 16);   // K + V tiles at HC = 1
+    static constexpr int NST = (HD <= 64) ? 5 : 3;
+    static constexpr int PT_BYTES = 2 * 8 * 48;                       // per warp: P^T hi and lo, 8 heads x 16 tokens
 };
+
+// Kv heads per CTA for a geometry: the largest of 8/4/2/1 (at most NCW) dividing n_kv.
+__host__ __device__ inline uint32_t heads_per_cta(uint32_t n_kv, uint32_t hd) {
+    const uint32_t cap = hd >= 256 ? 4u : 8u;
+    for (uint32_t hc = cap; hc > 1; hc >>= 1)
+        if (n_kv % hc == 0) return hc;
+    return 1;
+}
 
 struct DecodeParams {
     const YattnDecodeItem* items;
     const YattnDecodeWork* work;      // nullptr: single item, uniform splits (see below)
     YattnDecodeItem item0;            // used when work == nullptr
     uint32_t split_len;               // uniform split length when work == nullptr
-    uint32_t n_splits0;               // splits per kv head when work == nullptr
+    uint32_t n_splits0;               // splits per head group when work == nullptr
     uint32_t t_base;                  // key offset when work == nullptr
     uint32_t t_end0;                  // end key (exclusive) when work == nullptr
-    uint32_t n_heads, n_kv, kv_dim;
+    uint32_t n_heads, n_kv, kv_dim, hc;
     float scale_log2;                 // log2(e) / sqrt(head_dim)
     float* part_ml;                   // [n_parts][G][2]
     float* part_o;                    // [n_parts][G][HD]
     uint32_t* counters;               // [n_groups]
     int* status;
-    int partial_only;                 // write (m,l,o) for the whole work unit, never merge
+    int partial_only;                 // write the merged (m, l, o) instead of out
+    int defer_merge;                  // splits only write partials; k_merge_splits merges them
     float* out_ml;                    // partial_only: [n_heads][2]
     float* out_o;                     // partial_only: [n_heads][HD]
 };
 
-__device__ __forceinline__ void group_of(uint32_t kvh, uint32_t n_heads, uint32_t n_kv, uint32_t& first,
-                                         uint32_t& cnt) {
+__host__ __device__ __forceinline__ void group_of(uint32_t kvh, uint32_t n_heads, uint32_t n_kv, uint32_t& first,
+                                                  uint32_t& cnt) {
     // heads hh with hh*n_kv/n_heads == kvh: ceil(kvh*n_heads/n_kv) .. ceil((kvh+1)*n_heads/n_kv)-1
     uint32_t a = (kvh * n_heads + n_kv - 1) / n_kv;
     uint32_t b = ((kvh + 1) * n_heads + n_kv - 1) / n_kv;
@@ -66,63 +77,80 @@ __device__ __forceinline__ void group_of(uint32_t kvh, uint32_t n_heads, uint32_
     cnt = b - a;
 }
 
-template <int V>
-__device__ __forceinline__ void transpose_reduce(float (&a)[V], int lane) {
-    // Sum a[i] over the warp; afterwards a[0] holds sum #(lane >> (5 - log2 V))
-    // for V <= 32 (replicated over the low lanes).
-    static_assert(V == 8 || V == 16 || V == 32, "V");
-    constexpr int LOGV = (V == 8) ? 3 : (V == 16) ? 4 : 5;
-    int c = V;
-#pragma unroll
-    for (int step = 0; step < LOGV; ++step) {
-        const int off = 16 >> step;
-        const bool up = (lane & off) != 0;
-        c >>= 1;
-#pragma unroll
-        for (int j = 0; j < V / 2; ++j) {
-            if (j < c) {
-                float send = up ? a[j] : a[j + c];
-                float keep = up ? a[j + c] : a[j];
-                a[j] = keep + __shfl_xor_sync(0xffffffffu, send, off);
-            }
-        }
-    }
-#pragma unroll
-    for (int off = 16 >> LOGV; off >= 1; off >>= 1) a[0] += __shfl_xor_sync(0xffffffffu, a[0], off);
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t (&r)[4]) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"(addr));
+}
+__device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t (&r)[4]) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"(addr));
+}
+__device__ __forceinline__ void ldsm_x2(uint32_t addr, uint32_t& r0, uint32_t& r1) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x2.shared.b16 {%0,%1}, [%2];" : "=r"(r0), "=r"(r1) : "r"(addr));
+}
+// D(16x8 f32) += A(16x16 f16, row) * B(16x8 f16, col)
+__device__ __forceinline__ void mma16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
 
+__device__ __forceinline__ uint32_t pack_h2(float a, float b) {
+    __half2 h = __floats2half2_rn(a, b);
+    return *reinterpret_cast<uint32_t*>(&h);
+}
+// x = hi + lo with hi = fp16(x), lo = fp16(x - hi): about 22 significant bits in two fp16s.
+__device__ __forceinline__ void split_h2(float a, float b, uint32_t& hi, uint32_t& lo) {
+    const __half2 h = __floats2half2_rn(a, b);
+    const float2 f = __half22float2(h);
+    hi = *reinterpret_cast<const uint32_t*>(&h);
+    lo = pack_h2(a - f.x, b - f.y);
+}
+
+// Warp NCW is the producer; consumer warp w owns kv head kg*HC + (w % HC) of
+// the group and tokens [16*(w / HC), +16) of every stage (TOK = 16*NCW/HC tokens).
+// Per 16-token step, on the legacy tensor cores (mma.sync m16n8k16, fp32 accumulate):
+//   S^T (16 tok x 8 heads) = K (16 x HD) . Q^T (HD x 8),  q = q_hi + q_lo in fp16
+//   O^T (HD x 8 heads)    += V^T (HD x 16) . P^T (16 x 8), p = p_hi + p_lo in fp16
 template <int HD, int G>
-__global__ void __launch_bounds__(kThreads, 2) k_decode(const DecodeParams p) {
+__global__ void __launch_bounds__(DecodeCfg<HD>::THREADS, 1) k_decode(const DecodeParams p) {
     using C = DecodeCfg<HD>;
-    constexpr int DPL = C::DPL;
-    constexpr int GP = (G <= 1) ? 1 : (G <= 2) ? 2 : (G <= 4) ? 4 : 8;   // padded group
-    constexpr int TR = (GP == 8) ? 4 : 8;                                 // tokens per reduce round
-    constexpr int NR = 8 / TR;                                            // rounds per warp share
-    constexpr int V = TR * GP;                                            // values per lane per round
-    constexpr int REP = (V < 32) ? ((V == 16) ? 1 : 2) : 0;               // replicated low lane bits
-    constexpr int TB = ((GP == 1) ? 0 : (GP == 2) ? 1 : (GP == 4) ? 2 : 3) + REP;   // first token bit
+    constexpr int NCW = C::NCW;
+    constexpr int KS = HD / 16;                                       // k-steps (QK) and m-tiles (PV)
+    static_assert(G <= 8, "query group fits the MMA's 8 columns");
 
     extern __shared__ __align__(1024) uint8_t smem[];
     uint8_t* stages = smem;
-    uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::NST * C::STAGEB);
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::NST * C::STAGE_MAX);
     uint64_t* empty = full + C::NST;
-    float* sp = reinterpret_cast<float*>(empty + C::NST);       // [4][32] probabilities
-    float* salpha = sp + kConsumers * 32;                        // [4][8]
-    float* mrg_ml = salpha + kConsumers * 8;                     // [4][G][2]
-    volatile int* abort_flag = reinterpret_cast<volatile int*>(mrg_ml + kConsumers * G * 2);
+    uint8_t* pt_all = reinterpret_cast<uint8_t*>(empty + C::NST);    // [NCW][PT_BYTES]
+    float* mrg_ml = reinterpret_cast<float*>(pt_all + NCW * C::PT_BYTES);   // [NCW][G][2]
+    uint32_t* s_gfirst = reinterpret_cast<uint32_t*>(mrg_ml + NCW * G * 2); // [8]
+    uint32_t* s_gcnt = s_gfirst + 8;                                  // [8]
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(s_gcnt + 8);
     int* last_flag = const_cast<int*>(abort_flag) + 1;
-    float* mrg_o = reinterpret_cast<float*>(stages);             // [4][G][HD], aliases the ring after use
+    float* mrg_o = reinterpret_cast<float*>(stages);                 // [NCW][G][HD], aliases the ring after use
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
+    const uint32_t HC = p.hc;
+    const uint32_t TOK = 16u * NCW / HC;
+    const uint32_t ROWB = HC * HD * 2;                                // bytes of one row copy (HC heads)
+    const uint32_t RS = ROWB + 16;                                    // smem row stride
+    const uint32_t TILEB = TOK * RS;
+    const uint32_t STAGEB = 2 * TILEB;
 
     // ---- work unit ----
     YattnDecodeItem it;
-    uint32_t kvh, t0, t1, n_splits, split, part_base, group;
+    uint32_t kg, t0, t1, n_splits, split, part_base, group;
     if (p.work) {
         const YattnDecodeWork w = p.work[blockIdx.x];
         it = p.items[w.item];
-        kvh = w.kv_head;
+        kg = w.kv_head / HC;
         t0 = w.t_begin;
         t1 = w.t_end;
         n_splits = w.n_splits;
@@ -131,34 +159,33 @@ __global__ void __launch_bounds__(kThreads, 2) k_decode(const DecodeParams p) {
         group = w.group;
     } else {
         it = p.item0;
-        kvh = blockIdx.x / p.n_splits0;
+        kg = blockIdx.x / p.n_splits0;
         split = blockIdx.x % p.n_splits0;
         n_splits = p.n_splits0;
         t0 = p.t_base + split * p.split_len;
         t1 = min(t0 + p.split_len, p.t_end0);
-        part_base = kvh * p.n_splits0;
-        group = kvh;
+        part_base = kg * HC * p.n_splits0;
+        group = kg;
     }
-    uint32_t gfirst, gcnt;
-    group_of(kvh, p.n_heads, p.n_kv, gfirst, gcnt);
     const uint32_t ntok = t1 - t0;
-    const uint32_t ntiles = (ntok + kTok - 1) / kTok;
+    const uint32_t ntiles = (ntok + TOK - 1) / TOK;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < C::NST; ++s) {
             mbar_init(&full[s], 1);
-            mbar_init(&empty[s], kConsumers);
+            mbar_init(&empty[s], NCW);
         }
+        for (uint32_t hl = 0; hl < HC; ++hl) group_of(kg * HC + hl, p.n_heads, p.n_kv, s_gfirst[hl], s_gcnt[hl]);
         abort_flag[0] = 0;
         last_flag[0] = 0;
         fence_mbar_init();
     }
     __syncthreads();
 
-    if (warp == kConsumers) {
-        // ================= producer =================
-        const uint16_t* kb = it.k + static_cast<size_t>(kvh) * HD;
-        const uint16_t* vb = it.v + static_cast<size_t>(kvh) * HD;
+    if (warp == NCW) {
+        // ================= producer: one bulk copy per row per tensor =================
+        const uint16_t* kb = it.k + static_cast<size_t>(kg) * HC * HD;
+        const uint16_t* vb = it.v + static_cast<size_t>(kg) * HC * HD;
         uint32_t issued = 0;
         for (uint32_t i = 0; i < ntiles; ++i) {
             const int s = i % C::NST;
@@ -167,16 +194,16 @@ __global__ void __launch_bounds__(kThreads, 2) k_decode(const DecodeParams p) {
                                        abort_flag))
                     break;
             }
-            const uint32_t tile0 = t0 + i * kTok;
-            const uint32_t nrows = min(static_cast<uint32_t>(kTok), t1 - tile0);
-            uint8_t* kdst = stages + s * C::STAGEB;
-            uint8_t* vdst = kdst + kTok * C::ROWB;
-            if (lane == 0) mbar_arrive_expect_tx(&full[s], 2u * nrows * C::ROWB);
+            const uint32_t tile0 = t0 + i * TOK;
+            const uint32_t nrows = min(TOK, t1 - tile0);
+            uint8_t* kdst = stages + s * STAGEB;
+            uint8_t* vdst = kdst + TILEB;
+            if (lane == 0) mbar_arrive_expect_tx(&full[s], 2u * nrows * ROWB);
             __syncwarp();
             for (uint32_t r = lane; r < nrows; r += 32) {
                 const size_t off = static_cast<size_t>(tile0 + r) * p.kv_dim;
-                bulk_g2s(kdst + r * C::ROWB, kb + off, C::ROWB, &full[s]);
-                bulk_g2s(vdst + r * C::ROWB, vb + off, C::ROWB, &full[s]);
+                bulk_g2s(kdst + r * RS, kb + off, ROWB, &full[s]);
+                bulk_g2s(vdst + r * RS, vb + off, ROWB, &full[s]);
             }
             issued = i + 1;
         }
@@ -189,187 +216,192 @@ __global__ void __launch_bounds__(kThreads, 2) k_decode(const DecodeParams p) {
     }
 
     // ================= consumers =================
-    // query group in registers: lane owns dims [lane*DPL, lane*DPL + DPL)
-    float qr[G][DPL];
+    const uint32_t hl = warp % HC;                 // head within the group
+    const uint32_t sl = warp / HC;                 // 16-token slice of each stage
+    const uint32_t gfirst = s_gfirst[hl], gcnt = s_gcnt[hl];
+    const int g8 = lane >> 2;                      // fragment row group: token (S^T), dim (O^T), head (B)
+    const int t4 = lane & 3;                       // fragment column pair: heads 2*t4, 2*t4+1
+    // Q^T as the MMA B operand: b0 = q[head g8][16kk + 2t4 .. +1], b1 = q[head g8][16kk + 2t4 + 8 .. +9]
+    uint32_t qhi[KS][2], qlo[KS][2];
+    {
+        const bool hv = static_cast<uint32_t>(g8) < gcnt;
+        const float* qh = it.q + static_cast<size_t>(gfirst + (hv ? g8 : 0)) * HD;
 #pragma unroll
-    for (int g = 0; g < G; ++g) {
-#pragma unroll
-        for (int d = 0; d < DPL; ++d) qr[g][d] = 0.f;
-        if (static_cast<uint32_t>(g) < gcnt) {
-            const float* qh = it.q + static_cast<size_t>(gfirst + g) * HD + lane * DPL;
-            if constexpr (DPL == 4) {
-                float4 t = *reinterpret_cast<const float4*>(qh);
-                qr[g][0] = t.x; qr[g][1] = t.y; qr[g][2] = t.z; qr[g][3] = t.w;
-            } else if constexpr (DPL == 8) {
-                float4 t0v = *reinterpret_cast<const float4*>(qh);
-                float4 t1v = *reinterpret_cast<const float4*>(qh + 4);
-                qr[g][0] = t0v.x; qr[g][1] = t0v.y; qr[g][2] = t0v.z; qr[g][3] = t0v.w;
-                qr[g][4] = t1v.x; qr[g][5] = t1v.y; qr[g][6] = t1v.z; qr[g][7] = t1v.w;
-            } else {
-                float2 t = *reinterpret_cast<const float2*>(qh);
-                qr[g][0] = t.x; qr[g][1] = t.y;
+        for (int kk = 0; kk < KS; ++kk) {
+            float2 x0 = make_float2(0.f, 0.f), x1 = make_float2(0.f, 0.f);
+            if (hv) {
+                x0 = *reinterpret_cast<const float2*>(qh + kk * 16 + 2 * t4);
+                x1 = *reinterpret_cast<const float2*>(qh + kk * 16 + 2 * t4 + 8);
             }
+            split_h2(x0.x, x0.y, qhi[kk][0], qlo[kk][0]);
+            split_h2(x1.x, x1.y, qhi[kk][1], qlo[kk][1]);
         }
     }
-    float oacc[G][DPL];
+    float oc[KS][4];
 #pragma unroll
-    for (int g = 0; g < G; ++g)
-#pragma unroll
-        for (int d = 0; d < DPL; ++d) oacc[g][d] = 0.f;
-
-    // this lane's (token, head) slot after the transpose-reduce
-    const int idx = lane >> REP;
-    const int my_t = idx / GP;
-    const int my_g = idx % GP;
-    float m_mine = -INFINITY, l_mine = 0.f;
-    float* spw = sp + warp * 32;
-    float* saw = salpha + warp * 8;
+    for (int mt = 0; mt < KS; ++mt) oc[mt][0] = oc[mt][1] = oc[mt][2] = oc[mt][3] = 0.f;
+    float m_a = -INFINITY, m_b = -INFINITY, l_a = 0.f, l_b = 0.f;    // heads 2*t4 and 2*t4+1
+    uint8_t* pt = pt_all + warp * C::PT_BYTES;
+    const uint32_t pt_u = smem_u32(pt);
+    // ldmatrix lane addresses relative to the warp's 16-row slice of a tile
+    const uint32_t slice = (16 * sl) * RS + hl * HD * 2;
+    const uint32_t a_off = slice + ((lane & 7) + ((lane >> 3) & 1) * 8) * RS + ((lane >> 4) & 1) * 16;   // K
+    const uint32_t v_off = slice + ((lane & 7) + ((lane >> 4) & 1) * 8) * RS + ((lane >> 3) & 1) * 16;   // V^T
+    const uint32_t p_off = (lane & 7) * 48 + ((lane >> 3) & 1) * 16;                                     // P^T
 
     for (uint32_t i = 0; i < ntiles; ++i) {
         const int s = i % C::NST;
         if (!warp_wait_bounded(&full[s], (i / C::NST) & 1u, p.status, ST_DECODE_FULL_TIMEOUT, abort_flag)) break;
-        const uint32_t nrows = min(static_cast<uint32_t>(kTok), t1 - (t0 + i * kTok));
-        const int nvalid = max(0, min(8, static_cast<int>(nrows) - warp * 8));
-        const uint8_t* kt = stages + s * C::STAGEB + warp * 8 * C::ROWB;
-        const uint8_t* vt = kt + kTok * C::ROWB;
+        const uint32_t nrows = min(TOK, t1 - (t0 + i * TOK));
+        const int nvalid = max(0, min(16, static_cast<int>(nrows) - static_cast<int>(16 * sl)));
+        if (nvalid > 0) {
+            const uint32_t kt = smem_u32(stages + s * STAGEB);
+            const uint32_t vt = kt + TILEB;
+            // ---- S^T = K Q^T ----
+            float sc[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-        for (int rr = 0; rr < NR; ++rr) {
-            const int nv = min(TR, nvalid - rr * TR);
-            if (nv <= 0) break;
-            // ---- partial scores for TR tokens x GP heads ----
-            float part[V];
-#pragma unroll
-            for (int t = 0; t < TR; ++t) {
-                const uint8_t* row = kt + (rr * TR + t) * C::ROWB + lane * DPL * 2;
-                float kf[DPL];
-                if constexpr (DPL == 4) {
-                    uint2 raw = *reinterpret_cast<const uint2*>(row);
-                    float2 a = h2f2(raw.x), b = h2f2(raw.y);
-                    kf[0] = a.x; kf[1] = a.y; kf[2] = b.x; kf[3] = b.y;
-                } else if constexpr (DPL == 8) {
-                    uint4 raw = *reinterpret_cast<const uint4*>(row);
-                    float2 a = h2f2(raw.x), b = h2f2(raw.y), c = h2f2(raw.z), d = h2f2(raw.w);
-                    kf[0] = a.x; kf[1] = a.y; kf[2] = b.x; kf[3] = b.y;
-                    kf[4] = c.x; kf[5] = c.y; kf[6] = d.x; kf[7] = d.y;
-                } else {
-                    uint32_t raw = *reinterpret_cast<const uint32_t*>(row);
-                    float2 a = h2f2(raw);
-                    kf[0] = a.x; kf[1] = a.y;
-                }
-#pragma unroll
-                for (int g = 0; g < GP; ++g) {
-                    float acc = 0.f;
-                    if (g < G) {
-                        float2 a2 = make_float2(0.f, 0.f);
-#pragma unroll
-                        for (int d = 0; d < DPL; d += 2)
-                            a2 = __ffma2_rn(make_float2(qr[g][d], qr[g][d + 1]), make_float2(kf[d], kf[d + 1]), a2);
-                        acc = a2.x + a2.y;
-                    }
-                    part[t * GP + g] = acc;
-                }
+            for (int kk = 0; kk < KS; ++kk) {
+                uint32_t a[4];
+                ldsm_x4(kt + a_off + kk * 32, a);
+                mma16816(sc, a, qhi[kk][0], qhi[kk][1]);
+                mma16816(sc, a, qlo[kk][0], qlo[kk][1]);
             }
-            transpose_reduce<V>(part, lane);
-            // ---- online softmax for this lane's (token, head) ----
-            const bool valid = my_t < nv;
-            const float sc = valid ? part[0] * p.scale_log2 : -INFINITY;
-            float tmax = sc;
+            // sc: [0] = (token g8, head 2t4), [1] = (g8, 2t4+1), [2] = (g8+8, 2t4), [3] = (g8+8, 2t4+1)
+            const bool v0 = g8 < nvalid, v1 = g8 + 8 < nvalid;
+            const float s0 = v0 ? sc[0] * p.scale_log2 : -INFINITY;
+            const float s1 = v0 ? sc[1] * p.scale_log2 : -INFINITY;
+            const float s2 = v1 ? sc[2] * p.scale_log2 : -INFINITY;
+            const float s3 = v1 ? sc[3] * p.scale_log2 : -INFINITY;
+            float mx_a = fmaxf(s0, s2), mx_b = fmaxf(s1, s3);
 #pragma unroll
-            for (int b = TB; b < 5; ++b) tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, 1 << b));
-            const float m_new = fmaxf(m_mine, tmax);
-            const float pv = ex2_approx(sc - m_new);
-            const float alpha = ex2_approx(m_mine - m_new);
-            float psum = pv;
-#pragma unroll
-            for (int b = TB; b < 5; ++b) psum += __shfl_xor_sync(0xffffffffu, psum, 1 << b);
-            l_mine = l_mine * alpha + psum;
-            m_mine = m_new;
-            spw[idx] = pv;
-            if (my_t == 0) saw[my_g] = alpha;
-            __syncwarp();
-            // ---- rescale and accumulate p.V ----
-#pragma unroll
-            for (int g = 0; g < G; ++g) {
-                const float a = saw[g];
-#pragma unroll
-                for (int d = 0; d < DPL; ++d) oacc[g][d] *= a;
+            for (int o = 4; o <= 16; o <<= 1) {
+                mx_a = fmaxf(mx_a, __shfl_xor_sync(0xffffffffu, mx_a, o));
+                mx_b = fmaxf(mx_b, __shfl_xor_sync(0xffffffffu, mx_b, o));
             }
-            for (int t = 0; t < nv; ++t) {
-                const uint8_t* row = vt + (rr * TR + t) * C::ROWB + lane * DPL * 2;
-                float vf[DPL];
-                if constexpr (DPL == 4) {
-                    uint2 raw = *reinterpret_cast<const uint2*>(row);
-                    float2 a = h2f2(raw.x), b = h2f2(raw.y);
-                    vf[0] = a.x; vf[1] = a.y; vf[2] = b.x; vf[3] = b.y;
-                } else if constexpr (DPL == 8) {
-                    uint4 raw = *reinterpret_cast<const uint4*>(row);
-                    float2 a = h2f2(raw.x), b = h2f2(raw.y), c = h2f2(raw.z), d = h2f2(raw.w);
-                    vf[0] = a.x; vf[1] = a.y; vf[2] = b.x; vf[3] = b.y;
-                    vf[4] = c.x; vf[5] = c.y; vf[6] = d.x; vf[7] = d.y;
-                } else {
-                    uint32_t raw = *reinterpret_cast<const uint32_t*>(row);
-                    float2 a = h2f2(raw);
-                    vf[0] = a.x; vf[1] = a.y;
-                }
+            const float mn_a = fmaxf(m_a, mx_a), mn_b = fmaxf(m_b, mx_b);
+            const float al_a = ex2_approx(m_a - mn_a), al_b = ex2_approx(m_b - mn_b);
+            const float p0 = ex2_approx(s0 - mn_a), p1 = ex2_approx(s1 - mn_b);
+            const float p2 = ex2_approx(s2 - mn_a), p3 = ex2_approx(s3 - mn_b);
+            float sum_a = p0 + p2, sum_b = p1 + p3;
 #pragma unroll
-                for (int g = 0; g < G; ++g) {
-                    const float pg = spw[t * GP + g];
-                    const float2 p2 = make_float2(pg, pg);
-#pragma unroll
-                    for (int d = 0; d < DPL; d += 2) {
-                        float2 r = __ffma2_rn(p2, make_float2(vf[d], vf[d + 1]), make_float2(oacc[g][d], oacc[g][d + 1]));
-                        oacc[g][d] = r.x;
-                        oacc[g][d + 1] = r.y;
-                    }
-                }
+            for (int o = 4; o <= 16; o <<= 1) {
+                sum_a += __shfl_xor_sync(0xffffffffu, sum_a, o);
+                sum_b += __shfl_xor_sync(0xffffffffu, sum_b, o);
+            }
+            l_a = l_a * al_a + sum_a;
+            l_b = l_b * al_b + sum_b;
+            m_a = mn_a;
+            m_b = mn_b;
+            // ---- P^T (rows = heads, 16 tokens, 48 B row stride) as fp16 hi and lo planes ----
+            {
+                uint32_t h01, l01, h23, l23;
+                split_h2(p0, p1, h01, l01);      // (token g8: heads 2t4, 2t4+1)
+                split_h2(p2, p3, h23, l23);      // (token g8+8: heads 2t4, 2t4+1)
+                uint16_t* hp = reinterpret_cast<uint16_t*>(pt);
+                uint16_t* lp = reinterpret_cast<uint16_t*>(pt + 384);
+                const int ra = (2 * t4) * 24, rb = (2 * t4 + 1) * 24;   // row offsets in halves
+                hp[ra + g8] = static_cast<uint16_t>(h01);
+                hp[rb + g8] = static_cast<uint16_t>(h01 >> 16);
+                hp[ra + g8 + 8] = static_cast<uint16_t>(h23);
+                hp[rb + g8 + 8] = static_cast<uint16_t>(h23 >> 16);
+                lp[ra + g8] = static_cast<uint16_t>(l01);
+                lp[rb + g8] = static_cast<uint16_t>(l01 >> 16);
+                lp[ra + g8 + 8] = static_cast<uint16_t>(l23);
+                lp[rb + g8 + 8] = static_cast<uint16_t>(l23 >> 16);
             }
             __syncwarp();
+            uint32_t ph0, ph1, pl0, pl1;
+            ldsm_x2(pt_u + p_off, ph0, ph1);
+            ldsm_x2(pt_u + 384 + p_off, pl0, pl1);
+            // ---- O^T = O^T * alpha + V^T P^T ----
+            // V rows past nvalid hold stale (or never written) shared memory: their
+            // p is 0, but 0 * NaN would still poison the MMA, so zero those lanes.
+            // The A fragment holds tokens 2t4, 2t4+1 (a0, a1) and 2t4+8, 2t4+9 (a2, a3).
+            uint32_t vm01 = 0xffffffffu, vm23 = 0xffffffffu;
+            if (nvalid < 16) {
+                vm01 = (2 * t4 < nvalid ? 0x0000ffffu : 0u) | (2 * t4 + 1 < nvalid ? 0xffff0000u : 0u);
+                vm23 = (2 * t4 + 8 < nvalid ? 0x0000ffffu : 0u) | (2 * t4 + 9 < nvalid ? 0xffff0000u : 0u);
+            }
+#pragma unroll
+            for (int mt = 0; mt < KS; ++mt) {
+                oc[mt][0] *= al_a;
+                oc[mt][1] *= al_b;
+                oc[mt][2] *= al_a;
+                oc[mt][3] *= al_b;
+                uint32_t a[4];
+                ldsm_x4_t(vt + v_off + mt * 32, a);
+                a[0] &= vm01;
+                a[1] &= vm01;
+                a[2] &= vm23;
+                a[3] &= vm23;
+                mma16816(oc[mt], a, ph0, ph1);
+                mma16816(oc[mt], a, pl0, pl1);
+            }
+            __syncwarp();   // P^T is rewritten by the next step
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty[s]);
     }
 
-    // ---- merge the 4 consumer warps (ring is free: every stage was consumed) ----
-    named_bar_sync(1, 32 * kConsumers);
+    // ---- merge the consumer warps (ring is free: every stage was consumed) ----
+    named_bar_sync(1, 32 * NCW);
     if (abort_flag[0]) return;
-    if (my_t == 0 && (lane & ((1 << REP) - 1)) == 0 && my_g < G) {
-        mrg_ml[(warp * G + my_g) * 2 + 0] = m_mine;
-        mrg_ml[(warp * G + my_g) * 2 + 1] = l_mine;
+    {
+        const int ha = 2 * t4, hb = 2 * t4 + 1;
+        if (g8 == 0) {
+            if (ha < G) {
+                mrg_ml[(warp * G + ha) * 2 + 0] = m_a;
+                mrg_ml[(warp * G + ha) * 2 + 1] = l_a;
+            }
+            if (hb < G) {
+                mrg_ml[(warp * G + hb) * 2 + 0] = m_b;
+                mrg_ml[(warp * G + hb) * 2 + 1] = l_b;
+            }
+        }
+#pragma unroll
+        for (int mt = 0; mt < KS; ++mt) {
+            const int d0 = mt * 16 + g8, d1 = d0 + 8;
+            if (ha < G) {
+                mrg_o[(warp * G + ha) * HD + d0] = oc[mt][0];
+                mrg_o[(warp * G + ha) * HD + d1] = oc[mt][2];
+            }
+            if (hb < G) {
+                mrg_o[(warp * G + hb) * HD + d0] = oc[mt][1];
+                mrg_o[(warp * G + hb) * HD + d1] = oc[mt][3];
+            }
+        }
     }
-#pragma unroll
-    for (int g = 0; g < G; ++g)
-#pragma unroll
-        for (int d = 0; d < DPL; ++d) mrg_o[(warp * G + g) * HD + lane * DPL + d] = oacc[g][d];
-    named_bar_sync(1, 32 * kConsumers);
+    named_bar_sync(1, 32 * NCW);
 
-    const int tid = threadIdx.x;   // 0..127
-    const bool single = (n_splits == 1) && !p.partial_only;
-    for (int e = tid; e < static_cast<int>(gcnt) * HD; e += 32 * kConsumers) {
-        const int g = e / HD, d = e % HD;
+    const int tid = threadIdx.x;   // 0..32*NCW-1
+    const bool single = n_splits == 1;   // this CTA holds the whole key range of its (item, head group)
+    const uint32_t nsl = NCW / HC;       // slice warps per head
+    for (int e = tid; e < static_cast<int>(HC * G * HD); e += 32 * NCW) {
+        const uint32_t h = e / (G * HD), g = (e / HD) % G, d = e % HD;
+        if (g >= s_gcnt[h]) continue;
         float M = -INFINITY;
-#pragma unroll
-        for (int w = 0; w < kConsumers; ++w) M = fmaxf(M, mrg_ml[(w * G + g) * 2]);
+        for (uint32_t j = 0; j < nsl; ++j) M = fmaxf(M, mrg_ml[((h + j * HC) * G + g) * 2]);
         float o = 0.f, l = 0.f;
-#pragma unroll
-        for (int w = 0; w < kConsumers; ++w) {
+        for (uint32_t j = 0; j < nsl; ++j) {
+            const uint32_t w = h + j * HC;
             const float mw = mrg_ml[(w * G + g) * 2];
             const float sc = (mw == -INFINITY) ? 0.f : ex2_approx(mw - M);
             o += sc * mrg_o[(w * G + g) * HD + d];
             l += sc * mrg_ml[(w * G + g) * 2 + 1];
         }
-        const uint32_t hh = gfirst + g;
-        if (single) {
-            float r = o / l;
-            if (it.gate) r *= 1.0f / (1.0f + __expf(-it.gate[static_cast<size_t>(hh) * HD + d]));
-            it.out[static_cast<size_t>(hh) * HD + d] = r;
-        } else if (p.partial_only) {
+        const uint32_t hh = s_gfirst[h] + g;
+        if (single && p.partial_only) {
             p.out_o[static_cast<size_t>(hh) * HD + d] = o;
             if (d == 0) {
                 p.out_ml[hh * 2 + 0] = M;
                 p.out_ml[hh * 2 + 1] = l;
             }
+        } else if (single) {
+            float r = o / l;
+            if (it.gate) r *= 1.0f / (1.0f + __expf(-it.gate[static_cast<size_t>(hh) * HD + d]));
+            it.out[static_cast<size_t>(hh) * HD + d] = r;
         } else {
-            const size_t slot = static_cast<size_t>(part_base + split) * G + g;
+            const size_t slot = static_cast<size_t>(part_base + h * n_splits + split) * G + g;
             p.part_o[slot * HD + d] = o;
             if (d == 0) {
                 p.part_ml[slot * 2 + 0] = M;
@@ -377,36 +409,111 @@ __global__ void __launch_bounds__(kThreads, 2) k_decode(const DecodeParams p) {
             }
         }
     }
-    if (single || p.partial_only) return;
+    if (single || p.defer_merge) return;
 
-    // ---- last split of this (item, kv_head) merges all splits ----
+    // ---- last split of this (item, head group) merges all splits ----
     __threadfence();
-    named_bar_sync(1, 32 * kConsumers);
+    named_bar_sync(1, 32 * NCW);
     if (tid == 0) {
         const uint32_t prev = atomicAdd(&p.counters[group], 1u);
         last_flag[0] = (prev == n_splits - 1) ? 1 : 0;
     }
-    named_bar_sync(1, 32 * kConsumers);
+    named_bar_sync(1, 32 * NCW);
     if (!last_flag[0]) return;
     __threadfence();
-    for (int e = tid; e < static_cast<int>(gcnt) * HD; e += 32 * kConsumers) {
-        const int g = e / HD, d = e % HD;
+    for (int e = tid; e < static_cast<int>(HC * G * HD); e += 32 * NCW) {
+        const uint32_t h = e / (G * HD), g = (e / HD) % G, d = e % HD;
+        if (g >= s_gcnt[h]) continue;
+        const size_t base = static_cast<size_t>(part_base + h * n_splits);
         float M = -INFINITY;
         for (uint32_t sidx = 0; sidx < n_splits; ++sidx)
-            M = fmaxf(M, __ldcg(&p.part_ml[(static_cast<size_t>(part_base + sidx) * G + g) * 2]));
+            M = fmaxf(M, __ldcg(&p.part_ml[((base + sidx) * G + g) * 2]));
         float o = 0.f, l = 0.f;
         for (uint32_t sidx = 0; sidx < n_splits; ++sidx) {
-            const size_t slot = static_cast<size_t>(part_base + sidx) * G + g;
+            const size_t slot = (base + sidx) * G + g;
             const float sc = ex2_approx(__ldcg(&p.part_ml[slot * 2]) - M);
             o += sc * __ldcg(&p.part_o[slot * HD + d]);
             l += sc * __ldcg(&p.part_ml[slot * 2 + 1]);
         }
-        const uint32_t hh = gfirst + g;
+        const uint32_t hh = s_gfirst[h] + g;
+        if (p.partial_only) {   // merged (m, l, o) of the whole range, for a cross-GPU merge
+            p.out_o[static_cast<size_t>(hh) * HD + d] = o;
+            if (d == 0) {
+                p.out_ml[hh * 2 + 0] = M;
+                p.out_ml[hh * 2 + 1] = l;
+            }
+            continue;
+        }
         float r = o / l;
         if (it.gate) r *= 1.0f / (1.0f + __expf(-it.gate[static_cast<size_t>(hh) * HD + d]));
         it.out[static_cast<size_t>(hh) * HD + d] = r;
     }
     if (tid == 0) p.counters[group] = 0u;   // ready for the next launch
+}
+
+// ------------------------------------------------- parallel merge of many splits
+// One CTA per query head; its 8 warps each fold a strided subset of the ns
+// split partials (online log-sum-exp in registers, lane = dims lane + 32 i),
+// then the warps combine in shared memory.  Used when one query has more
+// splits than the last-arriving CTA can merge quickly on its own.
+constexpr uint32_t kInKernelMergeMax = 8;
+
+__global__ void __launch_bounds__(256) k_merge_splits(const float* __restrict__ part_ml,
+                                                      const float* __restrict__ part_o, uint32_t ns,
+                                                      uint32_t n_heads, uint32_t n_kv, uint32_t G, uint32_t hd,
+                                                      float* out, const float* gate, float* out_ml, float* out_o) {
+    __shared__ float s_m[8], s_l[8];
+    __shared__ float s_o[8][256];
+    const uint32_t hh = blockIdx.x;
+    const uint32_t kvh = hh * n_kv / n_heads;
+    uint32_t gfirst, gcnt;
+    group_of(kvh, n_heads, n_kv, gfirst, gcnt);
+    const uint32_t gl = hh - gfirst;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int dl = static_cast<int>(hd / 32);     // 2, 4 or 8 dims per lane
+    float m = -INFINITY, l = 0.f, acc[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) acc[i] = 0.f;
+    for (uint32_t s = warp; s < ns; s += 8) {
+        const size_t slot = (static_cast<size_t>(kvh) * ns + s) * G + gl;
+        const float ms = part_ml[slot * 2], ls = part_ml[slot * 2 + 1];
+        const float mn = fmaxf(m, ms);
+        const float a = ex2_approx(m - mn), b = ex2_approx(ms - mn);
+        l = l * a + ls * b;
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+            if (i < dl) acc[i] = acc[i] * a + b * part_o[slot * hd + lane + 32 * i];
+        m = mn;
+    }
+    if (lane == 0) {
+        s_m[warp] = m;
+        s_l[warp] = l;
+    }
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+        if (i < dl) s_o[warp][lane + 32 * i] = acc[i];
+    __syncthreads();
+    for (uint32_t d = threadIdx.x; d < hd; d += blockDim.x) {
+        float M = -INFINITY;
+        for (int w = 0; w < 8; ++w) M = fmaxf(M, s_m[w]);
+        float o = 0.f, L = 0.f;
+        for (int w = 0; w < 8; ++w) {
+            const float sc = (s_m[w] == -INFINITY) ? 0.f : ex2_approx(s_m[w] - M);
+            o += sc * s_o[w][d];
+            L += sc * s_l[w];
+        }
+        if (out_ml) {   // merged partial of the whole range
+            out_o[static_cast<size_t>(hh) * hd + d] = o;
+            if (d == 0) {
+                out_ml[hh * 2 + 0] = M;
+                out_ml[hh * 2 + 1] = L;
+            }
+            continue;
+        }
+        float r = o / L;
+        if (gate) r *= 1.0f / (1.0f + __expf(-gate[static_cast<size_t>(hh) * hd + d]));
+        out[static_cast<size_t>(hh) * hd + d] = r;
+    }
 }
 
 // ---------------------------------------------------------------- merge kernel
@@ -438,9 +545,9 @@ __global__ void k_merge_partials(float* out, const float* ml, const float* o, ui
 template <int HD, int G>
 int launch_t(const DecodeParams& p, uint32_t grid, cudaStream_t st, char* err, size_t errlen) {
     using C = DecodeCfg<HD>;
-    const size_t smem = C::NST * C::STAGEB + 2 * C::NST * 8 + (kConsumers * 32 + kConsumers * 8) * 4 +
-                        kConsumers * G * 2 * 4 + 16;
-    static_assert(C::NST * C::STAGEB >= kConsumers * G * HD * 4, "merge area must fit in the ring");
+    const size_t smem = C::NST * C::STAGE_MAX + 2 * C::NST * 8 + C::NCW * C::PT_BYTES + C::NCW * G * 2 * 4 +
+                        16 * 4 + 16;
+    static_assert(C::NST * C::STAGE_MAX >= C::NCW * G * HD * 4, "merge area must fit in the ring");
     static bool attr_done[64] = {};
     int dev = 0;
     cudaGetDevice(&dev);
@@ -453,7 +560,7 @@ int launch_t(const DecodeParams& p, uint32_t grid, cudaStream_t st, char* err, s
         }
         attr_done[dev] = true;
     }
-    k_decode<HD, G><<<grid, kThreads, smem, st>>>(p);
+    k_decode<HD, G><<<grid, C::THREADS, smem, st>>>(p);
     YATTN_CHECK_LAUNCH(err, errlen, "decode");
     return 0;
 }
@@ -508,14 +615,16 @@ bool aligned16(const void* ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 15u
 
 uint32_t gmax_of(uint32_t n_heads, uint32_t n_kv) { return (n_heads + n_kv - 1) / n_kv; }
 
-// Uniform split length for `tokens` keys of n_kv heads aiming at `target` CTAs.
-uint32_t auto_split(uint64_t token_heads, uint32_t target) {
-    uint64_t len = (token_heads + target - 1) / target;
+// Uniform split length aiming at `target` CTAs for `work` = keys x head groups.
+uint32_t auto_split(uint64_t work, uint32_t target) {
+    uint64_t len = (work + target - 1) / target;
     len = std::max<uint64_t>(len, 128);
-    len = (len + kTok - 1) / kTok * kTok;
+    len = (len + kSplitQuant - 1) / kSplitQuant * kSplitQuant;
     return static_cast<uint32_t>(std::min<uint64_t>(len, 1u << 30));
 }
 
+// Workspace: merge counters (one per multi-split (item, head group)), then
+// (m, l) and o of every partial slot (one per (item, kv head, split)).
 size_t ws_bytes_for(uint32_t n_parts, uint32_t n_groups, uint32_t gmax, uint32_t hd) {
     size_t c = (static_cast<size_t>(n_groups) * 4 + 255) / 256 * 256;
     size_t ml = (static_cast<size_t>(n_parts) * gmax * 2 * 4 + 255) / 256 * 256;
@@ -530,6 +639,58 @@ void carve_ws(void* ws, uint32_t n_parts, uint32_t n_groups, uint32_t gmax, Deco
     p.counters = reinterpret_cast<uint32_t*>(b);
     p.part_ml = reinterpret_cast<float*>(b + c);
     p.part_o = reinterpret_cast<float*>(b + c + ml);
+}
+
+// Uniform-split parameters for one query over keys [t_begin, t_end).
+struct SinglePlan {
+    uint32_t hc, n_groups_kv, split, ns, n_parts, n_groups;
+};
+
+SinglePlan plan_single(uint32_t ntok, uint32_t n_kv, uint32_t hd, uint32_t target) {
+    SinglePlan s{};
+    s.hc = heads_per_cta(n_kv, hd);
+    s.n_groups_kv = n_kv / s.hc;
+    s.split = auto_split(static_cast<uint64_t>(ntok) * s.n_groups_kv, target);
+    s.ns = (ntok + s.split - 1) / s.split;
+    s.n_parts = s.ns > 1 ? n_kv * s.ns : 0;
+    s.n_groups = s.ns > 1 ? s.n_groups_kv : 0;
+    return s;
+}
+
+DecodeParams single_params(const SinglePlan& sp, float* out, const float* q, const uint16_t* k, const uint16_t* v,
+                           const float* gate, uint32_t t_begin, uint32_t t_end, uint32_t n_heads, uint32_t n_kv,
+                           uint32_t hd, uint32_t kv_dim) {
+    DecodeParams p{};
+    p.item0.q = q;
+    p.item0.out = out;
+    p.item0.k = k;
+    p.item0.v = v;
+    p.item0.gate = gate;
+    p.item0.pos = t_end - 1;
+    p.split_len = sp.split;
+    p.n_splits0 = sp.ns;
+    p.t_base = t_begin;
+    p.t_end0 = t_end;
+    p.n_heads = n_heads;
+    p.n_kv = n_kv;
+    p.kv_dim = kv_dim;
+    p.hc = sp.hc;
+    p.scale_log2 = 1.4426950408889634f / sqrtf(static_cast<float>(hd));
+    return p;
+}
+
+// Launches a single-query decode; with many splits the merge runs as a
+// separate parallel kernel instead of in the last-arriving CTA.
+int launch_single(DecodeParams& p, const SinglePlan& sp, uint32_t hd, cudaStream_t st, char* err, size_t errlen) {
+    const bool defer = sp.ns > kInKernelMergeMax;
+    p.defer_merge = defer ? 1 : 0;
+    if (launch_decode(p, hd, sp.ns * sp.n_groups_kv, st, err, errlen)) return -1;
+    if (!defer) return 0;
+    const uint32_t G = gmax_of(p.n_heads, p.n_kv);
+    k_merge_splits<<<p.n_heads, 256, 0, st>>>(p.part_ml, p.part_o, sp.ns, p.n_heads, p.n_kv, G, hd, p.item0.out,
+                                               p.item0.gate, p.partial_only ? p.out_ml : nullptr, p.out_o);
+    YATTN_CHECK_LAUNCH(err, errlen, "decode merge");
+    return 0;
 }
 
 }  // namespace
@@ -556,34 +717,14 @@ int decode_single(float* out, const float* q, const uint16_t* k, const uint16_t*
     DevCtx* ctx = dev_ctx(err, errlen);
     if (!ctx) return -1;
     const uint32_t gmax = gmax_of(n_heads, n_kv);
-    const uint32_t ntok = t_end - t_begin;
-    const bool partial_only = partial_ml != nullptr;
-    uint32_t split = auto_split(static_cast<uint64_t>(ntok) * n_kv, static_cast<uint32_t>(ctx->num_sms) * 4);
-    if (partial_only) split = ntok;   // one work unit per kv head: the partial covers the whole range
-    const uint32_t ns = (ntok + split - 1) / split;
-    DecodeParams p{};
-    p.items = nullptr;
-    p.work = nullptr;
-    p.item0.q = q;
-    p.item0.out = out;
-    p.item0.k = k;
-    p.item0.v = v;
-    p.item0.gate = gate;
-    p.item0.pos = t_end - 1;
-    p.split_len = split;
-    p.n_splits0 = ns;
-    p.t_base = t_begin;
-    p.t_end0 = t_end;
-    p.n_heads = n_heads;
-    p.n_kv = n_kv;
-    p.kv_dim = kv_dim;
-    p.scale_log2 = 1.4426950408889634f / sqrtf(static_cast<float>(hd));
+    const SinglePlan sp = plan_single(t_end - t_begin, n_kv, hd, static_cast<uint32_t>(ctx->num_sms));
+    DecodeParams p = single_params(sp, out, q, k, v, gate, t_begin, t_end, n_heads, n_kv, hd, kv_dim);
     p.status = ctx->status;
-    p.partial_only = partial_only ? 1 : 0;
+    p.partial_only = partial_ml != nullptr ? 1 : 0;
     p.out_ml = partial_ml;
     p.out_o = partial_o;
-    if (ns > 1 && !partial_only) {
-        const size_t need = ws_bytes_for(ns * n_kv, n_kv, gmax, hd);
+    if (sp.ns > 1) {
+        const size_t need = ws_bytes_for(sp.n_parts, sp.n_groups, gmax, hd);
         if (ws) {
             if (ws_bytes < need) {
                 set_err(err, errlen, "decode: workspace %zu bytes < %zu needed", ws_bytes, need);
@@ -606,9 +747,9 @@ int decode_single(float* out, const float* q, const uint16_t* k, const uint16_t*
             }
             ws = ctx->ws;
         }
-        carve_ws(ws, ns * n_kv, n_kv, gmax, p);
+        carve_ws(ws, sp.n_parts, sp.n_groups, gmax, p);
     }
-    return launch_decode(p, hd, ns * n_kv, st, err, errlen);
+    return launch_single(p, sp, hd, st, err, errlen);
 }
 
 int decode_reserve(size_t bytes, char* err, size_t errlen) {
@@ -631,18 +772,25 @@ int decode_reserve(size_t bytes, char* err, size_t errlen) {
 using namespace yattn;
 
 extern "C" int yattn_decode_plan(const uint32_t* pos_host, uint32_t n_items, uint32_t n_kv_heads,
-                                 uint32_t split_tokens, uint32_t target_ctas, YattnDecodeWork* work_host,
-                                 uint32_t work_cap, uint32_t* n_work, uint32_t* n_parts, uint32_t* n_groups,
-                                 char* err, size_t errlen) {
+                                 uint32_t head_dim, uint32_t split_tokens, uint32_t target_ctas,
+                                 YattnDecodeWork* work_host, uint32_t work_cap, uint32_t* n_work, uint32_t* n_parts,
+                                 uint32_t* n_groups, char* err, size_t errlen) {
     if (!pos_host || !work_host || !n_work || !n_parts || !n_groups || n_kv_heads == 0 || n_kv_heads > 65535) {
         set_err(err, errlen, "decode_plan: bad arguments");
         return -1;
     }
+    if (head_dim != 64 && head_dim != 128 && head_dim != 256) {
+        set_err(err, errlen, "decode_plan: head_dim %u not supported (64/128/256)", head_dim);
+        return -1;
+    }
+    const uint32_t hc = heads_per_cta(n_kv_heads, head_dim);
+    const uint32_t nkg = n_kv_heads / hc;
     uint64_t total = 0;
     for (uint32_t i = 0; i < n_items; ++i) total += static_cast<uint64_t>(pos_host[i]) + 1;
-    total *= n_kv_heads;
-    if (target_ctas == 0) target_ctas = static_cast<uint32_t>(dev_num_sms()) * 4;
-    const uint32_t split = split_tokens ? (split_tokens + kTok - 1) / kTok * kTok : auto_split(total, target_ctas);
+    total *= nkg;
+    if (target_ctas == 0) target_ctas = static_cast<uint32_t>(dev_num_sms());
+    const uint32_t split = split_tokens ? (split_tokens + kSplitQuant - 1) / kSplitQuant * kSplitQuant
+                                        : auto_split(total, target_ctas);
     std::vector<YattnDecodeWork> w;
     uint32_t parts = 0, groups = 0;
     for (uint32_t i = 0; i < n_items; ++i) {
@@ -652,11 +800,11 @@ extern "C" int yattn_decode_plan(const uint32_t* pos_host, uint32_t n_items, uin
             set_err(err, errlen, "decode_plan: %u splits for item %u (max 65535)", ns, i);
             return -1;
         }
-        for (uint32_t h = 0; h < n_kv_heads; ++h) {
+        for (uint32_t kg = 0; kg < nkg; ++kg) {
             for (uint32_t s = 0; s < ns; ++s) {
                 YattnDecodeWork x{};
                 x.item = i;
-                x.kv_head = static_cast<uint16_t>(h);
+                x.kv_head = static_cast<uint16_t>(kg * hc);
                 x.n_splits = static_cast<uint16_t>(ns);
                 x.split = s;
                 x.t_begin = s * split;
@@ -666,7 +814,7 @@ extern "C" int yattn_decode_plan(const uint32_t* pos_host, uint32_t n_items, uin
                 w.push_back(x);
             }
             if (ns > 1) {
-                parts += ns;
+                parts += hc * ns;     // one slot per (kv head of the group, split)
                 groups += 1;
             }
         }
@@ -690,6 +838,7 @@ extern "C" int yattn_decode_plan(const uint32_t* pos_host, uint32_t n_items, uin
 extern "C" size_t yattn_decode_workspace_bytes(uint32_t n_parts, uint32_t n_groups, uint32_t n_heads,
                                                uint32_t n_kv_heads, uint32_t head_dim) {
     if (n_kv_heads == 0) return 0;
+    if (n_parts == 0) return 0;
     return ws_bytes_for(n_parts, n_groups, gmax_of(n_heads, n_kv_heads), head_dim);
 }
 
@@ -728,6 +877,7 @@ extern "C" int yattn_decode_run(const YattnDecodeItem* items_dev, const YattnDec
     p.n_heads = n_heads;
     p.n_kv = n_kv_heads;
     p.kv_dim = kv_dim;
+    p.hc = heads_per_cta(n_kv_heads, head_dim);
     p.scale_log2 = 1.4426950408889634f / sqrtf(static_cast<float>(head_dim));
     p.status = ctx->status;
     if (n_parts > 0) carve_ws(workspace, n_parts, n_groups, gmax, p);
@@ -736,8 +886,10 @@ extern "C" int yattn_decode_run(const YattnDecodeItem* items_dev, const YattnDec
 
 extern "C" size_t yattn_decode_partial_workspace_bytes(uint32_t n_tokens, uint32_t n_heads, uint32_t n_kv_heads,
                                                        uint32_t head_dim) {
-    (void)n_tokens; (void)n_heads; (void)n_kv_heads; (void)head_dim;
-    return 0;   // one work unit per kv head writes straight to ml/o
+    if (n_kv_heads == 0 || n_tokens == 0) return 0;
+    const SinglePlan sp = plan_single(n_tokens, n_kv_heads, head_dim, static_cast<uint32_t>(dev_num_sms()));
+    if (sp.ns <= 1) return 0;
+    return ws_bytes_for(sp.n_parts, sp.n_groups, gmax_of(n_heads, n_kv_heads), head_dim);
 }
 
 extern "C" int yattn_decode_partial(float* ml, float* o, const float* q, const uint16_t* kcache,
@@ -844,49 +996,34 @@ extern "C" int yattn_attn_decode_noalloc(float* att_out, const float* q, const u
         return -1;
     }
     // The split schedule is the one yattn_attn_decode uses, so both give the same result.
-    const uint32_t ntok = pos + 1;
     const uint32_t gmax = gmax_of(n_heads, n_kv_heads);
-    const uint32_t split = auto_split(static_cast<uint64_t>(ntok) * n_kv_heads, static_cast<uint32_t>(dev_num_sms()) * 4);
-    const uint32_t ns = (ntok + split - 1) / split;
-    const size_t need = ns > 1 ? ws_bytes_for(ns * n_kv_heads, n_kv_heads, gmax, head_dim) : 0;
+    const SinglePlan sp = plan_single(pos + 1, n_kv_heads, head_dim, static_cast<uint32_t>(dev_num_sms()));
+    const size_t need = sp.ns > 1 ? ws_bytes_for(sp.n_parts, sp.n_groups, gmax, head_dim) : 0;
     if (need > kNoAllocScratchBytes - kNoAllocHeader) {
         set_err(err, errlen,
                 "decode_noalloc: this query needs %zu bytes of split-KV scratch, more than the %zu-byte static "
                 "scratch (%u splits x %u kv heads x %u q heads x head_dim %u); use yattn_attn_decode",
-                need, kNoAllocScratchBytes - kNoAllocHeader, ns, n_kv_heads, gmax, head_dim);
+                need, kNoAllocScratchBytes - kNoAllocHeader, sp.ns, n_kv_heads, gmax, head_dim);
         return -1;
     }
     // First call on a device: looks up the scratch address (no allocation).
     uint8_t* base = static_cast<uint8_t*>(noalloc_scratch(dev, err, errlen));
     if (!base) return -1;
     cudaStream_t st = static_cast<cudaStream_t>(stream);
-    DecodeParams p{};
-    p.item0.q = q;
-    p.item0.out = att_out;
-    p.item0.k = kcache;
-    p.item0.v = vcache;
-    p.item0.gate = gate;
-    p.item0.pos = pos;
-    p.split_len = split;
-    p.n_splits0 = ns;
-    p.t_base = 0;
-    p.t_end0 = ntok;
-    p.n_heads = n_heads;
-    p.n_kv = n_kv_heads;
-    p.kv_dim = kv_dim;
-    p.scale_log2 = 1.4426950408889634f / sqrtf(static_cast<float>(head_dim));
+    DecodeParams p = single_params(sp, att_out, q, kcache, vcache, gate, 0, pos + 1, n_heads, n_kv_heads, head_dim,
+                                   kv_dim);
     p.status = reinterpret_cast<int*>(base);
     // The array keeps the previous call's contents: the status word and the merge
     // counters must start at zero, the partials are fully rewritten before use.
     size_t clear = sizeof(int);
-    if (ns > 1) {
-        carve_ws(base + kNoAllocHeader, ns * n_kv_heads, n_kv_heads, gmax, p);
-        clear = kNoAllocHeader + static_cast<size_t>(n_kv_heads) * sizeof(uint32_t);
+    if (sp.ns > 1) {
+        carve_ws(base + kNoAllocHeader, sp.n_parts, sp.n_groups, gmax, p);
+        clear = kNoAllocHeader + static_cast<size_t>(sp.n_groups) * sizeof(uint32_t);
     }
     cudaError_t e = cudaMemsetAsync(base, 0, clear, st);
     if (e != cudaSuccess) {
         set_err(err, errlen, "decode_noalloc: clearing the scratch failed: %s", cudaGetErrorString(e));
         return -1;
     }
-    return launch_decode(p, head_dim, ns * n_kv_heads, st, err, errlen);
+    return launch_single(p, sp, head_dim, st, err, errlen);
 }

@@ -37,6 +37,22 @@ def split_range(n: int, world: int, rank: int) -> tuple[int, int]:
     return begin, begin + base + (1 if rank < extra else 0)
 
 
+def causal_row_split(S: int, world: int, rank: int, quant: int = 128) -> tuple[int, int]:
+    """Query rows [r0, r1) of an S-token causal prefill for rank, with about
+    equal causal work (row r attends r+1 keys, so the boundaries sit at
+    S*sqrt(k/world)), rounded to multiples of `quant` (the kernel's row tile)."""
+    import math
+
+    def cut(k: int) -> int:
+        if k <= 0:
+            return 0
+        if k >= world:
+            return S
+        return min(S, int(round(S * math.sqrt(k / world) / quant)) * quant)
+
+    return cut(rank), cut(rank + 1)
+
+
 def env_rank() -> tuple[int, int, int]:
     return (int(os.environ.get("RANK", "0")), int(os.environ.get("WORLD_SIZE", "1")),
             int(os.environ.get("LOCAL_RANK", "0")))
@@ -54,22 +70,30 @@ def init(backend: str = "nccl", timeout_s: float = 120.0) -> tuple[int, int, int
     return rank, world, local
 
 
-def allgather_merge_partials(ml: torch.Tensor, o: torch.Tensor, out: torch.Tensor, n_heads: int, head_dim: int,
-                             gate: Optional[torch.Tensor] = None, group=None) -> None:
-    """Split-KV merge across ranks: all-gather this rank's (m, l) [n_heads, 2]
-    and o [n_heads, head_dim] partials, then merge them on this GPU with the
-    library's log-sum-exp kernel.  Every rank ends with the full output."""
-    from . import attn
-
+def gather_partials(ml: torch.Tensor, o: torch.Tensor, n_heads: int, head_dim: int,
+                    group=None) -> tuple[torch.Tensor, torch.Tensor, int]:
+    """All-gathers every rank's (m, l) [n_heads, 2] and o [n_heads, head_dim]
+    partials into local buffers: returns ([world, n_heads, 2], [world, n_heads,
+    head_dim], world).  One collective of n_heads*(2+head_dim) floats per rank."""
     world = dist.get_world_size(group) if dist.is_initialized() else 1
     if world == 1:
-        attn.merge_partials(out, ml, o, 1, n_heads, head_dim, gate)
-        return
+        return ml.reshape(1, n_heads, 2), o.reshape(1, n_heads, head_dim), 1
     payload = torch.cat([ml.reshape(-1), o.reshape(-1)])
-    gathered = torch.empty(world * payload.numel(), dtype=payload.dtype, device=payload.device)
-    dist.all_gather_into_tensor(gathered, payload, group=group)
-    g = gathered.view(world, -1)
+    parts = [torch.empty_like(payload) for _ in range(world)]
+    dist.all_gather(parts, payload, group=group)
+    g = torch.stack(parts)
     n_ml = n_heads * 2
-    all_ml = g[:, :n_ml].contiguous()
-    all_o = g[:, n_ml:].contiguous()
+    return (g[:, :n_ml].reshape(world, n_heads, 2).contiguous(),
+            g[:, n_ml:].reshape(world, n_heads, head_dim).contiguous(), world)
+
+
+def allgather_merge_partials(ml: torch.Tensor, o: torch.Tensor, out: torch.Tensor, n_heads: int, head_dim: int,
+                             gate: Optional[torch.Tensor] = None, group=None) -> None:
+    """Split-KV merge across ranks: gather every rank's partials (above), then
+    merge them on this GPU with the library's log-sum-exp kernel.  Every rank
+    ends with the full output.  Ranks with an empty key range send l = 0 and
+    are skipped by the merge."""
+    from . import attn
+
+    all_ml, all_o, world = gather_partials(ml, o, n_heads, head_dim, group)
     attn.merge_partials(out, all_ml, all_o, world, n_heads, head_dim, gate)
