@@ -7,20 +7,19 @@
 // hh*n_kv/n_heads; out has q's layout.  Optional qwen35 sigmoid output gate
 // (engine.c:958-960).
 //
-// One CTA = one (query head, 128-row query tile).  Warps:
+// One CTA = one (query head, 128-row query tile), heaviest tiles first.  Warps:
 //   0-3  softmax: thread i owns query row i = TMEM lane i.  Loads the fp32 Q
-//        tile once (-> fp16, SWIZZLE_128B K-major in smem), then per key block
-//        reads S from TMEM, applies the causal mask and the online softmax
-//        (log2 domain; the running max only moves when it grows by more than
-//        2^8, so O in TMEM is rarely rescaled), and writes P to smem as two
-//        fp16 planes P_hi + P_lo (P_lo = fp16(p - P_hi)), which keeps P to
-//        ~22 bits instead of fp16's 11.
-//   4    TMA for K blocks, 6 TMA for V blocks: separate two-stage rings, so K
-//        of block j+2 loads as soon as S(j) is done (not after PV(j)).
-//   5    MMA: one thread issues S(j) = Q K(j)^T into two alternating TMEM S
-//        buffers (the tensor core computes S(j+1) while softmax works on S(j))
-//        and O += P_hi V + P_lo V into one TMEM accumulator; tcgen05.commit
-//        signals the mbarriers.
+//        tile once (-> fp16, SWIZZLE_128B K-major in smem).  Per key block it
+//        reads S from TMEM, applies the causal mask (diagonal blocks only) and
+//        the online softmax in the log2 domain (the running max only moves when
+//        it grows by more than 2^8, so O in TMEM is rarely rescaled), and writes
+//        P back over its own S columns as two fp16 planes P_hi + P_lo
+//        (P_lo = fp16(p - P_hi), ~22 bits instead of fp16's 11).
+//   4    TMA for K blocks, 6 TMA for V blocks: separate rings, no multicast.
+//   5    MMA: one thread issues S(j) = Q K(j)^T (A, B from smem) into two
+//        alternating TMEM S buffers and O += P_hi V + P_lo V with A = P read
+//        straight from TMEM (B = V from smem).  The tensor core runs its MMAs in
+//        issue order, so S(j+2) cannot overwrite P(j) before PV(j) has read it.
 // Keys past the end of the cache are zero-filled by TMA and masked.
 #include "common.cuh"
 #include "tcgen05.cuh"
@@ -31,23 +30,23 @@ namespace yattn {
 namespace {
 
 constexpr int BM = 128;
-constexpr int KST = 2;
 constexpr int kPThreads = 224;
 
 template <int HD> struct PCfg {
     static constexpr int BN = (HD >= 256) ? 64 : 128;
+    static constexpr int KST = (HD >= 256) ? 2 : 3;         // K and V ring depth
     static constexpr int Q_BYTES = BM * HD * 2;
     static constexpr int KV_BYTES = BN * HD * 2;            // one K (or V) block
-    static constexpr int P_BYTES = BM * BN * 2;             // one P plane
     static constexpr int OFF_Q = 0;
     static constexpr int OFF_K = OFF_Q + Q_BYTES;
     static constexpr int OFF_V = OFF_K + KST * KV_BYTES;
-    static constexpr int OFF_P = OFF_V + KST * KV_BYTES;    // P_hi, then P_lo
-    static constexpr int OFF_BAR = OFF_P + 2 * P_BYTES;
-    static constexpr int SMEM = OFF_BAR + 256 + 1024;        // + barriers, + alignment slack
+    static constexpr int OFF_BAR = OFF_V + KST * KV_BYTES;
+    // + barriers, + alignment slack; at least 116 KB so one CTA (holding all 512 TMEM columns) runs per SM
+    static constexpr int SMEM = (OFF_BAR + 256 + 1024) > 118784 ? (OFF_BAR + 256 + 1024) : 118784;
     static constexpr uint32_t TMEM_COLS = 512;
-    static constexpr uint32_t COL_S = 0;                     // two S buffers: [0, BN), [BN, 2BN)
+    static constexpr uint32_t COL_S = 0;                     // two S buffers: [0, BN), [BN, 2BN); P over S
     static constexpr uint32_t COL_O = 2 * BN;
+    static constexpr uint32_t P_COLS = BN / 2;               // one fp16 P plane, two values per column
     static_assert(2 * BN + HD <= 512, "TMEM columns");
     static_assert(SMEM <= 232448, "shared memory");
 };
@@ -61,9 +60,9 @@ struct PrefillParams {
     int* status;
 };
 
-struct Bars {
+template <int KST> struct Bars {
     uint64_t k_full[KST], k_empty[KST], v_full[KST], v_empty[KST];
-    uint64_t s_full[2], s_free[2], p_full, pv_done, q_full, mma_drain;
+    uint64_t s_full[2], p_full[2], pv_done, o_done, q_full, mma_drain;
     uint32_t tmem_base;
     int abort_flag;
 };
@@ -73,7 +72,7 @@ template <int HD>
 __device__ __forceinline__ void produce(const CUtensorMap* map, uint8_t* ring, uint64_t* full, uint64_t* empty,
                                         uint32_t kvh, uint32_t nkb, int* status, volatile int* abort_flag) {
     using C = PCfg<HD>;
-    constexpr int BN = C::BN;
+    constexpr int BN = C::BN, KST = C::KST;
     prefetch_tensormap(map);
     uint32_t issued = 0;
     for (uint32_t j = 0; j < nkb; ++j) {
@@ -101,14 +100,13 @@ __global__ void __launch_bounds__(kPThreads, 1)
     k_prefill(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV, const PrefillParams p) {
     using C = PCfg<HD>;
     constexpr int BN = C::BN;
+    constexpr int KST = C::KST;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t* sQ = smem + C::OFF_Q;
     uint8_t* sK = smem + C::OFF_K;
     uint8_t* sV = smem + C::OFF_V;
-    uint8_t* sPh = smem + C::OFF_P;
-    uint8_t* sPl = sPh + C::P_BYTES;
-    Bars* bars = reinterpret_cast<Bars*>(smem + C::OFF_BAR);
+    Bars<KST>* bars = reinterpret_cast<Bars<KST>*>(smem + C::OFF_BAR);
     volatile int* abort_flag = &bars->abort_flag;
 
     const int warp = threadIdx.x >> 5;
@@ -131,10 +129,10 @@ __global__ void __launch_bounds__(kPThreads, 1)
         }
         for (int s = 0; s < 2; ++s) {
             mbar_init(&bars->s_full[s], 1);
-            mbar_init(&bars->s_free[s], 4);
+            mbar_init(&bars->p_full[s], 4);
         }
-        mbar_init(&bars->p_full, 4);
         mbar_init(&bars->pv_done, 1);
+        mbar_init(&bars->o_done, 1);
         mbar_init(&bars->q_full, 4);
         mbar_init(&bars->mma_drain, 1);
         bars->abort_flag = 0;
@@ -159,18 +157,20 @@ __global__ void __launch_bounds__(kPThreads, 1)
             tc_fence_after();
             auto do_pv = [&](uint32_t jj) -> bool {
                 const int s = jj % KST;
-                if (!mbar_wait_bounded(&bars->p_full, jj & 1u, p.status, ST_PREFILL_TIMEOUT, abort_flag) ||
+                const uint32_t sb = jj & 1u;
+                if (!mbar_wait_bounded(&bars->p_full[sb], (jj >> 1) & 1u, p.status, ST_PREFILL_TIMEOUT,
+                                       abort_flag) ||
                     !mbar_wait_bounded(&bars->v_full[s], (jj / KST) & 1u, p.status, ST_PREFILL_TIMEOUT, abort_flag))
                     return false;
                 tc_fence_after();
+                const uint32_t pcol = tmem + C::COL_S + sb * BN;
 #pragma unroll
                 for (int plane = 0; plane < 2; ++plane) {
-                    const uint8_t* sP = plane ? sPl : sPh;
 #pragma unroll
                     for (int kk = 0; kk < BN / 16; ++kk) {
-                        const uint64_t a = sdesc_sw128(sP + (kk >> 2) * (BM * 128) + (kk & 3) * 32, 16, 1024);
                         const uint64_t b = sdesc_sw128(sV + s * C::KV_BYTES + kk * 16 * 128, BN * 128, 1024);
-                        umma_f16(tmem + C::COL_O, a, b, IDESC_PV, (jj > 0 || plane > 0 || kk > 0) ? 1u : 0u);
+                        umma_f16_ts(tmem + C::COL_O, pcol + plane * C::P_COLS + kk * 8, b, IDESC_PV,
+                                    (jj > 0 || plane > 0 || kk > 0) ? 1u : 0u);
                     }
                 }
                 umma_commit(&bars->v_empty[s]);
@@ -182,11 +182,8 @@ __global__ void __launch_bounds__(kPThreads, 1)
                 if (!mbar_wait_bounded(&bars->k_full[s], (j / KST) & 1u, p.status, ST_PREFILL_TIMEOUT, abort_flag))
                     break;
                 const uint32_t sb = j & 1u;
-                if (j >= 2 &&
-                    !mbar_wait_bounded(&bars->s_free[sb], ((j >> 1) & 1u) ^ 1u, p.status, ST_PREFILL_TIMEOUT,
-                                       abort_flag))
-                    break;
                 tc_fence_after();
+                // S buffer sb last held P(j-2); PV(j-2) was issued before this MMA, so it is read first.
 #pragma unroll
                 for (int kk = 0; kk < HD / 16; ++kk) {
                     const uint64_t a = sdesc_sw128(sQ + (kk >> 2) * (BM * 128) + (kk & 3) * 32, 16, 1024);
@@ -201,7 +198,7 @@ __global__ void __launch_bounds__(kPThreads, 1)
                     break;
                 }
             }
-            if (ok && !*abort_flag) do_pv(nkb - 1);
+            if (ok && !*abort_flag && do_pv(nkb - 1)) umma_commit(&bars->o_done);
             // drain: every MMA issued so far completes before TMEM is freed
             umma_commit(&bars->mma_drain);
             volatile int dummy = 0;
@@ -230,7 +227,8 @@ __global__ void __launch_bounds__(kPThreads, 1)
 
         const uint32_t trow = tmem + (static_cast<uint32_t>(warp * 32) << 16);
         const uint32_t qpos = qpos0 + r;
-        float m_run = -INFINITY, l_run = 0.f;
+        const float sl2 = p.scale_log2;
+        float m_run = -INFINITY, l_run = 0.f;                        // m_run in scaled log2 units
         bool ok = true;
         for (uint32_t j = 0; j < nkb; ++j) {
             const uint32_t sb = j & 1u;
@@ -239,86 +237,82 @@ __global__ void __launch_bounds__(kPThreads, 1)
                 break;
             }
             tc_fence_after();
+            const uint32_t scol = trow + C::COL_S + sb * BN;
             float sv[BN];
 #pragma unroll
             for (int c = 0; c < BN / 32; ++c) {
                 uint32_t rr[32];
-                tmem_ld32(trow + C::COL_S + sb * BN + c * 32, rr);
-                tmem_wait_ld();
+                tmem_ld32(scol + c * 32, rr);
 #pragma unroll
                 for (int i = 0; i < 32; ++i) sv[c * 32 + i] = __uint_as_float(rr[i]);
             }
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&bars->s_free[sb]);
-            // ---- mask, scale, row max ----
+            tmem_wait_ld();
+            // ---- causal mask (diagonal blocks only), row max of raw scores ----
             const uint32_t kbase = j * BN;
-            const bool diag = kbase + BN - 1 > qpos0;
-            float mx = -INFINITY;
+            if (kbase + BN - 1 > qpos0) {
 #pragma unroll
-            for (int c = 0; c < BN; ++c) {
-                float x = sv[c] * p.scale_log2;
-                if (diag && kbase + c > qpos) x = -INFINITY;
-                sv[c] = x;
-                mx = fmaxf(mx, x);
+                for (int c = 0; c < BN; ++c)
+                    if (kbase + c > qpos) sv[c] = -INFINITY;
             }
+            float mx4[4] = {sv[0], sv[1], sv[2], sv[3]};
+#pragma unroll
+            for (int c = 4; c < BN; c += 4) {
+                mx4[0] = fmaxf(mx4[0], sv[c]);
+                mx4[1] = fmaxf(mx4[1], sv[c + 1]);
+                mx4[2] = fmaxf(mx4[2], sv[c + 2]);
+                mx4[3] = fmaxf(mx4[3], sv[c + 3]);
+            }
+            const float mx = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3])) * sl2;
             const float m_new = fmaxf(m_run, mx);
             const bool grow = m_new > m_run + 8.0f;                  // keep a stale max up to 2^8 headroom
             const float m_use = grow ? m_new : m_run;
             const float alpha = grow ? ex2_approx(m_run - m_use) : 1.0f;
-            float rs = 0.f;
+            // ---- p = 2^(s*scale - m): one FFMA + ex2 per element; P hi/lo into TMEM ----
+            float rs4[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-            for (int c = 0; c < BN; ++c) {
-                sv[c] = ex2_approx(sv[c] - m_use);
-                rs += sv[c];
+            for (int c = 0; c < BN / 64; ++c) {
+                uint32_t hi[32], lo[32];
+#pragma unroll
+                for (int i = 0; i < 32; ++i) {
+                    const float a = ex2_approx(fmaf(sv[c * 64 + 2 * i], sl2, -m_use));
+                    const float b = ex2_approx(fmaf(sv[c * 64 + 2 * i + 1], sl2, -m_use));
+                    rs4[i & 3] += a + b;
+                    const __half2 h = __floats2half2_rn(a, b);
+                    const float2 hf = __half22float2(h);
+                    hi[i] = h2_bits(h);
+                    lo[i] = h2_bits(__floats2half2_rn(a - hf.x, b - hf.y));
+                }
+                tmem_st32(scol + c * 32, hi);
+                tmem_st32(scol + C::P_COLS + c * 32, lo);
             }
-            l_run = l_run * alpha + rs;
+            l_run = l_run * alpha + ((rs4[0] + rs4[1]) + (rs4[2] + rs4[3]));
             m_run = m_use;
-            // ---- PV(j-1) must be finished before P is overwritten and O rescaled ----
-            if (j >= 1) {
+            // ---- O rescale (rare): PV(j-1) must have finished accumulating ----
+            if (j >= 1 && __any_sync(0xffffffffu, grow)) {
                 if (!warp_wait_bounded(&bars->pv_done, (j - 1) & 1u, p.status, ST_PREFILL_TIMEOUT, abort_flag)) {
                     ok = false;
                     break;
                 }
                 tc_fence_after();
-                if (__any_sync(0xffffffffu, grow)) {
 #pragma unroll 1
-                    for (int c = 0; c < HD / 32; ++c) {
-                        uint32_t rr[32];
-                        tmem_ld32(trow + C::COL_O + c * 32, rr);
-                        tmem_wait_ld();
+                for (int c = 0; c < HD / 32; ++c) {
+                    uint32_t rr[32];
+                    tmem_ld32(trow + C::COL_O + c * 32, rr);
+                    tmem_wait_ld();
 #pragma unroll
-                        for (int i = 0; i < 32; ++i) rr[i] = __float_as_uint(__uint_as_float(rr[i]) * alpha);
-                        tmem_st32(trow + C::COL_O + c * 32, rr);
-                    }
-                    tmem_wait_st();
+                    for (int i = 0; i < 32; ++i) rr[i] = __float_as_uint(__uint_as_float(rr[i]) * alpha);
+                    tmem_st32(trow + C::COL_O + c * 32, rr);
                 }
             }
-            // ---- P row -> smem as P_hi + P_lo (fp16 each, swizzled K-major) ----
-#pragma unroll
-            for (int c = 0; c < BN; c += 8) {
-                uint4 hi, lo;
-                uint32_t* hp = &hi.x;
-                uint32_t* lp = &lo.x;
-#pragma unroll
-                for (int e = 0; e < 4; ++e) {
-                    const float a = sv[c + 2 * e], b = sv[c + 2 * e + 1];
-                    const __half2 h = __floats2half2_rn(a, b);
-                    const float2 hf = __half22float2(h);
-                    hp[e] = h2_bits(h);
-                    lp[e] = h2_bits(__floats2half2_rn(a - hf.x, b - hf.y));
-                }
-                const uint32_t off = sw128_offset(r, c, BM);
-                *reinterpret_cast<uint4*>(sPh + off) = hi;
-                *reinterpret_cast<uint4*>(sPl + off) = lo;
-            }
-            fence_proxy_async_smem();
+            tmem_wait_st();
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(&bars->p_full);
+            if (lane == 0) mbar_arrive(&bars->p_full[sb]);
         }
         // ---- epilogue: O / l (x sigmoid(gate)) -> out ----
-        if (ok && warp_wait_bounded(&bars->pv_done, (nkb - 1) & 1u, p.status, ST_PREFILL_TIMEOUT, abort_flag)) {
+        // pv_done can trail by two phases here (P is double-buffered), so the
+        // final accumulation has its own barrier.
+        if (ok && warp_wait_bounded(&bars->o_done, 0, p.status, ST_PREFILL_TIMEOUT, abort_flag)) {
             tc_fence_after();
             const uint32_t b = row0 + r;
             const float inv_l = 1.0f / l_run;
