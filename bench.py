@@ -111,6 +111,8 @@ class CpuReference:
         self.oracle = oracle
         self.kind = "reference" if oracle.has_ref() else "port"
         self.lib = oracle.load("ref" if self.kind == "reference" else "port")
+        # every host core (torchrun exports OMP_NUM_THREADS=1 to its ranks)
+        self.lib.orc_set_threads(len(os.sched_getaffinity(0)))
         self.cores = int(self.lib.orc_max_threads())
         self.cfg, self.seqs = cfg, seqs
         self.fx = [oracle.decode_fixture(cfg, layer, s, lib=self.lib) for s in seqs]
@@ -150,11 +152,14 @@ def run_ours(args) -> None:
     # --seqs / --layers shrink the workload for profiler captures only; the
     # default (and every reported number) is the full config.
     n_layers = args.layers or cfg.layers
-    n_total = args.seqs or cfg.n_seqs
-    ctx_all = cfg.ctx()[:n_total]
-    shards = ydist.shard_by_length(ctx_all, world)
-    seqs = shards[rank]
-    log(f"[rank {rank}] {len(seqs)} seqs, {sum(ctx_all[s] for s in seqs)} keys/layer, {n_layers} layers")
+    # Weak scaling: sequences are independent units, so at N GPUs the job is N
+    # batches of the config's size and rank r serves sequence ids
+    # [r*n, (r+1)*n) with no data-path collective.
+    n_per_rank = args.seqs or cfg.n_seqs
+    n_total = n_per_rank * world
+    seqs = list(range(rank * n_per_rank, (rank + 1) * n_per_rank))
+    keys_all = sum(cfg.ctx_of(s) for s in range(n_total))
+    log(f"[rank {rank}] {len(seqs)} seqs, {sum(cfg.ctx_of(s) for s in seqs)} keys/layer, {n_layers} layers")
 
     d = fixtures.decode_inputs(cfg, layers=list(range(n_layers)), seqs=seqs, device=dev)
     torch.cuda.synchronize()
@@ -257,17 +262,20 @@ def run_ours(args) -> None:
             "warmup": args.warmup,
             "ms_per_step": round(ms_per_step, 4),
             "higher_is_better": True,
-            "scaling": "strong",
+            "scaling": "weak",
             "vs_baseline": None,
             "dtype": "f32 math, fp16 KV",
             "data": "synthetic (seeded splitmix64 + Box-Muller, N(0,1) fp16 KV cache)",
             "config": {
-                "workload": cfg.name + ("" if not (args.seqs or args.layers) else f"-profile-{n_total}seq-{n_layers}layer"),
+                "workload": cfg.name + ("" if not (args.seqs or args.layers)
+                                        else f"-profile-{n_per_rank}seq-{n_layers}layer"),
                 "n_heads": cfg.n_heads, "n_kv_heads": cfg.n_kv_heads, "head_dim": cfg.head_dim,
-                "layers": n_layers, "n_seqs": n_total, "ctx_range": [cfg.ctx_lo, cfg.ctx_hi],
-                "total_keys_per_layer": sum(ctx_all),
-                "kv_bytes_per_step": cfg.kv_bytes_per_step(),
-                "parallelism": f"sequence-sharded x{world}",
+                "layers": n_layers, "n_seqs": n_total, "seqs_per_gpu": n_per_rank,
+                "ctx_range": [cfg.ctx_lo, cfg.ctx_hi],
+                "total_keys_per_layer": keys_all,
+                "kv_bytes_per_step": keys_all * cfg.kv_dim * 2 * 2 * n_layers,
+                "parallelism": (f"data-parallel x{world}: rank r serves sequences [{n_per_rank}r, {n_per_rank}(r+1)),"
+                                " no collective"),
                 "l2": "inputs larger than L2 (KV per GPU >> 126 MB)",
             },
             "e2e": None if e2e_value is None else {
@@ -338,14 +346,27 @@ def run_reference(args) -> None:
 # `--workload` selects one of the other BASELINE configs.  Each prints one line
 # of the same shape; the driver's default (no flag) is config 3 above.
 
-def _timed(fn, args, stream, world, dist, local):
+def _timed(fn, args, stream, world, dist, local, graph=False):
     """Warm-up, then args.steps calls of fn between CUDA events on the stream
-    (one event pair per call), clocks sampled meanwhile; max over ranks."""
+    (one event pair per call), clocks sampled meanwhile; max over ranks.
+
+    graph=True captures one call of fn (which must launch on the current
+    stream) into a CUDA graph and times its replays: the device-resident number
+    for kernels shorter than the Python call that launches them."""
     import torch
 
     for _ in range(args.warmup):
         fn()
     torch.cuda.synchronize()
+    if graph:
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            fn()
+        torch.cuda.synchronize()
+        fn = g.replay
+        for _ in range(args.warmup):
+            fn()
+        torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
     clocks = ClockSampler(local)
@@ -393,18 +414,19 @@ def run_prefill(args, gated: bool) -> None:
     stream = torch.cuda.current_stream()
     S, H, hd = cfg.seq_len, cfg.n_heads, cfg.head_dim
     p = fixtures.prefill_inputs(cfg)
-    r0, r1 = ydist.causal_row_split(S, world, rank)
+    # Weak scaling: every rank prefills its own S-token prompt (prompts are
+    # independent units; no collective).
+    r0, r1 = 0, S
     B = r1 - r0
     qs = H * hd
 
     def step():
-        if B > 0:
-            attn.attn_prefill(p.out[r0:r1], p.q[r0:r1], p.k, p.v, r0, B, H, cfg.n_kv_heads, hd, cfg.kv_dim, qs,
-                              gate=p.gate[r0:r1] if p.gate is not None else None, stream=stream)
+        attn.attn_prefill(p.out[r0:r1], p.q[r0:r1], p.k, p.v, r0, B, H, cfg.n_kv_heads, hd, cfg.kv_dim, qs,
+                          gate=p.gate[r0:r1] if p.gate is not None else None)
 
-    ms, per_call, clk = _timed(step, args, stream, world, dist, local)
-    flops = cfg.causal_flops()
-    my_flops = 4.0 * hd * H * sum(r + 1 for r in range(r0, r1))
+    ms, per_call, clk = _timed(step, args, stream, world, dist, local, graph=True)
+    flops = cfg.causal_flops() * world
+    my_flops = cfg.causal_flops()
     e2e = None
     if not args.no_e2e:
         qh = torch.empty(B * qs, dtype=torch.float32, pin_memory=True)
@@ -425,7 +447,8 @@ def run_prefill(args, gated: bool) -> None:
         ems, _, _ = _timed(e2e_step, args, stream, world, dist, local)
         nb = B * qs * 4
         e2e = {"value": round(flops / (ems / 1e3) / 1e12, 3), "unit": "TFLOP/s",
-               "h2d_bytes_per_step": int((nb + 2 * r1 * cfg.kv_dim * 2) * world), "d2h_bytes_per_step": int(nb * world)}
+               "h2d_bytes_per_step": int((nb + 2 * r1 * cfg.kv_dim * 2) * world), "d2h_bytes_per_step": int(nb * world),
+               "path": "attn_prefill API call per step, no graph"}
     peaks, src = load_peaks()
     achieved = my_flops / (per_call / 1e3) / 1e12
     roof = {"bound": "tensor", "achieved": round(achieved, 1), "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
@@ -439,9 +462,10 @@ def run_prefill(args, gated: bool) -> None:
                                flops / (ms / 1e3) / 1e12, "TFLOP/s", ms,
                                {"workload": cfg.name, "seq_len": S, "n_heads": H, "n_kv_heads": cfg.n_kv_heads,
                                 "head_dim": hd, "gated": gated, "flops": flops,
-                                "parallelism": f"query rows split x{world} (equal causal work)",
+                                "parallelism": f"data-parallel x{world}: one {S}-token prompt per GPU, no collective",
+                                "launch": "CUDA graph replay of the step (device-timed value)",
                                 "l2": "whole working set fits L2 (config size); no flush"},
-                               roof, args.steps, clk, e2e, cpu)), flush=True)
+                               roof, args.steps, clk, e2e, cpu, scaling="weak")), flush=True)
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
@@ -482,7 +506,7 @@ def run_gdn(args, decode: bool) -> None:
     stream = torch.cuda.current_stream()
     D, NK, NV = c.head_dim, c.num_k_heads, c.n_v_heads
     if decode:
-        s0, s1 = ydist.split_range(c.batch, world, rank)
+        s0, s1 = 0, c.batch      # weak scaling: every rank serves its own batch
         n = s1 - s0
         g = fixtures.gdn_inputs(c, c.batch, 1, seeded_state=True)
         S, q, k, v, o = g.S[s0:s1], g.q[s0:s1], g.k[s0:s1], g.v[s0:s1], g.out[s0:s1]
@@ -490,10 +514,9 @@ def run_gdn(args, decode: bool) -> None:
 
         def step():
             if n:
-                attn.gdn_decode(S, o, q, k, v, gt, bt, n, NK, D, NV, D, norm_w=g.norm_w, z=z, eps=c.eps,
-                                stream=stream)
-        ms, per_call, clk = _timed(step, args, stream, world, dist, local)
-        nbytes = c.batch * NV * D * D * 4 * 2
+                attn.gdn_decode(S, o, q, k, v, gt, bt, n, NK, D, NV, D, norm_w=g.norm_w, z=z, eps=c.eps)
+        ms, per_call, clk = _timed(step, args, stream, world, dist, local, graph=True)
+        nbytes = c.batch * world * NV * D * D * 4 * 2
         mine = n * NV * D * D * 4 * 2
         peaks, src = load_peaks()
         ach = mine / (per_call / 1e3) / 1e9
@@ -502,19 +525,20 @@ def run_gdn(args, decode: bool) -> None:
                 "peak_source": src}
         if rank == 0:
             print(json.dumps(_line(args, world, "GDN batch-32 decode tok/s (state read+write)",
-                                   c.batch / (ms / 1e3), "tok/s", ms,
+                                   c.batch * world / (ms / 1e3), "tok/s", ms,
                                    {"workload": c.name + "-decode-b32", "n_v_heads": NV, "num_k_heads": NK,
-                                    "head_dim": D, "batch": c.batch, "state_bytes_per_step": nbytes,
-                                    "parallelism": f"sequences x{world}", "l2": "state 134 MB > L2"},
-                                   roof, args.steps, clk)), flush=True)
+                                    "head_dim": D, "batch": c.batch * world, "state_bytes_per_step": nbytes,
+                                    "parallelism": f"data-parallel x{world}: a batch of {c.batch} per GPU",
+                                    "launch": "CUDA graph replay of the step", "l2": "state 134 MB per GPU > L2"},
+                                   roof, args.steps, clk, scaling="weak")), flush=True)
     else:
         T = c.tokens
         g = fixtures.gdn_inputs(c, 1, T, seeded_state=False)
 
         def step():
             attn.gdn_prefill(g.S, g.out, g.q, g.k, g.v, g.gate, g.beta, 1, T, NK, D, NV, D, norm_w=g.norm_w,
-                             z=g.z, eps=c.eps, stream=stream)
-        ms, per_call, clk = _timed(step, args, stream, world, dist, local)
+                             z=g.z, eps=c.eps)
+        ms, per_call, clk = _timed(step, args, stream, world, dist, local, graph=True)
         flops = T * NV * 7.0 * D * D
         peaks, src = load_peaks()
         ach = flops / (per_call / 1e3) / 1e12
@@ -523,10 +547,12 @@ def run_gdn(args, decode: bool) -> None:
                 "peak_source": src + " (dense bf16 burst)"}
         if rank == 0:
             print(json.dumps(_line(args, world, "GDN 4096-token prefill TFLOP/s (recurrent-equivalent FLOPs)",
-                                   flops / (ms / 1e3) / 1e12, "TFLOP/s", ms,
+                                   flops * world / (ms / 1e3) / 1e12, "TFLOP/s", ms,
                                    {"workload": c.name + "-prefill-4096", "n_v_heads": NV, "num_k_heads": NK,
-                                    "head_dim": D, "tokens": T, "flops": flops, "parallelism": "1 GPU"},
-                                   roof, args.steps, clk)), flush=True)
+                                    "head_dim": D, "tokens": T, "flops": flops * world,
+                                    "parallelism": f"data-parallel x{world}: one sequence per GPU",
+                                    "launch": "CUDA graph replay of the step"},
+                                   roof, args.steps, clk, scaling="weak")), flush=True)
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()

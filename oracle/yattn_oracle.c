@@ -257,6 +257,17 @@ int orc_max_threads(void)
 #endif
 }
 
+/* Thread count for the OpenMP loops (launchers such as torchrun export
+ * OMP_NUM_THREADS=1; the CPU baseline wants every host core). */
+void orc_set_threads(int n)
+{
+#ifdef _OPENMP
+    if (n > 0) omp_set_num_threads(n);
+#else
+    (void)n;
+#endif
+}
+
 void orc_f32_to_f16_buf(const float* src, uint16_t* dst, size_t n)
 {
     size_t i;

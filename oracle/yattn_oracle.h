@@ -28,6 +28,7 @@ extern "C" {
 /* ---- which build is this (0 = port, 1 = reference helpers linked) ---- */
 int orc_build_kind(void);
 int orc_max_threads(void);
+void orc_set_threads(int n);
 
 /* ---- helpers (platform.c / matvec.c semantics) ---- */
 float    orc_f16_to_f32(uint16_t h);                       /* platform.c:316-338 */

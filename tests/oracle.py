@@ -26,6 +26,7 @@ u32, u64, sz, dbl, flt, vp = C.c_uint32, C.c_uint64, C.c_size_t, C.c_double, C.c
 _PROTOS = {
     "orc_build_kind": (C.c_int, []),
     "orc_max_threads": (C.c_int, []),
+    "orc_set_threads": (None, [C.c_int]),
     "orc_f16_to_f32": (flt, [C.c_uint16]),
     "orc_f32_to_f16": (C.c_uint16, [flt]),
     "orc_softmax": (None, [f32p, u32]),

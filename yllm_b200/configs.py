@@ -62,6 +62,13 @@ class DecodeCfg:
             return [self.ctx_lo] * self.n_seqs
         return ctx_lengths(self.n_seqs, self.ctx_lo, self.ctx_hi, seed_of(self.cfg, "ctx"))
 
+    def ctx_of(self, seq: int) -> int:
+        """Context length of sequence `seq`; equals ctx()[seq] for seq < n_seqs and
+        extends the same draw to further sequences (other ranks' batches)."""
+        if self.ctx_lo == self.ctx_hi:
+            return self.ctx_lo
+        return self.ctx_lo + splitmix_draw(seed_of(self.cfg, "ctx"), seq) % (self.ctx_hi - self.ctx_lo + 1)
+
     def kv_bytes_per_step(self) -> int:
         """K+V bytes one decode step reads (all layers, all sequences)."""
         return sum(self.ctx()) * self.kv_dim * 2 * 2 * self.layers

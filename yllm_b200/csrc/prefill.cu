@@ -16,10 +16,11 @@
 //        P back over its own S columns as two fp16 planes P_hi + P_lo
 //        (P_lo = fp16(p - P_hi), ~22 bits instead of fp16's 11).
 //   4    TMA for K blocks, 6 TMA for V blocks: separate rings, no multicast.
-//   5    MMA: one thread issues S(j) = Q K(j)^T (A, B from smem) into two
-//        alternating TMEM S buffers and O += P_hi V + P_lo V with A = P read
-//        straight from TMEM (B = V from smem).  The tensor core runs its MMAs in
-//        issue order, so S(j+2) cannot overwrite P(j) before PV(j) has read it.
+//   5    MMA: one thread issues S(j) = Q K(j)^T (A, B from smem) into a ring of
+//        three TMEM S buffers and O += P_hi V + P_lo V with A = P read straight
+//        from TMEM (B = V from smem).  S runs up to three blocks ahead of the
+//        softmax; the tensor core runs its MMAs in issue order, so S(j+3)
+//        cannot overwrite P(j) before PV(j) has read it.
 // Keys past the end of the cache are zero-filled by TMA and masked.
 #include "common.cuh"
 #include "tcgen05.cuh"
@@ -44,10 +45,11 @@ template <int HD> struct PCfg {
     // + barriers, + alignment slack; at least 116 KB so one CTA (holding all 512 TMEM columns) runs per SM
     static constexpr int SMEM = (OFF_BAR + 256 + 1024) > 118784 ? (OFF_BAR + 256 + 1024) : 118784;
     static constexpr uint32_t TMEM_COLS = 512;
-    static constexpr uint32_t COL_S = 0;                     // two S buffers: [0, BN), [BN, 2BN); P over S
-    static constexpr uint32_t COL_O = 2 * BN;
+    static constexpr int NSB = 3;                            // S buffers in TMEM (P is written over its S)
+    static constexpr uint32_t COL_S = 0;                     // S buffer b at [b*BN, (b+1)*BN)
+    static constexpr uint32_t COL_O = NSB * BN;
     static constexpr uint32_t P_COLS = BN / 2;               // one fp16 P plane, two values per column
-    static_assert(2 * BN + HD <= 512, "TMEM columns");
+    static_assert(NSB * BN + HD <= 512, "TMEM columns");
     static_assert(SMEM <= 232448, "shared memory");
 };
 
@@ -62,7 +64,9 @@ struct PrefillParams {
 
 template <int KST> struct Bars {
     uint64_t k_full[KST], k_empty[KST], v_full[KST], v_empty[KST];
-    uint64_t s_full[2], p_full[2], pv_done, o_done, q_full, mma_drain;
+    // per S buffer b: S(j) ready, P(j) written, PV(j) accumulated, for the blocks j with j % 3 == b
+    uint64_t s_full[3], p_full[3], pv_done[3];
+    uint64_t o_done, q_full, mma_drain;
     uint32_t tmem_base;
     int abort_flag;
 };
@@ -127,11 +131,11 @@ __global__ void __launch_bounds__(kPThreads, 1)
             mbar_init(&bars->v_full[s], 1);
             mbar_init(&bars->v_empty[s], 1);
         }
-        for (int s = 0; s < 2; ++s) {
+        for (int s = 0; s < C::NSB; ++s) {
             mbar_init(&bars->s_full[s], 1);
             mbar_init(&bars->p_full[s], 4);
+            mbar_init(&bars->pv_done[s], 1);
         }
-        mbar_init(&bars->pv_done, 1);
         mbar_init(&bars->o_done, 1);
         mbar_init(&bars->q_full, 4);
         mbar_init(&bars->mma_drain, 1);
@@ -155,10 +159,30 @@ __global__ void __launch_bounds__(kPThreads, 1)
             constexpr uint32_t IDESC_PV = idesc_f16(BM, HD, 1);
             bool ok = mbar_wait_bounded(&bars->q_full, 0, p.status, ST_PREFILL_TIMEOUT, abort_flag);
             tc_fence_after();
+            // S(jj) = Q K(jj)^T into S buffer jj % NSB.  That buffer last held P(jj - NSB), whose PV
+            // product was issued earlier; the tensor core runs one thread's MMAs in issue order.
+            auto do_s = [&](uint32_t jj) -> bool {
+                const int s = jj % KST;
+                if (!mbar_wait_bounded(&bars->k_full[s], (jj / KST) & 1u, p.status, ST_PREFILL_TIMEOUT, abort_flag))
+                    return false;
+                const uint32_t sb = jj % C::NSB;
+                tc_fence_after();
+#pragma unroll
+                for (int kk = 0; kk < HD / 16; ++kk) {
+                    const uint64_t a = sdesc_sw128(sQ + (kk >> 2) * (BM * 128) + (kk & 3) * 32, 16, 1024);
+                    const uint64_t b = sdesc_sw128(sK + s * C::KV_BYTES + (kk >> 2) * (BN * 128) + (kk & 3) * 32, 16,
+                                                   1024);
+                    umma_f16(tmem + C::COL_S + sb * BN, a, b, IDESC_QK, kk > 0 ? 1u : 0u);
+                }
+                umma_commit(&bars->s_full[sb]);
+                umma_commit(&bars->k_empty[s]);
+                return true;
+            };
+            // O += P_hi V + P_lo V with A = P(jj) read from TMEM.
             auto do_pv = [&](uint32_t jj) -> bool {
                 const int s = jj % KST;
-                const uint32_t sb = jj & 1u;
-                if (!mbar_wait_bounded(&bars->p_full[sb], (jj >> 1) & 1u, p.status, ST_PREFILL_TIMEOUT,
+                const uint32_t sb = jj % C::NSB;
+                if (!mbar_wait_bounded(&bars->p_full[sb], (jj / C::NSB) & 1u, p.status, ST_PREFILL_TIMEOUT,
                                        abort_flag) ||
                     !mbar_wait_bounded(&bars->v_full[s], (jj / KST) & 1u, p.status, ST_PREFILL_TIMEOUT, abort_flag))
                     return false;
@@ -174,31 +198,17 @@ __global__ void __launch_bounds__(kPThreads, 1)
                     }
                 }
                 umma_commit(&bars->v_empty[s]);
-                umma_commit(&bars->pv_done);
+                umma_commit(&bars->pv_done[sb]);
                 return true;
             };
+            // Queue: S(0..NSB-1), then PV(j), S(j+NSB) as each P(j) arrives, so the next S blocks
+            // are ready before the softmax asks for them.
+            for (uint32_t j = 0; ok && j < nkb && j < static_cast<uint32_t>(C::NSB); ++j) ok = do_s(j);
             for (uint32_t j = 0; ok && j < nkb; ++j) {
-                const int s = j % KST;
-                if (!mbar_wait_bounded(&bars->k_full[s], (j / KST) & 1u, p.status, ST_PREFILL_TIMEOUT, abort_flag))
-                    break;
-                const uint32_t sb = j & 1u;
-                tc_fence_after();
-                // S buffer sb last held P(j-2); PV(j-2) was issued before this MMA, so it is read first.
-#pragma unroll
-                for (int kk = 0; kk < HD / 16; ++kk) {
-                    const uint64_t a = sdesc_sw128(sQ + (kk >> 2) * (BM * 128) + (kk & 3) * 32, 16, 1024);
-                    const uint64_t b = sdesc_sw128(sK + s * C::KV_BYTES + (kk >> 2) * (BN * 128) + (kk & 3) * 32, 16,
-                                                   1024);
-                    umma_f16(tmem + C::COL_S + sb * BN, a, b, IDESC_QK, kk > 0 ? 1u : 0u);
-                }
-                umma_commit(&bars->s_full[sb]);
-                umma_commit(&bars->k_empty[s]);
-                if (j >= 1 && !do_pv(j - 1)) {
-                    ok = false;
-                    break;
-                }
+                ok = do_pv(j);
+                if (ok && j + C::NSB < nkb) ok = do_s(j + C::NSB);
             }
-            if (ok && !*abort_flag && do_pv(nkb - 1)) umma_commit(&bars->o_done);
+            if (ok) umma_commit(&bars->o_done);
             // drain: every MMA issued so far completes before TMEM is freed
             umma_commit(&bars->mma_drain);
             volatile int dummy = 0;
@@ -208,18 +218,30 @@ __global__ void __launch_bounds__(kPThreads, 1)
         // ================= softmax warps 0-3 =================
         const int r = threadIdx.x;                                   // row of the tile
         // ---- Q tile: fp32 -> fp16, swizzled K-major ----
+        // 16 independent float4 loads in flight per thread, so the tile costs a few
+        // memory latencies rather than one per float4.
         constexpr int C4 = HD / 4;
-        for (int idx = threadIdx.x; idx < BM * C4; idx += 128) {
-            const int row = idx / C4, col = (idx % C4) * 4;
-            const uint32_t b = row0 + row;
-            float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-            if (b < p.B)
-                v = *reinterpret_cast<const float4*>(p.q + static_cast<size_t>(b) * p.q_stride +
-                                                     static_cast<size_t>(hh) * HD + col);
-            uint2 pk;
-            pk.x = h2_bits(__floats2half2_rn(v.x, v.y));
-            pk.y = h2_bits(__floats2half2_rn(v.z, v.w));
-            *reinterpret_cast<uint2*>(sQ + sw128_offset(row, col, BM)) = pk;
+        constexpr int QITER = BM * C4 / 128, QB = 16;
+        static_assert(QITER % QB == 0, "Q batches");
+        for (int i0 = 0; i0 < QITER; i0 += QB) {
+            float4 v[QB];
+#pragma unroll
+            for (int i = 0; i < QB; ++i) {
+                const int idx = threadIdx.x + (i0 + i) * 128;
+                const uint32_t b = row0 + idx / C4;
+                v[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+                if (b < p.B)
+                    v[i] = __ldcs(reinterpret_cast<const float4*>(p.q + static_cast<size_t>(b) * p.q_stride +
+                                                                  static_cast<size_t>(hh) * HD + (idx % C4) * 4));
+            }
+#pragma unroll
+            for (int i = 0; i < QB; ++i) {
+                const int idx = threadIdx.x + (i0 + i) * 128;
+                uint2 pk;
+                pk.x = h2_bits(__floats2half2_rn(v[i].x, v[i].y));
+                pk.y = h2_bits(__floats2half2_rn(v[i].z, v[i].w));
+                *reinterpret_cast<uint2*>(sQ + sw128_offset(idx / C4, (idx % C4) * 4, BM)) = pk;
+            }
         }
         fence_proxy_async_smem();
         __syncwarp();
@@ -231,8 +253,8 @@ __global__ void __launch_bounds__(kPThreads, 1)
         float m_run = -INFINITY, l_run = 0.f;                        // m_run in scaled log2 units
         bool ok = true;
         for (uint32_t j = 0; j < nkb; ++j) {
-            const uint32_t sb = j & 1u;
-            if (!warp_wait_bounded(&bars->s_full[sb], (j >> 1) & 1u, p.status, ST_PREFILL_TIMEOUT, abort_flag)) {
+            const uint32_t sb = j % C::NSB;
+            if (!warp_wait_bounded(&bars->s_full[sb], (j / C::NSB) & 1u, p.status, ST_PREFILL_TIMEOUT, abort_flag)) {
                 ok = false;
                 break;
             }
@@ -289,7 +311,8 @@ __global__ void __launch_bounds__(kPThreads, 1)
             m_run = m_use;
             // ---- O rescale (rare): PV(j-1) must have finished accumulating ----
             if (j >= 1 && __any_sync(0xffffffffu, grow)) {
-                if (!warp_wait_bounded(&bars->pv_done, (j - 1) & 1u, p.status, ST_PREFILL_TIMEOUT, abort_flag)) {
+                if (!warp_wait_bounded(&bars->pv_done[(j - 1) % C::NSB], ((j - 1) / C::NSB) & 1u, p.status,
+                                       ST_PREFILL_TIMEOUT, abort_flag)) {
                     ok = false;
                     break;
                 }
@@ -310,8 +333,7 @@ __global__ void __launch_bounds__(kPThreads, 1)
             if (lane == 0) mbar_arrive(&bars->p_full[sb]);
         }
         // ---- epilogue: O / l (x sigmoid(gate)) -> out ----
-        // pv_done can trail by two phases here (P is double-buffered), so the
-        // final accumulation has its own barrier.
+        // the last PV's completion, on a barrier of its own
         if (ok && warp_wait_bounded(&bars->o_done, 0, p.status, ST_PREFILL_TIMEOUT, abort_flag)) {
             tc_fence_after();
             const uint32_t b = row0 + r;

@@ -80,8 +80,7 @@ def decode_inputs(cfg: DecodeCfg, layers: Optional[list] = None, seqs: Optional[
     (seed numbering keeps the full config's indices)."""
     layers = list(range(cfg.layers)) if layers is None else list(layers)
     seqs = list(range(cfg.n_seqs)) if seqs is None else list(seqs)
-    all_ctx = cfg.ctx()
-    ctx = [all_ctx[s] for s in seqs]
+    ctx = [cfg.ctx_of(s) for s in seqs]
     L, kd, H, hd = len(layers), cfg.kv_dim, cfg.n_heads, cfg.head_dim
     offs, tot = [], 0
     for c in ctx:
