@@ -153,12 +153,13 @@ def run_ours(args) -> None:
     # default (and every reported number) is the full config.
     n_layers = args.layers or cfg.layers
     # Weak scaling: sequences are independent units, so at N GPUs the job is N
-    # batches of the config's size and rank r serves sequence ids
-    # [r*n, (r+1)*n) with no data-path collective.
+    # batches of the config's size (sequence ids 0..N*n-1), dealt to the ranks
+    # longest-first by context length; no data-path collective.
     n_per_rank = args.seqs or cfg.n_seqs
     n_total = n_per_rank * world
-    seqs = list(range(rank * n_per_rank, (rank + 1) * n_per_rank))
-    keys_all = sum(cfg.ctx_of(s) for s in range(n_total))
+    ctx_all = [cfg.ctx_of(s) for s in range(n_total)]
+    seqs = ydist.shard_by_length(ctx_all, world)[rank]   # longest-first greedy balance of keys
+    keys_all = sum(ctx_all)
     log(f"[rank {rank}] {len(seqs)} seqs, {sum(cfg.ctx_of(s) for s in seqs)} keys/layer, {n_layers} layers")
 
     d = fixtures.decode_inputs(cfg, layers=list(range(n_layers)), seqs=seqs, device=dev)
@@ -274,8 +275,8 @@ def run_ours(args) -> None:
                 "ctx_range": [cfg.ctx_lo, cfg.ctx_hi],
                 "total_keys_per_layer": keys_all,
                 "kv_bytes_per_step": keys_all * cfg.kv_dim * 2 * 2 * n_layers,
-                "parallelism": (f"data-parallel x{world}: rank r serves sequences [{n_per_rank}r, {n_per_rank}(r+1)),"
-                                " no collective"),
+                "parallelism": (f"sequence-sharded x{world}: {n_total} sequences dealt longest-first by context "
+                                "length, no collective"),
                 "l2": "inputs larger than L2 (KV per GPU >> 126 MB)",
             },
             "e2e": None if e2e_value is None else {
@@ -574,19 +575,35 @@ def run_long_decode(args) -> None:
     n = d.ctx[0]
     k0, k1 = ydist.split_range(n, world, rank)
     H, hd = c.n_heads, c.head_dim
-    ml = torch.zeros(H, 2, device=f"cuda:{local}")
-    o = torch.zeros(H, hd, device=f"cuda:{local}")
+    ex = ydist.PartialExchange(H, hd, device=f"cuda:{local}")
     out = d.out[0, 0]
     kv, vv = d.k_view(0, 0), d.v_view(0, 0)
 
     def step():
+        # launches on the current stream, so the step (NCCL included) can be graph-captured
         if world == 1:
-            attn.attn_decode(out, d.q[0, 0], kv, vv, n - 1, H, c.n_kv_heads, hd, c.kv_dim, stream=stream)
+            attn.attn_decode(out, d.q[0, 0], kv, vv, n - 1, H, c.n_kv_heads, hd, c.kv_dim)
         else:
-            attn.decode_partial(ml, o, d.q[0, 0], kv, vv, k0, k1, H, c.n_kv_heads, hd, c.kv_dim, stream=stream)
-            ydist.allgather_merge_partials(ml, o, out, H, hd)
+            attn.decode_partial(ex.ml, ex.o, d.q[0, 0], kv, vv, k0, k1, H, c.n_kv_heads, hd, c.kv_dim)
+            ex.run(out)
 
-    ms, per_call, clk = _timed(step, args, stream, world, dist, local)
+    ms, per_call, clk = _timed(step, args, stream, world, dist, local, graph=True)
+    e2e = None
+    if not args.no_e2e:
+        qh = torch.empty(H * hd, dtype=torch.float32, pin_memory=True)
+        qh.copy_(d.q[0, 0].cpu())
+        oh = torch.empty(H * hd, dtype=torch.float32, pin_memory=True)
+
+        def e2e_step():
+            d.q[0, 0].copy_(qh, non_blocking=True)
+            step()
+            oh.copy_(out, non_blocking=True)
+
+        ems, _, _ = _timed(e2e_step, args, stream, world, dist, local)
+        e2e = {"value": round(n * c.kv_dim * 4 / (ems / 1e3) / 1e9, 1), "unit": "GB/s",
+               "h2d_bytes_per_step": H * hd * 4 * world, "d2h_bytes_per_step": H * hd * 4 * world,
+               "path": "API calls per step (no graph), pinned host q in, out back"}
+    torch.cuda.synchronize()
     nbytes = n * c.kv_dim * 2 * 2
     peaks, src = load_peaks()
     ach = nbytes / (ms / 1e3) / 1e9
@@ -598,8 +615,9 @@ def run_long_decode(args) -> None:
                                {"workload": c.name, "ctx": n, "n_heads": H, "n_kv_heads": c.n_kv_heads,
                                 "head_dim": hd, "kv_bytes": nbytes,
                                 "parallelism": f"split-KV x{world}, NCCL all-gather of (m,l,o) + LSE merge",
+                                "launch": "CUDA graph replay of the step (partial decode, NCCL, merge)",
                                 "l2": "KV 537 MB > L2"},
-                               roof, args.steps, clk)), flush=True)
+                               roof, args.steps, clk, e2e)), flush=True)
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()

@@ -162,6 +162,14 @@ int yattn_merge_partials(float* out, const float* ml, const float* o, uint32_t n
                          uint32_t n_heads, uint32_t head_dim, const float* gate,
                          void* stream, char* err, size_t errlen);
 
+/* Same merge over packed parts: part s is parts[s*n_heads*(2+head_dim) ...],
+ * its (m, l) pairs [n_heads][2] followed by its o [n_heads][head_dim] -- the
+ * layout one all-gather of every rank's (ml, o) payload produces.  No
+ * reference counterpart: the reference has no split-KV path. */
+int yattn_merge_partials_packed(float* out, const float* parts, uint32_t n_parts,
+                                uint32_t n_heads, uint32_t head_dim, const float* gate,
+                                void* stream, char* err, size_t errlen);
+
 /* Error-returning form of cuda_k_attn_decode with an explicit stream and gate. */
 int yattn_attn_decode(float* att_out, const float* q, const uint16_t* kcache,
                       const uint16_t* vcache, const float* gate, uint32_t pos,

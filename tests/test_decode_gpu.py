@@ -243,6 +243,27 @@ def test_split_partials_merge_to_full(dev):
     assert torch.equal(out, out2)
 
 
+def test_packed_exchange_payload_merge(dev):
+    """The multi-GPU exchange layout: each shard's partials written into a
+    PartialExchange payload, the payloads laid end to end (what one
+    all-gather produces) and merged by merge_partials_packed."""
+    from yllm_b200 import attn
+    from yllm_b200.dist import PartialExchange
+
+    H, KV, hd, T = 32, 8, 128, 9000
+    q, k, v, kd, tq, tk, tv = _rand_case(dev, H, KV, hd, T, seed=78)
+    bounds = [0, 2250, 4500, 6750, T]
+    exs = [PartialExchange(H, hd, device=dev) for _ in range(4)]
+    for i, ex in enumerate(exs):
+        attn.decode_partial(ex.ml, ex.o, tq, tk, tv, bounds[i], bounds[i + 1], H, KV, hd, kd)
+    parts = torch.cat([ex.payload for ex in exs])
+    out = torch.zeros(H * hd, device=dev)
+    attn.merge_partials_packed(out, parts, 4, H, hd)
+    torch.cuda.synchronize()
+    want = oracle.attn_decode(q, k, v, T - 1, H, KV, hd, kd)
+    oracle.assert_close(out.cpu().numpy(), want, what="packed exchange merge")
+
+
 def test_repeated_runs_are_deterministic_and_reuse_workspace(dev):
     from yllm_b200 import attn
 

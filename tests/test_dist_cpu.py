@@ -103,6 +103,44 @@ def test_split_kv_exchange_two_gloo_ranks():
     assert ret[0] < 1e-12 and ret[1] < 1e-12
 
 
+def _exchange_worker(rank, world, port, ret):
+    """PartialExchange: preallocated buffers, two steps with new partials each."""
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=30))
+    H, D, T = 4, 16, 999
+    ex = ydist.PartialExchange(H, D, device="cpu")
+    worst = 0.0
+    for step in range(2):
+        rng = np.random.default_rng(step)
+        scores = rng.standard_normal((H, T)) * 3
+        v = rng.standard_normal((T, D))
+        a, b = ydist.split_range(T, world, rank)
+        ml, o = _partials(scores[:, a:b], v[a:b])
+        ex.ml.copy_(torch.from_numpy(ml))
+        ex.o.copy_(torch.from_numpy(o))
+        all_ml, all_o = ex.gather()
+        assert all_ml.shape == (world, H, 2) and all_o.shape == (world, H, D)
+        merged = lse_merge(all_ml.double().numpy(), all_o.double().numpy())
+        full_ml, full_o = _partials(scores, v)
+        ref = full_o / full_ml[:, 1:2]
+        worst = max(worst, float(np.max(np.abs(merged - ref) / np.maximum(np.abs(ref), 1e-3))))
+    ret[rank] = worst
+    dist.destroy_process_group()
+
+
+def test_partial_exchange_three_gloo_ranks():
+    ctx = mp.get_context("spawn")
+    ret = ctx.Manager().dict()
+    port = _free_port()
+    procs = [ctx.Process(target=_exchange_worker, args=(r, 3, port, ret)) for r in range(3)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(120)
+        assert p.exitcode == 0
+    assert all(ret[r] < 1e-4 for r in range(3)), dict(ret)
+
+
 def _leaver(rank, world, port, ret):
     """Rank 1 leaves between steps; rank 0's next exchange ends in an error
     after the process-group timeout instead of waiting forever."""

@@ -123,3 +123,31 @@ def test_gdn_rejects_unsupported(dev):
         attn.gdn_decode(g.S, g.out, g.q, g.k, g.v, g.gate, g.beta, 1, 16, 64, 32, 64)
     with pytest.raises(_lib.YattnError, match="together"):
         attn.gdn_decode(g.S, g.out, g.q, g.k, g.v, g.gate, g.beta, 1, 16, 128, 32, 128, norm_w=g.norm_w)
+
+
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_gdn_prefill_vhead_shards_match_whole(dev, world):
+    """Split by value head (no collective): each rank holds its heads' state,
+    v, z, gate, beta and output densely and reads q/k through the k-head
+    offset; the shards reproduce the unsharded call bit for bit."""
+    from yllm_b200 import attn, fixtures
+    from yllm_b200.configs import CFG5_GDN as c
+    from yllm_b200.dist import gdn_vhead_shard
+
+    D, NK, NV, T = c.head_dim, c.num_k_heads, c.n_v_heads, 48
+    g = fixtures.gdn_inputs(c, 1, T, seeded_state=True, device=dev)
+    S_whole = g.S.clone()
+    attn.gdn_prefill(S_whole, g.out, g.q, g.k, g.v, g.gate, g.beta, 1, T, NK, D, NV, D, norm_w=g.norm_w, z=g.z,
+                     eps=c.eps)
+    for r in range(world):
+        v0, v1, koff = gdn_vhead_shard(NV, NK, world, r)
+        n = v1 - v0
+        S = g.S[:, v0:v1].contiguous()
+        out = torch.full((T, n * D), float("nan"), device=dev)
+        attn.gdn_prefill(S, out, g.q.view(-1)[koff * D:], g.k.view(-1)[koff * D:],
+                         g.v[:, v0 * D:v1 * D].contiguous(), g.gate[:, v0:v1].contiguous(),
+                         g.beta[:, v0:v1].contiguous(), 1, T, NK, D, n, D, norm_w=g.norm_w,
+                         z=g.z[:, v0 * D:v1 * D].contiguous(), eps=c.eps)
+        torch.cuda.synchronize()
+        assert torch.equal(out, g.out[:, v0 * D:v1 * D]), f"rank {r} output"
+        assert torch.equal(S, S_whole[:, v0:v1]), f"rank {r} state"

@@ -140,3 +140,24 @@ def test_prefill_rejects_bad_geometry(dev):
         attn.attn_prefill(out, c["tq"], c["tk"], c["tv"], 0, 10, 8, 2, 96, c["kd"], c["qs"])
     with pytest.raises(_lib.YattnError, match="q_stride"):
         attn.attn_prefill(out, c["tq"], c["tk"], c["tv"], 0, 10, 8, 2, 128, c["kd"], 1022)
+
+
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_prefill_kv_head_shards_match_whole(dev, world):
+    """Split by KV head (each rank keeps whole GQA groups, no collective): the
+    shards, addressed by pointer offsets with the row strides unchanged,
+    reproduce the unsharded call bit for bit."""
+    from yllm_b200 import attn
+    from yllm_b200.dist import kv_head_shard
+
+    H, KV, hd, P0, B = 16, 8, 128, 64, 300
+    c = _case(dev, H, KV, hd, P0, B, seed=world)
+    whole = torch.zeros(B, c["qs"], device=dev)
+    attn.attn_prefill(whole, c["tq"], c["tk"], c["tv"], P0, B, H, KV, hd, c["kd"], c["qs"])
+    parts = torch.full((B, c["qs"]), float("nan"), device=dev)
+    for r in range(world):
+        h0, h1, g0, g1 = kv_head_shard(H, KV, world, r)
+        attn.attn_prefill(parts.view(-1)[h0 * hd:], c["tq"].view(-1)[h0 * hd:], c["tk"].view(-1)[g0 * hd:],
+                          c["tv"].view(-1)[g0 * hd:], P0, B, h1 - h0, g1 - g0, hd, c["kd"], c["qs"])
+    torch.cuda.synchronize()
+    assert torch.equal(parts, whole)

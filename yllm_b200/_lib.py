@@ -83,6 +83,7 @@ PROTOS = {
     "yattn_decode_partial_workspace_bytes": (sz, [u32, u32, u32, u32]),
     "yattn_decode_partial": (C.c_int, [vp, vp, vp, vp, vp, u32, u32, u32, u32, u32, u32, vp, sz, vp, *E]),
     "yattn_merge_partials": (C.c_int, [vp, vp, vp, u32, u32, u32, vp, vp, *E]),
+    "yattn_merge_partials_packed": (C.c_int, [vp, vp, u32, u32, u32, vp, vp, *E]),
     "yattn_attn_decode": (C.c_int, [vp, vp, vp, vp, vp, u32, u32, u32, u32, u32, vp, *E]),
     "yattn_attn_decode_noalloc": (C.c_int, [vp, vp, vp, vp, vp, u32, u32, u32, u32, u32, vp, *E]),
     "yattn_reserve": (C.c_int, [sz, *E]),

@@ -201,6 +201,13 @@ def merge_partials(out: torch.Tensor, ml: torch.Tensor, o: torch.Tensor, n_parts
          _ptr(gate), _stream(stream))
 
 
+def merge_partials_packed(out: torch.Tensor, parts: torch.Tensor, n_parts: int, n_heads: int, head_dim: int,
+                          gate: Optional[torch.Tensor] = None, stream=None) -> None:
+    """Log-sum-exp merge of packed parts [n_parts][n_heads*2 (m, l) + n_heads*head_dim (o)]."""
+    call("yattn_merge_partials_packed", out.data_ptr(), parts.data_ptr(), n_parts, n_heads, head_dim, _ptr(gate),
+         _stream(stream))
+
+
 def cuda_k_gdn_state_update(S: torch.Tensor, out: torch.Tensor, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
                             gate: torch.Tensor, beta: torch.Tensor, num_k_heads: int, hk: int, n_vheads: int,
                             hv: int) -> None:

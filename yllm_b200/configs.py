@@ -63,11 +63,14 @@ class DecodeCfg:
         return ctx_lengths(self.n_seqs, self.ctx_lo, self.ctx_hi, seed_of(self.cfg, "ctx"))
 
     def ctx_of(self, seq: int) -> int:
-        """Context length of sequence `seq`; equals ctx()[seq] for seq < n_seqs and
-        extends the same draw to further sequences (other ranks' batches)."""
+        """Context length of sequence `seq`: ctx()[seq % n_seqs].  A job of N
+        batches (one per GPU under weak scaling) repeats the config's lengths,
+        so every GPU's share has the config's work; the KV/q bytes still differ
+        per sequence (their seeds use the full sequence id)."""
         if self.ctx_lo == self.ctx_hi:
             return self.ctx_lo
-        return self.ctx_lo + splitmix_draw(seed_of(self.cfg, "ctx"), seq) % (self.ctx_hi - self.ctx_lo + 1)
+        i = seq % self.n_seqs
+        return self.ctx_lo + splitmix_draw(seed_of(self.cfg, "ctx"), i) % (self.ctx_hi - self.ctx_lo + 1)
 
     def kv_bytes_per_step(self) -> int:
         """K+V bytes one decode step reads (all layers, all sequences)."""

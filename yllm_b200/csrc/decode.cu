@@ -517,22 +517,23 @@ __global__ void __launch_bounds__(256) k_merge_splits(const float* __restrict__ 
 }
 
 // ---------------------------------------------------------------- merge kernel
+// Part s of head hh: (m, l) at ml[s*ml_stride + 2*hh], o at o[s*o_stride + hh*hd].
 __global__ void k_merge_partials(float* out, const float* ml, const float* o, uint32_t n_parts, uint32_t n_heads,
-                                 uint32_t hd, const float* gate) {
+                                 uint32_t hd, const float* gate, size_t ml_stride, size_t o_stride) {
     const uint32_t hh = blockIdx.x;
     for (uint32_t d = threadIdx.x; d < hd; d += blockDim.x) {
         float M = -INFINITY;
         for (uint32_t s = 0; s < n_parts; ++s) {
-            const float l = ml[(static_cast<size_t>(s) * n_heads + hh) * 2 + 1];
-            if (l > 0.f) M = fmaxf(M, ml[(static_cast<size_t>(s) * n_heads + hh) * 2]);
+            const float* mls = ml + s * ml_stride + 2 * hh;
+            if (mls[1] > 0.f) M = fmaxf(M, mls[0]);
         }
         float acc = 0.f, l = 0.f;
         for (uint32_t s = 0; s < n_parts; ++s) {
-            const size_t slot = static_cast<size_t>(s) * n_heads + hh;
-            const float ls = ml[slot * 2 + 1];
+            const float* mls = ml + s * ml_stride + 2 * hh;
+            const float ls = mls[1];
             if (!(ls > 0.f)) continue;
-            const float sc = ex2_approx(ml[slot * 2] - M);
-            acc += sc * o[slot * hd + d];
+            const float sc = ex2_approx(mls[0] - M);
+            acc += sc * o[s * o_stride + static_cast<size_t>(hh) * hd + d];
             l += sc * ls;
         }
         float r = acc / l;
@@ -910,9 +911,24 @@ extern "C" int yattn_merge_partials(float* out, const float* ml, const float* o,
         set_err(err, errlen, "merge_partials: bad arguments");
         return -1;
     }
-    k_merge_partials<<<n_heads, 128, 0, static_cast<cudaStream_t>(stream)>>>(out, ml, o, n_parts, n_heads,
-                                                                             head_dim, gate);
+    k_merge_partials<<<n_heads, 128, 0, static_cast<cudaStream_t>(stream)>>>(
+        out, ml, o, n_parts, n_heads, head_dim, gate, static_cast<size_t>(n_heads) * 2,
+        static_cast<size_t>(n_heads) * head_dim);
     YATTN_CHECK_LAUNCH(err, errlen, "merge_partials");
+    return 0;
+}
+
+extern "C" int yattn_merge_partials_packed(float* out, const float* parts, uint32_t n_parts, uint32_t n_heads,
+                                           uint32_t head_dim, const float* gate, void* stream, char* err,
+                                           size_t errlen) {
+    if (!out || !parts || n_parts == 0 || n_heads == 0 || head_dim == 0) {
+        set_err(err, errlen, "merge_partials_packed: bad arguments");
+        return -1;
+    }
+    const size_t part = static_cast<size_t>(n_heads) * (2 + head_dim);
+    k_merge_partials<<<n_heads, 128, 0, static_cast<cudaStream_t>(stream)>>>(
+        out, parts, parts + static_cast<size_t>(n_heads) * 2, n_parts, n_heads, head_dim, gate, part, part);
+    YATTN_CHECK_LAUNCH(err, errlen, "merge_partials_packed");
     return 0;
 }
 

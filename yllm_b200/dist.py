@@ -53,6 +53,36 @@ def causal_row_split(S: int, world: int, rank: int, quant: int = 128) -> tuple[i
     return cut(rank), cut(rank + 1)
 
 
+def kv_head_shard(n_heads: int, n_kv_heads: int, world: int, rank: int) -> tuple[int, int, int, int]:
+    """Attention split by KV head: rank keeps whole GQA groups, query heads
+    [h0, h1) and KV heads [g0, g1), so it needs no collective.  The shard is
+    addressed by pointer offsets alone (q/out + h0*head_dim, K/V + g0*head_dim,
+    the row strides q_stride and kv_dim unchanged)."""
+    if n_kv_heads % world:
+        raise ValueError(f"{n_kv_heads} KV heads do not split over {world} ranks")
+    per = n_kv_heads // world
+    g0, g1 = rank * per, (rank + 1) * per
+    group = n_heads // n_kv_heads
+    return g0 * group, g1 * group, g0, g1
+
+
+def gdn_vhead_shard(n_vheads: int, num_k_heads: int, world: int, rank: int) -> tuple[int, int, int]:
+    """GDN split by value head: rank owns v-heads [v0, v1) (state, v, gate,
+    beta, z, out for those heads) and reads the q/k heads h % num_k_heads they
+    map to.  Returns (v0, v1, k_off): with the q/k base pointers advanced by
+    k_off heads, the kernel's own mapping (local head) % num_k_heads lands on
+    the right q/k head for every local head."""
+    if n_vheads % world:
+        raise ValueError(f"{n_vheads} v-heads do not split over {world} ranks")
+    per = n_vheads // world
+    v0, v1 = rank * per, (rank + 1) * per
+    if v0 % num_k_heads == 0:
+        return v0, v1, 0
+    if per <= num_k_heads and v0 % num_k_heads + per <= num_k_heads:
+        return v0, v1, v0 % num_k_heads
+    raise ValueError(f"v-head shard [{v0}, {v1}) wraps the {num_k_heads} k-heads")
+
+
 def env_rank() -> tuple[int, int, int]:
     return (int(os.environ.get("RANK", "0")), int(os.environ.get("WORLD_SIZE", "1")),
             int(os.environ.get("LOCAL_RANK", "0")))
@@ -97,3 +127,44 @@ def allgather_merge_partials(ml: torch.Tensor, o: torch.Tensor, out: torch.Tenso
 
     all_ml, all_o, world = gather_partials(ml, o, n_heads, head_dim, group)
     attn.merge_partials(out, all_ml, all_o, world, n_heads, head_dim, gate)
+
+
+class PartialExchange:
+    """Preallocated split-KV exchange for repeated decode steps.
+
+    This rank's partials live in one payload buffer: `ml` [n_heads, 2] (m, l)
+    followed by `o` [n_heads, head_dim], both views that decode_partial writes
+    in place.  run() all-gathers the payload into [world, payload] with ONE
+    NCCL all-gather (straight into its final layout, no host-side copies) and
+    merges the packed parts on this GPU with the log-sum-exp kernel.  Every
+    call issues the same collective in the same order, so a whole step
+    (partial decode + exchange + merge) can be captured in one CUDA graph."""
+
+    def __init__(self, n_heads: int, head_dim: int, device, group=None):
+        self.group = group
+        self.world = dist.get_world_size(group) if dist.is_initialized() else 1
+        self.n_heads, self.head_dim = n_heads, head_dim
+        n = n_heads * (2 + head_dim)
+        self.payload = torch.zeros(n, dtype=torch.float32, device=device)
+        self.ml = self.payload[:n_heads * 2].view(n_heads, 2)
+        self.o = self.payload[n_heads * 2:].view(n_heads, head_dim)
+        self.parts = torch.zeros(self.world * n, dtype=torch.float32, device=device)
+
+    def gather(self) -> tuple[torch.Tensor, torch.Tensor]:
+        """All ranks' partials as ([world, n_heads, 2], [world, n_heads, head_dim]) tensors."""
+        if self.world > 1:
+            dist.all_gather_into_tensor(self.parts, self.payload, group=self.group)
+        else:
+            self.parts.copy_(self.payload)
+        p = self.parts.view(self.world, -1)
+        H = self.n_heads
+        return p[:, :H * 2].reshape(self.world, H, 2), p[:, H * 2:].reshape(self.world, H, self.head_dim)
+
+    def run(self, out: torch.Tensor, gate: Optional[torch.Tensor] = None) -> None:
+        from . import attn
+
+        if self.world > 1:
+            dist.all_gather_into_tensor(self.parts, self.payload, group=self.group)
+            attn.merge_partials_packed(out, self.parts, self.world, self.n_heads, self.head_dim, gate)
+        else:
+            attn.merge_partials_packed(out, self.payload, 1, self.n_heads, self.head_dim, gate)
