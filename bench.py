@@ -39,20 +39,51 @@ def load_peaks() -> tuple[dict, str]:
     return dict(PEAKS_FALLBACK), "fallback"
 
 
+# roofline.traffic: DRAM bytes per launch (dram__bytes_read.sum + dram__bytes_write.sum)
+# from one ncu capture of exactly the launch the bench times (the commands and the
+# rest of those captures are summarised under profiles/).  Workloads without such a
+# capture report null.
+NCU_TRAFFIC = {"decode": 1216305664, "prefill": 25236992}
+
+
 class ClockSampler:
-    """nvidia-smi sampling of SM clocks / throttle reasons during the timed region."""
+    """SM clock / throttle-reason sampling during the timed region: NVML every
+    5 ms in a thread (read-only queries), nvidia-smi every 200 ms if NVML is
+    missing.  Only samples taken while the region runs are kept; a region
+    shorter than the poll period gets one sample taken as it ends."""
 
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    NAMES = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
 
     def __init__(self, gpu_index: int):
         self.gpu = gpu_index
         self.proc = None
         self.lines: list[str] = []
         self.thread = None
+        self.nvml = None
+        self.samples: list[tuple[float, float, float, set]] = []
+        self.running = False
+        self.t_begin = 0.0
+
+    def begin(self):
+        """Marks the start of the timed region (NVML samples before it are dropped)."""
+        self.t_begin = time.perf_counter()
 
     def start(self):
+        try:
+            import pynvml
+
+            pynvml.nvmlInit()
+            self.nvml = (pynvml, pynvml.nvmlDeviceGetHandleByIndex(self.gpu))
+        except Exception:  # noqa: BLE001 -- no NVML: fall back to nvidia-smi
+            self.nvml = None
+        self.running = True
+        if self.nvml is not None:
+            self.thread = threading.Thread(target=self._poll_nvml, daemon=True)
+            self.thread.start()
+            return
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
@@ -63,11 +94,45 @@ class ClockSampler:
         self.thread = threading.Thread(target=self._read, daemon=True)
         self.thread.start()
 
+    def _sample_nvml(self):
+        nv, h = self.nvml
+        bits = {"hw_slowdown": nv.nvmlClocksEventReasonHwSlowdown,
+                "hw_thermal_slowdown": nv.nvmlClocksEventReasonHwThermalSlowdown,
+                "sw_thermal_slowdown": nv.nvmlClocksEventReasonSwThermalSlowdown,
+                "sw_power_cap": nv.nvmlClocksEventReasonSwPowerCap}
+        try:
+            sm = nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM)
+            smax = nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM)
+            r = nv.nvmlDeviceGetCurrentClocksEventReasons(h)
+            self.samples.append((time.perf_counter(), float(sm), float(smax),
+                                 {n for n, b in bits.items() if r & b}))
+        except Exception:  # noqa: BLE001
+            pass
+
+    def _poll_nvml(self):
+        while self.running:
+            self._sample_nvml()
+            time.sleep(0.005)
+
     def _read(self):
         for line in self.proc.stdout:
             self.lines.append(line.strip())
 
     def stop(self) -> dict:
+        self.running = False
+        if self.nvml is not None:
+            if self.thread:
+                self.thread.join(timeout=2)
+            source = "nvml 5 ms"
+            if not any(x[0] >= self.t_begin for x in self.samples):
+                self._sample_nvml()   # region shorter than the poll period: sample as it ends
+                source = "nvml, one sample as the region ended (region < 5 ms)"
+            kept = [x for x in self.samples if x[0] >= self.t_begin]
+            sm = [x[1] for x in kept]
+            smax = [x[2] for x in kept]
+            reasons = set().union(*[x[3] for x in kept]) if kept else set()
+            return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(smax) if smax else None,
+                    "reasons": sorted(reasons), "samples": len(sm), "source": source}
         if self.proc is None:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"], "samples": 0}
         self.proc.terminate()
@@ -78,7 +143,6 @@ class ClockSampler:
         if self.thread:
             self.thread.join(timeout=2)
         sm, smax, reasons = [], [], set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         for ln in self.lines:
             parts = [x.strip() for x in ln.split(",")]
             if len(parts) < 9:
@@ -88,11 +152,11 @@ class ClockSampler:
                 smax.append(float(parts[2]))
             except ValueError:
                 continue
-            for name, val in zip(names, parts[5:9]):
+            for name, val in zip(self.NAMES, parts[5:9]):
                 if val.lower().startswith("active"):
                     reasons.add(name)
         return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(smax) if smax else None,
-                "reasons": sorted(reasons), "samples": len(sm)}
+                "reasons": sorted(reasons), "samples": len(sm), "source": "nvidia-smi 200 ms"}
 
 
 # --------------------------------------------------------------- CPU side
@@ -191,6 +255,7 @@ def run_ours(args) -> None:
           for _ in range(args.steps * n_layers)]
     t0 = torch.cuda.Event(enable_timing=True)
     t1 = torch.cuda.Event(enable_timing=True)
+    clocks.begin()
     t0.record(stream)
     k = 0
     for _ in range(args.steps):
@@ -284,10 +349,12 @@ def run_ours(args) -> None:
                 "h2d_bytes_per_step": int(n_q * 4 * world), "d2h_bytes_per_step": int(n_q * 4 * world)},
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"],
                          "unit": "GB/s", "frac": round(achieved / peaks["hbm_gbs"], 4),
-                         "traffic": None, "kernel": "k_decode<128,4>", "peak_source": peak_src,
+                         "traffic": None if (args.seqs or args.layers) else NCU_TRAFFIC["decode"],
+                         "kernel": "k_decode<128,4>", "peak_source": peak_src,
                          "bytes_per_launch": bytes_per_launch, "launch_ms": round(launch_ms, 5)},
             "gpu_launches": args.steps * n_layers,
-            "clocks": {"sm_mhz": clk["sm_mhz"], "sm_max_mhz": clk["sm_max_mhz"], "reasons": clk["reasons"]},
+            "clocks": {"sm_mhz": clk["sm_mhz"], "sm_max_mhz": clk["sm_max_mhz"], "reasons": clk["reasons"],
+                       "samples": clk["samples"], "source": clk.get("source")},
         }
         if cpu is not None:
             line["cpu_baseline"] = cpu
@@ -347,14 +414,20 @@ def run_reference(args) -> None:
 # `--workload` selects one of the other BASELINE configs.  Each prints one line
 # of the same shape; the driver's default (no flag) is config 3 above.
 
-def _timed(fn, args, stream, world, dist, local, graph=False):
+def _timed(fn, args, stream, world, dist, local, graph=False, flush_l2=False):
     """Warm-up, then args.steps calls of fn between CUDA events on the stream
     (one event pair per call), clocks sampled meanwhile; max over ranks.
 
     graph=True captures one call of fn (which must launch on the current
     stream) into a CUDA graph and times its replays: the device-resident number
-    for kernels shorter than the Python call that launches them."""
+    for kernels shorter than the Python call that launches them.
+
+    flush_l2=True writes a 256 MB buffer (twice the L2) between timed calls,
+    outside each call's event pair, for inputs that fit in L2; the step time is
+    then the sum of the per-call device times."""
     import torch
+
+    scrub = torch.empty(256 << 20, dtype=torch.uint8, device=f"cuda:{local}") if flush_l2 else None
 
     for _ in range(args.warmup):
         fn()
@@ -375,18 +448,22 @@ def _timed(fn, args, stream, world, dist, local, graph=False):
     time.sleep(0.3)
     ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    clocks.begin()
     t0.record(stream)
     for a, b in ev:
+        if scrub is not None:
+            scrub.fill_(1)
         a.record(stream)
         fn()
         b.record(stream)
     t1.record(stream)
     torch.cuda.synchronize()
     clk = clocks.stop()
-    total = torch.tensor([t0.elapsed_time(t1)], device=f"cuda:{local}")
+    per_call = sum(a.elapsed_time(b) for a, b in ev) / len(ev)
+    total = torch.tensor([per_call * args.steps if scrub is not None else t0.elapsed_time(t1)],
+                         device=f"cuda:{local}")
     if world > 1:
         dist.all_reduce(total, op=dist.ReduceOp.MAX)
-    per_call = sum(a.elapsed_time(b) for a, b in ev) / len(ev)
     return float(total.item()) / args.steps, per_call, clk
 
 
@@ -396,7 +473,8 @@ def _line(args, world, metric, value, unit, ms, cfg_dict, roofline, launches, cl
             "warmup": args.warmup, "ms_per_step": round(ms, 5), "higher_is_better": higher, "scaling": scaling,
             "vs_baseline": None, "dtype": "f32 math, fp16 Q/K/V/P hi+lo", "data": "synthetic (seeded)",
             "config": cfg_dict, "e2e": e2e, "roofline": roofline, "gpu_launches": launches,
-            "clocks": {"sm_mhz": clk["sm_mhz"], "sm_max_mhz": clk["sm_max_mhz"], "reasons": clk["reasons"]}}
+            "clocks": {"sm_mhz": clk["sm_mhz"], "sm_max_mhz": clk["sm_max_mhz"], "reasons": clk["reasons"],
+                       "samples": clk["samples"], "source": clk.get("source")}}
     if cpu is not None:
         line["cpu_baseline"] = cpu
     return line
@@ -425,7 +503,7 @@ def run_prefill(args, gated: bool) -> None:
         attn.attn_prefill(p.out[r0:r1], p.q[r0:r1], p.k, p.v, r0, B, H, cfg.n_kv_heads, hd, cfg.kv_dim, qs,
                           gate=p.gate[r0:r1] if p.gate is not None else None)
 
-    ms, per_call, clk = _timed(step, args, stream, world, dist, local, graph=True)
+    ms, per_call, clk = _timed(step, args, stream, world, dist, local, graph=True, flush_l2=True)
     flops = cfg.causal_flops() * world
     my_flops = cfg.causal_flops()
     e2e = None
@@ -453,7 +531,7 @@ def run_prefill(args, gated: bool) -> None:
     peaks, src = load_peaks()
     achieved = my_flops / (per_call / 1e3) / 1e12
     roof = {"bound": "tensor", "achieved": round(achieved, 1), "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
-            "frac": round(achieved / peaks["bf16_tflops"], 4), "traffic": None,
+            "frac": round(achieved / peaks["bf16_tflops"], 4), "traffic": None if gated else NCU_TRAFFIC["prefill"],
             "kernel": f"k_prefill<{hd}>", "peak_source": src + " (dense bf16 burst)"}
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -465,7 +543,7 @@ def run_prefill(args, gated: bool) -> None:
                                 "head_dim": hd, "gated": gated, "flops": flops,
                                 "parallelism": f"data-parallel x{world}: one {S}-token prompt per GPU, no collective",
                                 "launch": "CUDA graph replay of the step (device-timed value)",
-                                "l2": "whole working set fits L2 (config size); no flush"},
+                                "l2": "L2 flushed between timed steps (256 MB write outside the step's events)"},
                                roof, args.steps, clk, e2e, cpu, scaling="weak")), flush=True)
     if world > 1:
         dist.barrier()

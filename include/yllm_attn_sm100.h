@@ -111,15 +111,18 @@ typedef struct YattnDecodeWork {
     uint32_t t_end;
     uint32_t part_base;   /* first partial slot of this (item, head group); unused if n_splits == 1 */
     uint32_t group;       /* merge counter of this (item, head group); unused if n_splits == 1 */
-    uint32_t reserved;
+    uint32_t cta;         /* CTA that streams this unit; units are grouped by cta, in order */
 } YattnDecodeWork;
 
 /* Host-side schedule.  pos_host[n_items] are the items' query positions.
- * split_tokens = 0 picks a split length that gives about target_ctas work
- * units (target_ctas = 0: one per SM of the current device).  Writes up to
- * work_cap entries to work_host (host memory).  The schedule depends only on
- * the positions and the head geometry, so one plan serves every layer of a
- * decode step. */
+ * split_tokens = 0: balanced plan.  The key ranges of every (item, head group)
+ * are laid end to end and cut into target_ctas equal chunks (target_ctas = 0:
+ * one per SM of the current device); a CTA streams its chunk as one or more
+ * units (segments of one (item, head group) each), so every CTA moves the
+ * same bytes.  split_tokens > 0: uniform splits of that length, one unit per
+ * CTA, longest first.  Writes up to work_cap entries to work_host (host
+ * memory).  The schedule depends only on the positions and the head geometry,
+ * so one plan serves every layer of a decode step. */
 int yattn_decode_plan(const uint32_t* pos_host, uint32_t n_items, uint32_t n_kv_heads,
                       uint32_t head_dim, uint32_t split_tokens, uint32_t target_ctas,
                       YattnDecodeWork* work_host, uint32_t work_cap,

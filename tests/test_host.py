@@ -97,8 +97,43 @@ def test_decode_plan_covers_every_key_once(pos, n_kv, hd, split):
             assert sorted(s[2] for s in segs) == list(range(len(segs)))
             assert all(s[3] == len(segs) for s in segs)
     assert sorted(parts) == list(range(n_parts)) and groups == set(range(n_groups))
-    lens = [w.t_end - w.t_begin for w in work]
-    assert lens == sorted(lens, reverse=True)
+    ctas = [w.cta for w in work]
+    assert ctas == sorted(ctas)          # units grouped by the CTA that streams them
+    if split:                            # uniform splits: one unit per CTA, longest first
+        lens = [w.t_end - w.t_begin for w in work]
+        assert lens == sorted(lens, reverse=True) and ctas == list(range(len(work)))
+
+
+@pytest.mark.parametrize("target", [148, 37])
+def test_balanced_plan_evens_out_ctas(target):
+    """Automatic splits: units are grouped by CTA in increasing order, the plan
+    fits one wave, no CTA carries more than ~10 % over an equal share of keys
+    (each further unit charged 192 keys), no (item, head group) has more than
+    32 splits, and split numbering matches the range order."""
+    from yllm_b200.configs import CFG3 as c
+
+    pos = [x - 1 for x in c.ctx()]
+    hc = heads_per_cta(c.n_kv_heads, c.head_dim)
+    work, _, _ = _plan(pos, c.n_kv_heads, c.head_dim, 0, target)
+    ctas = [w.cta for w in work]
+    assert ctas == sorted(ctas) and ctas[0] == 0 and set(ctas) == set(range(ctas[-1] + 1))
+    load, units = {}, {}
+    for w in work:
+        load[w.cta] = load.get(w.cta, 0) + (w.t_end - w.t_begin)
+        units[w.cta] = units.get(w.cta, 0) + 1
+    total = sum(p + 1 for p in pos) * (c.n_kv_heads // hc)
+    share = total / target
+    charged = [load[k] + 192 * (units[k] - 1) for k in load]  # each further unit costs ~192 keys
+    assert max(charged) <= 1.1 * share + 128
+    assert len(load) <= target                               # one wave
+    by_range = {}
+    for w in work:
+        by_range.setdefault((w.item, w.kv_head), []).append(w)
+    for segs in by_range.values():
+        assert len(segs) <= 32
+        assert [w.split for w in segs] == list(range(len(segs)))
+        assert all(w.n_splits == len(segs) for w in segs)
+        assert all(w.t_end - w.t_begin >= 128 or len(segs) == 1 for w in segs)
 
 
 def test_plan_rejects_bad_args():

@@ -49,7 +49,7 @@ class YattnDecodeWork(C.Structure):
         ("t_end", u32),
         ("part_base", u32),
         ("group", u32),
-        ("reserved", u32),
+        ("cta", u32),
     ]
 
 

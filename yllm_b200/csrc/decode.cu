@@ -30,6 +30,9 @@ namespace yattn {
 namespace {
 
 constexpr int kSplitQuant = 64;     // split lengths are multiples of this
+constexpr uint32_t kSplitMin = 128;  // shortest split of a balanced plan (keys)
+constexpr uint32_t kMaxSplits = 32;  // most splits of one (item, head group) in a balanced plan
+constexpr uint32_t kUnitCost = 192;  // keys charged for each further unit of a CTA
 
 // Per head_dim: NCW consumer warps, ring of NST stages sized for the worst case (HC = 1).
 template <int HD> struct DecodeCfg {
@@ -57,6 +60,7 @@ struct DecodeParams {
     uint32_t t_base;                  // key offset when work == nullptr
     uint32_t t_end0;                  // end key (exclusive) when work == nullptr
     uint32_t n_heads, n_kv, kv_dim, hc;
+    uint32_t n_work;                  // entries of work (grouped by cta)
     float scale_log2;                 // log2(e) / sqrt(head_dim)
     float* part_ml;                   // [n_parts][G][2]
     float* part_o;                    // [n_parts][G][HD]
@@ -111,6 +115,25 @@ __device__ __forceinline__ void split_h2(float a, float b, uint32_t& hi, uint32_
     lo = pack_h2(a - f.x, b - f.y);
 }
 
+// First index i of work[0..n) with work[i].cta >= c (units are grouped by cta in
+// increasing order).  Called by a whole warp: each round the 32 lanes probe 32
+// evenly spaced units, narrowing the range 32-fold per dependent load.
+__device__ __forceinline__ uint32_t first_unit_from(const YattnDecodeWork* work, uint32_t n, uint32_t c, int lane) {
+    uint32_t lo = 0, hi = n;   // answer in [lo, hi]
+    while (hi > lo) {
+        const uint32_t step = (hi - lo + 31) / 32;
+        const uint32_t idx = lo + static_cast<uint32_t>(lane) * step;
+        const bool before = idx < hi && work[idx].cta < c;
+        const uint32_t k = __popc(__ballot_sync(0xffffffffu, before));   // probes before the answer
+        if (k == 0) return lo;
+        const uint32_t nlo = lo + (k - 1) * step + 1;
+        hi = min(hi, lo + k * step);
+        lo = nlo;
+        if (step == 1) return lo;
+    }
+    return lo;
+}
+
 // Warp NCW is the producer; consumer warp w owns kv head kg*HC + (w % HC) of
 // the group and tokens [16*(w / HC), +16) of every stage (TOK = 16*NCW/HC tokens).
 // Per 16-token step, on the legacy tensor cores (mma.sync m16n8k16, fp32 accumulate):
@@ -144,311 +167,372 @@ __global__ void __launch_bounds__(DecodeCfg<HD>::THREADS, 1) k_decode(const Deco
     const uint32_t TILEB = TOK * RS;
     const uint32_t STAGEB = 2 * TILEB;
 
-    // ---- work unit ----
-    YattnDecodeItem it;
-    uint32_t kg, t0, t1, n_splits, split, part_base, group;
-    if (p.work) {
-        const YattnDecodeWork w = p.work[blockIdx.x];
-        it = p.items[w.item];
-        kg = w.kv_head / HC;
-        t0 = w.t_begin;
-        t1 = w.t_end;
-        n_splits = w.n_splits;
-        split = w.split;
-        part_base = w.part_base;
-        group = w.group;
-    } else {
-        it = p.item0;
-        kg = blockIdx.x / p.n_splits0;
-        split = blockIdx.x % p.n_splits0;
-        n_splits = p.n_splits0;
-        t0 = p.t_base + split * p.split_len;
-        t1 = min(t0 + p.split_len, p.t_end0);
-        part_base = kg * HC * p.n_splits0;
-        group = kg;
+    // ---- this CTA's units: a run of the plan (grouped by cta) or one uniform split ----
+    uint32_t* s_range = reinterpret_cast<uint32_t*>(last_flag + 1);   // [2]
+    if (warp == 0) {
+        uint32_t ub = blockIdx.x, ue = blockIdx.x + 1;
+        if (p.work) {   // warp-wide 32-way searches: about two dependent loads each
+            ub = first_unit_from(p.work, p.n_work, blockIdx.x, lane);
+            ue = first_unit_from(p.work, p.n_work, blockIdx.x + 1, lane);
+        }
+        if (lane == 0) {
+            s_range[0] = ub;
+            s_range[1] = ue;
+        }
     }
-    const uint32_t ntok = t1 - t0;
-    const uint32_t ntiles = (ntok + TOK - 1) / TOK;
-
     if (threadIdx.x == 0) {
         for (int s = 0; s < C::NST; ++s) {
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], NCW);
         }
-        for (uint32_t hl = 0; hl < HC; ++hl) group_of(kg * HC + hl, p.n_heads, p.n_kv, s_gfirst[hl], s_gcnt[hl]);
         abort_flag[0] = 0;
-        last_flag[0] = 0;
         fence_mbar_init();
     }
     __syncthreads();
+    const uint32_t u_begin = s_range[0], u_end = s_range[1];
 
-    if (warp == NCW) {
-        // ================= producer: one bulk copy per row per tensor =================
-        const uint16_t* kb = it.k + static_cast<size_t>(kg) * HC * HD;
-        const uint16_t* vb = it.v + static_cast<size_t>(kg) * HC * HD;
-        uint32_t issued = 0;
-        for (uint32_t i = 0; i < ntiles; ++i) {
-            const int s = i % C::NST;
-            if (i >= static_cast<uint32_t>(C::NST)) {
-                if (!warp_wait_bounded(&empty[s], ((i / C::NST) & 1u) ^ 1u, p.status, ST_DECODE_EMPTY_TIMEOUT,
-                                       abort_flag))
-                    break;
-            }
-            const uint32_t tile0 = t0 + i * TOK;
-            const uint32_t nrows = min(TOK, t1 - tile0);
-            uint8_t* kdst = stages + s * STAGEB;
-            uint8_t* vdst = kdst + TILEB;
-            if (lane == 0) mbar_arrive_expect_tx(&full[s], 2u * nrows * ROWB);
-            __syncwarp();
-            for (uint32_t r = lane; r < nrows; r += 32) {
-                const size_t off = static_cast<size_t>(tile0 + r) * p.kv_dim;
-                bulk_g2s(kdst + r * RS, kb + off, ROWB, &full[s]);
-                bulk_g2s(vdst + r * RS, vb + off, ROWB, &full[s]);
-            }
-            issued = i + 1;
-        }
-        // Never leave with copies in flight: wait (bounded) for the last stages issued.
-        for (uint32_t i = (issued > static_cast<uint32_t>(C::NST) ? issued - C::NST : 0); i < issued; ++i) {
-            volatile int dummy = 0;
-            mbar_wait_bounded(&full[i % C::NST], (i / C::NST) & 1u, p.status, ST_DECODE_FULL_TIMEOUT, &dummy);
-        }
-        return;
-    }
-
-    // ================= consumers =================
-    const uint32_t hl = warp % HC;                 // head within the group
-    const uint32_t sl = warp / HC;                 // 16-token slice of each stage
-    const uint32_t gfirst = s_gfirst[hl], gcnt = s_gcnt[hl];
-    const int g8 = lane >> 2;                      // fragment row group: token (S^T), dim (O^T), head (B)
-    const int t4 = lane & 3;                       // fragment column pair: heads 2*t4, 2*t4+1
-    // Q^T as the MMA B operand: b0 = q[head g8][16kk + 2t4 .. +1], b1 = q[head g8][16kk + 2t4 + 8 .. +9]
-    uint32_t qhi[KS][2], qlo[KS][2];
-    {
-        const bool hv = static_cast<uint32_t>(g8) < gcnt;
-        const float* qh = it.q + static_cast<size_t>(gfirst + (hv ? g8 : 0)) * HD;
-#pragma unroll
-        for (int kk = 0; kk < KS; ++kk) {
-            float2 x0 = make_float2(0.f, 0.f), x1 = make_float2(0.f, 0.f);
-            if (hv) {
-                x0 = *reinterpret_cast<const float2*>(qh + kk * 16 + 2 * t4);
-                x1 = *reinterpret_cast<const float2*>(qh + kk * 16 + 2 * t4 + 8);
-            }
-            split_h2(x0.x, x0.y, qhi[kk][0], qlo[kk][0]);
-            split_h2(x1.x, x1.y, qhi[kk][1], qlo[kk][1]);
-        }
-    }
-    float oc[KS][4];
-#pragma unroll
-    for (int mt = 0; mt < KS; ++mt) oc[mt][0] = oc[mt][1] = oc[mt][2] = oc[mt][3] = 0.f;
-    float m_a = -INFINITY, m_b = -INFINITY, l_a = 0.f, l_b = 0.f;    // heads 2*t4 and 2*t4+1
-    uint8_t* pt = pt_all + warp * C::PT_BYTES;
-    const uint32_t pt_u = smem_u32(pt);
-    // ldmatrix lane addresses relative to the warp's 16-row slice of a tile
-    const uint32_t slice = (16 * sl) * RS + hl * HD * 2;
-    const uint32_t a_off = slice + ((lane & 7) + ((lane >> 3) & 1) * 8) * RS + ((lane >> 4) & 1) * 16;   // K
-    const uint32_t v_off = slice + ((lane & 7) + ((lane >> 4) & 1) * 8) * RS + ((lane >> 3) & 1) * 16;   // V^T
-    const uint32_t p_off = (lane & 7) * 48 + ((lane >> 3) & 1) * 16;                                     // P^T
-
-    for (uint32_t i = 0; i < ntiles; ++i) {
-        const int s = i % C::NST;
-        if (!warp_wait_bounded(&full[s], (i / C::NST) & 1u, p.status, ST_DECODE_FULL_TIMEOUT, abort_flag)) break;
-        const uint32_t nrows = min(TOK, t1 - (t0 + i * TOK));
-        const int nvalid = max(0, min(16, static_cast<int>(nrows) - static_cast<int>(16 * sl)));
-        if (nvalid > 0) {
-            const uint32_t kt = smem_u32(stages + s * STAGEB);
-            const uint32_t vt = kt + TILEB;
-            // ---- S^T = K Q^T ----
-            float sc[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-            for (int kk = 0; kk < KS; ++kk) {
-                uint32_t a[4];
-                ldsm_x4(kt + a_off + kk * 32, a);
-                mma16816(sc, a, qhi[kk][0], qhi[kk][1]);
-                mma16816(sc, a, qlo[kk][0], qlo[kk][1]);
-            }
-            // sc: [0] = (token g8, head 2t4), [1] = (g8, 2t4+1), [2] = (g8+8, 2t4), [3] = (g8+8, 2t4+1)
-            const bool v0 = g8 < nvalid, v1 = g8 + 8 < nvalid;
-            const float s0 = v0 ? sc[0] * p.scale_log2 : -INFINITY;
-            const float s1 = v0 ? sc[1] * p.scale_log2 : -INFINITY;
-            const float s2 = v1 ? sc[2] * p.scale_log2 : -INFINITY;
-            const float s3 = v1 ? sc[3] * p.scale_log2 : -INFINITY;
-            float mx_a = fmaxf(s0, s2), mx_b = fmaxf(s1, s3);
-#pragma unroll
-            for (int o = 4; o <= 16; o <<= 1) {
-                mx_a = fmaxf(mx_a, __shfl_xor_sync(0xffffffffu, mx_a, o));
-                mx_b = fmaxf(mx_b, __shfl_xor_sync(0xffffffffu, mx_b, o));
-            }
-            const float mn_a = fmaxf(m_a, mx_a), mn_b = fmaxf(m_b, mx_b);
-            const float al_a = ex2_approx(m_a - mn_a), al_b = ex2_approx(m_b - mn_b);
-            const float p0 = ex2_approx(s0 - mn_a), p1 = ex2_approx(s1 - mn_b);
-            const float p2 = ex2_approx(s2 - mn_a), p3 = ex2_approx(s3 - mn_b);
-            float sum_a = p0 + p2, sum_b = p1 + p3;
-#pragma unroll
-            for (int o = 4; o <= 16; o <<= 1) {
-                sum_a += __shfl_xor_sync(0xffffffffu, sum_a, o);
-                sum_b += __shfl_xor_sync(0xffffffffu, sum_b, o);
-            }
-            l_a = l_a * al_a + sum_a;
-            l_b = l_b * al_b + sum_b;
-            m_a = mn_a;
-            m_b = mn_b;
-            // ---- P^T (rows = heads, 16 tokens, 48 B row stride) as fp16 hi and lo planes ----
-            {
-                uint32_t h01, l01, h23, l23;
-                split_h2(p0, p1, h01, l01);      // (token g8: heads 2t4, 2t4+1)
-                split_h2(p2, p3, h23, l23);      // (token g8+8: heads 2t4, 2t4+1)
-                uint16_t* hp = reinterpret_cast<uint16_t*>(pt);
-                uint16_t* lp = reinterpret_cast<uint16_t*>(pt + 384);
-                const int ra = (2 * t4) * 24, rb = (2 * t4 + 1) * 24;   // row offsets in halves
-                hp[ra + g8] = static_cast<uint16_t>(h01);
-                hp[rb + g8] = static_cast<uint16_t>(h01 >> 16);
-                hp[ra + g8 + 8] = static_cast<uint16_t>(h23);
-                hp[rb + g8 + 8] = static_cast<uint16_t>(h23 >> 16);
-                lp[ra + g8] = static_cast<uint16_t>(l01);
-                lp[rb + g8] = static_cast<uint16_t>(l01 >> 16);
-                lp[ra + g8 + 8] = static_cast<uint16_t>(l23);
-                lp[rb + g8 + 8] = static_cast<uint16_t>(l23 >> 16);
-            }
-            __syncwarp();
-            uint32_t ph0, ph1, pl0, pl1;
-            ldsm_x2(pt_u + p_off, ph0, ph1);
-            ldsm_x2(pt_u + 384 + p_off, pl0, pl1);
-            // ---- O^T = O^T * alpha + V^T P^T ----
-            // V rows past nvalid hold stale (or never written) shared memory: their
-            // p is 0, but 0 * NaN would still poison the MMA, so zero those lanes.
-            // The A fragment holds tokens 2t4, 2t4+1 (a0, a1) and 2t4+8, 2t4+9 (a2, a3).
-            uint32_t vm01 = 0xffffffffu, vm23 = 0xffffffffu;
-            if (nvalid < 16) {
-                vm01 = (2 * t4 < nvalid ? 0x0000ffffu : 0u) | (2 * t4 + 1 < nvalid ? 0xffff0000u : 0u);
-                vm23 = (2 * t4 + 8 < nvalid ? 0x0000ffffu : 0u) | (2 * t4 + 9 < nvalid ? 0xffff0000u : 0u);
-            }
-#pragma unroll
-            for (int mt = 0; mt < KS; ++mt) {
-                oc[mt][0] *= al_a;
-                oc[mt][1] *= al_b;
-                oc[mt][2] *= al_a;
-                oc[mt][3] *= al_b;
-                uint32_t a[4];
-                ldsm_x4_t(vt + v_off + mt * 32, a);
-                a[0] &= vm01;
-                a[1] &= vm01;
-                a[2] &= vm23;
-                a[3] &= vm23;
-                mma16816(oc[mt], a, ph0, ph1);
-                mma16816(oc[mt], a, pl0, pl1);
-            }
-            __syncwarp();   // P^T is rewritten by the next step
-        }
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&empty[s]);
-    }
-
-    // ---- merge the consumer warps (ring is free: every stage was consumed) ----
-    named_bar_sync(1, 32 * NCW);
-    if (abort_flag[0]) return;
-    {
-        const int ha = 2 * t4, hb = 2 * t4 + 1;
-        if (g8 == 0) {
-            if (ha < G) {
-                mrg_ml[(warp * G + ha) * 2 + 0] = m_a;
-                mrg_ml[(warp * G + ha) * 2 + 1] = l_a;
-            }
-            if (hb < G) {
-                mrg_ml[(warp * G + hb) * 2 + 0] = m_b;
-                mrg_ml[(warp * G + hb) * 2 + 1] = l_b;
-            }
-        }
-#pragma unroll
-        for (int mt = 0; mt < KS; ++mt) {
-            const int d0 = mt * 16 + g8, d1 = d0 + 8;
-            if (ha < G) {
-                mrg_o[(warp * G + ha) * HD + d0] = oc[mt][0];
-                mrg_o[(warp * G + ha) * HD + d1] = oc[mt][2];
-            }
-            if (hb < G) {
-                mrg_o[(warp * G + hb) * HD + d0] = oc[mt][1];
-                mrg_o[(warp * G + hb) * HD + d1] = oc[mt][3];
-            }
-        }
-    }
-    named_bar_sync(1, 32 * NCW);
-
-    const int tid = threadIdx.x;   // 0..32*NCW-1
-    const bool single = n_splits == 1;   // this CTA holds the whole key range of its (item, head group)
-    const uint32_t nsl = NCW / HC;       // slice warps per head
-    for (int e = tid; e < static_cast<int>(HC * G * HD); e += 32 * NCW) {
-        const uint32_t h = e / (G * HD), g = (e / HD) % G, d = e % HD;
-        if (g >= s_gcnt[h]) continue;
-        float M = -INFINITY;
-        for (uint32_t j = 0; j < nsl; ++j) M = fmaxf(M, mrg_ml[((h + j * HC) * G + g) * 2]);
-        float o = 0.f, l = 0.f;
-        for (uint32_t j = 0; j < nsl; ++j) {
-            const uint32_t w = h + j * HC;
-            const float mw = mrg_ml[(w * G + g) * 2];
-            const float sc = (mw == -INFINITY) ? 0.f : ex2_approx(mw - M);
-            o += sc * mrg_o[(w * G + g) * HD + d];
-            l += sc * mrg_ml[(w * G + g) * 2 + 1];
-        }
-        const uint32_t hh = s_gfirst[h] + g;
-        if (single && p.partial_only) {
-            p.out_o[static_cast<size_t>(hh) * HD + d] = o;
-            if (d == 0) {
-                p.out_ml[hh * 2 + 0] = M;
-                p.out_ml[hh * 2 + 1] = l;
-            }
-        } else if (single) {
-            float r = o / l;
-            if (it.gate) r *= 1.0f / (1.0f + __expf(-it.gate[static_cast<size_t>(hh) * HD + d]));
-            it.out[static_cast<size_t>(hh) * HD + d] = r;
+    // The ring keeps running across units: unit tiles are numbered from tb, the
+    // tiles earlier units of this CTA streamed (stage = tile % NST, phase =
+    // (tile / NST) & 1).  Between units the whole CTA syncs, so the merge of one
+    // unit (which reuses the ring) ends before the next unit's copies start.
+    uint32_t tb = 0;
+    for (uint32_t u = u_begin; u < u_end; ++u) {
+        YattnDecodeItem it;
+        uint32_t kg, t0, t1, n_splits, split, part_base, group;
+        if (p.work) {
+            const YattnDecodeWork w = p.work[u];
+            it = p.items[w.item];
+            kg = w.kv_head / HC;
+            t0 = w.t_begin;
+            t1 = w.t_end;
+            n_splits = w.n_splits;
+            split = w.split;
+            part_base = w.part_base;
+            group = w.group;
         } else {
-            const size_t slot = static_cast<size_t>(part_base + h * n_splits + split) * G + g;
-            p.part_o[slot * HD + d] = o;
-            if (d == 0) {
-                p.part_ml[slot * 2 + 0] = M;
-                p.part_ml[slot * 2 + 1] = l;
-            }
+            it = p.item0;
+            kg = u / p.n_splits0;
+            split = u % p.n_splits0;
+            n_splits = p.n_splits0;
+            t0 = p.t_base + split * p.split_len;
+            t1 = min(t0 + p.split_len, p.t_end0);
+            part_base = kg * HC * p.n_splits0;
+            group = kg;
         }
-    }
-    if (single || p.defer_merge) return;
+        const uint32_t ntok = t1 - t0;
+        const uint32_t ntiles = (ntok + TOK - 1) / TOK;
+        if (threadIdx.x == 0) {
+            for (uint32_t hl = 0; hl < HC; ++hl)
+                group_of(kg * HC + hl, p.n_heads, p.n_kv, s_gfirst[hl], s_gcnt[hl]);
+            last_flag[0] = 0;
+        }
+        __syncthreads();
 
-    // ---- last split of this (item, head group) merges all splits ----
-    __threadfence();
-    named_bar_sync(1, 32 * NCW);
-    if (tid == 0) {
-        const uint32_t prev = atomicAdd(&p.counters[group], 1u);
-        last_flag[0] = (prev == n_splits - 1) ? 1 : 0;
-    }
-    named_bar_sync(1, 32 * NCW);
-    if (!last_flag[0]) return;
-    __threadfence();
-    for (int e = tid; e < static_cast<int>(HC * G * HD); e += 32 * NCW) {
-        const uint32_t h = e / (G * HD), g = (e / HD) % G, d = e % HD;
-        if (g >= s_gcnt[h]) continue;
-        const size_t base = static_cast<size_t>(part_base + h * n_splits);
-        float M = -INFINITY;
-        for (uint32_t sidx = 0; sidx < n_splits; ++sidx)
-            M = fmaxf(M, __ldcg(&p.part_ml[((base + sidx) * G + g) * 2]));
-        float o = 0.f, l = 0.f;
-        for (uint32_t sidx = 0; sidx < n_splits; ++sidx) {
-            const size_t slot = (base + sidx) * G + g;
-            const float sc = ex2_approx(__ldcg(&p.part_ml[slot * 2]) - M);
-            o += sc * __ldcg(&p.part_o[slot * HD + d]);
-            l += sc * __ldcg(&p.part_ml[slot * 2 + 1]);
-        }
-        const uint32_t hh = s_gfirst[h] + g;
-        if (p.partial_only) {   // merged (m, l, o) of the whole range, for a cross-GPU merge
-            p.out_o[static_cast<size_t>(hh) * HD + d] = o;
-            if (d == 0) {
-                p.out_ml[hh * 2 + 0] = M;
-                p.out_ml[hh * 2 + 1] = l;
+        if (warp == NCW) {
+            // ================= producer: one bulk copy per row per tensor =================
+            const uint16_t* kb = it.k + static_cast<size_t>(kg) * HC * HD;
+            const uint16_t* vb = it.v + static_cast<size_t>(kg) * HC * HD;
+            uint32_t issued = 0;
+            for (uint32_t i = 0; i < ntiles; ++i) {
+                const uint32_t gi = tb + i;
+                const int s = gi % C::NST;
+                if (gi >= static_cast<uint32_t>(C::NST)) {
+                    if (!warp_wait_bounded(&empty[s], ((gi / C::NST) & 1u) ^ 1u, p.status, ST_DECODE_EMPTY_TIMEOUT,
+                                           abort_flag))
+                        break;
+                }
+                const uint32_t tile0 = t0 + i * TOK;
+                const uint32_t nrows = min(TOK, t1 - tile0);
+                uint8_t* kdst = stages + s * STAGEB;
+                uint8_t* vdst = kdst + TILEB;
+                if (lane == 0) mbar_arrive_expect_tx(&full[s], 2u * nrows * ROWB);
+                __syncwarp();
+                for (uint32_t r = lane; r < nrows; r += 32) {
+                    const size_t off = static_cast<size_t>(tile0 + r) * p.kv_dim;
+                    bulk_g2s(kdst + r * RS, kb + off, ROWB, &full[s]);
+                    bulk_g2s(vdst + r * RS, vb + off, ROWB, &full[s]);
+                }
+                issued = i + 1;
             }
-            continue;
+            // No copy of this unit may still be in flight when the unit ends.
+            for (uint32_t i = (issued > static_cast<uint32_t>(C::NST) ? issued - C::NST : 0); i < issued; ++i) {
+                const uint32_t gi = tb + i;
+                volatile int dummy = 0;
+                mbar_wait_bounded(&full[gi % C::NST], (gi / C::NST) & 1u, p.status, ST_DECODE_FULL_TIMEOUT, &dummy);
+            }
+        } else {
+            // Consumer work of the unit; a return ends the unit for the calling
+            // thread (every return below is uniform across the consumer warps).
+            [&]() {
+            // ================= consumers =================
+            const uint32_t hl = warp % HC;                 // head within the group
+            const uint32_t sl = warp / HC;                 // 16-token slice of each stage
+            const uint32_t gfirst = s_gfirst[hl], gcnt = s_gcnt[hl];
+            const int g8 = lane >> 2;                      // fragment row group: token (S^T), dim (O^T), head (B)
+            const int t4 = lane & 3;                       // fragment column pair: heads 2*t4, 2*t4+1
+            // Q^T as the MMA B operand: b0 = q[head g8][16kk + 2t4 .. +1], b1 = q[head g8][16kk + 2t4 + 8 .. +9]
+            uint32_t qhi[KS][2], qlo[KS][2];
+            {
+                const bool hv = static_cast<uint32_t>(g8) < gcnt;
+                const float* qh = it.q + static_cast<size_t>(gfirst + (hv ? g8 : 0)) * HD;
+        #pragma unroll
+                for (int kk = 0; kk < KS; ++kk) {
+                    float2 x0 = make_float2(0.f, 0.f), x1 = make_float2(0.f, 0.f);
+                    if (hv) {
+                        x0 = *reinterpret_cast<const float2*>(qh + kk * 16 + 2 * t4);
+                        x1 = *reinterpret_cast<const float2*>(qh + kk * 16 + 2 * t4 + 8);
+                    }
+                    split_h2(x0.x, x0.y, qhi[kk][0], qlo[kk][0]);
+                    split_h2(x1.x, x1.y, qhi[kk][1], qlo[kk][1]);
+                }
+            }
+            float oc[KS][4];
+        #pragma unroll
+            for (int mt = 0; mt < KS; ++mt) oc[mt][0] = oc[mt][1] = oc[mt][2] = oc[mt][3] = 0.f;
+            float m_a = -INFINITY, m_b = -INFINITY, l_a = 0.f, l_b = 0.f;    // heads 2*t4 and 2*t4+1
+            uint8_t* pt = pt_all + warp * C::PT_BYTES;
+            const uint32_t pt_u = smem_u32(pt);
+            // ldmatrix lane addresses relative to the warp's 16-row slice of a tile
+            const uint32_t slice = (16 * sl) * RS + hl * HD * 2;
+            const uint32_t a_off = slice + ((lane & 7) + ((lane >> 3) & 1) * 8) * RS + ((lane >> 4) & 1) * 16;   // K
+            const uint32_t v_off = slice + ((lane & 7) + ((lane >> 4) & 1) * 8) * RS + ((lane >> 3) & 1) * 16;   // V^T
+            const uint32_t p_off = (lane & 7) * 48 + ((lane >> 3) & 1) * 16;                                     // P^T
+
+            for (uint32_t i = 0; i < ntiles; ++i) {
+                const uint32_t gi = tb + i;
+                const int s = gi % C::NST;
+                if (!warp_wait_bounded(&full[s], (gi / C::NST) & 1u, p.status, ST_DECODE_FULL_TIMEOUT, abort_flag)) break;
+                const uint32_t nrows = min(TOK, t1 - (t0 + i * TOK));
+                const int nvalid = max(0, min(16, static_cast<int>(nrows) - static_cast<int>(16 * sl)));
+                if (nvalid > 0) {
+                    const uint32_t kt = smem_u32(stages + s * STAGEB);
+                    const uint32_t vt = kt + TILEB;
+                    // ---- S^T = K Q^T ----
+                    // four independent accumulation chains (q hi / lo x even / odd k-step),
+                    // so the MMA latency is paid KS/2 times instead of 2*KS
+                    float sc[4], sc1[4] = {0.f, 0.f, 0.f, 0.f}, sc2[4] = {0.f, 0.f, 0.f, 0.f},
+                                 sc3[4] = {0.f, 0.f, 0.f, 0.f};
+                    sc[0] = sc[1] = sc[2] = sc[3] = 0.f;
+        #pragma unroll
+                    for (int kk = 0; kk < KS; kk += 2) {
+                        uint32_t a[4], b[4];
+                        ldsm_x4(kt + a_off + kk * 32, a);
+                        ldsm_x4(kt + a_off + (kk + 1) * 32, b);
+                        mma16816(sc, a, qhi[kk][0], qhi[kk][1]);
+                        mma16816(sc1, b, qhi[kk + 1][0], qhi[kk + 1][1]);
+                        mma16816(sc2, a, qlo[kk][0], qlo[kk][1]);
+                        mma16816(sc3, b, qlo[kk + 1][0], qlo[kk + 1][1]);
+                    }
+        #pragma unroll
+                    for (int r = 0; r < 4; ++r) sc[r] = (sc[r] + sc1[r]) + (sc2[r] + sc3[r]);
+                    // sc: [0] = (token g8, head 2t4), [1] = (g8, 2t4+1), [2] = (g8+8, 2t4), [3] = (g8+8, 2t4+1)
+                    const bool v0 = g8 < nvalid, v1 = g8 + 8 < nvalid;
+                    const float s0 = v0 ? sc[0] * p.scale_log2 : -INFINITY;
+                    const float s1 = v0 ? sc[1] * p.scale_log2 : -INFINITY;
+                    const float s2 = v1 ? sc[2] * p.scale_log2 : -INFINITY;
+                    const float s3 = v1 ? sc[3] * p.scale_log2 : -INFINITY;
+                    float mx_a = fmaxf(s0, s2), mx_b = fmaxf(s1, s3);
+        #pragma unroll
+                    for (int o = 4; o <= 16; o <<= 1) {
+                        mx_a = fmaxf(mx_a, __shfl_xor_sync(0xffffffffu, mx_a, o));
+                        mx_b = fmaxf(mx_b, __shfl_xor_sync(0xffffffffu, mx_b, o));
+                    }
+                    const float mn_a = fmaxf(m_a, mx_a), mn_b = fmaxf(m_b, mx_b);
+                    const float al_a = ex2_approx(m_a - mn_a), al_b = ex2_approx(m_b - mn_b);
+                    const float p0 = ex2_approx(s0 - mn_a), p1 = ex2_approx(s1 - mn_b);
+                    const float p2 = ex2_approx(s2 - mn_a), p3 = ex2_approx(s3 - mn_b);
+                    float sum_a = p0 + p2, sum_b = p1 + p3;
+        #pragma unroll
+                    for (int o = 4; o <= 16; o <<= 1) {
+                        sum_a += __shfl_xor_sync(0xffffffffu, sum_a, o);
+                        sum_b += __shfl_xor_sync(0xffffffffu, sum_b, o);
+                    }
+                    l_a = l_a * al_a + sum_a;
+                    l_b = l_b * al_b + sum_b;
+                    m_a = mn_a;
+                    m_b = mn_b;
+                    // ---- P^T (rows = heads, 16 tokens, 48 B row stride) as fp16 hi and lo planes ----
+                    {
+                        uint32_t h01, l01, h23, l23;
+                        split_h2(p0, p1, h01, l01);      // (token g8: heads 2t4, 2t4+1)
+                        split_h2(p2, p3, h23, l23);      // (token g8+8: heads 2t4, 2t4+1)
+                        uint16_t* hp = reinterpret_cast<uint16_t*>(pt);
+                        uint16_t* lp = reinterpret_cast<uint16_t*>(pt + 384);
+                        const int ra = (2 * t4) * 24, rb = (2 * t4 + 1) * 24;   // row offsets in halves
+                        hp[ra + g8] = static_cast<uint16_t>(h01);
+                        hp[rb + g8] = static_cast<uint16_t>(h01 >> 16);
+                        hp[ra + g8 + 8] = static_cast<uint16_t>(h23);
+                        hp[rb + g8 + 8] = static_cast<uint16_t>(h23 >> 16);
+                        lp[ra + g8] = static_cast<uint16_t>(l01);
+                        lp[rb + g8] = static_cast<uint16_t>(l01 >> 16);
+                        lp[ra + g8 + 8] = static_cast<uint16_t>(l23);
+                        lp[rb + g8 + 8] = static_cast<uint16_t>(l23 >> 16);
+                    }
+                    __syncwarp();
+                    uint32_t ph0, ph1, pl0, pl1;
+                    ldsm_x2(pt_u + p_off, ph0, ph1);
+                    ldsm_x2(pt_u + 384 + p_off, pl0, pl1);
+                    // ---- O^T = O^T * alpha + V^T P^T ----
+                    // V rows past nvalid hold stale (or never written) shared memory: their
+                    // p is 0, but 0 * NaN would still poison the MMA, so zero those lanes.
+                    // The A fragment holds tokens 2t4, 2t4+1 (a0, a1) and 2t4+8, 2t4+9 (a2, a3).
+                    uint32_t vm01 = 0xffffffffu, vm23 = 0xffffffffu;
+                    if (nvalid < 16) {
+                        vm01 = (2 * t4 < nvalid ? 0x0000ffffu : 0u) | (2 * t4 + 1 < nvalid ? 0xffff0000u : 0u);
+                        vm23 = (2 * t4 + 8 < nvalid ? 0x0000ffffu : 0u) | (2 * t4 + 9 < nvalid ? 0xffff0000u : 0u);
+                    }
+        #pragma unroll
+                    for (int mt = 0; mt < KS; ++mt) {
+                        oc[mt][0] *= al_a;
+                        oc[mt][1] *= al_b;
+                        oc[mt][2] *= al_a;
+                        oc[mt][3] *= al_b;
+                        uint32_t a[4];
+                        ldsm_x4_t(vt + v_off + mt * 32, a);
+                        a[0] &= vm01;
+                        a[1] &= vm01;
+                        a[2] &= vm23;
+                        a[3] &= vm23;
+                        mma16816(oc[mt], a, ph0, ph1);
+                        mma16816(oc[mt], a, pl0, pl1);
+                    }
+                    __syncwarp();   // P^T is rewritten by the next step
+                }
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&empty[s]);
+            }
+
+            // ---- merge the consumer warps (ring is free: every stage was consumed) ----
+            // No early exit on the abort flag here: every consumer warp must reach the
+            // same named barriers (a timed-out unit just writes meaningless partials).
+            named_bar_sync(1, 32 * NCW);
+            {
+                const int ha = 2 * t4, hb = 2 * t4 + 1;
+                if (g8 == 0) {
+                    if (ha < G) {
+                        mrg_ml[(warp * G + ha) * 2 + 0] = m_a;
+                        mrg_ml[(warp * G + ha) * 2 + 1] = l_a;
+                    }
+                    if (hb < G) {
+                        mrg_ml[(warp * G + hb) * 2 + 0] = m_b;
+                        mrg_ml[(warp * G + hb) * 2 + 1] = l_b;
+                    }
+                }
+        #pragma unroll
+                for (int mt = 0; mt < KS; ++mt) {
+                    const int d0 = mt * 16 + g8, d1 = d0 + 8;
+                    if (ha < G) {
+                        mrg_o[(warp * G + ha) * HD + d0] = oc[mt][0];
+                        mrg_o[(warp * G + ha) * HD + d1] = oc[mt][2];
+                    }
+                    if (hb < G) {
+                        mrg_o[(warp * G + hb) * HD + d0] = oc[mt][1];
+                        mrg_o[(warp * G + hb) * HD + d1] = oc[mt][3];
+                    }
+                }
+            }
+            named_bar_sync(1, 32 * NCW);
+
+            const int tid = threadIdx.x;   // 0..32*NCW-1
+            const bool single = n_splits == 1;   // this CTA holds the whole key range of its (item, head group)
+            const uint32_t nsl = NCW / HC;       // slice warps per head
+            for (int e = tid; e < static_cast<int>(HC * G * HD); e += 32 * NCW) {
+                const uint32_t h = e / (G * HD), g = (e / HD) % G, d = e % HD;
+                if (g >= s_gcnt[h]) continue;
+                float M = -INFINITY;
+                for (uint32_t j = 0; j < nsl; ++j) M = fmaxf(M, mrg_ml[((h + j * HC) * G + g) * 2]);
+                float o = 0.f, l = 0.f;
+                for (uint32_t j = 0; j < nsl; ++j) {
+                    const uint32_t w = h + j * HC;
+                    const float mw = mrg_ml[(w * G + g) * 2];
+                    const float sc = (mw == -INFINITY) ? 0.f : ex2_approx(mw - M);
+                    o += sc * mrg_o[(w * G + g) * HD + d];
+                    l += sc * mrg_ml[(w * G + g) * 2 + 1];
+                }
+                const uint32_t hh = s_gfirst[h] + g;
+                if (single && p.partial_only) {
+                    p.out_o[static_cast<size_t>(hh) * HD + d] = o;
+                    if (d == 0) {
+                        p.out_ml[hh * 2 + 0] = M;
+                        p.out_ml[hh * 2 + 1] = l;
+                    }
+                } else if (single) {
+                    float r = o / l;
+                    if (it.gate) r *= 1.0f / (1.0f + __expf(-it.gate[static_cast<size_t>(hh) * HD + d]));
+                    it.out[static_cast<size_t>(hh) * HD + d] = r;
+                } else {
+                    const size_t slot = static_cast<size_t>(part_base + h * n_splits + split) * G + g;
+                    p.part_o[slot * HD + d] = o;
+                    if (d == 0) {
+                        p.part_ml[slot * 2 + 0] = M;
+                        p.part_ml[slot * 2 + 1] = l;
+                    }
+                }
+            }
+            if (single || p.defer_merge) return;
+
+            // ---- last split of this (item, head group) merges all splits ----
+            __threadfence();
+            named_bar_sync(1, 32 * NCW);
+            if (tid == 0) {
+                const uint32_t prev = atomicAdd(&p.counters[group], 1u);
+                last_flag[0] = (prev == n_splits - 1) ? 1 : 0;
+            }
+            named_bar_sync(1, 32 * NCW);
+            if (!last_flag[0]) return;
+            __threadfence();
+            // One warp per (kv head, query head) row; lanes own dims lane + 32i.  The
+            // per-split loads are independent, so they are all in flight at once
+            // (a strided thread-per-element loop paid two L2 round trips per element
+            // group, tens of microseconds at the end of the grid).
+            constexpr int DPL = HD / 32;
+            for (uint32_t row = warp; row < HC * G; row += NCW) {
+                const uint32_t h = row / G, g = row % G;
+                if (g >= s_gcnt[h]) continue;
+                const size_t base = static_cast<size_t>(part_base + h * n_splits);
+                float mj = -INFINITY;
+                for (uint32_t sidx = lane; sidx < n_splits; sidx += 32)
+                    mj = fmaxf(mj, __ldcg(&p.part_ml[((base + sidx) * G + g) * 2]));
+#pragma unroll
+                for (int o = 16; o > 0; o >>= 1) mj = fmaxf(mj, __shfl_xor_sync(0xffffffffu, mj, o));
+                const float M = mj;
+                float acc[DPL], l = 0.f;
+#pragma unroll
+                for (int i = 0; i < DPL; ++i) acc[i] = 0.f;
+#pragma unroll 4
+                for (uint32_t sidx = 0; sidx < n_splits; ++sidx) {
+                    const size_t slot = (base + sidx) * G + g;
+                    const float2 mls = __ldcg(reinterpret_cast<const float2*>(&p.part_ml[slot * 2]));
+                    const float sc = ex2_approx(mls.x - M);
+                    l += sc * mls.y;
+#pragma unroll
+                    for (int i = 0; i < DPL; ++i) acc[i] += sc * __ldcg(&p.part_o[slot * HD + lane + 32 * i]);
+                }
+                const uint32_t hh = s_gfirst[h] + g;
+                if (p.partial_only) {   // merged (m, l, o) of the whole range, for a cross-GPU merge
+#pragma unroll
+                    for (int i = 0; i < DPL; ++i) p.out_o[static_cast<size_t>(hh) * HD + lane + 32 * i] = acc[i];
+                    if (lane == 0) {
+                        p.out_ml[hh * 2 + 0] = M;
+                        p.out_ml[hh * 2 + 1] = l;
+                    }
+                    continue;
+                }
+                const float inv_l = 1.0f / l;
+#pragma unroll
+                for (int i = 0; i < DPL; ++i) {
+                    const size_t idx = static_cast<size_t>(hh) * HD + lane + 32 * i;
+                    float r = acc[i] * inv_l;
+                    if (it.gate) r *= 1.0f / (1.0f + __expf(-it.gate[idx]));
+                    it.out[idx] = r;
+                }
+            }
+            if (tid == 0) p.counters[group] = 0u;   // ready for the next launch
+            }();
         }
-        float r = o / l;
-        if (it.gate) r *= 1.0f / (1.0f + __expf(-it.gate[static_cast<size_t>(hh) * HD + d]));
-        it.out[static_cast<size_t>(hh) * HD + d] = r;
+        tb += ntiles;
+        __syncthreads();
     }
-    if (tid == 0) p.counters[group] = 0u;   // ready for the next launch
 }
 
 // ------------------------------------------------- parallel merge of many splits
@@ -790,40 +874,120 @@ extern "C" int yattn_decode_plan(const uint32_t* pos_host, uint32_t n_items, uin
     for (uint32_t i = 0; i < n_items; ++i) total += static_cast<uint64_t>(pos_host[i]) + 1;
     total *= nkg;
     if (target_ctas == 0) target_ctas = static_cast<uint32_t>(dev_num_sms());
-    const uint32_t split = split_tokens ? (split_tokens + kSplitQuant - 1) / kSplitQuant * kSplitQuant
-                                        : auto_split(total, target_ctas);
     std::vector<YattnDecodeWork> w;
     uint32_t parts = 0, groups = 0;
-    for (uint32_t i = 0; i < n_items; ++i) {
-        const uint32_t ntok = pos_host[i] + 1;
-        const uint32_t ns = (ntok + split - 1) / split;
-        if (ns > 65535) {
-            set_err(err, errlen, "decode_plan: %u splits for item %u (max 65535)", ns, i);
-            return -1;
-        }
-        for (uint32_t kg = 0; kg < nkg; ++kg) {
-            for (uint32_t s = 0; s < ns; ++s) {
-                YattnDecodeWork x{};
-                x.item = i;
-                x.kv_head = static_cast<uint16_t>(kg * hc);
-                x.n_splits = static_cast<uint16_t>(ns);
-                x.split = s;
-                x.t_begin = s * split;
-                x.t_end = std::min(ntok, (s + 1) * split);
-                x.part_base = ns > 1 ? parts : 0u;
-                x.group = ns > 1 ? groups : 0u;
-                w.push_back(x);
+    if (split_tokens) {
+        // uniform splits, one unit per CTA, longest units first
+        const uint32_t split = (split_tokens + kSplitQuant - 1) / kSplitQuant * kSplitQuant;
+        for (uint32_t i = 0; i < n_items; ++i) {
+            const uint32_t ntok = pos_host[i] + 1;
+            const uint32_t ns = (ntok + split - 1) / split;
+            if (ns > 65535) {
+                set_err(err, errlen, "decode_plan: %u splits for item %u (max 65535)", ns, i);
+                return -1;
             }
-            if (ns > 1) {
-                parts += hc * ns;     // one slot per (kv head of the group, split)
-                groups += 1;
+            for (uint32_t kg = 0; kg < nkg; ++kg) {
+                for (uint32_t s = 0; s < ns; ++s) {
+                    YattnDecodeWork x{};
+                    x.item = i;
+                    x.kv_head = static_cast<uint16_t>(kg * hc);
+                    x.n_splits = static_cast<uint16_t>(ns);
+                    x.split = s;
+                    x.t_begin = s * split;
+                    x.t_end = std::min(ntok, (s + 1) * split);
+                    x.part_base = ns > 1 ? parts : 0u;
+                    x.group = ns > 1 ? groups : 0u;
+                    w.push_back(x);
+                }
+                if (ns > 1) {
+                    parts += hc * ns;     // one slot per (kv head of the group, split)
+                    groups += 1;
+                }
             }
         }
+        std::stable_sort(w.begin(), w.end(), [](const YattnDecodeWork& a, const YattnDecodeWork& b) {
+            return (a.t_end - a.t_begin) > (b.t_end - b.t_begin);
+        });
+        for (size_t u = 0; u < w.size(); ++u) w[u].cta = static_cast<uint32_t>(u);
+    } else {
+        // Balanced: the (item, head group) key ranges laid end to end, cut into
+        // chunks of `chunk` keys; CTA c streams the keys of chunk c as one unit per
+        // range it touches.  A CTA's second and later units are charged
+        // kUnitCost keys (pipeline drain and refill, descriptor fetch, merge).
+        // No piece is shorter than kSplitMin: a cut that would leave a shorter
+        // tail moves back so the tail has kSplitMin keys, or to the range end.  Chunks are at least max_tok / kMaxSplits long, so no range
+        // has more splits than the last-arriving CTA merges quickly, and grow
+        // until the charged plan fits in target_ctas CTAs.
+        uint32_t max_tok = 0;
+        for (uint32_t i = 0; i < n_items; ++i) max_tok = std::max(max_tok, pos_host[i] + 1);
+        uint64_t chunk = (total + target_ctas - 1) / target_ctas;
+        chunk = std::max<uint64_t>(chunk, kSplitMin);
+        chunk = std::max<uint64_t>(chunk, (max_tok + kMaxSplits - 1) / kMaxSplits);
+        for (int attempt = 0;; ++attempt) {
+            w.clear();
+            parts = groups = 0;
+            uint64_t pos = 0;            // keys (plus charges) laid down so far
+            uint64_t last_cta = ~0ull;   // CTA of the previous unit
+            for (uint32_t i = 0; i < n_items; ++i) {
+                const uint32_t ntok = pos_host[i] + 1;
+                for (uint32_t kg = 0; kg < nkg; ++kg) {
+                    const size_t first = w.size();
+                    uint32_t t = 0;
+                    while (t < ntok) {
+                        uint64_t c = pos / chunk;
+                        if (c == last_cta) {                 // another unit for this CTA
+                            pos += kUnitCost;
+                            if (pos / chunk != c) pos = (c + 1) * chunk;
+                            c = pos / chunk;
+                        }
+                        uint64_t room = (c + 1) * chunk - pos;
+                        if (room < kSplitMin && ntok - t > room) {   // too little room left: next CTA
+                            pos += room;
+                            ++c;
+                            room = chunk;
+                        }
+                        uint32_t len = static_cast<uint32_t>(std::min<uint64_t>(ntok - t, room));
+                        const uint32_t rest = ntok - t - len;
+                        if (rest > 0 && rest < kSplitMin) {   // no short tail:
+                            if (len >= 2 * kSplitMin - rest)
+                                len -= kSplitMin - rest;      // leave kSplitMin keys for the next CTA
+                            else
+                                len = ntok - t;               // or take the tail here
+                        }
+                        YattnDecodeWork x{};
+                        x.item = i;
+                        x.kv_head = static_cast<uint16_t>(kg * hc);
+                        x.t_begin = t;
+                        x.t_end = t + len;
+                        x.cta = static_cast<uint32_t>(c);
+                        w.push_back(x);
+                        t += len;
+                        pos += len;
+                        last_cta = c;
+                    }
+                    const uint32_t ns = static_cast<uint32_t>(w.size() - first);
+                    if (ns > 65535) {
+                        set_err(err, errlen, "decode_plan: %u splits for item %u (max 65535)", ns, i);
+                        return -1;
+                    }
+                    for (uint32_t s = 0; s < ns; ++s) {
+                        YattnDecodeWork& x = w[first + s];
+                        x.n_splits = static_cast<uint16_t>(ns);
+                        x.split = s;
+                        x.part_base = ns > 1 ? parts : 0u;
+                        x.group = ns > 1 ? groups : 0u;
+                    }
+                    if (ns > 1) {
+                        parts += hc * ns;
+                        groups += 1;
+                    }
+                }
+            }
+            if (w.empty() || w.back().cta < target_ctas || attempt >= 64) break;
+            chunk += chunk / 128 + 1;   // the charges pushed units past the last CTA
+        }
+        // units are already grouped by CTA in increasing order
     }
-    // longest units first: the tail of the grid is made of the short ones
-    std::stable_sort(w.begin(), w.end(), [](const YattnDecodeWork& a, const YattnDecodeWork& b) {
-        return (a.t_end - a.t_begin) > (b.t_end - b.t_begin);
-    });
     if (w.size() > work_cap) {
         set_err(err, errlen, "decode_plan: %zu work units exceed work_cap %u", w.size(), work_cap);
         *n_work = static_cast<uint32_t>(w.size());
@@ -875,6 +1039,7 @@ extern "C" int yattn_decode_run(const YattnDecodeItem* items_dev, const YattnDec
     DecodeParams p{};
     p.items = items_dev;
     p.work = work_dev;
+    p.n_work = n_work;
     p.n_heads = n_heads;
     p.n_kv = n_kv_heads;
     p.kv_dim = kv_dim;
