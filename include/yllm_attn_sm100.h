@@ -236,12 +236,24 @@ int yattn_gdn_decode(float* S, float* out, const float* q, const float* k, const
 
 /* T tokens of each of n_seqs sequences in order (the engine's qwen35 prefill,
  * engine.c:723-734, calls gdn_state_update once per token).  Per-token rows as
- * in yattn_gdn_decode, token t of sequence s at row s*T + t. */
+ * in yattn_gdn_decode, token t of sequence s at row s*T + t.  Runs the chunked
+ * form (64-token chunks, tensor cores, fp32 state); the library grows a
+ * per-device scratch of about (num_k_heads*64 + n_vheads*32.25) KiB per
+ * 64 tokens per sequence on first use. */
 int yattn_gdn_prefill(float* S, float* out, const float* q, const float* k, const float* v,
                       const float* gate, const float* beta, uint32_t n_seqs, uint32_t T,
                       uint32_t num_k_heads, uint32_t hk, uint32_t n_vheads, uint32_t hv,
                       const float* norm_w, const float* z, float eps, void* stream,
                       char* err, size_t errlen);
+
+/* The same prefill token by token in the reference's operation order (one
+ * recurrent kernel, no scratch).  No reference counterpart beyond
+ * gdn_state_update itself; kept as the GPU cross-check of the chunked form. */
+int yattn_gdn_prefill_recurrent(float* S, float* out, const float* q, const float* k,
+                                const float* v, const float* gate, const float* beta,
+                                uint32_t n_seqs, uint32_t T, uint32_t num_k_heads, uint32_t hk,
+                                uint32_t n_vheads, uint32_t hv, const float* norm_w,
+                                const float* z, float eps, void* stream, char* err, size_t errlen);
 
 /* ------------------------------------------------ seeded input generator
  * Deterministic on every device and bit-identical to the CPU restatement in

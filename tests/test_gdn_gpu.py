@@ -97,6 +97,28 @@ def test_gdn_prefill_config5a_full(dev):
     oracle.assert_close(_np(g.S), S_want, what="gdn 4096-token prefill state")
 
 
+@pytest.mark.parametrize("n_seqs,T,seeded", [(1, 63, True), (1, 64, True), (2, 65, True), (1, 200, False),
+                                              (3, 129, True)])
+def test_gdn_chunked_matches_recurrent_kernel(dev, n_seqs, T, seeded):
+    """The chunked tensor-core prefill (64-token chunks, ragged last chunk,
+    several sequences) against the token-by-token GPU kernel, which follows
+    the reference's operation order."""
+    from yllm_b200 import attn, fixtures
+    from yllm_b200.configs import CFG5_GDN as c
+
+    D, NK, NV = c.head_dim, c.num_k_heads, c.n_v_heads
+    a = fixtures.gdn_inputs(c, n_seqs, T, seeded_state=seeded, device=dev)
+    b = fixtures.gdn_inputs(c, n_seqs, T, seeded_state=seeded, device=dev)
+    attn.gdn_prefill(a.S, a.out, a.q, a.k, a.v, a.gate, a.beta, n_seqs, T, NK, D, NV, D, norm_w=a.norm_w, z=a.z,
+                     eps=c.eps)
+    attn.gdn_prefill_recurrent(b.S, b.out, b.q, b.k, b.v, b.gate, b.beta, n_seqs, T, NK, D, NV, D, norm_w=b.norm_w,
+                               z=b.z, eps=c.eps)
+    torch.cuda.synchronize()
+    oracle.assert_close(_np(a.out), _np(b.out), what=f"chunked vs recurrent out {n_seqs}x{T}")
+    oracle.assert_close(_np(a.S), _np(b.S), what=f"chunked vs recurrent state {n_seqs}x{T}")
+    assert attn.device_status() == 0
+
+
 def test_gdn_prefill_equals_decode_steps(dev):
     """T prefill tokens == T single-token decodes (two kernels, same recurrence)."""
     from yllm_b200 import attn, fixtures

@@ -92,6 +92,8 @@ PROTOS = {
     "yattn_gdn_decode": (C.c_int, [vp, vp, vp, vp, vp, vp, vp, u32, u32, u32, u32, u32, vp, vp, C.c_float, vp, *E]),
     "yattn_gdn_prefill": (
         C.c_int, [vp, vp, vp, vp, vp, vp, vp, u32, u32, u32, u32, u32, u32, vp, vp, C.c_float, vp, *E]),
+    "yattn_gdn_prefill_recurrent": (
+        C.c_int, [vp, vp, vp, vp, vp, vp, vp, u32, u32, u32, u32, u32, u32, vp, vp, C.c_float, vp, *E]),
     "yattn_gen_rows": (
         C.c_int,
         [vp, C.c_int, sz, sz, u32, u32, u64, u64, C.c_double, C.c_int, u32, C.c_double, vp, *E],

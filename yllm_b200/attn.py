@@ -238,6 +238,17 @@ def gdn_prefill(S, out, q, k, v, gate, beta, n_seqs: int, T: int, num_k_heads: i
          float(eps), _stream(stream))
 
 
+def gdn_prefill_recurrent(S, out, q, k, v, gate, beta, n_seqs: int, T: int, num_k_heads: int, hk: int,
+                          n_vheads: int, hv: int, norm_w: Optional[torch.Tensor] = None,
+                          z: Optional[torch.Tensor] = None, eps: float = 1e-6, stream=None) -> None:
+    """gdn_prefill token by token in the reference's operation order (GPU cross-check)."""
+    for name, t in (("S", S), ("out", out), ("q", q), ("k", k), ("v", v), ("gate", gate), ("beta", beta)):
+        _need(t, torch.float32, name)
+    call("yattn_gdn_prefill_recurrent", S.data_ptr(), out.data_ptr(), q.data_ptr(), k.data_ptr(), v.data_ptr(),
+         gate.data_ptr(), beta.data_ptr(), n_seqs, T, num_k_heads, hk, n_vheads, hv, _ptr(norm_w), _ptr(z),
+         float(eps), _stream(stream))
+
+
 def device_status(clear: bool = True) -> int:
     st = C.c_int(0)
     call("yattn_device_status", C.byref(st), 1 if clear else 0)

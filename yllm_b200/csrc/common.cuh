@@ -26,6 +26,8 @@ struct DevCtx {
     size_t ws_bytes = 0;
     void* small = nullptr;        // device scratch for drop-in items/work descriptors
     size_t small_bytes = 0;
+    void* gdn_ws = nullptr;       // chunked GDN prefill scratch (grown on demand)
+    size_t gdn_ws_bytes = 0;
 };
 DevCtx* dev_ctx(char* err, size_t errlen);   // current device's context (nullptr on failure)
 int dev_num_sms();

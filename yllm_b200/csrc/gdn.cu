@@ -11,10 +11,12 @@
 // beta), which is what both kernels exploit:
 //   k_gdn_decode   one token per sequence; CTA = (v-head, sequence) streams
 //                  the 64 KB fp32 state (HBM-bound), epilogue fused.
-//   k_gdn_prefill  T tokens of one or more sequences (the engine's qwen35
-//                  prefill runs them token by token, engine.c:723-734); CTA =
-//                  16 state rows of one v-head kept in registers for the whole
+//   k_gdn_prefill  T tokens of one or more sequences token by token, as the
+//                  engine's qwen35 prefill does (engine.c:723-734); CTA = 16
+//                  state rows of one v-head kept in registers for the whole
 //                  sequence, 16 threads per row, token inputs staged in smem.
+//                  yattn_gdn_prefill runs the chunked tensor-core form
+//                  (gdn_chunk.cu); this kernel backs yattn_gdn_prefill_recurrent.
 #include "common.cuh"
 
 #include <algorithm>
@@ -254,9 +256,16 @@ int gdn_decode(float* S, float* out, const float* q, const float* k, const float
     return 0;
 }
 
+size_t gdn_chunk_scratch_bytes(uint32_t n_seqs, uint32_t T, uint32_t num_k_heads, uint32_t n_vheads);
+int gdn_prefill_chunked(float* S, float* out, const float* q, const float* k, const float* v, const float* gate,
+                        const float* beta, uint32_t n_seqs, uint32_t T, uint32_t num_k_heads, uint32_t n_vheads,
+                        void* scratch, cudaStream_t st, char* err, size_t errlen);
+
+// chunked = true: the chunked tensor-core form (gdn_chunk.cu, scratch grown on
+// the device context); false: the token-by-token kernel above.
 int gdn_prefill(float* S, float* out, const float* q, const float* k, const float* v, const float* gate,
                 const float* beta, uint32_t n_seqs, uint32_t T, uint32_t num_k_heads, uint32_t hk, uint32_t n_vheads,
-                uint32_t hv, const float* norm_w, const float* z, float eps, cudaStream_t st, char* err,
+                uint32_t hv, const float* norm_w, const float* z, float eps, bool chunked, cudaStream_t st, char* err,
                 size_t errlen) {
     if (check_gdn(S, out, q, k, v, gate, beta, num_k_heads, hk, n_vheads, hv, norm_w, z, err, errlen)) return -1;
     if (n_seqs == 0 || T == 0) return 0;
@@ -264,9 +273,28 @@ int gdn_prefill(float* S, float* out, const float* q, const float* k, const floa
         set_err(err, errlen, "gdn_prefill: too many sequences/heads");
         return -1;
     }
-    GdnParams p{S, out, q, k, v, gate, beta, norm_w, z, T, num_k_heads, n_vheads, eps};
-    k_gdn_prefill<<<dim3(kGdnD / kRows, n_vheads, n_seqs), 256, 0, st>>>(p);
-    YATTN_CHECK_LAUNCH(err, errlen, "gdn_prefill");
+    if (chunked) {
+        DevCtx* ctx = dev_ctx(err, errlen);
+        if (!ctx) return -1;
+        const size_t need = gdn_chunk_scratch_bytes(n_seqs, T, num_k_heads, n_vheads);
+        if (ctx->gdn_ws_bytes < need) {
+            if (ctx->gdn_ws) cudaFree(ctx->gdn_ws);
+            ctx->gdn_ws = nullptr;
+            ctx->gdn_ws_bytes = 0;
+            if (cudaMalloc(&ctx->gdn_ws, need) != cudaSuccess) {
+                set_err(err, errlen, "gdn_prefill: cudaMalloc(%zu) of the chunk scratch failed", need);
+                return -1;
+            }
+            ctx->gdn_ws_bytes = need;
+        }
+        if (gdn_prefill_chunked(S, out, q, k, v, gate, beta, n_seqs, T, num_k_heads, n_vheads, ctx->gdn_ws, st, err,
+                                errlen))
+            return -1;
+    } else {
+        GdnParams p{S, out, q, k, v, gate, beta, norm_w, z, T, num_k_heads, n_vheads, eps};
+        k_gdn_prefill<<<dim3(kGdnD / kRows, n_vheads, n_seqs), 256, 0, st>>>(p);
+        YATTN_CHECK_LAUNCH(err, errlen, "gdn_prefill");
+    }
     if (norm_w) {
         const size_t n_vec = static_cast<size_t>(n_seqs) * T * n_vheads;
         const uint32_t blocks = static_cast<uint32_t>((n_vec + 7) / 8);
@@ -303,6 +331,15 @@ extern "C" int yattn_gdn_prefill(float* S, float* out, const float* q, const flo
                                  uint32_t num_k_heads, uint32_t hk, uint32_t n_vheads, uint32_t hv,
                                  const float* norm_w, const float* z, float eps, void* stream, char* err,
                                  size_t errlen) {
-    return gdn_prefill(S, out, q, k, v, gate, beta, n_seqs, T, num_k_heads, hk, n_vheads, hv, norm_w, z, eps,
+    return gdn_prefill(S, out, q, k, v, gate, beta, n_seqs, T, num_k_heads, hk, n_vheads, hv, norm_w, z, eps, true,
+                       static_cast<cudaStream_t>(stream), err, errlen);
+}
+
+extern "C" int yattn_gdn_prefill_recurrent(float* S, float* out, const float* q, const float* k, const float* v,
+                                           const float* gate, const float* beta, uint32_t n_seqs, uint32_t T,
+                                           uint32_t num_k_heads, uint32_t hk, uint32_t n_vheads, uint32_t hv,
+                                           const float* norm_w, const float* z, float eps, void* stream, char* err,
+                                           size_t errlen) {
+    return gdn_prefill(S, out, q, k, v, gate, beta, n_seqs, T, num_k_heads, hk, n_vheads, hv, norm_w, z, eps, false,
                        static_cast<cudaStream_t>(stream), err, errlen);
 }

@@ -1,0 +1,598 @@
+// gdn_chunk.cu -- chunked Gated DeltaNet prefill on tensor cores (sm_100a).
+//
+// Semantics: the token-by-token recurrence of gdn_state_update
+// (inference/core/matvec.c:975-1004), run once per token by the qwen35
+// prefill (engine.c:723-734).  Per v-head h (k-head h % num_k_heads), with
+// the state S (hv x hk, row j = v index) and per token t:
+//     S <- e^{a_t} S;   u_t = beta_t (v_t - S k_t);   S <- S + u_t k_t^T;
+//     o_t = S q_t / sqrt(hv)
+// (a_t = gate, beta_t = beta).  Over a chunk of C = 64 tokens with start
+// state S0, let Gamma_t = a_0 + ... + a_t (inclusive) and gamma_t = e^Gamma_t.
+// Unrolling the recurrence gives S_t = gamma_t S0 + sum_{i<=t}
+// e^{Gamma_t - Gamma_i} u_i k_i^T, and the u_t solve a unit lower-triangular
+// system (the WY / UT form of the delta rule: Yang et al. 2024, "Parallelizing
+// Linear Transformers with the Delta Rule over Sequence Length"; gating as in
+// "Gated Delta Networks"):
+//     A[t][i] = beta_t e^{Gamma_t - Gamma_i} (k_t . k_i)      (i < t)
+//     T = (I + A)^-1
+//     U = T (diag(beta) V - diag(beta gamma) K S0^T)          [C x hv]
+//     O = (diag(gamma) Q S0^T + P U) / sqrt(hv),  P[t][i] = e^{Gamma_t - Gamma_i} (q_t . k_i) (i <= t)
+//     S_C = gamma_{C-1} S0 + U^T diag(e^{Gamma_{C-1} - Gamma_i}) K
+// A partial last chunk is padded with k = q = v = 0, a = 0, beta = 0, which
+// leaves every formula exact for the real tokens.
+//
+// Two kernels:
+//   k_gdn_chunk_prep   (chunk, v-head, seq): everything that does not depend on
+//                      S -- Gamma, T and P -- plus fp16 hi/lo copies of K and Q.
+//                      Fully parallel.
+//   k_gdn_chunk_state  (32 state rows, v-head, seq): walks the chunks in order
+//                      with its 32 x 128 slice of S in fp32 registers; every
+//                      contraction is mma.sync m16n8k16 with both operands split
+//                      into fp16 hi + lo (3 products: hi.hi + hi.lo + lo.hi,
+//                      about 22 significant bits, fp32 accumulate).
+// The optional rmsnorm_gated epilogue runs after, as for the recurrent kernel.
+#include "common.cuh"
+
+#include <algorithm>
+
+namespace yattn {
+namespace {
+
+constexpr int kC = 64;          // tokens per chunk
+constexpr int kD = 128;         // head dim (hk == hv)
+constexpr int kR = 32;          // state rows (v index) per CTA of the state kernel
+constexpr int LDH = kD + 8;     // smem row stride (halves) of 128-wide fp16 tiles: 272 B, ldmatrix conflict-free
+constexpr int LDC = kC + 8;     // smem row stride (halves) of 64-wide fp16 tiles: 144 B
+constexpr int LA = kC + 4;      // fp32 row stride of 64 x 64 tiles in the prep kernel (16-B rows)
+
+// Scratch, per (sequence, chunk) sc = seq * n_chunks + chunk:
+//   kq[(sc * num_k_heads + kh)]: K_hi, K_lo, Q_hi, Q_lo   fp16 [64][128] each
+//   tp[(sc * n_vheads + h)]:     T_hi, T_lo, P_hi, P_lo   fp16 [64][64] each
+//   gam[(sc * n_vheads + h)]:    Gamma                    fp32 [64]
+constexpr size_t kKqHalves = 4ull * kC * kD;
+constexpr size_t kTpHalves = 4ull * kC * kC;
+
+struct ChunkParams {
+    const float* q;                 // [n_seq][T][num_k_heads*128]
+    const float* k;
+    const float* v;                 // [n_seq][T][n_vheads*128]
+    const float* gate;              // [n_seq][T][n_vheads]
+    const float* beta;
+    float* S;                       // [n_seq][n_vheads][128][128]
+    float* out;                     // [n_seq][T][n_vheads*128]
+    __half* kq;
+    __half* tp;
+    float* gam;
+    uint32_t T, n_chunks, num_k_heads, n_vheads;
+};
+
+// ------------------------------------------------------------- mma helpers
+
+__device__ __forceinline__ void ldsm4(uint32_t addr, uint32_t (&r)[4]) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"(addr));
+}
+__device__ __forceinline__ void ldsm4t(uint32_t addr, uint32_t (&r)[4]) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"(addr));
+}
+// D(16x8 f32) += A(16x16 f16, row) * B(16x8 f16, col)
+__device__ __forceinline__ void mma(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+// d += (ah + al)(bh + bl) without the lo.lo term
+__device__ __forceinline__ void mma3(float (&d)[4], const uint32_t (&ah)[4], const uint32_t (&al)[4], uint32_t bh0,
+                                     uint32_t bh1, uint32_t bl0, uint32_t bl1) {
+    mma(d, ah, bh0, bh1);
+    mma(d, ah, bl0, bl1);
+    mma(d, al, bh0, bh1);
+}
+// ldmatrix lane addresses (bytes), row-major halves arrays with row stride ld:
+//   A tile 16x16 at (m0, k0)                            -> a0..a3
+__device__ __forceinline__ uint32_t a_addr(uint32_t base, int m0, int k0, int ld, int lane) {
+    return base + 2u * static_cast<uint32_t>((m0 + (lane & 15)) * ld + k0 + ((lane >> 4) << 3));
+}
+//   B tiles (k16 x n8) for n-tiles n0, n0+8 of an [n][k] array, non-trans -> b0,b1 | b0,b1
+__device__ __forceinline__ uint32_t bnk_addr(uint32_t base, int n0, int k0, int ld, int lane) {
+    return base + 2u * static_cast<uint32_t>((n0 + (lane & 7) + ((lane >> 4) << 3)) * ld + k0 +
+                                             (((lane >> 3) & 1) << 3));
+}
+//   B tiles for n-tiles n0, n0+8 of a [k][n] array, trans        -> b0,b1 | b0,b1
+__device__ __forceinline__ uint32_t bkn_addr(uint32_t base, int k0, int n0, int ld, int lane) {
+    return base + 2u * static_cast<uint32_t>((k0 + (lane & 7) + (((lane >> 3) & 1) << 3)) * ld + n0 +
+                                             ((lane >> 4) << 3));
+}
+
+// x = hi + lo, hi = fp16(x), lo = fp16(x - hi)
+__device__ __forceinline__ void split2(float a, float b, __half2& hi, __half2& lo) {
+    hi = __floats2half2_rn(a, b);
+    const float2 f = __half22float2(hi);
+    lo = __floats2half2_rn(a - f.x, b - f.y);
+}
+__device__ __forceinline__ void split1(float a, __half& hi, __half& lo) {
+    hi = __float2half_rn(a);
+    lo = __float2half_rn(a - __half2float(hi));
+}
+
+__device__ __forceinline__ void cp16(void* dst_smem, const void* src, bool valid) {
+    // zero-fills the 16 bytes when !valid (src-size 0); src stays a valid address
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(dst_smem)), "l"(src),
+                 "r"(valid ? 16 : 0)
+                 : "memory");
+}
+__device__ __forceinline__ void cp_commit_wait() {
+    asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
+}
+
+// ------------------------------------------------------------------ prep
+// smem: Kh Kl Qh Ql [64][LDH] halves (T aliases Kh.. once K/Q are done), A and P
+// [64][LA] fp32, Gamma and beta [64].
+constexpr int kPrepSmem = 4 * kC * LDH * 2 + 2 * kC * LA * 4 + 2 * kC * 4;
+
+__global__ void __launch_bounds__(256) k_gdn_chunk_prep(const ChunkParams p) {
+    extern __shared__ __align__(16) uint8_t smp[];
+    __half* Kh = reinterpret_cast<__half*>(smp);
+    __half* Kl = Kh + kC * LDH;
+    __half* Qh = Kl + kC * LDH;
+    __half* Ql = Qh + kC * LDH;
+    float* Am = reinterpret_cast<float*>(Ql + kC * LDH);
+    float* Pm = Am + kC * LA;
+    float* G = Pm + kC * LA;
+    float* Bt = G + kC;
+    float* Tm = reinterpret_cast<float*>(Kh);           // [64][LA], after K/Q are consumed
+
+    const uint32_t ch = blockIdx.x, h = blockIdx.y, sq = blockIdx.z;
+    const uint32_t kh = h % p.num_k_heads;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const uint32_t t0 = ch * kC;
+    const uint32_t nvalid = min(static_cast<uint32_t>(kC), p.T - t0);
+    const size_t qk_row = static_cast<size_t>(p.num_k_heads) * kD;
+    const size_t tok0 = static_cast<size_t>(sq) * p.T + t0;
+    const size_t sc = static_cast<size_t>(sq) * p.n_chunks + ch;
+
+    // ---- K, Q -> fp16 hi/lo; gates, betas ----
+    for (int i = tid; i < kC * kD / 4; i += 256) {
+        const int t = i / (kD / 4), c = (i % (kD / 4)) * 4;
+        float4 kv = make_float4(0.f, 0.f, 0.f, 0.f), qv = kv;
+        if (static_cast<uint32_t>(t) < nvalid) {
+            kv = *reinterpret_cast<const float4*>(p.k + (tok0 + t) * qk_row + kh * kD + c);
+            qv = *reinterpret_cast<const float4*>(p.q + (tok0 + t) * qk_row + kh * kD + c);
+        }
+        __half2 h0, l0, h1, l1;
+        split2(kv.x, kv.y, h0, l0);
+        split2(kv.z, kv.w, h1, l1);
+        *reinterpret_cast<__half2*>(Kh + t * LDH + c) = h0;
+        *reinterpret_cast<__half2*>(Kh + t * LDH + c + 2) = h1;
+        *reinterpret_cast<__half2*>(Kl + t * LDH + c) = l0;
+        *reinterpret_cast<__half2*>(Kl + t * LDH + c + 2) = l1;
+        split2(qv.x, qv.y, h0, l0);
+        split2(qv.z, qv.w, h1, l1);
+        *reinterpret_cast<__half2*>(Qh + t * LDH + c) = h0;
+        *reinterpret_cast<__half2*>(Qh + t * LDH + c + 2) = h1;
+        *reinterpret_cast<__half2*>(Ql + t * LDH + c) = l0;
+        *reinterpret_cast<__half2*>(Ql + t * LDH + c + 2) = l1;
+    }
+    if (tid < kC) {
+        const bool ok = static_cast<uint32_t>(tid) < nvalid;
+        G[tid] = ok ? p.gate[(tok0 + tid) * p.n_vheads + h] : 0.f;
+        Bt[tid] = ok ? p.beta[(tok0 + tid) * p.n_vheads + h] : 0.f;
+    }
+    __syncthreads();
+    // Gamma: inclusive prefix sum of the gates (warp 0), published for the state kernel
+    if (warp == 0) {
+        float x0 = G[lane], x1 = G[32 + lane];
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const float y0 = __shfl_up_sync(0xffffffffu, x0, o), y1 = __shfl_up_sync(0xffffffffu, x1, o);
+            if (lane >= o) {
+                x0 += y0;
+                x1 += y1;
+            }
+        }
+        x1 += __shfl_sync(0xffffffffu, x0, 31);
+        G[lane] = x0;
+        G[32 + lane] = x1;
+        p.gam[(sc * p.n_vheads + h) * kC + lane] = x0;
+        p.gam[(sc * p.n_vheads + h) * kC + 32 + lane] = x1;
+    }
+    // K/Q hi/lo to the scratch, once per k-head (by the v-head that equals it)
+    if (h < p.num_k_heads) {
+        __half* dst = p.kq + (sc * p.num_k_heads + kh) * kKqHalves;
+        const __half* src[4] = {Kh, Kl, Qh, Ql};
+        for (int i = tid; i < 4 * kC * (kD / 8); i += 256) {
+            const int a = i / (kC * (kD / 8)), r = (i / (kD / 8)) % kC, c = (i % (kD / 8)) * 8;
+            *reinterpret_cast<uint4*>(dst + (static_cast<size_t>(a) * kC + r) * kD + c) =
+                *reinterpret_cast<const uint4*>(src[a] + r * LDH + c);
+        }
+    }
+    __syncthreads();
+
+    // ---- K K^T (warps 0-3) and Q K^T (warps 4-7), m-tile = warp & 3, all 64 columns ----
+    {
+        const int mt = warp & 3, which = warp >> 2;
+        const uint32_t ah_b = smem_u32(which ? Qh : Kh), al_b = smem_u32(which ? Ql : Kl);
+        const uint32_t bh_b = smem_u32(Kh), bl_b = smem_u32(Kl);
+        float acc[8][4];
+#pragma unroll
+        for (int n = 0; n < 8; ++n) acc[n][0] = acc[n][1] = acc[n][2] = acc[n][3] = 0.f;
+#pragma unroll
+        for (int ks = 0; ks < kD / 16; ++ks) {
+            uint32_t ah[4], al[4];
+            ldsm4(a_addr(ah_b, 16 * mt, 16 * ks, LDH, lane), ah);
+            ldsm4(a_addr(al_b, 16 * mt, 16 * ks, LDH, lane), al);
+#pragma unroll
+            for (int np = 0; np < 4; ++np) {
+                uint32_t bh[4], bl[4];
+                ldsm4(bnk_addr(bh_b, 16 * np, 16 * ks, LDH, lane), bh);
+                ldsm4(bnk_addr(bl_b, 16 * np, 16 * ks, LDH, lane), bl);
+                mma3(acc[2 * np], ah, al, bh[0], bh[1], bl[0], bl[1]);
+                mma3(acc[2 * np + 1], ah, al, bh[2], bh[3], bl[2], bl[3]);
+            }
+        }
+        // A[t][i] = beta_t e^{Gamma_t - Gamma_i} kk (i < t);  P[t][i] = e^{Gamma_t - Gamma_i} qk (i <= t)
+        const int g = lane >> 2, tq = lane & 3;
+#pragma unroll
+        for (int n = 0; n < 8; ++n) {
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const int t = 16 * mt + g + ((e >> 1) << 3), i = 8 * n + 2 * tq + (e & 1);
+                float val = 0.f;
+                if (which == 0) {
+                    if (i < t) val = Bt[t] * expf(G[t] - G[i]) * acc[n][e];
+                    Am[t * LA + i] = val;
+                } else {
+                    if (i <= t) val = expf(G[t] - G[i]) * acc[n][e];
+                    Pm[t * LA + i] = val;
+                }
+            }
+        }
+    }
+    __syncthreads();
+
+    // ---- T = (I + A)^-1 by forward substitution, one column per thread (threads 0-63) ----
+    // Column c: x_t = -sum_{i<t} A[t][i] x_i for t > c, x_c = 1, x_t = 0 for t < c.  A[t][i]
+    // is zero for i >= t, so each row sums over whole float4 groups; every thread reads the
+    // same A element at the same time (broadcast).
+    if (tid < kC) {
+        const int c = tid;
+        float x[kC];
+#pragma unroll
+        for (int t = 0; t < kC; ++t) x[t] = (t == c) ? 1.f : 0.f;
+#pragma unroll
+        for (int t = 1; t < kC; ++t) {
+            float s0 = 0.f, s1 = 0.f;
+#pragma unroll
+            for (int i4 = 0; i4 < (t + 3) / 4; ++i4) {
+                const float4 a = *reinterpret_cast<const float4*>(Am + t * LA + 4 * i4);
+                s0 = fmaf(a.x, x[4 * i4], s0);
+                s1 = fmaf(a.y, x[4 * i4 + 1], s1);
+                s0 = fmaf(a.z, x[4 * i4 + 2], s0);
+                s1 = fmaf(a.w, x[4 * i4 + 3], s1);
+            }
+            if (t > c) x[t] = -(s0 + s1);
+        }
+#pragma unroll
+        for (int t = 0; t < kC; ++t) Tm[t * LA + c] = x[t];
+    }
+    __syncthreads();
+
+    // ---- T, P -> fp16 hi/lo scratch ----
+    __half* dst = p.tp + (sc * p.n_vheads + h) * kTpHalves;
+    for (int i = tid; i < kC * kC / 2; i += 256) {
+        const int t = i / (kC / 2), c = (i % (kC / 2)) * 2;
+        __half2 th, tl, ph, pl;
+        split2(Tm[t * LA + c], Tm[t * LA + c + 1], th, tl);
+        split2(Pm[t * LA + c], Pm[t * LA + c + 1], ph, pl);
+        *reinterpret_cast<__half2*>(dst + 0 * kC * kC + t * kC + c) = th;
+        *reinterpret_cast<__half2*>(dst + 1 * kC * kC + t * kC + c) = tl;
+        *reinterpret_cast<__half2*>(dst + 2 * kC * kC + t * kC + c) = ph;
+        *reinterpret_cast<__half2*>(dst + 3 * kC * kC + t * kC + c) = pl;
+    }
+}
+
+// ------------------------------------------------------------------ state
+constexpr int kStateSmem = (4 * kC * LDH + 4 * kC * LDC + 2 * kR * LDH + 6 * kR * LDC) * 2 + kC * kR * 4 + 2 * kC * 4;
+
+__global__ void __launch_bounds__(256, 1) k_gdn_chunk_state(const ChunkParams p) {
+    extern __shared__ __align__(16) uint8_t sms[];
+    __half* Kh = reinterpret_cast<__half*>(sms);   // [64][LDH]  K hi   (A of K S^T; B of Ud^T K)
+    __half* Kl = Kh + kC * LDH;
+    __half* Qh = Kl + kC * LDH;                    // [64][LDH]  Q
+    __half* Ql = Qh + kC * LDH;
+    __half* Th = Ql + kC * LDH;                    // [64][LDC]  T
+    __half* Tl = Th + kC * LDC;
+    __half* Ph = Tl + kC * LDC;                    // [64][LDC]  P
+    __half* Pl = Ph + kC * LDC;
+    __half* Sh = Pl + kC * LDC;                    // [32][LDH]  S slice (rows r, cols c)
+    __half* Sl = Sh + kR * LDH;
+    __half* Rh = Sl + kR * LDH;                    // [32][LDC]  Rm^T  (r, token)
+    __half* Rl = Rh + kR * LDC;
+    __half* Uh = Rl + kR * LDC;                    // [32][LDC]  U^T
+    __half* Ul = Uh + kR * LDC;
+    __half* Dh = Ul + kR * LDC;                    // [32][LDC]  (decayed U)^T
+    __half* Dl = Dh + kR * LDC;
+    float* Vs = reinterpret_cast<float*>(Dl + kR * LDC);   // [64][32]
+    float* Gs = Vs + kC * kR;                      // [64] Gamma
+    float* Bs = Gs + kC;                           // [64] beta
+
+    const uint32_t rb = blockIdx.x, h = blockIdx.y, sq = blockIdx.z;
+    const uint32_t kh = h % p.num_k_heads;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int g = lane >> 2, tq = lane & 3;
+    const size_t v_row = static_cast<size_t>(p.n_vheads) * kD;
+    float* Sg = p.S + (static_cast<size_t>(sq) * p.n_vheads + h) * kD * kD + static_cast<size_t>(rb) * kR * kD;
+    const float inv_sqrt_d = 1.0f / sqrtf(static_cast<float>(kD));
+
+    // S slice accumulators: warp -> row tile ms = warp & 1 (16 rows), columns 32 * (warp >> 1) .. +31
+    const int ms = warp & 1, cq = warp >> 1;
+    float sacc[4][4];
+#pragma unroll
+    for (int n = 0; n < 4; ++n) {
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            const int r = 16 * ms + g + ((e >> 1) << 3), c = 32 * cq + 8 * n + 2 * tq + (e & 1);
+            sacc[n][e] = Sg[static_cast<size_t>(r) * kD + c];
+        }
+    }
+    auto publish_s = [&]() {
+#pragma unroll
+        for (int n = 0; n < 4; ++n) {
+#pragma unroll
+            for (int half = 0; half < 2; ++half) {
+                const int r = 16 * ms + g + 8 * half, c = 32 * cq + 8 * n + 2 * tq;
+                __half2 hi, lo;
+                split2(sacc[n][2 * half], sacc[n][2 * half + 1], hi, lo);
+                *reinterpret_cast<__half2*>(Sh + r * LDH + c) = hi;
+                *reinterpret_cast<__half2*>(Sl + r * LDH + c) = lo;
+            }
+        }
+    };
+    publish_s();
+
+    const uint32_t Kh_u = smem_u32(Kh), Kl_u = smem_u32(Kl), Qh_u = smem_u32(Qh), Ql_u = smem_u32(Ql);
+    const uint32_t Th_u = smem_u32(Th), Tl_u = smem_u32(Tl), Ph_u = smem_u32(Ph), Pl_u = smem_u32(Pl);
+    const uint32_t Sh_u = smem_u32(Sh), Sl_u = smem_u32(Sl), Rh_u = smem_u32(Rh), Rl_u = smem_u32(Rl);
+    const uint32_t Uh_u = smem_u32(Uh), Ul_u = smem_u32(Ul), Dh_u = smem_u32(Dh), Dl_u = smem_u32(Dl);
+
+    for (uint32_t ch = 0; ch < p.n_chunks; ++ch) {
+        const uint32_t t0 = ch * kC;
+        const uint32_t nvalid = min(static_cast<uint32_t>(kC), p.T - t0);
+        const size_t sc = static_cast<size_t>(sq) * p.n_chunks + ch;
+        const size_t tok0 = static_cast<size_t>(sq) * p.T + t0;
+        // ---- stage the chunk: K/Q hi/lo, T/P hi/lo, this slice's V, Gamma, beta ----
+        {
+            const __half* kq = p.kq + (sc * p.num_k_heads + kh) * kKqHalves;
+            for (int i = tid; i < 4 * kC * (kD / 8); i += 256) {
+                const int a = i / (kC * (kD / 8)), r = (i / (kD / 8)) % kC, c = (i % (kD / 8)) * 8;
+                cp16(Kh + a * kC * LDH + r * LDH + c, kq + (static_cast<size_t>(a) * kC + r) * kD + c, true);
+            }
+            const __half* tp = p.tp + (sc * p.n_vheads + h) * kTpHalves;
+            for (int i = tid; i < 4 * kC * (kC / 8); i += 256) {
+                const int a = i / (kC * (kC / 8)), r = (i / (kC / 8)) % kC, c = (i % (kC / 8)) * 8;
+                cp16(Th + a * kC * LDC + r * LDC + c, tp + (static_cast<size_t>(a) * kC + r) * kC + c, true);
+            }
+            for (int i = tid; i < kC * (kR / 4); i += 256) {
+                const int t = i / (kR / 4), c = (i % (kR / 4)) * 4;
+                const bool ok = static_cast<uint32_t>(t) < nvalid;
+                cp16(Vs + t * kR + c, p.v + (ok ? (tok0 + t) * v_row + h * kD + rb * kR + c : 0), ok);
+            }
+            if (tid < kC / 4)
+                cp16(Gs + 4 * tid, p.gam + (sc * p.n_vheads + h) * kC + 4 * tid, true);
+            if (tid >= 64 && tid < 64 + kC) {
+                const int t = tid - 64;
+                Bs[t] = static_cast<uint32_t>(t) < nvalid ? p.beta[(tok0 + t) * p.n_vheads + h] : 0.f;
+            }
+            cp_commit_wait();
+        }
+        __syncthreads();
+
+        // ---- phase A: R1 = K S^T (warps 0-3) and O1 = Q S^T (warps 4-7); m-tile = warp & 3 ----
+        const int mt = warp & 3, which = warp >> 2;
+        float acc[4][4];
+#pragma unroll
+        for (int n = 0; n < 4; ++n) acc[n][0] = acc[n][1] = acc[n][2] = acc[n][3] = 0.f;
+        {
+            const uint32_t ah_b = which ? Qh_u : Kh_u, al_b = which ? Ql_u : Kl_u;
+#pragma unroll
+            for (int ks = 0; ks < kD / 16; ++ks) {
+                uint32_t ah[4], al[4];
+                ldsm4(a_addr(ah_b, 16 * mt, 16 * ks, LDH, lane), ah);
+                ldsm4(a_addr(al_b, 16 * mt, 16 * ks, LDH, lane), al);
+#pragma unroll
+                for (int np = 0; np < 2; ++np) {
+                    uint32_t bh[4], bl[4];
+                    ldsm4(bnk_addr(Sh_u, 16 * np, 16 * ks, LDH, lane), bh);
+                    ldsm4(bnk_addr(Sl_u, 16 * np, 16 * ks, LDH, lane), bl);
+                    mma3(acc[2 * np], ah, al, bh[0], bh[1], bl[0], bl[1]);
+                    mma3(acc[2 * np + 1], ah, al, bh[2], bh[3], bl[2], bl[3]);
+                }
+            }
+        }
+        // epilogue A: Rm = beta (V - gamma R1) -> Rm^T hi/lo;  O1 <- gamma O1 (kept in registers)
+        {
+            const int ta = 16 * mt + g, tb = ta + 8;
+            const float ga = expf(Gs[ta]), gb = expf(Gs[tb]);
+            if (which == 0) {
+                const float ba = Bs[ta], bb = Bs[tb];
+#pragma unroll
+                for (int n = 0; n < 4; ++n) {
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) {
+                        const int t = (e < 2) ? ta : tb, r = 8 * n + 2 * tq + (e & 1);
+                        const float rm = ((e < 2) ? ba : bb) * (Vs[t * kR + r] - ((e < 2) ? ga : gb) * acc[n][e]);
+                        __half hi, lo;
+                        split1(rm, hi, lo);
+                        Rh[r * LDC + t] = hi;
+                        Rl[r * LDC + t] = lo;
+                    }
+                }
+            } else {
+#pragma unroll
+                for (int n = 0; n < 4; ++n) {
+                    acc[n][0] *= ga;
+                    acc[n][1] *= ga;
+                    acc[n][2] *= gb;
+                    acc[n][3] *= gb;
+                }
+            }
+        }
+        __syncthreads();
+
+        // ---- phase B: U = T Rm, all warps: m-tile = warp & 3, S-row tiles 16 * (warp >> 2) .. +15 ----
+        {
+            const int np = warp >> 2;
+            float u[2][4];
+#pragma unroll
+            for (int n = 0; n < 2; ++n) u[n][0] = u[n][1] = u[n][2] = u[n][3] = 0.f;
+            for (int ks = 0; ks <= mt; ++ks) {   // T is lower triangular
+                uint32_t th[4], tl[4], bh[4], bl[4];
+                ldsm4(a_addr(Th_u, 16 * mt, 16 * ks, LDC, lane), th);
+                ldsm4(a_addr(Tl_u, 16 * mt, 16 * ks, LDC, lane), tl);
+                ldsm4(bnk_addr(Rh_u, 16 * np, 16 * ks, LDC, lane), bh);
+                ldsm4(bnk_addr(Rl_u, 16 * np, 16 * ks, LDC, lane), bl);
+                mma3(u[0], th, tl, bh[0], bh[1], bl[0], bl[1]);
+                mma3(u[1], th, tl, bh[2], bh[3], bl[2], bl[3]);
+            }
+            const float glast = Gs[kC - 1];
+#pragma unroll
+            for (int n = 0; n < 2; ++n) {
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    const int t = 16 * mt + g + ((e >> 1) << 3), r = 16 * np + 8 * n + 2 * tq + (e & 1);
+                    __half hi, lo;
+                    split1(u[n][e], hi, lo);
+                    Uh[r * LDC + t] = hi;
+                    Ul[r * LDC + t] = lo;
+                    split1(u[n][e] * expf(glast - Gs[t]), hi, lo);
+                    Dh[r * LDC + t] = hi;
+                    Dl[r * LDC + t] = lo;
+                }
+            }
+        }
+        __syncthreads();
+
+        // ---- phase C1 (warps 4-7): O = gamma O1 + P U, written out / sqrt(hv) ----
+        if (which == 1) {
+            for (int ks = 0; ks <= mt; ++ks) {   // P is lower triangular
+                uint32_t ph[4], pl[4];
+                ldsm4(a_addr(Ph_u, 16 * mt, 16 * ks, LDC, lane), ph);
+                ldsm4(a_addr(Pl_u, 16 * mt, 16 * ks, LDC, lane), pl);
+#pragma unroll
+                for (int np = 0; np < 2; ++np) {
+                    uint32_t bh[4], bl[4];
+                    ldsm4(bnk_addr(Uh_u, 16 * np, 16 * ks, LDC, lane), bh);
+                    ldsm4(bnk_addr(Ul_u, 16 * np, 16 * ks, LDC, lane), bl);
+                    mma3(acc[2 * np], ph, pl, bh[0], bh[1], bl[0], bl[1]);
+                    mma3(acc[2 * np + 1], ph, pl, bh[2], bh[3], bl[2], bl[3]);
+                }
+            }
+#pragma unroll
+            for (int half = 0; half < 2; ++half) {
+                const int t = 16 * mt + g + 8 * half;
+                if (static_cast<uint32_t>(t) < nvalid) {
+                    float* o = p.out + (tok0 + t) * v_row + h * kD + rb * kR;
+#pragma unroll
+                    for (int n = 0; n < 4; ++n)
+                        *reinterpret_cast<float2*>(o + 8 * n + 2 * tq) =
+                            make_float2(acc[n][2 * half] * inv_sqrt_d, acc[n][2 * half + 1] * inv_sqrt_d);
+                }
+            }
+        }
+        // ---- phase C2 (all warps): S <- gamma_last S + (decayed U)^T K ----
+        {
+            const float gl = expf(Gs[kC - 1]);
+#pragma unroll
+            for (int n = 0; n < 4; ++n) {
+                sacc[n][0] *= gl;
+                sacc[n][1] *= gl;
+                sacc[n][2] *= gl;
+                sacc[n][3] *= gl;
+            }
+#pragma unroll
+            for (int ks = 0; ks < kC / 16; ++ks) {
+                uint32_t dh[4], dl[4];
+                ldsm4(a_addr(Dh_u, 16 * ms, 16 * ks, LDC, lane), dh);
+                ldsm4(a_addr(Dl_u, 16 * ms, 16 * ks, LDC, lane), dl);
+#pragma unroll
+                for (int np = 0; np < 2; ++np) {
+                    uint32_t bh[4], bl[4];
+                    ldsm4t(bkn_addr(Kh_u, 16 * ks, 32 * cq + 16 * np, LDH, lane), bh);
+                    ldsm4t(bkn_addr(Kl_u, 16 * ks, 32 * cq + 16 * np, LDH, lane), bl);
+                    mma3(sacc[2 * np], dh, dl, bh[0], bh[1], bl[0], bl[1]);
+                    mma3(sacc[2 * np + 1], dh, dl, bh[2], bh[3], bl[2], bl[3]);
+                }
+            }
+        }
+        publish_s();
+        __syncthreads();   // everything of this chunk read before the next chunk is staged
+    }
+#pragma unroll
+    for (int n = 0; n < 4; ++n) {
+#pragma unroll
+        for (int half = 0; half < 2; ++half) {
+            const int r = 16 * ms + g + 8 * half, c = 32 * cq + 8 * n + 2 * tq;
+            *reinterpret_cast<float2*>(Sg + static_cast<size_t>(r) * kD + c) =
+                make_float2(sacc[n][2 * half], sacc[n][2 * half + 1]);
+        }
+    }
+}
+
+}  // namespace
+
+size_t gdn_chunk_scratch_bytes(uint32_t n_seqs, uint32_t T, uint32_t num_k_heads, uint32_t n_vheads) {
+    const size_t n_chunks = (T + kC - 1) / kC;
+    const size_t sc = static_cast<size_t>(n_seqs) * n_chunks;
+    const size_t kq = sc * num_k_heads * kKqHalves * 2;
+    const size_t tp = sc * n_vheads * kTpHalves * 2;
+    const size_t gam = sc * n_vheads * kC * 4;
+    return kq + tp + gam;
+}
+
+// Geometry was checked by the caller (hk == hv == 128, aligned pointers).
+int gdn_prefill_chunked(float* S, float* out, const float* q, const float* k, const float* v, const float* gate,
+                        const float* beta, uint32_t n_seqs, uint32_t T, uint32_t num_k_heads, uint32_t n_vheads,
+                        void* scratch, cudaStream_t st, char* err, size_t errlen) {
+    static bool attr_done[64] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev >= 0 && dev < 64 && !attr_done[dev]) {
+        if (cudaFuncSetAttribute(k_gdn_chunk_prep, cudaFuncAttributeMaxDynamicSharedMemorySize, kPrepSmem) !=
+                cudaSuccess ||
+            cudaFuncSetAttribute(k_gdn_chunk_state, cudaFuncAttributeMaxDynamicSharedMemorySize, kStateSmem) !=
+                cudaSuccess) {
+            set_err(err, errlen, "gdn_prefill: shared-memory attribute failed");
+            return -1;
+        }
+        attr_done[dev] = true;
+    }
+    const uint32_t n_chunks = (T + kC - 1) / kC;
+    const size_t sc = static_cast<size_t>(n_seqs) * n_chunks;
+    ChunkParams p{};
+    p.q = q;
+    p.k = k;
+    p.v = v;
+    p.gate = gate;
+    p.beta = beta;
+    p.S = S;
+    p.out = out;
+    p.kq = static_cast<__half*>(scratch);
+    p.tp = p.kq + sc * num_k_heads * kKqHalves;
+    p.gam = reinterpret_cast<float*>(p.tp + sc * n_vheads * kTpHalves);
+    p.T = T;
+    p.n_chunks = n_chunks;
+    p.num_k_heads = num_k_heads;
+    p.n_vheads = n_vheads;
+    k_gdn_chunk_prep<<<dim3(n_chunks, n_vheads, n_seqs), 256, kPrepSmem, st>>>(p);
+    YATTN_CHECK_LAUNCH(err, errlen, "gdn_prefill chunk prep");
+    k_gdn_chunk_state<<<dim3(kD / kR, n_vheads, n_seqs), 256, kStateSmem, st>>>(p);
+    YATTN_CHECK_LAUNCH(err, errlen, "gdn_prefill chunk state");
+    return 0;
+}
+
+}  // namespace yattn
