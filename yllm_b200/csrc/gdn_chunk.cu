@@ -48,9 +48,10 @@ constexpr int LA = kC + 4;      // fp32 row stride of 64 x 64 tiles in the prep 
 // Scratch, per (sequence, chunk) sc = seq * n_chunks + chunk:
 //   kq[(sc * num_k_heads + kh)]: K_hi, K_lo, Q_hi, Q_lo   fp16 [64][128] each
 //   tp[(sc * n_vheads + h)]:     T_hi, T_lo, P_hi, P_lo   fp16 [64][64] each
-//   gam[(sc * n_vheads + h)]:    Gamma                    fp32 [64]
+//   gam[(sc * n_vheads + h)]:    Gamma, e^Gamma, e^(Gamma_63 - Gamma)   fp32 [3][64]
 constexpr size_t kKqHalves = 4ull * kC * kD;
 constexpr size_t kTpHalves = 4ull * kC * kC;
+constexpr size_t kGamFloats = 3ull * kC;
 
 struct ChunkParams {
     const float* q;                 // [n_seq][T][num_k_heads*128]
@@ -126,9 +127,6 @@ __device__ __forceinline__ void cp16(void* dst_smem, const void* src, bool valid
                  "r"(valid ? 16 : 0)
                  : "memory");
 }
-__device__ __forceinline__ void cp_commit_wait() {
-    asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
-}
 
 // ------------------------------------------------------------------ prep
 // smem: Kh Kl Qh Ql [64][LDH] halves (T aliases Kh.. once K/Q are done), A and P
@@ -156,14 +154,22 @@ __global__ void __launch_bounds__(256) k_gdn_chunk_prep(const ChunkParams p) {
     const size_t tok0 = static_cast<size_t>(sq) * p.T + t0;
     const size_t sc = static_cast<size_t>(sq) * p.n_chunks + ch;
 
-    // ---- K, Q -> fp16 hi/lo; gates, betas ----
-    for (int i = tid; i < kC * kD / 4; i += 256) {
-        const int t = i / (kD / 4), c = (i % (kD / 4)) * 4;
-        float4 kv = make_float4(0.f, 0.f, 0.f, 0.f), qv = kv;
+    // ---- K, Q -> fp16 hi/lo; gates, betas (all 16 float4 loads of a thread in flight) ----
+    constexpr int NL = kC * kD / 4 / 256;   // float4 of K (and of Q) per thread
+    float4 kvs[NL], qvs[NL];
+#pragma unroll
+    for (int j = 0; j < NL; ++j) {
+        const int i = tid + 256 * j, t = i / (kD / 4), c = (i % (kD / 4)) * 4;
+        kvs[j] = qvs[j] = make_float4(0.f, 0.f, 0.f, 0.f);
         if (static_cast<uint32_t>(t) < nvalid) {
-            kv = *reinterpret_cast<const float4*>(p.k + (tok0 + t) * qk_row + kh * kD + c);
-            qv = *reinterpret_cast<const float4*>(p.q + (tok0 + t) * qk_row + kh * kD + c);
+            kvs[j] = __ldcs(reinterpret_cast<const float4*>(p.k + (tok0 + t) * qk_row + kh * kD + c));
+            qvs[j] = __ldcs(reinterpret_cast<const float4*>(p.q + (tok0 + t) * qk_row + kh * kD + c));
         }
+    }
+#pragma unroll
+    for (int j = 0; j < NL; ++j) {
+        const int i = tid + 256 * j, t = i / (kD / 4), c = (i % (kD / 4)) * 4;
+        const float4 kv = kvs[j], qv = qvs[j];
         __half2 h0, l0, h1, l1;
         split2(kv.x, kv.y, h0, l0);
         split2(kv.z, kv.w, h1, l1);
@@ -198,17 +204,23 @@ __global__ void __launch_bounds__(256) k_gdn_chunk_prep(const ChunkParams p) {
         x1 += __shfl_sync(0xffffffffu, x0, 31);
         G[lane] = x0;
         G[32 + lane] = x1;
-        p.gam[(sc * p.n_vheads + h) * kC + lane] = x0;
-        p.gam[(sc * p.n_vheads + h) * kC + 32 + lane] = x1;
+        const float glast = __shfl_sync(0xffffffffu, x1, 31);
+        float* gm = p.gam + (sc * p.n_vheads + h) * kGamFloats;
+        gm[lane] = x0;
+        gm[32 + lane] = x1;
+        gm[kC + lane] = expf(x0);
+        gm[kC + 32 + lane] = expf(x1);
+        gm[2 * kC + lane] = expf(glast - x0);
+        gm[2 * kC + 32 + lane] = expf(glast - x1);
     }
     // K/Q hi/lo to the scratch, once per k-head (by the v-head that equals it)
-    if (h < p.num_k_heads) {
+    if (h < p.num_k_heads) {   // Kh, Kl, Qh, Ql are consecutive [64][LDH] arrays
         __half* dst = p.kq + (sc * p.num_k_heads + kh) * kKqHalves;
-        const __half* src[4] = {Kh, Kl, Qh, Ql};
+#pragma unroll 4
         for (int i = tid; i < 4 * kC * (kD / 8); i += 256) {
-            const int a = i / (kC * (kD / 8)), r = (i / (kD / 8)) % kC, c = (i % (kD / 8)) * 8;
-            *reinterpret_cast<uint4*>(dst + (static_cast<size_t>(a) * kC + r) * kD + c) =
-                *reinterpret_cast<const uint4*>(src[a] + r * LDH + c);
+            const int ar = i / (kD / 8), c = (i % (kD / 8)) * 8;   // ar = array * 64 + row
+            *reinterpret_cast<uint4*>(dst + static_cast<size_t>(ar) * kD + c) =
+                *reinterpret_cast<const uint4*>(Kh + ar * LDH + c);
         }
     }
     __syncthreads();
@@ -266,16 +278,16 @@ __global__ void __launch_bounds__(256) k_gdn_chunk_prep(const ChunkParams p) {
         for (int t = 0; t < kC; ++t) x[t] = (t == c) ? 1.f : 0.f;
 #pragma unroll
         for (int t = 1; t < kC; ++t) {
-            float s0 = 0.f, s1 = 0.f;
+            float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
 #pragma unroll
             for (int i4 = 0; i4 < (t + 3) / 4; ++i4) {
                 const float4 a = *reinterpret_cast<const float4*>(Am + t * LA + 4 * i4);
                 s0 = fmaf(a.x, x[4 * i4], s0);
                 s1 = fmaf(a.y, x[4 * i4 + 1], s1);
-                s0 = fmaf(a.z, x[4 * i4 + 2], s0);
-                s1 = fmaf(a.w, x[4 * i4 + 3], s1);
+                s2 = fmaf(a.z, x[4 * i4 + 2], s2);
+                s3 = fmaf(a.w, x[4 * i4 + 3], s3);
             }
-            if (t > c) x[t] = -(s0 + s1);
+            if (t > c) x[t] = -((s0 + s1) + (s2 + s3));
         }
 #pragma unroll
         for (int t = 0; t < kC; ++t) Tm[t * LA + c] = x[t];
@@ -297,19 +309,25 @@ __global__ void __launch_bounds__(256) k_gdn_chunk_prep(const ChunkParams p) {
 }
 
 // ------------------------------------------------------------------ state
-constexpr int kStateSmem = (4 * kC * LDH + 4 * kC * LDC + 2 * kR * LDH + 6 * kR * LDC) * 2 + kC * kR * 4 + 2 * kC * 4;
+// smem of the state kernel, in halves unless noted:
+//   K hi/lo   x2 buffers [64][LDH]   P hi/lo x2 buffers [64][LDC]   (chunk c uses buffer c & 1)
+//   Q hi/lo      [64][LDH]           T hi/lo            [64][LDC]
+//   S hi/lo      [32][LDH]           Rm^T, U^T, Ud^T hi/lo [32][LDC]
+//   V [64][32] fp32, (Gamma, e^Gamma, e^(Gamma_63 - Gamma)) and beta x2 [64] fp32
+constexpr int kStateSmem =
+    (4 * kC * LDH + 4 * kC * LDC + 2 * kC * LDH + 2 * kC * LDC + 2 * kR * LDH + 6 * kR * LDC) * 2 + kC * kR * 4 +
+    2 * (3 + 1) * kC * 4;
+static_assert(kStateSmem <= 232448, "state kernel shared memory");
 
 __global__ void __launch_bounds__(256, 1) k_gdn_chunk_state(const ChunkParams p) {
     extern __shared__ __align__(16) uint8_t sms[];
-    __half* Kh = reinterpret_cast<__half*>(sms);   // [64][LDH]  K hi   (A of K S^T; B of Ud^T K)
-    __half* Kl = Kh + kC * LDH;
-    __half* Qh = Kl + kC * LDH;                    // [64][LDH]  Q
+    __half* Kb = reinterpret_cast<__half*>(sms);   // [2 buf][hi, lo][64][LDH]
+    __half* Pb = Kb + 4 * kC * LDH;                // [2 buf][hi, lo][64][LDC]
+    __half* Qh = Pb + 4 * kC * LDC;                // [64][LDH]
     __half* Ql = Qh + kC * LDH;
-    __half* Th = Ql + kC * LDH;                    // [64][LDC]  T
+    __half* Th = Ql + kC * LDH;                    // [64][LDC]
     __half* Tl = Th + kC * LDC;
-    __half* Ph = Tl + kC * LDC;                    // [64][LDC]  P
-    __half* Pl = Ph + kC * LDC;
-    __half* Sh = Pl + kC * LDC;                    // [32][LDH]  S slice (rows r, cols c)
+    __half* Sh = Tl + kC * LDC;                    // [32][LDH]  S slice (rows r, cols c)
     __half* Sl = Sh + kR * LDH;
     __half* Rh = Sl + kR * LDH;                    // [32][LDC]  Rm^T  (r, token)
     __half* Rl = Rh + kR * LDC;
@@ -318,8 +336,8 @@ __global__ void __launch_bounds__(256, 1) k_gdn_chunk_state(const ChunkParams p)
     __half* Dh = Ul + kR * LDC;                    // [32][LDC]  (decayed U)^T
     __half* Dl = Dh + kR * LDC;
     float* Vs = reinterpret_cast<float*>(Dl + kR * LDC);   // [64][32]
-    float* Gs = Vs + kC * kR;                      // [64] Gamma
-    float* Bs = Gs + kC;                           // [64] beta
+    float* Gb = Vs + kC * kR;                      // [2][3][64] Gamma, e^Gamma, e^(Gamma_63 - Gamma)
+    float* Bb = Gb + 2 * kGamFloats;               // [2][64] beta
 
     const uint32_t rb = blockIdx.x, h = blockIdx.y, sq = blockIdx.z;
     const uint32_t kh = h % p.num_k_heads;
@@ -328,6 +346,56 @@ __global__ void __launch_bounds__(256, 1) k_gdn_chunk_state(const ChunkParams p)
     const size_t v_row = static_cast<size_t>(p.n_vheads) * kD;
     float* Sg = p.S + (static_cast<size_t>(sq) * p.n_vheads + h) * kD * kD + static_cast<size_t>(rb) * kR * kD;
     const float inv_sqrt_d = 1.0f / sqrtf(static_cast<float>(kD));
+
+    auto sc_of = [&](uint32_t ch) { return static_cast<size_t>(sq) * p.n_chunks + ch; };
+    auto tok_of = [&](uint32_t ch) { return static_cast<size_t>(sq) * p.T + static_cast<size_t>(ch) * kC; };
+    auto nvalid_of = [&](uint32_t ch) { return min(static_cast<uint32_t>(kC), p.T - ch * kC); };
+    // cp.async staging of chunk ch, one piece at a time (each piece's buffer must be free)
+    auto stage_kp = [&](uint32_t ch) {   // K hi/lo, P hi/lo, Gamma, beta into buffer ch & 1
+        const int b = ch & 1;
+        const size_t sc = sc_of(ch);
+        const __half* kq = p.kq + (sc * p.num_k_heads + kh) * kKqHalves;
+        for (int i = tid; i < 2 * kC * (kD / 8); i += 256) {
+            const int a = i / (kC * (kD / 8)), r = (i / (kD / 8)) % kC, c = (i % (kD / 8)) * 8;
+            cp16(Kb + (2 * b + a) * kC * LDH + r * LDH + c, kq + (static_cast<size_t>(a) * kC + r) * kD + c, true);
+        }
+        const __half* tp = p.tp + (sc * p.n_vheads + h) * kTpHalves + 2 * kC * kC;   // P hi, P lo
+        for (int i = tid; i < 2 * kC * (kC / 8); i += 256) {
+            const int a = i / (kC * (kC / 8)), r = (i / (kC / 8)) % kC, c = (i % (kC / 8)) * 8;
+            cp16(Pb + (2 * b + a) * kC * LDC + r * LDC + c, tp + (static_cast<size_t>(a) * kC + r) * kC + c, true);
+        }
+        if (tid < static_cast<int>(kGamFloats / 4))
+            cp16(Gb + b * kGamFloats + 4 * tid, p.gam + (sc * p.n_vheads + h) * kGamFloats + 4 * tid, true);
+        if (tid >= 64 && tid < 64 + kC) {
+            const int t = tid - 64;
+            Bb[b * kC + t] = static_cast<uint32_t>(t) < nvalid_of(ch) ? p.beta[(tok_of(ch) + t) * p.n_vheads + h] : 0.f;
+        }
+        asm volatile("cp.async.commit_group;" ::: "memory");
+    };
+    auto stage_qv = [&](uint32_t ch) {   // Q hi/lo and this slice's V
+        const size_t sc = sc_of(ch);
+        const __half* kq = p.kq + (sc * p.num_k_heads + kh) * kKqHalves + 2 * kC * kD;   // Q hi, Q lo
+        for (int i = tid; i < 2 * kC * (kD / 8); i += 256) {
+            const int a = i / (kC * (kD / 8)), r = (i / (kD / 8)) % kC, c = (i % (kD / 8)) * 8;
+            cp16(Qh + a * kC * LDH + r * LDH + c, kq + (static_cast<size_t>(a) * kC + r) * kD + c, true);
+        }
+        const uint32_t nv = nvalid_of(ch);
+        const size_t tok0 = tok_of(ch);
+        for (int i = tid; i < kC * (kR / 4); i += 256) {
+            const int t = i / (kR / 4), c = (i % (kR / 4)) * 4;
+            const bool ok = static_cast<uint32_t>(t) < nv;
+            cp16(Vs + t * kR + c, p.v + (ok ? (tok0 + t) * v_row + h * kD + rb * kR + c : 0), ok);
+        }
+        asm volatile("cp.async.commit_group;" ::: "memory");
+    };
+    auto stage_t = [&](uint32_t ch) {   // T hi/lo
+        const __half* tp = p.tp + (sc_of(ch) * p.n_vheads + h) * kTpHalves;
+        for (int i = tid; i < 2 * kC * (kC / 8); i += 256) {
+            const int a = i / (kC * (kC / 8)), r = (i / (kC / 8)) % kC, c = (i % (kC / 8)) * 8;
+            cp16(Th + a * kC * LDC + r * LDC + c, tp + (static_cast<size_t>(a) * kC + r) * kC + c, true);
+        }
+        asm volatile("cp.async.commit_group;" ::: "memory");
+    };
 
     // S slice accumulators: warp -> row tile ms = warp & 1 (16 rows), columns 32 * (warp >> 1) .. +31
     const int ms = warp & 1, cq = warp >> 1;
@@ -354,43 +422,28 @@ __global__ void __launch_bounds__(256, 1) k_gdn_chunk_state(const ChunkParams p)
         }
     };
     publish_s();
+    stage_kp(0);
+    stage_qv(0);
+    stage_t(0);
+    asm volatile("cp.async.wait_group 0;" ::: "memory");
+    __syncthreads();
 
-    const uint32_t Kh_u = smem_u32(Kh), Kl_u = smem_u32(Kl), Qh_u = smem_u32(Qh), Ql_u = smem_u32(Ql);
-    const uint32_t Th_u = smem_u32(Th), Tl_u = smem_u32(Tl), Ph_u = smem_u32(Ph), Pl_u = smem_u32(Pl);
+    const uint32_t Qh_u = smem_u32(Qh), Ql_u = smem_u32(Ql);
+    const uint32_t Th_u = smem_u32(Th), Tl_u = smem_u32(Tl);
     const uint32_t Sh_u = smem_u32(Sh), Sl_u = smem_u32(Sl), Rh_u = smem_u32(Rh), Rl_u = smem_u32(Rl);
     const uint32_t Uh_u = smem_u32(Uh), Ul_u = smem_u32(Ul), Dh_u = smem_u32(Dh), Dl_u = smem_u32(Dl);
 
     for (uint32_t ch = 0; ch < p.n_chunks; ++ch) {
-        const uint32_t t0 = ch * kC;
-        const uint32_t nvalid = min(static_cast<uint32_t>(kC), p.T - t0);
-        const size_t sc = static_cast<size_t>(sq) * p.n_chunks + ch;
-        const size_t tok0 = static_cast<size_t>(sq) * p.T + t0;
-        // ---- stage the chunk: K/Q hi/lo, T/P hi/lo, this slice's V, Gamma, beta ----
-        {
-            const __half* kq = p.kq + (sc * p.num_k_heads + kh) * kKqHalves;
-            for (int i = tid; i < 4 * kC * (kD / 8); i += 256) {
-                const int a = i / (kC * (kD / 8)), r = (i / (kD / 8)) % kC, c = (i % (kD / 8)) * 8;
-                cp16(Kh + a * kC * LDH + r * LDH + c, kq + (static_cast<size_t>(a) * kC + r) * kD + c, true);
-            }
-            const __half* tp = p.tp + (sc * p.n_vheads + h) * kTpHalves;
-            for (int i = tid; i < 4 * kC * (kC / 8); i += 256) {
-                const int a = i / (kC * (kC / 8)), r = (i / (kC / 8)) % kC, c = (i % (kC / 8)) * 8;
-                cp16(Th + a * kC * LDC + r * LDC + c, tp + (static_cast<size_t>(a) * kC + r) * kC + c, true);
-            }
-            for (int i = tid; i < kC * (kR / 4); i += 256) {
-                const int t = i / (kR / 4), c = (i % (kR / 4)) * 4;
-                const bool ok = static_cast<uint32_t>(t) < nvalid;
-                cp16(Vs + t * kR + c, p.v + (ok ? (tok0 + t) * v_row + h * kD + rb * kR + c : 0), ok);
-            }
-            if (tid < kC / 4)
-                cp16(Gs + 4 * tid, p.gam + (sc * p.n_vheads + h) * kC + 4 * tid, true);
-            if (tid >= 64 && tid < 64 + kC) {
-                const int t = tid - 64;
-                Bs[t] = static_cast<uint32_t>(t) < nvalid ? p.beta[(tok0 + t) * p.n_vheads + h] : 0.f;
-            }
-            cp_commit_wait();
-        }
-        __syncthreads();
+        const int b = ch & 1;
+        const bool more = ch + 1 < p.n_chunks;
+        const uint32_t nvalid = nvalid_of(ch);
+        const size_t tok0 = tok_of(ch);
+        const uint32_t Kh_u = smem_u32(Kb + (2 * b) * kC * LDH), Kl_u = smem_u32(Kb + (2 * b + 1) * kC * LDH);
+        const uint32_t Ph_u = smem_u32(Pb + (2 * b) * kC * LDC), Pl_u = smem_u32(Pb + (2 * b + 1) * kC * LDC);
+        const float* Ge = Gb + b * kGamFloats + kC;       // e^Gamma_t
+        const float* Gd = Gb + b * kGamFloats + 2 * kC;   // e^(Gamma_63 - Gamma_t)
+        const float* Bs = Bb + b * kC;
+        if (more) stage_kp(ch + 1);   // the other buffer: chunk ch - 1 is done with it
 
         // ---- phase A: R1 = K S^T (warps 0-3) and O1 = Q S^T (warps 4-7); m-tile = warp & 3 ----
         const int mt = warp & 3, which = warp >> 2;
@@ -417,7 +470,7 @@ __global__ void __launch_bounds__(256, 1) k_gdn_chunk_state(const ChunkParams p)
         // epilogue A: Rm = beta (V - gamma R1) -> Rm^T hi/lo;  O1 <- gamma O1 (kept in registers)
         {
             const int ta = 16 * mt + g, tb = ta + 8;
-            const float ga = expf(Gs[ta]), gb = expf(Gs[tb]);
+            const float ga = Ge[ta], gb = Ge[tb];
             if (which == 0) {
                 const float ba = Bs[ta], bb = Bs[tb];
 #pragma unroll
@@ -443,6 +496,7 @@ __global__ void __launch_bounds__(256, 1) k_gdn_chunk_state(const ChunkParams p)
             }
         }
         __syncthreads();
+        if (more) stage_qv(ch + 1);   // Q and V of this chunk are consumed
 
         // ---- phase B: U = T Rm, all warps: m-tile = warp & 3, S-row tiles 16 * (warp >> 2) .. +15 ----
         {
@@ -459,7 +513,6 @@ __global__ void __launch_bounds__(256, 1) k_gdn_chunk_state(const ChunkParams p)
                 mma3(u[0], th, tl, bh[0], bh[1], bl[0], bl[1]);
                 mma3(u[1], th, tl, bh[2], bh[3], bl[2], bl[3]);
             }
-            const float glast = Gs[kC - 1];
 #pragma unroll
             for (int n = 0; n < 2; ++n) {
 #pragma unroll
@@ -469,13 +522,14 @@ __global__ void __launch_bounds__(256, 1) k_gdn_chunk_state(const ChunkParams p)
                     split1(u[n][e], hi, lo);
                     Uh[r * LDC + t] = hi;
                     Ul[r * LDC + t] = lo;
-                    split1(u[n][e] * expf(glast - Gs[t]), hi, lo);
+                    split1(u[n][e] * Gd[t], hi, lo);
                     Dh[r * LDC + t] = hi;
                     Dl[r * LDC + t] = lo;
                 }
             }
         }
         __syncthreads();
+        if (more) stage_t(ch + 1);   // T of this chunk is consumed
 
         // ---- phase C1 (warps 4-7): O = gamma O1 + P U, written out / sqrt(hv) ----
         if (which == 1) {
@@ -506,7 +560,7 @@ __global__ void __launch_bounds__(256, 1) k_gdn_chunk_state(const ChunkParams p)
         }
         // ---- phase C2 (all warps): S <- gamma_last S + (decayed U)^T K ----
         {
-            const float gl = expf(Gs[kC - 1]);
+            const float gl = Ge[kC - 1];
 #pragma unroll
             for (int n = 0; n < 4; ++n) {
                 sacc[n][0] *= gl;
@@ -530,7 +584,8 @@ __global__ void __launch_bounds__(256, 1) k_gdn_chunk_state(const ChunkParams p)
             }
         }
         publish_s();
-        __syncthreads();   // everything of this chunk read before the next chunk is staged
+        asm volatile("cp.async.wait_group 0;" ::: "memory");   // chunk ch + 1 staged
+        __syncthreads();
     }
 #pragma unroll
     for (int n = 0; n < 4; ++n) {
@@ -550,7 +605,7 @@ size_t gdn_chunk_scratch_bytes(uint32_t n_seqs, uint32_t T, uint32_t num_k_heads
     const size_t sc = static_cast<size_t>(n_seqs) * n_chunks;
     const size_t kq = sc * num_k_heads * kKqHalves * 2;
     const size_t tp = sc * n_vheads * kTpHalves * 2;
-    const size_t gam = sc * n_vheads * kC * 4;
+    const size_t gam = sc * n_vheads * kGamFloats * 4;
     return kq + tp + gam;
 }
 
