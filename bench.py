@@ -364,6 +364,87 @@ def run_ours(args) -> None:
         dist.destroy_process_group()
 
 
+def run_decode_small(args) -> None:
+    """BASELINE config 1 (Qwen2.5-0.5B shape: one sequence, ctx 512, 24 layers)
+    and config 5c decode (qwen3.5 gated full attention, 32 sequences at ctx
+    4096, one layer).  A step is every layer of the batch through the batched
+    plan, replayed as one CUDA graph (the launches are shorter than the Python
+    call that makes them); L2 is scrubbed between timed steps when the step's
+    KV fits in it.  Weak scaling: each rank serves its own batch."""
+    import torch
+    import torch.distributed as dist
+
+    from yllm_b200 import attn, dist as ydist, fixtures
+    from yllm_b200.configs import CFG1, CFG5_GATED_DECODE
+
+    cfg = CFG1 if args.workload == "config1_decode" else CFG5_GATED_DECODE
+    rank, world, local = ydist.init("nccl" if args.gpus > 1 else "gloo")
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    stream = torch.cuda.current_stream()
+    seqs = list(range(rank * cfg.n_seqs, (rank + 1) * cfg.n_seqs))
+    d = fixtures.decode_inputs(cfg, seqs=seqs, device=dev)
+    torch.cuda.synchronize()
+    plan = attn.DecodePlan.build([c - 1 for c in d.ctx], cfg.n_heads, cfg.n_kv_heads, cfg.head_dim, cfg.kv_dim,
+                                 device=dev)
+    items = [attn.make_items([(d.q[l, i], d.out[l, i], d.k_ptr(l, i), d.v_ptr(l, i),
+                               d.gate[l, i] if d.gate is not None else None, d.ctx[i] - 1)
+                              for i in range(len(seqs))], device=dev) for l in range(d.n_layers)]
+
+    def step():
+        for l in range(d.n_layers):
+            plan.run(items[l])
+
+    kv_bytes = sum(d.ctx) * cfg.kv_dim * 2 * 2 * d.n_layers
+    flush = kv_bytes < (512 << 20)
+    ms, per_call, clk = _timed(step, args, stream, world, dist, local, graph=True, flush_l2=flush)
+    qo_bytes = d.n_layers * len(seqs) * cfg.n_heads * cfg.head_dim * 4 * (3 if cfg.gated else 2)
+    step_bytes = kv_bytes + qo_bytes
+    peaks, src = load_peaks()
+    ach = step_bytes / (per_call / 1e3) / 1e9
+    G = -(-cfg.n_heads // cfg.n_kv_heads)
+    roof = {"bound": "hbm", "achieved": round(ach, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
+            "frac": round(ach / peaks["hbm_gbs"], 4), "traffic": None, "kernel": f"k_decode<{cfg.head_dim},{G}>",
+            "peak_source": src, "bytes_per_step": step_bytes,
+            "note": f"{d.n_layers} launches per step in one graph; achieved = step bytes / step device time"}
+    e2e = None
+    if not args.no_e2e:
+        n_q = d.q.numel()
+        qh = torch.empty(n_q, dtype=torch.float32, pin_memory=True)
+        qh.copy_(d.q.reshape(-1).cpu())
+        oh = torch.empty(n_q, dtype=torch.float32, pin_memory=True)
+
+        def e2e_step():
+            d.q.view(-1).copy_(qh, non_blocking=True)
+            step()
+            oh.copy_(d.out.view(-1), non_blocking=True)
+
+        ems, _, _ = _timed(e2e_step, args, stream, world, dist, local)
+        e2e = {"value": round(len(seqs) * world / (ems / 1e3), 2), "unit": "tok/s",
+               "h2d_bytes_per_step": n_q * 4 * world, "d2h_bytes_per_step": n_q * 4 * world,
+               "path": "DecodePlan.run per layer per step (no graph), pinned host q in, out back"}
+    st = attn.device_status()
+    if st != 0:
+        raise RuntimeError(f"device status {st}: a kernel gave up waiting")
+    if rank == 0:
+        metric = ("attn decode tok/s (Qwen2.5-0.5B shape, 24 layers, ctx 512)" if cfg is CFG1
+                  else "gated attn decode tok/s (qwen3.5 shape, batch 32, ctx 4096)")
+        line = _line(args, world, metric, len(seqs) * world / (ms / 1e3), "tok/s", ms,
+                     {"workload": cfg.name, "n_heads": cfg.n_heads, "n_kv_heads": cfg.n_kv_heads,
+                      "head_dim": cfg.head_dim, "layers": d.n_layers, "n_seqs": len(seqs) * world,
+                      "ctx": cfg.ctx_hi, "gated": cfg.gated, "kv_bytes_per_step": kv_bytes * world,
+                      "parallelism": f"data-parallel x{world}: a batch per GPU, no collective",
+                      "launch": "CUDA graph replay of the step (device-timed value)",
+                      "l2": ("L2 flushed between timed steps (256 MB write outside the step's events)" if flush
+                             else "KV per step larger than L2")},
+                     roof, args.steps * d.n_layers, clk, e2e, scaling="weak")
+        line["dtype"] = "f32 math, fp16 KV" + (", bf16-valued q and gate" if cfg.gated else "")
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
 def run_reference(args) -> None:
     """The reference's own CPU attention for the same workload (rank 0 only)."""
     rank = int(os.environ.get("RANK", "0"))
@@ -705,7 +786,8 @@ def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--workload", default="decode",
-                    choices=["decode", "prefill", "gated_prefill", "gdn_prefill", "gdn_decode", "long_decode"],
+                    choices=["decode", "prefill", "gated_prefill", "gdn_prefill", "gdn_decode", "long_decode",
+                             "config1_decode", "gated_decode"],
                     help="decode = BASELINE config 3 (the default bench line)")
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
@@ -727,6 +809,8 @@ def main() -> None:
         run_prefill(args, gated=args.workload == "gated_prefill")
     elif args.workload in ("gdn_prefill", "gdn_decode"):
         run_gdn(args, decode=args.workload == "gdn_decode")
+    elif args.workload in ("config1_decode", "gated_decode"):
+        run_decode_small(args)
     else:
         run_long_decode(args)
 
