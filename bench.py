@@ -734,7 +734,8 @@ def run_long_decode(args) -> None:
     n = d.ctx[0]
     k0, k1 = ydist.split_range(n, world, rank)
     H, hd = c.n_heads, c.head_dim
-    ex = ydist.PartialExchange(H, hd, device=f"cuda:{local}")
+    peer = world > 1 and args.exchange == "peer"
+    ex = (ydist.PeerExchange if peer else ydist.PartialExchange)(H, hd, device=f"cuda:{local}")
     out = d.out[0, 0]
     kv, vv = d.k_view(0, 0), d.v_view(0, 0)
 
@@ -768,15 +769,20 @@ def run_long_decode(args) -> None:
     ach = nbytes / (ms / 1e3) / 1e9
     roof = {"bound": "hbm", "achieved": round(ach, 1), "peak": peaks["hbm_gbs"] * world, "unit": "GB/s",
             "frac": round(ach / (peaks["hbm_gbs"] * world), 4), "traffic": None,
-            "kernel": "k_decode<128,4> (+ NCCL all-gather + merge at N>1)", "peak_source": src + f" x{world} GPUs"}
+            "kernel": "k_decode<128,4>" + ((" + k_exchange_merge" if peer else " + NCCL all-gather + merge")
+                                           if world > 1 else ""), "peak_source": src + f" x{world} GPUs"}
     if rank == 0:
         print(json.dumps(_line(args, world, "long-context decode GB/s (131072 keys, one layer)", ach, "GB/s", ms,
                                {"workload": c.name, "ctx": n, "n_heads": H, "n_kv_heads": c.n_kv_heads,
                                 "head_dim": hd, "kv_bytes": nbytes,
-                                "parallelism": f"split-KV x{world}, NCCL all-gather of (m,l,o) + LSE merge",
-                                "launch": "CUDA graph replay of the step (partial decode, NCCL, merge)",
+                                "parallelism": (f"split-KV x{world}, " + (
+                                    "(m,l,o) pushed into every GPU over NVLink + LSE merge, one kernel"
+                                    if peer else "NCCL all-gather of (m,l,o) + LSE merge")),
+                                "launch": "CUDA graph replay of the step (partial decode, exchange, merge)",
                                 "l2": "KV 537 MB > L2"},
                                roof, args.steps, clk, e2e)), flush=True)
+    if peer:
+        ex.close()
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
@@ -797,6 +803,8 @@ def main() -> None:
     ap.add_argument("--seqs", type=int, default=0, help="profiling only: first N sequences")
     ap.add_argument("--layers", type=int, default=0, help="profiling only: first L layers")
     ap.add_argument("--cpu-budget", type=float, default=20.0, help="seconds of CPU attention in the baseline")
+    ap.add_argument("--exchange", choices=["peer", "nccl"], default="peer",
+                    help="long_decode at N>1: split-KV exchange over peer memory (one kernel) or NCCL all-gather")
     args = ap.parse_args()
     if args.warmup < 3:
         log("warmup raised to 3 (timing rule)")

@@ -173,6 +173,30 @@ int yattn_merge_partials_packed(float* out, const float* parts, uint32_t n_parts
                                 uint32_t n_heads, uint32_t head_dim, const float* gate,
                                 void* stream, char* err, size_t errlen);
 
+/* ---- split-KV exchange over peer memory (long-context decode on 1..8 GPUs) ----
+ * One process per GPU.  Each rank allocates a receive area
+ * (yattn_exchange_area_alloc: cudaMalloc'd, zeroed) and maps every peer's area
+ * through CUDA IPC (yattn_ipc_handle on the owner, 64-byte handles passed by
+ * the caller's own transport, yattn_ipc_open on the others).
+ * yattn_exchange_merge, after yattn_decode_partial wrote this rank's (ml, o):
+ * stores them into every rank's area over NVLink (stores only, no peer loads),
+ * raises this rank's per-head flags there (release, system scope), waits
+ * (bounded; a timeout sets yattn_device_status 401) for every rank's flags in
+ * the local area and merges all parts into out[n_heads*head_dim] (x sigmoid(gate)
+ * if gate).  areas[r] is rank r's area as mapped in this process; areas[rank]
+ * is the local one.  All ranks must make the same sequence of calls.  No
+ * reference counterpart: the reference has no multi-GPU attention. */
+size_t yattn_exchange_area_bytes(uint32_t world, uint32_t n_heads, uint32_t head_dim);
+int yattn_exchange_area_alloc(uint32_t world, uint32_t n_heads, uint32_t head_dim, void** area_out,
+                              char* err, size_t errlen);
+int yattn_exchange_area_free(void* area, char* err, size_t errlen);
+int yattn_ipc_handle(const void* area, void* handle_out /* 64 bytes */, char* err, size_t errlen);
+int yattn_ipc_open(const void* handle /* 64 bytes */, void** ptr_out, char* err, size_t errlen);
+int yattn_ipc_close(void* ptr, char* err, size_t errlen);
+int yattn_exchange_merge(const float* ml, const float* o, void* const* areas, uint32_t world,
+                         uint32_t rank, uint32_t n_heads, uint32_t head_dim, float* out,
+                         const float* gate, void* stream, char* err, size_t errlen);
+
 /* Error-returning form of cuda_k_attn_decode with an explicit stream and gate. */
 int yattn_attn_decode(float* att_out, const float* q, const uint16_t* kcache,
                       const uint16_t* vcache, const float* gate, uint32_t pos,

@@ -1,0 +1,130 @@
+"""Split-KV exchange over peer memory (yattn_exchange_merge), on one GPU and on
+two.  Long-context decode splits one query's keys over the GPUs; each GPU's
+(m, l, o) partial is stored into every GPU's receive area and each GPU merges
+all parts (log-sum-exp) -- compared here with the whole-range decode and the
+CPU oracle (engine.c:1074-1096).  Tolerance oracle.REL_TOL (2e-3)."""
+import datetime
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+import oracle
+
+pytestmark = pytest.mark.gpu
+
+H, KV, HD = 32, 8, 128
+
+
+def _case(seed, T):
+    rng = np.random.default_rng(seed)
+    kd = KV * HD
+    q = rng.standard_normal(H * HD).astype(np.float32)
+    k = oracle.f32_to_f16(rng.standard_normal(T * kd).astype(np.float32))
+    v = oracle.f32_to_f16(rng.standard_normal(T * kd).astype(np.float32))
+    return q, k, v, kd
+
+
+def _to_dev(dev, q, k, v):
+    tq = torch.from_numpy(q).to(dev)
+    tk = torch.from_numpy(k.view(np.int16)).to(dev).view(torch.uint16)
+    tv = torch.from_numpy(v.view(np.int16)).to(dev).view(torch.uint16)
+    return tq, tk, tv
+
+
+def test_exchange_single_rank_repeats_and_graph_replays():
+    """world = 1: the push lands in the rank's own area; the device epoch
+    advances on every launch, so eager calls and graph replays all merge."""
+    from yllm_b200 import attn
+    from yllm_b200.dist import PeerExchange
+
+    assert torch.cuda.is_available(), "GPU tests need a CUDA device"
+    dev = torch.device("cuda:0")
+    torch.cuda.set_device(dev)
+    T = 9000
+    q, k, v, kd = _case(11, T)
+    tq, tk, tv = _to_dev(dev, q, k, v)
+    want = oracle.attn_decode(q, k, v, T - 1, H, KV, HD, kd)
+    ex = PeerExchange(H, HD, device=dev)
+    try:
+        outs = []
+        for _ in range(3):
+            out = torch.full((H * HD,), float("nan"), device=dev)
+            attn.decode_partial(ex.ml, ex.o, tq, tk, tv, 0, T, H, KV, HD, kd)
+            ex.run(out)
+            outs.append(out)
+        torch.cuda.synchronize()
+        for out in outs:
+            oracle.assert_close(out.cpu().numpy(), want, what="exchange world 1")
+        out_g = torch.full((H * HD,), float("nan"), device=dev)
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=s):
+            attn.decode_partial(ex.ml, ex.o, tq, tk, tv, 0, T, H, KV, HD, kd)
+            ex.run(out_g)
+        for _ in range(3):
+            out_g.fill_(float("nan"))
+            g.replay()
+            torch.cuda.synchronize()
+            oracle.assert_close(out_g.cpu().numpy(), want, what="exchange world 1, graph replay")
+        del g
+        assert attn.device_status() == 0
+    finally:
+        ex.close()
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    return port
+
+
+def _worker(rank, world, port, T, ret):
+    import torch.distributed as dist
+
+    from yllm_b200 import attn
+    from yllm_b200.dist import PeerExchange, split_range
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dev = torch.device("cuda", rank)
+    torch.cuda.set_device(dev)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
+                            device_id=dev)
+    q, k, v, kd = _case(12, T)
+    tq, tk, tv = _to_dev(dev, q, k, v)
+    full = torch.zeros(H * HD, device=dev)
+    attn.attn_decode(full, tq, tk, tv, T - 1, H, KV, HD, kd)
+    ex = PeerExchange(H, HD, device=dev)
+    worst = 0.0
+    k0, k1 = split_range(T, world, rank)
+    for _ in range(4):
+        out = torch.full((H * HD,), float("nan"), device=dev)
+        attn.decode_partial(ex.ml, ex.o, tq, tk, tv, k0, k1, H, KV, HD, kd)
+        ex.run(out)
+        torch.cuda.synchronize()
+        worst = max(worst, oracle.rel_err(out.cpu().numpy(), full.cpu().numpy()))
+    ret[rank] = (worst, attn.device_status())
+    ex.close()
+    dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_exchange_two_ranks_matches_whole_range():
+    ctx = mp.get_context("spawn")
+    ret = ctx.Manager().dict()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, 20001, ret)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(180)
+        assert p.exitcode == 0
+    for r in range(2):
+        err, status = ret[r]
+        assert status == 0 and err <= oracle.REL_TOL, (r, err, status)

@@ -84,6 +84,13 @@ PROTOS = {
     "yattn_decode_partial": (C.c_int, [vp, vp, vp, vp, vp, u32, u32, u32, u32, u32, u32, vp, sz, vp, *E]),
     "yattn_merge_partials": (C.c_int, [vp, vp, vp, u32, u32, u32, vp, vp, *E]),
     "yattn_merge_partials_packed": (C.c_int, [vp, vp, u32, u32, u32, vp, vp, *E]),
+    "yattn_exchange_area_bytes": (sz, [u32, u32, u32]),
+    "yattn_exchange_area_alloc": (C.c_int, [u32, u32, u32, C.POINTER(vp), *E]),
+    "yattn_exchange_area_free": (C.c_int, [vp, *E]),
+    "yattn_ipc_handle": (C.c_int, [vp, vp, *E]),
+    "yattn_ipc_open": (C.c_int, [vp, C.POINTER(vp), *E]),
+    "yattn_ipc_close": (C.c_int, [vp, *E]),
+    "yattn_exchange_merge": (C.c_int, [vp, vp, vp, u32, u32, u32, u32, vp, vp, vp, *E]),
     "yattn_attn_decode": (C.c_int, [vp, vp, vp, vp, vp, u32, u32, u32, u32, u32, vp, *E]),
     "yattn_attn_decode_noalloc": (C.c_int, [vp, vp, vp, vp, vp, u32, u32, u32, u32, u32, vp, *E]),
     "yattn_reserve": (C.c_int, [sz, *E]),

@@ -51,6 +51,7 @@ enum : int {
     ST_DECODE_EMPTY_TIMEOUT = 102,
     ST_PREFILL_TIMEOUT = 201,
     ST_GDN_TIMEOUT = 301,
+    ST_EXCHANGE_TIMEOUT = 401,
 };
 
 // Upper bound of any spin in these kernels (ns of %globaltimer).  Far above

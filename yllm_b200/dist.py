@@ -168,3 +168,73 @@ class PartialExchange:
             attn.merge_partials_packed(out, self.parts, self.world, self.n_heads, self.head_dim, gate)
         else:
             attn.merge_partials_packed(out, self.payload, 1, self.n_heads, self.head_dim, gate)
+
+
+class PeerExchange:
+    """Split-KV exchange over peer memory: the one-kernel alternative to
+    PartialExchange's NCCL all-gather.
+
+    Every rank owns a receive area (library cudaMalloc) and maps all peers'
+    areas through CUDA IPC; the 64-byte handles travel over the process
+    group (all_gather_object).  run() launches yattn_exchange_merge: this
+    rank's (ml, o) go into every rank's area over NVLink (stores only), each
+    rank waits for all parts in its own memory and merges them.  The epoch
+    that pairs the ranks' calls lives on the device, so a step including
+    run() can be captured in a CUDA graph.  Every rank must make the same
+    sequence of run() calls; close() (collective) unmaps and frees."""
+
+    def __init__(self, n_heads: int, head_dim: int, device, group=None):
+        import ctypes as C
+
+        from ._lib import call, lib
+
+        self.group = group
+        self.world = dist.get_world_size(group) if dist.is_initialized() else 1
+        self.rank = dist.get_rank(group) if dist.is_initialized() else 0
+        self.n_heads, self.head_dim = n_heads, head_dim
+        n = n_heads * (2 + head_dim)
+        self.payload = torch.zeros(n, dtype=torch.float32, device=device)
+        self.ml = self.payload[:n_heads * 2].view(n_heads, 2)
+        self.o = self.payload[n_heads * 2:].view(n_heads, head_dim)
+        area = C.c_void_p()
+        call("yattn_exchange_area_alloc", self.world, n_heads, head_dim, C.byref(area))
+        self.area = area.value
+        handle = (C.c_uint8 * 64)()
+        call("yattn_ipc_handle", self.area, handle)
+        handles = [None] * self.world
+        if self.world > 1:
+            dist.all_gather_object(handles, bytes(handle), group=group)
+        else:
+            handles = [bytes(handle)]
+        self.peers = []
+        for r, hb in enumerate(handles):
+            if r == self.rank:
+                self.peers.append(self.area)
+                continue
+            ptr = C.c_void_p()
+            call("yattn_ipc_open", (C.c_uint8 * 64).from_buffer_copy(hb), C.byref(ptr))
+            self.peers.append(ptr.value)
+        self._areas = (C.c_void_p * self.world)(*self.peers)
+        self._lib = lib
+
+    def run(self, out: torch.Tensor, gate: Optional[torch.Tensor] = None) -> None:
+        from ._lib import call
+
+        call("yattn_exchange_merge", self.payload.data_ptr(), self.payload.data_ptr() + self.n_heads * 2 * 4,
+             self._areas, self.world, self.rank, self.n_heads, self.head_dim, out.data_ptr(),
+             gate.data_ptr() if gate is not None else None, torch.cuda.current_stream().cuda_stream)
+
+    def close(self) -> None:
+        """Collective: every rank's pushes are done before any area is unmapped or freed."""
+        from ._lib import call
+
+        torch.cuda.synchronize()
+        if self.world > 1:
+            dist.barrier(group=self.group)
+        for r, ptr in enumerate(self.peers):
+            if r != self.rank:
+                call("yattn_ipc_close", ptr)
+        if self.world > 1:
+            dist.barrier(group=self.group)
+        call("yattn_exchange_area_free", self.area)
+        self.peers = []
