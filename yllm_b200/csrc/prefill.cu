@@ -7,7 +7,9 @@
 // hh*n_kv/n_heads; out has q's layout.  Optional qwen35 sigmoid output gate
 // (engine.c:958-960).
 //
-// One CTA = one (query head, 128-row query tile), heaviest tiles first.  Warps:
+// One CTA = one (query head, 128-row query tile), heaviest tiles first (with
+// two CTAs per SM the 1-D grid would instead pair the heaviest tiles with the
+// lightest).  Warps:
 //   0-3  softmax: thread i owns query row i = TMEM lane i.  Loads the fp32 Q
 //        tile once (-> fp16, SWIZZLE_128B K-major in smem).  Per key block it
 //        reads S from TMEM, applies the causal mask (diagonal blocks only) and
@@ -17,15 +19,17 @@
 //        (P_lo = fp16(p - P_hi), ~22 bits instead of fp16's 11).
 //   4    TMA for K blocks, 6 TMA for V blocks: separate rings, no multicast.
 //   5    MMA: one thread issues S(j) = Q K(j)^T (A, B from smem) into a ring of
-//        three TMEM S buffers and O += P_hi V + P_lo V with A = P read straight
-//        from TMEM (B = V from smem).  S runs up to three blocks ahead of the
-//        softmax; the tensor core runs its MMAs in issue order, so S(j+3)
-//        cannot overwrite P(j) before PV(j) has read it.
+//        NSB TMEM S buffers (2 at head_dim <= 128, 3 at 256) and O += P_hi V +
+//        P_lo V with A = P read straight from TMEM (B = V from smem).  S runs up
+//        to NSB blocks ahead of the softmax; the tensor core runs its MMAs in
+//        issue order, so S(j+NSB) cannot overwrite P(j) before PV(j) has read it.
 // Keys past the end of the cache are zero-filled by TMA and masked.
 #include "common.cuh"
 #include "tcgen05.cuh"
 
 #include <cudaTypedefs.h>
+
+#include <algorithm>
 
 namespace yattn {
 namespace {
@@ -33,24 +37,33 @@ namespace {
 constexpr int BM = 128;
 constexpr int kPThreads = 224;
 
+// One CTA per SM: 128-key blocks (64 at head_dim 256), three TMEM S buffers, all
+// 512 columns.  DUAL (two CTAs per SM: 64-key blocks, two S buffers, 256 columns
+// each) overlaps one CTA's prologue with the other's key loop, but measured slower
+// on config 2 (320 vs 365 TFLOP/s): its N = 64 QK products are bound by
+// shared-memory operand bandwidth and the two CTAs share one tensor pipe.
 template <int HD> struct PCfg {
-    static constexpr int BN = (HD >= 256) ? 64 : 128;
-    static constexpr int KST = (HD >= 256) ? 2 : 3;         // K and V ring depth
+    static constexpr bool DUAL = false;
+    static constexpr int MIN_BLOCKS = DUAL ? 2 : 1;
+    static constexpr int BN = (DUAL || HD >= 256) ? 64 : 128;
+    static constexpr int KST = DUAL ? ((HD >= 128) ? 2 : 3) : ((HD >= 256) ? 2 : 3);   // K and V ring depth
     static constexpr int Q_BYTES = BM * HD * 2;
     static constexpr int KV_BYTES = BN * HD * 2;            // one K (or V) block
     static constexpr int OFF_Q = 0;
     static constexpr int OFF_K = OFF_Q + Q_BYTES;
     static constexpr int OFF_V = OFF_K + KST * KV_BYTES;
     static constexpr int OFF_BAR = OFF_V + KST * KV_BYTES;
-    // + barriers, + alignment slack; at least 116 KB so one CTA (holding all 512 TMEM columns) runs per SM
-    static constexpr int SMEM = (OFF_BAR + 256 + 1024) > 118784 ? (OFF_BAR + 256 + 1024) : 118784;
-    static constexpr uint32_t TMEM_COLS = 512;
-    static constexpr int NSB = 3;                            // S buffers in TMEM (P is written over its S)
+    // + barriers, + alignment slack; floors keep at most MIN_BLOCKS CTAs (each holding
+    // TMEM_COLS columns) resident per SM
+    static constexpr int SMEM_FLOOR = DUAL ? 78 * 1024 : 116 * 1024;
+    static constexpr int SMEM = (OFF_BAR + 256 + 1024) > SMEM_FLOOR ? (OFF_BAR + 256 + 1024) : SMEM_FLOOR;
+    static constexpr uint32_t TMEM_COLS = DUAL ? 256 : 512;
+    static constexpr int NSB = DUAL ? 2 : 3;                 // S buffers in TMEM (P is written over its S)
     static constexpr uint32_t COL_S = 0;                     // S buffer b at [b*BN, (b+1)*BN)
     static constexpr uint32_t COL_O = NSB * BN;
     static constexpr uint32_t P_COLS = BN / 2;               // one fp16 P plane, two values per column
-    static_assert(NSB * BN + HD <= 512, "TMEM columns");
-    static_assert(SMEM <= 232448, "shared memory");
+    static_assert(NSB * BN + HD <= static_cast<int>(TMEM_COLS), "TMEM columns");
+    static_assert(MIN_BLOCKS * SMEM <= 232448, "shared memory");
 };
 
 struct PrefillParams {
@@ -58,6 +71,9 @@ struct PrefillParams {
     float* out;
     const float* gate;
     uint32_t q_stride, pos_start, B, n_heads, n_kv;
+    uint32_t n_qt;                    // 128-row query tiles
+    uint32_t heavy;                   // grid order: the first `heavy` CTAs take the heaviest tiles, the rest the
+                                      // lightest first (pairs heavy and light tiles on an SM)
     float scale_log2;
     int* status;
 };
@@ -100,7 +116,7 @@ __device__ __forceinline__ void produce(const CUtensorMap* map, uint8_t* ring, u
 __device__ __forceinline__ uint32_t h2_bits(__half2 h) { return *reinterpret_cast<uint32_t*>(&h); }
 
 template <int HD>
-__global__ void __launch_bounds__(kPThreads, 1)
+__global__ void __launch_bounds__(kPThreads, PCfg<HD>::MIN_BLOCKS)
     k_prefill(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV, const PrefillParams p) {
     using C = PCfg<HD>;
     constexpr int BN = C::BN;
@@ -115,8 +131,11 @@ __global__ void __launch_bounds__(kPThreads, 1)
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
-    const uint32_t hh = blockIdx.x;
-    const uint32_t qt = gridDim.y - 1 - blockIdx.y;          // heaviest tiles first
+    // tile rank k in size order (heaviest first): k = blockIdx.x for the first `heavy` CTAs,
+    // then the lightest tiles first
+    const uint32_t k = blockIdx.x < p.heavy ? blockIdx.x : gridDim.x - 1 - (blockIdx.x - p.heavy);
+    const uint32_t hh = k % p.n_heads;
+    const uint32_t qt = p.n_qt - 1 - k / p.n_heads;
     const uint32_t kvh = hh * p.n_kv / p.n_heads;
     const uint32_t row0 = qt * BM;
     const uint32_t rows_valid = min(static_cast<uint32_t>(BM), p.B - row0);
@@ -292,20 +311,20 @@ __global__ void __launch_bounds__(kPThreads, 1)
             // ---- p = 2^(s*scale - m): one FFMA + ex2 per element; P hi/lo into TMEM ----
             float rs4[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-            for (int c = 0; c < BN / 64; ++c) {
-                uint32_t hi[32], lo[32];
+            for (int c = 0; c < BN / 32; ++c) {   // 32 keys -> 16 packed columns per plane
+                uint32_t hi[16], lo[16];
 #pragma unroll
-                for (int i = 0; i < 32; ++i) {
-                    const float a = ex2_approx(fmaf(sv[c * 64 + 2 * i], sl2, -m_use));
-                    const float b = ex2_approx(fmaf(sv[c * 64 + 2 * i + 1], sl2, -m_use));
+                for (int i = 0; i < 16; ++i) {
+                    const float a = ex2_approx(fmaf(sv[c * 32 + 2 * i], sl2, -m_use));
+                    const float b = ex2_approx(fmaf(sv[c * 32 + 2 * i + 1], sl2, -m_use));
                     rs4[i & 3] += a + b;
                     const __half2 h = __floats2half2_rn(a, b);
                     const float2 hf = __half22float2(h);
                     hi[i] = h2_bits(h);
                     lo[i] = h2_bits(__floats2half2_rn(a - hf.x, b - hf.y));
                 }
-                tmem_st32(scol + c * 32, hi);
-                tmem_st32(scol + C::P_COLS + c * 32, lo);
+                tmem_st16(scol + c * 16, hi);
+                tmem_st16(scol + C::P_COLS + c * 16, lo);
             }
             l_run = l_run * alpha + ((rs4[0] + rs4[1]) + (rs4[2] + rs4[3]));
             m_run = m_use;
@@ -423,8 +442,12 @@ int launch_prefill(const CUtensorMap& mk, const CUtensorMap& mv, const PrefillPa
         }
         attr_done[dev] = true;
     }
-    dim3 grid(p.n_heads, n_qtiles);
-    k_prefill<HD><<<grid, kPThreads, C::SMEM, st>>>(mk, mv, p);
+    PrefillParams q = p;
+    const uint32_t n_tiles = p.n_heads * n_qtiles;
+    const uint32_t sms = static_cast<uint32_t>(dev_num_sms());
+    q.n_qt = n_qtiles;
+    q.heavy = (C::DUAL && n_tiles <= 2 * sms) ? std::min(n_tiles, sms) : n_tiles;
+    k_prefill<HD><<<n_tiles, kPThreads, C::SMEM, st>>>(mk, mv, q);
     YATTN_CHECK_LAUNCH(err, errlen, "prefill");
     return 0;
 }
@@ -467,7 +490,7 @@ int prefill(float* out, const float* q, const uint16_t* kc, const uint16_t* vc, 
     DevCtx* ctx = dev_ctx(err, errlen);
     if (!ctx) return -1;
     const uint32_t n_keys = pos_start + B;
-    const uint32_t bn = (hd >= 256) ? 64u : 128u;
+    const uint32_t bn = hd == 64 ? PCfg<64>::BN : hd == 128 ? PCfg<128>::BN : PCfg<256>::BN;   // key block
     CUtensorMap mk, mv;
     if (make_kv_map(&mk, kc, kv_dim, n_keys, bn, err, errlen) || make_kv_map(&mv, vc, kv_dim, n_keys, bn, err, errlen))
         return -1;
