@@ -228,8 +228,9 @@ def run_ours(args) -> None:
 
     d = fixtures.decode_inputs(cfg, layers=list(range(n_layers)), seqs=seqs, device=dev)
     torch.cuda.synchronize()
+    # every sequence's KV lives in one pool: the pooled plan streams it with tensor copies
     plan = attn.DecodePlan.build([c - 1 for c in d.ctx], cfg.n_heads, cfg.n_kv_heads, cfg.head_dim, cfg.kv_dim,
-                                 device=dev)
+                                 device=dev, pool=(d.kv_pool.data_ptr(), d.kv_pool.numel() * 2))
     items = [attn.make_items([(d.q[l, i], d.out[l, i], d.k_ptr(l, i), d.v_ptr(l, i), None, d.ctx[i] - 1)
                               for i in range(len(seqs))], device=dev) for l in range(n_layers)]
     stream = torch.cuda.current_stream()
@@ -350,7 +351,7 @@ def run_ours(args) -> None:
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"],
                          "unit": "GB/s", "frac": round(achieved / peaks["hbm_gbs"], 4),
                          "traffic": None if (args.seqs or args.layers) else NCU_TRAFFIC["decode"],
-                         "kernel": "k_decode<128,4>", "peak_source": peak_src,
+                         "kernel": "k_decode<128,4,TM> (pooled tensor copies)", "peak_source": peak_src,
                          "bytes_per_launch": bytes_per_launch, "launch_ms": round(launch_ms, 5)},
             "gpu_launches": args.steps * n_layers,
             "clocks": {"sm_mhz": clk["sm_mhz"], "sm_max_mhz": clk["sm_max_mhz"], "reasons": clk["reasons"],
@@ -386,7 +387,7 @@ def run_decode_small(args) -> None:
     d = fixtures.decode_inputs(cfg, seqs=seqs, device=dev)
     torch.cuda.synchronize()
     plan = attn.DecodePlan.build([c - 1 for c in d.ctx], cfg.n_heads, cfg.n_kv_heads, cfg.head_dim, cfg.kv_dim,
-                                 device=dev)
+                                 device=dev, pool=(d.kv_pool.data_ptr(), d.kv_pool.numel() * 2))
     items = [attn.make_items([(d.q[l, i], d.out[l, i], d.k_ptr(l, i), d.v_ptr(l, i),
                                d.gate[l, i] if d.gate is not None else None, d.ctx[i] - 1)
                               for i in range(len(seqs))], device=dev) for l in range(d.n_layers)]

@@ -145,6 +145,24 @@ int yattn_decode_run(const YattnDecodeItem* items_dev, const YattnDecodeWork* wo
                      uint32_t n_heads, uint32_t n_kv_heads, uint32_t head_dim, uint32_t kv_dim,
                      void* workspace, size_t ws_bytes, void* stream, char* err, size_t errlen);
 
+/* Pooled variants: every item's K and V rows lie in one allocation
+ * [pool, pool + pool_bytes) with row stride kv_dim (the engine's per-sequence
+ * blobs carved from one pool).  One 2-D tensor map covers the pool, so K and V
+ * stream through tensor copies of 8-16 KB (64 dims x one stage of tokens,
+ * 128-byte swizzle) instead of one copy per row -- the faster path.  A pooled
+ * run needs a plan from yattn_decode_plan_pooled (one kv head per CTA); the
+ * work array, workspace sizing and item layout are as above. */
+int yattn_decode_plan_pooled(const uint32_t* pos_host, uint32_t n_items, uint32_t n_kv_heads,
+                             uint32_t head_dim, uint32_t split_tokens, uint32_t target_ctas,
+                             YattnDecodeWork* work_host, uint32_t work_cap,
+                             uint32_t* n_work, uint32_t* n_parts, uint32_t* n_groups,
+                             char* err, size_t errlen);
+int yattn_decode_run_pooled(const YattnDecodeItem* items_dev, const YattnDecodeWork* work_dev,
+                            uint32_t n_work, uint32_t n_parts, uint32_t n_groups,
+                            uint32_t n_heads, uint32_t n_kv_heads, uint32_t head_dim, uint32_t kv_dim,
+                            const void* pool, size_t pool_bytes,
+                            void* workspace, size_t ws_bytes, void* stream, char* err, size_t errlen);
+
 /* Split-KV partials without the final merge (long-context decode sharded over
  * GPUs).  Keys [t_begin, t_end) of one layer; writes per query head
  * ml[2*hh] = (m, l) and o[hh*head_dim ..] = unnormalised sum, where

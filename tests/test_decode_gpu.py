@@ -163,7 +163,12 @@ def test_decode_config1_all_layers(dev):
         oracle.assert_close(d.out[layer, 0].cpu().numpy(), want, what=f"config1 layer {layer}")
 
 
-def test_decode_config3_batched_plan(dev):
+def _pool(d):
+    return (d.kv_pool.data_ptr(), d.kv_pool.numel() * d.kv_pool.element_size())
+
+
+@pytest.mark.parametrize("pooled", [False, True])
+def test_decode_config3_batched_plan(dev, pooled):
     from yllm_b200 import attn, fixtures
     from yllm_b200.configs import CFG3 as c
 
@@ -171,7 +176,8 @@ def test_decode_config3_batched_plan(dev):
     seqs = sorted(set([int(np.argmin(ctx)), int(np.argmax(ctx)), 0, 1, 2, 31, 63]))
     layers = [0, 31]
     d = fixtures.decode_inputs(c, layers=layers, seqs=seqs, device=dev)
-    plan = attn.DecodePlan.build([x - 1 for x in d.ctx], c.n_heads, c.n_kv_heads, c.head_dim, c.kv_dim)
+    plan = attn.DecodePlan.build([x - 1 for x in d.ctx], c.n_heads, c.n_kv_heads, c.head_dim, c.kv_dim,
+                                 pool=_pool(d) if pooled else None)
     for li in range(len(layers)):
         items = attn.make_items([(d.q[li, si], d.out[li, si], d.k_ptr(li, si), d.v_ptr(li, si), None,
                                   d.ctx[si] - 1) for si in range(len(seqs))])
@@ -199,13 +205,15 @@ def test_decode_config4_long_context(dev):
     oracle.assert_close(d.out[0, 0].cpu().numpy(), want, what="config4")
 
 
-def test_gated_decode_qwen35(dev):
+@pytest.mark.parametrize("pooled", [False, True])
+def test_gated_decode_qwen35(dev, pooled):
     from yllm_b200 import attn, fixtures
     from yllm_b200.configs import CFG5_GATED_DECODE as c
 
     seqs = [0, 7, 31]
     d = fixtures.decode_inputs(c, seqs=seqs, device=dev)
-    plan = attn.DecodePlan.build([x - 1 for x in d.ctx], c.n_heads, c.n_kv_heads, c.head_dim, c.kv_dim)
+    plan = attn.DecodePlan.build([x - 1 for x in d.ctx], c.n_heads, c.n_kv_heads, c.head_dim, c.kv_dim,
+                                 pool=_pool(d) if pooled else None)
     items = attn.make_items([(d.q[0, si], d.out[0, si], d.k_ptr(0, si), d.v_ptr(0, si), d.gate[0, si],
                               d.ctx[si] - 1) for si in range(len(seqs))])
     plan.run(items)
@@ -215,6 +223,40 @@ def test_gated_decode_qwen35(dev):
         want = oracle.attn_decode(f["q"], f["k"], f["v"], f["pos"], c.n_heads, c.n_kv_heads, c.head_dim, c.kv_dim,
                                   gate=f["gate"])
         oracle.assert_close(d.out[0, si].cpu().numpy(), want, what=f"gated decode seq {s}")
+
+
+@pytest.mark.parametrize("H,KV,hd,ctxs", [
+    (32, 8, 128, [1, 17, 128, 129, 2000, 5000]), (14, 2, 64, [512, 1, 300, 3000]),
+    (16, 2, 256, [4096, 63, 64, 65]), (8, 1, 128, [9000, 5]), (24, 3, 64, [777, 1200]),
+])
+def test_pooled_batched_decode_ragged(dev, H, KV, hd, ctxs):
+    """yattn_decode_run_pooled: items' K and V at arbitrary row offsets of one
+    pool (tensor-copy kernels, one kv head per CTA) against the oracle."""
+    from yllm_b200 import attn
+
+    rng = np.random.default_rng(H * 7 + hd + len(ctxs))
+    kd = KV * hd
+    offs, rows = [], 3                      # leading rows belong to nobody
+    for c in ctxs:
+        offs.append(rows)
+        rows += 2 * c + 5                   # K rows, V rows, a gap
+    pool_np = oracle.f32_to_f16(rng.standard_normal(rows * kd).astype(np.float32)).reshape(rows, kd)
+    pool = torch.from_numpy(pool_np.view(np.int16)).to(dev).view(torch.uint16)
+    base = pool.data_ptr()
+    qs = [rng.standard_normal(H * hd).astype(np.float32) for _ in ctxs]
+    tq = [torch.from_numpy(q).to(dev) for q in qs]
+    outs = [torch.full((H * hd,), float("nan"), device=dev) for _ in ctxs]
+    plan = attn.DecodePlan.build([c - 1 for c in ctxs], H, KV, hd, kd, pool=(base, pool.numel() * 2))
+    items = attn.make_items([(tq[i], outs[i], base + offs[i] * kd * 2, base + (offs[i] + c) * kd * 2, None, c - 1)
+                             for i, c in enumerate(ctxs)])
+    plan.run(items)
+    torch.cuda.synchronize()
+    for i, c in enumerate(ctxs):
+        k = np.ascontiguousarray(pool_np[offs[i]:offs[i] + c]).reshape(-1)
+        v = np.ascontiguousarray(pool_np[offs[i] + c:offs[i] + 2 * c]).reshape(-1)
+        want = oracle.attn_decode(qs[i], k, v, c - 1, H, KV, hd, kd)
+        oracle.assert_close(outs[i].cpu().numpy(), want, what=f"pooled H{H} KV{KV} hd{hd} ctx{c}")
+    assert attn.device_status() == 0
 
 
 def test_split_partials_merge_to_full(dev):

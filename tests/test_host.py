@@ -136,6 +136,33 @@ def test_balanced_plan_evens_out_ctas(target):
         assert all(w.t_end - w.t_begin >= 128 or len(segs) == 1 for w in segs)
 
 
+@pytest.mark.parametrize("pooled", [False, True])
+def test_balanced_plan_cta_numbers_dense(pooled):
+    """Every CTA number 0..n-1 carries at least one unit (the run launches one
+    CTA per unit, so a gap would leave units unrun), for ragged random batches."""
+    from yllm_b200._lib import YattnDecodeWork, lib
+
+    rng = np.random.default_rng(7)
+    fn = lib.yattn_decode_plan_pooled if pooled else lib.yattn_decode_plan
+    for trial in range(300):
+        n = int(rng.integers(1, 40))
+        pos = rng.integers(0, int(rng.choice([300, 5000, 40000])), size=n).astype(np.uint32)
+        n_kv, hd = [(8, 128), (2, 256), (2, 64), (4, 128), (1, 128)][trial % 5]
+        target = int(rng.choice([148, 37, 296]))
+        cap = 200000
+        work = (YattnDecodeWork * cap)()
+        nw, npart, ng = C.c_uint32(), C.c_uint32(), C.c_uint32()
+        err = C.create_string_buffer(256)
+        rc = fn(pos.ctypes.data_as(C.POINTER(C.c_uint32)), n, n_kv, hd, 0, target, work, cap, C.byref(nw),
+                C.byref(npart), C.byref(ng), err, 256)
+        assert rc == 0, err.value
+        ctas = [work[i].cta for i in range(nw.value)]
+        assert ctas == sorted(ctas) and set(ctas) == set(range(ctas[-1] + 1)), (trial, n, n_kv, hd, target)
+        assert ctas[-1] + 1 <= nw.value                      # one CTA per unit is launched
+        if int(pos.astype(np.int64).sum()) >= 256 * target:   # enough work: one wave
+            assert ctas[-1] + 1 <= target
+
+
 def test_plan_rejects_bad_args():
     from yllm_b200._lib import YattnDecodeWork, lib
 

@@ -62,14 +62,30 @@ def test_noalloc_decode_matches_allocating_entry(H, KV, hd, T, gated):
         oracle.assert_close(out.cpu().numpy(), want, what=f"noalloc H{H} KV{KV} hd{hd} T{T}")
 
 
-def test_noalloc_rejects_scratch_overflow():
-    from yllm_b200._lib import YattnError
+def test_noalloc_scratch_covers_every_geometry():
+    """The plan keeps a query's split partials to about one wave of CTAs, so the
+    4 MiB static scratch (minus its 256-byte header) holds them for every
+    supported geometry -- head_dim up to 256, up to 8 query heads per kv head,
+    any context length; the entry still rejects a larger need with -1.  The
+    longest case also runs against the allocating entry."""
+    from yllm_b200._lib import lib
+
+    worst = 0
+    for hd in (64, 128, 256):
+        for kv in (1, 2, 4, 8, 16, 64):
+            for T in (1, 1000, 32768, 1 << 20, 1 << 22):
+                need = lib.yattn_decode_partial_workspace_bytes(T, 8 * kv, kv, hd)
+                worst = max(worst, need)
+    assert 0 < worst <= (4 << 20) - 256, worst
+
+    from yllm_b200 import attn
 
     dev = torch.device("cuda:0")
-    # head_dim 256, 8 query heads per kv head, 8 kv heads: ~74 splits x 8 heads of 8 KB partials > 4 MiB
-    H, KV, hd, T = 64, 8, 256, 32768
-    q = torch.zeros(H * hd, device=dev)
-    k = torch.zeros(T * KV * hd, dtype=torch.uint16, device=dev)
-    out = torch.zeros(H * hd, device=dev)
-    with pytest.raises(YattnError, match="static scratch"):
-        _noalloc(out, q, k, k, None, T - 1, H, KV, hd, KV * hd, torch.cuda.current_stream().cuda_stream)
+    H, KV, hd, T = 64, 8, 256, 40000
+    q, k, v, gate, kd = _case(dev, H, KV, hd, T, seed=5)
+    ref = torch.zeros(H * hd, device=dev)
+    attn.attn_decode(ref, q, k, v, T - 1, H, KV, hd, kd)
+    out = torch.full((H * hd,), float("nan"), device=dev)
+    _noalloc(out, q, k, v, None, T - 1, H, KV, hd, kd, torch.cuda.current_stream().cuda_stream)
+    torch.cuda.synchronize()
+    assert torch.equal(out, ref)

@@ -77,6 +77,13 @@ PROTOS = {
         [C.POINTER(u32), u32, u32, u32, u32, u32, C.POINTER(YattnDecodeWork), u32,
          C.POINTER(u32), C.POINTER(u32), C.POINTER(u32), *E],
     ),
+    "yattn_decode_plan_pooled": (
+        C.c_int,
+        [C.POINTER(u32), u32, u32, u32, u32, u32, C.POINTER(YattnDecodeWork), u32,
+         C.POINTER(u32), C.POINTER(u32), C.POINTER(u32), *E],
+    ),
+    "yattn_decode_run_pooled": (
+        C.c_int, [vp, vp, u32, u32, u32, u32, u32, u32, u32, vp, sz, vp, sz, vp, *E]),
     "yattn_decode_workspace_bytes": (sz, [u32, u32, u32, u32, u32]),
     "yattn_decode_workspace_init": (C.c_int, [vp, sz, vp, *E]),
     "yattn_decode_run": (C.c_int, [vp, vp, u32, u32, u32, u32, u32, u32, u32, vp, sz, vp, *E]),

@@ -134,10 +134,14 @@ class DecodePlan:
     n_parts: int
     n_groups: int
     workspace: Optional[torch.Tensor]
+    pool: Optional[tuple] = None      # (base pointer, bytes): run through the pooled tensor-copy kernels
 
     @staticmethod
     def build(positions: Sequence[int], n_heads: int, n_kv_heads: int, head_dim: int, kv_dim: int,
-              split_tokens: int = 0, target_ctas: int = 0, device=None) -> "DecodePlan":
+              split_tokens: int = 0, target_ctas: int = 0, device=None,
+              pool: Optional[tuple] = None) -> "DecodePlan":
+        """pool = (base, bytes) of one allocation holding every item's K and V rows
+        (row stride kv_dim): the plan and runs use the pooled variants."""
         pos = np.ascontiguousarray(np.asarray(positions, dtype=np.uint32))
         n = int(pos.size)
         cap = max(1, n * n_kv_heads * 64)
@@ -145,9 +149,10 @@ class DecodePlan:
             work = (YattnDecodeWork * cap)()
             n_work, n_parts, n_groups = C.c_uint32(), C.c_uint32(), C.c_uint32()
             err = C.create_string_buffer(512)
-            rc = lib.yattn_decode_plan(pos.ctypes.data_as(C.POINTER(C.c_uint32)), n, n_kv_heads, head_dim,
-                                       split_tokens, target_ctas, work, cap, C.byref(n_work), C.byref(n_parts),
-                                       C.byref(n_groups), err, 512)
+            plan_fn = lib.yattn_decode_plan_pooled if pool is not None else lib.yattn_decode_plan
+            rc = plan_fn(pos.ctypes.data_as(C.POINTER(C.c_uint32)), n, n_kv_heads, head_dim,
+                         split_tokens, target_ctas, work, cap, C.byref(n_work), C.byref(n_parts),
+                         C.byref(n_groups), err, 512)
             if rc == 0:
                 break
             if n_work.value > cap:
@@ -162,14 +167,19 @@ class DecodePlan:
         if ws_bytes:
             ws = torch.zeros(ws_bytes, dtype=torch.uint8, device=device or "cuda")
         return DecodePlan(n, n_heads, n_kv_heads, head_dim, kv_dim, dev, n_work.value, n_parts.value,
-                          n_groups.value, ws)
+                          n_groups.value, ws, tuple(pool) if pool is not None else None)
 
     def run(self, items_dev: torch.Tensor, stream=None) -> None:
         ws_ptr = self.workspace.data_ptr() if self.workspace is not None else None
         ws_len = self.workspace.numel() if self.workspace is not None else 0
-        call("yattn_decode_run", items_dev.data_ptr(), self.work.data_ptr(), self.n_work, self.n_parts,
-             self.n_groups, self.n_heads, self.n_kv_heads, self.head_dim, self.kv_dim, ws_ptr, ws_len,
-             _stream(stream))
+        if self.pool is not None:
+            call("yattn_decode_run_pooled", items_dev.data_ptr(), self.work.data_ptr(), self.n_work, self.n_parts,
+                 self.n_groups, self.n_heads, self.n_kv_heads, self.head_dim, self.kv_dim, self.pool[0],
+                 self.pool[1], ws_ptr, ws_len, _stream(stream))
+        else:
+            call("yattn_decode_run", items_dev.data_ptr(), self.work.data_ptr(), self.n_work, self.n_parts,
+                 self.n_groups, self.n_heads, self.n_kv_heads, self.head_dim, self.kv_dim, ws_ptr, ws_len,
+                 _stream(stream))
 
 
 def make_items(entries: Sequence[tuple], device=None) -> torch.Tensor:

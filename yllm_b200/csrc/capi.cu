@@ -1,5 +1,8 @@
 // capi.cu -- status, error strings and the per-device context of the C ABI.
 #include "common.cuh"
+#include "tcgen05.cuh"
+
+#include <cudaTypedefs.h>
 
 #include <mutex>
 #include <stdarg.h>
@@ -44,6 +47,43 @@ DevCtx* dev_ctx(char* err, size_t errlen) {
     c.status = st;
     c.device = dev;
     return &c;
+}
+
+// ------------------------------------------------------------- tensor maps
+
+namespace {
+PFN_cuTensorMapEncodeTiled_v12000 get_encode(char* err, size_t errlen) {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    if (fn) return fn;
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q{};
+    cudaError_t e = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q);
+    if (e != cudaSuccess || q != cudaDriverEntryPointSuccess || !ptr) {
+        set_err(err, errlen, "cuTensorMapEncodeTiled unavailable (%s)", cudaGetErrorString(e));
+        return nullptr;
+    }
+    fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+    return fn;
+}
+}  // namespace
+
+int encode_kv_map(CUtensorMap* map, const void* base, uint32_t kv_dim, uint64_t n_rows, uint32_t box_rows, char* err,
+                  size_t errlen) {
+    auto enc = get_encode(err, errlen);
+    if (!enc) return -1;
+    cuuint64_t dims[2] = {kv_dim, n_rows};
+    cuuint64_t strides[1] = {static_cast<cuuint64_t>(kv_dim) * 2};
+    cuuint32_t box[2] = {64, box_rows};
+    cuuint32_t estr[2] = {1, 1};
+    CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) {
+        set_err(err, errlen, "cuTensorMapEncodeTiled failed (%d): kv_dim %u, %llu rows, box %u", static_cast<int>(r),
+                kv_dim, static_cast<unsigned long long>(n_rows), box_rows);
+        return -1;
+    }
+    return 0;
 }
 
 int dev_num_sms() {

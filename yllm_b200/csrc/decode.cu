@@ -21,6 +21,7 @@
 //     partials to the workspace and the last split of an (item, head group) to
 //     arrive (atomic counter) merges all splits with log-sum-exp weights.
 #include "common.cuh"
+#include "tcgen05.cuh"
 
 #include <algorithm>
 #include <mutex>
@@ -43,6 +44,12 @@ template <int HD> struct DecodeCfg {
     static constexpr int PT_BYTES = 2 * 8 * 48;                       // per warp: P^T hi and lo, 8 heads x 16 tokens
 };
 
+// Kv heads per CTA of the tensor-copy (TM) kernels: two at head_dim <= 128 (a stage
+// of 64 tokens, so each copy is 64 tokens x 128 B = 8 KB), else one.
+__host__ __device__ inline uint32_t tm_heads_per_cta(uint32_t n_kv, uint32_t hd) {
+    return (hd <= 128 && n_kv % 2 == 0) ? 2u : 1u;
+}
+
 // Kv heads per CTA for a geometry: the largest of 8/4/2/1 (at most NCW) dividing n_kv.
 __host__ __device__ inline uint32_t heads_per_cta(uint32_t n_kv, uint32_t hd) {
     const uint32_t cap = hd >= 256 ? 4u : 8u;
@@ -61,6 +68,8 @@ struct DecodeParams {
     uint32_t t_end0;                  // end key (exclusive) when work == nullptr
     uint32_t n_heads, n_kv, kv_dim, hc;
     uint32_t n_work;                  // entries of work (grouped by cta)
+    uint64_t kmap_base, vmap_base;    // TM kernels: global base of the K and V tensor maps
+    uint32_t row_bytes;               // TM kernels: kv_dim * 2
     float scale_log2;                 // log2(e) / sqrt(head_dim)
     float* part_ml;                   // [n_parts][G][2]
     float* part_o;                    // [n_parts][G][HD]
@@ -139,14 +148,26 @@ __device__ __forceinline__ uint32_t first_unit_from(const YattnDecodeWork* work,
 // Per 16-token step, on the legacy tensor cores (mma.sync m16n8k16, fp32 accumulate):
 //   S^T (16 tok x 8 heads) = K (16 x HD) . Q^T (HD x 8),  q = q_hi + q_lo in fp16
 //   O^T (HD x 8 heads)    += V^T (HD x 16) . P^T (16 x 8), p = p_hi + p_lo in fp16
-template <int HD, int G>
-__global__ void __launch_bounds__(DecodeCfg<HD>::THREADS, 1) k_decode(const DecodeParams p) {
+//
+// TM = true: HC = p.hc kv heads per CTA, 16*NCW/HC tokens per stage, K and V
+// staged by 2-D tensor copies of 64 dims x one stage of tokens (8 KB at the
+// chosen HC, 128-byte swizzle, no row padding) from the maps kmap / vmap; the
+// consumers address the swizzled tiles.  Many-kilobyte copies stream at ~7.2 TB/s where one copy per
+// 1-2 KB row tops out at 4.6-6.4 TB/s.  TM = false: one cp.async.bulk per row of
+// the head group into padded rows (any base pointers, no tensor map).
+template <int HD, int G, bool TM>
+__global__ void __launch_bounds__(DecodeCfg<HD>::THREADS, 1)
+    k_decode(const __grid_constant__ CUtensorMap kmap, const __grid_constant__ CUtensorMap vmap,
+             const DecodeParams p) {
     using C = DecodeCfg<HD>;
     constexpr int NCW = C::NCW;
     constexpr int KS = HD / 16;                                       // k-steps (QK) and m-tiles (PV)
     static_assert(G <= 8, "query group fits the MMA's 8 columns");
 
-    extern __shared__ __align__(1024) uint8_t smem[];
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    // the 128-byte swizzle of the tensor copies repeats every 1024 B: align the ring
+    uint8_t* smem = TM ? reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023))
+                       : smem_raw;
     uint8_t* stages = smem;
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::NST * C::STAGE_MAX);
     uint64_t* empty = full + C::NST;
@@ -163,7 +184,7 @@ __global__ void __launch_bounds__(DecodeCfg<HD>::THREADS, 1) k_decode(const Deco
     const uint32_t HC = p.hc;
     const uint32_t TOK = 16u * NCW / HC;
     const uint32_t ROWB = HC * HD * 2;                                // bytes of one row copy (HC heads)
-    const uint32_t RS = ROWB + 16;                                    // smem row stride
+    const uint32_t RS = TM ? ROWB : ROWB + 16;                        // smem row stride
     const uint32_t TILEB = TOK * RS;
     const uint32_t STAGEB = 2 * TILEB;
 
@@ -229,9 +250,15 @@ __global__ void __launch_bounds__(DecodeCfg<HD>::THREADS, 1) k_decode(const Deco
         __syncthreads();
 
         if (warp == NCW) {
-            // ================= producer: one bulk copy per row per tensor =================
+            // ================= producer =================
             const uint16_t* kb = it.k + static_cast<size_t>(kg) * HC * HD;
             const uint16_t* vb = it.v + static_cast<size_t>(kg) * HC * HD;
+            const int32_t krow0 = TM ? static_cast<int32_t>((reinterpret_cast<uint64_t>(it.k) - p.kmap_base) / p.row_bytes) : 0;
+            const int32_t vrow0 = TM ? static_cast<int32_t>((reinterpret_cast<uint64_t>(it.v) - p.vmap_base) / p.row_bytes) : 0;
+            if (TM && u == u_begin && lane == 0) {
+                prefetch_tensormap(&kmap);
+                prefetch_tensormap(&vmap);
+            }
             uint32_t issued = 0;
             for (uint32_t i = 0; i < ntiles; ++i) {
                 const uint32_t gi = tb + i;
@@ -245,12 +272,25 @@ __global__ void __launch_bounds__(DecodeCfg<HD>::THREADS, 1) k_decode(const Deco
                 const uint32_t nrows = min(TOK, t1 - tile0);
                 uint8_t* kdst = stages + s * STAGEB;
                 uint8_t* vdst = kdst + TILEB;
-                if (lane == 0) mbar_arrive_expect_tx(&full[s], 2u * nrows * ROWB);
-                __syncwarp();
-                for (uint32_t r = lane; r < nrows; r += 32) {
-                    const size_t off = static_cast<size_t>(tile0 + r) * p.kv_dim;
-                    bulk_g2s(kdst + r * RS, kb + off, ROWB, &full[s]);
-                    bulk_g2s(vdst + r * RS, vb + off, ROWB, &full[s]);
+                if constexpr (TM) {
+                    // whole boxes of TOK rows (rows past the unit are masked; past the map, zero-filled)
+                    if (lane == 0) {
+                        mbar_arrive_expect_tx(&full[s], STAGEB);
+                        for (uint32_t c = 0; c < HC * (HD / 64); ++c) {   // HC heads, 64 dims per box
+                            const int32_t x = static_cast<int32_t>(kg * HC * HD + c * 64);
+                            tma_load_2d(kdst + c * TOK * 128, &kmap, x, krow0 + static_cast<int32_t>(tile0), &full[s]);
+                            tma_load_2d(vdst + c * TOK * 128, &vmap, x, vrow0 + static_cast<int32_t>(tile0), &full[s]);
+                        }
+                    }
+                    __syncwarp();
+                } else {
+                    if (lane == 0) mbar_arrive_expect_tx(&full[s], 2u * nrows * ROWB);
+                    __syncwarp();
+                    for (uint32_t r = lane; r < nrows; r += 32) {
+                        const size_t off = static_cast<size_t>(tile0 + r) * p.kv_dim;
+                        bulk_g2s(kdst + r * RS, kb + off, ROWB, &full[s]);
+                        bulk_g2s(vdst + r * RS, vb + off, ROWB, &full[s]);
+                    }
                 }
                 issued = i + 1;
             }
@@ -296,6 +336,24 @@ __global__ void __launch_bounds__(DecodeCfg<HD>::THREADS, 1) k_decode(const Deco
             const uint32_t slice = (16 * sl) * RS + hl * HD * 2;
             const uint32_t a_off = slice + ((lane & 7) + ((lane >> 3) & 1) * 8) * RS + ((lane >> 4) & 1) * 16;   // K
             const uint32_t v_off = slice + ((lane & 7) + ((lane >> 4) & 1) * 8) * RS + ((lane >> 3) & 1) * 16;   // V^T
+            // TM: tiles are HC*HD/64 panels of [TOK rows][128 B] (head hl's panels from hl*HD/64),
+            // 16-byte chunk c of row r at c ^ (r & 7)
+            const uint32_t rk = 16 * sl + (lane & 15), rv = 16 * sl + (lane & 7) + ((lane >> 4) & 1) * 8;
+            const uint32_t hpan = hl * (HD / 64);
+            auto k_addr = [&](uint32_t kt, int kk) -> uint32_t {   // K A-fragment, k-step kk
+                if constexpr (TM)
+                    return kt + (hpan + (kk >> 2)) * TOK * 128 + rk * 128 +
+                           ((static_cast<uint32_t>(((kk & 3) << 1) + (lane >> 4)) ^ (lane & 7)) << 4);
+                else
+                    return kt + a_off + kk * 32;
+            };
+            auto v_addr = [&](uint32_t vt, int mt) -> uint32_t {   // V^T A-fragment, m-tile mt
+                if constexpr (TM)
+                    return vt + (hpan + (mt >> 2)) * TOK * 128 + rv * 128 +
+                           ((static_cast<uint32_t>(((mt & 3) << 1) + ((lane >> 3) & 1)) ^ (lane & 7)) << 4);
+                else
+                    return vt + v_off + mt * 32;
+            };
             const uint32_t p_off = (lane & 7) * 48 + ((lane >> 3) & 1) * 16;                                     // P^T
 
             for (uint32_t i = 0; i < ntiles; ++i) {
@@ -316,8 +374,8 @@ __global__ void __launch_bounds__(DecodeCfg<HD>::THREADS, 1) k_decode(const Deco
         #pragma unroll
                     for (int kk = 0; kk < KS; kk += 2) {
                         uint32_t a[4], b[4];
-                        ldsm_x4(kt + a_off + kk * 32, a);
-                        ldsm_x4(kt + a_off + (kk + 1) * 32, b);
+                        ldsm_x4(k_addr(kt, kk), a);
+                        ldsm_x4(k_addr(kt, kk + 1), b);
                         mma16816(sc, a, qhi[kk][0], qhi[kk][1]);
                         mma16816(sc1, b, qhi[kk + 1][0], qhi[kk + 1][1]);
                         mma16816(sc2, a, qlo[kk][0], qlo[kk][1]);
@@ -388,7 +446,7 @@ __global__ void __launch_bounds__(DecodeCfg<HD>::THREADS, 1) k_decode(const Deco
                         oc[mt][2] *= al_a;
                         oc[mt][3] *= al_b;
                         uint32_t a[4];
-                        ldsm_x4_t(vt + v_off + mt * 32, a);
+                        ldsm_x4_t(v_addr(vt, mt), a);
                         a[0] &= vm01;
                         a[1] &= vm01;
                         a[2] &= vm23;
@@ -627,17 +685,19 @@ __global__ void k_merge_partials(float* out, const float* ml, const float* o, ui
 }
 
 // ------------------------------------------------------------------ dispatch
-template <int HD, int G>
-int launch_t(const DecodeParams& p, uint32_t grid, cudaStream_t st, char* err, size_t errlen) {
+template <int HD, int G, bool TM>
+int launch_t(const DecodeParams& p, const CUtensorMap& km, const CUtensorMap& vm, uint32_t grid, cudaStream_t st,
+             char* err, size_t errlen) {
     using C = DecodeCfg<HD>;
     const size_t smem = C::NST * C::STAGE_MAX + 2 * C::NST * 8 + C::NCW * C::PT_BYTES + C::NCW * G * 2 * 4 +
-                        16 * 4 + 16;
+                        16 * 4 + 16 + (TM ? 1024 : 0);
     static_assert(C::NST * C::STAGE_MAX >= C::NCW * G * HD * 4, "merge area must fit in the ring");
+    static_assert(C::STAGE_MAX >= 2 * 16 * C::NCW * HD * 2, "a TM stage fits the ring slot");
     static bool attr_done[64] = {};
     int dev = 0;
     cudaGetDevice(&dev);
     if (dev >= 0 && dev < 64 && !attr_done[dev]) {
-        cudaError_t e = cudaFuncSetAttribute(k_decode<HD, G>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        cudaError_t e = cudaFuncSetAttribute(k_decode<HD, G, TM>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                              static_cast<int>(smem));
         if (e != cudaSuccess) {
             set_err(err, errlen, "decode: smem attribute: %s", cudaGetErrorString(e));
@@ -645,35 +705,51 @@ int launch_t(const DecodeParams& p, uint32_t grid, cudaStream_t st, char* err, s
         }
         attr_done[dev] = true;
     }
-    k_decode<HD, G><<<grid, C::THREADS, smem, st>>>(p);
+    k_decode<HD, G, TM><<<grid, C::THREADS, smem, st>>>(km, vm, p);
     YATTN_CHECK_LAUNCH(err, errlen, "decode");
     return 0;
 }
 
-template <int HD>
-int launch_hd(const DecodeParams& p, uint32_t gmax, uint32_t grid, cudaStream_t st, char* err, size_t errlen) {
+template <int HD, bool TM>
+int launch_hd(const DecodeParams& p, const CUtensorMap& km, const CUtensorMap& vm, uint32_t gmax, uint32_t grid,
+              cudaStream_t st, char* err, size_t errlen) {
     switch (gmax) {
-        case 1: return launch_t<HD, 1>(p, grid, st, err, errlen);
-        case 2: return launch_t<HD, 2>(p, grid, st, err, errlen);
-        case 3: return launch_t<HD, 3>(p, grid, st, err, errlen);
-        case 4: return launch_t<HD, 4>(p, grid, st, err, errlen);
-        case 5: return launch_t<HD, 5>(p, grid, st, err, errlen);
-        case 6: return launch_t<HD, 6>(p, grid, st, err, errlen);
-        case 7: return launch_t<HD, 7>(p, grid, st, err, errlen);
-        case 8: return launch_t<HD, 8>(p, grid, st, err, errlen);
+        case 1: return launch_t<HD, 1, TM>(p, km, vm, grid, st, err, errlen);
+        case 2: return launch_t<HD, 2, TM>(p, km, vm, grid, st, err, errlen);
+        case 3: return launch_t<HD, 3, TM>(p, km, vm, grid, st, err, errlen);
+        case 4: return launch_t<HD, 4, TM>(p, km, vm, grid, st, err, errlen);
+        case 5: return launch_t<HD, 5, TM>(p, km, vm, grid, st, err, errlen);
+        case 6: return launch_t<HD, 6, TM>(p, km, vm, grid, st, err, errlen);
+        case 7: return launch_t<HD, 7, TM>(p, km, vm, grid, st, err, errlen);
+        case 8: return launch_t<HD, 8, TM>(p, km, vm, grid, st, err, errlen);
         default: set_err(err, errlen, "decode: %u query heads per kv head (max 8)", gmax); return -1;
     }
 }
 
-int launch_decode(const DecodeParams& p, uint32_t head_dim, uint32_t grid, cudaStream_t st, char* err,
-                  size_t errlen) {
+// tm: tensor-copy kernels (p.hc must be 1, km / vm valid); otherwise the row-copy kernels.
+int launch_decode(const DecodeParams& p, bool tm, const CUtensorMap* km, const CUtensorMap* vm, uint32_t head_dim,
+                  uint32_t grid, cudaStream_t st, char* err, size_t errlen) {
     const uint32_t gmax = (p.n_heads + p.n_kv - 1) / p.n_kv;
-    switch (head_dim) {
-        case 64: return launch_hd<64>(p, gmax, grid, st, err, errlen);
-        case 128: return launch_hd<128>(p, gmax, grid, st, err, errlen);
-        case 256: return launch_hd<256>(p, gmax, grid, st, err, errlen);
-        default: set_err(err, errlen, "decode: head_dim %u not supported (64/128/256)", head_dim); return -1;
+    static const CUtensorMap none{};
+    const CUtensorMap& k = km ? *km : none;
+    const CUtensorMap& v = vm ? *vm : none;
+    if (tm) {
+        switch (head_dim) {
+            case 64: return launch_hd<64, true>(p, k, v, gmax, grid, st, err, errlen);
+            case 128: return launch_hd<128, true>(p, k, v, gmax, grid, st, err, errlen);
+            case 256: return launch_hd<256, true>(p, k, v, gmax, grid, st, err, errlen);
+            default: break;
+        }
+    } else {
+        switch (head_dim) {
+            case 64: return launch_hd<64, false>(p, k, v, gmax, grid, st, err, errlen);
+            case 128: return launch_hd<128, false>(p, k, v, gmax, grid, st, err, errlen);
+            case 256: return launch_hd<256, false>(p, k, v, gmax, grid, st, err, errlen);
+            default: break;
+        }
     }
+    set_err(err, errlen, "decode: head_dim %u not supported (64/128/256)", head_dim);
+    return -1;
 }
 
 int check_geom(uint32_t n_heads, uint32_t n_kv, uint32_t hd, uint32_t kv_dim, char* err, size_t errlen) {
@@ -731,9 +807,10 @@ struct SinglePlan {
     uint32_t hc, n_groups_kv, split, ns, n_parts, n_groups;
 };
 
+// Single queries run the tensor-copy kernels (tm_heads_per_cta heads per CTA).
 SinglePlan plan_single(uint32_t ntok, uint32_t n_kv, uint32_t hd, uint32_t target) {
     SinglePlan s{};
-    s.hc = heads_per_cta(n_kv, hd);
+    s.hc = tm_heads_per_cta(n_kv, hd);
     s.n_groups_kv = n_kv / s.hc;
     s.split = auto_split(static_cast<uint64_t>(ntok) * s.n_groups_kv, target);
     s.ns = (ntok + s.split - 1) / s.split;
@@ -769,7 +846,16 @@ DecodeParams single_params(const SinglePlan& sp, float* out, const float* q, con
 int launch_single(DecodeParams& p, const SinglePlan& sp, uint32_t hd, cudaStream_t st, char* err, size_t errlen) {
     const bool defer = sp.ns > kInKernelMergeMax;
     p.defer_merge = defer ? 1 : 0;
-    if (launch_decode(p, hd, sp.ns * sp.n_groups_kv, st, err, errlen)) return -1;
+    // K and V maps over keys [0, t_end) of this layer; boxes of one stage (16 tokens per consumer warp)
+    CUtensorMap km, vm;
+    const uint32_t box_rows = 16u * (hd >= 256 ? DecodeCfg<256>::NCW : DecodeCfg<128>::NCW) / p.hc;
+    if (encode_kv_map(&km, p.item0.k, p.kv_dim, p.t_end0, box_rows, err, errlen) ||
+        encode_kv_map(&vm, p.item0.v, p.kv_dim, p.t_end0, box_rows, err, errlen))
+        return -1;
+    p.kmap_base = reinterpret_cast<uint64_t>(p.item0.k);
+    p.vmap_base = reinterpret_cast<uint64_t>(p.item0.v);
+    p.row_bytes = p.kv_dim * 2;
+    if (launch_decode(p, true, &km, &vm, hd, sp.ns * sp.n_groups_kv, st, err, errlen)) return -1;
     if (!defer) return 0;
     const uint32_t G = gmax_of(p.n_heads, p.n_kv);
     k_merge_splits<<<p.n_heads, 256, 0, st>>>(p.part_ml, p.part_o, sp.ns, p.n_heads, p.n_kv, G, hd, p.item0.out,
@@ -856,10 +942,12 @@ int decode_reserve(size_t bytes, char* err, size_t errlen) {
 
 using namespace yattn;
 
-extern "C" int yattn_decode_plan(const uint32_t* pos_host, uint32_t n_items, uint32_t n_kv_heads,
-                                 uint32_t head_dim, uint32_t split_tokens, uint32_t target_ctas,
-                                 YattnDecodeWork* work_host, uint32_t work_cap, uint32_t* n_work, uint32_t* n_parts,
-                                 uint32_t* n_groups, char* err, size_t errlen) {
+namespace {
+// tm: heads per CTA of the tensor-copy kernels (pooled run), else of the row-copy kernels.
+int decode_plan_impl(const uint32_t* pos_host, uint32_t n_items, uint32_t n_kv_heads, uint32_t head_dim,
+                     uint32_t split_tokens, uint32_t target_ctas, bool tm, YattnDecodeWork* work_host,
+                     uint32_t work_cap, uint32_t* n_work, uint32_t* n_parts, uint32_t* n_groups, char* err,
+                     size_t errlen) {
     if (!pos_host || !work_host || !n_work || !n_parts || !n_groups || n_kv_heads == 0 || n_kv_heads > 65535) {
         set_err(err, errlen, "decode_plan: bad arguments");
         return -1;
@@ -868,7 +956,7 @@ extern "C" int yattn_decode_plan(const uint32_t* pos_host, uint32_t n_items, uin
         set_err(err, errlen, "decode_plan: head_dim %u not supported (64/128/256)", head_dim);
         return -1;
     }
-    const uint32_t hc = heads_per_cta(n_kv_heads, head_dim);
+    const uint32_t hc = tm ? tm_heads_per_cta(n_kv_heads, head_dim) : heads_per_cta(n_kv_heads, head_dim);
     const uint32_t nkg = n_kv_heads / hc;
     uint64_t total = 0;
     for (uint32_t i = 0; i < n_items; ++i) total += static_cast<uint64_t>(pos_host[i]) + 1;
@@ -983,8 +1071,19 @@ extern "C" int yattn_decode_plan(const uint32_t* pos_host, uint32_t n_items, uin
                     }
                 }
             }
-            if (w.empty() || w.back().cta < target_ctas || attempt >= 64) break;
-            chunk += chunk / 128 + 1;   // the charges pushed units past the last CTA
+            // dense CTA numbers (a chunk that the cuts skipped holds no unit): the run
+            // launches one CTA per unit, so the CTA count must not exceed the unit count
+            uint32_t n_cta = 0, prev = ~0u;
+            for (YattnDecodeWork& x : w) {
+                if (x.cta != prev) {
+                    prev = x.cta;
+                    ++n_cta;
+                }
+                x.cta = n_cta - 1;
+            }
+            if (n_cta <= target_ctas || attempt >= 64) break;
+            // the charges pushed units past the last CTA: grow finely first, then faster
+            chunk += (attempt < 16 ? chunk / 128 : chunk / 16) + 1;
         }
         // units are already grouped by CTA in increasing order
     }
@@ -998,6 +1097,23 @@ extern "C" int yattn_decode_plan(const uint32_t* pos_host, uint32_t n_items, uin
     *n_parts = parts;
     *n_groups = groups;
     return 0;
+}
+}  // namespace
+
+extern "C" int yattn_decode_plan(const uint32_t* pos_host, uint32_t n_items, uint32_t n_kv_heads,
+                                 uint32_t head_dim, uint32_t split_tokens, uint32_t target_ctas,
+                                 YattnDecodeWork* work_host, uint32_t work_cap, uint32_t* n_work, uint32_t* n_parts,
+                                 uint32_t* n_groups, char* err, size_t errlen) {
+    return decode_plan_impl(pos_host, n_items, n_kv_heads, head_dim, split_tokens, target_ctas, false, work_host, work_cap,
+                            n_work, n_parts, n_groups, err, errlen);
+}
+
+extern "C" int yattn_decode_plan_pooled(const uint32_t* pos_host, uint32_t n_items, uint32_t n_kv_heads,
+                                        uint32_t head_dim, uint32_t split_tokens, uint32_t target_ctas,
+                                        YattnDecodeWork* work_host, uint32_t work_cap, uint32_t* n_work,
+                                        uint32_t* n_parts, uint32_t* n_groups, char* err, size_t errlen) {
+    return decode_plan_impl(pos_host, n_items, n_kv_heads, head_dim, split_tokens, target_ctas, true, work_host, work_cap,
+                            n_work, n_parts, n_groups, err, errlen);
 }
 
 extern "C" size_t yattn_decode_workspace_bytes(uint32_t n_parts, uint32_t n_groups, uint32_t n_heads,
@@ -1018,10 +1134,14 @@ extern "C" int yattn_decode_workspace_init(void* workspace, size_t ws_bytes, voi
     return 0;
 }
 
-extern "C" int yattn_decode_run(const YattnDecodeItem* items_dev, const YattnDecodeWork* work_dev, uint32_t n_work,
-                                uint32_t n_parts, uint32_t n_groups, uint32_t n_heads, uint32_t n_kv_heads,
-                                uint32_t head_dim, uint32_t kv_dim, void* workspace, size_t ws_bytes, void* stream,
-                                char* err, size_t errlen) {
+namespace {
+// pool == nullptr: row-copy kernels.  pool: every item's K and V rows lie in
+// [pool, pool + pool_bytes); one tensor map covers it (tensor-copy kernels, plan
+// made by yattn_decode_plan_pooled).
+int decode_run_impl(const YattnDecodeItem* items_dev, const YattnDecodeWork* work_dev, uint32_t n_work,
+                    uint32_t n_parts, uint32_t n_groups, uint32_t n_heads, uint32_t n_kv_heads, uint32_t head_dim,
+                    uint32_t kv_dim, const void* pool, size_t pool_bytes, void* workspace, size_t ws_bytes,
+                    void* stream, char* err, size_t errlen) {
     if (check_geom(n_heads, n_kv_heads, head_dim, kv_dim, err, errlen)) return -1;
     if (n_work == 0) return 0;
     if (!items_dev || !work_dev) {
@@ -1043,11 +1163,50 @@ extern "C" int yattn_decode_run(const YattnDecodeItem* items_dev, const YattnDec
     p.n_heads = n_heads;
     p.n_kv = n_kv_heads;
     p.kv_dim = kv_dim;
-    p.hc = heads_per_cta(n_kv_heads, head_dim);
+    p.hc = pool ? tm_heads_per_cta(n_kv_heads, head_dim) : heads_per_cta(n_kv_heads, head_dim);
     p.scale_log2 = 1.4426950408889634f / sqrtf(static_cast<float>(head_dim));
     p.status = ctx->status;
     if (n_parts > 0) carve_ws(workspace, n_parts, n_groups, gmax, p);
-    return launch_decode(p, head_dim, n_work, static_cast<cudaStream_t>(stream), err, errlen);
+    if (!pool)
+        return launch_decode(p, false, nullptr, nullptr, head_dim, n_work, static_cast<cudaStream_t>(stream), err,
+                             errlen);
+    if (reinterpret_cast<uintptr_t>(pool) & 15u) {
+        set_err(err, errlen, "decode_run_pooled: pool must be 16-byte aligned");
+        return -1;
+    }
+    const uint64_t rows = pool_bytes / (static_cast<uint64_t>(kv_dim) * 2);
+    if (rows == 0) {
+        set_err(err, errlen, "decode_run_pooled: pool of %zu bytes holds no row of kv_dim %u", pool_bytes, kv_dim);
+        return -1;
+    }
+    CUtensorMap map;
+    const uint32_t box_rows = 16u * (head_dim >= 256 ? DecodeCfg<256>::NCW : DecodeCfg<128>::NCW) / p.hc;
+    if (encode_kv_map(&map, pool, kv_dim, rows, box_rows, err, errlen)) return -1;
+    p.kmap_base = p.vmap_base = reinterpret_cast<uint64_t>(pool);
+    p.row_bytes = kv_dim * 2;
+    return launch_decode(p, true, &map, &map, head_dim, n_work, static_cast<cudaStream_t>(stream), err, errlen);
+}
+}  // namespace
+
+extern "C" int yattn_decode_run(const YattnDecodeItem* items_dev, const YattnDecodeWork* work_dev, uint32_t n_work,
+                                uint32_t n_parts, uint32_t n_groups, uint32_t n_heads, uint32_t n_kv_heads,
+                                uint32_t head_dim, uint32_t kv_dim, void* workspace, size_t ws_bytes, void* stream,
+                                char* err, size_t errlen) {
+    return decode_run_impl(items_dev, work_dev, n_work, n_parts, n_groups, n_heads, n_kv_heads, head_dim, kv_dim,
+                           nullptr, 0, workspace, ws_bytes, stream, err, errlen);
+}
+
+extern "C" int yattn_decode_run_pooled(const YattnDecodeItem* items_dev, const YattnDecodeWork* work_dev,
+                                       uint32_t n_work, uint32_t n_parts, uint32_t n_groups, uint32_t n_heads,
+                                       uint32_t n_kv_heads, uint32_t head_dim, uint32_t kv_dim, const void* pool,
+                                       size_t pool_bytes, void* workspace, size_t ws_bytes, void* stream, char* err,
+                                       size_t errlen) {
+    if (!pool) {
+        set_err(err, errlen, "decode_run_pooled: null pool");
+        return -1;
+    }
+    return decode_run_impl(items_dev, work_dev, n_work, n_parts, n_groups, n_heads, n_kv_heads, head_dim, kv_dim,
+                           pool, pool_bytes, workspace, ws_bytes, stream, err, errlen);
 }
 
 extern "C" size_t yattn_decode_partial_workspace_bytes(uint32_t n_tokens, uint32_t n_heads, uint32_t n_kv_heads,

@@ -27,8 +27,6 @@
 #include "common.cuh"
 #include "tcgen05.cuh"
 
-#include <cudaTypedefs.h>
-
 #include <algorithm>
 
 namespace yattn {
@@ -394,39 +392,6 @@ __global__ void __launch_bounds__(kPThreads, PCfg<HD>::MIN_BLOCKS)
 
 // ------------------------------------------------------------------ host side
 
-PFN_cuTensorMapEncodeTiled_v12000 get_encode(char* err, size_t errlen) {
-    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
-    if (fn) return fn;
-    void* ptr = nullptr;
-    cudaDriverEntryPointQueryResult q{};
-    cudaError_t e = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q);
-    if (e != cudaSuccess || q != cudaDriverEntryPointSuccess || !ptr) {
-        set_err(err, errlen, "prefill: cuTensorMapEncodeTiled unavailable (%s)", cudaGetErrorString(e));
-        return nullptr;
-    }
-    fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
-    return fn;
-}
-
-// 2-D map over a cache layer: rows of kv_dim fp16, n_rows rows; box 64 x box_rows, 128B swizzle.
-int make_kv_map(CUtensorMap* map, const void* base, uint32_t kv_dim, uint32_t n_rows, uint32_t box_rows, char* err,
-                size_t errlen) {
-    auto enc = get_encode(err, errlen);
-    if (!enc) return -1;
-    cuuint64_t dims[2] = {kv_dim, n_rows};
-    cuuint64_t strides[1] = {static_cast<cuuint64_t>(kv_dim) * 2};
-    cuuint32_t box[2] = {64, box_rows};
-    cuuint32_t estr[2] = {1, 1};
-    CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
-                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-    if (r != CUDA_SUCCESS) {
-        set_err(err, errlen, "prefill: cuTensorMapEncodeTiled failed (%d)", static_cast<int>(r));
-        return -1;
-    }
-    return 0;
-}
-
 template <int HD>
 int launch_prefill(const CUtensorMap& mk, const CUtensorMap& mv, const PrefillParams& p, uint32_t n_qtiles,
                    cudaStream_t st, char* err, size_t errlen) {
@@ -492,7 +457,7 @@ int prefill(float* out, const float* q, const uint16_t* kc, const uint16_t* vc, 
     const uint32_t n_keys = pos_start + B;
     const uint32_t bn = hd == 64 ? PCfg<64>::BN : hd == 128 ? PCfg<128>::BN : PCfg<256>::BN;   // key block
     CUtensorMap mk, mv;
-    if (make_kv_map(&mk, kc, kv_dim, n_keys, bn, err, errlen) || make_kv_map(&mv, vc, kv_dim, n_keys, bn, err, errlen))
+    if (encode_kv_map(&mk, kc, kv_dim, n_keys, bn, err, errlen) || encode_kv_map(&mv, vc, kv_dim, n_keys, bn, err, errlen))
         return -1;
     PrefillParams p{};
     p.q = q;

@@ -6,6 +6,11 @@
 
 namespace yattn {
 
+// Host: 2-D tensor map over fp16 rows of kv_dim elements (row stride kv_dim*2 B),
+// n_rows rows from base; box 64 elements x box_rows rows, 128-byte swizzle.
+int encode_kv_map(CUtensorMap* map, const void* base, uint32_t kv_dim, uint64_t n_rows, uint32_t box_rows, char* err,
+                  size_t errlen);
+
 // ----------------------------------------------------------------- TMA (tensor)
 
 // 2-D tiled load of one box into shared memory, completion on an mbarrier.
