@@ -43,7 +43,7 @@ def load_peaks() -> tuple[dict, str]:
 # from one ncu capture of exactly the launch the bench times (the commands and the
 # rest of those captures are summarised under profiles/).  Workloads without such a
 # capture report null.
-NCU_TRAFFIC = {"decode": 1216305664, "prefill": 25236992}
+NCU_TRAFFIC = {"decode": 1226090496, "prefill": 25236992}
 
 
 class ClockSampler:
@@ -405,7 +405,7 @@ def run_decode_small(args) -> None:
     ach = step_bytes / (per_call / 1e3) / 1e9
     G = -(-cfg.n_heads // cfg.n_kv_heads)
     roof = {"bound": "hbm", "achieved": round(ach, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
-            "frac": round(ach / peaks["hbm_gbs"], 4), "traffic": None, "kernel": f"k_decode<{cfg.head_dim},{G}>",
+            "frac": round(ach / peaks["hbm_gbs"], 4), "traffic": None, "kernel": f"k_decode<{cfg.head_dim},{G},TM> (pooled tensor copies)",
             "peak_source": src, "bytes_per_step": step_bytes,
             "note": f"{d.n_layers} launches per step in one graph; achieved = step bytes / step device time"}
     e2e = None

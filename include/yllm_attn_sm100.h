@@ -44,7 +44,9 @@ void yattn_clear_error(void);
 /* Reads (and with clear != 0 resets) the device-side status word of the
  * current device: 0 = no kernel gave up; otherwise the code of the first
  * bounded wait that timed out (a kernel that times out returns early instead
- * of hanging).  Synchronises the legacy default stream. */
+ * of hanging), or 103 if a decode run met a malformed work item (q or gate
+ * not 16-byte aligned; with a pool, K/V not at a row of the pool) and
+ * stopped.  Synchronises the legacy default stream. */
 int yattn_device_status(int* status_out, int clear, char* err, size_t errlen);
 
 /* ------------------------------------------------ drop-in replacements
@@ -139,7 +141,8 @@ int yattn_decode_workspace_init(void* workspace, size_t ws_bytes, void* stream,
 
 /* Runs a plan: items_dev[] and work_dev[] are device copies of the items and
  * of yattn_decode_plan's output.  Supported: head_dim 64/128/256, up to 8
- * query heads per kv head, kv_dim % 8 == 0, 16-byte aligned k/v bases. */
+ * query heads per kv head, kv_dim % 8 == 0, 16-byte aligned q, gate and k/v
+ * bases.  Plans hold no empty key range (t_end > t_begin). */
 int yattn_decode_run(const YattnDecodeItem* items_dev, const YattnDecodeWork* work_dev,
                      uint32_t n_work, uint32_t n_parts, uint32_t n_groups,
                      uint32_t n_heads, uint32_t n_kv_heads, uint32_t head_dim, uint32_t kv_dim,
@@ -150,8 +153,9 @@ int yattn_decode_run(const YattnDecodeItem* items_dev, const YattnDecodeWork* wo
  * blobs carved from one pool).  One 2-D tensor map covers the pool, so K and V
  * stream through tensor copies of 8-16 KB (64 dims x one stage of tokens,
  * 128-byte swizzle) instead of one copy per row -- the faster path.  A pooled
- * run needs a plan from yattn_decode_plan_pooled (one kv head per CTA); the
- * work array, workspace sizing and item layout are as above. */
+ * run needs a plan from yattn_decode_plan_pooled, which groups kv heads for
+ * the tensor copies (two per CTA at head_dim <= 128 with an even n_kv_heads,
+ * else one); the work array, workspace sizing and item layout are as above. */
 int yattn_decode_plan_pooled(const uint32_t* pos_host, uint32_t n_items, uint32_t n_kv_heads,
                              uint32_t head_dim, uint32_t split_tokens, uint32_t target_ctas,
                              YattnDecodeWork* work_host, uint32_t work_cap,

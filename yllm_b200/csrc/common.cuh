@@ -44,11 +44,13 @@ int dev_num_sms();
 
 // ---------------------------------------------------------------- device side
 
-// Status codes written to the device status word when a bounded wait gives up.
+// Status codes written to the device status word when a bounded wait gives up
+// (or a kernel finds a malformed work item and stops).
 enum : int {
     ST_OK = 0,
     ST_DECODE_FULL_TIMEOUT = 101,
     ST_DECODE_EMPTY_TIMEOUT = 102,
+    ST_DECODE_BAD_ITEM = 103,   // q / gate not 16-byte aligned, or (pooled) K/V not rows of the pool
     ST_PREFILL_TIMEOUT = 201,
     ST_GDN_TIMEOUT = 301,
     ST_EXCHANGE_TIMEOUT = 401,
@@ -142,6 +144,23 @@ __device__ __forceinline__ float ex2_approx(float x) {
 
 __device__ __forceinline__ void named_bar_sync(int id, int nthreads) {
     asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
+}
+
+// Named barrier that also ANDs a predicate over the participating threads: every
+// thread gets the same answer, so all of them can take the same branch after it.
+__device__ __forceinline__ bool named_bar_and(int id, int nthreads, bool pred) {
+    uint32_t r;
+    asm volatile(
+        "{\n\t.reg .pred p, q;\n\tsetp.ne.u32 q, %1, 0;\n\tbar.red.and.pred p, %2, %3, q;\n\tselp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(r)
+        : "r"(pred ? 1u : 0u), "r"(id), "r"(nthreads)
+        : "memory");
+    return r != 0;
+}
+
+// Prefetch [src, src + bytes) into L2 (bulk form; src 16-byte aligned, bytes a multiple of 16).
+__device__ __forceinline__ void bulk_prefetch_l2(const void* src, uint32_t bytes) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
 }
 
 // The engine's f32_to_f16 (platform.c:340-379): half-up rounding of the

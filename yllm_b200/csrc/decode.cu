@@ -35,19 +35,23 @@ constexpr uint32_t kSplitMin = 128;  // shortest split of a balanced plan (keys)
 constexpr uint32_t kMaxSplits = 32;  // most splits of one (item, head group) in a balanced plan
 constexpr uint32_t kUnitCost = 192;  // keys charged for each further unit of a CTA
 
-// Per head_dim: NCW consumer warps, ring of NST stages sized for the worst case (HC = 1).
+// Per head_dim: NCW consumer warps and a ring of NST stages.  A stage holds K and V
+// of 16 tokens per consumer warp: exactly STAGE_TM bytes for the tensor copies,
+// STAGE_ROW with the row copies' 16-byte row padding (largest at HC = 1).
 template <int HD> struct DecodeCfg {
     static constexpr int NCW = (HD >= 256) ? 4 : 8;
     static constexpr int THREADS = 32 * (NCW + 1);
-    static constexpr int STAGE_MAX = 2 * 16 * NCW * (HD * 2 + 16);   // K + V tiles at HC = 1
+    static constexpr int STAGE_TM = 2 * 16 * NCW * HD * 2;
+    static constexpr int STAGE_ROW = 2 * 16 * NCW * (HD * 2 + 16);
     static constexpr int NST = (HD <= 64) ? 5 : 3;
     static constexpr int PT_BYTES = 2 * 8 * 48;                       // per warp: P^T hi and lo, 8 heads x 16 tokens
+    static constexpr int HC_TM_MAX = HD <= 128 ? 2 : 1;               // most kv heads per CTA of the TM kernels
 };
 
 // Kv heads per CTA of the tensor-copy (TM) kernels: two at head_dim <= 128 (a stage
 // of 64 tokens, so each copy is 64 tokens x 128 B = 8 KB), else one.
 __host__ __device__ inline uint32_t tm_heads_per_cta(uint32_t n_kv, uint32_t hd) {
-    return (hd <= 128 && n_kv % 2 == 0) ? 2u : 1u;
+    return (hd <= 128 && n_kv % 2 == 0) ? 2u : 1u;   // within DecodeCfg<hd>::HC_TM_MAX
 }
 
 // Kv heads per CTA for a geometry: the largest of 8/4/2/1 (at most NCW) dividing n_kv.
@@ -143,6 +147,55 @@ __device__ __forceinline__ uint32_t first_unit_from(const YattnDecodeWork* work,
     return lo;
 }
 
+// One unit of a CTA: entry u of the plan, or split u of the single-query form.
+struct DecodeUnit {
+    YattnDecodeItem it;
+    uint32_t kg, t0, t1, n_splits, split, part_base, group;
+};
+__device__ __forceinline__ DecodeUnit unit_of(const DecodeParams& p, uint32_t u, uint32_t HC) {
+    DecodeUnit x;
+    if (p.work) {
+        const YattnDecodeWork w = p.work[u];
+        x.it = p.items[w.item];
+        x.kg = w.kv_head / HC;
+        x.t0 = w.t_begin;
+        x.t1 = w.t_end;
+        x.n_splits = w.n_splits;
+        x.split = w.split;
+        x.part_base = w.part_base;
+        x.group = w.group;
+    } else {
+        x.it = p.item0;
+        x.kg = u / p.n_splits0;
+        x.split = u % p.n_splits0;
+        x.n_splits = p.n_splits0;
+        x.t0 = p.t_base + x.split * p.split_len;
+        x.t1 = min(x.t0 + p.split_len, p.t_end0);
+        x.part_base = x.kg * HC * p.n_splits0;
+        x.group = x.kg;
+    }
+    return x;
+}
+
+// Shared-memory layout of k_decode<HD, G, TM>: the ring of NST stages, (TM) one
+// q slot per stage, the ring's barriers, one unit descriptor per stage, the
+// consumer warps' P^T staging, their (m, l) for the merge, and flags.
+template <int HD, int G, bool TM> struct DecodeSmem {
+    using C = DecodeCfg<HD>;
+    static constexpr int STAGE = TM ? C::STAGE_TM : C::STAGE_ROW;
+    static constexpr int QSLOT = TM ? C::HC_TM_MAX * G * HD * 4 : 0;   // q of a unit's query heads, fp32
+    static constexpr int OFF_Q = C::NST * STAGE;
+    static constexpr int OFF_BAR = OFF_Q + C::NST * QSLOT;
+    static constexpr int OFF_DESC = (OFF_BAR + 2 * C::NST * 8 + 15) / 16 * 16;
+    static constexpr int DESC = (static_cast<int>(sizeof(DecodeUnit)) + 15) / 16 * 16;
+    static constexpr int OFF_PT = OFF_DESC + C::NST * DESC;
+    static constexpr int OFF_ML = OFF_PT + C::NCW * C::PT_BYTES;
+    static constexpr int OFF_FLAGS = OFF_ML + C::NCW * G * 2 * 4;
+    static constexpr int BYTES = OFF_FLAGS + 16 + (TM ? 1024 : 0);   // + alignment slack of the ring
+    static_assert(2 * 16 * C::NCW * HD * 2 >= C::NCW * G * HD * 4, "the warps' merge fits in one ring stage");
+    static_assert(BYTES <= 232448, "shared memory of one CTA");
+};
+
 // Warp NCW is the producer; consumer warp w owns kv head kg*HC + (w % HC) of
 // the group and tokens [16*(w / HC), +16) of every stage (TOK = 16*NCW/HC tokens).
 // Per 16-token step, on the legacy tensor cores (mma.sync m16n8k16, fp32 accumulate):
@@ -155,13 +208,23 @@ __device__ __forceinline__ uint32_t first_unit_from(const YattnDecodeWork* work,
 // consumers address the swizzled tiles.  Many-kilobyte copies stream at ~7.2 TB/s where one copy per
 // 1-2 KB row tops out at 4.6-6.4 TB/s.  TM = false: one cp.async.bulk per row of
 // the head group into padded rows (any base pointers, no tensor map).
+//
+// Units hand over without a CTA-wide stop.  The producer streams every unit's
+// tiles back to back; with a unit's first tile it stores the unit's descriptor
+// in that stage's slot, (TM) copies the unit's q into the stage's q slot on the
+// same barrier, and prefetches the unit's gate into L2.  The consumers learn
+// the unit from the slot, so none of the unit's setup waits on global memory,
+// and they merge in the stage of the unit's last tile, which they release only
+// after the merge: the producer keeps the other stages streaming meanwhile.
 template <int HD, int G, bool TM>
 __global__ void __launch_bounds__(DecodeCfg<HD>::THREADS, 1)
     k_decode(const __grid_constant__ CUtensorMap kmap, const __grid_constant__ CUtensorMap vmap,
              const DecodeParams p) {
     using C = DecodeCfg<HD>;
+    using L = DecodeSmem<HD, G, TM>;
     constexpr int NCW = C::NCW;
     constexpr int KS = HD / 16;                                       // k-steps (QK) and m-tiles (PV)
+    constexpr int DPL = HD / 32;                                      // dims per lane in the merges
     static_assert(G <= 8, "query group fits the MMA's 8 columns");
 
     extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -169,15 +232,18 @@ __global__ void __launch_bounds__(DecodeCfg<HD>::THREADS, 1)
     uint8_t* smem = TM ? reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023))
                        : smem_raw;
     uint8_t* stages = smem;
-    uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::NST * C::STAGE_MAX);
+    uint8_t* qslots = smem + L::OFF_Q;
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + L::OFF_BAR);
     uint64_t* empty = full + C::NST;
-    uint8_t* pt_all = reinterpret_cast<uint8_t*>(empty + C::NST);    // [NCW][PT_BYTES]
-    float* mrg_ml = reinterpret_cast<float*>(pt_all + NCW * C::PT_BYTES);   // [NCW][G][2]
-    uint32_t* s_gfirst = reinterpret_cast<uint32_t*>(mrg_ml + NCW * G * 2); // [8]
-    uint32_t* s_gcnt = s_gfirst + 8;                                  // [8]
-    volatile int* abort_flag = reinterpret_cast<volatile int*>(s_gcnt + 8);
+    DecodeUnit* descs = reinterpret_cast<DecodeUnit*>(smem + L::OFF_DESC);   // [NST], stride L::DESC
+    uint8_t* pt_all = smem + L::OFF_PT;                                // [NCW][PT_BYTES]
+    float* mrg_ml = reinterpret_cast<float*>(smem + L::OFF_ML);         // [NCW][G][2]
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::OFF_FLAGS);
     int* last_flag = const_cast<int*>(abort_flag) + 1;
-    float* mrg_o = reinterpret_cast<float*>(stages);                 // [NCW][G][HD], aliases the ring after use
+    uint32_t* s_range = reinterpret_cast<uint32_t*>(last_flag + 1);    // [2]
+    auto desc_at = [&](int s) -> DecodeUnit* {
+        return reinterpret_cast<DecodeUnit*>(reinterpret_cast<uint8_t*>(descs) + s * L::DESC);
+    };
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
@@ -189,7 +255,6 @@ __global__ void __launch_bounds__(DecodeCfg<HD>::THREADS, 1)
     const uint32_t STAGEB = 2 * TILEB;
 
     // ---- this CTA's units: a run of the plan (grouped by cta) or one uniform split ----
-    uint32_t* s_range = reinterpret_cast<uint32_t*>(last_flag + 1);   // [2]
     if (warp == 0) {
         uint32_t ub = blockIdx.x, ue = blockIdx.x + 1;
         if (p.work) {   // warp-wide 32-way searches: about two dependent loads each
@@ -212,72 +277,70 @@ __global__ void __launch_bounds__(DecodeCfg<HD>::THREADS, 1)
     __syncthreads();
     const uint32_t u_begin = s_range[0], u_end = s_range[1];
 
-    // The ring keeps running across units: unit tiles are numbered from tb, the
-    // tiles earlier units of this CTA streamed (stage = tile % NST, phase =
-    // (tile / NST) & 1).  Between units the whole CTA syncs, so the merge of one
-    // unit (which reuses the ring) ends before the next unit's copies start.
-    uint32_t tb = 0;
-    for (uint32_t u = u_begin; u < u_end; ++u) {
-        YattnDecodeItem it;
-        uint32_t kg, t0, t1, n_splits, split, part_base, group;
-        if (p.work) {
-            const YattnDecodeWork w = p.work[u];
-            it = p.items[w.item];
-            kg = w.kv_head / HC;
-            t0 = w.t_begin;
-            t1 = w.t_end;
-            n_splits = w.n_splits;
-            split = w.split;
-            part_base = w.part_base;
-            group = w.group;
-        } else {
-            it = p.item0;
-            kg = u / p.n_splits0;
-            split = u % p.n_splits0;
-            n_splits = p.n_splits0;
-            t0 = p.t_base + split * p.split_len;
-            t1 = min(t0 + p.split_len, p.t_end0);
-            part_base = kg * HC * p.n_splits0;
-            group = kg;
+    // The ring runs across units: tile gi (counted over all of this CTA's units)
+    // uses stage gi % NST with phase (gi / NST) & 1.  Every unit has at least one
+    // tile (an empty key range streams one fully masked tile).
+    if (warp == NCW) {
+        // ================= producer =================
+        if (TM && lane == 0) {
+            prefetch_tensormap(&kmap);
+            prefetch_tensormap(&vmap);
         }
-        const uint32_t ntok = t1 - t0;
-        const uint32_t ntiles = (ntok + TOK - 1) / TOK;
-        if (threadIdx.x == 0) {
-            for (uint32_t hl = 0; hl < HC; ++hl)
-                group_of(kg * HC + hl, p.n_heads, p.n_kv, s_gfirst[hl], s_gcnt[hl]);
-            last_flag[0] = 0;
-        }
-        __syncthreads();
-
-        if (warp == NCW) {
-            // ================= producer =================
-            const uint16_t* kb = it.k + static_cast<size_t>(kg) * HC * HD;
-            const uint16_t* vb = it.v + static_cast<size_t>(kg) * HC * HD;
-            const int32_t krow0 = TM ? static_cast<int32_t>((reinterpret_cast<uint64_t>(it.k) - p.kmap_base) / p.row_bytes) : 0;
-            const int32_t vrow0 = TM ? static_cast<int32_t>((reinterpret_cast<uint64_t>(it.v) - p.vmap_base) / p.row_bytes) : 0;
-            if (TM && u == u_begin && lane == 0) {
-                prefetch_tensormap(&kmap);
-                prefetch_tensormap(&vmap);
+        uint32_t gi = 0;   // tiles issued so far
+        bool ok = true;
+        for (uint32_t u = u_begin; u < u_end && ok; ++u) {
+            const DecodeUnit un = unit_of(p, u, HC);
+            const uint32_t ntiles = max(1u, (un.t1 - un.t0 + TOK - 1) / TOK);
+            {   // items live on the device: check what the copies below rely on
+                const uint64_t ka = reinterpret_cast<uint64_t>(un.it.k), va = reinterpret_cast<uint64_t>(un.it.v);
+                bool bad = ((reinterpret_cast<uintptr_t>(un.it.q) | reinterpret_cast<uintptr_t>(un.it.gate)) & 15u) != 0;
+                if (TM)
+                    bad = bad || ka < p.kmap_base || va < p.vmap_base || (ka - p.kmap_base) % p.row_bytes != 0 ||
+                          (va - p.vmap_base) % p.row_bytes != 0;
+                if (bad) {
+                    if (lane == 0) {
+                        atomicCAS(p.status, 0, ST_DECODE_BAD_ITEM);
+                        *abort_flag = 1;
+                    }
+                    break;
+                }
             }
-            uint32_t issued = 0;
-            for (uint32_t i = 0; i < ntiles; ++i) {
-                const uint32_t gi = tb + i;
+            // the query heads of the unit's kv heads are one contiguous run [qa, qe)
+            uint32_t qa, qn, qb, qm;
+            group_of(un.kg * HC, p.n_heads, p.n_kv, qa, qn);
+            group_of(un.kg * HC + HC - 1, p.n_heads, p.n_kv, qb, qm);
+            const uint32_t qbytes = (qb + qm - qa) * HD * 4;
+            const uint16_t* kb = un.it.k + static_cast<size_t>(un.kg) * HC * HD;
+            const uint16_t* vb = un.it.v + static_cast<size_t>(un.kg) * HC * HD;
+            const int32_t krow0 =
+                TM ? static_cast<int32_t>((reinterpret_cast<uint64_t>(un.it.k) - p.kmap_base) / p.row_bytes) : 0;
+            const int32_t vrow0 =
+                TM ? static_cast<int32_t>((reinterpret_cast<uint64_t>(un.it.v) - p.vmap_base) / p.row_bytes) : 0;
+            for (uint32_t i = 0; i < ntiles; ++i, ++gi) {
                 const int s = gi % C::NST;
                 if (gi >= static_cast<uint32_t>(C::NST)) {
                     if (!warp_wait_bounded(&empty[s], ((gi / C::NST) & 1u) ^ 1u, p.status, ST_DECODE_EMPTY_TIMEOUT,
-                                           abort_flag))
+                                           abort_flag)) {
+                        ok = false;
                         break;
+                    }
                 }
-                const uint32_t tile0 = t0 + i * TOK;
-                const uint32_t nrows = min(TOK, t1 - tile0);
+                const uint32_t tile0 = un.t0 + i * TOK;
+                const uint32_t nrows = tile0 < un.t1 ? min(TOK, un.t1 - tile0) : 0u;
                 uint8_t* kdst = stages + s * STAGEB;
                 uint8_t* vdst = kdst + TILEB;
+                if (i == 0 && lane == 0) {
+                    *desc_at(s) = un;   // published by the arrive on full[s] below
+                    if (un.it.gate) bulk_prefetch_l2(un.it.gate + static_cast<size_t>(qa) * HD, qbytes);
+                }
                 if constexpr (TM) {
                     // whole boxes of TOK rows (rows past the unit are masked; past the map, zero-filled)
                     if (lane == 0) {
-                        mbar_arrive_expect_tx(&full[s], STAGEB);
+                        mbar_arrive_expect_tx(&full[s], STAGEB + (i == 0 ? qbytes : 0u));
+                        if (i == 0)
+                            bulk_g2s(qslots + s * L::QSLOT, un.it.q + static_cast<size_t>(qa) * HD, qbytes, &full[s]);
                         for (uint32_t c = 0; c < HC * (HD / 64); ++c) {   // HC heads, 64 dims per box
-                            const int32_t x = static_cast<int32_t>(kg * HC * HD + c * 64);
+                            const int32_t x = static_cast<int32_t>(un.kg * HC * HD + c * 64);
                             tma_load_2d(kdst + c * TOK * 128, &kmap, x, krow0 + static_cast<int32_t>(tile0), &full[s]);
                             tma_load_2d(vdst + c * TOK * 128, &vmap, x, vrow0 + static_cast<int32_t>(tile0), &full[s]);
                         }
@@ -292,304 +355,352 @@ __global__ void __launch_bounds__(DecodeCfg<HD>::THREADS, 1)
                         bulk_g2s(vdst + r * RS, vb + off, ROWB, &full[s]);
                     }
                 }
-                issued = i + 1;
             }
-            // No copy of this unit may still be in flight when the unit ends.
-            for (uint32_t i = (issued > static_cast<uint32_t>(C::NST) ? issued - C::NST : 0); i < issued; ++i) {
-                const uint32_t gi = tb + i;
-                volatile int dummy = 0;
-                mbar_wait_bounded(&full[gi % C::NST], (gi / C::NST) & 1u, p.status, ST_DECODE_FULL_TIMEOUT, &dummy);
-            }
-        } else {
-            // Consumer work of the unit; a return ends the unit for the calling
-            // thread (every return below is uniform across the consumer warps).
-            [&]() {
-            // ================= consumers =================
-            const uint32_t hl = warp % HC;                 // head within the group
-            const uint32_t sl = warp / HC;                 // 16-token slice of each stage
-            const uint32_t gfirst = s_gfirst[hl], gcnt = s_gcnt[hl];
-            const int g8 = lane >> 2;                      // fragment row group: token (S^T), dim (O^T), head (B)
-            const int t4 = lane & 3;                       // fragment column pair: heads 2*t4, 2*t4+1
-            // Q^T as the MMA B operand: b0 = q[head g8][16kk + 2t4 .. +1], b1 = q[head g8][16kk + 2t4 + 8 .. +9]
-            uint32_t qhi[KS][2], qlo[KS][2];
-            {
-                const bool hv = static_cast<uint32_t>(g8) < gcnt;
-                const float* qh = it.q + static_cast<size_t>(gfirst + (hv ? g8 : 0)) * HD;
-        #pragma unroll
-                for (int kk = 0; kk < KS; ++kk) {
-                    float2 x0 = make_float2(0.f, 0.f), x1 = make_float2(0.f, 0.f);
-                    if (hv) {
-                        x0 = *reinterpret_cast<const float2*>(qh + kk * 16 + 2 * t4);
-                        x1 = *reinterpret_cast<const float2*>(qh + kk * 16 + 2 * t4 + 8);
-                    }
-                    split_h2(x0.x, x0.y, qhi[kk][0], qlo[kk][0]);
-                    split_h2(x1.x, x1.y, qhi[kk][1], qlo[kk][1]);
-                }
-            }
-            float oc[KS][4];
-        #pragma unroll
-            for (int mt = 0; mt < KS; ++mt) oc[mt][0] = oc[mt][1] = oc[mt][2] = oc[mt][3] = 0.f;
-            float m_a = -INFINITY, m_b = -INFINITY, l_a = 0.f, l_b = 0.f;    // heads 2*t4 and 2*t4+1
-            uint8_t* pt = pt_all + warp * C::PT_BYTES;
-            const uint32_t pt_u = smem_u32(pt);
-            // ldmatrix lane addresses relative to the warp's 16-row slice of a tile
-            const uint32_t slice = (16 * sl) * RS + hl * HD * 2;
-            const uint32_t a_off = slice + ((lane & 7) + ((lane >> 3) & 1) * 8) * RS + ((lane >> 4) & 1) * 16;   // K
-            const uint32_t v_off = slice + ((lane & 7) + ((lane >> 4) & 1) * 8) * RS + ((lane >> 3) & 1) * 16;   // V^T
-            // TM: tiles are HC*HD/64 panels of [TOK rows][128 B] (head hl's panels from hl*HD/64),
-            // 16-byte chunk c of row r at c ^ (r & 7)
-            const uint32_t rk = 16 * sl + (lane & 15), rv = 16 * sl + (lane & 7) + ((lane >> 4) & 1) * 8;
-            const uint32_t hpan = hl * (HD / 64);
-            auto k_addr = [&](uint32_t kt, int kk) -> uint32_t {   // K A-fragment, k-step kk
-                if constexpr (TM)
-                    return kt + (hpan + (kk >> 2)) * TOK * 128 + rk * 128 +
-                           ((static_cast<uint32_t>(((kk & 3) << 1) + (lane >> 4)) ^ (lane & 7)) << 4);
-                else
-                    return kt + a_off + kk * 32;
-            };
-            auto v_addr = [&](uint32_t vt, int mt) -> uint32_t {   // V^T A-fragment, m-tile mt
-                if constexpr (TM)
-                    return vt + (hpan + (mt >> 2)) * TOK * 128 + rv * 128 +
-                           ((static_cast<uint32_t>(((mt & 3) << 1) + ((lane >> 3) & 1)) ^ (lane & 7)) << 4);
-                else
-                    return vt + v_off + mt * 32;
-            };
-            const uint32_t p_off = (lane & 7) * 48 + ((lane >> 3) & 1) * 16;                                     // P^T
+        }
+        // No copy may still be in flight when the CTA exits (consumers stop early on an abort).
+        for (uint32_t g = (gi > static_cast<uint32_t>(C::NST) ? gi - C::NST : 0); g < gi; ++g) {
+            volatile int dummy = 0;
+            mbar_wait_bounded(&full[g % C::NST], (g / C::NST) & 1u, p.status, ST_DECODE_FULL_TIMEOUT, &dummy);
+        }
+        return;
+    }
 
-            for (uint32_t i = 0; i < ntiles; ++i) {
-                const uint32_t gi = tb + i;
-                const int s = gi % C::NST;
-                if (!warp_wait_bounded(&full[s], (gi / C::NST) & 1u, p.status, ST_DECODE_FULL_TIMEOUT, abort_flag)) break;
-                const uint32_t nrows = min(TOK, t1 - (t0 + i * TOK));
-                const int nvalid = max(0, min(16, static_cast<int>(nrows) - static_cast<int>(16 * sl)));
-                if (nvalid > 0) {
-                    const uint32_t kt = smem_u32(stages + s * STAGEB);
-                    const uint32_t vt = kt + TILEB;
-                    // ---- S^T = K Q^T ----
-                    // four independent accumulation chains (q hi / lo x even / odd k-step),
-                    // so the MMA latency is paid KS/2 times instead of 2*KS
-                    float sc[4], sc1[4] = {0.f, 0.f, 0.f, 0.f}, sc2[4] = {0.f, 0.f, 0.f, 0.f},
-                                 sc3[4] = {0.f, 0.f, 0.f, 0.f};
-                    sc[0] = sc[1] = sc[2] = sc[3] = 0.f;
-        #pragma unroll
-                    for (int kk = 0; kk < KS; kk += 2) {
-                        uint32_t a[4], b[4];
-                        ldsm_x4(k_addr(kt, kk), a);
-                        ldsm_x4(k_addr(kt, kk + 1), b);
-                        mma16816(sc, a, qhi[kk][0], qhi[kk][1]);
-                        mma16816(sc1, b, qhi[kk + 1][0], qhi[kk + 1][1]);
-                        mma16816(sc2, a, qlo[kk][0], qlo[kk][1]);
-                        mma16816(sc3, b, qlo[kk + 1][0], qlo[kk + 1][1]);
-                    }
-        #pragma unroll
-                    for (int r = 0; r < 4; ++r) sc[r] = (sc[r] + sc1[r]) + (sc2[r] + sc3[r]);
-                    // sc: [0] = (token g8, head 2t4), [1] = (g8, 2t4+1), [2] = (g8+8, 2t4), [3] = (g8+8, 2t4+1)
-                    const bool v0 = g8 < nvalid, v1 = g8 + 8 < nvalid;
-                    const float s0 = v0 ? sc[0] * p.scale_log2 : -INFINITY;
-                    const float s1 = v0 ? sc[1] * p.scale_log2 : -INFINITY;
-                    const float s2 = v1 ? sc[2] * p.scale_log2 : -INFINITY;
-                    const float s3 = v1 ? sc[3] * p.scale_log2 : -INFINITY;
-                    float mx_a = fmaxf(s0, s2), mx_b = fmaxf(s1, s3);
-        #pragma unroll
-                    for (int o = 4; o <= 16; o <<= 1) {
-                        mx_a = fmaxf(mx_a, __shfl_xor_sync(0xffffffffu, mx_a, o));
-                        mx_b = fmaxf(mx_b, __shfl_xor_sync(0xffffffffu, mx_b, o));
-                    }
-                    const float mn_a = fmaxf(m_a, mx_a), mn_b = fmaxf(m_b, mx_b);
-                    const float al_a = ex2_approx(m_a - mn_a), al_b = ex2_approx(m_b - mn_b);
-                    const float p0 = ex2_approx(s0 - mn_a), p1 = ex2_approx(s1 - mn_b);
-                    const float p2 = ex2_approx(s2 - mn_a), p3 = ex2_approx(s3 - mn_b);
-                    float sum_a = p0 + p2, sum_b = p1 + p3;
-        #pragma unroll
-                    for (int o = 4; o <= 16; o <<= 1) {
-                        sum_a += __shfl_xor_sync(0xffffffffu, sum_a, o);
-                        sum_b += __shfl_xor_sync(0xffffffffu, sum_b, o);
-                    }
-                    l_a = l_a * al_a + sum_a;
-                    l_b = l_b * al_b + sum_b;
-                    m_a = mn_a;
-                    m_b = mn_b;
-                    // ---- P^T (rows = heads, 16 tokens, 48 B row stride) as fp16 hi and lo planes ----
-                    {
-                        uint32_t h01, l01, h23, l23;
-                        split_h2(p0, p1, h01, l01);      // (token g8: heads 2t4, 2t4+1)
-                        split_h2(p2, p3, h23, l23);      // (token g8+8: heads 2t4, 2t4+1)
-                        uint16_t* hp = reinterpret_cast<uint16_t*>(pt);
-                        uint16_t* lp = reinterpret_cast<uint16_t*>(pt + 384);
-                        const int ra = (2 * t4) * 24, rb = (2 * t4 + 1) * 24;   // row offsets in halves
-                        hp[ra + g8] = static_cast<uint16_t>(h01);
-                        hp[rb + g8] = static_cast<uint16_t>(h01 >> 16);
-                        hp[ra + g8 + 8] = static_cast<uint16_t>(h23);
-                        hp[rb + g8 + 8] = static_cast<uint16_t>(h23 >> 16);
-                        lp[ra + g8] = static_cast<uint16_t>(l01);
-                        lp[rb + g8] = static_cast<uint16_t>(l01 >> 16);
-                        lp[ra + g8 + 8] = static_cast<uint16_t>(l23);
-                        lp[rb + g8 + 8] = static_cast<uint16_t>(l23 >> 16);
-                    }
-                    __syncwarp();
-                    uint32_t ph0, ph1, pl0, pl1;
-                    ldsm_x2(pt_u + p_off, ph0, ph1);
-                    ldsm_x2(pt_u + 384 + p_off, pl0, pl1);
-                    // ---- O^T = O^T * alpha + V^T P^T ----
-                    // V rows past nvalid hold stale (or never written) shared memory: their
-                    // p is 0, but 0 * NaN would still poison the MMA, so zero those lanes.
-                    // The A fragment holds tokens 2t4, 2t4+1 (a0, a1) and 2t4+8, 2t4+9 (a2, a3).
-                    uint32_t vm01 = 0xffffffffu, vm23 = 0xffffffffu;
-                    if (nvalid < 16) {
-                        vm01 = (2 * t4 < nvalid ? 0x0000ffffu : 0u) | (2 * t4 + 1 < nvalid ? 0xffff0000u : 0u);
-                        vm23 = (2 * t4 + 8 < nvalid ? 0x0000ffffu : 0u) | (2 * t4 + 9 < nvalid ? 0xffff0000u : 0u);
-                    }
-        #pragma unroll
-                    for (int mt = 0; mt < KS; ++mt) {
-                        oc[mt][0] *= al_a;
-                        oc[mt][1] *= al_b;
-                        oc[mt][2] *= al_a;
-                        oc[mt][3] *= al_b;
-                        uint32_t a[4];
-                        ldsm_x4_t(v_addr(vt, mt), a);
-                        a[0] &= vm01;
-                        a[1] &= vm01;
-                        a[2] &= vm23;
-                        a[3] &= vm23;
-                        mma16816(oc[mt], a, ph0, ph1);
-                        mma16816(oc[mt], a, pl0, pl1);
-                    }
-                    __syncwarp();   // P^T is rewritten by the next step
+    // ================= consumers =================
+    const uint32_t hl = warp % HC;                 // head within the group
+    const uint32_t sl = warp / HC;                 // 16-token slice of each stage
+    const int g8 = lane >> 2;                      // fragment row group: token (S^T), dim (O^T), head (B)
+    const int t4 = lane & 3;                       // fragment column pair: heads 2*t4, 2*t4+1
+    const int tid = threadIdx.x;                   // 0..32*NCW-1
+    const uint32_t nsl = NCW / HC;                 // slice warps per head
+    uint8_t* pt = pt_all + warp * C::PT_BYTES;
+    const uint32_t pt_u = smem_u32(pt);
+    const uint32_t p_off = (lane & 7) * 48 + ((lane >> 3) & 1) * 16;   // P^T
+    // ldmatrix lane addresses relative to the warp's 16-row slice of a tile
+    const uint32_t slice = (16 * sl) * RS + hl * HD * 2;
+    const uint32_t a_off = slice + ((lane & 7) + ((lane >> 3) & 1) * 8) * RS + ((lane >> 4) & 1) * 16;   // K
+    const uint32_t v_off = slice + ((lane & 7) + ((lane >> 4) & 1) * 8) * RS + ((lane >> 3) & 1) * 16;   // V^T
+    // TM: tiles are HC*HD/64 panels of [TOK rows][128 B] (head hl's panels from hl*HD/64),
+    // 16-byte chunk c of row r at c ^ (r & 7)
+    const uint32_t rk = 16 * sl + (lane & 15), rv = 16 * sl + (lane & 7) + ((lane >> 4) & 1) * 8;
+    const uint32_t hpan = hl * (HD / 64);
+    auto k_addr = [&](uint32_t kt, int kk) -> uint32_t {   // K A-fragment, k-step kk
+        if constexpr (TM)
+            return kt + (hpan + (kk >> 2)) * TOK * 128 + rk * 128 +
+                   ((static_cast<uint32_t>(((kk & 3) << 1) + (lane >> 4)) ^ (lane & 7)) << 4);
+        else
+            return kt + a_off + kk * 32;
+    };
+    auto v_addr = [&](uint32_t vt, int mt) -> uint32_t {   // V^T A-fragment, m-tile mt
+        if constexpr (TM)
+            return vt + (hpan + (mt >> 2)) * TOK * 128 + rv * 128 +
+                   ((static_cast<uint32_t>(((mt & 3) << 1) + ((lane >> 3) & 1)) ^ (lane & 7)) << 4);
+        else
+            return vt + v_off + mt * 32;
+    };
+
+    uint32_t tb = 0;   // tiles of this CTA's earlier units
+    for (uint32_t u = u_begin; u < u_end; ++u) {
+        // The unit's first tile brings its descriptor (and q).  All consumer warps
+        // take the same way out if the wait gave up, so the named barriers below
+        // always see every consumer warp.
+        const int s0 = static_cast<int>(tb % C::NST);
+        const bool got = warp_wait_bounded(&full[s0], (tb / C::NST) & 1u, p.status, ST_DECODE_FULL_TIMEOUT, abort_flag);
+        if (!named_bar_and(1, 32 * NCW, got)) return;
+        const DecodeUnit un = *desc_at(s0);
+        const YattnDecodeItem& it = un.it;
+        const uint32_t kg = un.kg, t0 = un.t0, t1 = un.t1, n_splits = un.n_splits, split = un.split;
+        const uint32_t ntiles = max(1u, (t1 - t0 + TOK - 1) / TOK);
+        uint32_t gfirst, gcnt, qa, qn;
+        group_of(kg * HC + hl, p.n_heads, p.n_kv, gfirst, gcnt);
+        group_of(kg * HC, p.n_heads, p.n_kv, qa, qn);
+
+        // Q^T as the MMA B operand: b0 = q[head g8][16kk + 2t4 .. +1], b1 = q[head g8][16kk + 2t4 + 8 .. +9]
+        uint32_t qhi[KS][2], qlo[KS][2];
+        {
+            const bool hv = static_cast<uint32_t>(g8) < gcnt;
+            const float* qh = TM ? reinterpret_cast<const float*>(qslots + s0 * L::QSLOT) +
+                                       static_cast<size_t>(gfirst - qa + (hv ? g8 : 0)) * HD
+                                 : it.q + static_cast<size_t>(gfirst + (hv ? g8 : 0)) * HD;
+    #pragma unroll
+            for (int kk = 0; kk < KS; ++kk) {
+                float2 x0 = make_float2(0.f, 0.f), x1 = make_float2(0.f, 0.f);
+                if (hv) {
+                    x0 = *reinterpret_cast<const float2*>(qh + kk * 16 + 2 * t4);
+                    x1 = *reinterpret_cast<const float2*>(qh + kk * 16 + 2 * t4 + 8);
+                }
+                split_h2(x0.x, x0.y, qhi[kk][0], qlo[kk][0]);
+                split_h2(x1.x, x1.y, qhi[kk][1], qlo[kk][1]);
+            }
+        }
+        float oc[KS][4];
+    #pragma unroll
+        for (int mt = 0; mt < KS; ++mt) oc[mt][0] = oc[mt][1] = oc[mt][2] = oc[mt][3] = 0.f;
+        float m_a = -INFINITY, m_b = -INFINITY, l_a = 0.f, l_b = 0.f;    // heads 2*t4 and 2*t4+1
+
+        for (uint32_t i = 0; i < ntiles; ++i) {
+            const uint32_t gi = tb + i;
+            const int s = gi % C::NST;
+            if (i > 0 && !warp_wait_bounded(&full[s], (gi / C::NST) & 1u, p.status, ST_DECODE_FULL_TIMEOUT, abort_flag))
+                break;
+            const uint32_t tile0 = t0 + i * TOK;
+            const uint32_t nrows = tile0 < t1 ? min(TOK, t1 - tile0) : 0u;
+            const int nvalid = max(0, min(16, static_cast<int>(nrows) - static_cast<int>(16 * sl)));
+            if (nvalid > 0) {
+                const uint32_t kt = smem_u32(stages + s * STAGEB);
+                const uint32_t vt = kt + TILEB;
+                // ---- S^T = K Q^T ----
+                // four independent accumulation chains (q hi / lo x even / odd k-step),
+                // so the MMA latency is paid KS/2 times instead of 2*KS
+                float sc[4], sc1[4] = {0.f, 0.f, 0.f, 0.f}, sc2[4] = {0.f, 0.f, 0.f, 0.f},
+                             sc3[4] = {0.f, 0.f, 0.f, 0.f};
+                sc[0] = sc[1] = sc[2] = sc[3] = 0.f;
+    #pragma unroll
+                for (int kk = 0; kk < KS; kk += 2) {
+                    uint32_t a[4], b[4];
+                    ldsm_x4(k_addr(kt, kk), a);
+                    ldsm_x4(k_addr(kt, kk + 1), b);
+                    mma16816(sc, a, qhi[kk][0], qhi[kk][1]);
+                    mma16816(sc1, b, qhi[kk + 1][0], qhi[kk + 1][1]);
+                    mma16816(sc2, a, qlo[kk][0], qlo[kk][1]);
+                    mma16816(sc3, b, qlo[kk + 1][0], qlo[kk + 1][1]);
+                }
+    #pragma unroll
+                for (int r = 0; r < 4; ++r) sc[r] = (sc[r] + sc1[r]) + (sc2[r] + sc3[r]);
+                // sc: [0] = (token g8, head 2t4), [1] = (g8, 2t4+1), [2] = (g8+8, 2t4), [3] = (g8+8, 2t4+1)
+                const bool v0 = g8 < nvalid, v1 = g8 + 8 < nvalid;
+                const float s0 = v0 ? sc[0] * p.scale_log2 : -INFINITY;
+                const float s1 = v0 ? sc[1] * p.scale_log2 : -INFINITY;
+                const float s2 = v1 ? sc[2] * p.scale_log2 : -INFINITY;
+                const float s3 = v1 ? sc[3] * p.scale_log2 : -INFINITY;
+                float mx_a = fmaxf(s0, s2), mx_b = fmaxf(s1, s3);
+    #pragma unroll
+                for (int o = 4; o <= 16; o <<= 1) {
+                    mx_a = fmaxf(mx_a, __shfl_xor_sync(0xffffffffu, mx_a, o));
+                    mx_b = fmaxf(mx_b, __shfl_xor_sync(0xffffffffu, mx_b, o));
+                }
+                const float mn_a = fmaxf(m_a, mx_a), mn_b = fmaxf(m_b, mx_b);
+                const float al_a = ex2_approx(m_a - mn_a), al_b = ex2_approx(m_b - mn_b);
+                const float p0 = ex2_approx(s0 - mn_a), p1 = ex2_approx(s1 - mn_b);
+                const float p2 = ex2_approx(s2 - mn_a), p3 = ex2_approx(s3 - mn_b);
+                float sum_a = p0 + p2, sum_b = p1 + p3;
+    #pragma unroll
+                for (int o = 4; o <= 16; o <<= 1) {
+                    sum_a += __shfl_xor_sync(0xffffffffu, sum_a, o);
+                    sum_b += __shfl_xor_sync(0xffffffffu, sum_b, o);
+                }
+                l_a = l_a * al_a + sum_a;
+                l_b = l_b * al_b + sum_b;
+                m_a = mn_a;
+                m_b = mn_b;
+                // ---- P^T (rows = heads, 16 tokens, 48 B row stride) as fp16 hi and lo planes ----
+                {
+                    uint32_t h01, l01, h23, l23;
+                    split_h2(p0, p1, h01, l01);      // (token g8: heads 2t4, 2t4+1)
+                    split_h2(p2, p3, h23, l23);      // (token g8+8: heads 2t4, 2t4+1)
+                    uint16_t* hp = reinterpret_cast<uint16_t*>(pt);
+                    uint16_t* lp = reinterpret_cast<uint16_t*>(pt + 384);
+                    const int ra = (2 * t4) * 24, rb = (2 * t4 + 1) * 24;   // row offsets in halves
+                    hp[ra + g8] = static_cast<uint16_t>(h01);
+                    hp[rb + g8] = static_cast<uint16_t>(h01 >> 16);
+                    hp[ra + g8 + 8] = static_cast<uint16_t>(h23);
+                    hp[rb + g8 + 8] = static_cast<uint16_t>(h23 >> 16);
+                    lp[ra + g8] = static_cast<uint16_t>(l01);
+                    lp[rb + g8] = static_cast<uint16_t>(l01 >> 16);
+                    lp[ra + g8 + 8] = static_cast<uint16_t>(l23);
+                    lp[rb + g8 + 8] = static_cast<uint16_t>(l23 >> 16);
                 }
                 __syncwarp();
-                if (lane == 0) mbar_arrive(&empty[s]);
-            }
-
-            // ---- merge the consumer warps (ring is free: every stage was consumed) ----
-            // No early exit on the abort flag here: every consumer warp must reach the
-            // same named barriers (a timed-out unit just writes meaningless partials).
-            named_bar_sync(1, 32 * NCW);
-            {
-                const int ha = 2 * t4, hb = 2 * t4 + 1;
-                if (g8 == 0) {
-                    if (ha < G) {
-                        mrg_ml[(warp * G + ha) * 2 + 0] = m_a;
-                        mrg_ml[(warp * G + ha) * 2 + 1] = l_a;
-                    }
-                    if (hb < G) {
-                        mrg_ml[(warp * G + hb) * 2 + 0] = m_b;
-                        mrg_ml[(warp * G + hb) * 2 + 1] = l_b;
-                    }
+                uint32_t ph0, ph1, pl0, pl1;
+                ldsm_x2(pt_u + p_off, ph0, ph1);
+                ldsm_x2(pt_u + 384 + p_off, pl0, pl1);
+                // ---- O^T = O^T * alpha + V^T P^T ----
+                // V rows past nvalid hold stale (or never written) shared memory: their
+                // p is 0, but 0 * NaN would still poison the MMA, so zero those lanes.
+                // The A fragment holds tokens 2t4, 2t4+1 (a0, a1) and 2t4+8, 2t4+9 (a2, a3).
+                uint32_t vm01 = 0xffffffffu, vm23 = 0xffffffffu;
+                if (nvalid < 16) {
+                    vm01 = (2 * t4 < nvalid ? 0x0000ffffu : 0u) | (2 * t4 + 1 < nvalid ? 0xffff0000u : 0u);
+                    vm23 = (2 * t4 + 8 < nvalid ? 0x0000ffffu : 0u) | (2 * t4 + 9 < nvalid ? 0xffff0000u : 0u);
                 }
-        #pragma unroll
+    #pragma unroll
                 for (int mt = 0; mt < KS; ++mt) {
-                    const int d0 = mt * 16 + g8, d1 = d0 + 8;
-                    if (ha < G) {
-                        mrg_o[(warp * G + ha) * HD + d0] = oc[mt][0];
-                        mrg_o[(warp * G + ha) * HD + d1] = oc[mt][2];
-                    }
-                    if (hb < G) {
-                        mrg_o[(warp * G + hb) * HD + d0] = oc[mt][1];
-                        mrg_o[(warp * G + hb) * HD + d1] = oc[mt][3];
-                    }
+                    oc[mt][0] *= al_a;
+                    oc[mt][1] *= al_b;
+                    oc[mt][2] *= al_a;
+                    oc[mt][3] *= al_b;
+                    uint32_t a[4];
+                    ldsm_x4_t(v_addr(vt, mt), a);
+                    a[0] &= vm01;
+                    a[1] &= vm01;
+                    a[2] &= vm23;
+                    a[3] &= vm23;
+                    mma16816(oc[mt], a, ph0, ph1);
+                    mma16816(oc[mt], a, pl0, pl1);
                 }
+                __syncwarp();   // P^T is rewritten by the next step
             }
-            named_bar_sync(1, 32 * NCW);
+            __syncwarp();
+            // the last tile's stage is released after the merge below has used it
+            if (lane == 0 && i + 1 < ntiles) mbar_arrive(&empty[s]);
+        }
 
-            const int tid = threadIdx.x;   // 0..32*NCW-1
-            const bool single = n_splits == 1;   // this CTA holds the whole key range of its (item, head group)
-            const uint32_t nsl = NCW / HC;       // slice warps per head
-            for (int e = tid; e < static_cast<int>(HC * G * HD); e += 32 * NCW) {
-                const uint32_t h = e / (G * HD), g = (e / HD) % G, d = e % HD;
-                if (g >= s_gcnt[h]) continue;
-                float M = -INFINITY;
-                for (uint32_t j = 0; j < nsl; ++j) M = fmaxf(M, mrg_ml[((h + j * HC) * G + g) * 2]);
-                float o = 0.f, l = 0.f;
-                for (uint32_t j = 0; j < nsl; ++j) {
-                    const uint32_t w = h + j * HC;
-                    const float mw = mrg_ml[(w * G + g) * 2];
-                    const float sc = (mw == -INFINITY) ? 0.f : ex2_approx(mw - M);
-                    o += sc * mrg_o[(w * G + g) * HD + d];
-                    l += sc * mrg_ml[(w * G + g) * 2 + 1];
+        // ---- merge the consumer warps in the last tile's stage ----
+        // No early exit on the abort flag here: every consumer warp must reach the
+        // same named barriers (a timed-out unit just writes meaningless partials).
+        const int s_last = static_cast<int>((tb + ntiles - 1) % C::NST);
+        float* mrg_o = reinterpret_cast<float*>(stages + s_last * STAGEB);   // [NCW][G][HD]
+        named_bar_sync(1, 32 * NCW);
+        {
+            const int ha = 2 * t4, hb = 2 * t4 + 1;
+            if (g8 == 0) {
+                if (ha < G) {
+                    mrg_ml[(warp * G + ha) * 2 + 0] = m_a;
+                    mrg_ml[(warp * G + ha) * 2 + 1] = l_a;
                 }
-                const uint32_t hh = s_gfirst[h] + g;
-                if (single && p.partial_only) {
-                    p.out_o[static_cast<size_t>(hh) * HD + d] = o;
-                    if (d == 0) {
-                        p.out_ml[hh * 2 + 0] = M;
-                        p.out_ml[hh * 2 + 1] = l;
-                    }
-                } else if (single) {
-                    float r = o / l;
-                    if (it.gate) r *= 1.0f / (1.0f + __expf(-it.gate[static_cast<size_t>(hh) * HD + d]));
-                    it.out[static_cast<size_t>(hh) * HD + d] = r;
-                } else {
-                    const size_t slot = static_cast<size_t>(part_base + h * n_splits + split) * G + g;
-                    p.part_o[slot * HD + d] = o;
-                    if (d == 0) {
-                        p.part_ml[slot * 2 + 0] = M;
-                        p.part_ml[slot * 2 + 1] = l;
-                    }
+                if (hb < G) {
+                    mrg_ml[(warp * G + hb) * 2 + 0] = m_b;
+                    mrg_ml[(warp * G + hb) * 2 + 1] = l_b;
                 }
             }
-            if (single || p.defer_merge) return;
+    #pragma unroll
+            for (int mt = 0; mt < KS; ++mt) {
+                const int d0 = mt * 16 + g8, d1 = d0 + 8;
+                if (ha < G) {
+                    mrg_o[(warp * G + ha) * HD + d0] = oc[mt][0];
+                    mrg_o[(warp * G + ha) * HD + d1] = oc[mt][2];
+                }
+                if (hb < G) {
+                    mrg_o[(warp * G + hb) * HD + d0] = oc[mt][1];
+                    mrg_o[(warp * G + hb) * HD + d1] = oc[mt][3];
+                }
+            }
+        }
+        named_bar_sync(1, 32 * NCW);
 
-            // ---- last split of this (item, head group) merges all splits ----
-            __threadfence();
-            named_bar_sync(1, 32 * NCW);
-            if (tid == 0) {
-                const uint32_t prev = atomicAdd(&p.counters[group], 1u);
-                last_flag[0] = (prev == n_splits - 1) ? 1 : 0;
+        // One warp per output row (kv head h of the group, query head g); lane owns
+        // dims lane + 32 i.  The row's nsl slice partials are combined with
+        // log-sum-exp weights.
+        const bool single = n_splits == 1;   // this CTA holds the whole key range of its (item, head group)
+        for (uint32_t row = warp; row < HC * G; row += NCW) {
+            const uint32_t h = row / G, g = row % G;
+            uint32_t hfirst, hcnt;
+            group_of(kg * HC + h, p.n_heads, p.n_kv, hfirst, hcnt);
+            if (g >= hcnt) continue;
+            float M = -INFINITY;
+            for (uint32_t j = 0; j < nsl; ++j) M = fmaxf(M, mrg_ml[((h + j * HC) * G + g) * 2]);
+            float acc[DPL], l = 0.f;
+    #pragma unroll
+            for (int i = 0; i < DPL; ++i) acc[i] = 0.f;
+            for (uint32_t j = 0; j < nsl; ++j) {
+                const uint32_t w = h + j * HC;
+                const float mw = mrg_ml[(w * G + g) * 2];
+                const float sc = (mw == -INFINITY) ? 0.f : ex2_approx(mw - M);
+                l += sc * mrg_ml[(w * G + g) * 2 + 1];
+    #pragma unroll
+                for (int i = 0; i < DPL; ++i) acc[i] += sc * mrg_o[(w * G + g) * HD + lane + 32 * i];
             }
-            named_bar_sync(1, 32 * NCW);
-            if (!last_flag[0]) return;
-            __threadfence();
-            // One warp per (kv head, query head) row; lanes own dims lane + 32i.  The
-            // per-split loads are independent, so they are all in flight at once
-            // (a strided thread-per-element loop paid two L2 round trips per element
-            // group, tens of microseconds at the end of the grid).
-            constexpr int DPL = HD / 32;
-            for (uint32_t row = warp; row < HC * G; row += NCW) {
-                const uint32_t h = row / G, g = row % G;
-                if (g >= s_gcnt[h]) continue;
-                const size_t base = static_cast<size_t>(part_base + h * n_splits);
-                float mj = -INFINITY;
-                for (uint32_t sidx = lane; sidx < n_splits; sidx += 32)
-                    mj = fmaxf(mj, __ldcg(&p.part_ml[((base + sidx) * G + g) * 2]));
-#pragma unroll
-                for (int o = 16; o > 0; o >>= 1) mj = fmaxf(mj, __shfl_xor_sync(0xffffffffu, mj, o));
-                const float M = mj;
-                float acc[DPL], l = 0.f;
-#pragma unroll
-                for (int i = 0; i < DPL; ++i) acc[i] = 0.f;
-#pragma unroll 4
-                for (uint32_t sidx = 0; sidx < n_splits; ++sidx) {
-                    const size_t slot = (base + sidx) * G + g;
-                    const float2 mls = __ldcg(reinterpret_cast<const float2*>(&p.part_ml[slot * 2]));
-                    const float sc = ex2_approx(mls.x - M);
-                    l += sc * mls.y;
-#pragma unroll
-                    for (int i = 0; i < DPL; ++i) acc[i] += sc * __ldcg(&p.part_o[slot * HD + lane + 32 * i]);
+            const uint32_t hh = hfirst + g;
+            if (single && p.partial_only) {
+    #pragma unroll
+                for (int i = 0; i < DPL; ++i) p.out_o[static_cast<size_t>(hh) * HD + lane + 32 * i] = acc[i];
+                if (lane == 0) {
+                    p.out_ml[hh * 2 + 0] = M;
+                    p.out_ml[hh * 2 + 1] = l;
                 }
-                const uint32_t hh = s_gfirst[h] + g;
-                if (p.partial_only) {   // merged (m, l, o) of the whole range, for a cross-GPU merge
-#pragma unroll
-                    for (int i = 0; i < DPL; ++i) p.out_o[static_cast<size_t>(hh) * HD + lane + 32 * i] = acc[i];
-                    if (lane == 0) {
-                        p.out_ml[hh * 2 + 0] = M;
-                        p.out_ml[hh * 2 + 1] = l;
-                    }
-                    continue;
-                }
+            } else if (single) {
                 const float inv_l = 1.0f / l;
-#pragma unroll
+    #pragma unroll
                 for (int i = 0; i < DPL; ++i) {
                     const size_t idx = static_cast<size_t>(hh) * HD + lane + 32 * i;
                     float r = acc[i] * inv_l;
                     if (it.gate) r *= 1.0f / (1.0f + __expf(-it.gate[idx]));
                     it.out[idx] = r;
                 }
+            } else {
+                const size_t slot = static_cast<size_t>(un.part_base + h * n_splits + split) * G + g;
+    #pragma unroll
+                for (int i = 0; i < DPL; ++i) p.part_o[slot * HD + lane + 32 * i] = acc[i];
+                if (lane == 0) *reinterpret_cast<float2*>(&p.part_ml[slot * 2]) = make_float2(M, l);
             }
-            if (tid == 0) p.counters[group] = 0u;   // ready for the next launch
-            }();
         }
+        named_bar_sync(1, 32 * NCW);   // every warp is done with the merge area
+        if (lane == 0) mbar_arrive(&empty[s_last]);
         tb += ntiles;
-        __syncthreads();
+        if (single || p.defer_merge) continue;
+
+        // ---- last split of this (item, head group) merges all splits ----
+        __threadfence();
+        named_bar_sync(1, 32 * NCW);
+        if (tid == 0) {
+            const uint32_t prev = atomicAdd(&p.counters[un.group], 1u);
+            last_flag[0] = (prev == n_splits - 1) ? 1 : 0;
+        }
+        named_bar_sync(1, 32 * NCW);
+        if (!last_flag[0]) continue;
+        __threadfence();
+        // One warp per row.  The splits' (m, l) come in one load per lane (32 splits
+        // per round), their weights go to the lanes by shuffles, and the o loads of
+        // all splits are independent, so they are in flight together.
+        for (uint32_t row = warp; row < HC * G; row += NCW) {
+            const uint32_t h = row / G, g = row % G;
+            uint32_t hfirst, hcnt;
+            group_of(kg * HC + h, p.n_heads, p.n_kv, hfirst, hcnt);
+            if (g >= hcnt) continue;
+            const size_t base = static_cast<size_t>(un.part_base + h * n_splits);
+            const uint32_t hh = hfirst + g;
+            float gt[DPL];
+            if (!p.partial_only && it.gate) {   // prefetched into L2 with the unit's first tile
+    #pragma unroll
+                for (int i = 0; i < DPL; ++i) gt[i] = it.gate[static_cast<size_t>(hh) * HD + lane + 32 * i];
+            }
+            float2 ml0 = make_float2(-INFINITY, 0.f);   // (m, l) of split `lane` (first 32 splits)
+            if (static_cast<uint32_t>(lane) < n_splits) ml0 = __ldcg(reinterpret_cast<const float2*>(&p.part_ml[((base + lane) * G + g) * 2]));
+            float mj = ml0.x;
+            for (uint32_t sidx = 32 + lane; sidx < n_splits; sidx += 32)
+                mj = fmaxf(mj, __ldcg(&p.part_ml[((base + sidx) * G + g) * 2]));
+    #pragma unroll
+            for (int o = 16; o > 0; o >>= 1) mj = fmaxf(mj, __shfl_xor_sync(0xffffffffu, mj, o));
+            const float M = mj;
+            float acc[DPL], lsum = 0.f;
+    #pragma unroll
+            for (int i = 0; i < DPL; ++i) acc[i] = 0.f;
+            for (uint32_t c0 = 0; c0 < n_splits; c0 += 32) {
+                const float2 mlc = c0 == 0 ? ml0
+                                           : (c0 + lane < n_splits ? __ldcg(reinterpret_cast<const float2*>(
+                                                                          &p.part_ml[((base + c0 + lane) * G + g) * 2]))
+                                                                    : make_float2(-INFINITY, 0.f));
+                const float wl = (mlc.x == -INFINITY) ? 0.f : ex2_approx(mlc.x - M);
+                lsum += wl * mlc.y;
+                const uint32_t nc = min(32u, n_splits - c0);
+    #pragma unroll 4
+                for (uint32_t j = 0; j < nc; ++j) {
+                    const float w = __shfl_sync(0xffffffffu, wl, static_cast<int>(j));
+                    const float* po = &p.part_o[((base + c0 + j) * G + g) * HD + lane];
+    #pragma unroll
+                    for (int i = 0; i < DPL; ++i) acc[i] += w * __ldcg(po + 32 * i);
+                }
+            }
+    #pragma unroll
+            for (int o = 16; o > 0; o >>= 1) lsum += __shfl_xor_sync(0xffffffffu, lsum, o);
+            if (p.partial_only) {   // merged (m, l, o) of the whole range, for a cross-GPU merge
+    #pragma unroll
+                for (int i = 0; i < DPL; ++i) p.out_o[static_cast<size_t>(hh) * HD + lane + 32 * i] = acc[i];
+                if (lane == 0) {
+                    p.out_ml[hh * 2 + 0] = M;
+                    p.out_ml[hh * 2 + 1] = lsum;
+                }
+                continue;
+            }
+            const float inv_l = 1.0f / lsum;
+    #pragma unroll
+            for (int i = 0; i < DPL; ++i) {
+                const size_t idx = static_cast<size_t>(hh) * HD + lane + 32 * i;
+                float r = acc[i] * inv_l;
+                if (it.gate) r *= 1.0f / (1.0f + __expf(-gt[i]));
+                it.out[idx] = r;
+            }
+        }
+        if (tid == 0) p.counters[un.group] = 0u;   // ready for the next launch
     }
 }
 
@@ -688,11 +799,11 @@ __global__ void k_merge_partials(float* out, const float* ml, const float* o, ui
 template <int HD, int G, bool TM>
 int launch_t(const DecodeParams& p, const CUtensorMap& km, const CUtensorMap& vm, uint32_t grid, cudaStream_t st,
              char* err, size_t errlen) {
-    using C = DecodeCfg<HD>;
-    const size_t smem = C::NST * C::STAGE_MAX + 2 * C::NST * 8 + C::NCW * C::PT_BYTES + C::NCW * G * 2 * 4 +
-                        16 * 4 + 16 + (TM ? 1024 : 0);
-    static_assert(C::NST * C::STAGE_MAX >= C::NCW * G * HD * 4, "merge area must fit in the ring");
-    static_assert(C::STAGE_MAX >= 2 * 16 * C::NCW * HD * 2, "a TM stage fits the ring slot");
+    const size_t smem = DecodeSmem<HD, G, TM>::BYTES;
+    if (TM && p.hc > static_cast<uint32_t>(DecodeCfg<HD>::HC_TM_MAX)) {
+        set_err(err, errlen, "decode: %u kv heads per CTA with tensor copies (max %d)", p.hc, DecodeCfg<HD>::HC_TM_MAX);
+        return -1;
+    }
     static bool attr_done[64] = {};
     int dev = 0;
     cudaGetDevice(&dev);
@@ -705,7 +816,7 @@ int launch_t(const DecodeParams& p, const CUtensorMap& km, const CUtensorMap& vm
         }
         attr_done[dev] = true;
     }
-    k_decode<HD, G, TM><<<grid, C::THREADS, smem, st>>>(km, vm, p);
+    k_decode<HD, G, TM><<<grid, DecodeCfg<HD>::THREADS, smem, st>>>(km, vm, p);
     YATTN_CHECK_LAUNCH(err, errlen, "decode");
     return 0;
 }
