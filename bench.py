@@ -351,7 +351,8 @@ def run_ours(args) -> None:
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"],
                          "unit": "GB/s", "frac": round(achieved / peaks["hbm_gbs"], 4),
                          "traffic": None if (args.seqs or args.layers) else NCU_TRAFFIC["decode"],
-                         "kernel": "k_decode<128,4,TM> (pooled tensor copies)", "peak_source": peak_src,
+                         "kernel": "k_decode<128,4,TM> (pooled tensor copies)",
+                         "peak_source": peak_src,
                          "bytes_per_launch": bytes_per_launch, "launch_ms": round(launch_ms, 5)},
             "gpu_launches": args.steps * n_layers,
             "clocks": {"sm_mhz": clk["sm_mhz"], "sm_max_mhz": clk["sm_max_mhz"], "reasons": clk["reasons"],
@@ -405,7 +406,8 @@ def run_decode_small(args) -> None:
     ach = step_bytes / (per_call / 1e3) / 1e9
     G = -(-cfg.n_heads // cfg.n_kv_heads)
     roof = {"bound": "hbm", "achieved": round(ach, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
-            "frac": round(ach / peaks["hbm_gbs"], 4), "traffic": None, "kernel": f"k_decode<{cfg.head_dim},{G},TM> (pooled tensor copies)",
+            "frac": round(ach / peaks["hbm_gbs"], 4), "traffic": None,
+            "kernel": f"k_decode<{cfg.head_dim},{G},TM> (pooled tensor copies)",
             "peak_source": src, "bytes_per_step": step_bytes,
             "note": f"{d.n_layers} launches per step in one graph; achieved = step bytes / step device time"}
     e2e = None
@@ -436,7 +438,8 @@ def run_decode_small(args) -> None:
                       "ctx": cfg.ctx_hi, "gated": cfg.gated, "kv_bytes_per_step": kv_bytes * world,
                       "parallelism": f"data-parallel x{world}: a batch per GPU, no collective",
                       "launch": "CUDA graph replay of the step (device-timed value)",
-                      "l2": ("L2 flushed between timed steps (256 MB write outside the step's events)" if flush
+                      "l2": ("L2 scrubbed between timed steps outside the step's events (256 MB write, then "
+                             "256 MB read of another buffer, so no dirty scrub lines remain)" if flush
                              else "KV per step larger than L2")},
                      roof, args.steps * d.n_layers, clk, e2e, scaling="weak")
         line["dtype"] = "f32 math, fp16 KV" + (", bf16-valued q and gate" if cfg.gated else "")
@@ -504,12 +507,15 @@ def _timed(fn, args, stream, world, dist, local, graph=False, flush_l2=False):
     stream) into a CUDA graph and times its replays: the device-resident number
     for kernels shorter than the Python call that launches them.
 
-    flush_l2=True writes a 256 MB buffer (twice the L2) between timed calls,
-    outside each call's event pair, for inputs that fit in L2; the step time is
-    then the sum of the per-call device times."""
+    flush_l2=True scrubs L2 between timed calls, outside each call's event
+    pair, for inputs that fit in L2: it writes a 256 MB buffer (twice the L2),
+    then reads another 256 MB buffer, so the call starts with none of its
+    inputs in L2 and no dirty lines of the scrub left to write back during
+    it.  The step time is then the sum of the per-call device times."""
     import torch
 
     scrub = torch.empty(256 << 20, dtype=torch.uint8, device=f"cuda:{local}") if flush_l2 else None
+    scrub_rd = torch.ones(64 << 20, dtype=torch.float32, device=f"cuda:{local}") if flush_l2 else None
 
     for _ in range(args.warmup):
         fn()
@@ -535,6 +541,7 @@ def _timed(fn, args, stream, world, dist, local, graph=False, flush_l2=False):
     for a, b in ev:
         if scrub is not None:
             scrub.fill_(1)
+            scrub_rd.sum()
         a.record(stream)
         fn()
         b.record(stream)
@@ -625,7 +632,8 @@ def run_prefill(args, gated: bool) -> None:
                                 "head_dim": hd, "gated": gated, "flops": flops,
                                 "parallelism": f"data-parallel x{world}: one {S}-token prompt per GPU, no collective",
                                 "launch": "CUDA graph replay of the step (device-timed value)",
-                                "l2": "L2 flushed between timed steps (256 MB write outside the step's events)"},
+                                "l2": ("L2 scrubbed between timed steps outside the step's events (256 MB write, "
+                                       "then 256 MB read of another buffer)")},
                                roof, args.steps, clk, e2e, cpu, scaling="weak")), flush=True)
     if world > 1:
         dist.barrier()
@@ -770,8 +778,8 @@ def run_long_decode(args) -> None:
     ach = nbytes / (ms / 1e3) / 1e9
     roof = {"bound": "hbm", "achieved": round(ach, 1), "peak": peaks["hbm_gbs"] * world, "unit": "GB/s",
             "frac": round(ach / (peaks["hbm_gbs"] * world), 4), "traffic": None,
-            "kernel": "k_decode<128,4>" + ((" + k_exchange_merge" if peer else " + NCCL all-gather + merge")
-                                           if world > 1 else ""), "peak_source": src + f" x{world} GPUs"}
+            "kernel": "k_decode<128,4,TM>" + ((" + k_exchange_merge" if peer else " + NCCL all-gather + merge")
+                                              if world > 1 else ""), "peak_source": src + f" x{world} GPUs"}
     if rank == 0:
         print(json.dumps(_line(args, world, "long-context decode GB/s (131072 keys, one layer)", ach, "GB/s", ms,
                                {"workload": c.name, "ctx": n, "n_heads": H, "n_kv_heads": c.n_kv_heads,
@@ -781,7 +789,7 @@ def run_long_decode(args) -> None:
                                     if peer else "NCCL all-gather of (m,l,o) + LSE merge")),
                                 "launch": "CUDA graph replay of the step (partial decode, exchange, merge)",
                                 "l2": "KV 537 MB > L2"},
-                               roof, args.steps, clk, e2e)), flush=True)
+                               roof, args.steps * (2 if world > 1 else 1), clk, e2e)), flush=True)
     if peer:
         ex.close()
     if world > 1:

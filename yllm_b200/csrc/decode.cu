@@ -177,6 +177,27 @@ __device__ __forceinline__ DecodeUnit unit_of(const DecodeParams& p, uint32_t u,
     return x;
 }
 
+// DPL consecutive floats from global memory through L2 (written by other CTAs).
+template <int DPL> __device__ __forceinline__ void ldcg_vec(const float* src, float (&v)[DPL]) {
+    if constexpr (DPL % 4 == 0) {
+#pragma unroll
+        for (int i = 0; i < DPL; i += 4) {
+            const float4 x = __ldcg(reinterpret_cast<const float4*>(src + i));
+            v[i] = x.x;
+            v[i + 1] = x.y;
+            v[i + 2] = x.z;
+            v[i + 3] = x.w;
+        }
+    } else {
+#pragma unroll
+        for (int i = 0; i < DPL; i += 2) {
+            const float2 x = __ldcg(reinterpret_cast<const float2*>(src + i));
+            v[i] = x.x;
+            v[i + 1] = x.y;
+        }
+    }
+}
+
 // Shared-memory layout of k_decode<HD, G, TM>: the ring of NST stages, (TM) one
 // q slot per stage, the ring's barriers, one unit descriptor per stage, the
 // consumer warps' P^T staging, their (m, l) for the merge, and flags.
@@ -638,9 +659,12 @@ __global__ void __launch_bounds__(DecodeCfg<HD>::THREADS, 1)
         named_bar_sync(1, 32 * NCW);
         if (!last_flag[0]) continue;
         __threadfence();
-        // One warp per row.  The splits' (m, l) come in one load per lane (32 splits
-        // per round), their weights go to the lanes by shuffles, and the o loads of
-        // all splits are independent, so they are in flight together.
+        // One warp per row; lane owns dims [lane*DPL, +DPL).  Up to SMAX splits,
+        // every load (each split's (m, l) and o, and the gate, which the unit's
+        // first tile prefetched into L2) is issued before any is used, so a row
+        // costs one memory round trip.  More splits go 32 per round: lanes over
+        // splits for (m, l), weights to the lanes by shuffles, o loads in flight.
+        constexpr int SMAX = 16 / DPL > 4 ? 16 / DPL : 4;
         for (uint32_t row = warp; row < HC * G; row += NCW) {
             const uint32_t h = row / G, g = row % G;
             uint32_t hfirst, hcnt;
@@ -648,43 +672,64 @@ __global__ void __launch_bounds__(DecodeCfg<HD>::THREADS, 1)
             if (g >= hcnt) continue;
             const size_t base = static_cast<size_t>(un.part_base + h * n_splits);
             const uint32_t hh = hfirst + g;
+            const size_t ob = static_cast<size_t>(hh) * HD + lane * DPL;
             float gt[DPL];
-            if (!p.partial_only && it.gate) {   // prefetched into L2 with the unit's first tile
-    #pragma unroll
-                for (int i = 0; i < DPL; ++i) gt[i] = it.gate[static_cast<size_t>(hh) * HD + lane + 32 * i];
-            }
-            float2 ml0 = make_float2(-INFINITY, 0.f);   // (m, l) of split `lane` (first 32 splits)
-            if (static_cast<uint32_t>(lane) < n_splits) ml0 = __ldcg(reinterpret_cast<const float2*>(&p.part_ml[((base + lane) * G + g) * 2]));
-            float mj = ml0.x;
-            for (uint32_t sidx = 32 + lane; sidx < n_splits; sidx += 32)
-                mj = fmaxf(mj, __ldcg(&p.part_ml[((base + sidx) * G + g) * 2]));
-    #pragma unroll
-            for (int o = 16; o > 0; o >>= 1) mj = fmaxf(mj, __shfl_xor_sync(0xffffffffu, mj, o));
-            const float M = mj;
-            float acc[DPL], lsum = 0.f;
+            if (!p.partial_only && it.gate) ldcg_vec<DPL>(it.gate + ob, gt);
+            float M = -INFINITY, lsum = 0.f, acc[DPL];
     #pragma unroll
             for (int i = 0; i < DPL; ++i) acc[i] = 0.f;
-            for (uint32_t c0 = 0; c0 < n_splits; c0 += 32) {
-                const float2 mlc = c0 == 0 ? ml0
-                                           : (c0 + lane < n_splits ? __ldcg(reinterpret_cast<const float2*>(
-                                                                          &p.part_ml[((base + c0 + lane) * G + g) * 2]))
-                                                                    : make_float2(-INFINITY, 0.f));
-                const float wl = (mlc.x == -INFINITY) ? 0.f : ex2_approx(mlc.x - M);
-                lsum += wl * mlc.y;
-                const uint32_t nc = min(32u, n_splits - c0);
-    #pragma unroll 4
-                for (uint32_t j = 0; j < nc; ++j) {
-                    const float w = __shfl_sync(0xffffffffu, wl, static_cast<int>(j));
-                    const float* po = &p.part_o[((base + c0 + j) * G + g) * HD + lane];
+            if (n_splits <= static_cast<uint32_t>(SMAX)) {
+                float2 ml[SMAX];
+                float o[SMAX][DPL];
     #pragma unroll
-                    for (int i = 0; i < DPL; ++i) acc[i] += w * __ldcg(po + 32 * i);
+                for (int sx = 0; sx < SMAX; ++sx) {
+                    if (static_cast<uint32_t>(sx) < n_splits) {
+                        const size_t slot = (base + sx) * G + g;
+                        ml[sx] = __ldcg(reinterpret_cast<const float2*>(&p.part_ml[slot * 2]));
+                        ldcg_vec<DPL>(&p.part_o[slot * HD + lane * DPL], o[sx]);
+                    }
                 }
-            }
     #pragma unroll
-            for (int o = 16; o > 0; o >>= 1) lsum += __shfl_xor_sync(0xffffffffu, lsum, o);
+                for (int sx = 0; sx < SMAX; ++sx)
+                    if (static_cast<uint32_t>(sx) < n_splits) M = fmaxf(M, ml[sx].x);
+    #pragma unroll
+                for (int sx = 0; sx < SMAX; ++sx) {
+                    if (static_cast<uint32_t>(sx) < n_splits) {
+                        const float w = (ml[sx].x == -INFINITY) ? 0.f : ex2_approx(ml[sx].x - M);
+                        lsum += w * ml[sx].y;
+    #pragma unroll
+                        for (int i = 0; i < DPL; ++i) acc[i] += w * o[sx][i];
+                    }
+                }
+            } else {
+                float mj = -INFINITY;
+                for (uint32_t sidx = lane; sidx < n_splits; sidx += 32)
+                    mj = fmaxf(mj, __ldcg(&p.part_ml[((base + sidx) * G + g) * 2]));
+    #pragma unroll
+                for (int o = 16; o > 0; o >>= 1) mj = fmaxf(mj, __shfl_xor_sync(0xffffffffu, mj, o));
+                M = mj;
+                for (uint32_t c0 = 0; c0 < n_splits; c0 += 32) {
+                    const float2 mlc = c0 + lane < n_splits ? __ldcg(reinterpret_cast<const float2*>(
+                                                                   &p.part_ml[((base + c0 + lane) * G + g) * 2]))
+                                                             : make_float2(-INFINITY, 0.f);
+                    const float wl = (mlc.x == -INFINITY) ? 0.f : ex2_approx(mlc.x - M);
+                    lsum += wl * mlc.y;
+                    const uint32_t nc = min(32u, n_splits - c0);
+    #pragma unroll 4
+                    for (uint32_t j = 0; j < nc; ++j) {
+                        const float w = __shfl_sync(0xffffffffu, wl, static_cast<int>(j));
+                        float o[DPL];
+                        ldcg_vec<DPL>(&p.part_o[((base + c0 + j) * G + g) * HD + lane * DPL], o);
+    #pragma unroll
+                        for (int i = 0; i < DPL; ++i) acc[i] += w * o[i];
+                    }
+                }
+    #pragma unroll
+                for (int o = 16; o > 0; o >>= 1) lsum += __shfl_xor_sync(0xffffffffu, lsum, o);
+            }
             if (p.partial_only) {   // merged (m, l, o) of the whole range, for a cross-GPU merge
     #pragma unroll
-                for (int i = 0; i < DPL; ++i) p.out_o[static_cast<size_t>(hh) * HD + lane + 32 * i] = acc[i];
+                for (int i = 0; i < DPL; ++i) p.out_o[ob + i] = acc[i];
                 if (lane == 0) {
                     p.out_ml[hh * 2 + 0] = M;
                     p.out_ml[hh * 2 + 1] = lsum;
@@ -694,10 +739,9 @@ __global__ void __launch_bounds__(DecodeCfg<HD>::THREADS, 1)
             const float inv_l = 1.0f / lsum;
     #pragma unroll
             for (int i = 0; i < DPL; ++i) {
-                const size_t idx = static_cast<size_t>(hh) * HD + lane + 32 * i;
                 float r = acc[i] * inv_l;
                 if (it.gate) r *= 1.0f / (1.0f + __expf(-gt[i]));
-                it.out[idx] = r;
+                it.out[ob + i] = r;
             }
         }
         if (tid == 0) p.counters[un.group] = 0u;   // ready for the next launch
