@@ -86,6 +86,25 @@ int encode_kv_map(CUtensorMap* map, const void* base, uint32_t kv_dim, uint64_t 
     return 0;
 }
 
+int encode_f32_store_map(CUtensorMap* map, void* base, uint32_t cols, uint32_t stride_elems, uint64_t n_rows,
+                         uint32_t box_rows, char* err, size_t errlen) {
+    auto enc = get_encode(err, errlen);
+    if (!enc) return -1;
+    cuuint64_t dims[2] = {cols, n_rows};
+    cuuint64_t strides[1] = {static_cast<cuuint64_t>(stride_elems) * 4};
+    cuuint32_t box[2] = {32, box_rows};
+    cuuint32_t estr[2] = {1, 1};
+    CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, base, dims, strides, box, estr,
+                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) {
+        set_err(err, errlen, "cuTensorMapEncodeTiled (fp32 store map) failed (%d): %u cols, stride %u, %llu rows",
+                static_cast<int>(r), cols, stride_elems, static_cast<unsigned long long>(n_rows));
+        return -1;
+    }
+    return 0;
+}
+
 int dev_num_sms() {
     int dev = 0, sms = 0;
     if (cudaGetDevice(&dev) != cudaSuccess) return 148;

@@ -115,7 +115,8 @@ __device__ __forceinline__ uint32_t h2_bits(__half2 h) { return *reinterpret_cas
 
 template <int HD>
 __global__ void __launch_bounds__(kPThreads, PCfg<HD>::MIN_BLOCKS)
-    k_prefill(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV, const PrefillParams p) {
+    k_prefill(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
+              const __grid_constant__ CUtensorMap tmO, const PrefillParams p) {
     using C = PCfg<HD>;
     constexpr int BN = C::BN;
     constexpr int KST = C::KST;
@@ -235,10 +236,10 @@ __global__ void __launch_bounds__(kPThreads, PCfg<HD>::MIN_BLOCKS)
         // ================= softmax warps 0-3 =================
         const int r = threadIdx.x;                                   // row of the tile
         // ---- Q tile: fp32 -> fp16, swizzled K-major ----
-        // 16 independent float4 loads in flight per thread, so the tile costs a few
-        // memory latencies rather than one per float4.
+        // up to 32 independent float4 loads in flight per thread (the whole tile at
+        // head_dim <= 128), so the tile costs one or two memory latencies.
         constexpr int C4 = HD / 4;
-        constexpr int QITER = BM * C4 / 128, QB = 16;
+        constexpr int QITER = BM * C4 / 128, QB = QITER < 32 ? QITER : 32;
         static_assert(QITER % QB == 0, "Q batches");
         for (int i0 = 0; i0 < QITER; i0 += QB) {
             float4 v[QB];
@@ -353,32 +354,63 @@ __global__ void __launch_bounds__(kPThreads, PCfg<HD>::MIN_BLOCKS)
         // the last PV's completion, on a barrier of its own
         if (ok && warp_wait_bounded(&bars->o_done, 0, p.status, ST_PREFILL_TIMEOUT, abort_flag)) {
             tc_fence_after();
-            const uint32_t b = row0 + r;
             const float inv_l = 1.0f / l_run;
+            if (!p.gate) {
+                // Each warp stages 32 rows x 32 columns at a time in a 128-byte-swizzled box
+                // inside the Q buffer (free: every S product has completed) and one lane
+                // stores the box with a tensor copy, so the rows go out as whole 128-byte
+                // segments instead of one 16-byte piece per row per store; rows past B are
+                // clipped by the map.  NBOX boxes per warp rotate.
+                constexpr int WSTG = C::Q_BYTES / 4;                 // this warp's quarter of the Q buffer
+                constexpr int NBOX = WSTG / (32 * 128);
+                uint8_t* stg = sQ + warp * WSTG;
 #pragma unroll 1
-            for (int c = 0; c < HD / 32; ++c) {
-                uint32_t rr[32];
-                tmem_ld32(trow + C::COL_O + c * 32, rr);
-                tmem_wait_ld();
-                if (b < p.B) {
-                    float* dst = p.out + static_cast<size_t>(b) * p.q_stride + static_cast<size_t>(hh) * HD + c * 32;
-                    const float* g = p.gate ? p.gate + static_cast<size_t>(b) * p.q_stride +
-                                                   static_cast<size_t>(hh) * HD + c * 32
-                                            : nullptr;
+                for (int c = 0; c < HD / 32; ++c) {
+                    uint8_t* box = stg + (c % NBOX) * (32 * 128);
+                    if (c >= NBOX) {   // the store issued from this box NBOX boxes ago has read it
+                        if (lane == 0) bulk_wait_group_read<NBOX - 1>();
+                        __syncwarp();
+                    }
+                    uint32_t rr[32];
+                    tmem_ld32(trow + C::COL_O + c * 32, rr);
+                    tmem_wait_ld();
 #pragma unroll
-                    for (int i = 0; i < 32; i += 4) {
+                    for (int k4 = 0; k4 < 8; ++k4) {
                         float4 o;
-                        o.x = __uint_as_float(rr[i]) * inv_l;
-                        o.y = __uint_as_float(rr[i + 1]) * inv_l;
-                        o.z = __uint_as_float(rr[i + 2]) * inv_l;
-                        o.w = __uint_as_float(rr[i + 3]) * inv_l;
-                        if (g) {
-                            o.x *= 1.0f / (1.0f + __expf(-g[i]));
-                            o.y *= 1.0f / (1.0f + __expf(-g[i + 1]));
-                            o.z *= 1.0f / (1.0f + __expf(-g[i + 2]));
-                            o.w *= 1.0f / (1.0f + __expf(-g[i + 3]));
+                        o.x = __uint_as_float(rr[k4 * 4]) * inv_l;
+                        o.y = __uint_as_float(rr[k4 * 4 + 1]) * inv_l;
+                        o.z = __uint_as_float(rr[k4 * 4 + 2]) * inv_l;
+                        o.w = __uint_as_float(rr[k4 * 4 + 3]) * inv_l;
+                        *reinterpret_cast<float4*>(box + lane * 128 + ((k4 ^ (lane & 7)) << 4)) = o;
+                    }
+                    fence_proxy_async_smem();
+                    __syncwarp();
+                    if (lane == 0) {
+                        tma_store_2d(&tmO, box, static_cast<int32_t>(hh * HD + c * 32),
+                                     static_cast<int32_t>(row0 + warp * 32));
+                        bulk_commit_group();
+                    }
+                }
+                if (lane == 0) bulk_wait_group<0>();   // every staged store has landed
+            } else {
+                const uint32_t b = row0 + r;
+#pragma unroll 1
+                for (int c = 0; c < HD / 32; ++c) {
+                    uint32_t rr[32];
+                    tmem_ld32(trow + C::COL_O + c * 32, rr);
+                    tmem_wait_ld();
+                    if (b < p.B) {
+                        float* dst = p.out + static_cast<size_t>(b) * p.q_stride + static_cast<size_t>(hh) * HD + c * 32;
+                        const float* g = p.gate + static_cast<size_t>(b) * p.q_stride + static_cast<size_t>(hh) * HD + c * 32;
+#pragma unroll
+                        for (int i = 0; i < 32; i += 4) {
+                            float4 o;
+                            o.x = __uint_as_float(rr[i]) * inv_l / (1.0f + __expf(-g[i]));
+                            o.y = __uint_as_float(rr[i + 1]) * inv_l / (1.0f + __expf(-g[i + 1]));
+                            o.z = __uint_as_float(rr[i + 2]) * inv_l / (1.0f + __expf(-g[i + 2]));
+                            o.w = __uint_as_float(rr[i + 3]) * inv_l / (1.0f + __expf(-g[i + 3]));
+                            *reinterpret_cast<float4*>(dst + i) = o;
                         }
-                        *reinterpret_cast<float4*>(dst + i) = o;
                     }
                 }
             }
@@ -412,7 +444,9 @@ int launch_prefill(const CUtensorMap& mk, const CUtensorMap& mv, const PrefillPa
     const uint32_t sms = static_cast<uint32_t>(dev_num_sms());
     q.n_qt = n_qtiles;
     q.heavy = (C::DUAL && n_tiles <= 2 * sms) ? std::min(n_tiles, sms) : n_tiles;
-    k_prefill<HD><<<n_tiles, kPThreads, C::SMEM, st>>>(mk, mv, q);
+    CUtensorMap mo;   // out as fp32 rows of q_stride, for the epilogue's tensor-copy stores
+    if (encode_f32_store_map(&mo, p.out, p.n_heads * HD, p.q_stride, p.B, 32, err, errlen)) return -1;
+    k_prefill<HD><<<n_tiles, kPThreads, C::SMEM, st>>>(mk, mv, mo, q);
     YATTN_CHECK_LAUNCH(err, errlen, "prefill");
     return 0;
 }

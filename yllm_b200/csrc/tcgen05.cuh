@@ -11,6 +11,12 @@ namespace yattn {
 int encode_kv_map(CUtensorMap* map, const void* base, uint32_t kv_dim, uint64_t n_rows, uint32_t box_rows, char* err,
                   size_t errlen);
 
+// Host: 2-D tensor map over fp32 rows of `cols` elements (row stride stride_elems*4 B,
+// a multiple of 16), n_rows rows from base; box 32 elements (128 B) x box_rows rows,
+// 128-byte swizzle.  Used for stores: rows and columns outside the map are not written.
+int encode_f32_store_map(CUtensorMap* map, void* base, uint32_t cols, uint32_t stride_elems, uint64_t n_rows,
+                         uint32_t box_rows, char* err, size_t errlen);
+
 // ----------------------------------------------------------------- TMA (tensor)
 
 // 2-D tiled load of one box into shared memory, completion on an mbarrier.
@@ -22,6 +28,24 @@ __device__ __forceinline__ void tma_load_2d(void* dst_smem, const CUtensorMap* m
         "[%4];" ::"r"(smem_u32(dst_smem)),
         "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
         : "memory");
+}
+
+// 2-D tiled store of one box from shared memory (bulk-group completion).  The
+// coordinates must not be negative; x times the element size is a multiple of 16.
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, const void* src_smem, int32_t x, int32_t y) {
+    asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.tile.bulk_group [%0, {%1, %2}], [%3];" ::"l"(
+                     reinterpret_cast<uint64_t>(map)),
+                 "r"(x), "r"(y), "r"(smem_u32(src_smem))
+                 : "memory");
+}
+__device__ __forceinline__ void bulk_commit_group() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// Wait until at most N committed bulk groups still read shared memory.
+template <int N> __device__ __forceinline__ void bulk_wait_group_read() {
+    asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
+}
+// Wait until at most N committed bulk groups are still in flight (writes done).
+template <int N> __device__ __forceinline__ void bulk_wait_group() {
+    asm volatile("cp.async.bulk.wait_group %0;" ::"n"(N) : "memory");
 }
 
 __device__ __forceinline__ void prefetch_tensormap(const CUtensorMap* map) {
