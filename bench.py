@@ -43,7 +43,7 @@ def load_peaks() -> tuple[dict, str]:
 # from one ncu capture of exactly the launch the bench times (the commands and the
 # rest of those captures are summarised under profiles/).  Workloads without such a
 # capture report null.
-NCU_TRAFFIC = {"decode": 1226090496, "prefill": 25236992}
+NCU_TRAFFIC = {"decode": 1226090496, "prefill": 25245696}
 
 
 class ClockSampler:
