@@ -7,22 +7,24 @@
 // hh*n_kv/n_heads; out has q's layout.  Optional qwen35 sigmoid output gate
 // (engine.c:958-960).
 //
-// One CTA = one (query head, 128-row query tile), heaviest tiles first (with
-// two CTAs per SM the 1-D grid would instead pair the heaviest tiles with the
-// lightest).  Warps:
-//   0-3  softmax: thread i owns query row i = TMEM lane i.  Loads the fp32 Q
-//        tile once (-> fp16, SWIZZLE_128B K-major in smem).  Per key block it
-//        reads S from TMEM, applies the causal mask (diagonal blocks only) and
-//        the online softmax in the log2 domain (the running max only moves when
-//        it grows by more than 2^8, so O in TMEM is rarely rescaled), and writes
-//        P back over its own S columns as two fp16 planes P_hi + P_lo
-//        (P_lo = fp16(p - P_hi), ~22 bits instead of fp16's 11).
-//   4    TMA for K blocks, 6 TMA for V blocks: separate rings, no multicast.
-//   5    MMA: one thread issues S(j) = Q K(j)^T (A, B from smem) into a ring of
-//        NSB TMEM S buffers (2 at head_dim <= 128, 3 at 256) and O += P_hi V +
-//        P_lo V with A = P read straight from TMEM (B = V from smem).  S runs up
-//        to NSB blocks ahead of the softmax; the tensor core runs its MMAs in
-//        issue order, so S(j+NSB) cannot overwrite P(j) before PV(j) has read it.
+// One CTA = one (query head, 128-row query tile), heaviest tiles first.  Warps:
+//   0-7  softmax: row i of the tile (TMEM lane i) belongs to warps i/32 and
+//        i/32 + 4, which split each key block's columns in halves.  They load
+//        the fp32 Q tile once (-> fp16, SWIZZLE_128B K-major in smem).  Per key
+//        block each reads its half of S from TMEM, applies the causal mask
+//        (diagonal blocks only), and the two halves of a row combine their
+//        maxima through shared memory; the online softmax runs in the log2
+//        domain (the running max only moves when it grows by more than 2^8, so
+//        O in TMEM is rarely rescaled).  Each writes P back over the S columns
+//        it has read as two fp16 planes P_hi + P_lo (P_lo = fp16(p - P_hi),
+//        ~22 bits instead of fp16's 11), 16 columns of each per 32-key chunk.
+//        Each half keeps its own partial row sum; the epilogue adds them.
+//   8    TMA for K blocks, 10 TMA for V blocks: separate rings, no multicast.
+//   9    MMA: one thread issues S(j) = Q K(j)^T (A, B from smem) into a ring of
+//        three TMEM S buffers and O += P_hi V + P_lo V with A = P read straight
+//        from TMEM (B = V from smem).  S runs up to three blocks ahead of the
+//        softmax; the tensor core runs its MMAs in issue order, so S(j+3)
+//        cannot overwrite P(j) before PV(j) has read it.
 // Keys past the end of the cache are zero-filled by TMA and masked.
 #include "common.cuh"
 #include "tcgen05.cuh"
@@ -33,35 +35,30 @@ namespace yattn {
 namespace {
 
 constexpr int BM = 128;
-constexpr int kPThreads = 224;
+constexpr int kPThreads = 352;
 
-// One CTA per SM: 128-key blocks (64 at head_dim 256), three TMEM S buffers, all
-// 512 columns.  DUAL (two CTAs per SM: 64-key blocks, two S buffers, 256 columns
-// each) overlaps one CTA's prologue with the other's key loop, but measured slower
-// on config 2 (320 vs 365 TFLOP/s): its N = 64 QK products are bound by
-// shared-memory operand bandwidth and the two CTAs share one tensor pipe.
+// One CTA per SM (TMEM: all 512 columns).  128-key blocks (64 at head_dim 256),
+// three TMEM S buffers.  The V ring is one stage shallower than the K ring at
+// head_dim >= 128: V(j) is needed only by PV(j), two blocks after its slot frees.
 template <int HD> struct PCfg {
-    static constexpr bool DUAL = false;
-    static constexpr int MIN_BLOCKS = DUAL ? 2 : 1;
-    static constexpr int BN = (DUAL || HD >= 256) ? 64 : 128;
-    static constexpr int KST = DUAL ? ((HD >= 128) ? 2 : 3) : ((HD >= 256) ? 2 : 3);   // K and V ring depth
+    static constexpr int BN = HD >= 256 ? 64 : 128;
+    static constexpr int KST = HD >= 256 ? 2 : 3;           // K ring depth
+    static constexpr int VST = HD >= 128 ? 2 : 3;           // V ring depth
     static constexpr int Q_BYTES = BM * HD * 2;
     static constexpr int KV_BYTES = BN * HD * 2;            // one K (or V) block
     static constexpr int OFF_Q = 0;
     static constexpr int OFF_K = OFF_Q + Q_BYTES;
     static constexpr int OFF_V = OFF_K + KST * KV_BYTES;
-    static constexpr int OFF_BAR = OFF_V + KST * KV_BYTES;
-    // + barriers, + alignment slack; floors keep at most MIN_BLOCKS CTAs (each holding
-    // TMEM_COLS columns) resident per SM
-    static constexpr int SMEM_FLOOR = DUAL ? 78 * 1024 : 116 * 1024;
-    static constexpr int SMEM = (OFF_BAR + 256 + 1024) > SMEM_FLOOR ? (OFF_BAR + 256 + 1024) : SMEM_FLOOR;
-    static constexpr uint32_t TMEM_COLS = DUAL ? 256 : 512;
-    static constexpr int NSB = DUAL ? 2 : 3;                 // S buffers in TMEM (P is written over its S)
+    static constexpr int OFF_X = OFF_V + VST * KV_BYTES;    // [2 blocks][2 halves][BM] floats: row maxima / sums
+    static constexpr int OFF_BAR = OFF_X + 2 * 2 * BM * 4;
+    static constexpr int SMEM = OFF_BAR + 256 + 1024;       // + barriers, + alignment slack
+    static constexpr uint32_t TMEM_COLS = 512;
+    static constexpr int NSB = 3;                           // S buffers in TMEM (P is written over its S)
     static constexpr uint32_t COL_S = 0;                     // S buffer b at [b*BN, (b+1)*BN)
     static constexpr uint32_t COL_O = NSB * BN;
-    static constexpr uint32_t P_COLS = BN / 2;               // one fp16 P plane, two values per column
     static_assert(NSB * BN + HD <= static_cast<int>(TMEM_COLS), "TMEM columns");
-    static_assert(MIN_BLOCKS * SMEM <= 232448, "shared memory");
+    static_assert(SMEM <= 232448, "shared memory");
+    static_assert(KST * KV_BYTES >= 8 * 32 * 128, "the epilogue's store boxes fit in the K ring");
 };
 
 struct PrefillParams {
@@ -70,14 +67,12 @@ struct PrefillParams {
     const float* gate;
     uint32_t q_stride, pos_start, B, n_heads, n_kv;
     uint32_t n_qt;                    // 128-row query tiles
-    uint32_t heavy;                   // grid order: the first `heavy` CTAs take the heaviest tiles, the rest the
-                                      // lightest first (pairs heavy and light tiles on an SM)
     float scale_log2;
     int* status;
 };
 
-template <int KST> struct Bars {
-    uint64_t k_full[KST], k_empty[KST], v_full[KST], v_empty[KST];
+template <int KST, int VST> struct Bars {
+    uint64_t k_full[KST], k_empty[KST], v_full[VST], v_empty[VST];
     // per S buffer b: S(j) ready, P(j) written, PV(j) accumulated, for the blocks j with j % 3 == b
     uint64_t s_full[3], p_full[3], pv_done[3];
     uint64_t o_done, q_full, mma_drain;
@@ -85,18 +80,18 @@ template <int KST> struct Bars {
     int abort_flag;
 };
 
-// One TMA producer: block j of a K or V stream into a KST-deep ring.
-template <int HD>
+// One TMA producer: block j of a K or V stream into a DEPTH-deep ring.
+template <int HD, int DEPTH>
 __device__ __forceinline__ void produce(const CUtensorMap* map, uint8_t* ring, uint64_t* full, uint64_t* empty,
                                         uint32_t kvh, uint32_t nkb, int* status, volatile int* abort_flag) {
     using C = PCfg<HD>;
-    constexpr int BN = C::BN, KST = C::KST;
+    constexpr int BN = C::BN;
     prefetch_tensormap(map);
     uint32_t issued = 0;
     for (uint32_t j = 0; j < nkb; ++j) {
-        const int s = j % KST;
-        if (j >= static_cast<uint32_t>(KST) &&
-            !mbar_wait_bounded(&empty[s], ((j / KST) & 1u) ^ 1u, status, ST_PREFILL_TIMEOUT, abort_flag))
+        const int s = j % DEPTH;
+        if (j >= static_cast<uint32_t>(DEPTH) &&
+            !mbar_wait_bounded(&empty[s], ((j / DEPTH) & 1u) ^ 1u, status, ST_PREFILL_TIMEOUT, abort_flag))
             break;
         mbar_arrive_expect_tx(&full[s], C::KV_BYTES);
 #pragma unroll
@@ -107,32 +102,34 @@ __device__ __forceinline__ void produce(const CUtensorMap* map, uint8_t* ring, u
     }
     // no load may still be landing when the CTA exits
     volatile int dummy = 0;
-    for (uint32_t j = (issued > static_cast<uint32_t>(KST) ? issued - KST : 0); j < issued; ++j)
-        mbar_wait_bounded(&full[j % KST], (j / KST) & 1u, status, ST_PREFILL_TIMEOUT, &dummy);
+    for (uint32_t j = (issued > static_cast<uint32_t>(DEPTH) ? issued - DEPTH : 0); j < issued; ++j)
+        mbar_wait_bounded(&full[j % DEPTH], (j / DEPTH) & 1u, status, ST_PREFILL_TIMEOUT, &dummy);
 }
 
 __device__ __forceinline__ uint32_t h2_bits(__half2 h) { return *reinterpret_cast<uint32_t*>(&h); }
 
 template <int HD>
-__global__ void __launch_bounds__(kPThreads, PCfg<HD>::MIN_BLOCKS)
+__global__ void __launch_bounds__(kPThreads, 1)
     k_prefill(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
               const __grid_constant__ CUtensorMap tmO, const PrefillParams p) {
     using C = PCfg<HD>;
     constexpr int BN = C::BN;
+    constexpr int HB = BN / 2;        // columns of a block per half
     constexpr int KST = C::KST;
+    constexpr int VST = C::VST;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t* sQ = smem + C::OFF_Q;
     uint8_t* sK = smem + C::OFF_K;
     uint8_t* sV = smem + C::OFF_V;
-    Bars<KST>* bars = reinterpret_cast<Bars<KST>*>(smem + C::OFF_BAR);
+    float* xch = reinterpret_cast<float*>(smem + C::OFF_X);
+    Bars<KST, VST>* bars = reinterpret_cast<Bars<KST, VST>*>(smem + C::OFF_BAR);
     volatile int* abort_flag = &bars->abort_flag;
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
-    // tile rank k in size order (heaviest first): k = blockIdx.x for the first `heavy` CTAs,
-    // then the lightest tiles first
-    const uint32_t k = blockIdx.x < p.heavy ? blockIdx.x : gridDim.x - 1 - (blockIdx.x - p.heavy);
+    // tile rank k in size order (heaviest first)
+    const uint32_t k = blockIdx.x;
     const uint32_t hh = k % p.n_heads;
     const uint32_t qt = p.n_qt - 1 - k / p.n_heads;
     const uint32_t kvh = hh * p.n_kv / p.n_heads;
@@ -146,16 +143,18 @@ __global__ void __launch_bounds__(kPThreads, PCfg<HD>::MIN_BLOCKS)
         for (int s = 0; s < KST; ++s) {
             mbar_init(&bars->k_full[s], 1);
             mbar_init(&bars->k_empty[s], 1);
+        }
+        for (int s = 0; s < VST; ++s) {
             mbar_init(&bars->v_full[s], 1);
             mbar_init(&bars->v_empty[s], 1);
         }
         for (int s = 0; s < C::NSB; ++s) {
             mbar_init(&bars->s_full[s], 1);
-            mbar_init(&bars->p_full[s], 4);
+            mbar_init(&bars->p_full[s], 8);
             mbar_init(&bars->pv_done[s], 1);
         }
         mbar_init(&bars->o_done, 1);
-        mbar_init(&bars->q_full, 4);
+        mbar_init(&bars->q_full, 8);
         mbar_init(&bars->mma_drain, 1);
         bars->abort_flag = 0;
         fence_mbar_init();
@@ -166,11 +165,11 @@ __global__ void __launch_bounds__(kPThreads, PCfg<HD>::MIN_BLOCKS)
     tc_fence_after();
     const uint32_t tmem = bars->tmem_base;
 
-    if (warp == 4) {
-        if (lane == 0) produce<HD>(&tmK, sK, bars->k_full, bars->k_empty, kvh, nkb, p.status, abort_flag);
-    } else if (warp == 6) {
-        if (lane == 0) produce<HD>(&tmV, sV, bars->v_full, bars->v_empty, kvh, nkb, p.status, abort_flag);
-    } else if (warp == 5) {
+    if (warp == 8) {
+        if (lane == 0) produce<HD, KST>(&tmK, sK, bars->k_full, bars->k_empty, kvh, nkb, p.status, abort_flag);
+    } else if (warp == 10) {
+        if (lane == 0) produce<HD, VST>(&tmV, sV, bars->v_full, bars->v_empty, kvh, nkb, p.status, abort_flag);
+    } else if (warp == 9) {
         // ================= MMA issuer =================
         if (lane == 0) {
             constexpr uint32_t IDESC_QK = idesc_f16(BM, BN, 0);
@@ -196,13 +195,14 @@ __global__ void __launch_bounds__(kPThreads, PCfg<HD>::MIN_BLOCKS)
                 umma_commit(&bars->k_empty[s]);
                 return true;
             };
-            // O += P_hi V + P_lo V with A = P(jj) read from TMEM.
+            // O += P_hi V + P_lo V with A = P(jj) read from TMEM: keys [16kk, 16kk+16) of a plane
+            // are the 8 columns at 32*(kk/2) + 16*plane + 8*(kk%2) of the block's S buffer.
             auto do_pv = [&](uint32_t jj) -> bool {
-                const int s = jj % KST;
+                const int s = jj % VST;
                 const uint32_t sb = jj % C::NSB;
                 if (!mbar_wait_bounded(&bars->p_full[sb], (jj / C::NSB) & 1u, p.status, ST_PREFILL_TIMEOUT,
                                        abort_flag) ||
-                    !mbar_wait_bounded(&bars->v_full[s], (jj / KST) & 1u, p.status, ST_PREFILL_TIMEOUT, abort_flag))
+                    !mbar_wait_bounded(&bars->v_full[s], (jj / VST) & 1u, p.status, ST_PREFILL_TIMEOUT, abort_flag))
                     return false;
                 tc_fence_after();
                 const uint32_t pcol = tmem + C::COL_S + sb * BN;
@@ -211,7 +211,7 @@ __global__ void __launch_bounds__(kPThreads, PCfg<HD>::MIN_BLOCKS)
 #pragma unroll
                     for (int kk = 0; kk < BN / 16; ++kk) {
                         const uint64_t b = sdesc_sw128(sV + s * C::KV_BYTES + kk * 16 * 128, BN * 128, 1024);
-                        umma_f16_ts(tmem + C::COL_O, pcol + plane * C::P_COLS + kk * 8, b, IDESC_PV,
+                        umma_f16_ts(tmem + C::COL_O, pcol + 32 * (kk >> 1) + 16 * plane + 8 * (kk & 1), b, IDESC_PV,
                                     (jj > 0 || plane > 0 || kk > 0) ? 1u : 0u);
                     }
                 }
@@ -232,117 +232,136 @@ __global__ void __launch_bounds__(kPThreads, PCfg<HD>::MIN_BLOCKS)
             volatile int dummy = 0;
             mbar_wait_bounded(&bars->mma_drain, 0, p.status, ST_PREFILL_TIMEOUT, &dummy);
         }
-    } else {
-        // ================= softmax warps 0-3 =================
-        const int r = threadIdx.x;                                   // row of the tile
-        // ---- Q tile: fp32 -> fp16, swizzled K-major ----
-        // up to 32 independent float4 loads in flight per thread (the whole tile at
-        // head_dim <= 128), so the tile costs one or two memory latencies.
-        constexpr int C4 = HD / 4;
-        constexpr int QITER = BM * C4 / 128, QB = QITER < 32 ? QITER : 32;
-        static_assert(QITER % QB == 0, "Q batches");
-        for (int i0 = 0; i0 < QITER; i0 += QB) {
-            float4 v[QB];
+    } else if (warp < 8) {
+        // ================= softmax warps 0-7 =================
+        const int qd = warp & 3;                                     // TMEM lane quadrant
+        const int h = warp >> 2;                                     // half of each key block's columns
+        const int r = qd * 32 + lane;                                // row of the tile
+        // ---- Q tile: fp32 -> fp16, swizzled K-major; 256 threads, up to 32 loads in flight each ----
+        {
+            constexpr int C4 = HD / 4;
+            constexpr int QITER = BM * C4 / 256, QB = QITER < 32 ? QITER : 32;
+            static_assert(QITER % QB == 0, "Q batches");
+            for (int i0 = 0; i0 < QITER; i0 += QB) {
+                float4 v[QB];
 #pragma unroll
-            for (int i = 0; i < QB; ++i) {
-                const int idx = threadIdx.x + (i0 + i) * 128;
-                const uint32_t b = row0 + idx / C4;
-                v[i] = make_float4(0.f, 0.f, 0.f, 0.f);
-                if (b < p.B)
-                    v[i] = __ldcs(reinterpret_cast<const float4*>(p.q + static_cast<size_t>(b) * p.q_stride +
-                                                                  static_cast<size_t>(hh) * HD + (idx % C4) * 4));
-            }
+                for (int i = 0; i < QB; ++i) {
+                    const int idx = threadIdx.x + (i0 + i) * 256;
+                    const uint32_t b = row0 + idx / C4;
+                    v[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+                    if (b < p.B)
+                        v[i] = __ldcs(reinterpret_cast<const float4*>(p.q + static_cast<size_t>(b) * p.q_stride +
+                                                                      static_cast<size_t>(hh) * HD + (idx % C4) * 4));
+                }
 #pragma unroll
-            for (int i = 0; i < QB; ++i) {
-                const int idx = threadIdx.x + (i0 + i) * 128;
-                uint2 pk;
-                pk.x = h2_bits(__floats2half2_rn(v[i].x, v[i].y));
-                pk.y = h2_bits(__floats2half2_rn(v[i].z, v[i].w));
-                *reinterpret_cast<uint2*>(sQ + sw128_offset(idx / C4, (idx % C4) * 4, BM)) = pk;
+                for (int i = 0; i < QB; ++i) {
+                    const int idx = threadIdx.x + (i0 + i) * 256;
+                    uint2 pk;
+                    pk.x = h2_bits(__floats2half2_rn(v[i].x, v[i].y));
+                    pk.y = h2_bits(__floats2half2_rn(v[i].z, v[i].w));
+                    *reinterpret_cast<uint2*>(sQ + sw128_offset(idx / C4, (idx % C4) * 4, BM)) = pk;
+                }
             }
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&bars->q_full);
         }
-        fence_proxy_async_smem();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&bars->q_full);
 
-        const uint32_t trow = tmem + (static_cast<uint32_t>(warp * 32) << 16);
+        const uint32_t trow = tmem + (static_cast<uint32_t>(qd * 32) << 16);
         const uint32_t qpos = qpos0 + r;
         const float sl2 = p.scale_log2;
-        float m_run = -INFINITY, l_run = 0.f;                        // m_run in scaled log2 units
+        float m_run = -INFINITY, l_run = 0.f;                        // m_run in scaled log2 units; l_run: this half
         bool ok = true;
+        // The two halves of a row meet at a named barrier once per block.  Every wait result
+        // goes through that barrier (AND-reduced), so both halves always leave together and
+        // neither is left at a barrier its partner will not reach.
         for (uint32_t j = 0; j < nkb; ++j) {
             const uint32_t sb = j % C::NSB;
-            if (!warp_wait_bounded(&bars->s_full[sb], (j / C::NSB) & 1u, p.status, ST_PREFILL_TIMEOUT, abort_flag)) {
-                ok = false;
-                break;
+            const bool got =
+                warp_wait_bounded(&bars->s_full[sb], (j / C::NSB) & 1u, p.status, ST_PREFILL_TIMEOUT, abort_flag);
+            const uint32_t scol = trow + C::COL_S + sb * BN + h * HB;  // this half's columns of S(j)
+            float sv[HB];
+            if (got) {
+                tc_fence_after();
+#pragma unroll
+                for (int c = 0; c < HB / 32; ++c) {
+                    uint32_t rr[32];
+                    tmem_ld32(scol + c * 32, rr);
+#pragma unroll
+                    for (int i = 0; i < 32; ++i) sv[c * 32 + i] = __uint_as_float(rr[i]);
+                }
+                tmem_wait_ld();
+            } else {
+#pragma unroll
+                for (int c = 0; c < HB; ++c) sv[c] = -INFINITY;
             }
-            tc_fence_after();
-            const uint32_t scol = trow + C::COL_S + sb * BN;
-            float sv[BN];
+            // ---- causal mask (diagonal blocks only), row max of raw scores over both halves ----
+            const uint32_t kbase = j * BN + h * HB;
+            if (j * BN + BN - 1 > qpos0) {
 #pragma unroll
-            for (int c = 0; c < BN / 32; ++c) {
-                uint32_t rr[32];
-                tmem_ld32(scol + c * 32, rr);
-#pragma unroll
-                for (int i = 0; i < 32; ++i) sv[c * 32 + i] = __uint_as_float(rr[i]);
-            }
-            tmem_wait_ld();
-            // ---- causal mask (diagonal blocks only), row max of raw scores ----
-            const uint32_t kbase = j * BN;
-            if (kbase + BN - 1 > qpos0) {
-#pragma unroll
-                for (int c = 0; c < BN; ++c)
+                for (int c = 0; c < HB; ++c)
                     if (kbase + c > qpos) sv[c] = -INFINITY;
             }
             float mx4[4] = {sv[0], sv[1], sv[2], sv[3]};
 #pragma unroll
-            for (int c = 4; c < BN; c += 4) {
+            for (int c = 4; c < HB; c += 4) {
                 mx4[0] = fmaxf(mx4[0], sv[c]);
                 mx4[1] = fmaxf(mx4[1], sv[c + 1]);
                 mx4[2] = fmaxf(mx4[2], sv[c + 2]);
                 mx4[3] = fmaxf(mx4[3], sv[c + 3]);
             }
-            const float mx = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3])) * sl2;
+            float* xb = xch + (j & 1) * (2 * BM);                    // two slots alternate by block parity
+            xb[h * BM + r] = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3]));
+            if (!named_bar_and(1 + qd, 64, got)) {                   // the row's two halves
+                ok = false;
+                break;
+            }
+            const float mx = fmaxf(xb[r], xb[BM + r]) * sl2;
             const float m_new = fmaxf(m_run, mx);
             const bool grow = m_new > m_run + 8.0f;                  // keep a stale max up to 2^8 headroom
             const float m_use = grow ? m_new : m_run;
             const float alpha = grow ? ex2_approx(m_run - m_use) : 1.0f;
-            // ---- p = 2^(s*scale - m): one FFMA + ex2 per element; P hi/lo into TMEM ----
+            // a row whose keys so far are all masked keeps m = -inf and gets p = 0
+            const float m_sub = (m_use == -INFINITY) ? 0.f : m_use;
+            // ---- p = 2^(s*scale - m): one FFMA + ex2 per element; P hi/lo over this half's S ----
             float rs4[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-            for (int c = 0; c < BN / 32; ++c) {   // 32 keys -> 16 packed columns per plane
+            for (int c = 0; c < HB / 32; ++c) {   // 32 keys -> 16 columns of P_hi, then 16 of P_lo
                 uint32_t hi[16], lo[16];
 #pragma unroll
                 for (int i = 0; i < 16; ++i) {
-                    const float a = ex2_approx(fmaf(sv[c * 32 + 2 * i], sl2, -m_use));
-                    const float b = ex2_approx(fmaf(sv[c * 32 + 2 * i + 1], sl2, -m_use));
+                    const float a = ex2_approx(fmaf(sv[c * 32 + 2 * i], sl2, -m_sub));
+                    const float b = ex2_approx(fmaf(sv[c * 32 + 2 * i + 1], sl2, -m_sub));
                     rs4[i & 3] += a + b;
-                    const __half2 h = __floats2half2_rn(a, b);
-                    const float2 hf = __half22float2(h);
-                    hi[i] = h2_bits(h);
+                    const __half2 hv = __floats2half2_rn(a, b);
+                    const float2 hf = __half22float2(hv);
+                    hi[i] = h2_bits(hv);
                     lo[i] = h2_bits(__floats2half2_rn(a - hf.x, b - hf.y));
                 }
-                tmem_st16(scol + c * 16, hi);
-                tmem_st16(scol + C::P_COLS + c * 16, lo);
+                tmem_st16(scol + c * 32, hi);
+                tmem_st16(scol + c * 32 + 16, lo);
             }
             l_run = l_run * alpha + ((rs4[0] + rs4[1]) + (rs4[2] + rs4[3]));
             m_run = m_use;
-            // ---- O rescale (rare): PV(j-1) must have finished accumulating ----
+            // ---- O rescale (rare), this half's columns of O: PV(j-1) must have finished ----
+            // (both halves of these rows see the same `grow`, so both come here)
             if (j >= 1 && __any_sync(0xffffffffu, grow)) {
-                if (!warp_wait_bounded(&bars->pv_done[(j - 1) % C::NSB], ((j - 1) / C::NSB) & 1u, p.status,
-                                       ST_PREFILL_TIMEOUT, abort_flag)) {
+                const bool done = warp_wait_bounded(&bars->pv_done[(j - 1) % C::NSB], ((j - 1) / C::NSB) & 1u,
+                                                    p.status, ST_PREFILL_TIMEOUT, abort_flag);
+                if (!named_bar_and(1 + qd, 64, done)) {
                     ok = false;
                     break;
                 }
                 tc_fence_after();
 #pragma unroll 1
-                for (int c = 0; c < HD / 32; ++c) {
+                for (int c = 0; c < HD / 64; ++c) {
+                    const uint32_t oc = trow + C::COL_O + h * (HD / 2) + c * 32;
                     uint32_t rr[32];
-                    tmem_ld32(trow + C::COL_O + c * 32, rr);
+                    tmem_ld32(oc, rr);
                     tmem_wait_ld();
 #pragma unroll
                     for (int i = 0; i < 32; ++i) rr[i] = __float_as_uint(__uint_as_float(rr[i]) * alpha);
-                    tmem_st32(trow + C::COL_O + c * 32, rr);
+                    tmem_st32(oc, rr);
                 }
             }
             tmem_wait_st();
@@ -350,29 +369,31 @@ __global__ void __launch_bounds__(kPThreads, PCfg<HD>::MIN_BLOCKS)
             __syncwarp();
             if (lane == 0) mbar_arrive(&bars->p_full[sb]);
         }
-        // ---- epilogue: O / l (x sigmoid(gate)) -> out ----
-        // the last PV's completion, on a barrier of its own
-        if (ok && warp_wait_bounded(&bars->o_done, 0, p.status, ST_PREFILL_TIMEOUT, abort_flag)) {
+        // ---- epilogue: O / l (x sigmoid(gate)) -> out; each half takes its HD/2 columns ----
+        // the last PV's completion, on a barrier of its own; the row sums of the two halves
+        // meet in the exchange slots (slot 0 after a barrier: the last block's maxima are read)
+        // The slot block nkb-1 did not use is free: both halves read it (block nkb-2's maxima)
+        // before they met at block nkb-1's barrier.
+        ok = ok && warp_wait_bounded(&bars->o_done, 0, p.status, ST_PREFILL_TIMEOUT, abort_flag);
+        float* xl = xch + (nkb & 1) * (2 * BM);
+        xl[h * BM + r] = l_run;
+        ok = named_bar_and(1 + qd, 64, ok);
+        if (ok) {
             tc_fence_after();
-            const float inv_l = 1.0f / l_run;
+            const float inv_l = 1.0f / (xl[r] + xl[BM + r]);
             if (!p.gate) {
-                // Each warp stages 32 rows x 32 columns at a time in a 128-byte-swizzled box
-                // inside the Q buffer (free: every S product has completed) and one lane
-                // stores the box with a tensor copy, so the rows go out as whole 128-byte
-                // segments instead of one 16-byte piece per row per store; rows past B are
-                // clipped by the map.  NBOX boxes per warp rotate.
-                constexpr int WSTG = C::Q_BYTES / 4;                 // this warp's quarter of the Q buffer
-                constexpr int NBOX = WSTG / (32 * 128);
-                uint8_t* stg = sQ + warp * WSTG;
+                // Each warp stages 32 rows x 32 columns at a time in a 128-byte-swizzled box in
+                // the K ring (every K block has been consumed) and one lane stores the box with a
+                // tensor copy, so rows go out as whole 128-byte segments; rows past B are clipped
+                // by the map.
+                uint8_t* box = sK + warp * (32 * 128);
 #pragma unroll 1
-                for (int c = 0; c < HD / 32; ++c) {
-                    uint8_t* box = stg + (c % NBOX) * (32 * 128);
-                    if (c >= NBOX) {   // the store issued from this box NBOX boxes ago has read it
-                        if (lane == 0) bulk_wait_group_read<NBOX - 1>();
-                        __syncwarp();
-                    }
+                for (int c = 0; c < HD / 64; ++c) {
+                    const int col = h * (HD / 2) + c * 32;
+                    if (lane == 0) bulk_wait_group_read<0>();         // this warp's previous box has been read
+                    __syncwarp();
                     uint32_t rr[32];
-                    tmem_ld32(trow + C::COL_O + c * 32, rr);
+                    tmem_ld32(trow + C::COL_O + col, rr);
                     tmem_wait_ld();
 #pragma unroll
                     for (int k4 = 0; k4 < 8; ++k4) {
@@ -386,8 +407,7 @@ __global__ void __launch_bounds__(kPThreads, PCfg<HD>::MIN_BLOCKS)
                     fence_proxy_async_smem();
                     __syncwarp();
                     if (lane == 0) {
-                        tma_store_2d(&tmO, box, static_cast<int32_t>(hh * HD + c * 32),
-                                     static_cast<int32_t>(row0 + warp * 32));
+                        tma_store_2d(&tmO, box, static_cast<int32_t>(hh * HD + col), static_cast<int32_t>(row0 + qd * 32));
                         bulk_commit_group();
                     }
                 }
@@ -395,20 +415,22 @@ __global__ void __launch_bounds__(kPThreads, PCfg<HD>::MIN_BLOCKS)
             } else {
                 const uint32_t b = row0 + r;
 #pragma unroll 1
-                for (int c = 0; c < HD / 32; ++c) {
+                for (int c = 0; c < HD / 64; ++c) {
+                    const int col = h * (HD / 2) + c * 32;
                     uint32_t rr[32];
-                    tmem_ld32(trow + C::COL_O + c * 32, rr);
+                    tmem_ld32(trow + C::COL_O + col, rr);
                     tmem_wait_ld();
                     if (b < p.B) {
-                        float* dst = p.out + static_cast<size_t>(b) * p.q_stride + static_cast<size_t>(hh) * HD + c * 32;
-                        const float* g = p.gate + static_cast<size_t>(b) * p.q_stride + static_cast<size_t>(hh) * HD + c * 32;
+                        float* dst = p.out + static_cast<size_t>(b) * p.q_stride + static_cast<size_t>(hh) * HD + col;
+                        const float* g = p.gate + static_cast<size_t>(b) * p.q_stride + static_cast<size_t>(hh) * HD + col;
 #pragma unroll
                         for (int i = 0; i < 32; i += 4) {
+                            const float4 gv = *reinterpret_cast<const float4*>(g + i);
                             float4 o;
-                            o.x = __uint_as_float(rr[i]) * inv_l / (1.0f + __expf(-g[i]));
-                            o.y = __uint_as_float(rr[i + 1]) * inv_l / (1.0f + __expf(-g[i + 1]));
-                            o.z = __uint_as_float(rr[i + 2]) * inv_l / (1.0f + __expf(-g[i + 2]));
-                            o.w = __uint_as_float(rr[i + 3]) * inv_l / (1.0f + __expf(-g[i + 3]));
+                            o.x = __uint_as_float(rr[i]) * inv_l / (1.0f + __expf(-gv.x));
+                            o.y = __uint_as_float(rr[i + 1]) * inv_l / (1.0f + __expf(-gv.y));
+                            o.z = __uint_as_float(rr[i + 2]) * inv_l / (1.0f + __expf(-gv.z));
+                            o.w = __uint_as_float(rr[i + 3]) * inv_l / (1.0f + __expf(-gv.w));
                             *reinterpret_cast<float4*>(dst + i) = o;
                         }
                     }
@@ -441,9 +463,7 @@ int launch_prefill(const CUtensorMap& mk, const CUtensorMap& mv, const PrefillPa
     }
     PrefillParams q = p;
     const uint32_t n_tiles = p.n_heads * n_qtiles;
-    const uint32_t sms = static_cast<uint32_t>(dev_num_sms());
     q.n_qt = n_qtiles;
-    q.heavy = (C::DUAL && n_tiles <= 2 * sms) ? std::min(n_tiles, sms) : n_tiles;
     CUtensorMap mo;   // out as fp32 rows of q_stride, for the epilogue's tensor-copy stores
     if (encode_f32_store_map(&mo, p.out, p.n_heads * HD, p.q_stride, p.B, 32, err, errlen)) return -1;
     k_prefill<HD><<<n_tiles, kPThreads, C::SMEM, st>>>(mk, mv, mo, q);
@@ -478,8 +498,8 @@ int prefill(float* out, const float* q, const uint16_t* kc, const uint16_t* vc, 
         return -1;
     }
     if ((reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(out) | reinterpret_cast<uintptr_t>(kc) |
-         reinterpret_cast<uintptr_t>(vc)) & 15u) {
-        set_err(err, errlen, "prefill: q, out, kcache and vcache must be 16-byte aligned");
+         reinterpret_cast<uintptr_t>(vc) | reinterpret_cast<uintptr_t>(gate)) & 15u) {
+        set_err(err, errlen, "prefill: q, out, gate, kcache and vcache must be 16-byte aligned");
         return -1;
     }
     if (static_cast<uint64_t>(pos_start) + B > 0x7fffffffull) {
