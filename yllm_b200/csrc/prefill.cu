@@ -174,6 +174,12 @@ __global__ void __launch_bounds__(kPThreads, 1)
         if (lane == 0) {
             constexpr uint32_t IDESC_QK = idesc_f16(BM, BN, 0);
             constexpr uint32_t IDESC_PV = idesc_f16(BM, HD, 1);
+            // Shared-memory descriptors are built once: a descriptor's address field counts 16-byte
+            // units, so one at `base + off` is the base descriptor + off / 16 (every operand lies
+            // inside this CTA's shared memory, below 256 KB, so the 14-bit field never carries).
+            const uint64_t dq0 = sdesc_sw128(sQ, 16, 1024);
+            const uint64_t dk0 = sdesc_sw128(sK, 16, 1024);
+            const uint64_t dv0 = sdesc_sw128(sV, BN * 128, 1024);
             bool ok = mbar_wait_bounded(&bars->q_full, 0, p.status, ST_PREFILL_TIMEOUT, abort_flag);
             tc_fence_after();
             // S(jj) = Q K(jj)^T into S buffer jj % NSB.  That buffer last held P(jj - NSB), whose PV
@@ -184,11 +190,11 @@ __global__ void __launch_bounds__(kPThreads, 1)
                     return false;
                 const uint32_t sb = jj % C::NSB;
                 tc_fence_after();
+                const uint64_t dk = dk0 + ((s * C::KV_BYTES) >> 4);
 #pragma unroll
                 for (int kk = 0; kk < HD / 16; ++kk) {
-                    const uint64_t a = sdesc_sw128(sQ + (kk >> 2) * (BM * 128) + (kk & 3) * 32, 16, 1024);
-                    const uint64_t b = sdesc_sw128(sK + s * C::KV_BYTES + (kk >> 2) * (BN * 128) + (kk & 3) * 32, 16,
-                                                   1024);
+                    const uint64_t a = dq0 + (((kk >> 2) * (BM * 128) + (kk & 3) * 32) >> 4);
+                    const uint64_t b = dk + (((kk >> 2) * (BN * 128) + (kk & 3) * 32) >> 4);
                     umma_f16(tmem + C::COL_S + sb * BN, a, b, IDESC_QK, kk > 0 ? 1u : 0u);
                 }
                 umma_commit(&bars->s_full[sb]);
@@ -206,11 +212,12 @@ __global__ void __launch_bounds__(kPThreads, 1)
                     return false;
                 tc_fence_after();
                 const uint32_t pcol = tmem + C::COL_S + sb * BN;
+                const uint64_t dv = dv0 + ((s * C::KV_BYTES) >> 4);
 #pragma unroll
                 for (int plane = 0; plane < 2; ++plane) {
 #pragma unroll
                     for (int kk = 0; kk < BN / 16; ++kk) {
-                        const uint64_t b = sdesc_sw128(sV + s * C::KV_BYTES + kk * 16 * 128, BN * 128, 1024);
+                        const uint64_t b = dv + ((kk * 16 * 128) >> 4);
                         umma_f16_ts(tmem + C::COL_O, pcol + 32 * (kk >> 1) + 16 * plane + 8 * (kk & 1), b, IDESC_PV,
                                     (jj > 0 || plane > 0 || kk > 0) ? 1u : 0u);
                     }
