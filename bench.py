@@ -43,7 +43,7 @@ def load_peaks() -> tuple[dict, str]:
 # from one ncu capture of exactly the launch the bench times (the commands and the
 # rest of those captures are summarised under profiles/).  Workloads without such a
 # capture report null.
-NCU_TRAFFIC = {"decode": 1226090496, "prefill": 25245696}
+NCU_TRAFFIC = {"decode": 1226090496, "prefill": 25237504}
 
 
 class ClockSampler:
@@ -797,12 +797,124 @@ def run_long_decode(args) -> None:
         dist.destroy_process_group()
 
 
+def run_rope_store(args) -> None:
+    """The decode step's RoPE + KV store (engine.c:1052-1072 per sequence and
+    layer; cuda_fwd.c:136-147 launches three kernels per sequence) at config
+    3's shape: every layer's q rotated in place and k/v rounded into the
+    pooled cache at each sequence's newest position, one launch per layer for
+    all 64 sequences.  Inputs fit in L2, so L2 is scrubbed between timed
+    steps.  Weak scaling: each rank serves its own batch."""
+    import ctypes as C
+
+    import torch
+    import torch.distributed as dist
+
+    from yllm_b200 import attn, dist as ydist
+    from yllm_b200.configs import CFG3 as c
+
+    rank, world, local = ydist.init("nccl" if args.gpus > 1 else "gloo")
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    stream = torch.cuda.current_stream()
+    L, n, H, KV, hd, kd = c.layers, c.n_seqs, c.n_heads, c.n_kv_heads, c.head_dim, c.kv_dim
+    theta = 500000.0   # Llama-3 rope_theta
+    ctx = c.ctx()
+    offs = [sum(ctx[:i]) for i in range(n)]
+    rows = sum(ctx)
+    pool = torch.empty(2 * L * rows * kd, dtype=torch.int16, device=dev)   # [K layers | V layers][rows][kd]
+    g = torch.Generator(device=dev)
+    g.manual_seed(1234 + rank)
+    q = torch.randn(L, n, H * hd, generator=g, device=dev)
+    k = torch.randn(L, n, kd, generator=g, device=dev)
+    v = torch.randn(L, n, kd, generator=g, device=dev)
+    base = pool.data_ptr()
+    items = [attn.make_rope_items([(q[l, i], k[l, i], v[l, i], base + 2 * (l * rows + offs[i]) * kd,
+                                    base + 2 * ((L + l) * rows + offs[i]) * kd, ctx[i] - 1) for i in range(n)],
+                                  device=dev) for l in range(L)]
+
+    def step():
+        for l in range(L):
+            attn.rope_store_kv(items[l], n, H, KV, hd, kd, attn.ROPE_LLAMA, theta)
+
+    ms, per_call, clk = _timed(step, args, stream, world, dist, local, graph=True, flush_l2=True)
+    per_item = 2 * H * hd * 4 + 2 * kd * 4 + 2 * kd * 2     # q read + write, k and v read, k and v rows written
+    step_bytes = L * n * per_item
+    e2e = None
+    if not args.no_e2e:
+        hq = torch.empty(q.numel(), dtype=torch.float32, pin_memory=True)
+        hk = torch.empty(k.numel(), dtype=torch.float32, pin_memory=True)
+        hv = torch.empty(v.numel(), dtype=torch.float32, pin_memory=True)
+        hq.copy_(q.reshape(-1).cpu())
+        hk.copy_(k.reshape(-1).cpu())
+        hv.copy_(v.reshape(-1).cpu())
+        oq = torch.empty(q.numel(), dtype=torch.float32, pin_memory=True)
+
+        def e2e_step():
+            q.view(-1).copy_(hq, non_blocking=True)
+            k.view(-1).copy_(hk, non_blocking=True)
+            v.view(-1).copy_(hv, non_blocking=True)
+            step()
+            oq.copy_(q.view(-1), non_blocking=True)
+
+        ems, _, _ = _timed(e2e_step, args, stream, world, dist, local)
+        e2e = {"value": round(n * world / (ems / 1e3), 2), "unit": "tok/s",
+               "h2d_bytes_per_step": (q.numel() + k.numel() + v.numel()) * 4 * world,
+               "d2h_bytes_per_step": q.numel() * 4 * world,
+               "path": "rope_store_kv per layer per step (no graph), pinned host q/k/v in, rotated q back"}
+    st = attn.device_status()
+    if st != 0:
+        raise RuntimeError(f"device status {st}")
+    cpu = None
+    if rank == 0 and not args.no_cpu_baseline:
+        import numpy as np
+
+        sys.path.insert(0, str(ROOT / "tests"))
+        import oracle
+
+        kind = "reference" if oracle.has_ref() else "port"
+        lib = oracle.load("ref" if kind == "reference" else "port")
+        qh, kh, vh = q[0].cpu().numpy().copy(), k[0].cpu().numpy().copy(), v[0].cpu().numpy().copy()
+        kc = np.zeros(max(ctx) * kd, np.uint16)
+        vc = np.zeros(max(ctx) * kd, np.uint16)
+        times = []
+        while not times or (sum(times) < min(args.cpu_budget, 5.0) and len(times) < 50):
+            t0 = time.perf_counter()
+            for i in range(n):
+                lib.orc_rope_store(qh[i], kh[i], vh[i], kc, vc, H, KV, hd, kd, 0, hd, ctx[i] - 1, theta)
+            times.append(time.perf_counter() - t0)
+        step_s = statistics.median(times) * L
+        cpu = {"value": round(n / step_s, 2), "unit": "tok/s", "cores": 1, "kind": kind,
+               "sample": f"layer 0 of {n} seqs (engine.c:1052-1072 per sequence, one thread as in the engine), "
+                         f"timed {len(times)}x, x{L} layers per step"}
+    peaks, src = load_peaks()
+    ach = step_bytes / (per_call / 1e3) / 1e9
+    roof = {"bound": "hbm", "achieved": round(ach, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
+            "frac": round(ach / peaks["hbm_gbs"], 4), "traffic": None, "kernel": "k_rope_store",
+            "peak_source": src, "bytes_per_step": step_bytes,
+            "note": f"{L} launches of {per_item * n / 1e6:.2f} MB each per step in one graph: launch-latency "
+                    "bound, the HBM fraction is small by construction"}
+    if rank == 0:
+        line = _line(args, world, "RoPE + KV store tok/s (Llama-3-8B shape, 64 sequences, 32 layers)",
+                     n * world / (ms / 1e3), "tok/s", ms,
+                     {"workload": c.name + "-rope-store", "n_heads": H, "n_kv_heads": KV, "head_dim": hd,
+                      "layers": L, "n_seqs": n * world, "rope": "llama pairs, theta 500000",
+                      "parallelism": f"data-parallel x{world}: a batch per GPU, no collective",
+                      "launch": "CUDA graph replay of the step (one launch per layer)",
+                      "l2": "L2 scrubbed between timed steps outside the step's events"},
+                     roof, args.steps * L, clk, e2e, cpu=cpu, scaling="weak")
+        line["dtype"] = "f32 math, fp16 KV rows (engine rounding)"
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--workload", default="decode",
                     choices=["decode", "prefill", "gated_prefill", "gdn_prefill", "gdn_decode", "long_decode",
-                             "config1_decode", "gated_decode"],
+                             "config1_decode", "gated_decode", "rope_store"],
                     help="decode = BASELINE config 3 (the default bench line)")
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
@@ -828,6 +940,8 @@ def main() -> None:
         run_gdn(args, decode=args.workload == "gdn_decode")
     elif args.workload in ("config1_decode", "gated_decode"):
         run_decode_small(args)
+    elif args.workload == "rope_store":
+        run_rope_store(args)
     else:
         run_long_decode(args)
 

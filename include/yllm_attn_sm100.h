@@ -83,6 +83,47 @@ void cuda_k_store_kv(uint16_t* kcache, uint16_t* vcache, const float* k, const f
 void cuda_k_store_kv_batch(uint16_t* kcache, uint16_t* vcache, const float* k, const float* v,
                            uint32_t pos_start, uint32_t B, uint32_t kv_dim);
 
+/* -------------------------------------------- fused RoPE + KV store (decode) */
+
+/* One sequence's inputs of a decode step at one layer: q [n_heads*head_dim]
+ * fp32 (rotated in place), k and v [n_kv_heads*head_dim] fp32 (read only),
+ * the layer's K and V cache bases (row t at + t*kv_dim) and the position. */
+typedef struct YattnRopeItem {
+    float* q;
+    const float* k;
+    const float* v;
+    uint16_t* kcache;
+    uint16_t* vcache;
+    uint32_t pos;
+    uint32_t reserved;
+} YattnRopeItem;
+
+/* RoPE of q and k at each item's position, then k (rotated) and v into the
+ * cache at that position with the engine's f32_to_f16 rounding, for all
+ * n_items (device array) in one launch.  Replaces, per sequence, the
+ * reference's cuda_k_rope_{llama,qwen}_heads on q and on k plus
+ * cuda_k_store_kv (cuda_fwd.c:136-147; CPU engine.c:1052-1072).
+ * rope_kind: 0 = rope_inplace (pairs 2j, 2j+1; matvec.c:890-904),
+ * 1 = rope_inplace_qwen (pairs j, j + head_dim/2; matvec.c:907-921),
+ * 2 = rope_inplace_mrope (first n_rope_dims dims, pairs j, j + n_rope_dims/2;
+ * matvec.c:924-939).  n_rope_dims is ignored for kinds 0 and 1.  The inverse
+ * frequencies are the reference's powf values (computed on the host); the
+ * device's sinf/cosf can move a stored fp16 value by one ulp. */
+int yattn_rope_store_kv(const YattnRopeItem* items_dev, uint32_t n_items, uint32_t n_heads,
+                        uint32_t n_kv_heads, uint32_t head_dim, uint32_t kv_dim, int rope_kind,
+                        uint32_t n_rope_dims, float theta, void* stream, char* err, size_t errlen);
+
+/* The same for B consecutive tokens of one sequence (a prefill chunk): row b
+ * of q (at q + b*q_stride), k and v (at + b*kv_dim) is rotated at position
+ * pos_start + b and stored into cache row pos_start + b.  Replaces the
+ * batched cuda_k_rope_{llama,qwen}_heads_batch on q and k plus
+ * cuda_k_store_kv_batch (cuda_fwd.c:207-218): one launch for the chunk. */
+int yattn_rope_store_kv_batch(float* q, const float* k, const float* v, uint16_t* kcache,
+                              uint16_t* vcache, uint32_t pos_start, uint32_t B, uint32_t q_stride,
+                              uint32_t n_heads, uint32_t n_kv_heads, uint32_t head_dim, uint32_t kv_dim,
+                              int rope_kind, uint32_t n_rope_dims, float theta, void* stream, char* err,
+                              size_t errlen);
+
 /* ---------------------------------------------- batched / split-KV decode */
 
 /* One decode query: the attention of one sequence at one layer.

@@ -280,6 +280,32 @@ void orc_f16_to_f32_buf(const uint16_t* src, float* dst, size_t n)
     for (i = 0; i < n; i++) dst[i] = orc_f16_to_f32(src[i]);
 }
 
+/* ---------------- one token's RoPE + KV store ---------------- */
+
+/* engine.c:1052-1072 (llama / qwen pairs over the whole head) and
+ * engine.c:921-934 (qwen35 M-RoPE over the first n_dims dims): every q head
+ * and k head rotated in place at pos, then k and v rounded into cache row pos.
+ * kind 0 llama, 1 qwen, 2 mrope. */
+void orc_rope_store(float* q, float* k, const float* v, uint16_t* kcache, uint16_t* vcache,
+                    uint32_t n_heads, uint32_t n_kv, uint32_t hd, uint32_t kv_dim, int kind,
+                    uint32_t n_dims, uint32_t pos, float theta)
+{
+    uint32_t hh, j;
+    for (hh = 0; hh < n_heads + n_kv; hh++) {
+        float* x = hh < n_heads ? q + (size_t)hh * hd : k + (size_t)(hh - n_heads) * hd;
+        if (kind == 0)
+            orc_rope_inplace(x, hd, pos, theta);
+        else if (kind == 1)
+            orc_rope_inplace_qwen(x, hd, pos, theta);
+        else
+            orc_rope_inplace_mrope(x, hd, n_dims, pos, theta);
+    }
+    for (j = 0; j < kv_dim; j++) {
+        kcache[(size_t)pos * kv_dim + j] = orc_f32_to_f16(k[j]);
+        vcache[(size_t)pos * kv_dim + j] = orc_f32_to_f16(v[j]);
+    }
+}
+
 /* ---------------- attention loops (engine.c, operation order kept) ---------------- */
 
 /* One head of the engine's decode/prefill inner body: scores over keys

@@ -45,6 +45,9 @@ void     orc_gdn_state_update(float* S, float* out, const float* q, const float*
 void     orc_rmsnorm_gated_f32(float* y, const float* x, const float* w, const float* z,
                                uint32_t n, float eps);     /* matvec.c:1007-1021, DT_F32 weights */
 void     orc_f32_to_f16_buf(const float* src, uint16_t* dst, size_t n);
+void     orc_rope_store(float* q, float* k, const float* v, uint16_t* kcache, uint16_t* vcache,
+                        uint32_t n_heads, uint32_t n_kv, uint32_t hd, uint32_t kv_dim, int kind,
+                        uint32_t n_dims, uint32_t pos, float theta);
 void     orc_f16_to_f32_buf(const uint16_t* src, float* dst, size_t n);
 
 /* ---- attention loops (engine.c, restated in operation order) ---- */

@@ -202,3 +202,32 @@ def test_workspace_size_formula():
     n = lib.yattn_decode_workspace_bytes(10, 3, 32, 8, 128)
     assert n == 256 + 512 + 10 * 4 * 128 * 4
     assert lib.yattn_decode_workspace_bytes(0, 0, 32, 8, 128) == 0
+
+
+def test_rope_store_rejects_bad_arguments():
+    """yattn_rope_store_kv checks its geometry and rope kind on the host, before any launch."""
+    import ctypes as C
+
+    from yllm_b200._lib import lib
+
+    err = C.create_string_buffer(256)
+    fake = C.c_void_p(0x1000)   # never dereferenced: every case fails before a launch
+    assert lib.yattn_rope_store_kv(fake, 0, 32, 8, 128, 1024, 0, 0, 1e4, None, err, 256) == 0   # nothing to do
+    assert lib.yattn_rope_store_kv(fake, 4, 32, 8, 128, 1024, 3, 0, 1e4, None, err, 256) == -1
+    assert b"rope_kind" in err.value
+    assert lib.yattn_rope_store_kv(fake, 4, 32, 8, 127, 1024, 0, 0, 1e4, None, err, 256) == -1
+    assert b"geometry" in err.value
+    assert lib.yattn_rope_store_kv(fake, 4, 16, 2, 256, 512, 2, 300, 1e4, None, err, 256) == -1
+    assert b"rotated dims" in err.value
+    assert lib.yattn_rope_store_kv(None, 4, 32, 8, 128, 1024, 0, 0, 1e4, None, err, 256) == -1
+    # the batch form
+    assert lib.yattn_rope_store_kv_batch(fake, fake, fake, fake, fake, 0, 0, 4096, 32, 8, 128, 1024, 0, 0, 1e4,
+                                         None, err, 256) == 0
+    assert lib.yattn_rope_store_kv_batch(fake, fake, fake, fake, fake, 0, 8, 4000, 32, 8, 128, 1024, 0, 0, 1e4,
+                                         None, err, 256) == -1
+    assert b"q_stride" in err.value
+    assert lib.yattn_rope_store_kv_batch(fake, None, fake, fake, fake, 0, 8, 4096, 32, 8, 128, 1024, 0, 0, 1e4,
+                                         None, err, 256) == -1
+    assert lib.yattn_rope_store_kv_batch(fake, fake, fake, fake, fake, 0xFFFFFFF0, 64, 4096, 32, 8, 128, 1024, 0, 0,
+                                         1e4, None, err, 256) == -1
+    assert b"overflow" in err.value

@@ -126,6 +126,28 @@ def test_port_equals_reference_build_live(orc, orc_ref):
         assert np.array_equal(oa, ob) and np.array_equal(Sa, Sb)
 
 
+def test_rope_store_port_equals_reference_build(orc, orc_ref):
+    """orc_rope_store (engine.c:1052-1072, 921-934) on both builds: same q, k and cache bits, every kind."""
+    rng = np.random.default_rng(11)
+    for kind, H, KV, hd, nd, theta in ((0, 32, 8, 128, 128, 5e5), (1, 14, 2, 64, 64, 1e6), (2, 16, 2, 256, 64, 1e7)):
+        kd = KV * hd
+        for pos in (0, 3, 4095, 131071):
+            q = rng.standard_normal(H * hd).astype(np.float32)
+            k = rng.standard_normal(kd).astype(np.float32)
+            v = rng.standard_normal(kd).astype(np.float32)
+            outs = []
+            for lib in (orc, orc_ref):
+                qq, kk = q.copy(), k.copy()
+                kc = np.zeros((pos + 1) * kd, np.uint16)
+                vc = np.zeros((pos + 1) * kd, np.uint16)
+                lib.orc_rope_store(qq, kk, v, kc, vc, H, KV, hd, kd, kind, nd, pos, theta)
+                outs.append((qq, kk, kc[pos * kd:], vc[pos * kd:]))
+            for a, b in zip(*outs):
+                assert np.array_equal(a, b), (kind, pos)
+            if kind == 2:   # dims past n_dims pass through unrotated
+                assert np.array_equal(outs[0][1].reshape(KV, hd)[:, nd:], k.reshape(KV, hd)[:, nd:])
+
+
 def test_per_head_gdn_call_equals_all_heads_call(orc):
     """orc_gdn_step splits the reference call per head; same bits as one call."""
     rng = np.random.default_rng(9)

@@ -39,6 +39,18 @@ class YattnDecodeItem(C.Structure):
     ]
 
 
+class YattnRopeItem(C.Structure):
+    _fields_ = [
+        ("q", vp),
+        ("k", vp),
+        ("v", vp),
+        ("kcache", vp),
+        ("vcache", vp),
+        ("pos", u32),
+        ("reserved", u32),
+    ]
+
+
 class YattnDecodeWork(C.Structure):
     _fields_ = [
         ("item", u32),
@@ -102,6 +114,9 @@ PROTOS = {
     "yattn_attn_decode_noalloc": (C.c_int, [vp, vp, vp, vp, vp, u32, u32, u32, u32, u32, vp, *E]),
     "yattn_reserve": (C.c_int, [sz, *E]),
     "yattn_store_kv": (C.c_int, [vp, vp, vp, vp, u32, u32, u32, vp, *E]),
+    "yattn_rope_store_kv": (C.c_int, [vp, u32, u32, u32, u32, u32, C.c_int, u32, C.c_float, vp, *E]),
+    "yattn_rope_store_kv_batch": (C.c_int, [vp, vp, vp, vp, vp, u32, u32, u32, u32, u32, u32, u32, C.c_int, u32,
+                                            C.c_float, vp, *E]),
     "cuda_k_gdn_state_update": (None, [vp, vp, vp, vp, vp, vp, vp, u32, u32, u32, u32]),
     "yattn_gdn_decode": (C.c_int, [vp, vp, vp, vp, vp, vp, vp, u32, u32, u32, u32, u32, vp, vp, C.c_float, vp, *E]),
     "yattn_gdn_prefill": (

@@ -18,7 +18,7 @@ import numpy as np
 import torch
 
 from . import _lib
-from ._lib import YattnDecodeItem, YattnDecodeWork, call, call_void, lib
+from ._lib import YattnDecodeItem, YattnDecodeWork, YattnRopeItem, call, call_void, lib
 
 
 def _ptr(t: Optional[torch.Tensor]) -> Optional[int]:
@@ -194,6 +194,45 @@ def make_items(entries: Sequence[tuple], device=None) -> torch.Tensor:
         arr[i].pos = int(pos)
     raw = bytearray(C.string_at(arr, C.sizeof(arr)))
     return torch.frombuffer(raw, dtype=torch.uint8).to(device or "cuda")
+
+
+ROPE_LLAMA, ROPE_QWEN, ROPE_MROPE = 0, 1, 2
+
+
+def make_rope_items(entries: Sequence[tuple], device=None) -> torch.Tensor:
+    """Device array of YattnRopeItem from (q, k, v, kcache, vcache, pos) tuples; kcache / vcache are
+    tensors or raw device addresses of the layer's cache bases."""
+    arr = (YattnRopeItem * len(entries))()
+    for i, (q, k, v, kc, vc, pos) in enumerate(entries):
+        arr[i].q = q.data_ptr()
+        arr[i].k = k.data_ptr()
+        arr[i].v = v.data_ptr()
+        arr[i].kcache = kc.data_ptr() if isinstance(kc, torch.Tensor) else int(kc)
+        arr[i].vcache = vc.data_ptr() if isinstance(vc, torch.Tensor) else int(vc)
+        arr[i].pos = int(pos)
+    raw = bytearray(C.string_at(arr, C.sizeof(arr)))
+    return torch.frombuffer(raw, dtype=torch.uint8).to(device or "cuda")
+
+
+def rope_store_kv(items: torch.Tensor, n_items: int, n_heads: int, n_kv_heads: int, head_dim: int, kv_dim: int,
+                  rope_kind: int, theta: float, n_rope_dims: int = 0, stream=None) -> None:
+    """One decode step's RoPE of q (in place) and k, and the fp16 store of k and v at each item's position
+    (engine.c:1052-1072 / cuda_fwd.c:136-147 for every item, one launch)."""
+    call("yattn_rope_store_kv", items.data_ptr(), n_items, n_heads, n_kv_heads, head_dim, kv_dim, rope_kind,
+         n_rope_dims, theta, _stream(stream))
+
+
+def rope_store_kv_batch(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, kcache: torch.Tensor,
+                        vcache: torch.Tensor, pos_start: int, B: int, n_heads: int, n_kv_heads: int, head_dim: int,
+                        kv_dim: int, rope_kind: int, theta: float, n_rope_dims: int = 0, q_stride: int = 0,
+                        stream=None) -> None:
+    """RoPE + KV store of B consecutive tokens (rows of q, k, v) at positions pos_start.. (the batched prefill's
+    cuda_fwd.c:207-218 in one launch).  q is rotated in place."""
+    for name, t in (("q", q), ("k", k), ("v", v)):
+        _need(t, torch.float32, name)
+    call("yattn_rope_store_kv_batch", q.data_ptr(), k.data_ptr(), v.data_ptr(), kcache.data_ptr(), vcache.data_ptr(),
+         pos_start, B, q_stride or n_heads * head_dim, n_heads, n_kv_heads, head_dim, kv_dim, rope_kind, n_rope_dims,
+         theta, _stream(stream))
 
 
 def decode_partial(ml: torch.Tensor, o: torch.Tensor, q: torch.Tensor, kcache: torch.Tensor, vcache: torch.Tensor,

@@ -1,0 +1,207 @@
+// rope.cu -- one decode step's RoPE and KV store, fused, for many sequences.
+//
+// Reference: per sequence, engine.c:1052-1072 on the CPU (rope_inplace /
+// rope_inplace_qwen on every q and k head, matvec.c:890-921, then the fp32 ->
+// fp16 store of k and v through f32_to_f16, platform.c:340-379) and
+// cuda_fwd.c:136-147 on the GPU (cuda_k_rope_{llama,qwen}_heads on q, on k,
+// then cuda_k_store_kv: three launches per sequence and layer).  qwen35's
+// M-RoPE (rope_inplace_mrope, matvec.c:924-939: the first n_dims dims only) is
+// the third kind.
+//
+// One launch covers every item (sequence) of a layer: q is rotated in place
+// (the attention reads it next), k is rotated on the way into the cache, v is
+// stored as is.  The arithmetic follows the reference's fp32 operation order:
+// the inverse frequencies are computed on the host with the same powf
+// expression (so they are the reference's own values), the angle is one fp32
+// multiply, and a*c - b*s / a*s + b*c are evaluated without FMA contraction.
+// The only difference left is the device's sinf/cosf against the host
+// library's (a few ulps), which moves a stored fp16 value by one ulp rarely.
+#include "common.cuh"
+
+#include <algorithm>
+#include <cmath>
+
+namespace yattn {
+namespace {
+
+constexpr int kMaxPairs = 128;   // head_dim <= 256
+
+struct RopeParams {
+    const YattnRopeItem* items;      // NULL: the batch form below
+    YattnRopeItem batch;             // row 0 of a token batch: row b at q + b*q_stride, k/v + b*kv_dim, pos + b
+    uint32_t q_stride;
+    uint32_t n_items, n_heads, n_kv, hd, kv_dim;
+    uint32_t kind;                   // 0 llama (2j, 2j+1), 1 qwen (j, j + hd/2), 2 mrope (j, j + n_dims/2), j < n_dims/2
+    uint32_t n_dims;                 // rotated dims (hd for kinds 0 and 1)
+    float inv_freq[kMaxPairs];       // theta^(-2j/n_dims), the reference's powf values
+};
+
+// Rotates the pair (a, b) of pair index j at position pos.
+__device__ __forceinline__ void rotate(float& a, float& b, float inv_freq, uint32_t pos) {
+    const float ang = __fmul_rn(inv_freq, static_cast<float>(pos));
+    float s, c;
+    sincosf(ang, &s, &c);
+    const float ra = __fsub_rn(__fmul_rn(a, c), __fmul_rn(b, s));
+    const float rb = __fadd_rn(__fmul_rn(a, s), __fmul_rn(b, c));
+    a = ra;
+    b = rb;
+}
+
+// Element indices of pair j inside a head for the rope kind.
+__device__ __forceinline__ void pair_of(uint32_t kind, uint32_t hd, uint32_t n_dims, uint32_t j, uint32_t& e0,
+                                        uint32_t& e1) {
+    if (kind == 0) {
+        e0 = 2 * j;
+        e1 = 2 * j + 1;
+    } else if (kind == 1) {
+        e0 = j;
+        e1 = j + hd / 2;
+    } else {
+        e0 = j;
+        e1 = j + n_dims / 2;
+    }
+}
+
+// blockIdx.y = item.  Work of an item, grid-strided over blockIdx.x:
+//   [0, nq)            q pairs (head, j), rotated in place
+//   [nq, nq + nk)      k pairs, rotated and stored (engine rounding)
+//   [.., + nr)         k elements outside the rotated dims (mrope), stored as is
+//   [.., + kv_dim)     v elements, stored
+__global__ void __launch_bounds__(256) k_rope_store(const RopeParams p) {
+    YattnRopeItem it;
+    if (p.items) {
+        it = p.items[blockIdx.y];
+    } else {
+        it = p.batch;
+        it.q += static_cast<size_t>(blockIdx.y) * p.q_stride;
+        it.k += static_cast<size_t>(blockIdx.y) * p.kv_dim;
+        it.v += static_cast<size_t>(blockIdx.y) * p.kv_dim;
+        it.pos += blockIdx.y;
+    }
+    const uint32_t pairs = p.n_dims / 2;
+    const uint32_t nq = p.n_heads * pairs, nk = p.n_kv * pairs, nr = p.n_kv * (p.hd - p.n_dims);
+    const uint32_t total = nq + nk + nr + p.kv_dim;
+    uint16_t* krow = it.kcache + static_cast<size_t>(it.pos) * p.kv_dim;
+    uint16_t* vrow = it.vcache + static_cast<size_t>(it.pos) * p.kv_dim;
+    for (uint32_t u = blockIdx.x * blockDim.x + threadIdx.x; u < total; u += gridDim.x * blockDim.x) {
+        if (u < nq) {
+            const uint32_t h = u / pairs, j = u % pairs;
+            uint32_t e0, e1;
+            pair_of(p.kind, p.hd, p.n_dims, j, e0, e1);
+            float* qh = it.q + static_cast<size_t>(h) * p.hd;
+            float a = qh[e0], b = qh[e1];
+            rotate(a, b, p.inv_freq[j], it.pos);
+            qh[e0] = a;
+            qh[e1] = b;
+        } else if (u < nq + nk) {
+            const uint32_t w = u - nq, h = w / pairs, j = w % pairs;
+            uint32_t e0, e1;
+            pair_of(p.kind, p.hd, p.n_dims, j, e0, e1);
+            const float* kh = it.k + static_cast<size_t>(h) * p.hd;
+            float a = kh[e0], b = kh[e1];
+            rotate(a, b, p.inv_freq[j], it.pos);
+            krow[h * p.hd + e0] = engine_f32_to_f16(a);
+            krow[h * p.hd + e1] = engine_f32_to_f16(b);
+        } else if (u < nq + nk + nr) {
+            const uint32_t w = u - nq - nk, h = w / (p.hd - p.n_dims), e = p.n_dims + w % (p.hd - p.n_dims);
+            krow[h * p.hd + e] = engine_f32_to_f16(it.k[static_cast<size_t>(h) * p.hd + e]);
+        } else {
+            const uint32_t e = u - nq - nk - nr;
+            vrow[e] = engine_f32_to_f16(it.v[e]);
+        }
+    }
+}
+
+}  // namespace
+}  // namespace yattn
+
+using namespace yattn;
+
+namespace {
+
+// Checks the geometry and launches; p.items or p.batch already set.
+int launch_rope(RopeParams& p, uint32_t n_items, uint32_t n_heads, uint32_t n_kv_heads, uint32_t head_dim,
+                uint32_t kv_dim, int rope_kind, uint32_t n_rope_dims, float theta, void* stream, char* err,
+                size_t errlen, const char* who) {
+    if (n_heads == 0 || n_kv_heads == 0 || n_kv_heads > n_heads || head_dim == 0 || head_dim > 2 * kMaxPairs ||
+        (head_dim & 1) || kv_dim < n_kv_heads * head_dim) {
+        set_err(err, errlen, "%s: bad geometry n_heads=%u n_kv_heads=%u head_dim=%u kv_dim=%u", who, n_heads,
+                n_kv_heads, head_dim, kv_dim);
+        return -1;
+    }
+    if (rope_kind < 0 || rope_kind > 2) {
+        set_err(err, errlen, "%s: rope_kind %d (0 llama, 1 qwen, 2 mrope)", who, rope_kind);
+        return -1;
+    }
+    const uint32_t n_dims = rope_kind == 2 ? n_rope_dims : head_dim;
+    if (n_dims == 0 || (n_dims & 1) || n_dims > head_dim) {
+        set_err(err, errlen, "%s: %u rotated dims for head_dim %u", who, n_dims, head_dim);
+        return -1;
+    }
+    if (n_items > 65535) {
+        set_err(err, errlen, "%s: %u rows (max 65535 per launch)", who, n_items);
+        return -1;
+    }
+    p.n_items = n_items;
+    p.n_heads = n_heads;
+    p.n_kv = n_kv_heads;
+    p.hd = head_dim;
+    p.kv_dim = kv_dim;
+    p.kind = static_cast<uint32_t>(rope_kind);
+    p.n_dims = n_dims;
+    // the reference's expression, in the same fp32 operation order (matvec.c:895, 912, 929)
+    for (uint32_t j = 0; j < n_dims / 2; ++j)
+        p.inv_freq[j] = powf(theta, -2.0f * static_cast<float>(j) / static_cast<float>(n_dims));
+    const uint32_t work = n_heads * (n_dims / 2) + n_kv_heads * (n_dims / 2) + n_kv_heads * (head_dim - n_dims) + kv_dim;
+    const uint32_t bx = std::max(1u, std::min((work + 255) / 256, 8u));
+    k_rope_store<<<dim3(bx, n_items), 256, 0, static_cast<cudaStream_t>(stream)>>>(p);
+    YATTN_CHECK_LAUNCH(err, errlen, who);
+    return 0;
+}
+
+}  // namespace
+
+extern "C" int yattn_rope_store_kv(const YattnRopeItem* items_dev, uint32_t n_items, uint32_t n_heads,
+                                   uint32_t n_kv_heads, uint32_t head_dim, uint32_t kv_dim, int rope_kind,
+                                   uint32_t n_rope_dims, float theta, void* stream, char* err, size_t errlen) {
+    if (n_items == 0) return 0;
+    if (!items_dev) {
+        set_err(err, errlen, "rope_store_kv: null items");
+        return -1;
+    }
+    RopeParams p{};
+    p.items = items_dev;
+    return launch_rope(p, n_items, n_heads, n_kv_heads, head_dim, kv_dim, rope_kind, n_rope_dims, theta, stream,
+                       err, errlen, "rope_store_kv");
+}
+
+extern "C" int yattn_rope_store_kv_batch(float* q, const float* k, const float* v, uint16_t* kcache,
+                                         uint16_t* vcache, uint32_t pos_start, uint32_t B, uint32_t q_stride,
+                                         uint32_t n_heads, uint32_t n_kv_heads, uint32_t head_dim, uint32_t kv_dim,
+                                         int rope_kind, uint32_t n_rope_dims, float theta, void* stream, char* err,
+                                         size_t errlen) {
+    if (B == 0) return 0;
+    if (!q || !k || !v || !kcache || !vcache) {
+        set_err(err, errlen, "rope_store_kv_batch: null pointer");
+        return -1;
+    }
+    if (q_stride < n_heads * head_dim) {
+        set_err(err, errlen, "rope_store_kv_batch: q_stride %u < n_heads*head_dim %u", q_stride, n_heads * head_dim);
+        return -1;
+    }
+    if (static_cast<uint64_t>(pos_start) + B > 0xFFFFFFFFull) {
+        set_err(err, errlen, "rope_store_kv_batch: positions overflow");
+        return -1;
+    }
+    RopeParams p{};
+    p.items = nullptr;
+    p.batch.q = q;
+    p.batch.k = k;
+    p.batch.v = v;
+    p.batch.kcache = kcache;
+    p.batch.vcache = vcache;
+    p.batch.pos = pos_start;
+    p.q_stride = q_stride;
+    return launch_rope(p, B, n_heads, n_kv_heads, head_dim, kv_dim, rope_kind, n_rope_dims, theta, stream, err,
+                       errlen, "rope_store_kv_batch");
+}
