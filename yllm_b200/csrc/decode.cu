@@ -33,7 +33,7 @@ namespace {
 constexpr int kSplitQuant = 64;     // split lengths are multiples of this
 constexpr uint32_t kSplitMin = 128;  // shortest split of a balanced plan (keys)
 constexpr uint32_t kMaxSplits = 32;  // most splits of one (item, head group) in a balanced plan
-constexpr uint32_t kUnitCost = 192;  // keys charged for each further unit of a CTA
+constexpr uint32_t kUnitCost = 320;  // keys charged for each further unit of a CTA
 
 // Per head_dim: NCW consumer warps and a ring of NST stages.  A stage holds K and V
 // of 16 tokens per consumer warp: exactly STAGE_TM bytes for the tensor copies,
@@ -1119,9 +1119,10 @@ int decode_plan_impl(const uint32_t* pos_host, uint32_t n_items, uint32_t n_kv_h
     if (target_ctas == 0) target_ctas = static_cast<uint32_t>(dev_num_sms());
     std::vector<YattnDecodeWork> w;
     uint32_t parts = 0, groups = 0;
-    if (split_tokens) {
-        // uniform splits, one unit per CTA, longest units first
-        const uint32_t split = (split_tokens + kSplitQuant - 1) / kSplitQuant * kSplitQuant;
+    // uniform splits of `split` keys, one unit per CTA, longest units first
+    auto build_uniform = [&](uint32_t split) -> int {
+        w.clear();
+        parts = groups = 0;
         for (uint32_t i = 0; i < n_items; ++i) {
             const uint32_t ntok = pos_host[i] + 1;
             const uint32_t ns = (ntok + split - 1) / split;
@@ -1152,6 +1153,10 @@ int decode_plan_impl(const uint32_t* pos_host, uint32_t n_items, uint32_t n_kv_h
             return (a.t_end - a.t_begin) > (b.t_end - b.t_begin);
         });
         for (size_t u = 0; u < w.size(); ++u) w[u].cta = static_cast<uint32_t>(u);
+        return 0;
+    };
+    if (split_tokens) {
+        if (build_uniform((split_tokens + kSplitQuant - 1) / kSplitQuant * kSplitQuant) != 0) return -1;
     } else {
         // Balanced: the (item, head group) key ranges laid end to end, cut into
         // chunks of `chunk` keys; CTA c streams the keys of chunk c as one unit per
@@ -1240,7 +1245,43 @@ int decode_plan_impl(const uint32_t* pos_host, uint32_t n_items, uint32_t n_kv_h
             // the charges pushed units past the last CTA: grow finely first, then faster
             chunk += (attempt < 16 ? chunk / 128 : chunk / 16) + 1;
         }
-        // units are already grouped by CTA in increasing order
+        // units are already grouped by CTA in increasing order.  When the ranges
+        // are few and even (a batch of equal contexts, fewer ranges than CTAs),
+        // cutting every range into equal pieces can beat the balanced cut: each
+        // CTA then has one unit and every range fewer splits.  The uniform cut is
+        // taken when it finishes within one unit charge of the balanced plan's
+        // largest charged CTA, since the charge undercounts a unit's cost where
+        // the merged rows are wide (qwen35's 8 query heads of 256 dims per kv
+        // head: 56 us uniform against 58-61 us balanced at 32 x 4096 keys).
+        uint64_t est = 0, cur = 0;
+        for (size_t u = 0; u < w.size(); ++u) {
+            const bool first_of_cta = u == 0 || w[u].cta != w[u - 1].cta;
+            cur = (first_of_cta ? 0 : cur + kUnitCost) + (w[u].t_end - w[u].t_begin);
+            est = std::max(est, cur);
+        }
+        if (static_cast<uint64_t>(n_items) * nkg <= target_ctas) {
+            // smallest split (in kSplitQuant steps, at least kSplitMin) whose pieces fit in
+            // target_ctas CTAs; the piece count falls as the split grows, and at a split of
+            // max_tok every range is one piece
+            auto pieces = [&](uint64_t split) {
+                uint64_t n = 0;
+                for (uint32_t i = 0; i < n_items; ++i) n += (pos_host[i] + split) / split;   // ceil((pos+1)/split)
+                return n * nkg;
+            };
+            uint64_t lo = (std::max<uint32_t>(kSplitMin, kSplitQuant) + kSplitQuant - 1) / kSplitQuant;
+            uint64_t hi = std::max<uint64_t>(lo, (static_cast<uint64_t>(max_tok) + kSplitQuant - 1) / kSplitQuant);
+            while (lo < hi) {
+                const uint64_t mid = (lo + hi) / 2;
+                if (pieces(mid * kSplitQuant) <= target_ctas)
+                    hi = mid;
+                else
+                    lo = mid + 1;
+            }
+            const uint64_t best = lo * kSplitQuant;
+            if (pieces(best) <= target_ctas && std::min<uint64_t>(best, max_tok) <= est + kUnitCost &&
+                build_uniform(static_cast<uint32_t>(best)) != 0)
+                return -1;
+        }
     }
     if (w.size() > work_cap) {
         set_err(err, errlen, "decode_plan: %zu work units exceed work_cap %u", w.size(), work_cap);

@@ -79,6 +79,11 @@ __global__ void __launch_bounds__(256) k_rope_store(const RopeParams p) {
         it.pos += blockIdx.y;
     }
     const uint32_t pairs = p.n_dims / 2;
+    // staged in shared memory: a warp's threads index different pairs, and a divergent index into the
+    // kernel's parameter bank would serialise
+    __shared__ float s_freq[kMaxPairs];
+    for (uint32_t j = threadIdx.x; j < pairs; j += blockDim.x) s_freq[j] = p.inv_freq[j];
+    __syncthreads();
     const uint32_t nq = p.n_heads * pairs, nk = p.n_kv * pairs, nr = p.n_kv * (p.hd - p.n_dims);
     const uint32_t total = nq + nk + nr + p.kv_dim;
     uint16_t* krow = it.kcache + static_cast<size_t>(it.pos) * p.kv_dim;
@@ -90,7 +95,7 @@ __global__ void __launch_bounds__(256) k_rope_store(const RopeParams p) {
             pair_of(p.kind, p.hd, p.n_dims, j, e0, e1);
             float* qh = it.q + static_cast<size_t>(h) * p.hd;
             float a = qh[e0], b = qh[e1];
-            rotate(a, b, p.inv_freq[j], it.pos);
+            rotate(a, b, s_freq[j], it.pos);
             qh[e0] = a;
             qh[e1] = b;
         } else if (u < nq + nk) {
@@ -99,7 +104,7 @@ __global__ void __launch_bounds__(256) k_rope_store(const RopeParams p) {
             pair_of(p.kind, p.hd, p.n_dims, j, e0, e1);
             const float* kh = it.k + static_cast<size_t>(h) * p.hd;
             float a = kh[e0], b = kh[e1];
-            rotate(a, b, p.inv_freq[j], it.pos);
+            rotate(a, b, s_freq[j], it.pos);
             krow[h * p.hd + e0] = engine_f32_to_f16(a);
             krow[h * p.hd + e1] = engine_f32_to_f16(b);
         } else if (u < nq + nk + nr) {
@@ -153,7 +158,9 @@ int launch_rope(RopeParams& p, uint32_t n_items, uint32_t n_heads, uint32_t n_kv
     for (uint32_t j = 0; j < n_dims / 2; ++j)
         p.inv_freq[j] = powf(theta, -2.0f * static_cast<float>(j) / static_cast<float>(n_dims));
     const uint32_t work = n_heads * (n_dims / 2) + n_kv_heads * (n_dims / 2) + n_kv_heads * (head_dim - n_dims) + kv_dim;
-    const uint32_t bx = std::max(1u, std::min((work + 255) / 256, 8u));
+    // one work unit per thread up to 32 blocks per item: the loop body is a chain of dependent memory
+    // round trips (item, inputs, stores), so a second pass through it would double the kernel time
+    const uint32_t bx = std::max(1u, std::min((work + 255) / 256, 32u));
     k_rope_store<<<dim3(bx, n_items), 256, 0, static_cast<cudaStream_t>(stream)>>>(p);
     YATTN_CHECK_LAUNCH(err, errlen, who);
     return 0;
