@@ -321,6 +321,28 @@ int yattn_gdn_decode(float* S, float* out, const float* q, const float* k, const
                      uint32_t hk, uint32_t n_vheads, uint32_t hv, const float* norm_w,
                      const float* z, float eps, void* stream, char* err, size_t errlen);
 
+/* The GDN layer's inputs between its projections and the state update, for
+ * T tokens of each of n_seqs sequences (engine.c:785-821, token by token on
+ * the CPU): beta = sigmoid(beta_in), gate = softplus(alpha + ssm_dt) * ssm_a;
+ * the causal depthwise conv1d of the projection over the kwidth-row delay line
+ * (conv1d_update, matvec.c:956-967) and silu; the q / k / v split with
+ * l2norm_inplace (matvec.c:941-948) of every q and k head.  One launch.
+ *   qkv        [n_seqs][T][conv_chan]   projection (read only)
+ *   conv_state [n_seqs][kwidth][conv_chan]  delay line, newest row last; updated
+ *   conv_w     [conv_chan][kwidth]      fp32 taps (the GGUF layout)
+ *   alpha, beta_in [n_seqs][T][n_vheads]; ssm_dt, ssm_a [n_vheads]
+ *   q, k [n_seqs][T][num_k_heads*hk]; v [n_seqs][T][n_vheads*hv];
+ *   gate, beta [n_seqs][T][n_vheads]: the layouts yattn_gdn_decode /
+ *   yattn_gdn_prefill read.
+ * conv_chan must be 2*num_k_heads*hk + n_vheads*hv; hk, hv <= 256; kwidth <= 8.
+ * Operation order as the reference (fp32, no contraction); expf / log1pf are
+ * the device's. */
+int yattn_gdn_inputs(const float* qkv, float* conv_state, const float* conv_w, const float* alpha,
+                     const float* beta_in, const float* ssm_dt, const float* ssm_a, float* q, float* k,
+                     float* v, float* gate, float* beta, uint32_t n_seqs, uint32_t T,
+                     uint32_t conv_chan, uint32_t kwidth, uint32_t num_k_heads, uint32_t hk,
+                     uint32_t n_vheads, uint32_t hv, float eps, void* stream, char* err, size_t errlen);
+
 /* T tokens of each of n_seqs sequences in order (the engine's qwen35 prefill,
  * engine.c:723-734, calls gdn_state_update once per token).  Per-token rows as
  * in yattn_gdn_decode, token t of sequence s at row s*T + t.  Runs the chunked

@@ -42,6 +42,7 @@ void     gdn_state_update(float* S, float* out, const float* q, const float* k,
                           uint32_t num_k_heads, uint32_t hk, uint32_t n_vheads, uint32_t hv);
 void     rmsnorm_gated(float* y, const float* x, const uint8_t* w, const float* z,
                        uint32_t n, float eps, uint32_t dtype);
+void     conv1d_update(float* state, const float* x, const uint8_t* w, uint32_t dim, uint32_t kwidth);
 #define REF_DT_F32 1u   /* DT_F32, inference/include/llf.h:15 */
 
 int orc_build_kind(void) { return 1; }
@@ -60,6 +61,8 @@ void orc_gdn_state_update(float* S, float* out, const float* q, const float* k,
 { gdn_state_update(S, out, q, k, v, gate, beta, num_k_heads, hk, n_vheads, hv); }
 void orc_rmsnorm_gated_f32(float* y, const float* x, const float* w, const float* z, uint32_t n, float eps)
 { rmsnorm_gated(y, x, (const uint8_t*)w, z, n, eps, REF_DT_F32); }
+void orc_conv1d_update(float* state, float* x, const float* w, uint32_t dim, uint32_t kwidth)
+{ conv1d_update(state, x, (const uint8_t*)w, dim, kwidth); }
 
 #else  /* ---------------- restated helpers ("port") ---------------- */
 
@@ -246,6 +249,20 @@ void orc_rmsnorm_gated_f32(float* y, const float* x, const float* w, const float
         y[i] = x[i] * w[i] * inv * (zg / (1.0f + expf(-zg)));
     }
 }
+
+/* matvec.c:956-967: slide x into the newest row of the [kwidth][dim] delay
+ * line, then x[ch] = sum over rows i (oldest first) of state[i][ch] * w[ch][i]. */
+void orc_conv1d_update(float* state, float* x, const float* w, uint32_t dim, uint32_t kwidth)
+{
+    uint32_t i, ch;
+    memmove(state, state + dim, (size_t)(kwidth - 1) * dim * sizeof(float));
+    memcpy(state + (size_t)(kwidth - 1) * dim, x, (size_t)dim * sizeof(float));
+    for (ch = 0; ch < dim; ch++) {
+        float acc = 0.0f;
+        for (i = 0; i < kwidth; i++) acc += state[(size_t)i * dim + ch] * w[(size_t)ch * kwidth + i];
+        x[ch] = acc;
+    }
+}
 #endif /* ORACLE_LINK_REF */
 
 int orc_max_threads(void)
@@ -278,6 +295,48 @@ void orc_f16_to_f32_buf(const uint16_t* src, float* dst, size_t n)
 {
     size_t i;
     for (i = 0; i < n; i++) dst[i] = orc_f16_to_f32(src[i]);
+}
+
+/* ---------------- qwen35 GDN layer inputs ---------------- */
+
+/* engine.c:785-821 for T tokens of each of n_seqs sequences, token by token:
+ * gates (beta = sigmoid, gate = softplus(alpha + dt) * A), conv1d_update of
+ * the projection into the delay line, silu, then the q / k / v split with
+ * l2norm_inplace of every q and k head.  Layouts: qkv [n_seqs][T][conv_chan],
+ * conv_state [n_seqs][kwidth][conv_chan], conv_w [conv_chan][kwidth], alpha /
+ * beta_in / gate / beta [n_seqs][T][nv], q / k [n_seqs][T][nk*hk], v
+ * [n_seqs][T][nv*hv].  qkv is not modified. */
+void orc_gdn_inputs(const float* qkv, float* conv_state, const float* conv_w, const float* alpha,
+                    const float* beta_in, const float* dt, const float* a, float* q, float* k, float* v,
+                    float* gate, float* beta, uint32_t n_seqs, uint32_t T, uint32_t conv_chan, uint32_t kwidth,
+                    uint32_t nk, uint32_t hk, uint32_t nv, uint32_t hv, float eps)
+{
+    const uint32_t key_dim = nk * hk, value_dim = nv * hv;
+    float* x = (float*)malloc((size_t)conv_chan * sizeof(float));
+    uint32_t s, t, h, ch;
+    if (!x) return;
+    for (s = 0; s < n_seqs; s++) {
+        float* st = conv_state + (size_t)s * kwidth * conv_chan;
+        for (t = 0; t < T; t++) {
+            const size_t row = (size_t)s * T + t;
+            for (h = 0; h < nv; h++) {
+                const size_t i = row * nv + h;
+                beta[i] = 1.0f / (1.0f + expf(-beta_in[i]));
+                float ab = alpha[i] + dt[h];
+                float sp = log1pf(expf(ab));
+                gate[i] = sp * a[h];
+            }
+            memcpy(x, qkv + row * conv_chan, (size_t)conv_chan * sizeof(float));
+            orc_conv1d_update(st, x, conv_w, conv_chan, kwidth);
+            for (ch = 0; ch < conv_chan; ch++) x[ch] = x[ch] / (1.0f + expf(-x[ch]));
+            for (h = 0; h < nk; h++) orc_l2norm_inplace(x + (size_t)h * hk, hk, eps);
+            for (h = 0; h < nk; h++) orc_l2norm_inplace(x + key_dim + (size_t)h * hk, hk, eps);
+            memcpy(q + row * key_dim, x, (size_t)key_dim * sizeof(float));
+            memcpy(k + row * key_dim, x + key_dim, (size_t)key_dim * sizeof(float));
+            memcpy(v + row * value_dim, x + 2 * key_dim, (size_t)value_dim * sizeof(float));
+        }
+    }
+    free(x);
 }
 
 /* ---------------- one token's RoPE + KV store ---------------- */

@@ -45,6 +45,11 @@ void     orc_gdn_state_update(float* S, float* out, const float* q, const float*
 void     orc_rmsnorm_gated_f32(float* y, const float* x, const float* w, const float* z,
                                uint32_t n, float eps);     /* matvec.c:1007-1021, DT_F32 weights */
 void     orc_f32_to_f16_buf(const float* src, uint16_t* dst, size_t n);
+void     orc_conv1d_update(float* state, float* x, const float* w, uint32_t dim, uint32_t kwidth);
+void     orc_gdn_inputs(const float* qkv, float* conv_state, const float* conv_w, const float* alpha,
+                        const float* beta_in, const float* dt, const float* a, float* q, float* k, float* v,
+                        float* gate, float* beta, uint32_t n_seqs, uint32_t T, uint32_t conv_chan,
+                        uint32_t kwidth, uint32_t nk, uint32_t hk, uint32_t nv, uint32_t hv, float eps);
 void     orc_rope_store(float* q, float* k, const float* v, uint16_t* kcache, uint16_t* vcache,
                         uint32_t n_heads, uint32_t n_kv, uint32_t hd, uint32_t kv_dim, int kind,
                         uint32_t n_dims, uint32_t pos, float theta);

@@ -37,6 +37,9 @@ _PROTOS = {
     "orc_gdn_state_update": (None, [f32p, f32p, f32p, f32p, f32p, f32p, f32p, u32, u32, u32, u32]),
     "orc_rmsnorm_gated_f32": (None, [f32p, f32p, f32p, f32p, u32, flt]),
     "orc_f32_to_f16_buf": (None, [f32p, u16p, sz]),
+    "orc_conv1d_update": (None, [f32p, f32p, f32p, u32, u32]),
+    "orc_gdn_inputs": (None, [f32p, f32p, f32p, f32p, f32p, f32p, f32p, f32p, f32p, f32p, f32p, f32p, u32, u32, u32,
+                              u32, u32, u32, u32, u32, flt]),
     "orc_rope_store": (None, [f32p, f32p, f32p, u16p, u16p, u32, u32, u32, u32, C.c_int, u32, u32, flt]),
     "orc_f16_to_f32_buf": (None, [u16p, f32p, sz]),
     "orc_attn_decode": (None, [f32p, f32p, u16p, u16p, u32, u32, u32, u32, u32]),

@@ -173,3 +173,87 @@ def test_gdn_prefill_vhead_shards_match_whole(dev, world):
         torch.cuda.synchronize()
         assert torch.equal(out, g.out[:, v0 * D:v1 * D]), f"rank {r} output"
         assert torch.equal(S, S_whole[:, v0:v1]), f"rank {r} state"
+
+
+def _ref_lib():
+    return oracle.load("ref") if oracle.has_ref() else oracle.load("port")
+
+
+@pytest.mark.parametrize("n_seqs,T,nk,hk,nv,hv,kw", [
+    (32, 1, 16, 128, 32, 128, 4),     # config 5b decode step: the qwen35 GDN layer shape
+    (2, 100, 2, 128, 4, 128, 4),      # a prefill chunk with a ragged last tile
+    (3, 2, 2, 64, 6, 64, 4),          # fewer tokens than taps: the delay line keeps old rows
+    (1, 33, 1, 256, 2, 128, 3),       # wide k heads, three taps
+])
+def test_gdn_inputs_matches_reference(dev, n_seqs, T, nk, hk, nv, hv, kw):
+    """yattn_gdn_inputs against engine.c:785-821 run token by token (oracle/_ref's conv1d_update and
+    l2norm_inplace).  Relative error <= 1e-5 (device expf / log1pf); the delay line is moved bit for bit."""
+    from yllm_b200 import attn
+    from test_oracle import _gdn_inputs_case, run_gdn_inputs
+
+    rng = np.random.default_rng(1000 + T)
+    c = _gdn_inputs_case(rng, n_seqs, T, nk, hk, nv, hv, kw)
+    want = run_gdn_inputs(_ref_lib(), c, n_seqs, T, nk, hk, nv, hv, kw)
+    t = {n: torch.from_numpy(np.ascontiguousarray(x)).to(dev) for n, x in c.items()}
+    q = torch.zeros(n_seqs, T, nk * hk, device=dev)
+    k = torch.zeros_like(q)
+    v = torch.zeros(n_seqs, T, nv * hv, device=dev)
+    gate = torch.zeros(n_seqs, T, nv, device=dev)
+    beta = torch.zeros_like(gate)
+    attn.gdn_inputs(t["qkv"], t["state"], t["w"], t["alpha"], t["beta_in"], t["dt"], t["a"], q, k, v, gate, beta,
+                    n_seqs, T, kw, nk, hk, nv, hv, eps=1e-6)
+    torch.cuda.synchronize()
+    assert attn.device_status() == 0
+    for name, got, ref in zip(("q", "k", "v", "gate", "beta"), (q, k, v, gate, beta), want[:5]):
+        e = oracle.rel_err(_np(got), ref.ravel())
+        assert e <= 1e-5, f"{name}: relative error {e:.2e}"
+    assert np.array_equal(_np(t["state"]), want[5].ravel()), "delay line"
+    assert np.array_equal(_np(t["qkv"]), c["qkv"].ravel()), "qkv must not be modified"
+
+
+def test_gdn_layer_decode_from_projections(dev):
+    """A qwen35 GDN layer step on the GPU from its projections: yattn_gdn_inputs, then yattn_gdn_decode with
+    the rmsnorm_gated epilogue, against the oracle doing the same per token (engine.c:785-852)."""
+    from yllm_b200 import attn
+    from test_oracle import _gdn_inputs_case, run_gdn_inputs
+
+    n_seqs, T, nk, hk, nv, hv, kw = 4, 3, 16, 128, 32, 128, 4
+    lib = _ref_lib()
+    rng = np.random.default_rng(77)
+    c = _gdn_inputs_case(rng, n_seqs, T, nk, hk, nv, hv, kw)
+    S0 = (0.05 * rng.standard_normal((n_seqs, nv, hv, hk))).astype(np.float32)
+    z = rng.standard_normal((n_seqs, T, nv * hv)).astype(np.float32)
+    norm_w = (1 + 0.1 * rng.standard_normal(hv)).astype(np.float32)
+    qr, kr, vr, gr, br, _ = run_gdn_inputs(lib, c, n_seqs, T, nk, hk, nv, hv, kw)
+    S_ref = S0.copy()
+    out_ref = np.zeros((n_seqs, T, nv * hv), np.float32)
+    for s in range(n_seqs):
+        for t_ in range(T):
+            o = np.zeros(nv * hv, np.float32)
+            Ss = np.ascontiguousarray(S_ref[s])
+            lib.orc_gdn_step(Ss, o, qr[s, t_], kr[s, t_], vr[s, t_], gr[s, t_], br[s, t_], nk, hk, nv, hv,
+                             norm_w.ctypes.data, np.ascontiguousarray(z[s, t_]).ctypes.data, 1e-6)
+            S_ref[s] = Ss
+            out_ref[s, t_] = o
+    t = {n: torch.from_numpy(np.ascontiguousarray(x)).to(dev) for n, x in c.items()}
+    S = torch.from_numpy(S0).to(dev)
+    zt = torch.from_numpy(z).to(dev)
+    nw = torch.from_numpy(norm_w).to(dev)
+    out = torch.zeros(n_seqs, T, nv * hv, device=dev)
+    q = torch.zeros(n_seqs, 1, nk * hk, device=dev)
+    k = torch.zeros_like(q)
+    v = torch.zeros(n_seqs, 1, nv * hv, device=dev)
+    gate = torch.zeros(n_seqs, 1, nv, device=dev)
+    beta = torch.zeros_like(gate)
+    for t_ in range(T):   # one decode step per token: projections of token t_ of every sequence
+        sl = {n: t[n][:, t_:t_ + 1].contiguous() for n in ("qkv", "alpha", "beta_in")}
+        attn.gdn_inputs(sl["qkv"], t["state"], t["w"], sl["alpha"], sl["beta_in"], t["dt"], t["a"], q, k, v, gate,
+                        beta, n_seqs, 1, kw, nk, hk, nv, hv)
+        o = torch.zeros(n_seqs, nv * hv, device=dev)
+        attn.gdn_decode(S, o, q, k, v, gate, beta, n_seqs, nk, hk, nv, hv, norm_w=nw,
+                        z=zt[:, t_].contiguous(), eps=1e-6)
+        out[:, t_] = o
+    torch.cuda.synchronize()
+    assert attn.device_status() == 0
+    oracle.assert_close(_np(out), out_ref.ravel(), what="GDN layer output")
+    oracle.assert_close(_np(S), S_ref.ravel(), what="GDN state")

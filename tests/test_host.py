@@ -231,3 +231,24 @@ def test_rope_store_rejects_bad_arguments():
     assert lib.yattn_rope_store_kv_batch(fake, fake, fake, fake, fake, 0xFFFFFFF0, 64, 4096, 32, 8, 128, 1024, 0, 0,
                                          1e4, None, err, 256) == -1
     assert b"overflow" in err.value
+
+
+def test_gdn_inputs_rejects_bad_arguments():
+    """yattn_gdn_inputs checks the channel split and the taps on the host, before any launch."""
+    import ctypes as C
+
+    from yllm_b200._lib import lib
+
+    err = C.create_string_buffer(256)
+    f = C.c_void_p(0x1000)   # never dereferenced
+    ptrs = [f] * 12
+    assert lib.yattn_gdn_inputs(*ptrs, 0, 1, 8192, 4, 16, 128, 32, 128, 1e-6, None, err, 256) == 0   # no work
+    assert lib.yattn_gdn_inputs(*ptrs, 1, 1, 10000, 4, 16, 128, 32, 128, 1e-6, None, err, 256) == -1
+    assert b"conv_chan" in err.value
+    assert lib.yattn_gdn_inputs(*ptrs, 1, 1, 8192, 9, 16, 128, 32, 128, 1e-6, None, err, 256) == -1
+    assert b"kwidth" in err.value
+    assert lib.yattn_gdn_inputs(*ptrs, 1, 1, 2 * 512 + 512, 4, 1, 512, 1, 512, 1e-6, None, err, 256) == -1
+    bad = list(ptrs)
+    bad[3] = None
+    assert lib.yattn_gdn_inputs(*bad, 1, 1, 8192, 4, 16, 128, 32, 128, 1e-6, None, err, 256) == -1
+    assert b"null" in err.value

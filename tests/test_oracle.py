@@ -148,6 +148,43 @@ def test_rope_store_port_equals_reference_build(orc, orc_ref):
                 assert np.array_equal(outs[0][1].reshape(KV, hd)[:, nd:], k.reshape(KV, hd)[:, nd:])
 
 
+def _gdn_inputs_case(rng, n_seqs, T, nk, hk, nv, hv, kw):
+    C_ = 2 * nk * hk + nv * hv
+    return dict(qkv=rng.standard_normal((n_seqs, T, C_)).astype(np.float32),
+                state=rng.standard_normal((n_seqs, kw, C_)).astype(np.float32),
+                w=(0.5 * rng.standard_normal((C_, kw))).astype(np.float32),
+                alpha=rng.standard_normal((n_seqs, T, nv)).astype(np.float32),
+                beta_in=rng.standard_normal((n_seqs, T, nv)).astype(np.float32),
+                dt=rng.standard_normal(nv).astype(np.float32),
+                a=-np.abs(rng.standard_normal(nv)).astype(np.float32))
+
+
+def run_gdn_inputs(lib, c, n_seqs, T, nk, hk, nv, hv, kw, eps=1e-6):
+    q = np.zeros((n_seqs, T, nk * hk), np.float32)
+    k = np.zeros_like(q)
+    v = np.zeros((n_seqs, T, nv * hv), np.float32)
+    gate = np.zeros((n_seqs, T, nv), np.float32)
+    beta = np.zeros_like(gate)
+    st = c["state"].copy()
+    lib.orc_gdn_inputs(c["qkv"], st, c["w"], c["alpha"], c["beta_in"], c["dt"], c["a"], q, k, v, gate, beta,
+                       n_seqs, T, 2 * nk * hk + nv * hv, kw, nk, hk, nv, hv, eps)
+    return q, k, v, gate, beta, st
+
+
+def test_gdn_inputs_port_equals_reference_build(orc, orc_ref):
+    """orc_gdn_inputs (engine.c:785-821 per token) with the port's conv1d_update / l2norm against the
+    reference's matvec.c: same bits, including the delay line left behind."""
+    rng = np.random.default_rng(21)
+    for n_seqs, T, nk, hk, nv, hv, kw in ((2, 7, 2, 64, 4, 64, 4), (1, 3, 2, 128, 2, 128, 4), (1, 5, 1, 64, 2, 64, 2)):
+        c = _gdn_inputs_case(rng, n_seqs, T, nk, hk, nv, hv, kw)
+        a = run_gdn_inputs(orc, c, n_seqs, T, nk, hk, nv, hv, kw)
+        b = run_gdn_inputs(orc_ref, c, n_seqs, T, nk, hk, nv, hv, kw)
+        for x, y in zip(a, b):
+            assert np.array_equal(x, y)
+        q = a[0].reshape(n_seqs * T * nk, hk)
+        assert np.allclose(np.linalg.norm(q, axis=1), 1.0, atol=1e-5)   # l2-normalised heads
+
+
 def test_per_head_gdn_call_equals_all_heads_call(orc):
     """orc_gdn_step splits the reference call per head; same bits as one call."""
     rng = np.random.default_rng(9)

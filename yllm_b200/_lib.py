@@ -115,6 +115,7 @@ PROTOS = {
     "yattn_reserve": (C.c_int, [sz, *E]),
     "yattn_store_kv": (C.c_int, [vp, vp, vp, vp, u32, u32, u32, vp, *E]),
     "yattn_rope_store_kv": (C.c_int, [vp, u32, u32, u32, u32, u32, C.c_int, u32, C.c_float, vp, *E]),
+    "yattn_gdn_inputs": (C.c_int, [vp] * 12 + [u32] * 8 + [C.c_float, vp, *E]),
     "yattn_rope_store_kv_batch": (C.c_int, [vp, vp, vp, vp, vp, u32, u32, u32, u32, u32, u32, u32, C.c_int, u32,
                                             C.c_float, vp, *E]),
     "cuda_k_gdn_state_update": (None, [vp, vp, vp, vp, vp, vp, vp, u32, u32, u32, u32]),

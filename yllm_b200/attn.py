@@ -276,6 +276,22 @@ def gdn_decode(S, out, q, k, v, gate, beta, n_seqs: int, num_k_heads: int, hk: i
          _stream(stream))
 
 
+def gdn_inputs(qkv, conv_state, conv_w, alpha, beta_in, ssm_dt, ssm_a, q, k, v, gate, beta, n_seqs: int, T: int,
+               kwidth: int, num_k_heads: int, hk: int, n_vheads: int, hv: int, eps: float = 1e-6,
+               stream=None) -> None:
+    """The GDN layer's inputs for T tokens of n_seqs sequences (engine.c:785-821): gates, conv1d + silu, q/k/v
+    split with l2-normalised q and k heads; conv_state updated in place."""
+    for name, t in (("qkv", qkv), ("conv_state", conv_state), ("conv_w", conv_w), ("alpha", alpha),
+                    ("beta_in", beta_in), ("ssm_dt", ssm_dt), ("ssm_a", ssm_a), ("q", q), ("k", k), ("v", v),
+                    ("gate", gate), ("beta", beta)):
+        _need(t, torch.float32, name)
+    conv_chan = 2 * num_k_heads * hk + n_vheads * hv
+    call("yattn_gdn_inputs", qkv.data_ptr(), conv_state.data_ptr(), conv_w.data_ptr(), alpha.data_ptr(),
+         beta_in.data_ptr(), ssm_dt.data_ptr(), ssm_a.data_ptr(), q.data_ptr(), k.data_ptr(), v.data_ptr(),
+         gate.data_ptr(), beta.data_ptr(), n_seqs, T, conv_chan, kwidth, num_k_heads, hk, n_vheads, hv, float(eps),
+         _stream(stream))
+
+
 def gdn_prefill(S, out, q, k, v, gate, beta, n_seqs: int, T: int, num_k_heads: int, hk: int, n_vheads: int,
                 hv: int, norm_w: Optional[torch.Tensor] = None, z: Optional[torch.Tensor] = None,
                 eps: float = 1e-6, stream=None) -> None:
