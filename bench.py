@@ -909,12 +909,125 @@ def run_rope_store(args) -> None:
         dist.destroy_process_group()
 
 
+def run_sess_kv(args) -> None:
+    """The session KV file of a Llama-3-8B-shaped engine (32 blocks, kv_dim
+    1024, max_seq 8192, every row filled: 1 GiB of K and V) saved from and
+    loaded back into HBM through the library (cache.c:174-247 on the host
+    blob in the reference).  A step is one save plus one load.  The file sits
+    in the host's page cache (tmpfs or disk cache); the bound is the host
+    side: PCIe for the device copies, memory bandwidth for the file copy.
+    Rank 0 only (a host file per GPU adds nothing)."""
+    import ctypes as C
+    import tempfile
+
+    import torch
+
+    from yllm_b200 import attn
+
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", "0")))
+    nb, kd, max_seq, pos = 32, 1024, 8192, 8192
+    n = (2 * nb + 1) * max_seq * kd
+    blob = torch.randint(-32768, 32768, (n,), dtype=torch.int32, device="cuda").to(torch.int16)
+    back = torch.zeros_like(blob)
+    nbytes = 2 * nb * pos * kd * 2
+    # tmpfs where the host has one, so the line measures the library's path and not the box's virtual disk
+    # (a 1 GB write to the disk-backed /tmp runs at its writeback rate, under 2 GB/s for either arm)
+    shm = "/dev/shm" if os.path.isdir("/dev/shm") and os.access("/dev/shm", os.W_OK) else None
+    d = tempfile.mkdtemp(prefix="yattn_sess_", dir=shm)
+    path = os.path.join(d, "s.kv")
+
+    def step():
+        attn.sess_kv_save(blob, nb, kd, max_seq, pos, path)
+        attn.sess_kv_load(back, nb, kd, max_seq, path)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    assert torch.equal(back.view(2 * nb + 1, max_seq, kd)[1:], blob.view(2 * nb + 1, max_seq, kd)[1:])
+    clocks = ClockSampler(0)
+    clocks.start()
+    time.sleep(0.3)
+    clocks.begin()
+    ts, tsave = [], []
+    for _ in range(args.steps):
+        t0 = time.perf_counter()
+        attn.sess_kv_save(blob, nb, kd, max_seq, pos, path)
+        t1 = time.perf_counter()
+        attn.sess_kv_load(back, nb, kd, max_seq, path)
+        ts.append(time.perf_counter() - t0)
+        tsave.append(t1 - t0)
+    clk = clocks.stop()
+    ms = statistics.median(ts) * 1e3
+    save_ms = statistics.median(tsave) * 1e3
+    # the host-side peak this is bound by: pinned D2H + H2D of the same bytes (CUDA events)
+    pin = torch.empty(64 << 20, dtype=torch.uint8, pin_memory=True)
+    src = torch.empty(64 << 20, dtype=torch.uint8, device="cuda")
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    for _ in range(3):
+        pin.copy_(src, non_blocking=True)
+    e0.record()
+    for _ in range(16):
+        pin.copy_(src, non_blocking=True)
+        src.copy_(pin, non_blocking=True)
+    e1.record()
+    torch.cuda.synchronize()
+    pcie = 2 * 16 * (64 << 20) / (e0.elapsed_time(e1) / 1e3) / 1e9
+    ach = 2 * nbytes / (ms / 1e3) / 1e9
+    cpu = None
+    if not args.no_cpu_baseline:
+        sys.path.insert(0, str(ROOT / "tests"))
+        import numpy as np
+        import oracle
+
+        kind = "reference" if oracle.has_ref() else "port"
+        lib = oracle.load("ref" if kind == "reference" else "port")
+        hb = blob.cpu().numpy().view(np.uint16)
+        hback = np.zeros_like(hb)
+        p = C.c_uint32(0)
+        cts, csave = [], []
+        for _ in range(3):
+            t0 = time.perf_counter()
+            lib.orc_sess_kv_save(hb, nb, kd, max_seq, pos, path.encode())
+            t1 = time.perf_counter()
+            lib.orc_sess_kv_load(hback, nb, kd, max_seq, path.encode(), C.byref(p))
+            cts.append(time.perf_counter() - t0)
+            csave.append(t1 - t0)
+        cpu = {"value": round(2 * nbytes / statistics.median(cts) / 1e9, 3), "unit": "GB/s", "cores": 1,
+               "kind": kind, "sample": "the same 1 GiB file saved from and loaded into a host blob, 3x",
+               "save_gbs": round(nbytes / statistics.median(csave) / 1e9, 3)}
+    os.remove(path)
+    os.rmdir(d)
+    roof = {"bound": "pcie", "achieved": round(ach, 2), "peak": round(pcie, 2), "unit": "GB/s",
+            "frac": round(ach / pcie, 4), "traffic": None, "kernel": "cudaMemcpyAsync D2H / H2D via pinned staging",
+            "peak_source": "pinned D2H + H2D copy measured in this run (64 MiB x 16 each way)",
+            "note": "file bytes each way per step / step wall time; the page-cache copy shares the host memory"}
+    line = {"metric": "session KV save + load GB/s (device blob <-> engine session file)", "value": round(ach, 3),
+            "unit": "GB/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 3),
+            "higher_is_better": True, "scaling": "none", "vs_baseline": None, "dtype": "u16 (fp16 bits)",
+            "data": "synthetic (random fp16 bits)",
+            "config": {"workload": "sess-kv-llama3-8b", "n_blocks": nb, "kv_dim": kd, "max_seq": max_seq, "pos": pos,
+                       "file_bytes": 24 + nbytes, "timing": "host wall clock around save + load (host I/O path)",
+                       "save_gbs": round(nbytes / (save_ms / 1e3) / 1e9, 3),
+                       "load_gbs": round(nbytes / ((ms - save_ms) / 1e3) / 1e9, 3), "dir": d},
+            "e2e": {"value": round(ach, 3), "unit": "GB/s", "h2d_bytes_per_step": nbytes, "d2h_bytes_per_step": nbytes,
+                    "path": "yattn_sess_kv_save then yattn_sess_kv_load (the public calls)"},
+            "roofline": roof, "gpu_launches": 0,
+            "clocks": {"sm_mhz": clk["sm_mhz"], "sm_max_mhz": clk["sm_max_mhz"], "reasons": clk["reasons"],
+                       "samples": clk["samples"], "source": clk.get("source")}}
+    if cpu is not None:
+        line["cpu_baseline"] = cpu
+    print(json.dumps(line), flush=True)
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--workload", default="decode",
                     choices=["decode", "prefill", "gated_prefill", "gdn_prefill", "gdn_decode", "long_decode",
-                             "config1_decode", "gated_decode", "rope_store"],
+                             "config1_decode", "gated_decode", "rope_store", "sess_kv"],
                     help="decode = BASELINE config 3 (the default bench line)")
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
@@ -942,6 +1055,8 @@ def main() -> None:
         run_decode_small(args)
     elif args.workload == "rope_store":
         run_rope_store(args)
+    elif args.workload == "sess_kv":
+        run_sess_kv(args)
     else:
         run_long_decode(args)
 

@@ -364,6 +364,22 @@ int yattn_gdn_prefill_recurrent(float* S, float* out, const float* q, const floa
                                 uint32_t n_vheads, uint32_t hv, const float* norm_w,
                                 const float* z, float eps, void* stream, char* err, size_t errlen);
 
+/* ------------------------------------------------ session KV file (device KV)
+ * The engine's session KV file (sess_kv_save / sess_kv_load, cache.c:174-247)
+ * written from and read into a device KV blob in the engine's layout:
+ * 2*n_blocks + 1 regions of max_seq rows x kv_dim fp16 (engine.c:261), block
+ * l in 1..n_blocks using K region l and V region n_blocks + l.  The file holds
+ * the first pos rows of those regions and is byte for byte the reference's, so
+ * either side can read the other's files.  Rows move through pinned staging
+ * buffers, device copies overlapping the file I/O.  Returns 0, or -1 with a
+ * message (a load refuses a file of another n_blocks / kv_dim / max_seq or
+ * with pos > max_seq, like the reference).  Both calls return after the
+ * stream has finished the copies. */
+int yattn_sess_kv_save(const uint16_t* kv_dev, uint32_t n_blocks, uint32_t kv_dim, uint32_t max_seq,
+                       uint32_t pos, const char* path, void* stream, char* err, size_t errlen);
+int yattn_sess_kv_load(uint16_t* kv_dev, uint32_t n_blocks, uint32_t kv_dim, uint32_t max_seq,
+                       const char* path, uint32_t* pos, void* stream, char* err, size_t errlen);
+
 /* ------------------------------------------------ seeded input generator
  * Deterministic on every device and bit-identical to the CPU restatement in
  * the test oracle: splitmix64 (platform.c:411-417) draws, Box-Muller with

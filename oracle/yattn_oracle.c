@@ -21,6 +21,7 @@
 #include "yattn_oracle.h"
 
 #include <math.h>
+#include <stdio.h>
 #include <stdlib.h>
 #include <string.h>
 #ifdef _OPENMP
@@ -262,6 +263,55 @@ void orc_conv1d_update(float* state, float* x, const float* w, uint32_t dim, uin
         for (i = 0; i < kwidth; i++) acc += state[(size_t)i * dim + ch] * w[(size_t)ch * kwidth + i];
         x[ch] = acc;
     }
+}
+
+/* cache.c:174-195: magic (the first 8 bytes of "YLLMSKV01"), n_blocks,
+ * kv_dim, max_seq, pos, then for l = 1..n_blocks the first pos rows of K
+ * region l and of V region n_blocks + l of the (2*n_blocks + 1)-region blob. */
+int orc_sess_kv_save(const uint16_t* kv, uint32_t nb, uint32_t kv_dim, uint32_t max_seq, uint32_t pos,
+                     const char* path)
+{
+    FILE* f = fopen(path, "wb");
+    const uint32_t hdr[4] = {nb, kv_dim, max_seq, pos};
+    const size_t region = (size_t)max_seq * kv_dim, row = (size_t)pos * kv_dim;
+    uint32_t l;
+    int rc = 0;
+    if (!f) return -1;
+    if (fwrite("YLLMSKV0", 1, 8, f) != 8 || fwrite(hdr, 4, 4, f) != 4) rc = -1;
+    for (l = 1; !rc && l <= nb; l++) {
+        if (fwrite(kv + (size_t)l * region, 2, row, f) != row ||
+            fwrite(kv + (size_t)(nb + l) * region, 2, row, f) != row)
+            rc = -1;
+    }
+    fclose(f);
+    return rc;
+}
+
+/* cache.c:219-247: refuses a file whose magic, n_blocks, kv_dim or max_seq
+ * differ from the engine's, or whose pos exceeds max_seq. */
+int orc_sess_kv_load(uint16_t* kv, uint32_t nb, uint32_t kv_dim, uint32_t max_seq, const char* path, uint32_t* pos)
+{
+    FILE* f = fopen(path, "rb");
+    char magic[8];
+    uint32_t hdr[4];
+    uint32_t l;
+    int rc = 0;
+    if (!f) return -1;
+    if (fread(magic, 1, 8, f) != 8 || memcmp(magic, "YLLMSKV0", 8) != 0 || fread(hdr, 4, 4, f) != 4)
+        rc = -1;
+    else if (hdr[0] != nb || hdr[1] != kv_dim || hdr[2] != max_seq || hdr[3] > max_seq)
+        rc = -1;
+    else {
+        const size_t region = (size_t)max_seq * kv_dim, row = (size_t)hdr[3] * kv_dim;
+        for (l = 1; !rc && l <= nb; l++) {
+            if (fread(kv + (size_t)l * region, 2, row, f) != row ||
+                fread(kv + (size_t)(nb + l) * region, 2, row, f) != row)
+                rc = -1;
+        }
+        if (!rc && pos) *pos = hdr[3];
+    }
+    fclose(f);
+    return rc;
 }
 #endif /* ORACLE_LINK_REF */
 

@@ -50,6 +50,10 @@ void     orc_gdn_inputs(const float* qkv, float* conv_state, const float* conv_w
                         const float* beta_in, const float* dt, const float* a, float* q, float* k, float* v,
                         float* gate, float* beta, uint32_t n_seqs, uint32_t T, uint32_t conv_chan,
                         uint32_t kwidth, uint32_t nk, uint32_t hk, uint32_t nv, uint32_t hv, float eps);
+int      orc_sess_kv_save(const uint16_t* kv, uint32_t nb, uint32_t kv_dim, uint32_t max_seq, uint32_t pos,
+                          const char* path);
+int      orc_sess_kv_load(uint16_t* kv, uint32_t nb, uint32_t kv_dim, uint32_t max_seq, const char* path,
+                          uint32_t* pos);
 void     orc_rope_store(float* q, float* k, const float* v, uint16_t* kcache, uint16_t* vcache,
                         uint32_t n_heads, uint32_t n_kv, uint32_t hd, uint32_t kv_dim, int kind,
                         uint32_t n_dims, uint32_t pos, float theta);

@@ -40,6 +40,8 @@ _PROTOS = {
     "orc_conv1d_update": (None, [f32p, f32p, f32p, u32, u32]),
     "orc_gdn_inputs": (None, [f32p, f32p, f32p, f32p, f32p, f32p, f32p, f32p, f32p, f32p, f32p, f32p, u32, u32, u32,
                               u32, u32, u32, u32, u32, flt]),
+    "orc_sess_kv_save": (C.c_int, [u16p, u32, u32, u32, u32, C.c_char_p]),
+    "orc_sess_kv_load": (C.c_int, [u16p, u32, u32, u32, C.c_char_p, C.POINTER(u32)]),
     "orc_rope_store": (None, [f32p, f32p, f32p, u16p, u16p, u32, u32, u32, u32, C.c_int, u32, u32, flt]),
     "orc_f16_to_f32_buf": (None, [u16p, f32p, sz]),
     "orc_attn_decode": (None, [f32p, f32p, u16p, u16p, u32, u32, u32, u32, u32]),

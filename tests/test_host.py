@@ -252,3 +252,32 @@ def test_gdn_inputs_rejects_bad_arguments():
     bad[3] = None
     assert lib.yattn_gdn_inputs(*bad, 1, 1, 8192, 4, 16, 128, 32, 128, 1e-6, None, err, 256) == -1
     assert b"null" in err.value
+
+
+def test_sess_kv_checks_before_touching_the_device(tmp_path):
+    """The session KV calls check their arguments and the file header on the host before any device copy
+    (a fake device pointer is never dereferenced)."""
+    import ctypes as C
+    import struct
+
+    from yllm_b200._lib import lib
+
+    err = C.create_string_buffer(256)
+    fake = C.c_void_p(0x1000)
+    p = C.c_uint32(7)
+    path = tmp_path / "x.kv"
+    path.write_bytes(b"YLLMSKV0" + struct.pack("<4I", 2, 128, 16, 5))
+    assert lib.yattn_sess_kv_load(fake, 3, 128, 16, str(path).encode(), C.byref(p), None, err, 256) == -1
+    assert b"n_blocks=2" in err.value and p.value == 7
+    assert lib.yattn_sess_kv_load(fake, 2, 256, 16, str(path).encode(), C.byref(p), None, err, 256) == -1
+    assert lib.yattn_sess_kv_load(fake, 2, 128, 17, str(path).encode(), C.byref(p), None, err, 256) == -1
+    path.write_bytes(b"YLLMSKV0" + struct.pack("<4I", 2, 128, 16, 17))    # pos > max_seq
+    assert lib.yattn_sess_kv_load(fake, 2, 128, 16, str(path).encode(), C.byref(p), None, err, 256) == -1
+    path.write_bytes(b"YLLMSESS" + struct.pack("<4I", 2, 128, 16, 5))    # the token file's magic
+    assert lib.yattn_sess_kv_load(fake, 2, 128, 16, str(path).encode(), C.byref(p), None, err, 256) == -1
+    assert b"not a session KV file" in err.value
+    assert lib.yattn_sess_kv_load(fake, 2, 128, 16, str(tmp_path / "missing").encode(), C.byref(p), None, err,
+                                  256) == -1
+    assert lib.yattn_sess_kv_save(fake, 2, 128, 16, 17, str(path).encode(), None, err, 256) == -1
+    assert b"pos 17 > max_seq 16" in err.value
+    assert lib.yattn_sess_kv_save(None, 2, 128, 16, 5, str(path).encode(), None, err, 256) == -1

@@ -185,6 +185,31 @@ def test_gdn_inputs_port_equals_reference_build(orc, orc_ref):
         assert np.allclose(np.linalg.norm(q, axis=1), 1.0, atol=1e-5)   # l2-normalised heads
 
 
+def test_sess_kv_port_equals_reference_build(orc, orc_ref, tmp_path):
+    """The session KV file (cache.c:174-247): the restated writer makes the reference's bytes, and both
+    loaders read either file back into the same regions, refusing a different geometry."""
+    rng = np.random.default_rng(3)
+    nb, kd, max_seq = 3, 64, 40
+    blob = rng.integers(0, 1 << 16, (2 * nb + 1) * max_seq * kd, dtype=np.uint16)
+    for pos in (0, 1, 17, max_seq):
+        fa, fb = tmp_path / f"a{pos}.kv", tmp_path / f"b{pos}.kv"
+        assert orc.orc_sess_kv_save(blob, nb, kd, max_seq, pos, str(fa).encode()) == 0
+        assert orc_ref.orc_sess_kv_save(blob, nb, kd, max_seq, pos, str(fb).encode()) == 0
+        assert fa.read_bytes() == fb.read_bytes()
+        assert len(fa.read_bytes()) == 24 + 2 * nb * pos * kd * 2
+        for lib in (orc, orc_ref):
+            back = np.zeros_like(blob)
+            p = C.c_uint32(99)
+            assert lib.orc_sess_kv_load(back, nb, kd, max_seq, str(fa).encode(), C.byref(p)) == 0
+            assert p.value == pos
+            want = np.zeros_like(blob).reshape(2 * nb + 1, max_seq, kd)
+            src = blob.reshape(2 * nb + 1, max_seq, kd)
+            want[1:, :pos] = src[1:, :pos]
+            assert np.array_equal(back.reshape(want.shape), want)
+            assert lib.orc_sess_kv_load(back, nb + 1, kd, max_seq, str(fa).encode(), C.byref(p)) == -1
+            assert lib.orc_sess_kv_load(back, nb, kd, max_seq + 1, str(fa).encode(), C.byref(p)) == -1
+
+
 def test_per_head_gdn_call_equals_all_heads_call(orc):
     """orc_gdn_step splits the reference call per head; same bits as one call."""
     rng = np.random.default_rng(9)

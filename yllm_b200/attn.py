@@ -11,6 +11,7 @@ library, and a missing library fails at import.
 from __future__ import annotations
 
 import ctypes as C
+import os
 from dataclasses import dataclass
 from typing import Optional, Sequence
 
@@ -312,6 +313,25 @@ def gdn_prefill_recurrent(S, out, q, k, v, gate, beta, n_seqs: int, T: int, num_
     call("yattn_gdn_prefill_recurrent", S.data_ptr(), out.data_ptr(), q.data_ptr(), k.data_ptr(), v.data_ptr(),
          gate.data_ptr(), beta.data_ptr(), n_seqs, T, num_k_heads, hk, n_vheads, hv, _ptr(norm_w), _ptr(z),
          float(eps), _stream(stream))
+
+
+def sess_kv_save(kv: torch.Tensor, n_blocks: int, kv_dim: int, max_seq: int, pos: int, path: str,
+                 stream=None) -> None:
+    """Writes the first pos rows of every block's K and V regions of the device blob kv
+    ([2*n_blocks+1][max_seq][kv_dim] fp16) as the engine's session KV file (cache.c:174-195)."""
+    if kv.numel() * kv.element_size() < (2 * n_blocks + 1) * max_seq * kv_dim * 2:
+        raise ValueError("kv is smaller than the (2*n_blocks+1)-region blob")
+    call("yattn_sess_kv_save", kv.data_ptr(), n_blocks, kv_dim, max_seq, pos, os.fsencode(path), _stream(stream))
+
+
+def sess_kv_load(kv: torch.Tensor, n_blocks: int, kv_dim: int, max_seq: int, path: str, stream=None) -> int:
+    """Reads an engine session KV file into the device blob kv; returns the file's pos (cache.c:219-247)."""
+    if kv.numel() * kv.element_size() < (2 * n_blocks + 1) * max_seq * kv_dim * 2:
+        raise ValueError("kv is smaller than the (2*n_blocks+1)-region blob")
+    p = C.c_uint32(0)
+    call("yattn_sess_kv_load", kv.data_ptr(), n_blocks, kv_dim, max_seq, os.fsencode(path), C.byref(p),
+         _stream(stream))
+    return p.value
 
 
 def device_status(clear: bool = True) -> int:
