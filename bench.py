@@ -909,6 +909,109 @@ def run_rope_store(args) -> None:
         dist.destroy_process_group()
 
 
+def run_gemv(args) -> None:
+    """The per-layer linear layers of a Llama-3-8B decode step with Q4_K
+    weights (cuda_fwd.c:94-168 brackets attention with these GEMVs): per
+    layer q, k, v, o (4096/1024 x 4096), gate and up (14336 x 4096) and down
+    (4096 x 14336), 218 M weights = 123 MB; 32 layers, each with its own
+    weights (3.9 GB, far above L2).  One step = 224 launches replayed as a
+    CUDA graph.  Bound: HBM on the weight bytes.  Weak scaling: each rank
+    streams its own copy."""
+    import ctypes as C
+
+    import torch
+    import torch.distributed as dist
+
+    from yllm_b200 import attn, dist as ydist
+
+    rank, world, local = ydist.init("nccl" if args.gpus > 1 else "gloo")
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    stream = torch.cuda.current_stream()
+    L, H = 32, 4096
+    shapes = [(4096, H), (1024, H), (1024, H), (H, 4096), (14336, H), (14336, H), (H, 14336)]
+    per_layer = sum(o * (i // 256) * 144 for o, i in shapes)
+    g = torch.Generator(device=dev)
+    g.manual_seed(7 + rank)
+    wbuf = torch.randint(0, 256, (L * per_layer,), dtype=torch.uint8, device=dev, generator=g)
+    # d and dmin of every block: small positive fp16 so the outputs stay finite
+    blocks = wbuf.view(-1, 144)
+    dd = (torch.rand(blocks.shape[0], 2, device=dev, generator=g) * 1e-3 + 5e-4).half()
+    blocks[:, 0:4] = dd.view(torch.uint8).view(-1, 4)
+    xs = {i: torch.randn(i, device=dev, generator=g) for i in (H, 14336)}
+    ys = {o: torch.empty(o, device=dev) for o in (1024, 4096, 14336)}
+    mats = []
+    off = 0
+    for l in range(L):
+        for o, i in shapes:
+            n = o * (i // 256) * 144
+            mats.append((wbuf[off:off + n], o, i))
+            off += n
+
+    def step():
+        for w, o, i in mats:
+            attn.gemv_q4k(ys[o], w, xs[i], o, i, 1)
+
+    ms, per_call, clk = _timed(step, args, stream, world, dist, local, graph=True)
+    step_bytes = L * per_layer
+    peaks, src = load_peaks()
+    ach = step_bytes / (per_call / 1e3) / 1e9
+    roof = {"bound": "hbm", "achieved": round(ach, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
+            "frac": round(ach / peaks["hbm_gbs"], 4), "traffic": None, "kernel": "k_gemv_q4k<4,1>",
+            "peak_source": src, "bytes_per_step": step_bytes,
+            "note": "224 launches per step in one graph; achieved = Q4_K weight bytes / step device time"}
+    e2e = None
+    if not args.no_e2e:
+        hx = torch.empty(H, dtype=torch.float32, pin_memory=True)
+        hx.copy_(xs[H].cpu())
+        hy = torch.empty(H, dtype=torch.float32, pin_memory=True)
+
+        def e2e_step():
+            xs[H].copy_(hx, non_blocking=True)
+            step()
+            hy.copy_(ys[4096], non_blocking=True)
+
+        ems, _, _ = _timed(e2e_step, args, stream, world, dist, local)
+        e2e = {"value": round(world / (ems / 1e3), 2), "unit": "tok/s", "h2d_bytes_per_step": H * 4 * world,
+               "d2h_bytes_per_step": H * 4 * world, "path": "yattn_gemv_q4k per matrix per step (no graph), "
+                                                            "pinned x in, y back"}
+    cpu = None
+    if rank == 0 and not args.no_cpu_baseline:
+        import numpy as np
+
+        sys.path.insert(0, str(ROOT / "tests"))
+        import oracle
+
+        kind = "reference" if oracle.has_ref() else "port"
+        lib = oracle.load("ref" if kind == "reference" else "port")
+        lib.orc_set_threads(len(os.sched_getaffinity(0)))
+        host = [(mats[j][0].cpu().numpy(), mats[j][1], mats[j][2]) for j in range(len(shapes))]   # layer 0
+        hxs = {i: xs[i].cpu().numpy() for i in xs}
+        hys = {o: np.zeros(o, np.float32) for o in ys}
+        times = []
+        while not times or (sum(times) < min(args.cpu_budget, 10.0) and len(times) < 20):
+            t0 = time.perf_counter()
+            for w, o, i in host:
+                lib.orc_matmul_q4k(hys[o], hxs[i], w, o, i)
+            times.append(time.perf_counter() - t0)
+        step_s = statistics.median(times) * L
+        cpu = {"value": round(1 / step_s, 3), "unit": "tok/s", "cores": int(lib.orc_max_threads()), "kind": kind,
+               "sample": f"layer 0's seven Q4_K matmuls (matvec.c:514, the engine's AVX2 path), timed "
+                         f"{len(times)}x, x{L} layers"}
+    if rank == 0:
+        line = _line(args, world, "Q4_K linear layers tok/s (Llama-3-8B decode step, 32 layers, batch 1)",
+                     world / (ms / 1e3), "tok/s", ms,
+                     {"workload": "llama3-8b-q4k-gemv-decode", "layers": L, "hidden": H, "ffn": 14336,
+                      "weight_bytes_per_step": step_bytes, "parallelism": f"replicas x{world}",
+                      "launch": "CUDA graph replay of the step", "l2": "weights per step 3.9 GB > L2"},
+                     roof, args.steps * len(mats), clk, e2e, cpu=cpu, scaling="weak")
+        line["dtype"] = "Q4_K weights, f32 x and accumulation"
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
 def run_sess_kv(args) -> None:
     """The session KV file of a Llama-3-8B-shaped engine (32 blocks, kv_dim
     1024, max_seq 8192, every row filled: 1 GiB of K and V) saved from and
@@ -1027,7 +1130,7 @@ def main() -> None:
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--workload", default="decode",
                     choices=["decode", "prefill", "gated_prefill", "gdn_prefill", "gdn_decode", "long_decode",
-                             "config1_decode", "gated_decode", "rope_store", "sess_kv"],
+                             "config1_decode", "gated_decode", "rope_store", "sess_kv", "gemv"],
                     help="decode = BASELINE config 3 (the default bench line)")
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
@@ -1057,6 +1160,8 @@ def main() -> None:
         run_rope_store(args)
     elif args.workload == "sess_kv":
         run_sess_kv(args)
+    elif args.workload == "gemv":
+        run_gemv(args)
     else:
         run_long_decode(args)
 

@@ -364,6 +364,33 @@ int yattn_gdn_prefill_recurrent(float* S, float* out, const float* q, const floa
                                 uint32_t n_vheads, uint32_t hv, const float* norm_w,
                                 const float* z, float eps, void* stream, char* err, size_t errlen);
 
+/* ------------------------------------------------ linear layers (decode glue)
+ * y = W x for the engine's weight formats, W row-major [out][in]:
+ *   Q4_K: 144-byte blocks of 256 weights (fp16 d, dmin; 12 bytes of 6-bit
+ *         scales/mins; 128 bytes of nibbles), in % 256 == 0;
+ *   fp16: [out][in] uint16_t.
+ * x fp32 [B][in], y fp32 [B][out] (token t at row t).  Every weight byte is
+ * read once per 4 tokens; fp32 accumulation with x kept fp32.  x and a Q4_K w
+ * must be 16-byte aligned; fp16 takes any in and alignment (a slower path
+ * unless in % 8 == 0 and both are 16-byte aligned).  Returns 0 or -1 + err. */
+int yattn_gemv_q4k(float* y, const uint8_t* w, const float* x, uint32_t out, uint32_t in, uint32_t B,
+                   void* stream, char* err, size_t errlen);
+int yattn_gemv_f16(float* y, const uint16_t* w, const float* x, uint32_t out, uint32_t in, uint32_t B,
+                   void* stream, char* err, size_t errlen);
+
+/* Drop-ins with the reference's names and signatures (cuda_kernels.h; kernels
+ * cuda_kernels.cu:36-249), legacy default stream.  The f16 pair accepts the
+ * reference's cuBLAS handle and fp16 x scratch and uses neither: x stays fp32
+ * (the reference's cuBLAS path rounds x to fp16). */
+int cuda_k_gemv_q4k(float* y, const uint8_t* w, const float* x, uint32_t out, uint32_t in,
+                    char* err, size_t errlen);
+int cuda_k_gemm_q4k(float* y, const uint8_t* w, const float* x, uint32_t out, uint32_t in,
+                    uint32_t B, char* err, size_t errlen);
+int cuda_k_gemv_f16(void* cublas, float* y, const uint16_t* w, const float* x, uint16_t* xf16,
+                    uint32_t out, uint32_t in, char* err, size_t errlen);
+int cuda_k_gemm_f16(void* cublas, float* y, const uint16_t* w, const float* x, uint16_t* xf16,
+                    uint32_t out, uint32_t in, uint32_t B, char* err, size_t errlen);
+
 /* ------------------------------------------------ session KV file (device KV)
  * The engine's session KV file (sess_kv_save / sess_kv_load, cache.c:174-247)
  * written from and read into a device KV blob in the engine's layout:

@@ -44,6 +44,10 @@ void     gdn_state_update(float* S, float* out, const float* q, const float* k,
 void     rmsnorm_gated(float* y, const float* x, const uint8_t* w, const float* z,
                        uint32_t n, float eps, uint32_t dtype);
 void     conv1d_update(float* state, const float* x, const uint8_t* w, uint32_t dim, uint32_t kwidth);
+void     q4k_block(float* y, const uint8_t* blk, uint32_t stride);
+void     matmul(float* y, const float* x, const uint8_t* w, uint32_t out, uint32_t in, uint32_t dtype);
+#define REF_DT_F16 0u   /* DT_F16, inference/include/llf.h:14 */
+#define REF_DT_Q4K 3u   /* DT_Q4K, inference/include/llf.h:17 */
 #define REF_DT_F32 1u   /* DT_F32, inference/include/llf.h:15 */
 
 int orc_build_kind(void) { return 1; }
@@ -64,6 +68,13 @@ void orc_rmsnorm_gated_f32(float* y, const float* x, const float* w, const float
 { rmsnorm_gated(y, x, (const uint8_t*)w, z, n, eps, REF_DT_F32); }
 void orc_conv1d_update(float* state, float* x, const float* w, uint32_t dim, uint32_t kwidth)
 { conv1d_update(state, x, (const uint8_t*)w, dim, kwidth); }
+void orc_q4k_block(float* y, const uint8_t* blk) { q4k_block(y, blk, 0); }
+/* the engine's CPU matmul of one token (matvec.c:787-797): fp16 rows, or Q4_K
+ * (the AVX2 build quantises x to int8 first, matvec.c:514-520) */
+void orc_matmul_f16(float* y, const float* x, const uint16_t* w, uint32_t out, uint32_t in)
+{ matmul(y, x, (const uint8_t*)w, out, in, REF_DT_F16); }
+void orc_matmul_q4k(float* y, const float* x, const uint8_t* w, uint32_t out, uint32_t in)
+{ matmul(y, x, w, out, in, REF_DT_Q4K); }
 
 #else  /* ---------------- restated helpers ("port") ---------------- */
 
@@ -313,6 +324,54 @@ int orc_sess_kv_load(uint16_t* kv, uint32_t nb, uint32_t kv_dim, uint32_t max_se
     fclose(f);
     return rc;
 }
+
+/* matvec.c:26-35: 6-bit scale and min of group j from the 12 scale bytes. */
+static void scale_min_k4(int j, const uint8_t* q, uint8_t* d, uint8_t* m)
+{
+    if (j < 4) {
+        *d = q[j] & 63;
+        *m = q[j + 4] & 63;
+    } else {
+        *d = (q[j + 4] & 0xF) | ((q[j - 4] >> 6) << 4);
+        *m = (q[j + 4] >> 4) | ((q[j] >> 6) << 4);
+    }
+}
+
+/* matvec.c:40-59: 256 weights of a 144-byte Q4_K block, d*sc*nib - dmin*mn. */
+void orc_q4k_block(float* y, const uint8_t* blk)
+{
+    float d = orc_f16_to_f32(((const uint16_t*)blk)[0]);
+    float mn = orc_f16_to_f32(((const uint16_t*)blk)[1]);
+    uint32_t g, e;
+    for (g = 0; g < 8; g++) {
+        uint8_t sc, m;
+        scale_min_k4((int)g, blk + 4, &sc, &m);
+        float d1 = d * (float)sc, m1 = mn * (float)m;
+        const uint8_t* q = blk + 16 + (g >> 1) * 32;
+        for (e = 0; e < 32; e++) {
+            uint8_t nib = (g & 1) ? (q[e] >> 4) : (q[e] & 0xF);
+            y[g * 32 + e] = d1 * (float)nib - m1;
+        }
+    }
+}
+
+/* matvec.c:111-122 (row-major fp16, fp32 accumulation in index order). */
+void orc_matmul_f16(float* y, const float* x, const uint16_t* w, uint32_t out, uint32_t in)
+{
+    uint32_t oo;
+    #pragma omp parallel for schedule(static)
+    for (oo = 0; oo < out; oo++) {
+        float acc = 0.0f;
+        uint32_t ii;
+        for (ii = 0; ii < in; ii++) acc += x[ii] * orc_f16_to_f32(w[(size_t)oo * in + ii]);
+        y[oo] = acc;
+    }
+}
+
+void orc_gemv_q4k(float* y, const uint8_t* w, const float* x, uint32_t out, uint32_t in, uint32_t B);
+/* The port has no int8 path: its Q4_K matmul is the fp32 one. */
+void orc_matmul_q4k(float* y, const float* x, const uint8_t* w, uint32_t out, uint32_t in)
+{ orc_gemv_q4k(y, w, x, out, in, 1); }
 #endif /* ORACLE_LINK_REF */
 
 int orc_max_threads(void)
@@ -345,6 +404,38 @@ void orc_f16_to_f32_buf(const uint16_t* src, float* dst, size_t n)
 {
     size_t i;
     for (i = 0; i < n; i++) dst[i] = orc_f16_to_f32(src[i]);
+}
+
+/* ---------------- linear layers ---------------- */
+
+/* y[t][o] = sum over the row of x[t][i] * w(o, i) with every Q4_K weight
+ * dequantised to fp32 as the reference does (q4k_block, matvec.c:40-59; the
+ * same d*sc*nib - dmin*mn as its GPU kernel, cuda_kernels.cu:142-159), summed
+ * in index order in fp32.  x [B][in], y [B][out]. */
+void orc_gemv_q4k(float* y, const uint8_t* w, const float* x, uint32_t out, uint32_t in, uint32_t B)
+{
+    const uint32_t nb = in / 256;
+    uint32_t t, oo;
+    for (t = 0; t < B; t++) {
+        #pragma omp parallel for schedule(static)
+        for (oo = 0; oo < out; oo++) {
+            float tmp[256];
+            float acc = 0.0f;
+            uint32_t b, e;
+            for (b = 0; b < nb; b++) {
+                orc_q4k_block(tmp, w + ((size_t)oo * nb + b) * 144);
+                for (e = 0; e < 256; e++) acc += x[(size_t)t * in + b * 256 + e] * tmp[e];
+            }
+            y[(size_t)t * out + oo] = acc;
+        }
+    }
+}
+
+/* The engine's fp16 matmul (matvec.c:111-122) for each of B tokens. */
+void orc_gemv_f16(float* y, const uint16_t* w, const float* x, uint32_t out, uint32_t in, uint32_t B)
+{
+    uint32_t t;
+    for (t = 0; t < B; t++) orc_matmul_f16(y + (size_t)t * out, x + (size_t)t * in, w, out, in);
 }
 
 /* ---------------- qwen35 GDN layer inputs ---------------- */

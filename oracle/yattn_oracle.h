@@ -54,6 +54,11 @@ int      orc_sess_kv_save(const uint16_t* kv, uint32_t nb, uint32_t kv_dim, uint
                           const char* path);
 int      orc_sess_kv_load(uint16_t* kv, uint32_t nb, uint32_t kv_dim, uint32_t max_seq, const char* path,
                           uint32_t* pos);
+void     orc_q4k_block(float* y, const uint8_t* blk);
+void     orc_matmul_f16(float* y, const float* x, const uint16_t* w, uint32_t out, uint32_t in);
+void     orc_matmul_q4k(float* y, const float* x, const uint8_t* w, uint32_t out, uint32_t in);
+void     orc_gemv_q4k(float* y, const uint8_t* w, const float* x, uint32_t out, uint32_t in, uint32_t B);
+void     orc_gemv_f16(float* y, const uint16_t* w, const float* x, uint32_t out, uint32_t in, uint32_t B);
 void     orc_rope_store(float* q, float* k, const float* v, uint16_t* kcache, uint16_t* vcache,
                         uint32_t n_heads, uint32_t n_kv, uint32_t hd, uint32_t kv_dim, int kind,
                         uint32_t n_dims, uint32_t pos, float theta);

@@ -21,6 +21,7 @@ REF_SO = ORACLE_DIR / "_ref" / "libyattn_ref.so"
 
 f32p = np.ctypeslib.ndpointer(dtype=np.float32, flags="C_CONTIGUOUS")
 u16p = np.ctypeslib.ndpointer(dtype=np.uint16, flags="C_CONTIGUOUS")
+u8p = np.ctypeslib.ndpointer(dtype=np.uint8, flags="C_CONTIGUOUS")
 u32, u64, sz, dbl, flt, vp = C.c_uint32, C.c_uint64, C.c_size_t, C.c_double, C.c_float, C.c_void_p
 
 _PROTOS = {
@@ -42,6 +43,11 @@ _PROTOS = {
                               u32, u32, u32, u32, u32, flt]),
     "orc_sess_kv_save": (C.c_int, [u16p, u32, u32, u32, u32, C.c_char_p]),
     "orc_sess_kv_load": (C.c_int, [u16p, u32, u32, u32, C.c_char_p, C.POINTER(u32)]),
+    "orc_q4k_block": (None, [f32p, u8p]),
+    "orc_matmul_f16": (None, [f32p, f32p, u16p, u32, u32]),
+    "orc_matmul_q4k": (None, [f32p, f32p, u8p, u32, u32]),
+    "orc_gemv_q4k": (None, [f32p, u8p, f32p, u32, u32, u32]),
+    "orc_gemv_f16": (None, [f32p, u16p, f32p, u32, u32, u32]),
     "orc_rope_store": (None, [f32p, f32p, f32p, u16p, u16p, u32, u32, u32, u32, C.c_int, u32, u32, flt]),
     "orc_f16_to_f32_buf": (None, [u16p, f32p, sz]),
     "orc_attn_decode": (None, [f32p, f32p, u16p, u16p, u32, u32, u32, u32, u32]),

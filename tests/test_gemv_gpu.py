@@ -1,0 +1,98 @@
+"""GPU parity of the linear-layer glue (yattn_gemv_q4k / _f16 and the
+cuda_k_gemv_* / cuda_k_gemm_* drop-ins) against the oracle: Q4_K weights
+dequantised by the reference's q4k_block (matvec.c:40-59) and summed in fp32
+(the arithmetic of cuda_kernels.cu:142-159); fp16 rows through the engine's
+matmul (matvec.c:111-122).  The GPU sums in another order: relative error
+<= 2e-5 (against max(|cpu|, rms(cpu)))."""
+import ctypes as C
+
+import numpy as np
+import pytest
+import torch
+
+import oracle
+
+pytestmark = pytest.mark.gpu
+TOL = 2e-5
+
+
+@pytest.fixture(scope="module")
+def dev():
+    assert torch.cuda.is_available(), "GPU tests need a CUDA device"
+    torch.cuda.set_device(0)
+    return torch.device("cuda:0")
+
+
+def _ref_lib():
+    return oracle.load("ref") if oracle.has_ref() else oracle.load("port")
+
+
+def q4k_weights(rng, out, in_):
+    """Random Q4_K rows: d, dmin small fp16, random 6-bit scales/mins and nibbles."""
+    nb = in_ // 256
+    blk = rng.integers(0, 256, (out, nb, 144), dtype=np.uint8)
+    d = (rng.uniform(0.5, 2.0, (out, nb)) * 1e-3).astype(np.float16)
+    dmin = (rng.uniform(0.5, 2.0, (out, nb)) * 1e-3).astype(np.float16)
+    blk[:, :, 0:2] = d.view(np.uint8).reshape(out, nb, 2)
+    blk[:, :, 2:4] = dmin.view(np.uint8).reshape(out, nb, 2)
+    return np.ascontiguousarray(blk.reshape(-1))
+
+
+@pytest.mark.parametrize("out,in_,B", [(4096, 4096, 1), (1000, 512, 3), (14336, 4096, 4), (96, 2048, 9)])
+def test_gemv_q4k_matches_reference(dev, out, in_, B):
+    from yllm_b200 import attn
+
+    rng = np.random.default_rng(out + in_ + B)
+    w = q4k_weights(rng, out, in_)
+    x = rng.standard_normal((B, in_)).astype(np.float32)
+    want = np.zeros((B, out), np.float32)
+    _ref_lib().orc_gemv_q4k(want, w, x, out, in_, B)
+    tw, tx = torch.from_numpy(w).to(dev), torch.from_numpy(x).to(dev)
+    y = torch.zeros(B, out, device=dev)
+    attn.gemv_q4k(y, tw, tx, out, in_, B)
+    torch.cuda.synchronize()
+    e = oracle.rel_err(y.cpu().numpy(), want)
+    assert e <= TOL, f"relative error {e:.2e}"
+
+
+@pytest.mark.parametrize("out,in_,B", [(4096, 4096, 1), (1000, 1003, 2), (11008, 4096, 4), (64, 4096, 6)])
+def test_gemv_f16_matches_engine_matmul(dev, out, in_, B):
+    from yllm_b200 import attn
+
+    rng = np.random.default_rng(out * 3 + in_ + B)
+    w = (0.02 * rng.standard_normal((out, in_))).astype(np.float16).view(np.uint16).reshape(-1)
+    x = rng.standard_normal((B, in_)).astype(np.float32)
+    want = np.zeros((B, out), np.float32)
+    _ref_lib().orc_gemv_f16(want, np.ascontiguousarray(w), x, out, in_, B)
+    tw = torch.from_numpy(w.view(np.int16)).to(dev)
+    tx = torch.from_numpy(x).to(dev)
+    y = torch.zeros(B, out, device=dev)
+    attn.gemv_f16(y, tw, tx, out, in_, B)
+    torch.cuda.synchronize()
+    e = oracle.rel_err(y.cpu().numpy(), want)
+    assert e <= TOL, f"relative error {e:.2e}"
+
+
+def test_gemv_dropins_match(dev):
+    """The reference-named entry points give the same bits as the yattn_ calls they wrap."""
+    from yllm_b200 import attn
+    from yllm_b200._lib import lib
+
+    rng = np.random.default_rng(5)
+    out, in_, B = 512, 1024, 3
+    w4 = torch.from_numpy(q4k_weights(rng, out, in_)).to(dev)
+    w16 = torch.from_numpy((0.02 * rng.standard_normal((out, in_))).astype(np.float16).view(np.int16)).to(dev)
+    x = torch.from_numpy(rng.standard_normal((B, in_)).astype(np.float32)).to(dev)
+    err = C.create_string_buffer(256)
+    for name_v, name_m, w, fn, extra in (("cuda_k_gemv_q4k", "cuda_k_gemm_q4k", w4, attn.gemv_q4k, ()),
+                                         ("cuda_k_gemv_f16", "cuda_k_gemm_f16", w16, attn.gemv_f16, (None,))):
+        ya, yb, yc, y1 = (torch.zeros(B, out, device=dev) for _ in range(4))
+        fn(ya, w, x, out, in_, B)
+        fn(y1, w, x, out, in_, 1)   # one token takes the single-token kernel, as the GEMV drop-in does
+        pre = extra
+        args_v = (*pre, yb.data_ptr(), w.data_ptr(), x.data_ptr(), *(() if not pre else (None,)), out, in_)
+        assert getattr(lib, name_v)(*args_v, err, 256) == 0, err.value
+        args_m = (*pre, yc.data_ptr(), w.data_ptr(), x.data_ptr(), *(() if not pre else (None,)), out, in_, B)
+        assert getattr(lib, name_m)(*args_m, err, 256) == 0, err.value
+        torch.cuda.synchronize()
+        assert torch.equal(yb[0], y1[0]) and torch.equal(yc, ya), name_v

@@ -281,3 +281,20 @@ def test_sess_kv_checks_before_touching_the_device(tmp_path):
     assert lib.yattn_sess_kv_save(fake, 2, 128, 16, 17, str(path).encode(), None, err, 256) == -1
     assert b"pos 17 > max_seq 16" in err.value
     assert lib.yattn_sess_kv_save(None, 2, 128, 16, 5, str(path).encode(), None, err, 256) == -1
+
+
+def test_gemv_checks_arguments():
+    """The linear-layer calls reject a Q4_K row that is not whole blocks and unaligned Q4_K operands on the host."""
+    import ctypes as C
+
+    from yllm_b200._lib import lib
+
+    err = C.create_string_buffer(256)
+    f = C.c_void_p(0x1000)
+    assert lib.yattn_gemv_q4k(f, f, f, 64, 300, 1, None, err, 256) == -1
+    assert b"multiple of 256" in err.value
+    assert lib.yattn_gemv_q4k(f, C.c_void_p(0x1004), f, 64, 256, 1, None, err, 256) == -1
+    assert b"aligned" in err.value
+    assert lib.cuda_k_gemv_q4k(f, f, f, 0, 256, err, 256) == -1
+    assert lib.cuda_k_gemm_f16(None, f, f, f, None, 64, 64, 0, err, 256) == -1
+    assert lib.yattn_gemv_f16(None, f, f, 64, 64, 1, None, err, 256) == -1

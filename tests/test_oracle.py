@@ -210,6 +210,49 @@ def test_sess_kv_port_equals_reference_build(orc, orc_ref, tmp_path):
             assert lib.orc_sess_kv_load(back, nb, kd, max_seq + 1, str(fa).encode(), C.byref(p)) == -1
 
 
+def _q4k_decode_numpy(blk):
+    """An independent numpy decoder of one 144-byte Q4_K block (the published GGML layout)."""
+    d = float(np.frombuffer(blk[0:2].tobytes(), np.float16)[0])
+    dmin = float(np.frombuffer(blk[2:4].tobytes(), np.float16)[0])
+    q = blk[4:16].astype(np.int64)
+    out = np.zeros(256, np.float64)
+    for g in range(8):
+        if g < 4:
+            sc, mn = q[g] & 63, q[g + 4] & 63
+        else:
+            sc = (q[g + 4] & 0xF) | ((q[g - 4] >> 6) << 4)
+            mn = (q[g + 4] >> 4) | ((q[g] >> 6) << 4)
+        nib = blk[16 + (g // 2) * 32: 16 + (g // 2) * 32 + 32].astype(np.int64)
+        nib = (nib >> 4) if g & 1 else (nib & 0xF)
+        out[g * 32:(g + 1) * 32] = d * sc * nib - dmin * mn
+    return out
+
+
+def test_q4k_and_f16_matmul_port_equals_reference(orc, orc_ref):
+    """q4k_block against an independent decoder; the fp32 Q4_K dot and the engine's fp16 matmul bit for bit
+    between the port and the reference build."""
+    rng = np.random.default_rng(9)
+    out, in_, B = 37, 512, 2
+    nb = in_ // 256
+    w = rng.integers(0, 256, (out, nb, 144), dtype=np.uint8)
+    w[:, :, 0:2] = (rng.uniform(0.5, 2, (out, nb)) * 1e-3).astype(np.float16).view(np.uint8).reshape(out, nb, 2)
+    w[:, :, 2:4] = (rng.uniform(0.5, 2, (out, nb)) * 1e-3).astype(np.float16).view(np.uint8).reshape(out, nb, 2)
+    w = np.ascontiguousarray(w.reshape(-1))
+    for lib in (orc, orc_ref):
+        y = np.zeros(256, np.float32)
+        lib.orc_q4k_block(y, np.ascontiguousarray(w[:144]))
+        assert np.allclose(y, _q4k_decode_numpy(w[:144]), rtol=1e-6, atol=1e-9)
+    x = rng.standard_normal((B, in_)).astype(np.float32)
+    ya, yb = np.zeros((B, out), np.float32), np.zeros((B, out), np.float32)
+    orc.orc_gemv_q4k(ya, w, x, out, in_, B)
+    orc_ref.orc_gemv_q4k(yb, w, x, out, in_, B)
+    assert np.array_equal(ya, yb)
+    w16 = (0.02 * rng.standard_normal((out, in_))).astype(np.float16).view(np.uint16).reshape(-1)
+    orc.orc_gemv_f16(ya, np.ascontiguousarray(w16), x, out, in_, B)
+    orc_ref.orc_gemv_f16(yb, np.ascontiguousarray(w16), x, out, in_, B)
+    assert np.array_equal(ya, yb)
+
+
 def test_per_head_gdn_call_equals_all_heads_call(orc):
     """orc_gdn_step splits the reference call per head; same bits as one call."""
     rng = np.random.default_rng(9)

@@ -118,6 +118,12 @@ PROTOS = {
     "yattn_gdn_inputs": (C.c_int, [vp] * 12 + [u32] * 8 + [C.c_float, vp, *E]),
     "yattn_sess_kv_save": (C.c_int, [vp, u32, u32, u32, u32, C.c_char_p, vp, *E]),
     "yattn_sess_kv_load": (C.c_int, [vp, u32, u32, u32, C.c_char_p, C.POINTER(u32), vp, *E]),
+    "yattn_gemv_q4k": (C.c_int, [vp, vp, vp, u32, u32, u32, vp, *E]),
+    "yattn_gemv_f16": (C.c_int, [vp, vp, vp, u32, u32, u32, vp, *E]),
+    "cuda_k_gemv_q4k": (C.c_int, [vp, vp, vp, u32, u32, *E]),
+    "cuda_k_gemm_q4k": (C.c_int, [vp, vp, vp, u32, u32, u32, *E]),
+    "cuda_k_gemv_f16": (C.c_int, [vp, vp, vp, vp, vp, u32, u32, *E]),
+    "cuda_k_gemm_f16": (C.c_int, [vp, vp, vp, vp, vp, u32, u32, u32, *E]),
     "yattn_rope_store_kv_batch": (C.c_int, [vp, vp, vp, vp, vp, u32, u32, u32, u32, u32, u32, u32, C.c_int, u32,
                                             C.c_float, vp, *E]),
     "cuda_k_gdn_state_update": (None, [vp, vp, vp, vp, vp, vp, vp, u32, u32, u32, u32]),

@@ -315,6 +315,26 @@ def gdn_prefill_recurrent(S, out, q, k, v, gate, beta, n_seqs: int, T: int, num_
          float(eps), _stream(stream))
 
 
+def gemv_q4k(y: torch.Tensor, w: torch.Tensor, x: torch.Tensor, out: int, in_: int, B: int = 1,
+             stream=None) -> None:
+    """y[B][out] = Q4_K W[out][in] . x[B][in] (cuda_kernels.cu:161-249 semantics, fp32 x)."""
+    _need(y, torch.float32, "y")
+    _need(x, torch.float32, "x")
+    if w.dtype != torch.uint8 or not w.is_cuda or w.numel() < out * (in_ // 256) * 144:
+        raise ValueError("w must be a CUDA uint8 tensor of out * in/256 Q4_K blocks")
+    call("yattn_gemv_q4k", y.data_ptr(), w.data_ptr(), x.data_ptr(), out, in_, B, _stream(stream))
+
+
+def gemv_f16(y: torch.Tensor, w: torch.Tensor, x: torch.Tensor, out: int, in_: int, B: int = 1,
+             stream=None) -> None:
+    """y[B][out] = fp16 W[out][in] . x[B][in] in fp32 (matvec.c:111-122 per token)."""
+    _need(y, torch.float32, "y")
+    _need(x, torch.float32, "x")
+    if w.element_size() != 2 or not w.is_cuda or w.numel() < out * in_:
+        raise ValueError("w must be a CUDA 16-bit tensor of out * in fp16 weights")
+    call("yattn_gemv_f16", y.data_ptr(), w.data_ptr(), x.data_ptr(), out, in_, B, _stream(stream))
+
+
 def sess_kv_save(kv: torch.Tensor, n_blocks: int, kv_dim: int, max_seq: int, pos: int, path: str,
                  stream=None) -> None:
     """Writes the first pos rows of every block's K and V regions of the device blob kv

@@ -53,6 +53,7 @@ enum : int {
     ST_DECODE_BAD_ITEM = 103,   // q / gate not 16-byte aligned, or (pooled) K/V not rows of the pool
     ST_PREFILL_TIMEOUT = 201,
     ST_GDN_TIMEOUT = 301,
+    ST_GEMV_TIMEOUT = 501,
     ST_EXCHANGE_TIMEOUT = 401,
 };
 
