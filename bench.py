@@ -817,6 +817,7 @@ def run_rope_store(args) -> None:
     dev = torch.device("cuda", local)
     stream = torch.cuda.current_stream()
     L, n, H, KV, hd, kd = c.layers, c.n_seqs, c.n_heads, c.n_kv_heads, c.head_dim, c.kv_dim
+    L = args.layers or L   # --layers shrinks the step for profiler captures only
     theta = 500000.0   # Llama-3 rope_theta
     ctx = c.ctx()
     offs = [sum(ctx[:i]) for i in range(n)]
@@ -896,7 +897,7 @@ def run_rope_store(args) -> None:
     if rank == 0:
         line = _line(args, world, "RoPE + KV store tok/s (Llama-3-8B shape, 64 sequences, 32 layers)",
                      n * world / (ms / 1e3), "tok/s", ms,
-                     {"workload": c.name + "-rope-store", "n_heads": H, "n_kv_heads": KV, "head_dim": hd,
+                     {"workload": c.name + "-rope-store" + (f"-profile-{L}-layers" if args.layers else ""), "n_heads": H, "n_kv_heads": KV, "head_dim": hd,
                       "layers": L, "n_seqs": n * world, "rope": "llama pairs, theta 500000",
                       "parallelism": f"data-parallel x{world}: a batch per GPU, no collective",
                       "launch": "CUDA graph replay of the step (one launch per layer)",
@@ -928,7 +929,7 @@ def run_gemv(args) -> None:
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
     stream = torch.cuda.current_stream()
-    L, H = 32, 4096
+    L, H = args.layers or 32, 4096   # --layers shrinks the step for profiler captures only
     shapes = [(4096, H), (1024, H), (1024, H), (H, 4096), (14336, H), (14336, H), (H, 14336)]
     per_layer = sum(o * (i // 256) * 144 for o, i in shapes)
     g = torch.Generator(device=dev)
@@ -1001,11 +1002,69 @@ def run_gemv(args) -> None:
     if rank == 0:
         line = _line(args, world, "Q4_K linear layers tok/s (Llama-3-8B decode step, 32 layers, batch 1)",
                      world / (ms / 1e3), "tok/s", ms,
-                     {"workload": "llama3-8b-q4k-gemv-decode", "layers": L, "hidden": H, "ffn": 14336,
+                     {"workload": "llama3-8b-q4k-gemv-decode" + (f"-profile-{L}-layers" if args.layers else ""), "layers": L, "hidden": H, "ffn": 14336,
                       "weight_bytes_per_step": step_bytes, "parallelism": f"replicas x{world}",
                       "launch": "CUDA graph replay of the step", "l2": "weights per step 3.9 GB > L2"},
                      roof, args.steps * len(mats), clk, e2e, cpu=cpu, scaling="weak")
         line["dtype"] = "Q4_K weights, f32 x and accumulation"
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def run_gdn_inputs(args) -> None:
+    """The qwen35 GDN layer's input preparation (engine.c:785-821) for config
+    5a's 4096-token chunk: gates, conv1d delay line + silu, q/k l2norm, one
+    launch.  Bound: HBM (the projection read, q/k/v written).  Inputs above L2.
+    Weak scaling: each rank prepares its own sequence."""
+    import torch
+    import torch.distributed as dist
+
+    from yllm_b200 import attn, dist as ydist
+    from yllm_b200.configs import CFG5_GDN as c
+
+    rank, world, local = ydist.init("nccl" if args.gpus > 1 else "gloo")
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    stream = torch.cuda.current_stream()
+    T, NK, NV, D, KW = c.tokens, c.num_k_heads, c.n_v_heads, c.head_dim, 4
+    CC = 2 * NK * D + NV * D
+    g = torch.Generator(device=dev)
+    g.manual_seed(11 + rank)
+    qkv = torch.randn(1, T, CC, device=dev, generator=g)
+    st = torch.randn(1, KW, CC, device=dev, generator=g)
+    wc = 0.5 * torch.randn(CC, KW, device=dev, generator=g)
+    al = torch.randn(1, T, NV, device=dev, generator=g)
+    bi = torch.randn(1, T, NV, device=dev, generator=g)
+    dt = torch.randn(NV, device=dev, generator=g)
+    a = -dt.abs()
+    q = torch.empty(1, T, NK * D, device=dev)
+    k = torch.empty_like(q)
+    v = torch.empty(1, T, NV * D, device=dev)
+    ga = torch.empty(1, T, NV, device=dev)
+    be = torch.empty_like(ga)
+
+    def step():
+        attn.gdn_inputs(qkv, st, wc, al, bi, dt, a, q, k, v, ga, be, 1, T, KW, NK, D, NV, D, eps=c.eps)
+
+    ms, per_call, clk = _timed(step, args, stream, world, dist, local, graph=True, flush_l2=True)
+    nbytes = (qkv.numel() + q.numel() + k.numel() + v.numel() + 4 * al.numel()) * 4
+    peaks, src = load_peaks()
+    ach = nbytes / (per_call / 1e3) / 1e9
+    roof = {"bound": "hbm", "achieved": round(ach, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
+            "frac": round(ach / peaks["hbm_gbs"], 4), "traffic": None, "kernel": "k_gdn_inputs<4,32>",
+            "peak_source": src, "bytes_per_step": nbytes}
+    if rank == 0:
+        line = _line(args, world, "GDN layer inputs tok/s (qwen3.5 shape, one 4096-token chunk)",
+                     T * world / (ms / 1e3), "tok/s", ms,
+                     {"workload": c.name + "-inputs-4096", "tokens": T, "conv_chan": CC, "kwidth": KW,
+                      "num_k_heads": NK, "n_v_heads": NV, "head_dim": D,
+                      "parallelism": f"data-parallel x{world}: one sequence per GPU",
+                      "launch": "CUDA graph replay of the step",
+                      "l2": "L2 scrubbed between timed steps outside the step's events"},
+                     roof, args.steps, clk, scaling="weak")
+        line["dtype"] = "f32"
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.barrier()
@@ -1130,7 +1189,7 @@ def main() -> None:
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--workload", default="decode",
                     choices=["decode", "prefill", "gated_prefill", "gdn_prefill", "gdn_decode", "long_decode",
-                             "config1_decode", "gated_decode", "rope_store", "sess_kv", "gemv"],
+                             "config1_decode", "gated_decode", "rope_store", "sess_kv", "gemv", "gdn_inputs"],
                     help="decode = BASELINE config 3 (the default bench line)")
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
@@ -1162,6 +1221,8 @@ def main() -> None:
         run_sess_kv(args)
     elif args.workload == "gemv":
         run_gemv(args)
+    elif args.workload == "gdn_inputs":
+        run_gdn_inputs(args)
     else:
         run_long_decode(args)
 

@@ -137,9 +137,9 @@ __global__ void __launch_bounds__(kThreads) k_gdn_inputs(const InParams p) {
     }
     __syncthreads();
     float* out = (is_q ? p.q : p.k) + tok0 * key_dim + (is_q ? ch0 : ch0 - key_dim);
-    for (uint32_t u = tid; u < nt * seg_len; u += blockDim.x) {
-        const uint32_t t = u / seg_len, c = u % seg_len;
-        out[static_cast<size_t>(t) * key_dim + c] = __fmul_rn(rows[t][c], scale[t]);
+    if (tid < seg_len) {   // one channel per thread, token by token (coalesced rows, no index division)
+        for (uint32_t t = 0; t < nt; ++t)
+            out[static_cast<size_t>(t) * key_dim + tid] = __fmul_rn(rows[t][tid], scale[t]);
     }
 }
 

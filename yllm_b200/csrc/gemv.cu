@@ -388,13 +388,14 @@ void launch_q4k_t1(float* y, const uint8_t* w, const float* x, uint32_t out, uin
 template <int NT>
 void launch_q4k(float* y, const uint8_t* w, const float* x, uint32_t out, uint32_t in, uint32_t nt, cudaStream_t st) {
     if (NT == 1) {
-        // k-slices so each warp walks about 4 steps (its loads run a step ahead); more rows per CTA otherwise
+        // as many k-slices as a row has steps (up to the CTA's 8 warps): the fewest rows per CTA, so even a
+        // matrix of 1024 rows spreads over every SM
         const uint32_t nsteps = (in / 256 + 3) / 4;   // 4-block steps per row
-        if (nsteps >= 32)
+        if (nsteps >= 8)
             launch_q4k_t1<8>(y, w, x, out, in, st);
-        else if (nsteps >= 16)
+        else if (nsteps >= 4)
             launch_q4k_t1<4>(y, w, x, out, in, st);
-        else if (nsteps >= 8)
+        else if (nsteps >= 2)
             launch_q4k_t1<2>(y, w, x, out, in, st);
         else
             launch_q4k_t1<1>(y, w, x, out, in, st);
