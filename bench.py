@@ -43,7 +43,11 @@ def load_peaks() -> tuple[dict, str]:
 # from one ncu capture of exactly the launch the bench times (the commands and the
 # rest of those captures are summarised under profiles/).  Workloads without such a
 # capture report null.
-NCU_TRAFFIC = {"decode": 1226090496, "prefill": 25237504}
+# dram__bytes_read.sum + dram__bytes_write.sum of one launch of each workload's dominant kernel, from the ncu
+# captures summarised under profiles/ (same workloads; --layers-reduced steps have the same per-launch bytes)
+NCU_TRAFFIC = {"decode": 1226090496, "prefill": 25237504, "gated_prefill": 168607744, "gated_decode": 274070272,
+               "long_decode": 541052160, "gdn_inputs": 225114112, "rope_store": 1590784,
+               "gdn_decode": 78914048, "gdn_prefill_state": 257715456}
 
 
 class ClockSampler:
@@ -406,7 +410,7 @@ def run_decode_small(args) -> None:
     ach = step_bytes / (per_call / 1e3) / 1e9
     G = -(-cfg.n_heads // cfg.n_kv_heads)
     roof = {"bound": "hbm", "achieved": round(ach, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
-            "frac": round(ach / peaks["hbm_gbs"], 4), "traffic": None,
+            "frac": round(ach / peaks["hbm_gbs"], 4), "traffic": NCU_TRAFFIC["gated_decode"] if cfg.gated else None,
             "kernel": f"k_decode<{cfg.head_dim},{G},TM> (pooled tensor copies)",
             "peak_source": src, "bytes_per_step": step_bytes,
             "note": f"{d.n_layers} launches per step in one graph; achieved = step bytes / step device time"}
@@ -620,7 +624,8 @@ def run_prefill(args, gated: bool) -> None:
     peaks, src = load_peaks()
     achieved = my_flops / (per_call / 1e3) / 1e12
     roof = {"bound": "tensor", "achieved": round(achieved, 1), "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
-            "frac": round(achieved / peaks["bf16_tflops"], 4), "traffic": None if gated else NCU_TRAFFIC["prefill"],
+            "frac": round(achieved / peaks["bf16_tflops"], 4),
+            "traffic": NCU_TRAFFIC["gated_prefill" if gated else "prefill"],
             "kernel": f"k_prefill<{hd}>", "peak_source": src + " (dense bf16 burst)"}
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -690,7 +695,9 @@ def run_gdn(args, decode: bool) -> None:
         peaks, src = load_peaks()
         ach = mine / (per_call / 1e3) / 1e9
         roof = {"bound": "hbm", "achieved": round(ach, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
-                "frac": round(ach / peaks["hbm_gbs"], 4), "traffic": None, "kernel": "k_gdn_decode",
+                "frac": round(ach / peaks["hbm_gbs"], 4), "traffic": NCU_TRAFFIC["gdn_decode"],
+                "traffic_note": "below the state bytes: part of the 134 MB state stays in L2 across launches",
+                "kernel": "k_gdn_decode",
                 "peak_source": src}
         if rank == 0:
             print(json.dumps(_line(args, world, "GDN batch-32 decode tok/s (state read+write)",
@@ -712,7 +719,8 @@ def run_gdn(args, decode: bool) -> None:
         peaks, src = load_peaks()
         ach = flops / (per_call / 1e3) / 1e12
         roof = {"bound": "tensor", "achieved": round(ach, 2), "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
-                "frac": round(ach / peaks["bf16_tflops"], 4), "traffic": None, "kernel": "k_gdn_prefill",
+                "frac": round(ach / peaks["bf16_tflops"], 4), "traffic": NCU_TRAFFIC["gdn_prefill_state"],
+                "traffic_note": "k_gdn_chunk_state, the larger of the step's two kernels", "kernel": "k_gdn_prefill",
                 "peak_source": src + " (dense bf16 burst)"}
         if rank == 0:
             print(json.dumps(_line(args, world, "GDN 4096-token prefill TFLOP/s (recurrent-equivalent FLOPs)",
@@ -777,7 +785,7 @@ def run_long_decode(args) -> None:
     peaks, src = load_peaks()
     ach = nbytes / (ms / 1e3) / 1e9
     roof = {"bound": "hbm", "achieved": round(ach, 1), "peak": peaks["hbm_gbs"] * world, "unit": "GB/s",
-            "frac": round(ach / (peaks["hbm_gbs"] * world), 4), "traffic": None,
+            "frac": round(ach / (peaks["hbm_gbs"] * world), 4), "traffic": NCU_TRAFFIC["long_decode"] if world == 1 else None,
             "kernel": "k_decode<128,4,TM>" + ((" + k_exchange_merge" if peer else " + NCCL all-gather + merge")
                                               if world > 1 else ""), "peak_source": src + f" x{world} GPUs"}
     if rank == 0:
@@ -890,7 +898,7 @@ def run_rope_store(args) -> None:
     peaks, src = load_peaks()
     ach = step_bytes / (per_call / 1e3) / 1e9
     roof = {"bound": "hbm", "achieved": round(ach, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
-            "frac": round(ach / peaks["hbm_gbs"], 4), "traffic": None, "kernel": "k_rope_store",
+            "frac": round(ach / peaks["hbm_gbs"], 4), "traffic": NCU_TRAFFIC["rope_store"], "kernel": "k_rope_store",
             "peak_source": src, "bytes_per_step": step_bytes,
             "note": f"{L} launches of {per_item * n / 1e6:.2f} MB each per step in one graph: launch-latency "
                     "bound, the HBM fraction is small by construction"}
@@ -958,7 +966,7 @@ def run_gemv(args) -> None:
     peaks, src = load_peaks()
     ach = step_bytes / (per_call / 1e3) / 1e9
     roof = {"bound": "hbm", "achieved": round(ach, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
-            "frac": round(ach / peaks["hbm_gbs"], 4), "traffic": None, "kernel": "k_gemv_q4k<4,1>",
+            "frac": round(ach / peaks["hbm_gbs"], 4), "traffic": None, "kernel": "k_gemv_q4k_t1<4,KS>",
             "peak_source": src, "bytes_per_step": step_bytes,
             "note": "224 launches per step in one graph; achieved = Q4_K weight bytes / step device time"}
     e2e = None
@@ -1053,7 +1061,7 @@ def run_gdn_inputs(args) -> None:
     peaks, src = load_peaks()
     ach = nbytes / (per_call / 1e3) / 1e9
     roof = {"bound": "hbm", "achieved": round(ach, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
-            "frac": round(ach / peaks["hbm_gbs"], 4), "traffic": None, "kernel": "k_gdn_inputs<4,32>",
+            "frac": round(ach / peaks["hbm_gbs"], 4), "traffic": NCU_TRAFFIC["gdn_inputs"], "kernel": "k_gdn_inputs<4,32>",
             "peak_source": src, "bytes_per_step": nbytes}
     if rank == 0:
         line = _line(args, world, "GDN layer inputs tok/s (qwen3.5 shape, one 4096-token chunk)",
