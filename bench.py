@@ -479,7 +479,8 @@ def run_reference(args) -> None:
         "metric": "attn decode tok/s (batched ragged GQA decode, all layers)",
         "value": round(value, 4),
         "unit": "tok/s",
-        "n_gpus": 0,
+        "n_gpus": args.gpus,
+        "runs_on": "host cores of rank 0 (the reference's CPU attention); no GPU work",
         "steps": args.steps,
         "warmup": args.warmup,
         "ms_per_step": round(step_s * 1e3, 2),
