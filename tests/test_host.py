@@ -298,3 +298,45 @@ def test_gemv_checks_arguments():
     assert lib.cuda_k_gemv_q4k(f, f, f, 0, 256, err, 256) == -1
     assert lib.cuda_k_gemm_f16(None, f, f, f, None, 64, 64, 0, err, 256) == -1
     assert lib.yattn_gemv_f16(None, f, f, 64, 64, 1, None, err, 256) == -1
+
+
+def _plan_ctas(ctx, n_kv, hd, target=148):
+    import ctypes as C
+
+    from yllm_b200._lib import YattnDecodeWork, lib
+
+    pos = (C.c_uint32 * len(ctx))(*[c - 1 for c in ctx])
+    cap = 8192
+    w = (YattnDecodeWork * cap)()
+    nw, npp, ng = C.c_uint32(), C.c_uint32(), C.c_uint32()
+    err = C.create_string_buffer(256)
+    assert lib.yattn_decode_plan_pooled(pos, len(ctx), n_kv, hd, 0, target, w, cap, C.byref(nw), C.byref(npp),
+                                        C.byref(ng), err, 256) == 0, err.value
+    ctas = {}
+    for i in range(nw.value):
+        ctas.setdefault(w[i].cta, []).append((w[i].item, w[i].kv_head, w[i].t_begin, w[i].t_end))
+    return ctas
+
+
+def test_decode_plan_cuts():
+    """The balanced plan covers every key of every (item, kv head) once; equal ranges fewer than the CTAs take the
+    equal cut (one unit per CTA), ragged ones the balanced cut within the CTA budget."""
+    from yllm_b200.configs import CFG3, CFG5_GATED_DECODE
+
+    for cfg, expect_uniform in ((CFG5_GATED_DECODE, True), (CFG3, False)):
+        ctx = cfg.ctx()
+        ctas = _plan_ctas(ctx, cfg.n_kv_heads, cfg.head_dim)
+        assert len(ctas) <= 148
+        cover = {}
+        for units in ctas.values():
+            for item, kvh, b, e in units:
+                cover.setdefault((item, kvh), []).append((b, e))
+        for (item, kvh), spans in cover.items():
+            spans.sort()
+            assert spans[0][0] == 0 and spans[-1][1] == ctx[item]
+            assert all(a[1] == b[0] for a, b in zip(spans, spans[1:])), "gap or overlap"
+        one_unit = all(len(u) == 1 for u in ctas.values())
+        assert one_unit == expect_uniform, cfg.name
+    # config 5c: 32 x 4096 keys over 2 kv heads -> 2 pieces of 2048 per range on 128 CTAs
+    ctas = _plan_ctas(CFG5_GATED_DECODE.ctx(), 2, 256)
+    assert len(ctas) == 128 and all(u[0][3] - u[0][2] == 2048 for u in ctas.values())
