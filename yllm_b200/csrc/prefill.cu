@@ -331,24 +331,28 @@ __global__ void __launch_bounds__(kPThreads, 1)
             // a row whose keys so far are all masked keeps m = -inf and gets p = 0
             const float m_sub = (m_use == -INFINITY) ? 0.f : m_use;
             // ---- p = 2^(s*scale - m): one FFMA + ex2 per element; P hi/lo over this half's S ----
-            float rs4[4] = {0.f, 0.f, 0.f, 0.f};
+            // pairs of elements in packed fp32x2 arithmetic (FFMA2 / FADD2): half the FMA, add and
+            // subtract instructions of the scalar form
+            const float2 sl2x2 = make_float2(sl2, sl2), negm = make_float2(-m_sub, -m_sub);
+            const float2 neg1 = make_float2(-1.f, -1.f);
+            float2 rs2[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
 #pragma unroll
             for (int c = 0; c < HB / 32; ++c) {   // 32 keys -> 16 columns of P_hi, then 16 of P_lo
                 uint32_t hi[16], lo[16];
 #pragma unroll
                 for (int i = 0; i < 16; ++i) {
-                    const float a = ex2_approx(fmaf(sv[c * 32 + 2 * i], sl2, -m_sub));
-                    const float b = ex2_approx(fmaf(sv[c * 32 + 2 * i + 1], sl2, -m_sub));
-                    rs4[i & 3] += a + b;
-                    const __half2 hv = __floats2half2_rn(a, b);
-                    const float2 hf = __half22float2(hv);
+                    const float2 x = __ffma2_rn(make_float2(sv[c * 32 + 2 * i], sv[c * 32 + 2 * i + 1]), sl2x2, negm);
+                    const float2 pp = make_float2(ex2_approx(x.x), ex2_approx(x.y));
+                    rs2[i & 1] = __fadd2_rn(rs2[i & 1], pp);
+                    const __half2 hv = __floats2half2_rn(pp.x, pp.y);
+                    const float2 r = __ffma2_rn(__half22float2(hv), neg1, pp);   // p - fp16(p)
                     hi[i] = h2_bits(hv);
-                    lo[i] = h2_bits(__floats2half2_rn(a - hf.x, b - hf.y));
+                    lo[i] = h2_bits(__floats2half2_rn(r.x, r.y));
                 }
                 tmem_st16(scol + c * 32, hi);
                 tmem_st16(scol + c * 32 + 16, lo);
             }
-            l_run = l_run * alpha + ((rs4[0] + rs4[1]) + (rs4[2] + rs4[3]));
+            l_run = l_run * alpha + ((rs2[0].x + rs2[0].y) + (rs2[1].x + rs2[1].y));
             m_run = m_use;
             // ---- O rescale (rare), this half's columns of O: PV(j-1) must have finished ----
             // (both halves of these rows see the same `grow`, so both come here)
