@@ -919,13 +919,13 @@ def run_rope_store(args) -> None:
         dist.destroy_process_group()
 
 
-def run_gemv(args) -> None:
-    """The per-layer linear layers of a Llama-3-8B decode step with Q4_K
-    weights (cuda_fwd.c:94-168 brackets attention with these GEMVs): per
-    layer q, k, v, o (4096/1024 x 4096), gate and up (14336 x 4096) and down
-    (4096 x 14336), 218 M weights = 123 MB; 32 layers, each with its own
-    weights (3.9 GB, far above L2).  One step = 224 launches replayed as a
-    CUDA graph.  Bound: HBM on the weight bytes.  Weak scaling: each rank
+def run_gemv(args, fmt: str = "q4k") -> None:
+    """The per-layer linear layers of a Llama-3-8B decode step (cuda_fwd.c:94-168
+    brackets attention with these GEMVs): per layer q, k, v, o (4096/1024 x
+    4096), gate and up (14336 x 4096) and down (4096 x 14336), 218 M weights:
+    123 MB as Q4_K (fmt "q4k"), 436 MB as fp16 (fmt "f16"); 32 layers, each
+    with its own weights (far above L2).  One step = 224 launches replayed as
+    a CUDA graph.  Bound: HBM on the weight bytes.  Weak scaling: each rank
     streams its own copy."""
     import ctypes as C
 
@@ -940,36 +940,44 @@ def run_gemv(args) -> None:
     stream = torch.cuda.current_stream()
     L, H = args.layers or 32, 4096   # --layers shrinks the step for profiler captures only
     shapes = [(4096, H), (1024, H), (1024, H), (H, 4096), (14336, H), (14336, H), (H, 14336)]
-    per_layer = sum(o * (i // 256) * 144 for o, i in shapes)
+    f16 = fmt == "f16"
+    nbytes_of = (lambda o, i: o * i * 2) if f16 else (lambda o, i: o * (i // 256) * 144)
+    per_layer = sum(nbytes_of(o, i) for o, i in shapes)
     g = torch.Generator(device=dev)
     g.manual_seed(7 + rank)
-    wbuf = torch.randint(0, 256, (L * per_layer,), dtype=torch.uint8, device=dev, generator=g)
-    # d and dmin of every block: small positive fp16 so the outputs stay finite
-    blocks = wbuf.view(-1, 144)
-    dd = (torch.rand(blocks.shape[0], 2, device=dev, generator=g) * 1e-3 + 5e-4).half()
-    blocks[:, 0:4] = dd.view(torch.uint8).view(-1, 4)
+    if f16:
+        wbuf = torch.empty(L * per_layer // 2, dtype=torch.float16, device=dev).normal_(0.0, 0.02, generator=g)
+        wbuf = wbuf.view(torch.uint8)
+    else:
+        wbuf = torch.randint(0, 256, (L * per_layer,), dtype=torch.uint8, device=dev, generator=g)
+        # d and dmin of every block: small positive fp16 so the outputs stay finite
+        blocks = wbuf.view(-1, 144)
+        dd = (torch.rand(blocks.shape[0], 2, device=dev, generator=g) * 1e-3 + 5e-4).half()
+        blocks[:, 0:4] = dd.view(torch.uint8).view(-1, 4)
     xs = {i: torch.randn(i, device=dev, generator=g) for i in (H, 14336)}
     ys = {o: torch.empty(o, device=dev) for o in (1024, 4096, 14336)}
     mats = []
     off = 0
     for l in range(L):
         for o, i in shapes:
-            n = o * (i // 256) * 144
-            mats.append((wbuf[off:off + n], o, i))
+            n = nbytes_of(o, i)
+            mats.append((wbuf[off:off + n].view(torch.int16) if f16 else wbuf[off:off + n], o, i))
             off += n
+    gemv = attn.gemv_f16 if f16 else attn.gemv_q4k
 
     def step():
         for w, o, i in mats:
-            attn.gemv_q4k(ys[o], w, xs[i], o, i, 1)
+            gemv(ys[o], w, xs[i], o, i, 1)
 
     ms, per_call, clk = _timed(step, args, stream, world, dist, local, graph=True)
     step_bytes = L * per_layer
     peaks, src = load_peaks()
     ach = step_bytes / (per_call / 1e3) / 1e9
     roof = {"bound": "hbm", "achieved": round(ach, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
-            "frac": round(ach / peaks["hbm_gbs"], 4), "traffic": None, "kernel": "k_gemv_q4k_t1<4,KS>",
+            "frac": round(ach / peaks["hbm_gbs"], 4), "traffic": None,
+            "kernel": "k_gemv_f16<4,1,2>" if f16 else "k_gemv_q4k_t1<4,KS>",
             "peak_source": src, "bytes_per_step": step_bytes,
-            "note": "224 launches per step in one graph; achieved = Q4_K weight bytes / step device time"}
+            "note": "224 launches per step in one graph; achieved = weight bytes / step device time"}
     e2e = None
     if not args.no_e2e:
         hx = torch.empty(H, dtype=torch.float32, pin_memory=True)
@@ -983,8 +991,8 @@ def run_gemv(args) -> None:
 
         ems, _, _ = _timed(e2e_step, args, stream, world, dist, local)
         e2e = {"value": round(world / (ems / 1e3), 2), "unit": "tok/s", "h2d_bytes_per_step": H * 4 * world,
-               "d2h_bytes_per_step": H * 4 * world, "path": "yattn_gemv_q4k per matrix per step (no graph), "
-                                                            "pinned x in, y back"}
+               "d2h_bytes_per_step": H * 4 * world,
+               "path": f"yattn_gemv_{fmt} per matrix per step (no graph), pinned x in, y back"}
     cpu = None
     if rank == 0 and not args.no_cpu_baseline:
         import numpy as np
@@ -995,27 +1003,31 @@ def run_gemv(args) -> None:
         kind = "reference" if oracle.has_ref() else "port"
         lib = oracle.load("ref" if kind == "reference" else "port")
         lib.orc_set_threads(len(os.sched_getaffinity(0)))
-        host = [(mats[j][0].cpu().numpy(), mats[j][1], mats[j][2]) for j in range(len(shapes))]   # layer 0
+        host = [(mats[j][0].cpu().numpy().view(np.uint16 if f16 else np.uint8), mats[j][1], mats[j][2])
+                for j in range(len(shapes))]   # layer 0
         hxs = {i: xs[i].cpu().numpy() for i in xs}
         hys = {o: np.zeros(o, np.float32) for o in ys}
         times = []
         while not times or (sum(times) < min(args.cpu_budget, 10.0) and len(times) < 20):
             t0 = time.perf_counter()
             for w, o, i in host:
-                lib.orc_matmul_q4k(hys[o], hxs[i], w, o, i)
+                (lib.orc_matmul_f16 if f16 else lib.orc_matmul_q4k)(hys[o], hxs[i], w, o, i)
             times.append(time.perf_counter() - t0)
         step_s = statistics.median(times) * L
         cpu = {"value": round(1 / step_s, 3), "unit": "tok/s", "cores": int(lib.orc_max_threads()), "kind": kind,
-               "sample": f"layer 0's seven Q4_K matmuls (matvec.c:514, the engine's AVX2 path), timed "
-                         f"{len(times)}x, x{L} layers"}
+               "sample": f"layer 0's seven {'fp16 matmuls (matvec.c:111' if f16 else 'Q4_K matmuls (matvec.c:514'}"
+                         f", the engine's path), timed {len(times)}x, x{L} layers"}
     if rank == 0:
-        line = _line(args, world, "Q4_K linear layers tok/s (Llama-3-8B decode step, 32 layers, batch 1)",
+        name = "fp16" if f16 else "Q4_K"
+        line = _line(args, world, f"{name} linear layers tok/s (Llama-3-8B decode step, 32 layers, batch 1)",
                      world / (ms / 1e3), "tok/s", ms,
-                     {"workload": "llama3-8b-q4k-gemv-decode" + (f"-profile-{L}-layers" if args.layers else ""), "layers": L, "hidden": H, "ffn": 14336,
+                     {"workload": f"llama3-8b-{fmt}-gemv-decode" + (f"-profile-{L}-layers" if args.layers else ""),
+                      "layers": L, "hidden": H, "ffn": 14336,
                       "weight_bytes_per_step": step_bytes, "parallelism": f"replicas x{world}",
-                      "launch": "CUDA graph replay of the step", "l2": "weights per step 3.9 GB > L2"},
+                      "launch": "CUDA graph replay of the step",
+                      "l2": f"weights per step {step_bytes / 1e9:.1f} GB > L2"},
                      roof, args.steps * len(mats), clk, e2e, cpu=cpu, scaling="weak")
-        line["dtype"] = "Q4_K weights, f32 x and accumulation"
+        line["dtype"] = f"{name} weights, f32 x and accumulation"
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.barrier()
@@ -1198,7 +1210,7 @@ def main() -> None:
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--workload", default="decode",
                     choices=["decode", "prefill", "gated_prefill", "gdn_prefill", "gdn_decode", "long_decode",
-                             "config1_decode", "gated_decode", "rope_store", "sess_kv", "gemv", "gdn_inputs"],
+                             "config1_decode", "gated_decode", "rope_store", "sess_kv", "gemv", "gemv_f16", "gdn_inputs"],
                     help="decode = BASELINE config 3 (the default bench line)")
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
@@ -1228,8 +1240,8 @@ def main() -> None:
         run_rope_store(args)
     elif args.workload == "sess_kv":
         run_sess_kv(args)
-    elif args.workload == "gemv":
-        run_gemv(args)
+    elif args.workload in ("gemv", "gemv_f16"):
+        run_gemv(args, "f16" if args.workload == "gemv_f16" else "q4k")
     elif args.workload == "gdn_inputs":
         run_gdn_inputs(args)
     else:
