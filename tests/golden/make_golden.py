@@ -7,6 +7,11 @@
                       matvec.c / platform.c compiled unmodified under the
                       restated engine.c loops -- on small seeded cases, so the
                       port can be pinned on a machine without the reference tree.
+  golden_glue.npz     the same for the rows around the attention path (RoPE +
+                      KV store, GDN layer inputs, Q4_K / fp16 matmul, the
+                      session KV file), plus the reference's own Q4_K decode
+                      golden vector (tests/ref_data.h K4_RAW / K4_REF, checked
+                      by its test_matvec.c:57-69 to 1e-6), parsed from that file.
 
 Run from the repo root (needs the reference tree to build oracle/_ref):
     python tests/golden/make_golden.py
@@ -121,11 +126,101 @@ def golden(lib) -> dict:
     return g
 
 
+def ref_q4k_golden(ref_tree: Path) -> dict:
+    """K4_RAW (two 144-byte Q4_K blocks) and K4_REF (their 512 decoded values) from the reference's
+    tests/ref_data.h, parsed from the C initialisers."""
+    import re
+
+    text = (ref_tree / "tests" / "ref_data.h").read_text()
+
+    def array(name):
+        m = re.search(r"%s\[\]\s*=\s*\{(.*?)\};" % name, text, re.S)
+        return [t.strip() for t in m.group(1).replace("\n", " ").split(",") if t.strip()]
+
+    raw = np.array([int(t, 16) for t in array("K4_RAW")], dtype=np.uint8)
+    ref = np.array([float(t.rstrip("fF")) for t in array("K4_REF")], dtype=np.float32)
+    assert raw.size == 288 and ref.size == 512, (raw.size, ref.size)
+    return {"q4k_raw": raw, "q4k_ref": ref}
+
+
+def glue(lib) -> dict:
+    rng = np.random.default_rng(20261202)
+    g = {}
+    # RoPE + KV store, one token of each kind (engine.c:1052-1072, 921-934)
+    for kind, (H, KV, hd, nd, theta, pos) in {0: (8, 2, 128, 128, 5e5, 4095), 1: (4, 2, 64, 64, 1e6, 37),
+                                              2: (4, 2, 256, 64, 1e7, 70000)}.items():
+        kd = KV * hd
+        q = rng.standard_normal(H * hd).astype(np.float32)
+        k = rng.standard_normal(kd).astype(np.float32)
+        v = rng.standard_normal(kd).astype(np.float32)
+        qo, ko = q.copy(), k.copy()
+        kc = np.zeros((pos + 1) * kd, np.uint16)
+        vc = np.zeros((pos + 1) * kd, np.uint16)
+        lib.orc_rope_store(qo, ko, v, kc, vc, H, KV, hd, kd, kind, nd, pos, theta)
+        tag = f"rope{kind}_"
+        g[tag + "in"] = np.concatenate([q, k, v])
+        g[tag + "q"], g[tag + "krow"], g[tag + "vrow"] = qo, kc[pos * kd:], vc[pos * kd:]
+        g[tag + "geom"] = np.array([H, KV, hd, nd, pos], dtype=np.int64)
+        g[tag + "theta"] = np.array([theta], dtype=np.float32)
+    # GDN layer inputs, 2 sequences x 5 tokens (engine.c:785-821)
+    n_seqs, T, nk, hk, nv, hv, kw = 2, 5, 2, 32, 4, 32, 4
+    cc = 2 * nk * hk + nv * hv
+    case = dict(qkv=rng.standard_normal((n_seqs, T, cc)).astype(np.float32),
+                state=rng.standard_normal((n_seqs, kw, cc)).astype(np.float32),
+                w=(0.5 * rng.standard_normal((cc, kw))).astype(np.float32),
+                alpha=rng.standard_normal((n_seqs, T, nv)).astype(np.float32),
+                beta_in=rng.standard_normal((n_seqs, T, nv)).astype(np.float32),
+                dt=rng.standard_normal(nv).astype(np.float32),
+                a=-np.abs(rng.standard_normal(nv)).astype(np.float32))
+    q = np.zeros((n_seqs, T, nk * hk), np.float32)
+    k = np.zeros_like(q)
+    v = np.zeros((n_seqs, T, nv * hv), np.float32)
+    gate = np.zeros((n_seqs, T, nv), np.float32)
+    beta = np.zeros_like(gate)
+    st = case["state"].copy()
+    lib.orc_gdn_inputs(case["qkv"], st, case["w"], case["alpha"], case["beta_in"], case["dt"], case["a"], q, k, v,
+                       gate, beta, n_seqs, T, cc, kw, nk, hk, nv, hv, 1e-6)
+    for key, val in case.items():
+        g["gdni_" + key] = val
+    for key, val in dict(q=q, k=k, v=v, gate=gate, beta=beta, state_out=st).items():
+        g["gdni_out_" + key] = val
+    g["gdni_geom"] = np.array([n_seqs, T, nk, hk, nv, hv, kw], dtype=np.int64)
+    # linear layers: fp32 Q4_K dequant-dot and the engine's fp16 matmul, 2 tokens
+    out, inn, B = 24, 512, 2
+    nb = inn // 256
+    w4 = rng.integers(0, 256, (out, nb, 144), dtype=np.uint8)
+    w4[:, :, 0:2] = (rng.uniform(0.5, 2, (out, nb)) * 1e-3).astype(np.float16).view(np.uint8).reshape(out, nb, 2)
+    w4[:, :, 2:4] = (rng.uniform(0.5, 2, (out, nb)) * 1e-3).astype(np.float16).view(np.uint8).reshape(out, nb, 2)
+    w4 = np.ascontiguousarray(w4.reshape(-1))
+    w16 = (0.02 * rng.standard_normal((out, inn))).astype(np.float16).view(np.uint16).reshape(-1)
+    x = rng.standard_normal((B, inn)).astype(np.float32)
+    y4 = np.zeros((B, out), np.float32)
+    y16 = np.zeros((B, out), np.float32)
+    lib.orc_gemv_q4k(y4, w4, x, out, inn, B)
+    lib.orc_gemv_f16(y16, np.ascontiguousarray(w16), x, out, inn, B)
+    g.update(lin_w4=w4, lin_w16=w16, lin_x=x, lin_y4=y4, lin_y16=y16,
+             lin_geom=np.array([out, inn, B], dtype=np.int64))
+    # session KV file bytes (cache.c:174-195): 2 blocks, kv_dim 16, max_seq 8, pos 5
+    nb_, kd_, ms_, pos_ = 2, 16, 8, 5
+    blob = rng.integers(0, 1 << 16, (2 * nb_ + 1) * ms_ * kd_, dtype=np.uint16)
+    import tempfile
+
+    with tempfile.TemporaryDirectory() as d:
+        path = Path(d) / "s.kv"
+        assert lib.orc_sess_kv_save(blob, nb_, kd_, ms_, pos_, str(path).encode()) == 0
+        g["sess_file"] = np.frombuffer(path.read_bytes(), dtype=np.uint8).copy()
+    g["sess_blob"] = blob
+    g["sess_geom"] = np.array([nb_, kd_, ms_, pos_], dtype=np.int64)
+    return g
+
+
 def main() -> None:
     (HERE / "reference_kat.json").write_text(json.dumps(kat(), indent=1) + "\n")
     lib = oracle.load("ref")
     np.savez_compressed(HERE / "golden_ref.npz", **golden(lib))
-    print("wrote", HERE / "reference_kat.json", HERE / "golden_ref.npz")
+    ref_tree = Path(oracle.REF_TREE)
+    np.savez_compressed(HERE / "golden_glue.npz", **glue(lib), **ref_q4k_golden(ref_tree))
+    print("wrote", HERE / "reference_kat.json", HERE / "golden_ref.npz", HERE / "golden_glue.npz")
 
 
 if __name__ == "__main__":

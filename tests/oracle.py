@@ -18,6 +18,8 @@ ROOT = Path(__file__).resolve().parent.parent
 ORACLE_DIR = ROOT / "oracle"
 PORT_SO = ORACLE_DIR / "liboracle.so"
 REF_SO = ORACLE_DIR / "_ref" / "libyattn_ref.so"
+# the reference source tree (present where the oracle's reference build is made; absent on GPU boxes)
+REF_TREE = Path(os.environ.get("YATTN_REF_TREE", "/root/reference"))
 
 f32p = np.ctypeslib.ndpointer(dtype=np.float32, flags="C_CONTIGUOUS")
 u16p = np.ctypeslib.ndpointer(dtype=np.uint16, flags="C_CONTIGUOUS")
@@ -77,7 +79,7 @@ _cache: dict = {}
 
 def ensure_built() -> None:
     """Builds the oracle (and, where the reference tree exists, oracle/_ref)."""
-    if PORT_SO.exists() and (REF_SO.exists() or not Path("/root/reference").exists()):
+    if PORT_SO.exists() and (REF_SO.exists() or not REF_TREE.exists()):
         return
     subprocess.run(["make", "-C", str(ORACLE_DIR)], check=True, capture_output=True)
 

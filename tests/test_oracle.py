@@ -253,6 +253,67 @@ def test_q4k_and_f16_matmul_port_equals_reference(orc, orc_ref):
     assert np.array_equal(ya, yb)
 
 
+@pytest.fixture(scope="module")
+def glue():
+    return dict(np.load(GOLD / "golden_glue.npz"))
+
+
+def test_q4k_block_matches_reference_golden_vector(orc, glue):
+    """The reference's own Q4_K decode golden (tests/ref_data.h, two blocks of a real model row; its
+    test_matvec.c:57-69 checks q4k_block against it to 1e-6): the port and, where built, the reference build."""
+    import oracle
+
+    libs = [orc] + ([oracle.load("ref")] if oracle.has_ref() else [])
+    for lib in libs:
+        out = np.zeros(512, np.float32)
+        for b in range(2):
+            y = np.zeros(256, np.float32)
+            lib.orc_q4k_block(y, np.ascontiguousarray(glue["q4k_raw"][b * 144:(b + 1) * 144]))
+            out[b * 256:(b + 1) * 256] = y
+        assert np.max(np.abs(out - glue["q4k_ref"])) <= 1e-6
+
+
+def test_port_matches_reference_golden_glue(orc, glue):
+    """The port reproduces the reference build's outputs bit for bit on the rows around the attention path:
+    RoPE + KV store, GDN layer inputs, the Q4_K / fp16 matmuls and the session KV file."""
+    for kind in (0, 1, 2):
+        t = f"rope{kind}_"
+        H, KV, hd, nd, pos = (int(x) for x in glue[t + "geom"])
+        kd = KV * hd
+        inp = glue[t + "in"]
+        q, k, v = inp[:H * hd].copy(), inp[H * hd:H * hd + kd].copy(), inp[H * hd + kd:].copy()
+        kc = np.zeros((pos + 1) * kd, np.uint16)
+        vc = np.zeros((pos + 1) * kd, np.uint16)
+        orc.orc_rope_store(q, k, v, kc, vc, H, KV, hd, kd, kind, nd, pos, float(glue[t + "theta"][0]))
+        assert np.array_equal(q, glue[t + "q"]) and np.array_equal(kc[pos * kd:], glue[t + "krow"])
+        assert np.array_equal(vc[pos * kd:], glue[t + "vrow"])
+    n_seqs, T, nk, hk, nv, hv, kw = (int(x) for x in glue["gdni_geom"])
+    cc = 2 * nk * hk + nv * hv
+    outs = dict(q=np.zeros((n_seqs, T, nk * hk), np.float32), k=np.zeros((n_seqs, T, nk * hk), np.float32),
+                v=np.zeros((n_seqs, T, nv * hv), np.float32), gate=np.zeros((n_seqs, T, nv), np.float32),
+                beta=np.zeros((n_seqs, T, nv), np.float32))
+    st = glue["gdni_state"].copy()
+    orc.orc_gdn_inputs(glue["gdni_qkv"], st, glue["gdni_w"], glue["gdni_alpha"], glue["gdni_beta_in"],
+                       glue["gdni_dt"], glue["gdni_a"], outs["q"], outs["k"], outs["v"], outs["gate"], outs["beta"],
+                       n_seqs, T, cc, kw, nk, hk, nv, hv, 1e-6)
+    for key, val in outs.items():
+        assert np.array_equal(val, glue["gdni_out_" + key]), key
+    assert np.array_equal(st, glue["gdni_out_state_out"])
+    out, inn, B = (int(x) for x in glue["lin_geom"])
+    y = np.zeros((B, out), np.float32)
+    orc.orc_gemv_q4k(y, glue["lin_w4"], glue["lin_x"], out, inn, B)
+    assert np.array_equal(y, glue["lin_y4"])
+    orc.orc_gemv_f16(y, glue["lin_w16"], glue["lin_x"], out, inn, B)
+    assert np.array_equal(y, glue["lin_y16"])
+
+
+def test_port_session_file_matches_reference_golden(orc, glue, tmp_path):
+    nb, kd, ms, pos = (int(x) for x in glue["sess_geom"])
+    path = tmp_path / "s.kv"
+    assert orc.orc_sess_kv_save(glue["sess_blob"], nb, kd, ms, pos, str(path).encode()) == 0
+    assert path.read_bytes() == glue["sess_file"].tobytes()
+
+
 def test_per_head_gdn_call_equals_all_heads_call(orc):
     """orc_gdn_step splits the reference call per head; same bits as one call."""
     rng = np.random.default_rng(9)
