@@ -18,6 +18,7 @@ ROOT = Path(__file__).resolve().parent.parent
 ORACLE_DIR = ROOT / "oracle"
 PORT_SO = ORACLE_DIR / "liboracle.so"
 REF_SO = ORACLE_DIR / "_ref" / "libyattn_ref.so"
+REF_GPU_SO = ORACLE_DIR / "_ref" / "libref_cuda.so"   # the reference's own cuda_kernels.cu, built for sm_100a
 # the reference source tree (present where the oracle's reference build is made; absent on GPU boxes)
 REF_TREE = Path(os.environ.get("YATTN_REF_TREE", "/root/reference"))
 
@@ -79,7 +80,7 @@ _cache: dict = {}
 
 def ensure_built() -> None:
     """Builds the oracle (and, where the reference tree exists, oracle/_ref)."""
-    if PORT_SO.exists() and (REF_SO.exists() or not REF_TREE.exists()):
+    if PORT_SO.exists() and ((REF_SO.exists() and REF_GPU_SO.exists()) or not REF_TREE.exists()):
         return
     subprocess.run(["make", "-C", str(ORACLE_DIR)], check=True, capture_output=True)
 
@@ -99,6 +100,31 @@ def load(kind: str = "port") -> C.CDLL:
         fn.argtypes = args
     _cache[kind] = lib
     return lib
+
+
+def load_ref_gpu() -> C.CDLL:
+    """The reference's CUDA kernels (inference/cuda/cuda_kernels.cu, unmodified): its attention entry points take
+    device pointers and launch on the legacy default stream (cuda_kernels.h:55-63)."""
+    if "ref_gpu" in _cache:
+        return _cache["ref_gpu"]
+    ensure_built()
+    if not REF_GPU_SO.exists():
+        raise FileNotFoundError(f"{REF_GPU_SO} not built")
+    lib = C.CDLL(str(REF_GPU_SO))
+    lib.cuda_k_attn_decode.restype = None
+    lib.cuda_k_attn_decode.argtypes = [vp] * 4 + [u32] * 5
+    lib.cuda_k_attn_prefill.restype = None
+    lib.cuda_k_attn_prefill.argtypes = [vp] * 4 + [u32] * 7
+    _cache["ref_gpu"] = lib
+    return lib
+
+
+def has_ref_gpu() -> bool:
+    try:
+        load_ref_gpu()
+        return True
+    except (FileNotFoundError, OSError, subprocess.CalledProcessError):
+        return False
 
 
 def has_ref() -> bool:

@@ -1,0 +1,93 @@
+"""Our attention beside the reference's own CUDA attention kernels.
+
+The reference's inference/cuda/cuda_kernels.cu is compiled unmodified for
+sm_100a into oracle/_ref/libref_cuda.so.  Its cuda_k_attn_decode /
+cuda_k_attn_prefill (cuda_kernels.cu:543-655: one block per query head,
+one key per step) and ours get identical device inputs: the outputs must
+agree within the parity tolerance (2e-3 against max(|ref|, rms(ref))), and
+ours must be faster.  Run with -s to see the timings.
+"""
+import numpy as np
+import pytest
+import torch
+
+import oracle
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def ref_gpu():
+    assert torch.cuda.is_available(), "GPU tests need a CUDA device"
+    torch.cuda.set_device(0)
+    if not oracle.has_ref_gpu():
+        pytest.skip("oracle/_ref/libref_cuda.so not built (reference sources absent)")
+    return oracle.load_ref_gpu()
+
+
+def _kv(rng, rows, kd, dev):
+    k = oracle.f32_to_f16(rng.standard_normal(rows * kd).astype(np.float32))
+    v = oracle.f32_to_f16(rng.standard_normal(rows * kd).astype(np.float32))
+    return (torch.from_numpy(k.view(np.int16)).to(dev).view(torch.uint16),
+            torch.from_numpy(v.view(np.int16)).to(dev).view(torch.uint16))
+
+
+def _time(fn, reps):
+    fn()
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(reps):
+        fn()
+    b.record()
+    torch.cuda.synchronize()
+    return a.elapsed_time(b) * 1e3 / reps   # us per call
+
+
+@pytest.mark.parametrize("H,KV,hd,T", [(14, 2, 64, 512),      # config 1 shape
+                                       (32, 8, 128, 4096),    # one config-3 sequence
+                                       (16, 2, 256, 4096)])   # qwen35 gated-attention shape, no gate
+def test_decode_against_reference_cuda(ref_gpu, H, KV, hd, T):
+    from yllm_b200 import attn
+
+    dev = torch.device("cuda:0")
+    rng = np.random.default_rng(T + hd)
+    kd = KV * hd
+    q = torch.from_numpy(rng.standard_normal(H * hd).astype(np.float32)).to(dev)
+    k, v = _kv(rng, T, kd, dev)
+    out_ref = torch.zeros(H * hd, device=dev)
+    out = torch.zeros(H * hd, device=dev)
+    run_ref = lambda: ref_gpu.cuda_k_attn_decode(out_ref.data_ptr(), q.data_ptr(), k.data_ptr(), v.data_ptr(),
+                                                 T - 1, H, KV, hd, kd)
+    run_ours = lambda: attn.attn_decode(out, q, k, v, T - 1, H, KV, hd, kd)
+    t_ref = _time(run_ref, 3)
+    t_ours = _time(run_ours, 20)
+    oracle.assert_close(out.cpu().numpy(), out_ref.cpu().numpy(), what=f"decode vs reference CUDA H{H} hd{hd} T{T}")
+    print(f"\ndecode H={H} KV={KV} hd={hd} T={T}: reference CUDA {t_ref:.1f} us, ours {t_ours:.1f} us, "
+          f"{t_ref / t_ours:.1f}x")
+    assert t_ours < t_ref / 2
+
+
+def test_prefill_chunk_against_reference_cuda(ref_gpu):
+    """The engine's batched prefill calls the kernel on chunks of at most 64 tokens (engine.c:622-654): the last
+    64-token chunk of config 2 (Qwen3-0.6B shape, 2048 tokens)."""
+    from yllm_b200 import attn
+
+    dev = torch.device("cuda:0")
+    H, KV, hd, S, B = 16, 8, 128, 2048, 64
+    p0 = S - B
+    kd = KV * hd
+    rng = np.random.default_rng(2)
+    q = torch.from_numpy((0.5 * rng.standard_normal(B * H * hd)).astype(np.float32)).to(dev)
+    k, v = _kv(rng, S, kd, dev)
+    out_ref = torch.zeros(B * H * hd, device=dev)
+    out = torch.zeros(B * H * hd, device=dev)
+    run_ref = lambda: ref_gpu.cuda_k_attn_prefill(out_ref.data_ptr(), q.data_ptr(), k.data_ptr(), v.data_ptr(),
+                                                  p0, B, H, KV, hd, kd, H * hd)
+    run_ours = lambda: attn.attn_prefill(out, q, k, v, p0, B, H, KV, hd, kd, H * hd)
+    t_ref = _time(run_ref, 3)
+    t_ours = _time(run_ours, 20)
+    oracle.assert_close(out.cpu().numpy(), out_ref.cpu().numpy(), what="prefill chunk vs reference CUDA")
+    print(f"\nprefill chunk B={B} at pos {p0}: reference CUDA {t_ref:.1f} us, ours {t_ours:.1f} us, "
+          f"{t_ref / t_ours:.1f}x")
+    assert t_ours < t_ref / 2
