@@ -115,6 +115,14 @@ def load_ref_gpu() -> C.CDLL:
     lib.cuda_k_attn_decode.argtypes = [vp] * 4 + [u32] * 5
     lib.cuda_k_attn_prefill.restype = None
     lib.cuda_k_attn_prefill.argtypes = [vp] * 4 + [u32] * 7
+    lib.cuda_k_gemv_q4k.restype = C.c_int
+    lib.cuda_k_gemv_q4k.argtypes = [vp, vp, vp, u32, u32, C.c_char_p, sz]
+    lib.cuda_k_gemv_f16.restype = C.c_int
+    lib.cuda_k_gemv_f16.argtypes = [vp, vp, vp, vp, vp, u32, u32, C.c_char_p, sz]
+    lib.cuda_k_cublas_create.restype = C.c_int
+    lib.cuda_k_cublas_create.argtypes = [C.POINTER(vp), C.c_char_p, sz]
+    lib.cuda_k_cublas_destroy.restype = None
+    lib.cuda_k_cublas_destroy.argtypes = [vp]
     _cache["ref_gpu"] = lib
     return lib
 

@@ -91,3 +91,44 @@ def test_prefill_chunk_against_reference_cuda(ref_gpu):
     print(f"\nprefill chunk B={B} at pos {p0}: reference CUDA {t_ref:.1f} us, ours {t_ours:.1f} us, "
           f"{t_ref / t_ours:.1f}x")
     assert t_ours < t_ref / 2
+
+
+def test_gemv_against_reference_cuda(ref_gpu):
+    """One 14336 x 4096 matrix (Llama-3-8B gate/up): the reference's cuda_k_gemv_q4k (one CTA per output row,
+    cuda_kernels.cu:161-199) and its cuda_k_gemv_f16 on cuBLAS (x rounded to fp16, cuda_kernels.cu:53-87) beside
+    ours.  Q4_K within 2e-5 (both fp32); fp16 within the parity tolerance (the reference rounds x)."""
+    import ctypes as C
+
+    from yllm_b200 import attn
+
+    dev = torch.device("cuda:0")
+    out, inn = 14336, 4096
+    rng = np.random.default_rng(11)
+    nb = inn // 256
+    w4 = rng.integers(0, 256, (out, nb, 144), dtype=np.uint8)
+    w4[:, :, 0:2] = (rng.uniform(0.5, 2, (out, nb)) * 1e-3).astype(np.float16).view(np.uint8).reshape(out, nb, 2)
+    w4[:, :, 2:4] = (rng.uniform(0.5, 2, (out, nb)) * 1e-3).astype(np.float16).view(np.uint8).reshape(out, nb, 2)
+    tw4 = torch.from_numpy(w4.reshape(-1)).to(dev)
+    tw16 = torch.from_numpy((0.02 * rng.standard_normal((out, inn))).astype(np.float16).view(np.int16)).to(dev)
+    x = torch.from_numpy(rng.standard_normal(inn).astype(np.float32)).to(dev)
+    xf16 = torch.empty(inn, dtype=torch.int16, device=dev)
+    y_ref, y = torch.zeros(out, device=dev), torch.zeros(out, device=dev)
+    err = C.create_string_buffer(256)
+    handle = C.c_void_p()
+    assert ref_gpu.cuda_k_cublas_create(C.byref(handle), err, 256) == 0, err.value
+    try:
+        for name, ours, theirs, tol in (
+                ("q4k", lambda: attn.gemv_q4k(y, tw4, x, out, inn, 1),
+                 lambda: ref_gpu.cuda_k_gemv_q4k(y_ref.data_ptr(), tw4.data_ptr(), x.data_ptr(), out, inn, err, 256),
+                 2e-5),
+                ("f16", lambda: attn.gemv_f16(y, tw16, x, out, inn, 1),
+                 lambda: ref_gpu.cuda_k_gemv_f16(handle, y_ref.data_ptr(), tw16.data_ptr(), x.data_ptr(),
+                                                 xf16.data_ptr(), out, inn, err, 256),
+                 oracle.REL_TOL)):
+            t_ref = _time(theirs, 20)
+            t_ours = _time(ours, 20)
+            oracle.assert_close(y.cpu().numpy(), y_ref.cpu().numpy(), tol=tol, what=f"gemv {name} vs reference")
+            print(f"\ngemv {name} {out}x{inn}: reference CUDA {t_ref:.1f} us, ours {t_ours:.1f} us, "
+                  f"{t_ref / t_ours:.2f}x")
+    finally:
+        ref_gpu.cuda_k_cublas_destroy(handle)
