@@ -123,6 +123,10 @@ def load_ref_gpu() -> C.CDLL:
     lib.cuda_k_cublas_create.argtypes = [C.POINTER(vp), C.c_char_p, sz]
     lib.cuda_k_cublas_destroy.restype = None
     lib.cuda_k_cublas_destroy.argtypes = [vp]
+    lib.cuda_k_rope_llama_heads.restype = None
+    lib.cuda_k_rope_llama_heads.argtypes = [vp, u32, u32, u32, flt]
+    lib.cuda_k_store_kv.restype = None
+    lib.cuda_k_store_kv.argtypes = [vp, vp, vp, vp, u32, u32]
     _cache["ref_gpu"] = lib
     return lib
 
