@@ -46,6 +46,19 @@ def test_struct_layout_matches_header(tmp_path):
     assert c == YattnDecodeItem.pos.offset and d == YattnDecodeWork.part_base.offset
 
 
+def test_rope_item_layout_matches_header(tmp_path):
+    from yllm_b200._lib import YattnRopeItem
+
+    src = tmp_path / "r.c"
+    src.write_text('#include "yllm_attn_sm100.h"\n#include <stdio.h>\n#include <stddef.h>\n'
+                   'int main(void){printf("%zu %zu %zu\\n", sizeof(YattnRopeItem), offsetof(YattnRopeItem,vcache),'
+                   ' offsetof(YattnRopeItem,pos));return 0;}\n')
+    exe = tmp_path / "r"
+    subprocess.run(["gcc", "-I", str(ROOT / "include"), str(src), "-o", str(exe)], check=True)
+    a, b, c = (int(x) for x in subprocess.run([str(exe)], capture_output=True, text=True).stdout.split())
+    assert a == C.sizeof(YattnRopeItem) and b == YattnRopeItem.vcache.offset and c == YattnRopeItem.pos.offset
+
+
 def heads_per_cta(n_kv, hd):
     """The library's kv-head grouping: largest of 8/4/2/1 (4 at head_dim 256) dividing n_kv."""
     cap = 4 if hd >= 256 else 8
