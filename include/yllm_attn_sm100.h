@@ -46,7 +46,9 @@ void yattn_clear_error(void);
  * bounded wait that timed out (a kernel that times out returns early instead
  * of hanging), or 103 if a decode run met a malformed work item (q or gate
  * not 16-byte aligned; with a pool, K/V not at a row of the pool) and
- * stopped.  Synchronises the legacy default stream. */
+ * stopped.  It covers the allocation-free decode too, whose word sits in its
+ * static scratch; polling creates neither word.  Synchronises the legacy
+ * default stream. */
 int yattn_device_status(int* status_out, int clear, char* err, size_t errlen);
 
 /* ------------------------------------------------ drop-in replacements
@@ -64,9 +66,12 @@ void cuda_k_attn_decode(float* att_out,
 /* Replaces cuda_k_attn_prefill (cuda_kernels.h:60-63; kernel cuda_kernels.cu:602-655).
  * B query tokens at positions pos_start..pos_start+B-1 (q row b at
  * q + b*q_stride); token b attends keys 0..pos_start+b.  Any B (the reference
- * caps a chunk at 64).  Flash attention on tcgen05 tensor cores: q is rounded
- * to fp16 on load, P is fp16, accumulation fp32.  Needs 16-byte aligned
- * pointers, q_stride % 4 == 0, kv_dim % 8 == 0, head_dim 64/128/256. */
+ * caps a chunk at 64).  Flash attention on tcgen05 tensor cores with fp32
+ * accumulation.  q is split into fp16 hi + lo planes (about 22 significant
+ * bits) in every 128-row query tile that holds a value fp16 does not represent
+ * exactly; a tile of fp16-exact q uses the hi plane alone.  |q| must stay below
+ * 65504.  P is split the same way.  Needs 16-byte aligned pointers,
+ * q_stride % 4 == 0, kv_dim % 8 == 0, head_dim 64/128/256. */
 void cuda_k_attn_prefill(float* att_out,
                          const float* q, const uint16_t* kcache, const uint16_t* vcache,
                          uint32_t pos_start, uint32_t B, uint32_t n_heads, uint32_t n_kv_heads,
@@ -244,9 +249,12 @@ int yattn_merge_partials_packed(float* out, const float* parts, uint32_t n_parts
  * yattn_exchange_merge, after yattn_decode_partial wrote this rank's (ml, o):
  * stores them into every rank's area over NVLink (stores only, no peer loads),
  * raises this rank's per-head flags there (release, system scope), waits
- * (bounded; a timeout sets yattn_device_status 401) for every rank's flags in
- * the local area and merges all parts into out[n_heads*head_dim] (x sigmoid(gate)
- * if gate).  areas[r] is rank r's area as mapped in this process; areas[rank]
+ * (bounded by wait_limit_ns, 0 = 2 s) for every rank's flags in the local area
+ * and merges all parts into out[n_heads*head_dim] (x sigmoid(gate) if gate).
+ * A head whose parts all have l == 0 (every shard empty) gets 0.  If a rank's
+ * flags do not arrive in time, yattn_device_status reads 401, out is NaN and
+ * the areas' epochs are out of step: free and re-create them before another
+ * call.  areas[r] is rank r's area as mapped in this process; areas[rank]
  * is the local one.  All ranks must make the same sequence of calls.  No
  * reference counterpart: the reference has no multi-GPU attention. */
 size_t yattn_exchange_area_bytes(uint32_t world, uint32_t n_heads, uint32_t head_dim);
@@ -258,7 +266,8 @@ int yattn_ipc_open(const void* handle /* 64 bytes */, void** ptr_out, char* err,
 int yattn_ipc_close(void* ptr, char* err, size_t errlen);
 int yattn_exchange_merge(const float* ml, const float* o, void* const* areas, uint32_t world,
                          uint32_t rank, uint32_t n_heads, uint32_t head_dim, float* out,
-                         const float* gate, void* stream, char* err, size_t errlen);
+                         const float* gate, uint64_t wait_limit_ns, void* stream, char* err,
+                         size_t errlen);
 
 /* Error-returning form of cuda_k_attn_decode with an explicit stream and gate. */
 int yattn_attn_decode(float* att_out, const float* q, const uint16_t* kcache,
@@ -282,10 +291,14 @@ int yattn_attn_prefill(float* att_out, const float* q, const uint16_t* kcache,
  * not fit (many splits at head_dim 256 with 8 query heads per kv head) is
  * rejected with an error naming the bytes needed.  The first call on a device
  * looks up the array's device address (no allocation), so make that first
- * call before any stream capture.  Every call on a device shares the array and
- * clears what must start at zero; calls that overlap on the GPU (other
- * streams or host threads) race on it and must be serialised by the caller.
- * Same arguments, results and errors as yattn_attn_decode otherwise. */
+ * call before any stream capture; after cudaDeviceReset() that address is
+ * stale and this entry must not be called again in the process.  Every call on
+ * a device shares the array and clears what must start at zero (the merge
+ * counters); calls that overlap on the GPU (other streams or host threads) race
+ * on it and must be serialised by the caller.  Device-side failures (a bounded
+ * wait that gave up, a misaligned gate) are kept in the array's status word
+ * until yattn_device_status reads and clears them.  Same arguments, results and
+ * errors as yattn_attn_decode otherwise. */
 int yattn_attn_decode_noalloc(float* att_out, const float* q, const uint16_t* kcache,
                               const uint16_t* vcache, const float* gate, uint32_t pos,
                               uint32_t n_heads, uint32_t n_kv_heads, uint32_t head_dim,

@@ -28,3 +28,18 @@ def orc_ref():
     if not oracle.has_ref():
         pytest.skip("oracle/_ref not built (reference sources absent)")
     return oracle.load("ref")
+
+
+def pytest_sessionfinish(session, exitstatus):
+    """With YATTN_PARITY_LOG set, writes every parity check's error and floor
+    (oracle.PARITY_LOG) there as JSON."""
+    import json
+    import os
+
+    path = os.environ.get("YATTN_PARITY_LOG")
+    if not path:
+        return
+    import oracle
+
+    with open(path, "w") as f:
+        json.dump(oracle.PARITY_LOG, f, indent=0)

@@ -307,23 +307,176 @@ def checksum(a: np.ndarray, lib=None) -> int:
 
 # ------------------------------------------------------------ tolerance
 
-REL_TOL = 2e-3
+REL_TOL = 2e-3      # the north star's 2e-3 relative bar
+RMS_FLOOR = 1e-3    # the per-element floor of the parity metric, in units of rms(cpu)
+
+# (what, error, floor) of every assert_close in this process; the GPU test run
+# writes it out (tests/conftest.py) so the achieved margins are on record.
+PARITY_LOG: list = []
 
 
-def rel_err(gpu: np.ndarray, cpu: np.ndarray) -> float:
-    """max |gpu - cpu| / max(|cpu|, rms(cpu)): the relative error the parity
-    bar (2e-3) is stated in.  The rms floor keeps near-zero outputs (where the
-    CPU's own fp32 summation order already differs from any other order by
-    more than 2e-3 relative) from dominating."""
+def rel_err(gpu: np.ndarray, cpu: np.ndarray, floor: float = RMS_FLOOR) -> float:
+    """max_i |gpu_i - cpu_i| / max(|cpu_i|, floor * rms(cpu)).
+
+    With the default floor this is the parity metric the work is held to:
+    per element |gpu - cpu| <= 2e-3 * max(|cpu|, 1e-3 * rms(cpu))."""
     gpu = np.asarray(gpu, dtype=np.float64)
     cpu = np.asarray(cpu, dtype=np.float64)
+    if not cpu.size:
+        return 0.0
+    rms = float(np.sqrt(np.mean(cpu * cpu)))
+    den = np.maximum(np.abs(cpu), max(floor * rms, 1e-300))
+    return float(np.max(np.abs(gpu - cpu) / den))
+
+
+def noise_floor(cpu: np.ndarray, exact: np.ndarray, margin: float = 2.0, tol: float = REL_TOL) -> float:
+    """The rms floor that the CPU result's own rounding requires.
+
+    `exact` is the same computation in float64.  The fp32 CPU result differs
+    from it by up to e = max|cpu - exact|; an equally accurate GPU result can
+    differ from the CPU's by up to 2e.  The returned floor is the smallest one
+    at which a difference of margin * e passes the bar `tol` on every element,
+    and never below RMS_FLOOR: on short reductions this is RMS_FLOOR itself,
+    on long ones (many keys, thousands of recurrent steps) the fp32 summation
+    noise near zero outputs sets it."""
+    cpu = np.asarray(cpu, dtype=np.float64)
+    exact = np.asarray(exact, dtype=np.float64)
     rms = float(np.sqrt(np.mean(cpu * cpu))) if cpu.size else 0.0
-    den = np.maximum(np.abs(cpu), rms if rms > 0 else 1e-30)
-    return float(np.max(np.abs(gpu - cpu) / den)) if cpu.size else 0.0
+    if rms == 0.0:
+        return RMS_FLOOR
+    e = float(np.max(np.abs(cpu - exact)))
+    return max(RMS_FLOOR, margin * e / (tol * rms))
 
 
-def assert_close(gpu: np.ndarray, cpu: np.ndarray, tol: float = REL_TOL, what: str = "") -> float:
+def assert_close(gpu: np.ndarray, cpu: np.ndarray, tol: float = REL_TOL, what: str = "",
+                 exact: Optional[np.ndarray] = None, floor: Optional[float] = None) -> float:
+    """Asserts the parity metric rel_err(gpu, cpu, floor) <= tol.  The floor is
+    RMS_FLOOR unless `exact` (the float64 evaluation) is given, in which case
+    it is noise_floor(cpu, exact)."""
+    gpu = np.asarray(gpu)
     assert np.all(np.isfinite(gpu)), f"{what}: non-finite GPU output"
-    e = rel_err(gpu, cpu)
-    assert e <= tol, f"{what}: relative error {e:.3e} > {tol:.1e}"
+    if floor is None:
+        floor = RMS_FLOOR if exact is None else noise_floor(cpu, exact, tol=tol)
+    e = rel_err(gpu, cpu, floor)
+    PARITY_LOG.append({"what": what, "err": e, "floor": floor, "tol": tol,
+                       "err_at_1e-3": rel_err(gpu, cpu, RMS_FLOOR)})
+    assert e <= tol, f"{what}: relative error {e:.3e} > {tol:.1e} (rms floor {floor:.2e})"
     return e
+
+
+# ------------------------------------------------------------ RoPE
+
+def rope_pair_norm(x, kind, hd, n_dims):
+    """Per element: the norm of its rotation pair (llama 2j/2j+1, qwen j/j+hd/2,
+    M-RoPE j/j+n/2 within the first n dims; unrotated dims: the element)."""
+    x = np.asarray(x, np.float64)
+    heads = x.reshape(-1, hd)
+    mate = np.arange(hd)
+    if kind == 0:
+        mate = mate ^ 1
+    elif kind == 1:
+        mate = (mate + hd // 2) % hd
+    else:
+        half = n_dims // 2
+        m = np.arange(n_dims)
+        mate[:n_dims] = np.where(m < half, m + half, m - half)
+    return np.sqrt(heads * heads + heads[:, mate] ** 2).reshape(x.shape)
+
+
+def rope_err(gpu, ref, kind, hd, n_dims):
+    """max |gpu - ref| / max(|pair|, 1e-3 * rms(ref)): the error of rotated q
+    measured against the norm of each element's rotation pair, which a
+    rotation keeps (a few-ulp sin/cos difference moves both outputs by a few
+    ulps of it; the output element alone can be a cancellation)."""
+    ref = np.asarray(ref, np.float64)
+    rms = float(np.sqrt(np.mean(ref * ref)))
+    den = np.maximum(rope_pair_norm(ref, kind, hd, n_dims), 1e-3 * rms)
+    return float(np.max(np.abs(np.asarray(gpu, np.float64) - ref) / den))
+
+
+# ------------------------------------------------- float64 evaluations
+#
+# The same attention and recurrence as the engine (engine.c:1074-1096, 533-563,
+# 935-960; matvec.c:975-1021), evaluated in float64 from the same input bits.
+# They are not the parity target (the fp32 oracle is); they measure how far the
+# fp32 oracle itself sits from the exact value, which sets noise_floor.
+
+def _heads_of(g, H, KV):
+    return [h for h in range(H) if h * KV // H == g]
+
+
+def exact_decode(q, k, v, pos, n_heads, n_kv, hd, kv_dim, gate=None) -> np.ndarray:
+    kf = f16_to_f32(np.asarray(k, np.uint16).ravel()[: (pos + 1) * kv_dim]).astype(np.float64).reshape(-1, kv_dim)
+    vf = f16_to_f32(np.asarray(v, np.uint16).ravel()[: (pos + 1) * kv_dim]).astype(np.float64).reshape(-1, kv_dim)
+    q64 = np.asarray(q, np.float64).reshape(n_heads, hd)
+    out = np.empty((n_heads, hd))
+    for g in range(n_kv):
+        hs = _heads_of(g, n_heads, n_kv)
+        if not hs:
+            continue
+        s = (q64[hs] @ kf[:, g * hd:(g + 1) * hd].T) / np.sqrt(hd)
+        s -= s.max(axis=1, keepdims=True)
+        p = np.exp(s)
+        p /= p.sum(axis=1, keepdims=True)
+        out[hs] = p @ vf[:, g * hd:(g + 1) * hd]
+    out = out.ravel()
+    if gate is not None:
+        out = out / (1.0 + np.exp(-np.asarray(gate, np.float64).ravel()))
+    return out
+
+
+def exact_prefill(q, k, v, pos_start, B, n_heads, n_kv, hd, kv_dim, q_stride, gate=None,
+                  rows: Optional[slice] = None) -> np.ndarray:
+    """float64 causal prefill, [B, q_stride] (columns past n_heads*hd are 0)."""
+    n = pos_start + B
+    kf = f16_to_f32(np.asarray(k, np.uint16).ravel()[: n * kv_dim]).astype(np.float64).reshape(n, kv_dim)
+    vf = f16_to_f32(np.asarray(v, np.uint16).ravel()[: n * kv_dim]).astype(np.float64).reshape(n, kv_dim)
+    q64 = np.asarray(q, np.float64).reshape(B, q_stride)
+    out = np.zeros((B, q_stride))
+    pos = pos_start + np.arange(B)
+    for h in range(n_heads):
+        g = h * n_kv // n_heads
+        Kg, Vg = kf[:, g * hd:(g + 1) * hd], vf[:, g * hd:(g + 1) * hd]
+        for r0 in range(0, B, 512):
+            r1 = min(B, r0 + 512)
+            s = (q64[r0:r1, h * hd:(h + 1) * hd] @ Kg.T) / np.sqrt(hd)
+            s[np.arange(n)[None, :] > pos[r0:r1, None]] = -np.inf
+            s -= s.max(axis=1, keepdims=True)
+            p = np.exp(s)
+            p /= p.sum(axis=1, keepdims=True)
+            out[r0:r1, h * hd:(h + 1) * hd] = p @ Vg
+    if gate is not None:
+        g64 = np.asarray(gate, np.float64).reshape(B, q_stride)
+        out[:, : n_heads * hd] /= 1.0 + np.exp(-g64[:, : n_heads * hd])
+    return out
+
+
+def exact_gdn(fx: dict, cfg, n_seqs: int, T: int, epilogue: bool) -> tuple:
+    """float64 form of gdn_run: (final state, outputs)."""
+    D, NK, NV = cfg.head_dim, cfg.num_k_heads, cfg.n_v_heads
+    S_all = np.asarray(fx["S"], np.float64).reshape(n_seqs, NV, D, D).copy()
+    q = np.asarray(fx["q"], np.float64).reshape(n_seqs, T, NK, D)
+    k = np.asarray(fx["k"], np.float64).reshape(n_seqs, T, NK, D)
+    v = np.asarray(fx["v"], np.float64).reshape(n_seqs, T, NV, D)
+    z = np.asarray(fx["z"], np.float64).reshape(n_seqs, T, NV, D)
+    gate = np.asarray(fx["gate"], np.float64).reshape(n_seqs, T, NV)
+    beta = np.asarray(fx["beta"], np.float64).reshape(n_seqs, T, NV)
+    w = np.asarray(fx["norm_w"], np.float64)
+    kh = np.arange(NV) % NK
+    out = np.empty((n_seqs, T, NV, D))
+    scale = 1.0 / np.sqrt(D)
+    for s in range(n_seqs):
+        S = S_all[s]                                   # [NV, D(v row j), D(k index i)]
+        for t in range(T):
+            kt, qt = k[s, t, kh], q[s, t, kh]           # [NV, D]
+            S *= np.exp(gate[s, t])[:, None, None]
+            dot = np.einsum("hji,hi->hj", S, kt)
+            delta = (v[s, t] - dot) * beta[s, t][:, None]
+            S += delta[:, :, None] * kt[:, None, :]
+            o = np.einsum("hji,hi->hj", S, qt) * scale
+            if epilogue:
+                zz = z[s, t]
+                inv = 1.0 / np.sqrt(np.mean(o * o, axis=1, keepdims=True) + cfg.eps)
+                o = o * w[None, :] * inv * (zz / (1.0 + np.exp(-zz)))
+            out[s, t] = o
+    return S_all.ravel(), out.ravel()

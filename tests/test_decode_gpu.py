@@ -1,7 +1,9 @@
 """GPU parity of the decode path against the CPU oracle (engine.c:1074-1096).
 
-Tolerance: oracle.REL_TOL = 2e-3, relative to max(|cpu|, rms(cpu)) per element
-(oracle.rel_err).  Seeded-input plumbing is checked bit for bit.
+Tolerance: per element |gpu - cpu| <= 2e-3 * max(|cpu|, f * rms(cpu))
+(oracle.assert_close), f = 1e-3 unless the CPU's own fp32 rounding, measured
+against a float64 evaluation of the same inputs (oracle.exact_decode), needs a
+higher floor (oracle.noise_floor).  Seeded-input plumbing is checked bit for bit.
 """
 import numpy as np
 import pytest
@@ -125,8 +127,9 @@ def test_decode_matches_oracle(dev, H, KV, hd, T):
     out = torch.zeros(H * hd, device=dev)
     attn.attn_decode(out, tq, tk, tv, T - 1, H, KV, hd, kd)
     want = oracle.attn_decode(q, k, v, T - 1, H, KV, hd, kd)
+    exact = oracle.exact_decode(q, k, v, T - 1, H, KV, hd, kd)
     torch.cuda.synchronize()
-    oracle.assert_close(out.cpu().numpy(), want, what=f"decode H{H} KV{KV} hd{hd} T{T}")
+    oracle.assert_close(out.cpu().numpy(), want, what=f"decode H{H} KV{KV} hd{hd} T{T}", exact=exact)
     # the drop-in entry point gives the same bits
     out2 = torch.zeros_like(out)
     attn.cuda_k_attn_decode(out2, tq, tk, tv, T - 1, H, KV, hd, kd)
@@ -145,7 +148,8 @@ def test_decode_padded_kv_rows(dev):
     attn.attn_decode(out, tq, tk, tv, T - 1, H, KV, hd, kd)
     want = oracle.attn_decode(q, k, v, T - 1, H, KV, hd, kd)
     torch.cuda.synchronize()
-    oracle.assert_close(out.cpu().numpy(), want, what="padded rows")
+    oracle.assert_close(out.cpu().numpy(), want, what="padded rows",
+                        exact=oracle.exact_decode(q, k, v, T - 1, H, KV, hd, kd))
 
 
 def test_decode_config1_all_layers(dev):
@@ -160,7 +164,8 @@ def test_decode_config1_all_layers(dev):
     for layer in range(c.layers):
         f = oracle.decode_fixture(c, layer, 0)
         want = oracle.attn_decode(f["q"], f["k"], f["v"], f["pos"], c.n_heads, c.n_kv_heads, c.head_dim, c.kv_dim)
-        oracle.assert_close(d.out[layer, 0].cpu().numpy(), want, what=f"config1 layer {layer}")
+        exact = oracle.exact_decode(f["q"], f["k"], f["v"], f["pos"], c.n_heads, c.n_kv_heads, c.head_dim, c.kv_dim)
+        oracle.assert_close(d.out[layer, 0].cpu().numpy(), want, what=f"config1 layer {layer}", exact=exact)
 
 
 def _pool(d):
@@ -173,8 +178,9 @@ def test_decode_config3_batched_plan(dev, pooled):
     from yllm_b200.configs import CFG3 as c
 
     ctx = c.ctx()
-    seqs = sorted(set([int(np.argmin(ctx)), int(np.argmax(ctx)), 0, 1, 2, 31, 63]))
-    layers = [0, 31]
+    # 16 of the 64 sequences (the shortest, the longest, and an even spread) x 4 of the 32 layers
+    seqs = sorted(set([int(np.argmin(ctx)), int(np.argmax(ctx))] + list(range(0, 64, 4))))[:16]
+    layers = [0, 9, 22, 31]
     d = fixtures.decode_inputs(c, layers=layers, seqs=seqs, device=dev)
     plan = attn.DecodePlan.build([x - 1 for x in d.ctx], c.n_heads, c.n_kv_heads, c.head_dim, c.kv_dim,
                                  pool=_pool(d) if pooled else None)
@@ -188,7 +194,10 @@ def test_decode_config3_batched_plan(dev, pooled):
             f = oracle.decode_fixture(c, layer, s)
             want = oracle.attn_decode(f["q"], f["k"], f["v"], f["pos"], c.n_heads, c.n_kv_heads, c.head_dim,
                                       c.kv_dim)
-            oracle.assert_close(d.out[li, si].cpu().numpy(), want, what=f"config3 layer {layer} seq {s}")
+            exact = oracle.exact_decode(f["q"], f["k"], f["v"], f["pos"], c.n_heads, c.n_kv_heads, c.head_dim,
+                                        c.kv_dim)
+            oracle.assert_close(d.out[li, si].cpu().numpy(), want, what=f"config3 layer {layer} seq {s}",
+                                exact=exact)
     assert attn.device_status() == 0
 
 
@@ -202,7 +211,8 @@ def test_decode_config4_long_context(dev):
     torch.cuda.synchronize()
     f = oracle.decode_fixture(c, 0, 0)
     want = oracle.attn_decode(f["q"], f["k"], f["v"], f["pos"], c.n_heads, c.n_kv_heads, c.head_dim, c.kv_dim)
-    oracle.assert_close(d.out[0, 0].cpu().numpy(), want, what="config4")
+    exact = oracle.exact_decode(f["q"], f["k"], f["v"], f["pos"], c.n_heads, c.n_kv_heads, c.head_dim, c.kv_dim)
+    oracle.assert_close(d.out[0, 0].cpu().numpy(), want, what="config4", exact=exact)
 
 
 @pytest.mark.parametrize("pooled", [False, True])
@@ -210,7 +220,7 @@ def test_gated_decode_qwen35(dev, pooled):
     from yllm_b200 import attn, fixtures
     from yllm_b200.configs import CFG5_GATED_DECODE as c
 
-    seqs = [0, 7, 31]
+    seqs = list(range(c.n_seqs))   # all 32 sequences of the batch
     d = fixtures.decode_inputs(c, seqs=seqs, device=dev)
     plan = attn.DecodePlan.build([x - 1 for x in d.ctx], c.n_heads, c.n_kv_heads, c.head_dim, c.kv_dim,
                                  pool=_pool(d) if pooled else None)
@@ -222,7 +232,9 @@ def test_gated_decode_qwen35(dev, pooled):
         f = oracle.decode_fixture(c, 0, s)
         want = oracle.attn_decode(f["q"], f["k"], f["v"], f["pos"], c.n_heads, c.n_kv_heads, c.head_dim, c.kv_dim,
                                   gate=f["gate"])
-        oracle.assert_close(d.out[0, si].cpu().numpy(), want, what=f"gated decode seq {s}")
+        exact = oracle.exact_decode(f["q"], f["k"], f["v"], f["pos"], c.n_heads, c.n_kv_heads, c.head_dim,
+                                    c.kv_dim, gate=f["gate"])
+        oracle.assert_close(d.out[0, si].cpu().numpy(), want, what=f"gated decode seq {s}", exact=exact)
 
 
 @pytest.mark.parametrize("H,KV,hd,ctxs", [
@@ -255,7 +267,8 @@ def test_pooled_batched_decode_ragged(dev, H, KV, hd, ctxs):
         k = np.ascontiguousarray(pool_np[offs[i]:offs[i] + c]).reshape(-1)
         v = np.ascontiguousarray(pool_np[offs[i] + c:offs[i] + 2 * c]).reshape(-1)
         want = oracle.attn_decode(qs[i], k, v, c - 1, H, KV, hd, kd)
-        oracle.assert_close(outs[i].cpu().numpy(), want, what=f"pooled H{H} KV{KV} hd{hd} ctx{c}")
+        oracle.assert_close(outs[i].cpu().numpy(), want, what=f"pooled H{H} KV{KV} hd{hd} ctx{c}",
+                            exact=oracle.exact_decode(qs[i], k, v, c - 1, H, KV, hd, kd))
     assert attn.device_status() == 0
 
 
@@ -275,7 +288,8 @@ def test_split_partials_merge_to_full(dev):
     attn.merge_partials(out, ml, o, n, H, hd)
     torch.cuda.synchronize()
     want = oracle.attn_decode(q, k, v, T - 1, H, KV, hd, kd)
-    oracle.assert_close(out.cpu().numpy(), want, what="split merge")
+    oracle.assert_close(out.cpu().numpy(), want, what="split merge",
+                        exact=oracle.exact_decode(q, k, v, T - 1, H, KV, hd, kd))
     # an empty shard (l = 0) is ignored by the merge
     ml2 = torch.cat([ml, torch.zeros(1, H, 2, device=dev)])
     o2 = torch.cat([o, torch.zeros(1, H, hd, device=dev)])
@@ -303,7 +317,8 @@ def test_packed_exchange_payload_merge(dev):
     attn.merge_partials_packed(out, parts, 4, H, hd)
     torch.cuda.synchronize()
     want = oracle.attn_decode(q, k, v, T - 1, H, KV, hd, kd)
-    oracle.assert_close(out.cpu().numpy(), want, what="packed exchange merge")
+    oracle.assert_close(out.cpu().numpy(), want, what="packed exchange merge",
+                        exact=oracle.exact_decode(q, k, v, T - 1, H, KV, hd, kd))
 
 
 def test_repeated_runs_are_deterministic_and_reuse_workspace(dev):

@@ -1,7 +1,9 @@
 """GPU parity of the Gated DeltaNet kernels against the CPU oracle
 (gdn_state_update, matvec.c:975-1004; rmsnorm_gated, matvec.c:1007-1021;
-token-by-token prefill, engine.c:723-734).  Tolerance oracle.REL_TOL (2e-3,
-relative to max(|cpu|, rms(cpu))) on outputs and on the final fp32 state."""
+token-by-token prefill, engine.c:723-734).  Tolerance on outputs and on the
+final fp32 state: per element |gpu - cpu| <= 2e-3 * max(|cpu|, f * rms(cpu)),
+f = 1e-3 unless the CPU's own fp32 rounding against a float64 run of the same
+recurrence (oracle.exact_gdn) needs more (oracle.noise_floor)."""
 import numpy as np
 import pytest
 import torch
@@ -47,8 +49,9 @@ def test_gdn_decode_batch32(dev, epilogue):
     torch.cuda.synchronize()
     fx = oracle.gdn_fixture(c, n, 1, seeded_state=True)
     S_want, out_want = oracle.gdn_run(fx, c, n, 1, epilogue)
-    oracle.assert_close(_np(g.out), out_want, what="gdn decode out")
-    oracle.assert_close(_np(g.S), S_want, what="gdn decode state")
+    S_ex, out_ex = oracle.exact_gdn(fx, c, n, 1, epilogue)
+    oracle.assert_close(_np(g.out), out_want, what="gdn decode out", exact=out_ex)
+    oracle.assert_close(_np(g.S), S_want, what="gdn decode state", exact=S_ex)
 
 
 def test_gdn_dropin_matches_reference_signature(dev):
@@ -61,8 +64,9 @@ def test_gdn_dropin_matches_reference_signature(dev):
     torch.cuda.synchronize()
     fx = oracle.gdn_fixture(c, 1, 1, seeded_state=True)
     S_want, out_want = oracle.gdn_run(fx, c, 1, 1, False)
-    oracle.assert_close(_np(g.out), out_want, what="drop-in out")
-    oracle.assert_close(_np(g.S), S_want, what="drop-in state")
+    S_ex, out_ex = oracle.exact_gdn(fx, c, 1, 1, False)
+    oracle.assert_close(_np(g.out), out_want, what="drop-in out", exact=out_ex)
+    oracle.assert_close(_np(g.S), S_want, what="drop-in state", exact=S_ex)
 
 
 @pytest.mark.parametrize("n_seqs,T,seeded,epilogue", [(1, 37, True, True), (3, 100, False, False),
@@ -77,8 +81,9 @@ def test_gdn_prefill_small(dev, n_seqs, T, seeded, epilogue):
     torch.cuda.synchronize()
     fx = oracle.gdn_fixture(c, n_seqs, T, seeded_state=seeded)
     S_want, out_want = oracle.gdn_run(fx, c, n_seqs, T, epilogue)
-    oracle.assert_close(_np(g.out), out_want, what=f"gdn prefill out {n_seqs}x{T}")
-    oracle.assert_close(_np(g.S), S_want, what=f"gdn prefill state {n_seqs}x{T}")
+    S_ex, out_ex = oracle.exact_gdn(fx, c, n_seqs, T, epilogue)
+    oracle.assert_close(_np(g.out), out_want, what=f"gdn prefill out {n_seqs}x{T}", exact=out_ex)
+    oracle.assert_close(_np(g.S), S_want, what=f"gdn prefill state {n_seqs}x{T}", exact=S_ex)
 
 
 def test_gdn_prefill_config5a_full(dev):
@@ -93,8 +98,9 @@ def test_gdn_prefill_config5a_full(dev):
     torch.cuda.synchronize()
     fx = oracle.gdn_fixture(c, 1, T, seeded_state=False)
     S_want, out_want = oracle.gdn_run(fx, c, 1, T, True)
-    oracle.assert_close(_np(g.out), out_want, what="gdn 4096-token prefill out")
-    oracle.assert_close(_np(g.S), S_want, what="gdn 4096-token prefill state")
+    S_ex, out_ex = oracle.exact_gdn(fx, c, 1, T, True)
+    oracle.assert_close(_np(g.out), out_want, what="gdn 4096-token prefill out", exact=out_ex)
+    oracle.assert_close(_np(g.S), S_want, what="gdn 4096-token prefill state", exact=S_ex)
 
 
 @pytest.mark.parametrize("n_seqs,T,seeded", [(1, 63, True), (1, 64, True), (2, 65, True), (1, 200, False),
@@ -114,8 +120,10 @@ def test_gdn_chunked_matches_recurrent_kernel(dev, n_seqs, T, seeded):
     attn.gdn_prefill_recurrent(b.S, b.out, b.q, b.k, b.v, b.gate, b.beta, n_seqs, T, NK, D, NV, D, norm_w=b.norm_w,
                                z=b.z, eps=c.eps)
     torch.cuda.synchronize()
-    oracle.assert_close(_np(a.out), _np(b.out), what=f"chunked vs recurrent out {n_seqs}x{T}")
-    oracle.assert_close(_np(a.S), _np(b.S), what=f"chunked vs recurrent state {n_seqs}x{T}")
+    fx = oracle.gdn_fixture(c, n_seqs, T, seeded_state=seeded)
+    S_ex, out_ex = oracle.exact_gdn(fx, c, n_seqs, T, True)
+    oracle.assert_close(_np(a.out), _np(b.out), what=f"chunked vs recurrent out {n_seqs}x{T}", exact=out_ex)
+    oracle.assert_close(_np(a.S), _np(b.S), what=f"chunked vs recurrent state {n_seqs}x{T}", exact=S_ex)
     assert attn.device_status() == 0
 
 
@@ -132,8 +140,10 @@ def test_gdn_prefill_equals_decode_steps(dev):
     for t in range(T):
         attn.gdn_decode(b.S, b.out[t], b.q[t], b.k[t], b.v[t], b.gate[t], b.beta[t], 1, NK, D, NV, D)
     torch.cuda.synchronize()
-    oracle.assert_close(_np(a.out), _np(b.out), what="prefill vs decode out")
-    oracle.assert_close(_np(a.S), _np(b.S), what="prefill vs decode state")
+    fx = oracle.gdn_fixture(c, 1, T, seeded_state=True)
+    S_ex, out_ex = oracle.exact_gdn(fx, c, 1, T, False)
+    oracle.assert_close(_np(a.out), _np(b.out), what="prefill vs decode out", exact=out_ex)
+    oracle.assert_close(_np(a.S), _np(b.S), what="prefill vs decode state", exact=S_ex)
 
 
 def test_gdn_rejects_unsupported(dev):
@@ -255,5 +265,9 @@ def test_gdn_layer_decode_from_projections(dev):
         out[:, t_] = o
     torch.cuda.synchronize()
     assert attn.device_status() == 0
-    oracle.assert_close(_np(out), out_ref.ravel(), what="GDN layer output")
-    oracle.assert_close(_np(S), S_ref.ravel(), what="GDN state")
+    from types import SimpleNamespace
+    fx = dict(S=S0, q=qr, k=kr, v=vr, z=z, gate=gr, beta=br, norm_w=norm_w)
+    S_ex, out_ex = oracle.exact_gdn(fx, SimpleNamespace(head_dim=hk, num_k_heads=nk, n_v_heads=nv, eps=1e-6),
+                                    n_seqs, T, True)
+    oracle.assert_close(_np(out), out_ref.ravel(), what="GDN layer output", exact=out_ex)
+    oracle.assert_close(_np(S), S_ref.ravel(), what="GDN state", exact=S_ex)

@@ -2,8 +2,10 @@
 cuda_k_gemv_* / cuda_k_gemm_* drop-ins) against the oracle: Q4_K weights
 dequantised by the reference's q4k_block (matvec.c:40-59) and summed in fp32
 (the arithmetic of cuda_kernels.cu:142-159); fp16 rows through the engine's
-matmul (matvec.c:111-122).  The GPU sums in another order: relative error
-<= 2e-5 (against max(|cpu|, rms(cpu)))."""
+matmul (matvec.c:111-122).  The GPU sums in another order: per element
+|gpu - cpu| <= 2e-5 * max(|cpu|, f * rms(cpu)), f = 1e-3 unless the CPU's own
+fp32 summation, measured against a float64 product of the same dequantised
+weights, needs more (oracle.noise_floor)."""
 import ctypes as C
 
 import numpy as np
@@ -38,6 +40,26 @@ def q4k_weights(rng, out, in_):
     return np.ascontiguousarray(blk.reshape(-1))
 
 
+def q4k_dequant_f64(w, out, in_):
+    """The published Q4_K block layout decoded in float64 for every block at once:
+    [out, in_] weights d*sc*n - dmin*m (the decode of matvec.c:26-59)."""
+    blk = np.asarray(w, np.uint8).reshape(out * (in_ // 256), 144)
+    d = blk[:, 0:2].copy().view(np.float16).astype(np.float64)
+    dmin = blk[:, 2:4].copy().view(np.float16).astype(np.float64)
+    q = blk[:, 4:16].astype(np.int64)
+    y = np.empty((blk.shape[0], 256))
+    for g in range(8):
+        if g < 4:
+            sc, mn = q[:, g] & 63, q[:, g + 4] & 63
+        else:
+            sc = (q[:, g + 4] & 0xF) | ((q[:, g - 4] >> 6) << 4)
+            mn = (q[:, g + 4] >> 4) | ((q[:, g] >> 6) << 4)
+        nib = blk[:, 16 + (g // 2) * 32: 16 + (g // 2) * 32 + 32].astype(np.int64)
+        nib = (nib >> 4) if g & 1 else (nib & 0xF)
+        y[:, g * 32:(g + 1) * 32] = d * sc[:, None] * nib - (dmin[:, 0] * mn)[:, None]
+    return y.reshape(out, in_)
+
+
 @pytest.mark.parametrize("out,in_,B", [(4096, 4096, 1), (1000, 512, 3), (14336, 4096, 4), (96, 2048, 9)])
 def test_gemv_q4k_matches_reference(dev, out, in_, B):
     from yllm_b200 import attn
@@ -51,8 +73,8 @@ def test_gemv_q4k_matches_reference(dev, out, in_, B):
     y = torch.zeros(B, out, device=dev)
     attn.gemv_q4k(y, tw, tx, out, in_, B)
     torch.cuda.synchronize()
-    e = oracle.rel_err(y.cpu().numpy(), want)
-    assert e <= TOL, f"relative error {e:.2e}"
+    exact = x.astype(np.float64) @ q4k_dequant_f64(w, out, in_).T
+    oracle.assert_close(y.cpu().numpy(), want, tol=TOL, what=f"q4k gemv {out}x{in_} B{B}", exact=exact)
 
 
 @pytest.mark.parametrize("out,in_,B", [(4096, 4096, 1), (1000, 1003, 2), (11008, 4096, 4), (64, 4096, 6)])
@@ -69,8 +91,8 @@ def test_gemv_f16_matches_engine_matmul(dev, out, in_, B):
     y = torch.zeros(B, out, device=dev)
     attn.gemv_f16(y, tw, tx, out, in_, B)
     torch.cuda.synchronize()
-    e = oracle.rel_err(y.cpu().numpy(), want)
-    assert e <= TOL, f"relative error {e:.2e}"
+    exact = x.astype(np.float64) @ w.view(np.float16).reshape(out, in_).astype(np.float64).T
+    oracle.assert_close(y.cpu().numpy(), want, tol=TOL, what=f"f16 gemv {out}x{in_} B{B}", exact=exact)
 
 
 def test_gemv_dropins_match(dev):

@@ -3,6 +3,10 @@
 It serves callers that cannot call cudaMalloc while decoding (a fixed device
 memory budget, or an allocator that must not be re-entered from the decode
 thread): its split-KV scratch is a static device array inside the library.
+Each case is checked against the allocating entry point and against the CPU
+oracle (engine.c:1074-1096 restated), on two calls in a row, and the device
+status word must stay 0.  A misaligned gate is rejected on the device (status
+103, read through yattn_device_status) without any access through it.
 This file is collected last so a failure here leaves every other test run.
 """
 import ctypes as C
@@ -26,13 +30,16 @@ def _noalloc(out, q, k, v, gate, pos, H, KV, hd, kd, stream):
 def _case(dev, H, KV, hd, T, seed, gated=False):
     rng = np.random.default_rng(seed)
     kd = KV * hd
-    q = torch.from_numpy(rng.standard_normal(H * hd).astype(np.float32)).to(dev)
+    qn = rng.standard_normal(H * hd).astype(np.float32)
     k = oracle.f32_to_f16(rng.standard_normal(T * kd).astype(np.float32))
     v = oracle.f32_to_f16(rng.standard_normal(T * kd).astype(np.float32))
+    gn = rng.standard_normal(H * hd).astype(np.float32) if gated else None
+    q = torch.from_numpy(qn).to(dev)
     tk = torch.from_numpy(k.view(np.int16)).to(dev).view(torch.uint16)
     tv = torch.from_numpy(v.view(np.int16)).to(dev).view(torch.uint16)
-    gate = torch.from_numpy(rng.standard_normal(H * hd).astype(np.float32)).to(dev) if gated else None
-    return q, tk, tv, gate, kd
+    gate = torch.from_numpy(gn).to(dev) if gated else None
+    want = oracle.attn_decode(qn, k, v, T - 1, H, KV, hd, kd, gate=gn)
+    return q, tk, tv, gate, kd, want
 
 
 @pytest.mark.parametrize("H,KV,hd,T,gated", [
@@ -47,7 +54,8 @@ def test_noalloc_decode_matches_allocating_entry(H, KV, hd, T, gated):
     assert torch.cuda.is_available(), "GPU tests need a CUDA device"
     dev = torch.device("cuda:0")
     torch.cuda.set_device(dev)
-    q, k, v, gate, kd = _case(dev, H, KV, hd, T, seed=H + T, gated=gated)
+    attn.device_status(clear=True)   # start from a clean status word
+    q, k, v, gate, kd, want_cpu = _case(dev, H, KV, hd, T, seed=H + T, gated=gated)
     stream = torch.cuda.current_stream().cuda_stream
     ref = torch.zeros(H * hd, device=dev)
     attn.attn_decode(ref, q, k, v, T - 1, H, KV, hd, kd, gate=gate)
@@ -59,7 +67,10 @@ def test_noalloc_decode_matches_allocating_entry(H, KV, hd, T, gated):
     torch.cuda.synchronize()
     want = ref.cpu().numpy()
     for out in outs:
-        oracle.assert_close(out.cpu().numpy(), want, what=f"noalloc H{H} KV{KV} hd{hd} T{T}")
+        got = out.cpu().numpy()
+        oracle.assert_close(got, want, what=f"noalloc vs yattn_attn_decode H{H} KV{KV} hd{hd} T{T}")
+        oracle.assert_close(got, want_cpu, what=f"noalloc vs CPU oracle H{H} KV{KV} hd{hd} T{T}")
+    assert attn.device_status() == 0
 
 
 def test_noalloc_scratch_covers_every_geometry():
@@ -82,10 +93,47 @@ def test_noalloc_scratch_covers_every_geometry():
 
     dev = torch.device("cuda:0")
     H, KV, hd, T = 64, 8, 256, 40000
-    q, k, v, gate, kd = _case(dev, H, KV, hd, T, seed=5)
+    q, k, v, gate, kd, _ = _case(dev, H, KV, hd, T, seed=5)
     ref = torch.zeros(H * hd, device=dev)
     attn.attn_decode(ref, q, k, v, T - 1, H, KV, hd, kd)
     out = torch.full((H * hd,), float("nan"), device=dev)
     _noalloc(out, q, k, v, None, T - 1, H, KV, hd, kd, torch.cuda.current_stream().cuda_stream)
     torch.cuda.synchronize()
     assert torch.equal(out, ref)
+
+
+def test_noalloc_device_failure_reaches_device_status():
+    """A gate that is not 16-byte aligned is rejected on the device: the
+    decode stops with status 103, which yattn_device_status reports (and
+    clears); the next call with a good gate runs clean."""
+    from yllm_b200 import attn
+
+    dev = torch.device("cuda:0")
+    torch.cuda.set_device(dev)
+    attn.device_status(clear=True)
+    H, KV, hd, T = 16, 2, 256, 700
+    q, k, v, gate, kd, want_cpu = _case(dev, H, KV, hd, T, seed=9, gated=True)
+    stream = torch.cuda.current_stream().cuda_stream
+    bad = torch.zeros(H * hd + 4, device=dev)
+    bad[1:1 + H * hd].copy_(gate)
+    out = torch.zeros(H * hd, device=dev)
+    _noalloc(out, q, k, v, bad[1:], T - 1, H, KV, hd, kd, stream)   # 4 bytes off a 16-byte boundary
+    torch.cuda.synchronize()
+    assert attn.device_status(clear=True) == 103
+    assert attn.device_status() == 0
+    _noalloc(out, q, k, v, gate, T - 1, H, KV, hd, kd, stream)
+    torch.cuda.synchronize()
+    assert attn.device_status() == 0
+    oracle.assert_close(out.cpu().numpy(), want_cpu, what="noalloc after a rejected call")
+
+
+def test_noalloc_rejects_wrapping_position():
+    """pos = 2^32 - 1 would make the key range [0, pos + 1) wrap to empty: a
+    host-side error, as yattn_attn_decode gives."""
+    from yllm_b200._lib import YattnError
+
+    dev = torch.device("cuda:0")
+    q, k, v, gate, kd, _ = _case(dev, 8, 2, 128, 16, seed=3)
+    out = torch.zeros(8 * 128, device=dev)
+    with pytest.raises(YattnError, match="empty key range"):
+        _noalloc(out, q, k, v, None, 0xFFFFFFFF, 8, 2, 128, kd, torch.cuda.current_stream().cuda_stream)

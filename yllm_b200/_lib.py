@@ -109,7 +109,7 @@ PROTOS = {
     "yattn_ipc_handle": (C.c_int, [vp, vp, *E]),
     "yattn_ipc_open": (C.c_int, [vp, C.POINTER(vp), *E]),
     "yattn_ipc_close": (C.c_int, [vp, *E]),
-    "yattn_exchange_merge": (C.c_int, [vp, vp, vp, u32, u32, u32, u32, vp, vp, vp, *E]),
+    "yattn_exchange_merge": (C.c_int, [vp, vp, vp, u32, u32, u32, u32, vp, vp, u64, vp, *E]),
     "yattn_attn_decode": (C.c_int, [vp, vp, vp, vp, vp, u32, u32, u32, u32, u32, vp, *E]),
     "yattn_attn_decode_noalloc": (C.c_int, [vp, vp, vp, vp, vp, u32, u32, u32, u32, u32, vp, *E]),
     "yattn_reserve": (C.c_int, [sz, *E]),

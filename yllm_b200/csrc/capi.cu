@@ -123,17 +123,34 @@ extern "C" const char* yattn_last_error(void) { return g_last_error.c_str(); }
 extern "C" void yattn_clear_error(void) { g_last_error.clear(); }
 
 extern "C" int yattn_device_status(int* status_out, int clear, char* err, size_t errlen) {
-    DevCtx* c = dev_ctx(err, errlen);
-    if (!c) return -1;
-    int v = 0;
-    cudaError_t e = cudaMemcpy(&v, c->status, sizeof(int), cudaMemcpyDeviceToHost);
-    if (e != cudaSuccess) {
-        set_err(err, errlen, "device_status: %s", cudaGetErrorString(e));
-        return -1;
+    // Two words can hold a code: the context's (every allocating entry point) and the
+    // allocation-free decode's, inside its static scratch.  Neither is created here if it
+    // does not exist yet, so a caller that only uses the allocation-free entry point
+    // allocates nothing by polling.
+    int* words[2] = {nullptr, noalloc_status_word()};
+    {
+        int dev = -1;
+        if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) {
+            set_err(err, errlen, "device_status: no usable CUDA device");
+            return -1;
+        }
+        std::lock_guard<std::mutex> lk(g_ctx_mu);
+        if (g_ctx[dev].device == dev) words[0] = g_ctx[dev].status;
     }
-    if (clear && cudaMemset(c->status, 0, sizeof(int)) != cudaSuccess) {
-        set_err(err, errlen, "device_status: clear failed");
-        return -1;
+    int v = 0;
+    for (int* w : words) {
+        if (!w) continue;
+        int x = 0;
+        cudaError_t e = cudaMemcpy(&x, w, sizeof(int), cudaMemcpyDeviceToHost);
+        if (e != cudaSuccess) {
+            set_err(err, errlen, "device_status: %s", cudaGetErrorString(e));
+            return -1;
+        }
+        if (v == 0) v = x;
+        if (clear && x != 0 && cudaMemset(w, 0, sizeof(int)) != cudaSuccess) {
+            set_err(err, errlen, "device_status: clear failed");
+            return -1;
+        }
     }
     if (status_out) *status_out = v;
     return 0;

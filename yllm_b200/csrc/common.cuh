@@ -30,6 +30,8 @@ struct DevCtx {
     size_t gdn_ws_bytes = 0;
 };
 DevCtx* dev_ctx(char* err, size_t errlen);   // current device's context (nullptr on failure)
+// Status word of the allocation-free decode on the current device (nullptr before its first call).
+int* noalloc_status_word();
 int dev_num_sms();
 
 #define YATTN_CHECK_LAUNCH(err, errlen, what)                                            \
@@ -153,6 +155,17 @@ __device__ __forceinline__ bool named_bar_and(int id, int nthreads, bool pred) {
     uint32_t r;
     asm volatile(
         "{\n\t.reg .pred p, q;\n\tsetp.ne.u32 q, %1, 0;\n\tbar.red.and.pred p, %2, %3, q;\n\tselp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(r)
+        : "r"(pred ? 1u : 0u), "r"(id), "r"(nthreads)
+        : "memory");
+    return r != 0;
+}
+
+// Named barrier that ORs a predicate over the participating threads.
+__device__ __forceinline__ bool named_bar_or(int id, int nthreads, bool pred) {
+    uint32_t r;
+    asm volatile(
+        "{\n\t.reg .pred p, q;\n\tsetp.ne.u32 q, %1, 0;\n\tbar.red.or.pred p, %2, %3, q;\n\tselp.u32 %0, 1, 0, p;\n\t}"
         : "=r"(r)
         : "r"(pred ? 1u : 0u), "r"(id), "r"(nthreads)
         : "memory");

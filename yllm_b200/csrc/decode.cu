@@ -1483,6 +1483,11 @@ extern "C" void cuda_k_attn_decode(float* att_out, const float* q, const uint16_
 // The array is shared by every call on a device: calls that overlap on the GPU
 // (different streams, or host threads) race on it and must be serialised by
 // the caller.
+//
+// The status word (the array's first int) is never cleared by a decode call:
+// a bounded wait that gave up, or a malformed item, stays recorded there until
+// yattn_device_status(..., clear = 1) reads and resets it, exactly like the
+// status word of the allocating entry points.
 
 namespace {
 
@@ -1491,8 +1496,11 @@ constexpr size_t kNoAllocHeader = 256;              // status word, then 256-ali
 
 static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
 
-// Device address of g_noalloc_scratch, looked up once per device.  In host
-// code the symbol itself is only a host-side stand-in, never a device address.
+// Device address of g_noalloc_scratch, looked up once per device by the first
+// call on it.  In host code the symbol itself is only a host-side stand-in,
+// never a device address.  The cached address belongs to the device's primary
+// context: after cudaDeviceReset() the module is loaded again and the cache is
+// stale, so a process that resets a device must not call this entry again.
 void* g_noalloc_addr[64];
 std::mutex g_noalloc_mu;
 
@@ -1513,11 +1521,28 @@ void* noalloc_scratch(int dev, char* err, size_t errlen) {
 
 }  // namespace
 
+namespace yattn {
+
+// The no-alloc status word of the current device, or nullptr if no
+// allocation-free call has run on it yet (then nothing can be recorded there).
+int* noalloc_status_word() {
+    int dev = -1;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
+    std::lock_guard<std::mutex> lk(g_noalloc_mu);
+    return static_cast<int*>(g_noalloc_addr[dev]);
+}
+
+}  // namespace yattn
+
 extern "C" int yattn_attn_decode_noalloc(float* att_out, const float* q, const uint16_t* kcache,
                                          const uint16_t* vcache, const float* gate, uint32_t pos, uint32_t n_heads,
                                          uint32_t n_kv_heads, uint32_t head_dim, uint32_t kv_dim, void* stream,
                                          char* err, size_t errlen) {
     if (check_geom(n_heads, n_kv_heads, head_dim, kv_dim, err, errlen)) return -1;
+    if (pos == UINT32_MAX) {   // keys [0, pos + 1) would wrap to an empty range
+        set_err(err, errlen, "decode: empty key range [0, %u)", 0u);
+        return -1;
+    }
     if (!att_out || !q || !kcache || !vcache) {
         set_err(err, errlen, "decode_noalloc: null pointer argument");
         return -1;
@@ -1548,18 +1573,18 @@ extern "C" int yattn_attn_decode_noalloc(float* att_out, const float* q, const u
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     DecodeParams p = single_params(sp, att_out, q, kcache, vcache, gate, 0, pos + 1, n_heads, n_kv_heads, head_dim,
                                    kv_dim);
-    p.status = reinterpret_cast<int*>(base);
-    // The array keeps the previous call's contents: the status word and the merge
-    // counters must start at zero, the partials are fully rewritten before use.
-    size_t clear = sizeof(int);
+    p.status = reinterpret_cast<int*>(base);   // read and reset by yattn_device_status
     if (sp.ns > 1) {
+        // The array keeps the previous call's contents: the merge counters must start at
+        // zero (a call that gave up can leave them raised), the partials are fully
+        // rewritten before use.  The status word is left as it is.
         carve_ws(base + kNoAllocHeader, sp.n_parts, sp.n_groups, gmax, p);
-        clear = kNoAllocHeader + static_cast<size_t>(sp.n_groups) * sizeof(uint32_t);
-    }
-    cudaError_t e = cudaMemsetAsync(base, 0, clear, st);
-    if (e != cudaSuccess) {
-        set_err(err, errlen, "decode_noalloc: clearing the scratch failed: %s", cudaGetErrorString(e));
-        return -1;
+        cudaError_t e = cudaMemsetAsync(base + kNoAllocHeader, 0, static_cast<size_t>(sp.n_groups) * sizeof(uint32_t),
+                                        st);
+        if (e != cudaSuccess) {
+            set_err(err, errlen, "decode_noalloc: clearing the merge counters failed: %s", cudaGetErrorString(e));
+            return -1;
+        }
     }
     return launch_single(p, sp, head_dim, st, err, errlen);
 }

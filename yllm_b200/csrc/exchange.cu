@@ -52,6 +52,7 @@ struct ExParams {
     float* out;
     const float* gate;
     uint32_t world, rank, n_heads, hd;
+    unsigned long long wait_ns;      // bound of the flag wait
     int* status;
 };
 
@@ -102,7 +103,7 @@ __global__ void __launch_bounds__(128) k_exchange_merge(const ExParams p) {
         const unsigned long long t0 = globaltimer_ns();
         for (uint32_t it = 0;; ++it) {
             if (static_cast<int>(ld_acquire_sys(f) - epoch) >= 0) break;
-            if ((it & 255u) == 255u && globaltimer_ns() - t0 > kWaitLimitNs) {
+            if ((it & 255u) == 255u && globaltimer_ns() - t0 > p.wait_ns) {
                 atomicCAS(p.status, 0, ST_EXCHANGE_TIMEOUT);
                 s_ok = 0;
                 break;
@@ -128,10 +129,16 @@ __global__ void __launch_bounds__(128) k_exchange_merge(const ExParams p) {
                 acc += sc * __ldcg(pr + 2 + d);
                 l += sc * lr;
             }
-            float res = acc / l;
+            // every rank's shard empty: no key was attended, the output is 0 (not 0/0)
+            float res = l > 0.f ? acc / l : 0.f;
             if (p.gate) res *= 1.0f / (1.0f + __expf(-p.gate[static_cast<size_t>(hh) * p.hd + d]));
             p.out[static_cast<size_t>(hh) * p.hd + d] = res;
         }
+    } else {
+        // a peer never published: the output is NaN, so a caller that skips the status
+        // poll cannot take a stale result for this call's
+        for (uint32_t d = threadIdx.x; d < p.hd; d += blockDim.x)
+            p.out[static_cast<size_t>(hh) * p.hd + d] = __int_as_float(0x7fc00000);
     }
     // ---- the last CTA of the launch advances the local epoch ----
     __syncthreads();
@@ -216,7 +223,7 @@ extern "C" int yattn_ipc_close(void* ptr, char* err, size_t errlen) {
 
 extern "C" int yattn_exchange_merge(const float* ml, const float* o, void* const* areas, uint32_t world,
                                     uint32_t rank, uint32_t n_heads, uint32_t head_dim, float* out, const float* gate,
-                                    void* stream, char* err, size_t errlen) {
+                                    uint64_t wait_limit_ns, void* stream, char* err, size_t errlen) {
     if (!ml || !o || !areas || !out || world == 0 || world > kMaxWorld || rank >= world || n_heads == 0 ||
         head_dim == 0) {
         set_err(err, errlen, "exchange_merge: bad arguments (world 1..%u, rank < world)", kMaxWorld);
@@ -240,6 +247,7 @@ extern "C" int yattn_exchange_merge(const float* ml, const float* o, void* const
     p.rank = rank;
     p.n_heads = n_heads;
     p.hd = head_dim;
+    p.wait_ns = wait_limit_ns ? wait_limit_ns : kWaitLimitNs;
     p.status = ctx->status;
     k_exchange_merge<<<n_heads, 128, 0, static_cast<cudaStream_t>(stream)>>>(p);
     YATTN_CHECK_LAUNCH(err, errlen, "exchange_merge");

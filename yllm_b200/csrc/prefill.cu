@@ -10,7 +10,12 @@
 // One CTA = one (query head, 128-row query tile), heaviest tiles first.  Warps:
 //   0-7  softmax: row i of the tile (TMEM lane i) belongs to warps i/32 and
 //        i/32 + 4, which split each key block's columns in halves.  They load
-//        the fp32 Q tile once (-> fp16, SWIZZLE_128B K-major in smem).  Per key
+//        the fp32 Q tile once: Q_hi = fp16(q) goes to smem (SWIZZLE_128B
+//        K-major).  If any q of the tile is not exactly an fp16 value (the
+//        engine passes fp32 projections), Q_lo = fp16(q - Q_hi) goes to free
+//        TMEM columns and S gets a second product Q_lo K^T (TS form), so q
+//        keeps about 22 significant bits; the tile then runs with two S
+//        buffers instead of three to make room.  Per key
 //        block each reads its half of S from TMEM, applies the causal mask
 //        (diagonal blocks only), and the two halves of a row combine their
 //        maxima through shared memory; the online softmax runs in the log2
@@ -20,10 +25,11 @@
 //        ~22 bits instead of fp16's 11), 16 columns of each per 32-key chunk.
 //        Each half keeps its own partial row sum; the epilogue adds them.
 //   8    TMA for K blocks, 10 TMA for V blocks: separate rings, no multicast.
-//   9    MMA: one thread issues S(j) = Q K(j)^T (A, B from smem) into a ring of
-//        three TMEM S buffers and O += P_hi V + P_lo V with A = P read straight
-//        from TMEM (B = V from smem).  S runs up to three blocks ahead of the
-//        softmax; the tensor core runs its MMAs in issue order, so S(j+3)
+//   9    MMA: one thread issues S(j) = Q K(j)^T (A, B from smem; + Q_lo K(j)^T
+//        with A from TMEM when the tile needs it) into a ring of NSB (3, or 2
+//        with Q_lo) TMEM S buffers and O += P_hi V + P_lo V with A = P read
+//        straight from TMEM (B = V from smem).  S runs up to NSB blocks ahead of
+//        the softmax; the tensor core runs its MMAs in issue order, so S(j+NSB)
 //        cannot overwrite P(j) before PV(j) has read it.
 // Keys past the end of the cache are zero-filled by TMA and masked.
 #include "common.cuh"
@@ -57,6 +63,16 @@ template <int HD> struct PCfg {
     static constexpr uint32_t COL_S = 0;                     // S buffer b at [b*BN, (b+1)*BN)
     static constexpr uint32_t COL_O = NSB * BN;
     static_assert(NSB * BN + HD <= static_cast<int>(TMEM_COLS), "TMEM columns");
+    // Q_lo (the A operand of the second S product, 16-bit pairs, HD/2 columns):
+    // 16-key chunk kk at qlo_col(kk).  head_dim 64: after O, beside three S buffers.
+    // 128: the third S buffer.  256: the third S buffer, then after O.
+    static constexpr int NSB_QLO = HD == 64 ? 3 : 2;
+    __host__ __device__ static constexpr uint32_t qlo_col(int kk) {
+        return HD == 64 ? COL_O + HD + 8u * kk
+             : HD == 128 ? 2u * BN + 8u * kk
+             : (kk < 8 ? 2u * BN + 8u * kk : COL_O + HD + 8u * (kk - 8));
+    }
+    static_assert(qlo_col(HD / 16 - 1) + 8 <= TMEM_COLS, "Q_lo columns");
     static_assert(SMEM <= 232448, "shared memory");
     static_assert(KST * KV_BYTES >= 8 * 32 * 128, "the epilogue's store boxes fit in the K ring");
 };
@@ -78,6 +94,7 @@ template <int KST, int VST> struct Bars {
     uint64_t o_done, q_full, mma_drain;
     uint32_t tmem_base;
     int abort_flag;
+    int qlo;                          // the tile needs Q_lo (set before q_full completes)
 };
 
 // One TMA producer: block j of a K or V stream into a DEPTH-deep ring.
@@ -157,6 +174,7 @@ __global__ void __launch_bounds__(kPThreads, 1)
         mbar_init(&bars->q_full, 8);
         mbar_init(&bars->mma_drain, 1);
         bars->abort_flag = 0;
+        bars->qlo = 0;
         fence_mbar_init();
     }
     if (warp == 0) tmem_alloc(&bars->tmem_base, C::TMEM_COLS);
@@ -182,13 +200,15 @@ __global__ void __launch_bounds__(kPThreads, 1)
             const uint64_t dv0 = sdesc_sw128(sV, BN * 128, 1024);
             bool ok = mbar_wait_bounded(&bars->q_full, 0, p.status, ST_PREFILL_TIMEOUT, abort_flag);
             tc_fence_after();
-            // S(jj) = Q K(jj)^T into S buffer jj % NSB.  That buffer last held P(jj - NSB), whose PV
+            const bool qlo = ok && bars->qlo != 0;
+            const uint32_t nsb = qlo ? C::NSB_QLO : C::NSB;
+            // S(jj) = Q K(jj)^T into S buffer jj % nsb.  That buffer last held P(jj - nsb), whose PV
             // product was issued earlier; the tensor core runs one thread's MMAs in issue order.
             auto do_s = [&](uint32_t jj) -> bool {
                 const int s = jj % KST;
                 if (!mbar_wait_bounded(&bars->k_full[s], (jj / KST) & 1u, p.status, ST_PREFILL_TIMEOUT, abort_flag))
                     return false;
-                const uint32_t sb = jj % C::NSB;
+                const uint32_t sb = jj % nsb;
                 tc_fence_after();
                 const uint64_t dk = dk0 + ((s * C::KV_BYTES) >> 4);
 #pragma unroll
@@ -196,6 +216,13 @@ __global__ void __launch_bounds__(kPThreads, 1)
                     const uint64_t a = dq0 + (((kk >> 2) * (BM * 128) + (kk & 3) * 32) >> 4);
                     const uint64_t b = dk + (((kk >> 2) * (BN * 128) + (kk & 3) * 32) >> 4);
                     umma_f16(tmem + C::COL_S + sb * BN, a, b, IDESC_QK, kk > 0 ? 1u : 0u);
+                }
+                if (qlo) {   // + Q_lo K^T, A (16-key chunk kk of Q_lo) from TMEM
+#pragma unroll
+                    for (int kk = 0; kk < HD / 16; ++kk) {
+                        const uint64_t b = dk + (((kk >> 2) * (BN * 128) + (kk & 3) * 32) >> 4);
+                        umma_f16_ts(tmem + C::COL_S + sb * BN, tmem + C::qlo_col(kk), b, IDESC_QK, 1u);
+                    }
                 }
                 umma_commit(&bars->s_full[sb]);
                 umma_commit(&bars->k_empty[s]);
@@ -205,8 +232,8 @@ __global__ void __launch_bounds__(kPThreads, 1)
             // are the 8 columns at 32*(kk/2) + 16*plane + 8*(kk%2) of the block's S buffer.
             auto do_pv = [&](uint32_t jj) -> bool {
                 const int s = jj % VST;
-                const uint32_t sb = jj % C::NSB;
-                if (!mbar_wait_bounded(&bars->p_full[sb], (jj / C::NSB) & 1u, p.status, ST_PREFILL_TIMEOUT,
+                const uint32_t sb = jj % nsb;
+                if (!mbar_wait_bounded(&bars->p_full[sb], (jj / nsb) & 1u, p.status, ST_PREFILL_TIMEOUT,
                                        abort_flag) ||
                     !mbar_wait_bounded(&bars->v_full[s], (jj / VST) & 1u, p.status, ST_PREFILL_TIMEOUT, abort_flag))
                     return false;
@@ -226,12 +253,12 @@ __global__ void __launch_bounds__(kPThreads, 1)
                 umma_commit(&bars->pv_done[sb]);
                 return true;
             };
-            // Queue: S(0..NSB-1), then PV(j), S(j+NSB) as each P(j) arrives, so the next S blocks
+            // Queue: S(0..nsb-1), then PV(j), S(j+nsb) as each P(j) arrives, so the next S blocks
             // are ready before the softmax asks for them.
-            for (uint32_t j = 0; ok && j < nkb && j < static_cast<uint32_t>(C::NSB); ++j) ok = do_s(j);
+            for (uint32_t j = 0; ok && j < nkb && j < nsb; ++j) ok = do_s(j);
             for (uint32_t j = 0; ok && j < nkb; ++j) {
                 ok = do_pv(j);
-                if (ok && j + C::NSB < nkb) ok = do_s(j + C::NSB);
+                if (ok && j + nsb < nkb) ok = do_s(j + nsb);
             }
             if (ok) umma_commit(&bars->o_done);
             // drain: every MMA issued so far completes before TMEM is freed
@@ -244,37 +271,75 @@ __global__ void __launch_bounds__(kPThreads, 1)
         const int qd = warp & 3;                                     // TMEM lane quadrant
         const int h = warp >> 2;                                     // half of each key block's columns
         const int r = qd * 32 + lane;                                // row of the tile
-        // ---- Q tile: fp32 -> fp16, swizzled K-major; 256 threads, up to 32 loads in flight each ----
+        const uint32_t trow = tmem + (static_cast<uint32_t>(qd * 32) << 16);
+        // ---- Q tile: fp32 -> Q_hi = fp16(q) (smem, swizzled K-major) and, if any q of the
+        //      tile is not an fp16 value, Q_lo = fp16(q - Q_hi) (TMEM); 256 threads, one batch
+        //      of loads in flight each ----
+        bool qlo;
         {
             constexpr int C4 = HD / 4;
-            constexpr int QITER = BM * C4 / 256, QB = QITER < 32 ? QITER : 32;
-            static_assert(QITER % QB == 0, "Q batches");
-            for (int i0 = 0; i0 < QITER; i0 += QB) {
-                float4 v[QB];
+            constexpr int QITER = BM * C4 / 256;
+            static_assert(QITER <= 32, "Q loads in one batch");
+            float4 v[QITER];
 #pragma unroll
-                for (int i = 0; i < QB; ++i) {
-                    const int idx = threadIdx.x + (i0 + i) * 256;
-                    const uint32_t b = row0 + idx / C4;
-                    v[i] = make_float4(0.f, 0.f, 0.f, 0.f);
-                    if (b < p.B)
-                        v[i] = __ldcs(reinterpret_cast<const float4*>(p.q + static_cast<size_t>(b) * p.q_stride +
-                                                                      static_cast<size_t>(hh) * HD + (idx % C4) * 4));
-                }
+            for (int i = 0; i < QITER; ++i) {
+                const int idx = threadIdx.x + i * 256;
+                const uint32_t b = row0 + idx / C4;
+                v[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+                if (b < p.B)
+                    v[i] = __ldcs(reinterpret_cast<const float4*>(p.q + static_cast<size_t>(b) * p.q_stride +
+                                                                  static_cast<size_t>(hh) * HD + (idx % C4) * 4));
+            }
+            // Q_lo first goes through the Q buffer (this thread's elements), so the thread that
+            // owns a row's TMEM lane can pick it up; Q_hi then overwrites it.
+            bool any_lo = false;
 #pragma unroll
-                for (int i = 0; i < QB; ++i) {
-                    const int idx = threadIdx.x + (i0 + i) * 256;
-                    uint2 pk;
-                    pk.x = h2_bits(__floats2half2_rn(v[i].x, v[i].y));
-                    pk.y = h2_bits(__floats2half2_rn(v[i].z, v[i].w));
-                    *reinterpret_cast<uint2*>(sQ + sw128_offset(idx / C4, (idx % C4) * 4, BM)) = pk;
+            for (int i = 0; i < QITER; ++i) {
+                const int idx = threadIdx.x + i * 256;
+                const __half2 h0 = __floats2half2_rn(v[i].x, v[i].y), h1 = __floats2half2_rn(v[i].z, v[i].w);
+                const float2 f0 = __half22float2(h0), f1 = __half22float2(h1);
+                uint2 lo;
+                lo.x = h2_bits(__floats2half2_rn(v[i].x - f0.x, v[i].y - f0.y));
+                lo.y = h2_bits(__floats2half2_rn(v[i].z - f1.x, v[i].w - f1.y));
+                any_lo = any_lo || ((lo.x | lo.y) & 0x7fff7fffu) != 0u;
+                *reinterpret_cast<uint2*>(sQ + sw128_offset(idx / C4, (idx % C4) * 4, BM)) = lo;
+            }
+            qlo = named_bar_or(5, 256, any_lo);   // the same answer in every softmax thread
+            if (qlo) {
+                // row r, this half's dims [h*HD/2, +HD/2): 32 dims (16 TMEM columns) at a time
+#pragma unroll
+                for (int c = 0; c < HD / 64; ++c) {
+                    const int d0 = h * (HD / 2) + c * 32;
+                    uint32_t w[16];
+#pragma unroll
+                    for (int u = 0; u < 4; ++u) {
+                        const uint4 x = *reinterpret_cast<const uint4*>(sQ + sw128_offset(r, d0 + 8 * u, BM));
+                        w[4 * u] = x.x;
+                        w[4 * u + 1] = x.y;
+                        w[4 * u + 2] = x.z;
+                        w[4 * u + 3] = x.w;
+                    }
+                    tmem_st16(trow + C::qlo_col(d0 / 16), w);
                 }
+                tmem_wait_st();
+                named_bar_sync(5, 256);           // every row's Q_lo is read before Q_hi replaces it
+                if (threadIdx.x == 0) bars->qlo = 1;
+            }
+#pragma unroll
+            for (int i = 0; i < QITER; ++i) {
+                const int idx = threadIdx.x + i * 256;
+                uint2 pk;
+                pk.x = h2_bits(__floats2half2_rn(v[i].x, v[i].y));
+                pk.y = h2_bits(__floats2half2_rn(v[i].z, v[i].w));
+                *reinterpret_cast<uint2*>(sQ + sw128_offset(idx / C4, (idx % C4) * 4, BM)) = pk;
             }
             fence_proxy_async_smem();
+            tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(&bars->q_full);
         }
+        const uint32_t nsb = qlo ? C::NSB_QLO : C::NSB;
 
-        const uint32_t trow = tmem + (static_cast<uint32_t>(qd * 32) << 16);
         const uint32_t qpos = qpos0 + r;
         const float sl2 = p.scale_log2;
         float m_run = -INFINITY, l_run = 0.f;                        // m_run in scaled log2 units; l_run: this half
@@ -283,9 +348,9 @@ __global__ void __launch_bounds__(kPThreads, 1)
         // goes through that barrier (AND-reduced), so both halves always leave together and
         // neither is left at a barrier its partner will not reach.
         for (uint32_t j = 0; j < nkb; ++j) {
-            const uint32_t sb = j % C::NSB;
+            const uint32_t sb = j % nsb;
             const bool got =
-                warp_wait_bounded(&bars->s_full[sb], (j / C::NSB) & 1u, p.status, ST_PREFILL_TIMEOUT, abort_flag);
+                warp_wait_bounded(&bars->s_full[sb], (j / nsb) & 1u, p.status, ST_PREFILL_TIMEOUT, abort_flag);
             const uint32_t scol = trow + C::COL_S + sb * BN + h * HB;  // this half's columns of S(j)
             float sv[HB];
             if (got) {
@@ -357,7 +422,7 @@ __global__ void __launch_bounds__(kPThreads, 1)
             // ---- O rescale (rare), this half's columns of O: PV(j-1) must have finished ----
             // (both halves of these rows see the same `grow`, so both come here)
             if (j >= 1 && __any_sync(0xffffffffu, grow)) {
-                const bool done = warp_wait_bounded(&bars->pv_done[(j - 1) % C::NSB], ((j - 1) / C::NSB) & 1u,
+                const bool done = warp_wait_bounded(&bars->pv_done[(j - 1) % nsb], ((j - 1) / nsb) & 1u,
                                                     p.status, ST_PREFILL_TIMEOUT, abort_flag);
                 if (!named_bar_and(1 + qd, 64, done)) {
                     ok = false;

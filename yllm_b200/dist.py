@@ -217,12 +217,15 @@ class PeerExchange:
         self._areas = (C.c_void_p * self.world)(*self.peers)
         self._lib = lib
 
-    def run(self, out: torch.Tensor, gate: Optional[torch.Tensor] = None) -> None:
+    def run(self, out: torch.Tensor, gate: Optional[torch.Tensor] = None, wait_limit_ns: int = 0) -> None:
+        """wait_limit_ns bounds the wait for the peers' parts (0: the library's 2 s).  On
+        timeout out is NaN and yattn_device_status reads 401; the areas' epochs are then
+        out of step, so the exchange must be rebuilt before the next call."""
         from ._lib import call
 
         call("yattn_exchange_merge", self.payload.data_ptr(), self.payload.data_ptr() + self.n_heads * 2 * 4,
              self._areas, self.world, self.rank, self.n_heads, self.head_dim, out.data_ptr(),
-             gate.data_ptr() if gate is not None else None, torch.cuda.current_stream().cuda_stream)
+             gate.data_ptr() if gate is not None else None, wait_limit_ns, torch.cuda.current_stream().cuda_stream)
 
     def close(self) -> None:
         """Collective: every rank's pushes are done before any area is unmapped or freed."""
