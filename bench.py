@@ -4,8 +4,10 @@ Default workload: BASELINE config 3 -- batched ragged GQA decode, Llama-3-8B
 attention shape (32 q / 8 kv heads, head_dim 128, 32 layers), 64 sequences
 with seeded context lengths in [1024, 8192], fp16 KV cache.  One step = one
 decode step of attention: 32 per-layer launches over all sequences, as the
-engine calls it layer by layer.  Sharded by sequence over N GPUs (no
-collective in the data path); value = total tokens/s of the whole job.
+engine calls it layer by layer.  At N GPUs the 64 sequences are sharded by
+sequence (strong scaling, no collective in the data path); value = the job's
+tokens/s.  The same line carries config 4 (131072-key decode, split-KV over
+the N GPUs with the partial exchange) as its long_decode sub-object.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
     torchrun --nproc-per-node N bench.py --gpus N ...
@@ -166,13 +168,20 @@ class ClockSampler:
 # --------------------------------------------------------------- CPU side
 
 class CpuReference:
-    """The reference's CPU attention for the workload: oracle/_ref (the
+    """The reference's CPU attention for config 3: oracle/_ref (the
     reference's matvec.c/platform.c under the restated engine.c:1074-1096
-    loop, OpenMP over query heads), or the port if _ref is absent.  The
-    sample is one layer of every sequence (same seeded bytes as the GPU
-    arm); a full step is that layer's time x the number of layers."""
+    loop, OpenMP over query heads, every host core), or the port if _ref is
+    absent.
 
-    def __init__(self, cfg, seqs: list, layer: int = 0):
+    A step is a bounded sample of the workload, timed whole: n_sample of the
+    64 sequences -- every (64/n_sample)-th by context length, so their mean
+    context is the config's -- through all 32 layers, one engine attention
+    call per (layer, sequence).  The K/V/q of fix_layers distinct layers are
+    generated (the same seeded bytes as the GPU arm) and cycled over the 32
+    layers: each layer's sample is ~150 MB, and consecutive calls alternate
+    between layers, so the working set (~600 MB) stays far beyond any L3."""
+
+    def __init__(self, cfg, n_sample: int = 8, fix_layers: int = 4):
         sys.path.insert(0, str(ROOT / "tests"))
         import oracle
 
@@ -182,27 +191,54 @@ class CpuReference:
         # every host core (torchrun exports OMP_NUM_THREADS=1 to its ranks)
         self.lib.orc_set_threads(len(os.sched_getaffinity(0)))
         self.cores = int(self.lib.orc_max_threads())
-        self.cfg, self.seqs = cfg, seqs
-        self.fx = [oracle.decode_fixture(cfg, layer, s, lib=self.lib) for s in seqs]
+        self.cfg = cfg
+        ctx = cfg.ctx()
+        order = sorted(range(cfg.n_seqs), key=lambda s: (ctx[s], s))
+        stride = cfg.n_seqs // n_sample
+        self.seqs = [order[i * stride + stride // 2] for i in range(n_sample)]
+        self.keys = sum(ctx[s] for s in self.seqs)
+        self.fx = [[oracle.decode_fixture(cfg, layer, s, lib=self.lib) for s in self.seqs]
+                   for layer in range(fix_layers)]
 
-    def time_layer(self) -> float:
+    def time_step(self) -> float:
+        """Seconds for one sample step: every layer of every sampled sequence."""
         c = self.cfg
         t0 = time.perf_counter()
-        for f in self.fx:
-            self.oracle.attn_decode(f["q"], f["k"], f["v"], f["pos"], c.n_heads, c.n_kv_heads, c.head_dim,
-                                    c.kv_dim, lib=self.lib)
+        for layer in range(c.layers):
+            for f in self.fx[layer % len(self.fx)]:
+                self.oracle.attn_decode(f["q"], f["k"], f["v"], f["pos"], c.n_heads, c.n_kv_heads, c.head_dim,
+                                        c.kv_dim, lib=self.lib)
         return time.perf_counter() - t0
+
+    def describe(self, n_steps: int, seconds: float) -> str:
+        c = self.cfg
+        return (f"{len(self.seqs)} of the {c.n_seqs} sequences (every {c.n_seqs // len(self.seqs)}th by context "
+                f"length: {self.keys} keys per layer, mean {self.keys / len(self.seqs):.0f} against the config's "
+                f"{sum(c.ctx()) / c.n_seqs:.0f}) x all {c.layers} layers per step; {n_steps} steps timed "
+                f"({seconds:.1f} s)")
 
     def rate(self, budget_s: float) -> dict:
         times = []
         while not times or (sum(times) < budget_s and len(times) < 8):
-            times.append(self.time_layer())
-        step_s = statistics.median(times) * self.cfg.layers
+            times.append(self.time_step())
+        step_s = statistics.median(times)
         return {"value": round(len(self.seqs) / step_s, 4), "unit": "tok/s", "cores": self.cores,
-                "kind": self.kind,
-                "sample": f"layer 0 of {len(self.seqs)} seqs ({sum(self.fx[i]['pos'] + 1 for i in range(len(self.fx)))}"
-                          f" keys), timed {len(times)}x ({sum(times):.1f} s), x{self.cfg.layers} layers per step",
-                "step_s": step_s}
+                "kind": self.kind, "sample": self.describe(len(times), sum(times))}
+
+
+def config3_dict(cfg, world: int, n_layers: int, n_seqs: int, profile: bool = False) -> dict:
+    """The config of the config-3 line: the same keys and values for the GPU arm and for the reference arm
+    launched at the same N."""
+    keys = sum(cfg.ctx_of(s) for s in range(n_seqs))
+    return {
+        "workload": cfg.name + ("" if not profile else f"-profile-{n_seqs}seq-{n_layers}layer"),
+        "n_heads": cfg.n_heads, "n_kv_heads": cfg.n_kv_heads, "head_dim": cfg.head_dim,
+        "layers": n_layers, "n_seqs": n_seqs, "ctx_range": [cfg.ctx_lo, cfg.ctx_hi],
+        "total_keys_per_layer": keys, "kv_bytes_per_step": keys * cfg.kv_dim * 2 * 2 * n_layers,
+        "parallelism": (f"the {n_seqs} sequences sharded by sequence over {world} GPU(s), longest-first by "
+                        "context length; no collective"),
+        "l2": "inputs larger than L2 (KV per GPU >> 126 MB)",
+    }
 
 
 # --------------------------------------------------------------- GPU side
@@ -220,15 +256,14 @@ def run_ours(args) -> None:
     # --seqs / --layers shrink the workload for profiler captures only; the
     # default (and every reported number) is the full config.
     n_layers = args.layers or cfg.layers
-    # Weak scaling: sequences are independent units, so at N GPUs the job is N
-    # batches of the config's size (sequence ids 0..N*n-1), dealt to the ranks
-    # longest-first by context length; no data-path collective.
+    # Strong scaling (the config as stated): the config's 64 sequences are dealt to the ranks
+    # longest-first by context length, so each GPU holds about 1/N of the keys; no data-path
+    # collective.  --weak instead gives every rank a whole batch of the config's size.
     n_per_rank = args.seqs or cfg.n_seqs
-    n_total = n_per_rank * world
+    n_total = n_per_rank * world if args.weak else n_per_rank
     ctx_all = [cfg.ctx_of(s) for s in range(n_total)]
-    seqs = ydist.shard_by_length(ctx_all, world)[rank]   # longest-first greedy balance of keys
-    keys_all = sum(ctx_all)
-    log(f"[rank {rank}] {len(seqs)} seqs, {sum(cfg.ctx_of(s) for s in seqs)} keys/layer, {n_layers} layers")
+    seqs = ydist.shard_by_length(ctx_all, world)[rank]
+    log(f"[rank {rank}] {len(seqs)} seqs, {sum(ctx_all[s] for s in seqs)} keys/layer, {n_layers} layers")
 
     d = fixtures.decode_inputs(cfg, layers=list(range(n_layers)), seqs=seqs, device=dev)
     torch.cuda.synchronize()
@@ -275,10 +310,10 @@ def run_ours(args) -> None:
     barrier()
     elapsed_ms = t0.elapsed_time(t1)
     launch_ms = sum(a.elapsed_time(b) for a, b in ev) / len(ev)
-    t = torch.tensor([elapsed_ms], device=dev)
+    t = torch.tensor([elapsed_ms, launch_ms], device=dev)
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    elapsed_ms = float(t.item())
+    elapsed_ms = float(t[0].item())
     ms_per_step = elapsed_ms / args.steps
     value = n_total / (ms_per_step / 1e3)
 
@@ -310,20 +345,31 @@ def run_ours(args) -> None:
         if world > 1:
             dist.all_reduce(te, op=dist.ReduceOp.MAX)
         e2e_value = n_total / (float(te.item()) / args.steps / 1e3)
+    h2d = torch.tensor([n_q * 4], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(h2d)   # every rank's q bytes (the out bytes are the same)
+    io_bytes = int(h2d.item())
 
-    # ---- roofline of the decode kernel (per launch = one layer of this rank's seqs) ----
+    # ---- roofline of the decode kernel (per launch = one layer of this rank's seqs; slowest rank) ----
     bytes_per_launch = sum(d.ctx) * cfg.kv_dim * 2 * 2 + len(seqs) * cfg.n_heads * cfg.head_dim * 4 * 2
-    achieved = bytes_per_launch / (launch_ms / 1e3) / 1e9
+    bt = torch.tensor([bytes_per_launch / (launch_ms / 1e3)], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(bt, op=dist.ReduceOp.MIN)
+    achieved = float(bt.item()) / 1e9
     peaks, peak_src = load_peaks()
     st = attn.device_status()
     if st != 0:
         raise RuntimeError(f"device status {st}: a kernel gave up waiting")
+    del d, plan, items
+    torch.cuda.empty_cache()
+
+    # ---- config 4 in the same run: the one cross-GPU exchange (split-KV over the ranks) ----
+    long = None if args.no_long else _long_decode(args, rank, world, local, dist, sub=True)
 
     if rank == 0:
         cpu = None
         if not args.no_cpu_baseline and world == 1 and not (args.seqs or args.layers):
-            cpu = CpuReference(cfg, list(range(cfg.n_seqs))).rate(args.cpu_budget)
-            cpu.pop("step_s", None)
+            cpu = CpuReference(cfg).rate(args.cpu_budget)
         line = {
             "metric": "attn decode tok/s (batched ragged GQA decode, all layers)",
             "value": round(value, 2),
@@ -333,35 +379,29 @@ def run_ours(args) -> None:
             "warmup": args.warmup,
             "ms_per_step": round(ms_per_step, 4),
             "higher_is_better": True,
-            "scaling": "weak",
+            "scaling": "weak" if args.weak else "strong",
             "vs_baseline": None,
             "dtype": "f32 math, fp16 KV",
             "data": "synthetic (seeded splitmix64 + Box-Muller, N(0,1) fp16 KV cache)",
-            "config": {
-                "workload": cfg.name + ("" if not (args.seqs or args.layers)
-                                        else f"-profile-{n_per_rank}seq-{n_layers}layer"),
-                "n_heads": cfg.n_heads, "n_kv_heads": cfg.n_kv_heads, "head_dim": cfg.head_dim,
-                "layers": n_layers, "n_seqs": n_total, "seqs_per_gpu": n_per_rank,
-                "ctx_range": [cfg.ctx_lo, cfg.ctx_hi],
-                "total_keys_per_layer": keys_all,
-                "kv_bytes_per_step": keys_all * cfg.kv_dim * 2 * 2 * n_layers,
-                "parallelism": (f"sequence-sharded x{world}: {n_total} sequences dealt longest-first by context "
-                                "length, no collective"),
-                "l2": "inputs larger than L2 (KV per GPU >> 126 MB)",
-            },
+            "config": config3_dict(cfg, world, n_layers, n_total, profile=bool(args.seqs or args.layers)),
             "e2e": None if e2e_value is None else {
                 "value": round(e2e_value, 2), "unit": "tok/s",
-                "h2d_bytes_per_step": int(n_q * 4 * world), "d2h_bytes_per_step": int(n_q * 4 * world)},
+                "h2d_bytes_per_step": io_bytes, "d2h_bytes_per_step": io_bytes},
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"],
                          "unit": "GB/s", "frac": round(achieved / peaks["hbm_gbs"], 4),
-                         "traffic": None if (args.seqs or args.layers) else NCU_TRAFFIC["decode"],
+                         "traffic": None if (args.seqs or args.layers or world > 1) else NCU_TRAFFIC["decode"],
                          "kernel": "k_decode<128,4,TM> (pooled tensor copies)",
                          "peak_source": peak_src,
-                         "bytes_per_launch": bytes_per_launch, "launch_ms": round(launch_ms, 5)},
+                         "bytes_per_launch": bytes_per_launch, "launch_ms": round(launch_ms, 5),
+                         "note": "per GPU: the slowest rank's bytes per launch / its mean launch time"},
             "gpu_launches": args.steps * n_layers,
             "clocks": {"sm_mhz": clk["sm_mhz"], "sm_max_mhz": clk["sm_max_mhz"], "reasons": clk["reasons"],
                        "samples": clk["samples"], "source": clk.get("source")},
         }
+        if world > 1:
+            line["config"]["seqs_per_gpu"] = [len(x) for x in ydist.shard_by_length(ctx_all, world)]
+        if long is not None:
+            line["long_decode"] = long
         if cpu is not None:
             line["cpu_baseline"] = cpu
         print(json.dumps(line), flush=True)
@@ -454,33 +494,33 @@ def run_decode_small(args) -> None:
 
 
 def run_reference(args) -> None:
-    """The reference's own CPU attention for the same workload (rank 0 only)."""
+    """The reference's own CPU attention for the config-3 workload (rank 0 only;
+    the other ranks exit without work).  Each step is a bounded sample of the
+    workload (CpuReference), timed whole: value = the sample's tokens / the
+    median step time, so ms_per_step x steps is the time actually spent."""
     rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", str(args.gpus)))
     if rank != 0:
         return
     from yllm_b200.configs import CFG3 as cfg
 
-    ref = CpuReference(cfg, list(range(cfg.n_seqs)))
-    per_step = []
-    t_start = time.perf_counter()
+    ref = CpuReference(cfg)
+    times = []
     for i in range(args.warmup + args.steps):
-        t = ref.time_layer()
+        t = ref.time_step()
         if i >= args.warmup:
-            per_step.append(t * cfg.layers)
-        if time.perf_counter() - t_start > args.cpu_budget * 6 and len(per_step) >= 1:
-            break   # keep the whole run within a few minutes
-    step_s = statistics.median(per_step)
-    value = cfg.n_seqs / step_s
-    res = {"cores": ref.cores, "kind": ref.kind,
-           "sample": f"layer 0 of all {cfg.n_seqs} seqs per step (x{cfg.layers} layers), "
-                     f"{len(per_step)} timed steps"}
+            times.append(t)
+    step_s = statistics.median(times)
+    value = len(ref.seqs) / step_s
+    sample = ref.describe(len(times), sum(times))
     line = {
         "impl": "reference",
         "metric": "attn decode tok/s (batched ragged GQA decode, all layers)",
         "value": round(value, 4),
         "unit": "tok/s",
-        "n_gpus": args.gpus,
-        "runs_on": "host cores of rank 0 (the reference's CPU attention); no GPU work",
+        "n_gpus": world,
+        "runs_on": (f"host cores of rank 0 ({ref.cores} threads; OpenMP over query heads, as the engine); no GPU "
+                    "work"),
         "steps": args.steps,
         "warmup": args.warmup,
         "ms_per_step": round(step_s * 1e3, 2),
@@ -489,11 +529,9 @@ def run_reference(args) -> None:
         "vs_baseline": None,
         "dtype": "f32 math, fp16 KV",
         "data": "synthetic (seeded splitmix64 + Box-Muller, N(0,1) fp16 KV cache)",
-        "config": {"workload": cfg.name, "n_heads": cfg.n_heads, "n_kv_heads": cfg.n_kv_heads,
-                   "head_dim": cfg.head_dim, "layers": cfg.layers, "n_seqs": cfg.n_seqs,
-                   "ctx_range": [cfg.ctx_lo, cfg.ctx_hi], "parallelism": "host cores (OpenMP over q heads)"},
-        "cpu_baseline": {"value": round(value, 4), "unit": "tok/s", "cores": res["cores"], "kind": res["kind"],
-                         "sample": res["sample"]},
+        "config": config3_dict(cfg, world, cfg.layers, cfg.n_seqs),
+        "cpu_baseline": {"value": round(value, 4), "unit": "tok/s", "cores": ref.cores, "kind": ref.kind,
+                         "sample": sample},
         "e2e": {"value": round(value, 4), "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -736,17 +774,17 @@ def run_gdn(args, decode: bool) -> None:
         dist.destroy_process_group()
 
 
-def run_long_decode(args) -> None:
-    """Config 4: one 131072-key decode, key range split over the ranks, per-rank
-    (m, l, o) partials all-gathered over NCCL and merged on every GPU."""
+def _long_decode(args, rank, world, local, dist, sub=False):
+    """Config 4: one 131072-key decode, the key range split over the ranks.
+    Each rank reduces its range to (m, l, o) partials; at N > 1 the partials are
+    exchanged over NVLink (k_exchange_merge: pushed into every rank's area,
+    merged on every GPU) or by an NCCL all-gather.  Returns the line's fields
+    (rank 0) -- a sub-object of the config-3 line when sub is True."""
     import torch
-    import torch.distributed as dist
 
     from yllm_b200 import attn, dist as ydist, fixtures
     from yllm_b200.configs import CFG4 as c
 
-    rank, world, local = ydist.init("nccl" if args.gpus > 1 else "gloo")
-    torch.cuda.set_device(local)
     stream = torch.cuda.current_stream()
     d = fixtures.decode_inputs(c)
     n = d.ctx[0]
@@ -757,15 +795,23 @@ def run_long_decode(args) -> None:
     out = d.out[0, 0]
     kv, vv = d.k_view(0, 0), d.v_view(0, 0)
 
+    def partial():
+        attn.decode_partial(ex.ml, ex.o, d.q[0, 0], kv, vv, k0, k1, H, c.n_kv_heads, hd, c.kv_dim)
+
     def step():
         # launches on the current stream, so the step (NCCL included) can be graph-captured
         if world == 1:
             attn.attn_decode(out, d.q[0, 0], kv, vv, n - 1, H, c.n_kv_heads, hd, c.kv_dim)
         else:
-            attn.decode_partial(ex.ml, ex.o, d.q[0, 0], kv, vv, k0, k1, H, c.n_kv_heads, hd, c.kv_dim)
+            partial()
             ex.run(out)
 
     ms, per_call, clk = _timed(step, args, stream, world, dist, local, graph=True)
+    # the split: the partial decode alone (graph-replayed), slowest rank
+    split = None
+    if world > 1:
+        ms_p, _, _ = _timed(partial, args, stream, world, dist, local, graph=True)
+        split = {"partial_decode_ms": round(ms_p, 5), "exchange_and_merge_ms": round(ms - ms_p, 5)}
     e2e = None
     if not args.no_e2e:
         qh = torch.empty(H * hd, dtype=torch.float32, pin_memory=True)
@@ -782,25 +828,54 @@ def run_long_decode(args) -> None:
                "h2d_bytes_per_step": H * hd * 4 * world, "d2h_bytes_per_step": H * hd * 4 * world,
                "path": "API calls per step (no graph), pinned host q in, out back"}
     torch.cuda.synchronize()
+    st = attn.device_status()
+    if st != 0:
+        raise RuntimeError(f"device status {st}: a kernel gave up waiting")
     nbytes = n * c.kv_dim * 2 * 2
     peaks, src = load_peaks()
     ach = nbytes / (ms / 1e3) / 1e9
     roof = {"bound": "hbm", "achieved": round(ach, 1), "peak": peaks["hbm_gbs"] * world, "unit": "GB/s",
-            "frac": round(ach / (peaks["hbm_gbs"] * world), 4), "traffic": NCU_TRAFFIC["long_decode"] if world == 1 else None,
+            "frac": round(ach / (peaks["hbm_gbs"] * world), 4),
+            "traffic": NCU_TRAFFIC["long_decode"] if world == 1 else None,
             "kernel": "k_decode<128,4,TM>" + ((" + k_exchange_merge" if peer else " + NCCL all-gather + merge")
                                               if world > 1 else ""), "peak_source": src + f" x{world} GPUs"}
-    if rank == 0:
-        print(json.dumps(_line(args, world, "long-context decode GB/s (131072 keys, one layer)", ach, "GB/s", ms,
-                               {"workload": c.name, "ctx": n, "n_heads": H, "n_kv_heads": c.n_kv_heads,
-                                "head_dim": hd, "kv_bytes": nbytes,
-                                "parallelism": (f"split-KV x{world}, " + (
-                                    "(m,l,o) pushed into every GPU over NVLink + LSE merge, one kernel"
-                                    if peer else "NCCL all-gather of (m,l,o) + LSE merge")),
-                                "launch": "CUDA graph replay of the step (partial decode, exchange, merge)",
-                                "l2": "KV 537 MB > L2"},
-                               roof, args.steps * (2 if world > 1 else 1), clk, e2e)), flush=True)
+    cfg_d = {"workload": c.name, "ctx": n, "n_heads": H, "n_kv_heads": c.n_kv_heads, "head_dim": hd,
+             "kv_bytes": nbytes,
+             "parallelism": (f"split-KV x{world}, " + (
+                 "(m,l,o) pushed into every GPU over NVLink + LSE merge, one kernel"
+                 if peer else "NCCL all-gather of (m,l,o) + LSE merge")) if world > 1 else "one GPU",
+             "launch": "CUDA graph replay of the step (partial decode, exchange, merge)",
+             "l2": "KV 537 MB > L2"}
     if peer:
         ex.close()
+    del d
+    torch.cuda.empty_cache()
+    if rank != 0:
+        return None
+    if sub:
+        return {"metric": "long-context decode GB/s (131072 keys, one layer)", "value": round(ach, 1),
+                "unit": "GB/s", "ms_per_step": round(ms, 5), "scaling": "strong", "config": cfg_d,
+                "roofline": roof, "split": split, "e2e": e2e,
+                "clocks": {"sm_mhz": clk["sm_mhz"], "reasons": clk["reasons"], "samples": clk["samples"]}}
+    line = _line(args, world, "long-context decode GB/s (131072 keys, one layer)", ach, "GB/s", ms, cfg_d, roof,
+                 args.steps * (2 if world > 1 else 1), clk, e2e)
+    if split:
+        line["split"] = split
+    return line
+
+
+def run_long_decode(args) -> None:
+    """Config 4 on its own line (see _long_decode)."""
+    import torch
+    import torch.distributed as dist
+
+    from yllm_b200 import dist as ydist
+
+    rank, world, local = ydist.init("nccl" if args.gpus > 1 else "gloo")
+    torch.cuda.set_device(local)
+    line = _long_decode(args, rank, world, local, dist)
+    if rank == 0:
+        print(json.dumps(line), flush=True)
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
@@ -1220,6 +1295,9 @@ def main() -> None:
     ap.add_argument("--seqs", type=int, default=0, help="profiling only: first N sequences")
     ap.add_argument("--layers", type=int, default=0, help="profiling only: first L layers")
     ap.add_argument("--cpu-budget", type=float, default=20.0, help="seconds of CPU attention in the baseline")
+    ap.add_argument("--weak", action="store_true",
+                    help="decode at N>1: every rank serves a whole 64-sequence batch (default: the 64 sharded)")
+    ap.add_argument("--no-long", action="store_true", help="decode: skip the config-4 long_decode sub-object")
     ap.add_argument("--exchange", choices=["peer", "nccl"], default="peer",
                     help="long_decode at N>1: split-KV exchange over peer memory (one kernel) or NCCL all-gather")
     args = ap.parse_args()

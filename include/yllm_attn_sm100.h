@@ -103,6 +103,18 @@ typedef struct YattnRopeItem {
     uint32_t reserved;
 } YattnRopeItem;
 
+/* Optional QK-norm ahead of the rotation (qwen3: engine.c:1036-1045; qwen35:
+ * engine.c:915-919): every q head and every k head becomes rmsnorm(x, w)
+ * (matvec.c:152-165: y = x * w / sqrt(mean(x^2) + eps)) with the layer's
+ * shared head_dim weights q_w / k_w (device pointers; fp32, or fp16 bits when
+ * w_f16 != 0).  Passed by host pointer; NULL = no norm.  head_dim <= 256. */
+typedef struct YattnQkNorm {
+    const void* q_w;
+    const void* k_w;
+    int w_f16;
+    float eps;
+} YattnQkNorm;
+
 /* RoPE of q and k at each item's position, then k (rotated) and v into the
  * cache at that position with the engine's f32_to_f16 rounding, for all
  * n_items (device array) in one launch.  Replaces, per sequence, the
@@ -113,10 +125,12 @@ typedef struct YattnRopeItem {
  * 2 = rope_inplace_mrope (first n_rope_dims dims, pairs j, j + n_rope_dims/2;
  * matvec.c:924-939).  n_rope_dims is ignored for kinds 0 and 1.  The inverse
  * frequencies are the reference's powf values (computed on the host); the
- * device's sinf/cosf can move a stored fp16 value by one ulp. */
+ * device's sinf/cosf can move a stored fp16 value by one ulp.  With qk_norm,
+ * q and k are first normalised per head (YattnQkNorm above; one CTA per head). */
 int yattn_rope_store_kv(const YattnRopeItem* items_dev, uint32_t n_items, uint32_t n_heads,
                         uint32_t n_kv_heads, uint32_t head_dim, uint32_t kv_dim, int rope_kind,
-                        uint32_t n_rope_dims, float theta, void* stream, char* err, size_t errlen);
+                        uint32_t n_rope_dims, float theta, const YattnQkNorm* qk_norm, void* stream,
+                        char* err, size_t errlen);
 
 /* The same for B consecutive tokens of one sequence (a prefill chunk): row b
  * of q (at q + b*q_stride), k and v (at + b*kv_dim) is rotated at position
@@ -126,8 +140,8 @@ int yattn_rope_store_kv(const YattnRopeItem* items_dev, uint32_t n_items, uint32
 int yattn_rope_store_kv_batch(float* q, const float* k, const float* v, uint16_t* kcache,
                               uint16_t* vcache, uint32_t pos_start, uint32_t B, uint32_t q_stride,
                               uint32_t n_heads, uint32_t n_kv_heads, uint32_t head_dim, uint32_t kv_dim,
-                              int rope_kind, uint32_t n_rope_dims, float theta, void* stream, char* err,
-                              size_t errlen);
+                              int rope_kind, uint32_t n_rope_dims, float theta,
+                              const YattnQkNorm* qk_norm, void* stream, char* err, size_t errlen);
 
 /* ---------------------------------------------- batched / split-KV decode */
 

@@ -43,6 +43,7 @@ void     gdn_state_update(float* S, float* out, const float* q, const float* k,
                           uint32_t num_k_heads, uint32_t hk, uint32_t n_vheads, uint32_t hv);
 void     rmsnorm_gated(float* y, const float* x, const uint8_t* w, const float* z,
                        uint32_t n, float eps, uint32_t dtype);
+void     rmsnorm(float* y, const float* x, const uint8_t* w, uint32_t n, float eps, uint32_t dtype);
 void     conv1d_update(float* state, const float* x, const uint8_t* w, uint32_t dim, uint32_t kwidth);
 void     q4k_block(float* y, const uint8_t* blk, uint32_t stride);
 void     matmul(float* y, const float* x, const uint8_t* w, uint32_t out, uint32_t in, uint32_t dtype);
@@ -66,6 +67,8 @@ void orc_gdn_state_update(float* S, float* out, const float* q, const float* k,
 { gdn_state_update(S, out, q, k, v, gate, beta, num_k_heads, hk, n_vheads, hv); }
 void orc_rmsnorm_gated_f32(float* y, const float* x, const float* w, const float* z, uint32_t n, float eps)
 { rmsnorm_gated(y, x, (const uint8_t*)w, z, n, eps, REF_DT_F32); }
+void orc_rmsnorm(float* y, const float* x, const void* w, uint32_t n, float eps, int w_f16)
+{ rmsnorm(y, x, (const uint8_t*)w, n, eps, w_f16 ? REF_DT_F16 : REF_DT_F32); }
 void orc_conv1d_update(float* state, float* x, const float* w, uint32_t dim, uint32_t kwidth)
 { conv1d_update(state, x, (const uint8_t*)w, dim, kwidth); }
 void orc_q4k_block(float* y, const uint8_t* blk) { q4k_block(y, blk, 0); }
@@ -259,6 +262,23 @@ void orc_rmsnorm_gated_f32(float* y, const float* x, const float* w, const float
     for (i = 0; i < n; i++) {
         float zg = z[i];
         y[i] = x[i] * w[i] * inv * (zg / (1.0f + expf(-zg)));
+    }
+}
+
+/* matvec.c:152-165: y = x * w / sqrt(mean(x^2) + eps), the sum of squares in
+ * index order; w is fp32, or fp16 bits (w_f16) widened with f16_to_f32. */
+void orc_rmsnorm(float* y, const float* x, const void* w, uint32_t n, float eps, int w_f16)
+{
+    float s = 0.0f;
+    uint32_t i;
+    for (i = 0; i < n; i++) s += x[i] * x[i];
+    float inv = 1.0f / sqrtf(s / (float)n + eps);
+    if (!w_f16) {
+        const float* wp = (const float*)w;
+        for (i = 0; i < n; i++) y[i] = x[i] * wp[i] * inv;
+    } else {
+        const uint16_t* wp = (const uint16_t*)w;
+        for (i = 0; i < n; i++) y[i] = x[i] * orc_f16_to_f32(wp[i]) * inv;
     }
 }
 
@@ -504,6 +524,20 @@ void orc_rope_store(float* q, float* k, const float* v, uint16_t* kcache, uint16
         kcache[(size_t)pos * kv_dim + j] = orc_f32_to_f16(k[j]);
         vcache[(size_t)pos * kv_dim + j] = orc_f32_to_f16(v[j]);
     }
+}
+
+/* QK-norm before the rotation: engine.c:915-919 (qwen35, then M-RoPE 922-925)
+ * and 1036-1045 (qwen3): rmsnorm of every q head and every k head with the
+ * layer's shared head_dim weights, then orc_rope_store. */
+void orc_qknorm_rope_store(float* q, float* k, const float* v, uint16_t* kcache, uint16_t* vcache,
+                           uint32_t n_heads, uint32_t n_kv, uint32_t hd, uint32_t kv_dim, int kind,
+                           uint32_t n_dims, uint32_t pos, float theta, const void* q_w, const void* k_w,
+                           int w_f16, float eps)
+{
+    uint32_t hh;
+    for (hh = 0; hh < n_heads; hh++) orc_rmsnorm(q + (size_t)hh * hd, q + (size_t)hh * hd, q_w, hd, eps, w_f16);
+    for (hh = 0; hh < n_kv; hh++) orc_rmsnorm(k + (size_t)hh * hd, k + (size_t)hh * hd, k_w, hd, eps, w_f16);
+    orc_rope_store(q, k, v, kcache, vcache, n_heads, n_kv, hd, kv_dim, kind, n_dims, pos, theta);
 }
 
 /* ---------------- attention loops (engine.c, operation order kept) ---------------- */

@@ -62,6 +62,13 @@ void     orc_gemv_f16(float* y, const uint16_t* w, const float* x, uint32_t out,
 void     orc_rope_store(float* q, float* k, const float* v, uint16_t* kcache, uint16_t* vcache,
                         uint32_t n_heads, uint32_t n_kv, uint32_t hd, uint32_t kv_dim, int kind,
                         uint32_t n_dims, uint32_t pos, float theta);
+/* matvec.c:152-165 (rmsnorm; fp32 weights, or fp16 bits when w_f16) */
+void     orc_rmsnorm(float* y, const float* x, const void* w, uint32_t n, float eps, int w_f16);
+/* engine.c:915-934 / 1036-1072: QK-norm of every q and k head, then orc_rope_store */
+void     orc_qknorm_rope_store(float* q, float* k, const float* v, uint16_t* kcache, uint16_t* vcache,
+                               uint32_t n_heads, uint32_t n_kv, uint32_t hd, uint32_t kv_dim, int kind,
+                               uint32_t n_dims, uint32_t pos, float theta, const void* q_w, const void* k_w,
+                               int w_f16, float eps);
 void     orc_f16_to_f32_buf(const uint16_t* src, float* dst, size_t n);
 
 /* ---- attention loops (engine.c, restated in operation order) ---- */

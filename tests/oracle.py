@@ -52,6 +52,9 @@ _PROTOS = {
     "orc_gemv_q4k": (None, [f32p, u8p, f32p, u32, u32, u32]),
     "orc_gemv_f16": (None, [f32p, u16p, f32p, u32, u32, u32]),
     "orc_rope_store": (None, [f32p, f32p, f32p, u16p, u16p, u32, u32, u32, u32, C.c_int, u32, u32, flt]),
+    "orc_rmsnorm": (None, [f32p, f32p, vp, u32, flt, C.c_int]),
+    "orc_qknorm_rope_store": (None, [f32p, f32p, f32p, u16p, u16p, u32, u32, u32, u32, C.c_int, u32, u32, flt, vp, vp,
+                                     C.c_int, flt]),
     "orc_f16_to_f32_buf": (None, [u16p, f32p, sz]),
     "orc_attn_decode": (None, [f32p, f32p, u16p, u16p, u32, u32, u32, u32, u32]),
     "orc_attn_prefill": (None, [f32p, f32p, u16p, u16p, u32, u32, u32, u32, u32, u32, u32]),
@@ -329,16 +332,24 @@ def rel_err(gpu: np.ndarray, cpu: np.ndarray, floor: float = RMS_FLOOR) -> float
     return float(np.max(np.abs(gpu - cpu) / den))
 
 
-def noise_floor(cpu: np.ndarray, exact: np.ndarray, margin: float = 2.0, tol: float = REL_TOL) -> float:
+# The GPU kernels multiply fp32 values as fp16 hi + lo pairs (q and p in
+# decode, q and P in prefill, every contraction of the chunked GDN): 22
+# significant bits, unit roundoff 2^-22 against fp32's 2^-24.  Their rounding
+# noise can therefore reach 4 times the CPU's, and a GPU-CPU difference
+# carries both: 1 + 4 = 5.  PARITY_LOG records the measured ratio
+# max|gpu - exact| / max|cpu - exact| of every check beside it.
+NOISE_MARGIN = 5.0
+
+
+def noise_floor(cpu: np.ndarray, exact: np.ndarray, margin: float = NOISE_MARGIN, tol: float = REL_TOL) -> float:
     """The rms floor that the CPU result's own rounding requires.
 
     `exact` is the same computation in float64.  The fp32 CPU result differs
-    from it by up to e = max|cpu - exact|; an equally accurate GPU result can
-    differ from the CPU's by up to 2e.  The returned floor is the smallest one
-    at which a difference of margin * e passes the bar `tol` on every element,
-    and never below RMS_FLOOR: on short reductions this is RMS_FLOOR itself,
-    on long ones (many keys, thousands of recurrent steps) the fp32 summation
-    noise near zero outputs sets it."""
+    from it by up to e = max|cpu - exact|.  The returned floor is the smallest
+    one at which a GPU-CPU difference of margin * e passes the bar `tol` on
+    every element, and never below RMS_FLOOR: on short reductions this is
+    RMS_FLOOR itself, on long ones (many keys, thousands of recurrent steps)
+    the fp32 summation noise near zero outputs sets it."""
     cpu = np.asarray(cpu, dtype=np.float64)
     exact = np.asarray(exact, dtype=np.float64)
     rms = float(np.sqrt(np.mean(cpu * cpu))) if cpu.size else 0.0
@@ -358,8 +369,14 @@ def assert_close(gpu: np.ndarray, cpu: np.ndarray, tol: float = REL_TOL, what: s
     if floor is None:
         floor = RMS_FLOOR if exact is None else noise_floor(cpu, exact, tol=tol)
     e = rel_err(gpu, cpu, floor)
-    PARITY_LOG.append({"what": what, "err": e, "floor": floor, "tol": tol,
-                       "err_at_1e-3": rel_err(gpu, cpu, RMS_FLOOR)})
+    rec = {"what": what, "err": e, "floor": floor, "tol": tol, "err_at_1e-3": rel_err(gpu, cpu, RMS_FLOOR)}
+    if exact is not None:   # how much noisier than the CPU the GPU result is, against float64
+        g = np.asarray(gpu, np.float64).ravel()
+        c = np.asarray(cpu, np.float64).ravel()
+        x = np.asarray(exact, np.float64).ravel()
+        ce = float(np.max(np.abs(c - x)))
+        rec["noise_ratio"] = float(np.max(np.abs(g - x))) / ce if ce > 0 else None
+    PARITY_LOG.append(rec)
     assert e <= tol, f"{what}: relative error {e:.3e} > {tol:.1e} (rms floor {floor:.2e})"
     return e
 

@@ -107,8 +107,8 @@ def test_gdn_prefill_config5a_full(dev):
                                               (3, 129, True)])
 def test_gdn_chunked_matches_recurrent_kernel(dev, n_seqs, T, seeded):
     """The chunked tensor-core prefill (64-token chunks, ragged last chunk,
-    several sequences) against the token-by-token GPU kernel, which follows
-    the reference's operation order."""
+    several sequences) and the token-by-token GPU kernel, which follows the
+    reference's operation order, both against the oracle."""
     from yllm_b200 import attn, fixtures
     from yllm_b200.configs import CFG5_GDN as c
 
@@ -121,14 +121,16 @@ def test_gdn_chunked_matches_recurrent_kernel(dev, n_seqs, T, seeded):
                                z=b.z, eps=c.eps)
     torch.cuda.synchronize()
     fx = oracle.gdn_fixture(c, n_seqs, T, seeded_state=seeded)
+    S_want, out_want = oracle.gdn_run(fx, c, n_seqs, T, True)
     S_ex, out_ex = oracle.exact_gdn(fx, c, n_seqs, T, True)
-    oracle.assert_close(_np(a.out), _np(b.out), what=f"chunked vs recurrent out {n_seqs}x{T}", exact=out_ex)
-    oracle.assert_close(_np(a.S), _np(b.S), what=f"chunked vs recurrent state {n_seqs}x{T}", exact=S_ex)
+    for name, g_ in (("chunked", a), ("recurrent", b)):
+        oracle.assert_close(_np(g_.out), out_want, what=f"{name} out {n_seqs}x{T}", exact=out_ex)
+        oracle.assert_close(_np(g_.S), S_want, what=f"{name} state {n_seqs}x{T}", exact=S_ex)
     assert attn.device_status() == 0
 
 
 def test_gdn_prefill_equals_decode_steps(dev):
-    """T prefill tokens == T single-token decodes (two kernels, same recurrence)."""
+    """T prefill tokens and T single-token decodes (two kernels, same recurrence) both match the oracle."""
     from yllm_b200 import attn, fixtures
     from yllm_b200.configs import CFG5_GDN as c
 
@@ -141,9 +143,11 @@ def test_gdn_prefill_equals_decode_steps(dev):
         attn.gdn_decode(b.S, b.out[t], b.q[t], b.k[t], b.v[t], b.gate[t], b.beta[t], 1, NK, D, NV, D)
     torch.cuda.synchronize()
     fx = oracle.gdn_fixture(c, 1, T, seeded_state=True)
+    S_want, out_want = oracle.gdn_run(fx, c, 1, T, False)
     S_ex, out_ex = oracle.exact_gdn(fx, c, 1, T, False)
-    oracle.assert_close(_np(a.out), _np(b.out), what="prefill vs decode out", exact=out_ex)
-    oracle.assert_close(_np(a.S), _np(b.S), what="prefill vs decode state", exact=S_ex)
+    for name, g_ in (("prefill", a), ("decode steps", b)):
+        oracle.assert_close(_np(g_.out), out_want, what=f"gdn {name} out", exact=out_ex)
+        oracle.assert_close(_np(g_.S), S_want, what=f"gdn {name} state", exact=S_ex)
 
 
 def test_gdn_rejects_unsupported(dev):

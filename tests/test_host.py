@@ -225,24 +225,33 @@ def test_rope_store_rejects_bad_arguments():
 
     err = C.create_string_buffer(256)
     fake = C.c_void_p(0x1000)   # never dereferenced: every case fails before a launch
-    assert lib.yattn_rope_store_kv(fake, 0, 32, 8, 128, 1024, 0, 0, 1e4, None, err, 256) == 0   # nothing to do
-    assert lib.yattn_rope_store_kv(fake, 4, 32, 8, 128, 1024, 3, 0, 1e4, None, err, 256) == -1
+    assert lib.yattn_rope_store_kv(fake, 0, 32, 8, 128, 1024, 0, 0, 1e4, None, None, err, 256) == 0   # nothing to do
+    assert lib.yattn_rope_store_kv(fake, 4, 32, 8, 128, 1024, 3, 0, 1e4, None, None, err, 256) == -1
     assert b"rope_kind" in err.value
-    assert lib.yattn_rope_store_kv(fake, 4, 32, 8, 127, 1024, 0, 0, 1e4, None, err, 256) == -1
+    assert lib.yattn_rope_store_kv(fake, 4, 32, 8, 127, 1024, 0, 0, 1e4, None, None, err, 256) == -1
     assert b"geometry" in err.value
-    assert lib.yattn_rope_store_kv(fake, 4, 16, 2, 256, 512, 2, 300, 1e4, None, err, 256) == -1
+    assert lib.yattn_rope_store_kv(fake, 4, 16, 2, 256, 512, 2, 300, 1e4, None, None, err, 256) == -1
     assert b"rotated dims" in err.value
-    assert lib.yattn_rope_store_kv(None, 4, 32, 8, 128, 1024, 0, 0, 1e4, None, err, 256) == -1
+    assert lib.yattn_rope_store_kv(None, 4, 32, 8, 128, 1024, 0, 0, 1e4, None, None, err, 256) == -1
     # the batch form
     assert lib.yattn_rope_store_kv_batch(fake, fake, fake, fake, fake, 0, 0, 4096, 32, 8, 128, 1024, 0, 0, 1e4,
-                                         None, err, 256) == 0
+                                         None, None, err, 256) == 0
     assert lib.yattn_rope_store_kv_batch(fake, fake, fake, fake, fake, 0, 8, 4000, 32, 8, 128, 1024, 0, 0, 1e4,
-                                         None, err, 256) == -1
+                                         None, None, err, 256) == -1
     assert b"q_stride" in err.value
     assert lib.yattn_rope_store_kv_batch(fake, None, fake, fake, fake, 0, 8, 4096, 32, 8, 128, 1024, 0, 0, 1e4,
-                                         None, err, 256) == -1
+                                         None, None, err, 256) == -1
+    # QK-norm needs both weight vectors, aligned to their element size
+    from yllm_b200._lib import YattnQkNorm
+
+    half = YattnQkNorm(0x1000, None, 0, 1e-6)
+    assert lib.yattn_rope_store_kv(fake, 4, 16, 8, 128, 1024, 1, 0, 1e6, C.byref(half), None, err, 256) == -1
+    assert b"both" in err.value
+    odd = YattnQkNorm(0x1002, 0x2000, 0, 1e-6)
+    assert lib.yattn_rope_store_kv(fake, 4, 16, 8, 128, 1024, 1, 0, 1e6, C.byref(odd), None, err, 256) == -1
+    assert b"aligned" in err.value
     assert lib.yattn_rope_store_kv_batch(fake, fake, fake, fake, fake, 0xFFFFFFF0, 64, 4096, 32, 8, 128, 1024, 0, 0,
-                                         1e4, None, err, 256) == -1
+                                         1e4, None, None, err, 256) == -1
     assert b"overflow" in err.value
 
 

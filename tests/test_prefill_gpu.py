@@ -188,7 +188,8 @@ def test_prefill_mixed_tiles(dev):
 
 
 def test_prefill_last_row_equals_decode(dev):
-    """The last prefill row and a decode at the same position agree (two kernels)."""
+    """The last prefill row and a decode at the same position (two kernels) both match the oracle's decode
+    of that row."""
     from yllm_b200 import attn
 
     H, KV, hd, B = 32, 8, 128, 777
@@ -198,8 +199,10 @@ def test_prefill_last_row_equals_decode(dev):
     dec = torch.zeros(H * hd, device=dev)
     attn.attn_decode(dec, c["tq"][B - 1].contiguous(), c["tk"], c["tv"], B - 1, H, KV, hd, c["kd"])
     torch.cuda.synchronize()
+    want = oracle.attn_decode(c["q"][B - 1], c["k"], c["v"], B - 1, H, KV, hd, c["kd"])
     exact = oracle.exact_decode(c["q"][B - 1], c["k"], c["v"], B - 1, H, KV, hd, c["kd"])
-    oracle.assert_close(out[B - 1].cpu().numpy(), dec.cpu().numpy(), what="prefill vs decode", exact=exact)
+    oracle.assert_close(out[B - 1].cpu().numpy(), want, what="prefill last row vs oracle decode", exact=exact)
+    oracle.assert_close(dec.cpu().numpy(), want, what="decode vs oracle decode", exact=exact)
 
 
 def test_prefill_rejects_bad_geometry(dev):

@@ -132,3 +132,98 @@ def test_rope_store_batch_matches_reference(dev, kind, H, KV, hd, n_dims, theta,
     dk = np.abs(kc_np.astype(np.int32) - kc_ref.astype(np.int32))
     assert dk.max() <= 1, f"K rows off by {dk.max()} fp16 ulps"
     assert (dk != 0).mean() <= 0.01
+
+
+def _norm_weights(rng, hd, f16):
+    w = (1.0 + 0.3 * rng.standard_normal((2, hd))).astype(np.float32)
+    if f16:
+        w = oracle.f32_to_f16(w).reshape(2, hd)
+    return w
+
+
+@pytest.mark.parametrize("kind,H,KV,hd,n_dims,theta,f16", [
+    (1, 16, 8, 128, 128, 1000000.0, False),   # Qwen3-0.6B: QK-norm then the qwen half-split rotation
+    (1, 16, 8, 128, 128, 1000000.0, True),    # the same with fp16 norm weights
+    (2, 16, 2, 256, 64, 10000000.0, False),   # qwen35 gated attention: QK-norm then M-RoPE on 64 of 256 dims
+    (2, 16, 2, 256, 64, 10000000.0, True),
+])
+def test_qknorm_rope_store_matches_reference(dev, kind, H, KV, hd, n_dims, theta, f16):
+    """QK-norm (rmsnorm of every q and k head with the layer's weights, engine.c:915-919 / 1036-1045) fused
+    into the RoPE store, against the reference's rmsnorm + rope + f32_to_f16 per item (oracle/_ref)."""
+    from yllm_b200 import attn
+
+    lib = _ref_lib()
+    rng = np.random.default_rng(31 * hd + kind + f16)
+    kd = KV * hd
+    positions = [0, 3, 511, 4095, 70000]
+    rows = max(positions) + 1
+    n = len(positions)
+    q = (3.0 * rng.standard_normal((n, H * hd))).astype(np.float32)   # unnormalised projections
+    k = (3.0 * rng.standard_normal((n, kd))).astype(np.float32)
+    v = rng.standard_normal((n, kd)).astype(np.float32)
+    w = _norm_weights(rng, hd, f16)
+    eps = 1e-6
+    kc = torch.zeros(rows * kd, dtype=torch.int16, device=dev)
+    vc = torch.zeros_like(kc)
+    tq, tk, tv = (torch.from_numpy(x).to(dev) for x in (q, k, v))
+    wt = torch.from_numpy(w.view(np.int16) if f16 else w).to(dev)
+    items = attn.make_rope_items([(tq[i], tk[i], tv[i], kc, vc, positions[i]) for i in range(n)], device=dev)
+    attn.rope_store_kv(items, n, H, KV, hd, kd, kind, theta, n_rope_dims=n_dims,
+                       norm=attn.qk_norm(wt[0], wt[1], eps))
+    torch.cuda.synchronize()
+    assert attn.device_status() == 0
+    assert torch.equal(tk, torch.from_numpy(k).to(dev)), "k must not be modified"
+    q_ref, k_ref = q.copy(), k.copy()
+    kc_ref = np.zeros(rows * kd, np.uint16)
+    vc_ref = np.zeros(rows * kd, np.uint16)
+    wq, wk = np.ascontiguousarray(w[0]), np.ascontiguousarray(w[1])
+    for i, pos in enumerate(positions):
+        qi, ki = np.ascontiguousarray(q_ref[i]), np.ascontiguousarray(k_ref[i])
+        lib.orc_qknorm_rope_store(qi, ki, np.ascontiguousarray(v[i]), kc_ref, vc_ref, H, KV, hd, kd, kind, n_dims,
+                                  pos, theta, wq.ctypes.data, wk.ctypes.data, 1 if f16 else 0, eps)
+        q_ref[i] = qi
+    e = oracle.rope_err(tq.cpu().numpy(), q_ref, kind, hd, n_dims)
+    assert e <= 1e-5, f"q after QK-norm + RoPE: relative error {e:.2e}"
+    kc_np = kc.cpu().numpy().view(np.uint16)
+    vc_np = vc.cpu().numpy().view(np.uint16)
+    assert np.array_equal(vc_np, vc_ref), "V rows differ from the engine's rounding"
+    dk = np.abs(kc_np.astype(np.int32) - kc_ref.astype(np.int32))
+    assert dk.max() <= 1, f"K rows off by {dk.max()} fp16 ulps"
+    assert (dk != 0).sum() <= max(1, 0.01 * n * kd), f"{(dk != 0).sum()} K values differ by one ulp"
+
+
+def test_qknorm_rope_store_batch_matches_reference(dev):
+    """The batch form (a prefill chunk of consecutive tokens) with QK-norm, qwen35 shape."""
+    from yllm_b200 import attn
+
+    lib = _ref_lib()
+    kind, H, KV, hd, n_dims, theta, eps = 2, 16, 2, 256, 64, 10000000.0, 1e-6
+    rng = np.random.default_rng(5)
+    kd = KV * hd
+    B, pos_start = 200, 4000
+    rows = pos_start + B
+    q = (2.0 * rng.standard_normal((B, H * hd))).astype(np.float32)
+    k = (2.0 * rng.standard_normal((B, kd))).astype(np.float32)
+    v = rng.standard_normal((B, kd)).astype(np.float32)
+    w = _norm_weights(rng, hd, False)
+    kc = torch.zeros(rows * kd, dtype=torch.int16, device=dev)
+    vc = torch.zeros_like(kc)
+    tq, tk, tv = (torch.from_numpy(x).to(dev) for x in (q, k, v))
+    wt = torch.from_numpy(w).to(dev)
+    attn.rope_store_kv_batch(tq, tk, tv, kc, vc, pos_start, B, H, KV, hd, kd, kind, theta, n_rope_dims=n_dims,
+                             norm=attn.qk_norm(wt[0], wt[1], eps))
+    torch.cuda.synchronize()
+    assert attn.device_status() == 0
+    q_ref, k_ref = q.copy(), k.copy()
+    kc_ref = np.zeros(rows * kd, np.uint16)
+    vc_ref = np.zeros(rows * kd, np.uint16)
+    for b in range(B):
+        qi, ki = np.ascontiguousarray(q_ref[b]), np.ascontiguousarray(k_ref[b])
+        lib.orc_qknorm_rope_store(qi, ki, np.ascontiguousarray(v[b]), kc_ref, vc_ref, H, KV, hd, kd, kind, n_dims,
+                                  pos_start + b, theta, w[0].ctypes.data, w[1].ctypes.data, 0, eps)
+        q_ref[b] = qi
+    e = oracle.rope_err(tq.cpu().numpy(), q_ref, kind, hd, n_dims)
+    assert e <= 1e-5, f"q after QK-norm + RoPE: relative error {e:.2e}"
+    assert np.array_equal(vc.cpu().numpy().view(np.uint16), vc_ref)
+    dk = np.abs(kc.cpu().numpy().view(np.uint16).astype(np.int32) - kc_ref.astype(np.int32))
+    assert dk.max() <= 1 and (dk != 0).mean() <= 0.01

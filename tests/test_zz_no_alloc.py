@@ -39,7 +39,8 @@ def _case(dev, H, KV, hd, T, seed, gated=False):
     tv = torch.from_numpy(v.view(np.int16)).to(dev).view(torch.uint16)
     gate = torch.from_numpy(gn).to(dev) if gated else None
     want = oracle.attn_decode(qn, k, v, T - 1, H, KV, hd, kd, gate=gn)
-    return q, tk, tv, gate, kd, want
+    exact = oracle.exact_decode(qn, k, v, T - 1, H, KV, hd, kd, gate=gn)
+    return q, tk, tv, gate, kd, (want, exact)
 
 
 @pytest.mark.parametrize("H,KV,hd,T,gated", [
@@ -68,8 +69,10 @@ def test_noalloc_decode_matches_allocating_entry(H, KV, hd, T, gated):
     want = ref.cpu().numpy()
     for out in outs:
         got = out.cpu().numpy()
-        oracle.assert_close(got, want, what=f"noalloc vs yattn_attn_decode H{H} KV{KV} hd{hd} T{T}")
-        oracle.assert_close(got, want_cpu, what=f"noalloc vs CPU oracle H{H} KV{KV} hd{hd} T{T}")
+        oracle.assert_close(got, want, what=f"noalloc vs yattn_attn_decode H{H} KV{KV} hd{hd} T{T}",
+                            exact=want_cpu[1])
+        oracle.assert_close(got, want_cpu[0], what=f"noalloc vs CPU oracle H{H} KV{KV} hd{hd} T{T}",
+                            exact=want_cpu[1])
     assert attn.device_status() == 0
 
 
@@ -124,7 +127,7 @@ def test_noalloc_device_failure_reaches_device_status():
     _noalloc(out, q, k, v, gate, T - 1, H, KV, hd, kd, stream)
     torch.cuda.synchronize()
     assert attn.device_status() == 0
-    oracle.assert_close(out.cpu().numpy(), want_cpu, what="noalloc after a rejected call")
+    oracle.assert_close(out.cpu().numpy(), want_cpu[0], what="noalloc after a rejected call", exact=want_cpu[1])
 
 
 def test_noalloc_rejects_wrapping_position():

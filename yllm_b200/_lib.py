@@ -51,6 +51,15 @@ class YattnRopeItem(C.Structure):
     ]
 
 
+class YattnQkNorm(C.Structure):
+    _fields_ = [
+        ("q_w", vp),
+        ("k_w", vp),
+        ("w_f16", C.c_int),
+        ("eps", C.c_float),
+    ]
+
+
 class YattnDecodeWork(C.Structure):
     _fields_ = [
         ("item", u32),
@@ -114,7 +123,7 @@ PROTOS = {
     "yattn_attn_decode_noalloc": (C.c_int, [vp, vp, vp, vp, vp, u32, u32, u32, u32, u32, vp, *E]),
     "yattn_reserve": (C.c_int, [sz, *E]),
     "yattn_store_kv": (C.c_int, [vp, vp, vp, vp, u32, u32, u32, vp, *E]),
-    "yattn_rope_store_kv": (C.c_int, [vp, u32, u32, u32, u32, u32, C.c_int, u32, C.c_float, vp, *E]),
+    "yattn_rope_store_kv": (C.c_int, [vp, u32, u32, u32, u32, u32, C.c_int, u32, C.c_float, vp, vp, *E]),
     "yattn_gdn_inputs": (C.c_int, [vp] * 12 + [u32] * 8 + [C.c_float, vp, *E]),
     "yattn_sess_kv_save": (C.c_int, [vp, u32, u32, u32, u32, C.c_char_p, vp, *E]),
     "yattn_sess_kv_load": (C.c_int, [vp, u32, u32, u32, C.c_char_p, C.POINTER(u32), vp, *E]),
@@ -125,7 +134,7 @@ PROTOS = {
     "cuda_k_gemv_f16": (C.c_int, [vp, vp, vp, vp, vp, u32, u32, *E]),
     "cuda_k_gemm_f16": (C.c_int, [vp, vp, vp, vp, vp, u32, u32, u32, *E]),
     "yattn_rope_store_kv_batch": (C.c_int, [vp, vp, vp, vp, vp, u32, u32, u32, u32, u32, u32, u32, C.c_int, u32,
-                                            C.c_float, vp, *E]),
+                                            C.c_float, vp, vp, *E]),
     "cuda_k_gdn_state_update": (None, [vp, vp, vp, vp, vp, vp, vp, u32, u32, u32, u32]),
     "yattn_gdn_decode": (C.c_int, [vp, vp, vp, vp, vp, vp, vp, u32, u32, u32, u32, u32, vp, vp, C.c_float, vp, *E]),
     "yattn_gdn_prefill": (

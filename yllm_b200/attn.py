@@ -19,7 +19,7 @@ import numpy as np
 import torch
 
 from . import _lib
-from ._lib import YattnDecodeItem, YattnDecodeWork, YattnRopeItem, call, call_void, lib
+from ._lib import YattnDecodeItem, YattnDecodeWork, YattnQkNorm, YattnRopeItem, call, call_void, lib
 
 
 def _ptr(t: Optional[torch.Tensor]) -> Optional[int]:
@@ -215,25 +215,42 @@ def make_rope_items(entries: Sequence[tuple], device=None) -> torch.Tensor:
     return torch.frombuffer(raw, dtype=torch.uint8).to(device or "cuda")
 
 
+def qk_norm(q_w: torch.Tensor, k_w: torch.Tensor, eps: float):
+    """The QK-norm argument of rope_store_kv(_batch): the layer's q and k rmsnorm weights (head_dim values, fp32,
+    or fp16 as int16/uint16/float16 tensors) and eps (engine.c:915-919, 1036-1045)."""
+    f16 = q_w.dtype in (torch.int16, torch.uint16, torch.float16)
+    if f16 != (k_w.dtype in (torch.int16, torch.uint16, torch.float16)):
+        raise ValueError("q and k norm weights must have the same dtype")
+    if not f16:
+        _need(q_w, torch.float32, "q_w")
+        _need(k_w, torch.float32, "k_w")
+    return YattnQkNorm(q_w.data_ptr(), k_w.data_ptr(), 1 if f16 else 0, float(eps))
+
+
+def _norm_arg(norm):
+    return None if norm is None else C.byref(norm)
+
+
 def rope_store_kv(items: torch.Tensor, n_items: int, n_heads: int, n_kv_heads: int, head_dim: int, kv_dim: int,
-                  rope_kind: int, theta: float, n_rope_dims: int = 0, stream=None) -> None:
+                  rope_kind: int, theta: float, n_rope_dims: int = 0, norm=None, stream=None) -> None:
     """One decode step's RoPE of q (in place) and k, and the fp16 store of k and v at each item's position
-    (engine.c:1052-1072 / cuda_fwd.c:136-147 for every item, one launch)."""
+    (engine.c:1052-1072 / cuda_fwd.c:136-147 for every item, one launch).  norm (qk_norm(...)) applies the
+    per-head QK-norm first."""
     call("yattn_rope_store_kv", items.data_ptr(), n_items, n_heads, n_kv_heads, head_dim, kv_dim, rope_kind,
-         n_rope_dims, theta, _stream(stream))
+         n_rope_dims, theta, _norm_arg(norm), _stream(stream))
 
 
 def rope_store_kv_batch(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, kcache: torch.Tensor,
                         vcache: torch.Tensor, pos_start: int, B: int, n_heads: int, n_kv_heads: int, head_dim: int,
                         kv_dim: int, rope_kind: int, theta: float, n_rope_dims: int = 0, q_stride: int = 0,
-                        stream=None) -> None:
+                        norm=None, stream=None) -> None:
     """RoPE + KV store of B consecutive tokens (rows of q, k, v) at positions pos_start.. (the batched prefill's
-    cuda_fwd.c:207-218 in one launch).  q is rotated in place."""
+    cuda_fwd.c:207-218 in one launch).  q is rotated in place; norm as in rope_store_kv."""
     for name, t in (("q", q), ("k", k), ("v", v)):
         _need(t, torch.float32, name)
     call("yattn_rope_store_kv_batch", q.data_ptr(), k.data_ptr(), v.data_ptr(), kcache.data_ptr(), vcache.data_ptr(),
          pos_start, B, q_stride or n_heads * head_dim, n_heads, n_kv_heads, head_dim, kv_dim, rope_kind, n_rope_dims,
-         theta, _stream(stream))
+         theta, _norm_arg(norm), _stream(stream))
 
 
 def decode_partial(ml: torch.Tensor, o: torch.Tensor, q: torch.Tensor, kcache: torch.Tensor, vcache: torch.Tensor,

@@ -21,6 +21,13 @@
 // A partial last chunk is padded with k = q = v = 0, a = 0, beta = 0, which
 // leaves every formula exact for the real tokens.
 //
+// Gamma is a prefix sum in double.  In fp32, |Gamma| reaches tens within a
+// chunk, and the difference Gamma_t - Gamma_i of two rounded prefix sums loses
+// about ulp(Gamma) (4e-6 at |Gamma| ~ 45) in the exponent of every decay: that
+// alone made the chunked state several times noisier than the engine's fp32
+// token-by-token products of expf(a_t).  The decays are expf of the
+// double-precision difference, e^Gamma and e^(Gamma_63 - Gamma) exp in double.
+//
 // Two kernels:
 //   k_gdn_chunk_prep   (chunk, v-head, seq): everything that does not depend on
 //                      S -- Gamma, T and P -- plus fp16 hi/lo copies of K and Q.
@@ -130,8 +137,8 @@ __device__ __forceinline__ void cp16(void* dst_smem, const void* src, bool valid
 
 // ------------------------------------------------------------------ prep
 // smem: Kh Kl Qh Ql [64][LDH] halves (T aliases Kh.. once K/Q are done), A and P
-// [64][LA] fp32, Gamma and beta [64].
-constexpr int kPrepSmem = 4 * kC * LDH * 2 + 2 * kC * LA * 4 + 2 * kC * 4;
+// [64][LA] fp32, gates then Gamma [64] double, beta [64] fp32.
+constexpr int kPrepSmem = 4 * kC * LDH * 2 + 2 * kC * LA * 4 + kC * 8 + kC * 4;
 
 __global__ void __launch_bounds__(256) k_gdn_chunk_prep(const ChunkParams p) {
     extern __shared__ __align__(16) uint8_t smp[];
@@ -141,8 +148,8 @@ __global__ void __launch_bounds__(256) k_gdn_chunk_prep(const ChunkParams p) {
     __half* Ql = Qh + kC * LDH;
     float* Am = reinterpret_cast<float*>(Ql + kC * LDH);
     float* Pm = Am + kC * LA;
-    float* G = Pm + kC * LA;
-    float* Bt = G + kC;
+    double* G = reinterpret_cast<double*>(Pm + kC * LA);   // 8-byte aligned: every array above is
+    float* Bt = reinterpret_cast<float*>(G + kC);
     float* Tm = reinterpret_cast<float*>(Kh);           // [64][LA], after K/Q are consumed
 
     const uint32_t ch = blockIdx.x, h = blockIdx.y, sq = blockIdx.z;
@@ -190,12 +197,12 @@ __global__ void __launch_bounds__(256) k_gdn_chunk_prep(const ChunkParams p) {
         Bt[tid] = ok ? p.beta[(tok0 + tid) * p.n_vheads + h] : 0.f;
     }
     __syncthreads();
-    // Gamma: inclusive prefix sum of the gates (warp 0), published for the state kernel
+    // Gamma: inclusive prefix sum of the gates in double (warp 0), published for the state kernel
     if (warp == 0) {
-        float x0 = G[lane], x1 = G[32 + lane];
+        double x0 = G[lane], x1 = G[32 + lane];
 #pragma unroll
         for (int o = 1; o < 32; o <<= 1) {
-            const float y0 = __shfl_up_sync(0xffffffffu, x0, o), y1 = __shfl_up_sync(0xffffffffu, x1, o);
+            const double y0 = __shfl_up_sync(0xffffffffu, x0, o), y1 = __shfl_up_sync(0xffffffffu, x1, o);
             if (lane >= o) {
                 x0 += y0;
                 x1 += y1;
@@ -204,14 +211,14 @@ __global__ void __launch_bounds__(256) k_gdn_chunk_prep(const ChunkParams p) {
         x1 += __shfl_sync(0xffffffffu, x0, 31);
         G[lane] = x0;
         G[32 + lane] = x1;
-        const float glast = __shfl_sync(0xffffffffu, x1, 31);
+        const double glast = __shfl_sync(0xffffffffu, x1, 31);
         float* gm = p.gam + (sc * p.n_vheads + h) * kGamFloats;
-        gm[lane] = x0;
-        gm[32 + lane] = x1;
-        gm[kC + lane] = expf(x0);
-        gm[kC + 32 + lane] = expf(x1);
-        gm[2 * kC + lane] = expf(glast - x0);
-        gm[2 * kC + 32 + lane] = expf(glast - x1);
+        gm[lane] = static_cast<float>(x0);
+        gm[32 + lane] = static_cast<float>(x1);
+        gm[kC + lane] = static_cast<float>(exp(x0));
+        gm[kC + 32 + lane] = static_cast<float>(exp(x1));
+        gm[2 * kC + lane] = static_cast<float>(exp(glast - x0));
+        gm[2 * kC + 32 + lane] = static_cast<float>(exp(glast - x1));
     }
     // K/Q hi/lo to the scratch, once per k-head (by the v-head that equals it)
     if (h < p.num_k_heads) {   // Kh, Kl, Qh, Ql are consecutive [64][LDH] arrays
@@ -256,10 +263,10 @@ __global__ void __launch_bounds__(256) k_gdn_chunk_prep(const ChunkParams p) {
                 const int t = 16 * mt + g + ((e >> 1) << 3), i = 8 * n + 2 * tq + (e & 1);
                 float val = 0.f;
                 if (which == 0) {
-                    if (i < t) val = Bt[t] * expf(G[t] - G[i]) * acc[n][e];
+                    if (i < t) val = Bt[t] * expf(static_cast<float>(G[t] - G[i])) * acc[n][e];
                     Am[t * LA + i] = val;
                 } else {
-                    if (i <= t) val = expf(G[t] - G[i]) * acc[n][e];
+                    if (i <= t) val = expf(static_cast<float>(G[t] - G[i])) * acc[n][e];
                     Pm[t * LA + i] = val;
                 }
             }

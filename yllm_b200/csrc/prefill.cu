@@ -202,13 +202,17 @@ __global__ void __launch_bounds__(kPThreads, 1)
             tc_fence_after();
             const bool qlo = ok && bars->qlo != 0;
             const uint32_t nsb = qlo ? C::NSB_QLO : C::NSB;
+            // S buffer and phase of the next S(jj) and of the next PV(jj): both advance by one
+            // block per call (no division by the runtime buffer count)
+            uint32_t s_sb = 0, pv_sb = 0, pv_ph = 0;
             // S(jj) = Q K(jj)^T into S buffer jj % nsb.  That buffer last held P(jj - nsb), whose PV
             // product was issued earlier; the tensor core runs one thread's MMAs in issue order.
             auto do_s = [&](uint32_t jj) -> bool {
                 const int s = jj % KST;
                 if (!mbar_wait_bounded(&bars->k_full[s], (jj / KST) & 1u, p.status, ST_PREFILL_TIMEOUT, abort_flag))
                     return false;
-                const uint32_t sb = jj % nsb;
+                const uint32_t sb = s_sb;
+                if (++s_sb == nsb) s_sb = 0;
                 tc_fence_after();
                 const uint64_t dk = dk0 + ((s * C::KV_BYTES) >> 4);
 #pragma unroll
@@ -232,11 +236,14 @@ __global__ void __launch_bounds__(kPThreads, 1)
             // are the 8 columns at 32*(kk/2) + 16*plane + 8*(kk%2) of the block's S buffer.
             auto do_pv = [&](uint32_t jj) -> bool {
                 const int s = jj % VST;
-                const uint32_t sb = jj % nsb;
-                if (!mbar_wait_bounded(&bars->p_full[sb], (jj / nsb) & 1u, p.status, ST_PREFILL_TIMEOUT,
-                                       abort_flag) ||
+                const uint32_t sb = pv_sb, ph = pv_ph;
+                if (!mbar_wait_bounded(&bars->p_full[sb], ph, p.status, ST_PREFILL_TIMEOUT, abort_flag) ||
                     !mbar_wait_bounded(&bars->v_full[s], (jj / VST) & 1u, p.status, ST_PREFILL_TIMEOUT, abort_flag))
                     return false;
+                if (++pv_sb == nsb) {
+                    pv_sb = 0;
+                    pv_ph ^= 1u;
+                }
                 tc_fence_after();
                 const uint32_t pcol = tmem + C::COL_S + sb * BN;
                 const uint64_t dv = dv0 + ((s * C::KV_BYTES) >> 4);
@@ -290,22 +297,29 @@ __global__ void __launch_bounds__(kPThreads, 1)
                     v[i] = __ldcs(reinterpret_cast<const float4*>(p.q + static_cast<size_t>(b) * p.q_stride +
                                                                   static_cast<size_t>(hh) * HD + (idx % C4) * 4));
             }
-            // Q_lo first goes through the Q buffer (this thread's elements), so the thread that
-            // owns a row's TMEM lane can pick it up; Q_hi then overwrites it.
+            // hi and lo halves of this thread's q, packed (4 registers per float4 loaded)
+            uint2 qh[QITER], ql[QITER];
             bool any_lo = false;
 #pragma unroll
             for (int i = 0; i < QITER; ++i) {
-                const int idx = threadIdx.x + i * 256;
                 const __half2 h0 = __floats2half2_rn(v[i].x, v[i].y), h1 = __floats2half2_rn(v[i].z, v[i].w);
                 const float2 f0 = __half22float2(h0), f1 = __half22float2(h1);
-                uint2 lo;
-                lo.x = h2_bits(__floats2half2_rn(v[i].x - f0.x, v[i].y - f0.y));
-                lo.y = h2_bits(__floats2half2_rn(v[i].z - f1.x, v[i].w - f1.y));
-                any_lo = any_lo || ((lo.x | lo.y) & 0x7fff7fffu) != 0u;
-                *reinterpret_cast<uint2*>(sQ + sw128_offset(idx / C4, (idx % C4) * 4, BM)) = lo;
+                qh[i].x = h2_bits(h0);
+                qh[i].y = h2_bits(h1);
+                ql[i].x = h2_bits(__floats2half2_rn(v[i].x - f0.x, v[i].y - f0.y));
+                ql[i].y = h2_bits(__floats2half2_rn(v[i].z - f1.x, v[i].w - f1.y));
+                any_lo = any_lo || (f0.x != v[i].x) || (f0.y != v[i].y) || (f1.x != v[i].z) || (f1.y != v[i].w);
             }
             qlo = named_bar_or(5, 256, any_lo);   // the same answer in every softmax thread
             if (qlo) {
+                // Q_lo goes through the Q buffer (this thread's elements), so the thread that owns
+                // a row's TMEM lane can pick it up; Q_hi then overwrites it.
+#pragma unroll
+                for (int i = 0; i < QITER; ++i) {
+                    const int idx = threadIdx.x + i * 256;
+                    *reinterpret_cast<uint2*>(sQ + sw128_offset(idx / C4, (idx % C4) * 4, BM)) = ql[i];
+                }
+                named_bar_sync(5, 256);
                 // row r, this half's dims [h*HD/2, +HD/2): 32 dims (16 TMEM columns) at a time
 #pragma unroll
                 for (int c = 0; c < HD / 64; ++c) {
@@ -328,10 +342,7 @@ __global__ void __launch_bounds__(kPThreads, 1)
 #pragma unroll
             for (int i = 0; i < QITER; ++i) {
                 const int idx = threadIdx.x + i * 256;
-                uint2 pk;
-                pk.x = h2_bits(__floats2half2_rn(v[i].x, v[i].y));
-                pk.y = h2_bits(__floats2half2_rn(v[i].z, v[i].w));
-                *reinterpret_cast<uint2*>(sQ + sw128_offset(idx / C4, (idx % C4) * 4, BM)) = pk;
+                *reinterpret_cast<uint2*>(sQ + sw128_offset(idx / C4, (idx % C4) * 4, BM)) = qh[i];
             }
             fence_proxy_async_smem();
             tc_fence_before();
@@ -339,6 +350,8 @@ __global__ void __launch_bounds__(kPThreads, 1)
             if (lane == 0) mbar_arrive(&bars->q_full);
         }
         const uint32_t nsb = qlo ? C::NSB_QLO : C::NSB;
+        uint32_t sb = 0, sph = 0;            // S buffer of block j and its phase
+        uint32_t pb = 0, pph = 0;            // the same for block j - 1 (its PV completion)
 
         const uint32_t qpos = qpos0 + r;
         const float sl2 = p.scale_log2;
@@ -348,9 +361,7 @@ __global__ void __launch_bounds__(kPThreads, 1)
         // goes through that barrier (AND-reduced), so both halves always leave together and
         // neither is left at a barrier its partner will not reach.
         for (uint32_t j = 0; j < nkb; ++j) {
-            const uint32_t sb = j % nsb;
-            const bool got =
-                warp_wait_bounded(&bars->s_full[sb], (j / nsb) & 1u, p.status, ST_PREFILL_TIMEOUT, abort_flag);
+            const bool got = warp_wait_bounded(&bars->s_full[sb], sph, p.status, ST_PREFILL_TIMEOUT, abort_flag);
             const uint32_t scol = trow + C::COL_S + sb * BN + h * HB;  // this half's columns of S(j)
             float sv[HB];
             if (got) {
@@ -422,8 +433,8 @@ __global__ void __launch_bounds__(kPThreads, 1)
             // ---- O rescale (rare), this half's columns of O: PV(j-1) must have finished ----
             // (both halves of these rows see the same `grow`, so both come here)
             if (j >= 1 && __any_sync(0xffffffffu, grow)) {
-                const bool done = warp_wait_bounded(&bars->pv_done[(j - 1) % nsb], ((j - 1) / nsb) & 1u,
-                                                    p.status, ST_PREFILL_TIMEOUT, abort_flag);
+                const bool done =
+                    warp_wait_bounded(&bars->pv_done[pb], pph, p.status, ST_PREFILL_TIMEOUT, abort_flag);
                 if (!named_bar_and(1 + qd, 64, done)) {
                     ok = false;
                     break;
@@ -444,6 +455,12 @@ __global__ void __launch_bounds__(kPThreads, 1)
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(&bars->p_full[sb]);
+            pb = sb;
+            pph = sph;
+            if (++sb == nsb) {
+                sb = 0;
+                sph ^= 1u;
+            }
         }
         // ---- epilogue: O / l (x sigmoid(gate)) -> out; each half takes its HD/2 columns ----
         // the last PV's completion, on a barrier of its own; the row sums of the two halves

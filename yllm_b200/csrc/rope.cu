@@ -16,6 +16,12 @@
 // multiply, and a*c - b*s / a*s + b*c are evaluated without FMA contraction.
 // The only difference left is the device's sinf/cosf against the host
 // library's (a few ulps), which moves a stored fp16 value by one ulp rarely.
+//
+// With QK-norm (qwen3, engine.c:1036-1045; qwen35, engine.c:915-919) every q
+// head and every k head is first normalised by rmsnorm (matvec.c:152-165) with
+// the layer's shared head_dim weights, then rotated.  That launch runs one CTA
+// per head: the sum of squares goes in index order through one thread, as the
+// reference's loop does, and y = (x * w) * inv keeps its operation order.
 #include "common.cuh"
 
 #include <algorithm>
@@ -28,6 +34,10 @@ constexpr int kMaxPairs = 128;   // head_dim <= 256
 
 struct RopeParams {
     const YattnRopeItem* items;      // NULL: the batch form below
+    const void* q_norm_w;            // QK-norm weights [hd] (fp32, or fp16 bits if norm_f16); NULL: no norm
+    const void* k_norm_w;
+    uint32_t norm_f16;
+    float norm_eps;
     YattnRopeItem batch;             // row 0 of a token batch: row b at q + b*q_stride, k/v + b*kv_dim, pos + b
     uint32_t q_stride;
     uint32_t n_items, n_heads, n_kv, hd, kv_dim;
@@ -62,12 +72,8 @@ __device__ __forceinline__ void pair_of(uint32_t kind, uint32_t hd, uint32_t n_d
     }
 }
 
-// blockIdx.y = item.  Work of an item, grid-strided over blockIdx.x:
-//   [0, nq)            q pairs (head, j), rotated in place
-//   [nq, nq + nk)      k pairs, rotated and stored (engine rounding)
-//   [.., + nr)         k elements outside the rotated dims (mrope), stored as is
-//   [.., + kv_dim)     v elements, stored
-__global__ void __launch_bounds__(256) k_rope_store(const RopeParams p) {
+// Row `blockIdx.y` of the launch: the item, or row b of the batch form.
+__device__ __forceinline__ YattnRopeItem item_of(const RopeParams& p) {
     YattnRopeItem it;
     if (p.items) {
         it = p.items[blockIdx.y];
@@ -78,6 +84,16 @@ __global__ void __launch_bounds__(256) k_rope_store(const RopeParams p) {
         it.v += static_cast<size_t>(blockIdx.y) * p.kv_dim;
         it.pos += blockIdx.y;
     }
+    return it;
+}
+
+// blockIdx.y = item.  Work of an item, grid-strided over blockIdx.x:
+//   [0, nq)            q pairs (head, j), rotated in place
+//   [nq, nq + nk)      k pairs, rotated and stored (engine rounding)
+//   [.., + nr)         k elements outside the rotated dims (mrope), stored as is
+//   [.., + kv_dim)     v elements, stored
+__global__ void __launch_bounds__(256) k_rope_store(const RopeParams p) {
+    const YattnRopeItem it = item_of(p);
     const uint32_t pairs = p.n_dims / 2;
     // staged in shared memory: a warp's threads index different pairs, and a divergent index into the
     // kernel's parameter bank would serialise
@@ -117,6 +133,75 @@ __global__ void __launch_bounds__(256) k_rope_store(const RopeParams p) {
     }
 }
 
+// QK-norm + RoPE + store.  blockIdx.x: q head [0, n_heads), k head [n_heads,
+// n_heads + n_kv), then v blocks of 128 elements.  128 threads; head_dim <= 256.
+__global__ void __launch_bounds__(128) k_qknorm_rope_store(const RopeParams p) {
+    const YattnRopeItem it = item_of(p);
+    const uint32_t hd = p.hd, t = threadIdx.x;
+    const uint32_t nh = p.n_heads + p.n_kv;
+    if (blockIdx.x >= nh) {   // v elements, stored as they are
+        const uint32_t e = (blockIdx.x - nh) * 128 + t;
+        if (e < p.kv_dim)
+            it.vcache[static_cast<size_t>(it.pos) * p.kv_dim + e] = engine_f32_to_f16(it.v[e]);
+        return;
+    }
+    const bool is_q = blockIdx.x < p.n_heads;
+    const uint32_t h = is_q ? blockIdx.x : blockIdx.x - p.n_heads;
+    const float* src = is_q ? it.q + static_cast<size_t>(h) * hd : it.k + static_cast<size_t>(h) * hd;
+    const void* wv = is_q ? p.q_norm_w : p.k_norm_w;
+    __shared__ float s_freq[kMaxPairs];
+    __shared__ float s_x[2 * kMaxPairs];
+    __shared__ float s_inv;
+    for (uint32_t j = t; j < p.n_dims / 2; j += 128) s_freq[j] = p.inv_freq[j];
+    for (uint32_t e = t; e < hd; e += 128) s_x[e] = src[e];
+    __syncthreads();
+    if (t == 0) {   // matvec.c:154-157: s += x*x in index order, inv = 1 / sqrt(s/n + eps)
+        float sum = 0.0f;
+        for (uint32_t i = 0; i < hd; ++i) sum = __fadd_rn(sum, __fmul_rn(s_x[i], s_x[i]));
+        s_inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(sum, static_cast<float>(hd)), p.norm_eps)));
+    }
+    __syncthreads();
+    const float inv = s_inv;
+    float y[2];
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {   // matvec.c:160/163: y = x * w * inv, left to right
+        const uint32_t e = t + 128 * i;
+        if (e < hd) {
+            const float w = p.norm_f16 ? h2f(static_cast<const uint16_t*>(wv)[e]) : static_cast<const float*>(wv)[e];
+            y[i] = __fmul_rn(__fmul_rn(s_x[e], w), inv);
+        }
+    }
+    __syncthreads();   // every x read before the normalised values replace them
+#pragma unroll
+    for (int i = 0; i < 2; ++i)
+        if (t + 128 * i < hd) s_x[t + 128 * i] = y[i];
+    __syncthreads();
+    float* qh = is_q ? it.q + static_cast<size_t>(h) * hd : nullptr;
+    uint16_t* krow = it.kcache + static_cast<size_t>(it.pos) * p.kv_dim + static_cast<size_t>(h) * hd;
+    const uint32_t pairs = p.n_dims / 2;
+    for (uint32_t u = t; u < pairs + (hd - p.n_dims); u += 128) {
+        if (u < pairs) {
+            uint32_t e0, e1;
+            pair_of(p.kind, hd, p.n_dims, u, e0, e1);
+            float a = s_x[e0], b = s_x[e1];
+            rotate(a, b, s_freq[u], it.pos);
+            if (is_q) {
+                qh[e0] = a;
+                qh[e1] = b;
+            } else {
+                krow[e0] = engine_f32_to_f16(a);
+                krow[e1] = engine_f32_to_f16(b);
+            }
+        } else {   // dims past the rotated ones (M-RoPE): normalised only
+            const uint32_t e = p.n_dims + (u - pairs);
+            if (is_q)
+                qh[e] = s_x[e];
+            else
+                krow[e] = engine_f32_to_f16(s_x[e]);
+        }
+    }
+}
+
 }  // namespace
 }  // namespace yattn
 
@@ -126,8 +211,8 @@ namespace {
 
 // Checks the geometry and launches; p.items or p.batch already set.
 int launch_rope(RopeParams& p, uint32_t n_items, uint32_t n_heads, uint32_t n_kv_heads, uint32_t head_dim,
-                uint32_t kv_dim, int rope_kind, uint32_t n_rope_dims, float theta, void* stream, char* err,
-                size_t errlen, const char* who) {
+                uint32_t kv_dim, int rope_kind, uint32_t n_rope_dims, float theta, const YattnQkNorm* qk_norm,
+                void* stream, char* err, size_t errlen, const char* who) {
     if (n_heads == 0 || n_kv_heads == 0 || n_kv_heads > n_heads || head_dim == 0 || head_dim > 2 * kMaxPairs ||
         (head_dim & 1) || kv_dim < n_kv_heads * head_dim) {
         set_err(err, errlen, "%s: bad geometry n_heads=%u n_kv_heads=%u head_dim=%u kv_dim=%u", who, n_heads,
@@ -147,6 +232,25 @@ int launch_rope(RopeParams& p, uint32_t n_items, uint32_t n_heads, uint32_t n_kv
         set_err(err, errlen, "%s: %u rows (max 65535 per launch)", who, n_items);
         return -1;
     }
+    if (qk_norm) {
+        if (!qk_norm->q_w || !qk_norm->k_w) {
+            set_err(err, errlen, "%s: QK-norm needs both the q and the k weights", who);
+            return -1;
+        }
+        if ((reinterpret_cast<uintptr_t>(qk_norm->q_w) | reinterpret_cast<uintptr_t>(qk_norm->k_w)) &
+            (qk_norm->w_f16 ? 1u : 3u)) {
+            set_err(err, errlen, "%s: QK-norm weights must be aligned to their element size", who);
+            return -1;
+        }
+        if (n_heads + n_kv_heads + (kv_dim + 127) / 128 > 0x7fffffffu) {
+            set_err(err, errlen, "%s: too many heads", who);
+            return -1;
+        }
+        p.q_norm_w = qk_norm->q_w;
+        p.k_norm_w = qk_norm->k_w;
+        p.norm_f16 = qk_norm->w_f16 ? 1u : 0u;
+        p.norm_eps = qk_norm->eps;
+    }
     p.n_items = n_items;
     p.n_heads = n_heads;
     p.n_kv = n_kv_heads;
@@ -157,6 +261,12 @@ int launch_rope(RopeParams& p, uint32_t n_items, uint32_t n_heads, uint32_t n_kv
     // the reference's expression, in the same fp32 operation order (matvec.c:895, 912, 929)
     for (uint32_t j = 0; j < n_dims / 2; ++j)
         p.inv_freq[j] = powf(theta, -2.0f * static_cast<float>(j) / static_cast<float>(n_dims));
+    if (p.q_norm_w) {
+        k_qknorm_rope_store<<<dim3(n_heads + n_kv_heads + (kv_dim + 127) / 128, n_items), 128, 0,
+                              static_cast<cudaStream_t>(stream)>>>(p);
+        YATTN_CHECK_LAUNCH(err, errlen, who);
+        return 0;
+    }
     const uint32_t work = n_heads * (n_dims / 2) + n_kv_heads * (n_dims / 2) + n_kv_heads * (head_dim - n_dims) + kv_dim;
     // one work unit per thread up to 32 blocks per item: the loop body is a chain of dependent memory
     // round trips (item, inputs, stores), so a second pass through it would double the kernel time
@@ -170,7 +280,8 @@ int launch_rope(RopeParams& p, uint32_t n_items, uint32_t n_heads, uint32_t n_kv
 
 extern "C" int yattn_rope_store_kv(const YattnRopeItem* items_dev, uint32_t n_items, uint32_t n_heads,
                                    uint32_t n_kv_heads, uint32_t head_dim, uint32_t kv_dim, int rope_kind,
-                                   uint32_t n_rope_dims, float theta, void* stream, char* err, size_t errlen) {
+                                   uint32_t n_rope_dims, float theta, const YattnQkNorm* qk_norm, void* stream,
+                                   char* err, size_t errlen) {
     if (n_items == 0) return 0;
     if (!items_dev) {
         set_err(err, errlen, "rope_store_kv: null items");
@@ -178,15 +289,15 @@ extern "C" int yattn_rope_store_kv(const YattnRopeItem* items_dev, uint32_t n_it
     }
     RopeParams p{};
     p.items = items_dev;
-    return launch_rope(p, n_items, n_heads, n_kv_heads, head_dim, kv_dim, rope_kind, n_rope_dims, theta, stream,
-                       err, errlen, "rope_store_kv");
+    return launch_rope(p, n_items, n_heads, n_kv_heads, head_dim, kv_dim, rope_kind, n_rope_dims, theta, qk_norm,
+                       stream, err, errlen, "rope_store_kv");
 }
 
 extern "C" int yattn_rope_store_kv_batch(float* q, const float* k, const float* v, uint16_t* kcache,
                                          uint16_t* vcache, uint32_t pos_start, uint32_t B, uint32_t q_stride,
                                          uint32_t n_heads, uint32_t n_kv_heads, uint32_t head_dim, uint32_t kv_dim,
-                                         int rope_kind, uint32_t n_rope_dims, float theta, void* stream, char* err,
-                                         size_t errlen) {
+                                         int rope_kind, uint32_t n_rope_dims, float theta,
+                                         const YattnQkNorm* qk_norm, void* stream, char* err, size_t errlen) {
     if (B == 0) return 0;
     if (!q || !k || !v || !kcache || !vcache) {
         set_err(err, errlen, "rope_store_kv_batch: null pointer");
@@ -209,6 +320,6 @@ extern "C" int yattn_rope_store_kv_batch(float* q, const float* k, const float* 
     p.batch.vcache = vcache;
     p.batch.pos = pos_start;
     p.q_stride = q_stride;
-    return launch_rope(p, B, n_heads, n_kv_heads, head_dim, kv_dim, rope_kind, n_rope_dims, theta, stream, err,
-                       errlen, "rope_store_kv_batch");
+    return launch_rope(p, B, n_heads, n_kv_heads, head_dim, kv_dim, rope_kind, n_rope_dims, theta, qk_norm, stream,
+                       err, errlen, "rope_store_kv_batch");
 }
