@@ -19,8 +19,9 @@ ORACLE_DIR = ROOT / "oracle"
 PORT_SO = ORACLE_DIR / "liboracle.so"
 REF_SO = ORACLE_DIR / "_ref" / "libyattn_ref.so"
 REF_GPU_SO = ORACLE_DIR / "_ref" / "libref_cuda.so"   # the reference's own cuda_kernels.cu, built for sm_100a
-# the reference source tree (present where the oracle's reference build is made; absent on GPU boxes)
-REF_TREE = Path(os.environ.get("YATTN_REF_TREE", "/root/reference"))
+# the reference source tree (present where the oracle's reference build is made; absent on GPU boxes):
+# $YATTN_REF_TREE, else a checkout named `reference` beside this repository
+REF_TREE = Path(os.environ["YATTN_REF_TREE"]) if os.environ.get("YATTN_REF_TREE") else ROOT.parent / "reference"
 
 f32p = np.ctypeslib.ndpointer(dtype=np.float32, flags="C_CONTIGUOUS")
 u16p = np.ctypeslib.ndpointer(dtype=np.uint16, flags="C_CONTIGUOUS")
