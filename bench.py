@@ -631,11 +631,15 @@ def run_prefill(args, gated: bool) -> None:
     B = r1 - r0
     qs = H * hd
 
-    def step():
+    # The config's q is fp16 by construction (drawn in fp16), so the step uses the q hi-only kernel
+    # (YATTN_PREFILL_Q_F16, which checks the claim on the device).  The default kernel -- q split into
+    # hi + lo, what the engine's fp32 projections need -- is timed beside it on the same inputs.
+    def step(q_f16=True):
         attn.attn_prefill(p.out[r0:r1], p.q[r0:r1], p.k, p.v, r0, B, H, cfg.n_kv_heads, hd, cfg.kv_dim, qs,
-                          gate=p.gate[r0:r1] if p.gate is not None else None)
+                          gate=p.gate[r0:r1] if p.gate is not None else None, q_f16=q_f16)
 
     ms, per_call, clk = _timed(step, args, stream, world, dist, local, graph=True, flush_l2=True)
+    ms_lo, per_call_lo, _ = _timed(lambda: step(False), args, stream, world, dist, local, graph=True, flush_l2=True)
     flops = cfg.causal_flops() * world
     my_flops = cfg.causal_flops()
     e2e = None
@@ -665,7 +669,13 @@ def run_prefill(args, gated: bool) -> None:
     roof = {"bound": "tensor", "achieved": round(achieved, 1), "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
             "frac": round(achieved / peaks["bf16_tflops"], 4),
             "traffic": NCU_TRAFFIC["gated_prefill" if gated else "prefill"],
-            "kernel": f"k_prefill<{hd}>", "peak_source": src + " (dense bf16 burst)"}
+            "kernel": f"k_prefill<{hd},QLO=false> (q hi only)", "peak_source": src + " (dense bf16 burst)"}
+    fp32_q = {"value": round(flops / (ms_lo / 1e3) / 1e12, 4), "unit": "TFLOP/s", "ms_per_step": round(ms_lo, 5),
+              "frac": round(my_flops / (per_call_lo / 1e3) / 1e12 / peaks["bf16_tflops"], 4),
+              "kernel": f"k_prefill<{hd},QLO=true> (q hi + lo: the default, and the drop-in's, for fp32 q)"}
+    st = attn.device_status()
+    if st != 0:
+        raise RuntimeError(f"device status {st}")
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         cpu = cpu_prefill_rate(cfg, args.cpu_budget)
@@ -676,9 +686,11 @@ def run_prefill(args, gated: bool) -> None:
                                 "head_dim": hd, "gated": gated, "flops": flops,
                                 "parallelism": f"data-parallel x{world}: one {S}-token prompt per GPU, no collective",
                                 "launch": "CUDA graph replay of the step (device-timed value)",
+                                "q": "fp16-valued (the config's q/k/v are drawn in fp16): YATTN_PREFILL_Q_F16",
                                 "l2": ("L2 scrubbed between timed steps outside the step's events (256 MB write, "
                                        "then 256 MB read of another buffer)")},
-                               roof, args.steps, clk, e2e, cpu, scaling="weak")), flush=True)
+                               roof, args.steps, clk, e2e, cpu, scaling="weak") | {"fp32_q_kernel": fp32_q}),
+              flush=True)
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()

@@ -44,9 +44,10 @@ void yattn_clear_error(void);
 /* Reads (and with clear != 0 resets) the device-side status word of the
  * current device: 0 = no kernel gave up; otherwise the code of the first
  * bounded wait that timed out (a kernel that times out returns early instead
- * of hanging), or 103 if a decode run met a malformed work item (q or gate
+ * of hanging), 103 if a decode run met a malformed work item (q or gate
  * not 16-byte aligned; with a pool, K/V not at a row of the pool) and
- * stopped.  It covers the allocation-free decode too, whose word sits in its
+ * stopped, or 202 if a prefill told YATTN_PREFILL_Q_F16 met a q value that is
+ * not an fp16 value.  It covers the allocation-free decode too, whose word sits in its
  * static scratch; polling creates neither word.  Synchronises the legacy
  * default stream. */
 int yattn_device_status(int* status_out, int clear, char* err, size_t errlen);
@@ -67,11 +68,10 @@ void cuda_k_attn_decode(float* att_out,
  * B query tokens at positions pos_start..pos_start+B-1 (q row b at
  * q + b*q_stride); token b attends keys 0..pos_start+b.  Any B (the reference
  * caps a chunk at 64).  Flash attention on tcgen05 tensor cores with fp32
- * accumulation.  q is split into fp16 hi + lo planes (about 22 significant
- * bits) in every 128-row query tile that holds a value fp16 does not represent
- * exactly; a tile of fp16-exact q uses the hi plane alone.  |q| must stay below
- * 65504.  P is split the same way.  Needs 16-byte aligned pointers,
- * q_stride % 4 == 0, kv_dim % 8 == 0, head_dim 64/128/256. */
+ * accumulation.  q (the engine's fp32 projections) is split into fp16 hi + lo
+ * planes, about 22 significant bits, and both are multiplied into the scores;
+ * |q| must stay below 65504.  P is split the same way.  Needs 16-byte aligned
+ * pointers, q_stride % 4 == 0, kv_dim % 8 == 0, head_dim 64/128/256. */
 void cuda_k_attn_prefill(float* att_out,
                          const float* q, const uint16_t* kcache, const uint16_t* vcache,
                          uint32_t pos_start, uint32_t B, uint32_t n_heads, uint32_t n_kv_heads,
@@ -289,12 +289,20 @@ int yattn_attn_decode(float* att_out, const float* q, const uint16_t* kcache,
                       uint32_t n_heads, uint32_t n_kv_heads, uint32_t head_dim, uint32_t kv_dim,
                       void* stream, char* err, size_t errlen);
 
-/* Error-returning form of cuda_k_attn_prefill with an explicit stream and the
- * qwen35 output gate (gate rows laid out like q, or NULL; engine.c:958-960). */
+/* flags of yattn_attn_prefill: every q value is exactly an fp16 value (q built
+ * from fp16 data).  The kernel then multiplies q's hi plane alone (no lo plane,
+ * three TMEM score buffers instead of two): faster, with the same results for
+ * such q.  It checks the claim; a q value that is not an fp16 value sets
+ * yattn_device_status to 202 and that tile runs on the hi plane only. */
+#define YATTN_PREFILL_Q_F16 1u
+
+/* Error-returning form of cuda_k_attn_prefill with an explicit stream, the
+ * qwen35 output gate (gate rows laid out like q, or NULL; engine.c:958-960) and
+ * flags (0, or YATTN_PREFILL_Q_F16). */
 int yattn_attn_prefill(float* att_out, const float* q, const uint16_t* kcache,
                        const uint16_t* vcache, const float* gate, uint32_t pos_start, uint32_t B,
                        uint32_t n_heads, uint32_t n_kv_heads, uint32_t head_dim, uint32_t kv_dim,
-                       uint32_t q_stride, void* stream, char* err, size_t errlen);
+                       uint32_t q_stride, uint32_t flags, void* stream, char* err, size_t errlen);
 
 /* Allocation-free form of yattn_attn_decode.  No counterpart in the reference:
  * it exists for callers that cannot call cudaMalloc while decoding (a serving

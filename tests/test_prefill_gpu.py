@@ -3,9 +3,10 @@
 Tolerance: per element |gpu - cpu| <= 2e-3 * max(|cpu|, f * rms(cpu)), f = 1e-3
 unless the CPU's own fp32 rounding against a float64 evaluation of the same
 inputs (oracle.exact_prefill) needs more (oracle.noise_floor).  q is either
-fp16-exact (config 2's fixture; the kernel's hi plane holds it exactly) or
-plain fp32, as the engine passes its projections (cuda_fwd.c:220): then the
-kernel adds a lo plane.  P is held as fp16 hi + lo, accumulation is fp32.
+plain fp32, as the engine passes its projections (cuda_fwd.c:220), for the
+default kernel (q split into fp16 hi + lo), or fp16-exact (config 2's fixture),
+for which both the default kernel and the hi-only kernel a caller selects with
+YATTN_PREFILL_Q_F16 are checked.  P is held as fp16 hi + lo, accumulation fp32.
 """
 import numpy as np
 import pytest
@@ -53,14 +54,15 @@ def test_prefill_matches_oracle(dev, H, KV, hd, P0, B):
     from yllm_b200 import attn
 
     c = _case(dev, H, KV, hd, P0, B, seed=H + hd + P0 + B)
-    out = torch.zeros(B, c["qs"], device=dev)
-    attn.attn_prefill(out, c["tq"], c["tk"], c["tv"], P0, B, H, KV, hd, c["kd"], c["qs"])
     want = oracle.attn_prefill(c["q"], c["k"], c["v"], P0, B, H, KV, hd, c["kd"], c["qs"])
     exact = oracle.exact_prefill(c["q"], c["k"], c["v"], P0, B, H, KV, hd, c["kd"], c["qs"])
-    torch.cuda.synchronize()
-    oracle.assert_close(out.cpu().numpy()[:, :H * hd], want[:, :H * hd], what=f"prefill H{H} KV{KV} hd{hd} P0{P0} B{B}",
-                        exact=exact[:, :H * hd])
-    assert attn.device_status() == 0
+    for q_f16 in (False, True):   # the default kernel and the hi-only one (q here is fp16-exact)
+        out = torch.zeros(B, c["qs"], device=dev)
+        attn.attn_prefill(out, c["tq"], c["tk"], c["tv"], P0, B, H, KV, hd, c["kd"], c["qs"], q_f16=q_f16)
+        torch.cuda.synchronize()
+        oracle.assert_close(out.cpu().numpy()[:, :H * hd], want[:, :H * hd],
+                            what=f"prefill H{H} KV{KV} hd{hd} P0{P0} B{B} q_f16={q_f16}", exact=exact[:, :H * hd])
+        assert attn.device_status() == 0
 
 
 def test_prefill_strides_and_dropin(dev):
@@ -98,15 +100,18 @@ def test_prefill_config2_full(dev):
     from yllm_b200.configs import CFG2 as c
 
     p = fixtures.prefill_inputs(c, device=dev)
-    attn.attn_prefill(p.out, p.q, p.k, p.v, 0, c.seq_len, c.n_heads, c.n_kv_heads, c.head_dim, c.kv_dim,
-                      c.n_heads * c.head_dim)
-    torch.cuda.synchronize()
     f = oracle.prefill_fixture(c)
     want = oracle.attn_prefill(f["q"], f["k"], f["v"], 0, c.seq_len, c.n_heads, c.n_kv_heads, c.head_dim, c.kv_dim,
                                c.n_heads * c.head_dim)
     exact = oracle.exact_prefill(f["q"], f["k"], f["v"], 0, c.seq_len, c.n_heads, c.n_kv_heads, c.head_dim,
                                  c.kv_dim, c.n_heads * c.head_dim)
-    oracle.assert_close(p.out.cpu().numpy(), want, what="config2 prefill", exact=exact)
+    for q_f16 in (True, False):   # the config's q is fp16: the hi-only kernel (the bench's) and the default one
+        p.out.zero_()
+        attn.attn_prefill(p.out, p.q, p.k, p.v, 0, c.seq_len, c.n_heads, c.n_kv_heads, c.head_dim, c.kv_dim,
+                          c.n_heads * c.head_dim, q_f16=q_f16)
+        torch.cuda.synchronize()
+        oracle.assert_close(p.out.cpu().numpy(), want, what=f"config2 prefill q_f16={q_f16}", exact=exact)
+    assert attn.device_status() == 0
 
 
 def test_prefill_config5_gated_full(dev):
@@ -118,14 +123,18 @@ def test_prefill_config5_gated_full(dev):
 
     S, H, hd = c.seq_len, c.n_heads, c.head_dim
     p = fixtures.prefill_inputs(c, device=dev)
-    attn.attn_prefill(p.out, p.q, p.k, p.v, 0, S, H, c.n_kv_heads, hd, c.kv_dim, H * hd, gate=p.gate)
-    torch.cuda.synchronize()
     f = oracle.prefill_fixture(c)
-    got = p.out.cpu().numpy()
     want = oracle.attn_prefill(f["q"], f["k"], f["v"], 0, S, H, c.n_kv_heads, hd, c.kv_dim, H * hd, gate=f["gate"])
     exact = oracle.exact_prefill(f["q"], f["k"], f["v"], 0, S, H, c.n_kv_heads, hd, c.kv_dim, H * hd,
                                  gate=f["gate"])
-    oracle.assert_close(got, want, what="config5 gated prefill (all 4096 rows)", exact=exact)
+    for q_f16 in (False, True):   # the config's q is fp16: the default kernel and the hi-only one
+        p.out.zero_()
+        attn.attn_prefill(p.out, p.q, p.k, p.v, 0, S, H, c.n_kv_heads, hd, c.kv_dim, H * hd, gate=p.gate,
+                          q_f16=q_f16)
+        torch.cuda.synchronize()
+        got = p.out.cpu().numpy()
+        oracle.assert_close(got, want, what=f"config5 gated prefill (all 4096 rows) q_f16={q_f16}", exact=exact)
+    assert attn.device_status() == 0
     B = 64
     chunk = oracle.attn_prefill(f["q"][S - B:], f["k"], f["v"], S - B, B, H, c.n_kv_heads, hd, c.kv_dim, H * hd,
                                 gate=f["gate"][S - B:])
@@ -169,9 +178,11 @@ def test_prefill_fp32_q_other_head_dims(dev, H, KV, hd, P0, B, gated):
     assert attn.device_status() == 0
 
 
-def test_prefill_mixed_tiles(dev):
-    """One call whose first query tile is fp16-exact and second is not: each
-    tile takes its own path (hi alone, or hi + lo) in the same launch."""
+def test_prefill_q_f16_flag_checks_its_claim(dev):
+    """YATTN_PREFILL_Q_F16 promises fp16-exact q.  A call whose first query tile
+    keeps that promise and whose second breaks it reports device status 202
+    (the broken tile runs on q's hi plane alone); the same q without the flag
+    matches the oracle."""
     from yllm_b200 import attn
 
     H, KV, hd, B = 8, 2, 128, 256
@@ -180,11 +191,17 @@ def test_prefill_mixed_tiles(dev):
     q[:128] = oracle.f16_to_f32(oracle.f32_to_f16(q[:128])).reshape(128, -1)
     tq = torch.from_numpy(q).to(dev)
     out = torch.zeros(B, c["qs"], device=dev)
+    assert attn.device_status() == 0
+    attn.attn_prefill(out, tq, c["tk"], c["tv"], 0, B, H, KV, hd, c["kd"], c["qs"], q_f16=True)
+    torch.cuda.synchronize()
+    assert attn.device_status() == 202
+    assert attn.device_status() == 0
     attn.attn_prefill(out, tq, c["tk"], c["tv"], 0, B, H, KV, hd, c["kd"], c["qs"])
     want = oracle.attn_prefill(q, c["k"], c["v"], 0, B, H, KV, hd, c["kd"], c["qs"])
     exact = oracle.exact_prefill(q, c["k"], c["v"], 0, B, H, KV, hd, c["kd"], c["qs"])
     torch.cuda.synchronize()
-    oracle.assert_close(out.cpu().numpy(), want, what="mixed fp16/fp32 q tiles", exact=exact)
+    oracle.assert_close(out.cpu().numpy(), want, what="half fp16-exact, half fp32 q", exact=exact)
+    assert attn.device_status() == 0
 
 
 def test_prefill_last_row_equals_decode(dev):

@@ -90,7 +90,7 @@ PROTOS = {
     "yattn_device_status": (C.c_int, [C.POINTER(C.c_int), C.c_int, *E]),
     "cuda_k_attn_decode": (None, [vp, vp, vp, vp, u32, u32, u32, u32, u32]),
     "cuda_k_attn_prefill": (None, [vp, vp, vp, vp, u32, u32, u32, u32, u32, u32, u32]),
-    "yattn_attn_prefill": (C.c_int, [vp, vp, vp, vp, vp, u32, u32, u32, u32, u32, u32, u32, vp, *E]),
+    "yattn_attn_prefill": (C.c_int, [vp, vp, vp, vp, vp, u32, u32, u32, u32, u32, u32, u32, u32, vp, *E]),
     "cuda_k_store_kv": (None, [vp, vp, vp, vp, u32, u32]),
     "cuda_k_store_kv_batch": (None, [vp, vp, vp, vp, u32, u32, u32]),
     "yattn_decode_plan": (

@@ -70,16 +70,22 @@ def cuda_k_attn_prefill(att_out: torch.Tensor, q: torch.Tensor, kcache: torch.Te
               pos_start, B, n_heads, n_kv_heads, head_dim, kv_dim, q_stride)
 
 
+PREFILL_Q_F16 = 1   # YATTN_PREFILL_Q_F16: every q value is an fp16 value
+
+
 def attn_prefill(att_out: torch.Tensor, q: torch.Tensor, kcache: torch.Tensor, vcache: torch.Tensor,
                  pos_start: int, B: int, n_heads: int, n_kv_heads: int, head_dim: int, kv_dim: int, q_stride: int,
-                 gate: Optional[torch.Tensor] = None, stream=None) -> None:
-    """Causal prefill of B tokens at pos_start (keys 0..pos_start+b), optional qwen35 gate."""
+                 gate: Optional[torch.Tensor] = None, q_f16: bool = False, stream=None) -> None:
+    """Causal prefill of B tokens at pos_start (keys 0..pos_start+b), optional qwen35 gate.  q_f16=True
+    promises that every q value is exactly an fp16 value (the kernel then skips q's lo plane; it checks the
+    promise and reports a broken one as device status 202)."""
     _need(att_out, torch.float32, "att_out")
     _need(q, torch.float32, "q")
     if gate is not None:
         _need(gate, torch.float32, "gate")
     call("yattn_attn_prefill", att_out.data_ptr(), q.data_ptr(), kcache.data_ptr(), vcache.data_ptr(), _ptr(gate),
-         pos_start, B, n_heads, n_kv_heads, head_dim, kv_dim, q_stride, _stream(stream))
+         pos_start, B, n_heads, n_kv_heads, head_dim, kv_dim, q_stride, PREFILL_Q_F16 if q_f16 else 0,
+         _stream(stream))
 
 
 def cuda_k_store_kv(kcache: torch.Tensor, vcache: torch.Tensor, k: torch.Tensor, v: torch.Tensor, pos: int,

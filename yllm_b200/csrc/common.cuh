@@ -54,6 +54,7 @@ enum : int {
     ST_DECODE_EMPTY_TIMEOUT = 102,
     ST_DECODE_BAD_ITEM = 103,   // q / gate not 16-byte aligned, or (pooled) K/V not rows of the pool
     ST_PREFILL_TIMEOUT = 201,
+    ST_PREFILL_Q_NOT_F16 = 202,  // YATTN_PREFILL_Q_F16 given, but a q value is not an fp16 value
     ST_GDN_TIMEOUT = 301,
     ST_GEMV_TIMEOUT = 501,
     ST_EXCHANGE_TIMEOUT = 401,

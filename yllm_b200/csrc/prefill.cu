@@ -11,11 +11,13 @@
 //   0-7  softmax: row i of the tile (TMEM lane i) belongs to warps i/32 and
 //        i/32 + 4, which split each key block's columns in halves.  They load
 //        the fp32 Q tile once: Q_hi = fp16(q) goes to smem (SWIZZLE_128B
-//        K-major).  If any q of the tile is not exactly an fp16 value (the
-//        engine passes fp32 projections), Q_lo = fp16(q - Q_hi) goes to free
-//        TMEM columns and S gets a second product Q_lo K^T (TS form), so q
-//        keeps about 22 significant bits; the tile then runs with two S
-//        buffers instead of three to make room.  Per key
+//        K-major).  The default kernel (QLO) also writes Q_lo = fp16(q - Q_hi)
+//        to free TMEM columns, and S gets a second product Q_lo K^T (TS form),
+//        so q keeps about 22 significant bits, as the engine's fp32 projections
+//        need; it runs with two S buffers instead of three to make room.  A
+//        caller whose q is fp16 by construction asks for the hi-only kernel,
+//        which checks that claim (status 202 if a q value is not an fp16
+//        value) and runs three S buffers and no second product.  Per key
 //        block each reads its half of S from TMEM, applies the causal mask
 //        (diagonal blocks only), and the two halves of a row combine their
 //        maxima through shared memory; the online softmax runs in the log2
@@ -26,8 +28,8 @@
 //        Each half keeps its own partial row sum; the epilogue adds them.
 //   8    TMA for K blocks, 10 TMA for V blocks: separate rings, no multicast.
 //   9    MMA: one thread issues S(j) = Q K(j)^T (A, B from smem; + Q_lo K(j)^T
-//        with A from TMEM when the tile needs it) into a ring of NSB (3, or 2
-//        with Q_lo) TMEM S buffers and O += P_hi V + P_lo V with A = P read
+//        with A from TMEM in the QLO kernel) into a ring of NSB (3, or 2 with
+//        Q_lo) TMEM S buffers and O += P_hi V + P_lo V with A = P read
 //        straight from TMEM (B = V from smem).  S runs up to NSB blocks ahead of
 //        the softmax; the tensor core runs its MMAs in issue order, so S(j+NSB)
 //        cannot overwrite P(j) before PV(j) has read it.
@@ -94,7 +96,6 @@ template <int KST, int VST> struct Bars {
     uint64_t o_done, q_full, mma_drain;
     uint32_t tmem_base;
     int abort_flag;
-    int qlo;                          // the tile needs Q_lo (set before q_full completes)
 };
 
 // One TMA producer: block j of a K or V stream into a DEPTH-deep ring.
@@ -125,7 +126,7 @@ __device__ __forceinline__ void produce(const CUtensorMap* map, uint8_t* ring, u
 
 __device__ __forceinline__ uint32_t h2_bits(__half2 h) { return *reinterpret_cast<uint32_t*>(&h); }
 
-template <int HD>
+template <int HD, bool QLO>
 __global__ void __launch_bounds__(kPThreads, 1)
     k_prefill(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
               const __grid_constant__ CUtensorMap tmO, const PrefillParams p) {
@@ -174,7 +175,6 @@ __global__ void __launch_bounds__(kPThreads, 1)
         mbar_init(&bars->q_full, 8);
         mbar_init(&bars->mma_drain, 1);
         bars->abort_flag = 0;
-        bars->qlo = 0;
         fence_mbar_init();
     }
     if (warp == 0) tmem_alloc(&bars->tmem_base, C::TMEM_COLS);
@@ -200,72 +200,73 @@ __global__ void __launch_bounds__(kPThreads, 1)
             const uint64_t dv0 = sdesc_sw128(sV, BN * 128, 1024);
             bool ok = mbar_wait_bounded(&bars->q_full, 0, p.status, ST_PREFILL_TIMEOUT, abort_flag);
             tc_fence_after();
-            const bool qlo = ok && bars->qlo != 0;
-            const uint32_t nsb = qlo ? C::NSB_QLO : C::NSB;
-            // S buffer and phase of the next S(jj) and of the next PV(jj): both advance by one
-            // block per call (no division by the runtime buffer count)
-            uint32_t s_sb = 0, pv_sb = 0, pv_ph = 0;
-            // S(jj) = Q K(jj)^T into S buffer jj % nsb.  That buffer last held P(jj - nsb), whose PV
-            // product was issued earlier; the tensor core runs one thread's MMAs in issue order.
-            auto do_s = [&](uint32_t jj) -> bool {
-                const int s = jj % KST;
-                if (!mbar_wait_bounded(&bars->k_full[s], (jj / KST) & 1u, p.status, ST_PREFILL_TIMEOUT, abort_flag))
-                    return false;
-                const uint32_t sb = s_sb;
-                if (++s_sb == nsb) s_sb = 0;
-                tc_fence_after();
-                const uint64_t dk = dk0 + ((s * C::KV_BYTES) >> 4);
-#pragma unroll
-                for (int kk = 0; kk < HD / 16; ++kk) {
-                    const uint64_t a = dq0 + (((kk >> 2) * (BM * 128) + (kk & 3) * 32) >> 4);
-                    const uint64_t b = dk + (((kk >> 2) * (BN * 128) + (kk & 3) * 32) >> 4);
-                    umma_f16(tmem + C::COL_S + sb * BN, a, b, IDESC_QK, kk > 0 ? 1u : 0u);
-                }
-                if (qlo) {   // + Q_lo K^T, A (16-key chunk kk of Q_lo) from TMEM
-#pragma unroll
+            {
+                constexpr uint32_t nsb = QLO ? C::NSB_QLO : C::NSB;
+                // S buffer and phase of the next S(jj) and of the next PV(jj): both advance by one
+                // block per call (no division by the runtime buffer count)
+                uint32_t s_sb = 0, pv_sb = 0, pv_ph = 0;
+                // S(jj) = Q K(jj)^T into S buffer jj % nsb.  That buffer last held P(jj - nsb), whose PV
+                // product was issued earlier; the tensor core runs one thread's MMAs in issue order.
+                auto do_s = [&](uint32_t jj) -> bool {
+                    const int s = jj % KST;
+                    if (!mbar_wait_bounded(&bars->k_full[s], (jj / KST) & 1u, p.status, ST_PREFILL_TIMEOUT, abort_flag))
+                        return false;
+                    const uint32_t sb = s_sb;
+                    if (++s_sb == nsb) s_sb = 0;
+                    tc_fence_after();
+                    const uint64_t dk = dk0 + ((s * C::KV_BYTES) >> 4);
+    #pragma unroll
                     for (int kk = 0; kk < HD / 16; ++kk) {
+                        const uint64_t a = dq0 + (((kk >> 2) * (BM * 128) + (kk & 3) * 32) >> 4);
                         const uint64_t b = dk + (((kk >> 2) * (BN * 128) + (kk & 3) * 32) >> 4);
-                        umma_f16_ts(tmem + C::COL_S + sb * BN, tmem + C::qlo_col(kk), b, IDESC_QK, 1u);
+                        umma_f16(tmem + C::COL_S + sb * BN, a, b, IDESC_QK, kk > 0 ? 1u : 0u);
                     }
-                }
-                umma_commit(&bars->s_full[sb]);
-                umma_commit(&bars->k_empty[s]);
-                return true;
-            };
-            // O += P_hi V + P_lo V with A = P(jj) read from TMEM: keys [16kk, 16kk+16) of a plane
-            // are the 8 columns at 32*(kk/2) + 16*plane + 8*(kk%2) of the block's S buffer.
-            auto do_pv = [&](uint32_t jj) -> bool {
-                const int s = jj % VST;
-                const uint32_t sb = pv_sb, ph = pv_ph;
-                if (!mbar_wait_bounded(&bars->p_full[sb], ph, p.status, ST_PREFILL_TIMEOUT, abort_flag) ||
-                    !mbar_wait_bounded(&bars->v_full[s], (jj / VST) & 1u, p.status, ST_PREFILL_TIMEOUT, abort_flag))
-                    return false;
-                if (++pv_sb == nsb) {
-                    pv_sb = 0;
-                    pv_ph ^= 1u;
-                }
-                tc_fence_after();
-                const uint32_t pcol = tmem + C::COL_S + sb * BN;
-                const uint64_t dv = dv0 + ((s * C::KV_BYTES) >> 4);
-#pragma unroll
-                for (int plane = 0; plane < 2; ++plane) {
-#pragma unroll
-                    for (int kk = 0; kk < BN / 16; ++kk) {
-                        const uint64_t b = dv + ((kk * 16 * 128) >> 4);
-                        umma_f16_ts(tmem + C::COL_O, pcol + 32 * (kk >> 1) + 16 * plane + 8 * (kk & 1), b, IDESC_PV,
-                                    (jj > 0 || plane > 0 || kk > 0) ? 1u : 0u);
+                    if constexpr (QLO) {   // + Q_lo K^T, A (16-key chunk kk of Q_lo) from TMEM
+    #pragma unroll
+                        for (int kk = 0; kk < HD / 16; ++kk) {
+                            const uint64_t b = dk + (((kk >> 2) * (BN * 128) + (kk & 3) * 32) >> 4);
+                            umma_f16_ts(tmem + C::COL_S + sb * BN, tmem + C::qlo_col(kk), b, IDESC_QK, 1u);
+                        }
                     }
+                    umma_commit(&bars->s_full[sb]);
+                    umma_commit(&bars->k_empty[s]);
+                    return true;
+                };
+                // O += P_hi V + P_lo V with A = P(jj) read from TMEM: keys [16kk, 16kk+16) of a plane
+                // are the 8 columns at 32*(kk/2) + 16*plane + 8*(kk%2) of the block's S buffer.
+                auto do_pv = [&](uint32_t jj) -> bool {
+                    const int s = jj % VST;
+                    const uint32_t sb = pv_sb, ph = pv_ph;
+                    if (!mbar_wait_bounded(&bars->p_full[sb], ph, p.status, ST_PREFILL_TIMEOUT, abort_flag) ||
+                        !mbar_wait_bounded(&bars->v_full[s], (jj / VST) & 1u, p.status, ST_PREFILL_TIMEOUT, abort_flag))
+                        return false;
+                    if (++pv_sb == nsb) {
+                        pv_sb = 0;
+                        pv_ph ^= 1u;
+                    }
+                    tc_fence_after();
+                    const uint32_t pcol = tmem + C::COL_S + sb * BN;
+                    const uint64_t dv = dv0 + ((s * C::KV_BYTES) >> 4);
+    #pragma unroll
+                    for (int plane = 0; plane < 2; ++plane) {
+    #pragma unroll
+                        for (int kk = 0; kk < BN / 16; ++kk) {
+                            const uint64_t b = dv + ((kk * 16 * 128) >> 4);
+                            umma_f16_ts(tmem + C::COL_O, pcol + 32 * (kk >> 1) + 16 * plane + 8 * (kk & 1), b, IDESC_PV,
+                                        (jj > 0 || plane > 0 || kk > 0) ? 1u : 0u);
+                        }
+                    }
+                    umma_commit(&bars->v_empty[s]);
+                    umma_commit(&bars->pv_done[sb]);
+                    return true;
+                };
+                // Queue: S(0..nsb-1), then PV(j), S(j+nsb) as each P(j) arrives, so the next S blocks
+                // are ready before the softmax asks for them.
+                for (uint32_t j = 0; ok && j < nkb && j < nsb; ++j) ok = do_s(j);
+                for (uint32_t j = 0; ok && j < nkb; ++j) {
+                    ok = do_pv(j);
+                    if (ok && j + nsb < nkb) ok = do_s(j + nsb);
                 }
-                umma_commit(&bars->v_empty[s]);
-                umma_commit(&bars->pv_done[sb]);
-                return true;
-            };
-            // Queue: S(0..nsb-1), then PV(j), S(j+nsb) as each P(j) arrives, so the next S blocks
-            // are ready before the softmax asks for them.
-            for (uint32_t j = 0; ok && j < nkb && j < nsb; ++j) ok = do_s(j);
-            for (uint32_t j = 0; ok && j < nkb; ++j) {
-                ok = do_pv(j);
-                if (ok && j + nsb < nkb) ok = do_s(j + nsb);
             }
             if (ok) umma_commit(&bars->o_done);
             // drain: every MMA issued so far completes before TMEM is freed
@@ -282,7 +283,6 @@ __global__ void __launch_bounds__(kPThreads, 1)
         // ---- Q tile: fp32 -> Q_hi = fp16(q) (smem, swizzled K-major) and, if any q of the
         //      tile is not an fp16 value, Q_lo = fp16(q - Q_hi) (TMEM); 256 threads, one batch
         //      of loads in flight each ----
-        bool qlo;
         {
             constexpr int C4 = HD / 4;
             constexpr int QITER = BM * C4 / 256;
@@ -306,12 +306,18 @@ __global__ void __launch_bounds__(kPThreads, 1)
                 const float2 f0 = __half22float2(h0), f1 = __half22float2(h1);
                 qh[i].x = h2_bits(h0);
                 qh[i].y = h2_bits(h1);
-                ql[i].x = h2_bits(__floats2half2_rn(v[i].x - f0.x, v[i].y - f0.y));
-                ql[i].y = h2_bits(__floats2half2_rn(v[i].z - f1.x, v[i].w - f1.y));
-                any_lo = any_lo || (f0.x != v[i].x) || (f0.y != v[i].y) || (f1.x != v[i].z) || (f1.y != v[i].w);
+                if constexpr (QLO) {
+                    ql[i].x = h2_bits(__floats2half2_rn(v[i].x - f0.x, v[i].y - f0.y));
+                    ql[i].y = h2_bits(__floats2half2_rn(v[i].z - f1.x, v[i].w - f1.y));
+                } else {
+                    any_lo = any_lo || (f0.x != v[i].x) || (f0.y != v[i].y) || (f1.x != v[i].z) || (f1.y != v[i].w);
+                }
             }
-            qlo = named_bar_or(5, 256, any_lo);   // the same answer in every softmax thread
-            if (qlo) {
+            if constexpr (!QLO) {
+                // the caller said q is fp16 by construction: a value that is not is reported
+                // (status 202) and the tile runs on Q_hi alone
+                if (__any_sync(0xffffffffu, any_lo) && lane == 0) atomicCAS(p.status, 0, ST_PREFILL_Q_NOT_F16);
+            } else {
                 // Q_lo goes through the Q buffer (this thread's elements), so the thread that owns
                 // a row's TMEM lane can pick it up; Q_hi then overwrites it.
 #pragma unroll
@@ -337,7 +343,6 @@ __global__ void __launch_bounds__(kPThreads, 1)
                 }
                 tmem_wait_st();
                 named_bar_sync(5, 256);           // every row's Q_lo is read before Q_hi replaces it
-                if (threadIdx.x == 0) bars->qlo = 1;
             }
 #pragma unroll
             for (int i = 0; i < QITER; ++i) {
@@ -349,10 +354,6 @@ __global__ void __launch_bounds__(kPThreads, 1)
             __syncwarp();
             if (lane == 0) mbar_arrive(&bars->q_full);
         }
-        const uint32_t nsb = qlo ? C::NSB_QLO : C::NSB;
-        uint32_t sb = 0, sph = 0;            // S buffer of block j and its phase
-        uint32_t pb = 0, pph = 0;            // the same for block j - 1 (its PV completion)
-
         const uint32_t qpos = qpos0 + r;
         const float sl2 = p.scale_log2;
         float m_run = -INFINITY, l_run = 0.f;                        // m_run in scaled log2 units; l_run: this half
@@ -360,106 +361,111 @@ __global__ void __launch_bounds__(kPThreads, 1)
         // The two halves of a row meet at a named barrier once per block.  Every wait result
         // goes through that barrier (AND-reduced), so both halves always leave together and
         // neither is left at a barrier its partner will not reach.
-        for (uint32_t j = 0; j < nkb; ++j) {
-            const bool got = warp_wait_bounded(&bars->s_full[sb], sph, p.status, ST_PREFILL_TIMEOUT, abort_flag);
-            const uint32_t scol = trow + C::COL_S + sb * BN + h * HB;  // this half's columns of S(j)
-            float sv[HB];
-            if (got) {
-                tc_fence_after();
-#pragma unroll
-                for (int c = 0; c < HB / 32; ++c) {
-                    uint32_t rr[32];
-                    tmem_ld32(scol + c * 32, rr);
-#pragma unroll
-                    for (int i = 0; i < 32; ++i) sv[c * 32 + i] = __uint_as_float(rr[i]);
+        {
+            constexpr uint32_t nsb = QLO ? C::NSB_QLO : C::NSB;
+            uint32_t sb = 0, sph = 0;            // S buffer of block j and its phase
+            uint32_t pb = 0, pph = 0;            // the same for block j - 1 (its PV completion)
+            for (uint32_t j = 0; j < nkb; ++j) {
+                const bool got = warp_wait_bounded(&bars->s_full[sb], sph, p.status, ST_PREFILL_TIMEOUT, abort_flag);
+                const uint32_t scol = trow + C::COL_S + sb * BN + h * HB;  // this half's columns of S(j)
+                float sv[HB];
+                if (got) {
+                    tc_fence_after();
+    #pragma unroll
+                    for (int c = 0; c < HB / 32; ++c) {
+                        uint32_t rr[32];
+                        tmem_ld32(scol + c * 32, rr);
+    #pragma unroll
+                        for (int i = 0; i < 32; ++i) sv[c * 32 + i] = __uint_as_float(rr[i]);
+                    }
+                    tmem_wait_ld();
+                } else {
+    #pragma unroll
+                    for (int c = 0; c < HB; ++c) sv[c] = -INFINITY;
                 }
-                tmem_wait_ld();
-            } else {
-#pragma unroll
-                for (int c = 0; c < HB; ++c) sv[c] = -INFINITY;
-            }
-            // ---- causal mask (diagonal blocks only), row max of raw scores over both halves ----
-            const uint32_t kbase = j * BN + h * HB;
-            if (j * BN + BN - 1 > qpos0) {
-#pragma unroll
-                for (int c = 0; c < HB; ++c)
-                    if (kbase + c > qpos) sv[c] = -INFINITY;
-            }
-            float mx4[4] = {sv[0], sv[1], sv[2], sv[3]};
-#pragma unroll
-            for (int c = 4; c < HB; c += 4) {
-                mx4[0] = fmaxf(mx4[0], sv[c]);
-                mx4[1] = fmaxf(mx4[1], sv[c + 1]);
-                mx4[2] = fmaxf(mx4[2], sv[c + 2]);
-                mx4[3] = fmaxf(mx4[3], sv[c + 3]);
-            }
-            float* xb = xch + (j & 1) * (2 * BM);                    // two slots alternate by block parity
-            xb[h * BM + r] = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3]));
-            if (!named_bar_and(1 + qd, 64, got)) {                   // the row's two halves
-                ok = false;
-                break;
-            }
-            const float mx = fmaxf(xb[r], xb[BM + r]) * sl2;
-            const float m_new = fmaxf(m_run, mx);
-            const bool grow = m_new > m_run + 8.0f;                  // keep a stale max up to 2^8 headroom
-            const float m_use = grow ? m_new : m_run;
-            const float alpha = grow ? ex2_approx(m_run - m_use) : 1.0f;
-            // a row whose keys so far are all masked keeps m = -inf and gets p = 0
-            const float m_sub = (m_use == -INFINITY) ? 0.f : m_use;
-            // ---- p = 2^(s*scale - m): one FFMA + ex2 per element; P hi/lo over this half's S ----
-            // pairs of elements in packed fp32x2 arithmetic (FFMA2 / FADD2): half the FMA, add and
-            // subtract instructions of the scalar form
-            const float2 sl2x2 = make_float2(sl2, sl2), negm = make_float2(-m_sub, -m_sub);
-            const float2 neg1 = make_float2(-1.f, -1.f);
-            float2 rs2[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
-#pragma unroll
-            for (int c = 0; c < HB / 32; ++c) {   // 32 keys -> 16 columns of P_hi, then 16 of P_lo
-                uint32_t hi[16], lo[16];
-#pragma unroll
-                for (int i = 0; i < 16; ++i) {
-                    const float2 x = __ffma2_rn(make_float2(sv[c * 32 + 2 * i], sv[c * 32 + 2 * i + 1]), sl2x2, negm);
-                    const float2 pp = make_float2(ex2_approx(x.x), ex2_approx(x.y));
-                    rs2[i & 1] = __fadd2_rn(rs2[i & 1], pp);
-                    const __half2 hv = __floats2half2_rn(pp.x, pp.y);
-                    const float2 r = __ffma2_rn(__half22float2(hv), neg1, pp);   // p - fp16(p)
-                    hi[i] = h2_bits(hv);
-                    lo[i] = h2_bits(__floats2half2_rn(r.x, r.y));
+                // ---- causal mask (diagonal blocks only), row max of raw scores over both halves ----
+                const uint32_t kbase = j * BN + h * HB;
+                if (j * BN + BN - 1 > qpos0) {
+    #pragma unroll
+                    for (int c = 0; c < HB; ++c)
+                        if (kbase + c > qpos) sv[c] = -INFINITY;
                 }
-                tmem_st16(scol + c * 32, hi);
-                tmem_st16(scol + c * 32 + 16, lo);
-            }
-            l_run = l_run * alpha + ((rs2[0].x + rs2[0].y) + (rs2[1].x + rs2[1].y));
-            m_run = m_use;
-            // ---- O rescale (rare), this half's columns of O: PV(j-1) must have finished ----
-            // (both halves of these rows see the same `grow`, so both come here)
-            if (j >= 1 && __any_sync(0xffffffffu, grow)) {
-                const bool done =
-                    warp_wait_bounded(&bars->pv_done[pb], pph, p.status, ST_PREFILL_TIMEOUT, abort_flag);
-                if (!named_bar_and(1 + qd, 64, done)) {
+                float mx4[4] = {sv[0], sv[1], sv[2], sv[3]};
+    #pragma unroll
+                for (int c = 4; c < HB; c += 4) {
+                    mx4[0] = fmaxf(mx4[0], sv[c]);
+                    mx4[1] = fmaxf(mx4[1], sv[c + 1]);
+                    mx4[2] = fmaxf(mx4[2], sv[c + 2]);
+                    mx4[3] = fmaxf(mx4[3], sv[c + 3]);
+                }
+                float* xb = xch + (j & 1) * (2 * BM);                    // two slots alternate by block parity
+                xb[h * BM + r] = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3]));
+                if (!named_bar_and(1 + qd, 64, got)) {                   // the row's two halves
                     ok = false;
                     break;
                 }
-                tc_fence_after();
-#pragma unroll 1
-                for (int c = 0; c < HD / 64; ++c) {
-                    const uint32_t oc = trow + C::COL_O + h * (HD / 2) + c * 32;
-                    uint32_t rr[32];
-                    tmem_ld32(oc, rr);
-                    tmem_wait_ld();
-#pragma unroll
-                    for (int i = 0; i < 32; ++i) rr[i] = __float_as_uint(__uint_as_float(rr[i]) * alpha);
-                    tmem_st32(oc, rr);
+                const float mx = fmaxf(xb[r], xb[BM + r]) * sl2;
+                const float m_new = fmaxf(m_run, mx);
+                const bool grow = m_new > m_run + 8.0f;                  // keep a stale max up to 2^8 headroom
+                const float m_use = grow ? m_new : m_run;
+                const float alpha = grow ? ex2_approx(m_run - m_use) : 1.0f;
+                // a row whose keys so far are all masked keeps m = -inf and gets p = 0
+                const float m_sub = (m_use == -INFINITY) ? 0.f : m_use;
+                // ---- p = 2^(s*scale - m): one FFMA + ex2 per element; P hi/lo over this half's S ----
+                // pairs of elements in packed fp32x2 arithmetic (FFMA2 / FADD2): half the FMA, add and
+                // subtract instructions of the scalar form
+                const float2 sl2x2 = make_float2(sl2, sl2), negm = make_float2(-m_sub, -m_sub);
+                const float2 neg1 = make_float2(-1.f, -1.f);
+                float2 rs2[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
+    #pragma unroll
+                for (int c = 0; c < HB / 32; ++c) {   // 32 keys -> 16 columns of P_hi, then 16 of P_lo
+                    uint32_t hi[16], lo[16];
+    #pragma unroll
+                    for (int i = 0; i < 16; ++i) {
+                        const float2 x = __ffma2_rn(make_float2(sv[c * 32 + 2 * i], sv[c * 32 + 2 * i + 1]), sl2x2, negm);
+                        const float2 pp = make_float2(ex2_approx(x.x), ex2_approx(x.y));
+                        rs2[i & 1] = __fadd2_rn(rs2[i & 1], pp);
+                        const __half2 hv = __floats2half2_rn(pp.x, pp.y);
+                        const float2 r = __ffma2_rn(__half22float2(hv), neg1, pp);   // p - fp16(p)
+                        hi[i] = h2_bits(hv);
+                        lo[i] = h2_bits(__floats2half2_rn(r.x, r.y));
+                    }
+                    tmem_st16(scol + c * 32, hi);
+                    tmem_st16(scol + c * 32 + 16, lo);
                 }
-            }
-            tmem_wait_st();
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&bars->p_full[sb]);
-            pb = sb;
-            pph = sph;
-            if (++sb == nsb) {
-                sb = 0;
-                sph ^= 1u;
+                l_run = l_run * alpha + ((rs2[0].x + rs2[0].y) + (rs2[1].x + rs2[1].y));
+                m_run = m_use;
+                // ---- O rescale (rare), this half's columns of O: PV(j-1) must have finished ----
+                // (both halves of these rows see the same `grow`, so both come here)
+                if (j >= 1 && __any_sync(0xffffffffu, grow)) {
+                    const bool done =
+                        warp_wait_bounded(&bars->pv_done[pb], pph, p.status, ST_PREFILL_TIMEOUT, abort_flag);
+                    if (!named_bar_and(1 + qd, 64, done)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+    #pragma unroll 1
+                    for (int c = 0; c < HD / 64; ++c) {
+                        const uint32_t oc = trow + C::COL_O + h * (HD / 2) + c * 32;
+                        uint32_t rr[32];
+                        tmem_ld32(oc, rr);
+                        tmem_wait_ld();
+    #pragma unroll
+                        for (int i = 0; i < 32; ++i) rr[i] = __float_as_uint(__uint_as_float(rr[i]) * alpha);
+                        tmem_st32(oc, rr);
+                    }
+                }
+                tmem_wait_st();
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&bars->p_full[sb]);
+                pb = sb;
+                pph = sph;
+                if (++sb == nsb) {
+                    sb = 0;
+                    sph ^= 1u;
+                }
             }
         }
         // ---- epilogue: O / l (x sigmoid(gate)) -> out; each half takes its HD/2 columns ----
@@ -539,7 +545,7 @@ __global__ void __launch_bounds__(kPThreads, 1)
 
 // ------------------------------------------------------------------ host side
 
-template <int HD>
+template <int HD, bool QLO>
 int launch_prefill(const CUtensorMap& mk, const CUtensorMap& mv, const PrefillParams& p, uint32_t n_qtiles,
                    cudaStream_t st, char* err, size_t errlen) {
     using C = PCfg<HD>;
@@ -547,7 +553,7 @@ int launch_prefill(const CUtensorMap& mk, const CUtensorMap& mv, const PrefillPa
     int dev = 0;
     cudaGetDevice(&dev);
     if (dev >= 0 && dev < 64 && !attr_done[dev]) {
-        cudaError_t e = cudaFuncSetAttribute(k_prefill<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
+        cudaError_t e = cudaFuncSetAttribute(k_prefill<HD, QLO>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
         if (e != cudaSuccess) {
             set_err(err, errlen, "prefill: smem attribute (%d bytes): %s", C::SMEM, cudaGetErrorString(e));
             return -1;
@@ -559,7 +565,7 @@ int launch_prefill(const CUtensorMap& mk, const CUtensorMap& mv, const PrefillPa
     q.n_qt = n_qtiles;
     CUtensorMap mo;   // out as fp32 rows of q_stride, for the epilogue's tensor-copy stores
     if (encode_f32_store_map(&mo, p.out, p.n_heads * HD, p.q_stride, p.B, 32, err, errlen)) return -1;
-    k_prefill<HD><<<n_tiles, kPThreads, C::SMEM, st>>>(mk, mv, mo, q);
+    k_prefill<HD, QLO><<<n_tiles, kPThreads, C::SMEM, st>>>(mk, mv, mo, q);
     YATTN_CHECK_LAUNCH(err, errlen, "prefill");
     return 0;
 }
@@ -568,12 +574,16 @@ int launch_prefill(const CUtensorMap& mk, const CUtensorMap& mv, const PrefillPa
 
 int prefill(float* out, const float* q, const uint16_t* kc, const uint16_t* vc, const float* gate,
             uint32_t pos_start, uint32_t B, uint32_t n_heads, uint32_t n_kv, uint32_t hd, uint32_t kv_dim,
-            uint32_t q_stride, cudaStream_t st, char* err, size_t errlen) {
+            uint32_t q_stride, uint32_t flags, cudaStream_t st, char* err, size_t errlen) {
     if (!out || !q || !kc || !vc) {
         set_err(err, errlen, "prefill: null pointer argument");
         return -1;
     }
     if (B == 0) return 0;
+    if (flags & ~static_cast<uint32_t>(YATTN_PREFILL_Q_F16)) {
+        set_err(err, errlen, "prefill: unknown flags 0x%x", flags);
+        return -1;
+    }
     if (n_heads == 0 || n_kv == 0 || n_kv > n_heads) {
         set_err(err, errlen, "prefill: bad head counts n_heads=%u n_kv_heads=%u", n_heads, n_kv);
         return -1;
@@ -618,10 +628,14 @@ int prefill(float* out, const float* q, const uint16_t* kc, const uint16_t* vc, 
     p.scale_log2 = 1.4426950408889634f / sqrtf(static_cast<float>(hd));
     p.status = ctx->status;
     const uint32_t n_qtiles = (B + BM - 1) / BM;
+    const bool f16q = (flags & YATTN_PREFILL_Q_F16) != 0;
     switch (hd) {
-        case 64: return launch_prefill<64>(mk, mv, p, n_qtiles, st, err, errlen);
-        case 128: return launch_prefill<128>(mk, mv, p, n_qtiles, st, err, errlen);
-        default: return launch_prefill<256>(mk, mv, p, n_qtiles, st, err, errlen);
+        case 64: return f16q ? launch_prefill<64, false>(mk, mv, p, n_qtiles, st, err, errlen)
+                             : launch_prefill<64, true>(mk, mv, p, n_qtiles, st, err, errlen);
+        case 128: return f16q ? launch_prefill<128, false>(mk, mv, p, n_qtiles, st, err, errlen)
+                              : launch_prefill<128, true>(mk, mv, p, n_qtiles, st, err, errlen);
+        default: return f16q ? launch_prefill<256, false>(mk, mv, p, n_qtiles, st, err, errlen)
+                             : launch_prefill<256, true>(mk, mv, p, n_qtiles, st, err, errlen);
     }
 }
 
@@ -632,9 +646,9 @@ using namespace yattn;
 extern "C" int yattn_attn_prefill(float* att_out, const float* q, const uint16_t* kcache, const uint16_t* vcache,
                                   const float* gate, uint32_t pos_start, uint32_t B, uint32_t n_heads,
                                   uint32_t n_kv_heads, uint32_t head_dim, uint32_t kv_dim, uint32_t q_stride,
-                                  void* stream, char* err, size_t errlen) {
+                                  uint32_t flags, void* stream, char* err, size_t errlen) {
     return prefill(att_out, q, kcache, vcache, gate, pos_start, B, n_heads, n_kv_heads, head_dim, kv_dim, q_stride,
-                   static_cast<cudaStream_t>(stream), err, errlen);
+                   flags, static_cast<cudaStream_t>(stream), err, errlen);
 }
 
 extern "C" void cuda_k_attn_prefill(float* att_out, const float* q, const uint16_t* kcache, const uint16_t* vcache,
@@ -642,7 +656,8 @@ extern "C" void cuda_k_attn_prefill(float* att_out, const float* q, const uint16
                                     uint32_t head_dim, uint32_t kv_dim, uint32_t q_stride) {
     char err[256];
     err[0] = 0;
-    if (prefill(att_out, q, kcache, vcache, nullptr, pos_start, B, n_heads, n_kv_heads, head_dim, kv_dim, q_stride,
+    // the engine passes its fp32 projections: the q hi + lo kernel
+    if (prefill(att_out, q, kcache, vcache, nullptr, pos_start, B, n_heads, n_kv_heads, head_dim, kv_dim, q_stride, 0,
                 nullptr, err, sizeof(err)) != 0)
         set_last_error(err);
 }
