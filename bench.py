@@ -814,6 +814,8 @@ def _long_decode(args, rank, world, local, dist, sub=False):
         # launches on the current stream, so the step (NCCL included) can be graph-captured
         if world == 1:
             attn.attn_decode(out, d.q[0, 0], kv, vv, n - 1, H, c.n_kv_heads, hd, c.kv_dim)
+        elif peer:   # two launches: the shard's split decode, then merge + exchange + merge in one kernel
+            ex.decode(out, d.q[0, 0], kv, vv, k0, k1, c.n_kv_heads, c.kv_dim)
         else:
             partial()
             ex.run(out)
@@ -823,7 +825,9 @@ def _long_decode(args, rank, world, local, dist, sub=False):
     split = None
     if world > 1:
         ms_p, _, _ = _timed(partial, args, stream, world, dist, local, graph=True)
-        split = {"partial_decode_ms": round(ms_p, 5), "exchange_and_merge_ms": round(ms - ms_p, 5)}
+        split = {"partial_decode_ms": round(ms_p, 5), "exchange_and_merge_ms": round(ms - ms_p, 5),
+                 "note": "partial_decode_ms: this rank's shard reduced to one (m, l, o) per head on its GPU "
+                         "(yattn_decode_partial); the rest of the step is the exchange"}
     e2e = None
     if not args.no_e2e:
         qh = torch.empty(H * hd, dtype=torch.float32, pin_memory=True)
@@ -849,8 +853,10 @@ def _long_decode(args, rank, world, local, dist, sub=False):
     roof = {"bound": "hbm", "achieved": round(ach, 1), "peak": peaks["hbm_gbs"] * world, "unit": "GB/s",
             "frac": round(ach / (peaks["hbm_gbs"] * world), 4),
             "traffic": NCU_TRAFFIC["long_decode"] if world == 1 else None,
-            "kernel": "k_decode<128,4,TM>" + ((" + k_exchange_merge" if peer else " + NCCL all-gather + merge")
-                                              if world > 1 else ""), "peak_source": src + f" x{world} GPUs"}
+            "kernel": "k_decode<128,4,TM>" + ((" + k_merge_splits<EX> (split merge + exchange + merge)" if peer
+                                               else " + NCCL all-gather + merge")
+                                              if world > 1 else " + k_merge_splits"),
+            "peak_source": src + f" x{world} GPUs"}
     cfg_d = {"workload": c.name, "ctx": n, "n_heads": H, "n_kv_heads": c.n_kv_heads, "head_dim": hd,
              "kv_bytes": nbytes,
              "parallelism": (f"split-KV x{world}, " + (

@@ -283,6 +283,22 @@ int yattn_exchange_merge(const float* ml, const float* o, void* const* areas, ui
                          const float* gate, uint64_t wait_limit_ns, void* stream, char* err,
                          size_t errlen);
 
+/* One rank's step of a decode split over the GPUs, in two launches: the
+ * partial decode of keys [k_begin, k_end) of this rank's cache, then one kernel
+ * that merges this GPU's splits per head and exchanges the merged heads with
+ * every rank through the receive areas (as yattn_exchange_merge does), so every
+ * rank's out[n_heads*head_dim] holds the whole range's attention (x
+ * sigmoid(gate) if gate).  k_begin == k_end (an empty shard) is allowed.
+ * workspace: NULL (the per-device workspace) or yattn_decode_partial's.  Same
+ * wait bound, timeout status (401, NaN output) and call discipline as
+ * yattn_exchange_merge.  No reference counterpart: the reference has no
+ * multi-GPU attention. */
+int yattn_decode_exchange(const float* q, const uint16_t* kcache, const uint16_t* vcache,
+                          uint32_t k_begin, uint32_t k_end, uint32_t n_heads, uint32_t n_kv_heads,
+                          uint32_t head_dim, uint32_t kv_dim, void* const* areas, uint32_t world,
+                          uint32_t rank, float* out, const float* gate, uint64_t wait_limit_ns,
+                          void* workspace, size_t ws_bytes, void* stream, char* err, size_t errlen);
+
 /* Error-returning form of cuda_k_attn_decode with an explicit stream and gate. */
 int yattn_attn_decode(float* att_out, const float* q, const uint16_t* kcache,
                       const uint16_t* vcache, const float* gate, uint32_t pos,

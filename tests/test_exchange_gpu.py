@@ -107,10 +107,13 @@ def _worker(rank, world, port, T, ret):
     ex = PeerExchange(H, HD, device=dev)
     worst = 0.0
     k0, k1 = split_range(T, world, rank)
-    for _ in range(4):
+    for it in range(8):   # alternating the two-call form and the fused one, on the same areas and epochs
         out = torch.full((H * HD,), float("nan"), device=dev)
-        attn.decode_partial(ex.ml, ex.o, tq, tk, tv, k0, k1, H, KV, HD, kd)
-        ex.run(out)
+        if it % 2 == 0:
+            attn.decode_partial(ex.ml, ex.o, tq, tk, tv, k0, k1, H, KV, HD, kd)
+            ex.run(out)
+        else:
+            ex.decode(out, tq, tk, tv, k0, k1, KV, kd)
         torch.cuda.synchronize()
         worst = max(worst, oracle.rel_err(out.cpu().numpy(), full.cpu().numpy(), floor))
     ret[rank] = (worst, attn.device_status())
@@ -213,6 +216,66 @@ def test_exchange_wait_runs_out_and_reports_401():
         torch.cuda.synchronize()
         oracle.assert_close(out.cpu().numpy(), want, what="exchange after a timeout",
                             exact=oracle.exact_decode(q, k, v, T - 1, H, KV, HD, kd))
+        assert attn.device_status() == 0
+    finally:
+        ex.close()
+
+
+@pytest.mark.parametrize("T,gated", [(50, False), (3000, True), (40000, False)])
+def test_fused_decode_exchange_world1(T, gated):
+    """yattn_decode_exchange at world 1: the partial decode and the merge +
+    exchange kernel (one split, and many) against the oracle, eagerly and in
+    graph replays."""
+    from yllm_b200 import attn
+    from yllm_b200.dist import PeerExchange
+
+    dev = torch.device("cuda:0")
+    torch.cuda.set_device(dev)
+    q, k, v, kd = _case(21 + T, T)
+    tq, tk, tv = _to_dev(dev, q, k, v)
+    gate = np.random.default_rng(T).standard_normal(H * HD).astype(np.float32) if gated else None
+    tg = torch.from_numpy(gate).to(dev) if gated else None
+    want = oracle.attn_decode(q, k, v, T - 1, H, KV, HD, kd, gate=gate)
+    exact = oracle.exact_decode(q, k, v, T - 1, H, KV, HD, kd, gate=gate)
+    ex = PeerExchange(H, HD, device=dev)
+    try:
+        for _ in range(2):
+            out = torch.full((H * HD,), float("nan"), device=dev)
+            ex.decode(out, tq, tk, tv, 0, T, KV, kd, gate=tg)
+            torch.cuda.synchronize()
+            oracle.assert_close(out.cpu().numpy(), want, what=f"fused decode exchange T{T}", exact=exact)
+        out_g = torch.full((H * HD,), float("nan"), device=dev)
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=s):
+            ex.decode(out_g, tq, tk, tv, 0, T, KV, kd, gate=tg)
+        for _ in range(3):
+            out_g.fill_(float("nan"))
+            g.replay()
+            torch.cuda.synchronize()
+            oracle.assert_close(out_g.cpu().numpy(), want, what=f"fused decode exchange T{T}, graph", exact=exact)
+        del g
+        assert attn.device_status() == 0
+    finally:
+        ex.close()
+
+
+def test_fused_decode_exchange_empty_shard_world1():
+    """A rank with no keys (k_begin == k_end) still takes part: at world 1 every head is 0."""
+    from yllm_b200 import attn
+    from yllm_b200.dist import PeerExchange
+
+    dev = torch.device("cuda:0")
+    torch.cuda.set_device(dev)
+    q, k, v, kd = _case(5, 64)
+    tq, tk, tv = _to_dev(dev, q, k, v)
+    ex = PeerExchange(H, HD, device=dev)
+    try:
+        out = torch.full((H * HD,), float("nan"), device=dev)
+        ex.decode(out, tq, tk, tv, 10, 10, KV, kd)
+        torch.cuda.synchronize()
+        assert torch.count_nonzero(out).item() == 0
         assert attn.device_status() == 0
     finally:
         ex.close()

@@ -120,6 +120,8 @@ PROTOS = {
     "yattn_ipc_close": (C.c_int, [vp, *E]),
     "yattn_exchange_merge": (C.c_int, [vp, vp, vp, u32, u32, u32, u32, vp, vp, u64, vp, *E]),
     "yattn_attn_decode": (C.c_int, [vp, vp, vp, vp, vp, u32, u32, u32, u32, u32, vp, *E]),
+    "yattn_decode_exchange": (C.c_int, [vp, vp, vp, u32, u32, u32, u32, u32, u32, vp, u32, u32, vp, vp, u64, vp, sz,
+                                        vp, *E]),
     "yattn_attn_decode_noalloc": (C.c_int, [vp, vp, vp, vp, vp, u32, u32, u32, u32, u32, vp, *E]),
     "yattn_reserve": (C.c_int, [sz, *E]),
     "yattn_store_kv": (C.c_int, [vp, vp, vp, vp, u32, u32, u32, vp, *E]),

@@ -21,6 +21,7 @@
 //     partials to the workspace and the last split of an (item, head group) to
 //     arrive (atomic counter) merges all splits with log-sum-exp weights.
 #include "common.cuh"
+#include "exchange.cuh"
 #include "tcgen05.cuh"
 
 #include <algorithm>
@@ -601,7 +602,8 @@ __global__ void __launch_bounds__(DecodeCfg<HD>::THREADS, 1)
         // One warp per output row (kv head h of the group, query head g); lane owns
         // dims lane + 32 i.  The row's nsl slice partials are combined with
         // log-sum-exp weights.
-        const bool single = n_splits == 1;   // this CTA holds the whole key range of its (item, head group)
+        // this CTA holds the whole key range of its (item, head group), and writes the result itself
+        const bool single = n_splits == 1 && !p.defer_merge;
         for (uint32_t row = warp; row < HC * G; row += NCW) {
             const uint32_t h = row / G, g = row % G;
             uint32_t hfirst, hcnt;
@@ -749,18 +751,28 @@ __global__ void __launch_bounds__(DecodeCfg<HD>::THREADS, 1)
 }
 
 // ------------------------------------------------- parallel merge of many splits
-// One CTA per query head; its 8 warps each fold a strided subset of the ns
-// split partials (online log-sum-exp in registers, lane = dims lane + 32 i),
-// then the warps combine in shared memory.  Used when one query has more
-// splits than the last-arriving CTA can merge quickly on its own.
+// One CTA per query head merges the head's ns split partials with log-sum-exp
+// weights.  Every split's (m, l) is loaded in one round (threads over splits);
+// the global max and the weights w_s = 2^(m_s - M) go to shared memory; then
+// warp w sums w_s o_s over the splits s = w (mod 8) with lanes over dims and the
+// loads of 8 splits in flight at a time, and the 8 warps' sums are added.  Used
+// when one query has more splits than the last-arriving CTA merges quickly, and
+// always for the cross-GPU exchange (EX), which then sends the merged head to
+// every rank and merges the ranks' heads (exchange.cuh).
 constexpr uint32_t kInKernelMergeMax = 8;
+constexpr uint32_t kMergeMaxSplits = 1024;
 
+template <bool EX>
 __global__ void __launch_bounds__(256) k_merge_splits(const float* __restrict__ part_ml,
                                                       const float* __restrict__ part_o, uint32_t ns,
                                                       uint32_t n_heads, uint32_t n_kv, uint32_t G, uint32_t hd,
-                                                      float* out, const float* gate, float* out_ml, float* out_o) {
-    __shared__ float s_m[8], s_l[8];
+                                                      float* out, const float* gate, float* out_ml, float* out_o,
+                                                      const ExchangeArgs ex, int* status) {
+    __shared__ float s_w[kMergeMaxSplits];   // m_s, then the weight of split s
+    __shared__ float s_l[kMergeMaxSplits];
+    __shared__ float s_red[2][8];
     __shared__ float s_o[8][256];
+    __shared__ uint32_t s_epoch;
     const uint32_t hh = blockIdx.x;
     const uint32_t kvh = hh * n_kv / n_heads;
     uint32_t gfirst, gcnt;
@@ -768,36 +780,70 @@ __global__ void __launch_bounds__(256) k_merge_splits(const float* __restrict__ 
     const uint32_t gl = hh - gfirst;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int dl = static_cast<int>(hd / 32);     // 2, 4 or 8 dims per lane
-    float m = -INFINITY, l = 0.f, acc[8];
+    auto slot = [&](uint32_t s) { return (static_cast<size_t>(kvh) * ns + s) * G + gl; };
+    if constexpr (EX) exchange_epoch(ex, &s_epoch);
+    // ---- every split's (m, l); the maximum m ----
+    float mloc = -INFINITY;
+    for (uint32_t s = threadIdx.x; s < ns; s += blockDim.x) {
+        const float2 ml = __ldcg(reinterpret_cast<const float2*>(part_ml + slot(s) * 2));
+        s_w[s] = ml.x;
+        s_l[s] = ml.y;
+        mloc = fmaxf(mloc, ml.x);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) mloc = fmaxf(mloc, __shfl_xor_sync(0xffffffffu, mloc, o));
+    if (lane == 0) s_red[0][warp] = mloc;
+    __syncthreads();
+    float M = s_red[0][0];
+#pragma unroll
+    for (int w = 1; w < 8; ++w) M = fmaxf(M, s_red[0][w]);
+    // ---- weights, the weighted sum of l ----
+    float lloc = 0.f;
+    for (uint32_t s = threadIdx.x; s < ns; s += blockDim.x) {
+        const float m = s_w[s];
+        const float w = (m == -INFINITY) ? 0.f : ex2_approx(m - M);
+        s_w[s] = w;
+        lloc += w * s_l[s];
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) lloc += __shfl_xor_sync(0xffffffffu, lloc, o);
+    if (lane == 0) s_red[1][warp] = lloc;
+    __syncthreads();
+    float L = 0.f;
+#pragma unroll
+    for (int w = 0; w < 8; ++w) L += s_red[1][w];
+    // ---- sum of w_s o_s: warp w takes splits w, w + 8, ...; 8 splits' loads in flight ----
+    float acc[8];
 #pragma unroll
     for (int i = 0; i < 8; ++i) acc[i] = 0.f;
-    for (uint32_t s = warp; s < ns; s += 8) {
-        const size_t slot = (static_cast<size_t>(kvh) * ns + s) * G + gl;
-        const float ms = part_ml[slot * 2], ls = part_ml[slot * 2 + 1];
-        const float mn = fmaxf(m, ms);
-        const float a = ex2_approx(m - mn), b = ex2_approx(ms - mn);
-        l = l * a + ls * b;
+    for (uint32_t s0 = warp; s0 < ns; s0 += 64) {
+        float ov[8][8];
 #pragma unroll
-        for (int i = 0; i < 8; ++i)
-            if (i < dl) acc[i] = acc[i] * a + b * part_o[slot * hd + lane + 32 * i];
-        m = mn;
-    }
-    if (lane == 0) {
-        s_m[warp] = m;
-        s_l[warp] = l;
+        for (int j = 0; j < 8; ++j) {
+            const uint32_t s = s0 + 8 * j;
+#pragma unroll
+            for (int i = 0; i < 8; ++i)
+                ov[j][i] = (s < ns && i < dl) ? __ldcg(part_o + slot(s) * hd + lane + 32 * i) : 0.f;
+        }
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const uint32_t s = s0 + 8 * j;
+            const float w = s < ns ? s_w[s] : 0.f;
+#pragma unroll
+            for (int i = 0; i < 8; ++i) acc[i] += w * ov[j][i];
+        }
     }
 #pragma unroll
     for (int i = 0; i < 8; ++i)
         if (i < dl) s_o[warp][lane + 32 * i] = acc[i];
     __syncthreads();
     for (uint32_t d = threadIdx.x; d < hd; d += blockDim.x) {
-        float M = -INFINITY;
-        for (int w = 0; w < 8; ++w) M = fmaxf(M, s_m[w]);
-        float o = 0.f, L = 0.f;
-        for (int w = 0; w < 8; ++w) {
-            const float sc = (s_m[w] == -INFINITY) ? 0.f : ex2_approx(s_m[w] - M);
-            o += sc * s_o[w][d];
-            L += sc * s_l[w];
+        float o = 0.f;
+#pragma unroll
+        for (int w = 0; w < 8; ++w) o += s_o[w][d];
+        if constexpr (EX) {
+            s_o[0][d] = o;   // the merged head, for the exchange (each d read and written by one thread)
+            continue;
         }
         if (out_ml) {   // merged partial of the whole range
             out_o[static_cast<size_t>(hh) * hd + d] = o;
@@ -810,6 +856,12 @@ __global__ void __launch_bounds__(256) k_merge_splits(const float* __restrict__ 
         float r = o / L;
         if (gate) r *= 1.0f / (1.0f + __expf(-gate[static_cast<size_t>(hh) * hd + d]));
         out[static_cast<size_t>(hh) * hd + d] = r;
+    }
+    if constexpr (EX) {
+        __syncthreads();
+        const uint32_t epoch = s_epoch;
+        exchange_head(ex, epoch, n_heads, hd, hh, M, L, s_o[0], out, gate, status);
+        exchange_finish(ex, epoch);
     }
 }
 
@@ -997,10 +1049,16 @@ DecodeParams single_params(const SinglePlan& sp, float* out, const float* q, con
 }
 
 // Launches a single-query decode; with many splits the merge runs as a
-// separate parallel kernel instead of in the last-arriving CTA.
-int launch_single(DecodeParams& p, const SinglePlan& sp, uint32_t hd, cudaStream_t st, char* err, size_t errlen) {
-    const bool defer = sp.ns > kInKernelMergeMax;
+// separate parallel kernel instead of in the last-arriving CTA, and with ex that
+// kernel also exchanges the merged heads with the other ranks.
+int launch_single(DecodeParams& p, const SinglePlan& sp, uint32_t hd, cudaStream_t st, char* err, size_t errlen,
+                  const ExchangeArgs* ex = nullptr) {
+    const bool defer = ex || sp.ns > kInKernelMergeMax;
     p.defer_merge = defer ? 1 : 0;
+    if (defer && sp.ns > kMergeMaxSplits) {
+        set_err(err, errlen, "decode: %u splits per head group (at most %u)", sp.ns, kMergeMaxSplits);
+        return -1;
+    }
     // K and V maps over keys [0, t_end) of this layer; boxes of one stage (16 tokens per consumer warp)
     CUtensorMap km, vm;
     const uint32_t box_rows = 16u * (hd >= 256 ? DecodeCfg<256>::NCW : DecodeCfg<128>::NCW) / p.hc;
@@ -1013,8 +1071,14 @@ int launch_single(DecodeParams& p, const SinglePlan& sp, uint32_t hd, cudaStream
     if (launch_decode(p, true, &km, &vm, hd, sp.ns * sp.n_groups_kv, st, err, errlen)) return -1;
     if (!defer) return 0;
     const uint32_t G = gmax_of(p.n_heads, p.n_kv);
-    k_merge_splits<<<p.n_heads, 256, 0, st>>>(p.part_ml, p.part_o, sp.ns, p.n_heads, p.n_kv, G, hd, p.item0.out,
-                                               p.item0.gate, p.partial_only ? p.out_ml : nullptr, p.out_o);
+    if (ex)
+        k_merge_splits<true><<<p.n_heads, 256, 0, st>>>(p.part_ml, p.part_o, sp.ns, p.n_heads, p.n_kv, G, hd,
+                                                         p.item0.out, p.item0.gate, nullptr, nullptr, *ex, p.status);
+    else
+        k_merge_splits<false><<<p.n_heads, 256, 0, st>>>(p.part_ml, p.part_o, sp.ns, p.n_heads, p.n_kv, G, hd,
+                                                          p.item0.out, p.item0.gate,
+                                                          p.partial_only ? p.out_ml : nullptr, p.out_o,
+                                                          ExchangeArgs{}, p.status);
     YATTN_CHECK_LAUNCH(err, errlen, "decode merge");
     return 0;
 }
@@ -1026,7 +1090,7 @@ int launch_single(DecodeParams& p, const SinglePlan& sp, uint32_t hd, cudaStream
 int decode_single(float* out, const float* q, const uint16_t* k, const uint16_t* v, const float* gate,
                   uint32_t t_begin, uint32_t t_end, uint32_t n_heads, uint32_t n_kv, uint32_t hd, uint32_t kv_dim,
                   float* partial_ml, float* partial_o, void* ws, size_t ws_bytes, cudaStream_t st, char* err,
-                  size_t errlen) {
+                  size_t errlen, const ExchangeArgs* ex = nullptr) {
     if (check_geom(n_heads, n_kv, hd, kv_dim, err, errlen)) return -1;
     if (t_end <= t_begin) {
         set_err(err, errlen, "decode: empty key range [%u, %u)", t_begin, t_end);
@@ -1043,13 +1107,17 @@ int decode_single(float* out, const float* q, const uint16_t* k, const uint16_t*
     DevCtx* ctx = dev_ctx(err, errlen);
     if (!ctx) return -1;
     const uint32_t gmax = gmax_of(n_heads, n_kv);
-    const SinglePlan sp = plan_single(t_end - t_begin, n_kv, hd, static_cast<uint32_t>(ctx->num_sms));
+    SinglePlan sp = plan_single(t_end - t_begin, n_kv, hd, static_cast<uint32_t>(ctx->num_sms));
+    if (ex && sp.ns == 1) {   // the exchange merges split slots: one split per head group still writes one
+        sp.n_parts = n_kv;
+        sp.n_groups = sp.n_groups_kv;
+    }
     DecodeParams p = single_params(sp, out, q, k, v, gate, t_begin, t_end, n_heads, n_kv, hd, kv_dim);
     p.status = ctx->status;
     p.partial_only = partial_ml != nullptr ? 1 : 0;
     p.out_ml = partial_ml;
     p.out_o = partial_o;
-    if (sp.ns > 1) {
+    if (sp.n_parts > 0) {
         const size_t need = ws_bytes_for(sp.n_parts, sp.n_groups, gmax, hd);
         if (ws) {
             if (ws_bytes < need) {
@@ -1075,7 +1143,7 @@ int decode_single(float* out, const float* q, const uint16_t* k, const uint16_t*
         }
         carve_ws(ws, sp.n_parts, sp.n_groups, gmax, p);
     }
-    return launch_single(p, sp, hd, st, err, errlen);
+    return launch_single(p, sp, hd, st, err, errlen, ex);
 }
 
 int decode_reserve(size_t bytes, char* err, size_t errlen) {
@@ -1469,6 +1537,51 @@ extern "C" void cuda_k_attn_decode(float* att_out, const float* q, const uint16_
     if (decode_single(att_out, q, kcache, vcache, nullptr, 0, pos + 1, n_heads, n_kv_heads, head_dim, kv_dim,
                       nullptr, nullptr, nullptr, 0, nullptr, err, sizeof(err)) != 0)
         set_last_error(err);
+}
+
+// ------------------------------------------------------- split-KV decode + exchange
+//
+// One rank's step of a decode whose key range is split over the GPUs: the
+// partial decode of keys [k_begin, k_end) (split-KV over this GPU's SMs), then
+// one kernel that merges this GPU's splits per head and exchanges the merged
+// heads with every rank over peer memory (exchange.cuh), writing the whole
+// range's output on every rank.  Two launches per step; an empty shard
+// (k_begin == k_end) takes part in the exchange with l = 0.
+
+extern "C" int yattn_decode_exchange(const float* q, const uint16_t* kcache, const uint16_t* vcache,
+                                     uint32_t k_begin, uint32_t k_end, uint32_t n_heads, uint32_t n_kv_heads,
+                                     uint32_t head_dim, uint32_t kv_dim, void* const* areas, uint32_t world,
+                                     uint32_t rank, float* out, const float* gate, uint64_t wait_limit_ns,
+                                     void* workspace, size_t ws_bytes, void* stream, char* err, size_t errlen) {
+    if (check_geom(n_heads, n_kv_heads, head_dim, kv_dim, err, errlen)) return -1;
+    if (!areas || !out || world == 0 || world > kMaxWorld || rank >= world || k_end < k_begin) {
+        set_err(err, errlen, "decode_exchange: bad arguments (world 1..%u, rank < world, k_begin <= k_end)",
+                kMaxWorld);
+        return -1;
+    }
+    ExchangeArgs ex{};
+    for (uint32_t r = 0; r < world; ++r) {
+        if (!areas[r]) {
+            set_err(err, errlen, "decode_exchange: null area for rank %u", r);
+            return -1;
+        }
+        ex.area[r] = static_cast<uint8_t*>(areas[r]);
+    }
+    ex.world = world;
+    ex.rank = rank;
+    ex.wait_ns = wait_limit_ns ? wait_limit_ns : kWaitLimitNs;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    if (k_end > k_begin)
+        return decode_single(out, q, kcache, vcache, gate, k_begin, k_end, n_heads, n_kv_heads, head_dim, kv_dim,
+                             nullptr, nullptr, workspace, ws_bytes, st, err, errlen, &ex);
+    // no keys on this rank: its part of every head has l = 0
+    DevCtx* ctx = dev_ctx(err, errlen);
+    if (!ctx) return -1;
+    k_merge_splits<true><<<n_heads, 256, 0, st>>>(nullptr, nullptr, 0, n_heads, n_kv_heads,
+                                                   gmax_of(n_heads, n_kv_heads), head_dim, out, gate, nullptr,
+                                                   nullptr, ex, ctx->status);
+    YATTN_CHECK_LAUNCH(err, errlen, "decode_exchange");
+    return 0;
 }
 
 // ------------------------------------------------------- allocation-free decode

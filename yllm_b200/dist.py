@@ -227,6 +227,18 @@ class PeerExchange:
              self._areas, self.world, self.rank, self.n_heads, self.head_dim, out.data_ptr(),
              gate.data_ptr() if gate is not None else None, wait_limit_ns, torch.cuda.current_stream().cuda_stream)
 
+    def decode(self, out: torch.Tensor, q: torch.Tensor, kcache: torch.Tensor, vcache: torch.Tensor, k_begin: int,
+               k_end: int, n_kv_heads: int, kv_dim: int, gate: Optional[torch.Tensor] = None,
+               wait_limit_ns: int = 0) -> None:
+        """One step of the split decode in two launches (yattn_decode_exchange): this rank's keys
+        [k_begin, k_end) reduced on its GPU, merged and exchanged with every rank in one kernel."""
+        from ._lib import call
+
+        call("yattn_decode_exchange", q.data_ptr(), kcache.data_ptr(), vcache.data_ptr(), k_begin, k_end,
+             self.n_heads, n_kv_heads, self.head_dim, kv_dim, self._areas, self.world, self.rank, out.data_ptr(),
+             gate.data_ptr() if gate is not None else None, wait_limit_ns, None, 0,
+             torch.cuda.current_stream().cuda_stream)
+
     def close(self) -> None:
         """Collective: every rank's pushes are done before any area is unmapped or freed."""
         from ._lib import call
