@@ -1012,6 +1012,85 @@ def run_rope_store(args) -> None:
         dist.destroy_process_group()
 
 
+def run_fused_decode(args) -> None:
+    """Config 3's whole attention step with the decode step's RoPE + KV store
+    (engine.c:1052-1096 per sequence and layer): per layer, the new token's k and
+    v rotated / rounded into every sequence's cache row pos, q rotated, and the
+    attention over keys 0..pos.  Timed two ways on the same inputs: one fused
+    launch per layer (yattn_decode_run_pooled_rope), and two (yattn_rope_store_kv,
+    then yattn_decode_run_pooled).  KV per GPU far above L2.  Weak scaling."""
+    import torch
+    import torch.distributed as dist
+
+    from yllm_b200 import attn, dist as ydist, fixtures
+    from yllm_b200.configs import CFG3 as cfg
+
+    rank, world, local = ydist.init("nccl" if args.gpus > 1 else "gloo")
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    stream = torch.cuda.current_stream()
+    n_layers = args.layers or cfg.layers
+    seqs = list(range(args.seqs or cfg.n_seqs))
+    H, KV, hd, kd = cfg.n_heads, cfg.n_kv_heads, cfg.head_dim, cfg.kv_dim
+    theta = 500000.0   # Llama-3 rope_theta
+    d = fixtures.decode_inputs(cfg, layers=list(range(n_layers)), seqs=seqs, device=dev)
+    n = len(seqs)
+    g = torch.Generator(device=dev)
+    g.manual_seed(77 + rank)
+    kn = torch.randn(n_layers, n, kd, generator=g, device=dev)
+    vn = torch.randn(n_layers, n, kd, generator=g, device=dev)
+    q_raw = d.q.clone()   # the fused path reads q unrotated and leaves it so
+    pool = (d.kv_pool.data_ptr(), d.kv_pool.numel() * 2)
+    pos = [c - 1 for c in d.ctx]
+    plan = attn.DecodePlan.build(pos, H, KV, hd, kd, device=dev, pool=pool)
+    items = [attn.make_items([(q_raw[l, i], d.out[l, i], d.k_ptr(l, i), d.v_ptr(l, i), None, pos[i])
+                              for i in range(n)], device=dev) for l in range(n_layers)]
+    rows = [attn.make_new_rows([(kn[l, i], vn[l, i]) for i in range(n)], device=dev) for l in range(n_layers)]
+    ritems = [attn.make_rope_items([(d.q[l, i], kn[l, i], vn[l, i], d.k_ptr(l, i), d.v_ptr(l, i), pos[i])
+                                    for i in range(n)], device=dev) for l in range(n_layers)]
+    items2 = [attn.make_items([(d.q[l, i], d.out[l, i], d.k_ptr(l, i), d.v_ptr(l, i), None, pos[i])
+                               for i in range(n)], device=dev) for l in range(n_layers)]
+
+    def fused():
+        for l in range(n_layers):
+            plan.run_rope(items[l], rows[l], attn.ROPE_LLAMA, theta)
+
+    def two_launch():
+        # the store rotates q in place, so repeated steps rotate an already rotated q: the same work
+        for l in range(n_layers):
+            attn.rope_store_kv(ritems[l], n, H, KV, hd, kd, attn.ROPE_LLAMA, theta)
+            plan.run(items2[l])
+
+    ms_f, _, clk = _timed(fused, args, stream, world, dist, local)
+    ms_2, _, _ = _timed(two_launch, args, stream, world, dist, local)
+    st = attn.device_status()
+    if st != 0:
+        raise RuntimeError(f"device status {st}")
+    keys = sum(d.ctx)
+    step_bytes = n_layers * (keys * kd * 2 * 2 + n * (H * hd * 4 * 2 + kd * 4 * 2))
+    peaks, src = load_peaks()
+    roof = {"bound": "hbm", "achieved": round(step_bytes / (ms_f / 1e3) / 1e9, 1), "peak": peaks["hbm_gbs"],
+            "unit": "GB/s", "frac": round(step_bytes / (ms_f / 1e3) / 1e9 / peaks["hbm_gbs"], 4), "traffic": None,
+            "kernel": "k_decode<128,4,TM,ROPE> (pooled tensor copies, RoPE + store fused)", "peak_source": src,
+            "bytes_per_step": step_bytes}
+    if rank == 0:
+        line = _line(args, world, "attn decode tok/s with the RoPE + KV store (batched ragged GQA decode, all layers)",
+                     n * world / (ms_f / 1e3), "tok/s", ms_f,
+                     {"workload": cfg.name + "-rope-store-fused", "n_heads": H, "n_kv_heads": KV, "head_dim": hd,
+                      "layers": n_layers, "n_seqs": n * world, "rope": "llama pairs, theta 500000",
+                      "parallelism": f"data-parallel x{world}: a batch per GPU, no collective",
+                      "launch": "one API call per layer per step (no graph)",
+                      "l2": "inputs larger than L2 (KV per GPU >> 126 MB)"},
+                     roof, args.steps * n_layers, clk, scaling="weak")
+        line["two_launch"] = {"value": round(n * world / (ms_2 / 1e3), 2), "unit": "tok/s", "ms_per_step": round(ms_2, 4),
+                              "path": "yattn_rope_store_kv, then yattn_decode_run_pooled, per layer"}
+        line["dtype"] = "f32 math, fp16 KV (engine rounding of the new rows)"
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
 def run_gemv(args, fmt: str = "q4k") -> None:
     """The per-layer linear layers of a Llama-3-8B decode step (cuda_fwd.c:94-168
     brackets attention with these GEMVs): per layer q, k, v, o (4096/1024 x
@@ -1303,7 +1382,8 @@ def main() -> None:
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--workload", default="decode",
                     choices=["decode", "prefill", "gated_prefill", "gdn_prefill", "gdn_decode", "long_decode",
-                             "config1_decode", "gated_decode", "rope_store", "sess_kv", "gemv", "gemv_f16", "gdn_inputs"],
+                             "config1_decode", "gated_decode", "rope_store", "sess_kv", "gemv", "gemv_f16", "gdn_inputs",
+                             "fused_decode"],
                     help="decode = BASELINE config 3 (the default bench line)")
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
@@ -1340,6 +1420,8 @@ def main() -> None:
         run_gemv(args, "f16" if args.workload == "gemv_f16" else "q4k")
     elif args.workload == "gdn_inputs":
         run_gdn_inputs(args)
+    elif args.workload == "fused_decode":
+        run_fused_decode(args)
     else:
         run_long_decode(args)
 

@@ -299,6 +299,33 @@ int yattn_decode_exchange(const float* q, const uint16_t* kcache, const uint16_t
                           uint32_t rank, float* out, const float* gate, uint64_t wait_limit_ns,
                           void* workspace, size_t ws_bytes, void* stream, char* err, size_t errlen);
 
+/* The new token's k and v of one item (device pointers, fp32, n_kv_heads*head_dim
+ * each; k not yet rotated). */
+typedef struct YattnDecodeNewRow {
+    const float* k;
+    const float* v;
+} YattnDecodeNewRow;
+
+/* yattn_decode_run_pooled with the decode step's RoPE and KV store fused into the
+ * attention kernel: engine.c:1052-1072 (and 921-934 for qwen35's M-RoPE) for every
+ * item in the same launch as its attention.  Each item's q is read unrotated (and
+ * left as it is) and rotated at the item's pos; rows_dev[i] (same order as the
+ * items) holds the new token's k and v: k is rotated, both are rounded with the
+ * engine's f32_to_f16 and written into cache row pos of the item's K and V, and
+ * the attention over keys 0..pos uses those fp16 values.  In the CTA of the split
+ * that ends at pos, a warp of its own writes the row into the cache before that
+ * split's last tile is copied; the rest of the cache is only read.  Row pos of an
+ * item must lie inside the pool (else device status 103 and nothing is written).
+ * rope_kind / n_rope_dims / theta as in yattn_rope_store_kv (no QK-norm here:
+ * with QK-norm, run yattn_rope_store_kv first).  The plan, pool and workspace are
+ * yattn_decode_plan_pooled's. */
+int yattn_decode_run_pooled_rope(const YattnDecodeItem* items_dev, const YattnDecodeNewRow* rows_dev,
+                                 const YattnDecodeWork* work_dev, uint32_t n_work, uint32_t n_parts,
+                                 uint32_t n_groups, uint32_t n_heads, uint32_t n_kv_heads,
+                                 uint32_t head_dim, uint32_t kv_dim, const void* pool, size_t pool_bytes,
+                                 int rope_kind, uint32_t n_rope_dims, float theta, void* workspace,
+                                 size_t ws_bytes, void* stream, char* err, size_t errlen);
+
 /* Error-returning form of cuda_k_attn_decode with an explicit stream and gate. */
 int yattn_attn_decode(float* att_out, const float* q, const uint16_t* kcache,
                       const uint16_t* vcache, const float* gate, uint32_t pos,

@@ -344,3 +344,85 @@ def test_dropin_reports_misaligned_pointer(dev):
     with pytest.raises(_lib.YattnError, match="aligned"):
         _lib.call_void("cuda_k_attn_decode", out.data_ptr(), tq.data_ptr(), tk.data_ptr() + 2, tv.data_ptr(),
                        T - 2, H, KV, hd, kd)
+
+
+@pytest.mark.parametrize("kind,H,KV,hd,n_dims,theta,ctxs,gated,ctas", [
+    (0, 32, 8, 128, 128, 500000.0, [1, 17, 64, 65, 700, 1500, 4096], False, 0),   # Llama-3-8B heads, llama pairs
+    (1, 14, 2, 64, 64, 1000000.0, [512, 1, 300, 3000], False, 0),                 # Qwen2.5-0.5B heads, qwen pairs
+    (2, 16, 2, 256, 64, 10000000.0, [4096, 63, 64, 65], True, 0),                 # qwen35 gated attention, M-RoPE
+    # few CTAs: each runs many units of many tiles back to back, so the RoPE warp runs whole units
+    # ahead of the ring (its q slots and arrives must still land in their tiles' phases)
+    (0, 32, 8, 128, 128, 500000.0, [1, 17, 64, 65, 700, 1500, 4096], False, 3),
+    (1, 14, 2, 64, 64, 1000000.0, [512, 1, 300, 3000, 2047], False, 2),
+    (2, 16, 2, 256, 64, 10000000.0, [4096, 63, 64, 65, 1000], True, 2),
+])
+def test_fused_rope_store_decode(dev, kind, H, KV, hd, n_dims, theta, ctxs, gated, ctas):
+    """yattn_decode_run_pooled_rope: the decode step's RoPE + KV store (engine.c:1052-1072; M-RoPE 921-934)
+    fused into the attention launch.  Against the same step as two launches (yattn_rope_store_kv, then
+    yattn_decode_run_pooled): the pool after the step (every cache row, the new ones included) is identical
+    and the outputs agree; against the oracle, the new K rows are within one fp16 ulp of the reference's
+    rope + f32_to_f16 (V bit-exact) and the outputs pass the parity bar.  q is left unrotated."""
+    from yllm_b200 import attn
+
+    rng = np.random.default_rng(kind * 31 + hd + len(ctxs))
+    kd = KV * hd
+    offs, rows = [], 3
+    for c in ctxs:
+        offs.append(rows)
+        rows += 2 * c + 5
+    hist = oracle.f32_to_f16(rng.standard_normal(rows * kd).astype(np.float32)).reshape(rows, kd)
+    pool_a = torch.from_numpy(hist.view(np.int16)).to(dev).view(torch.uint16)
+    pool_b = pool_a.clone()
+    q = [rng.standard_normal(H * hd).astype(np.float32) for _ in ctxs]
+    kn = [rng.standard_normal(kd).astype(np.float32) for _ in ctxs]
+    vn = [rng.standard_normal(kd).astype(np.float32) for _ in ctxs]
+    gates = [rng.standard_normal(H * hd).astype(np.float32) if gated else None for _ in ctxs]
+    t = lambda x: torch.from_numpy(x).to(dev) if x is not None else None
+    tk, tv, tg = [t(x) for x in kn], [t(x) for x in vn], [t(x) for x in gates]
+    qa, qb = [t(x) for x in q], [t(x) for x in q]
+    outa = [torch.full((H * hd,), float("nan"), device=dev) for _ in ctxs]
+    outb = [torch.full((H * hd,), float("nan"), device=dev) for _ in ctxs]
+    pos = [c - 1 for c in ctxs]
+    kbase = lambda pool, i: pool.data_ptr() + offs[i] * kd * 2
+    vbase = lambda pool, i: pool.data_ptr() + (offs[i] + ctxs[i]) * kd * 2
+    # two launches: RoPE + store, then the pooled decode
+    ritems = attn.make_rope_items([(qa[i], tk[i], tv[i], kbase(pool_a, i), vbase(pool_a, i), pos[i])
+                                   for i in range(len(ctxs))])
+    attn.rope_store_kv(ritems, len(ctxs), H, KV, hd, kd, kind, theta, n_rope_dims=n_dims)
+    plan_a = attn.DecodePlan.build(pos, H, KV, hd, kd, pool=(pool_a.data_ptr(), pool_a.numel() * 2))
+    plan_a.run(attn.make_items([(qa[i], outa[i], kbase(pool_a, i), vbase(pool_a, i), tg[i], pos[i])
+                                for i in range(len(ctxs))]))
+    # one launch
+    plan_b = attn.DecodePlan.build(pos, H, KV, hd, kd, target_ctas=ctas, pool=(pool_b.data_ptr(), pool_b.numel() * 2))
+    items_b = attn.make_items([(qb[i], outb[i], kbase(pool_b, i), vbase(pool_b, i), tg[i], pos[i])
+                               for i in range(len(ctxs))])
+    rows_b = attn.make_new_rows([(tk[i], tv[i]) for i in range(len(ctxs))])
+    for _ in range(2):   # a repeat rewrites the same rows with the same values
+        plan_b.run_rope(items_b, rows_b, kind, theta, n_rope_dims=n_dims)
+    torch.cuda.synchronize()
+    assert attn.device_status() == 0
+    assert torch.equal(pool_a, pool_b), "fused store differs from the RoPE store kernel"
+    for i in range(len(ctxs)):
+        assert torch.equal(qb[i].cpu(), torch.from_numpy(q[i])), "q must be left unrotated"
+    lib = oracle.load("ref") if oracle.has_ref() else oracle.load("port")
+    pool_np = pool_b.cpu().numpy().view(np.uint16).reshape(rows, kd)
+    for i, c in enumerate(ctxs):
+        # the new rows against the reference's rope + f32_to_f16
+        qr, kr = q[i].copy(), kn[i].copy()
+        kc = np.zeros((c) * kd, np.uint16)
+        vc = np.zeros((c) * kd, np.uint16)
+        lib.orc_rope_store(qr, kr, vn[i].copy(), kc, vc, H, KV, hd, kd, kind, n_dims, pos[i], theta)
+        krow = pool_np[offs[i] + pos[i]]
+        vrow = pool_np[offs[i] + c + pos[i]]
+        assert np.array_equal(vrow, vc[pos[i] * kd:]), f"V row of seq {i}"
+        dk = np.abs(krow.astype(np.int32) - kc[pos[i] * kd:].astype(np.int32))
+        assert dk.max() <= 1 and (dk != 0).sum() <= max(1, kd // 100), f"K row of seq {i}"
+        # the outputs: the two paths, and the engine's attention over the stored cache with the reference's q
+        k_i = np.ascontiguousarray(pool_np[offs[i]:offs[i] + c]).reshape(-1)
+        v_i = np.ascontiguousarray(pool_np[offs[i] + c:offs[i] + 2 * c]).reshape(-1)
+        want = oracle.attn_decode(qr, k_i, v_i, pos[i], H, KV, hd, kd, gate=gates[i])
+        exact = oracle.exact_decode(qr, k_i, v_i, pos[i], H, KV, hd, kd, gate=gates[i])
+        got_b = outb[i].cpu().numpy()
+        oracle.assert_close(got_b, outa[i].cpu().numpy(), what=f"fused vs two launches, kind {kind} ctx {c}",
+                            exact=exact)
+        oracle.assert_close(got_b, want, what=f"fused RoPE store decode vs oracle, kind {kind} ctx {c}", exact=exact)

@@ -51,6 +51,13 @@ class YattnRopeItem(C.Structure):
     ]
 
 
+class YattnDecodeNewRow(C.Structure):
+    _fields_ = [
+        ("k", vp),
+        ("v", vp),
+    ]
+
+
 class YattnQkNorm(C.Structure):
     _fields_ = [
         ("q_w", vp),
@@ -120,6 +127,8 @@ PROTOS = {
     "yattn_ipc_close": (C.c_int, [vp, *E]),
     "yattn_exchange_merge": (C.c_int, [vp, vp, vp, u32, u32, u32, u32, vp, vp, u64, vp, *E]),
     "yattn_attn_decode": (C.c_int, [vp, vp, vp, vp, vp, u32, u32, u32, u32, u32, vp, *E]),
+    "yattn_decode_run_pooled_rope": (C.c_int, [vp, vp, vp, u32, u32, u32, u32, u32, u32, u32, vp, sz, C.c_int, u32,
+                                               C.c_float, vp, sz, vp, *E]),
     "yattn_decode_exchange": (C.c_int, [vp, vp, vp, u32, u32, u32, u32, u32, u32, vp, u32, u32, vp, vp, u64, vp, sz,
                                         vp, *E]),
     "yattn_attn_decode_noalloc": (C.c_int, [vp, vp, vp, vp, vp, u32, u32, u32, u32, u32, vp, *E]),

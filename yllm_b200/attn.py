@@ -19,7 +19,8 @@ import numpy as np
 import torch
 
 from . import _lib
-from ._lib import YattnDecodeItem, YattnDecodeWork, YattnQkNorm, YattnRopeItem, call, call_void, lib
+from ._lib import (YattnDecodeItem, YattnDecodeNewRow, YattnDecodeWork, YattnQkNorm, YattnRopeItem, call,
+                   call_void, lib)
 
 
 def _ptr(t: Optional[torch.Tensor]) -> Optional[int]:
@@ -176,6 +177,18 @@ class DecodePlan:
         return DecodePlan(n, n_heads, n_kv_heads, head_dim, kv_dim, dev, n_work.value, n_parts.value,
                           n_groups.value, ws, tuple(pool) if pool is not None else None)
 
+    def run_rope(self, items_dev: torch.Tensor, rows_dev: torch.Tensor, rope_kind: int, theta: float,
+                 n_rope_dims: int = 0, stream=None) -> None:
+        """run() with the step's RoPE + KV store fused in (yattn_decode_run_pooled_rope): items' q unrotated,
+        rows_dev (make_new_rows) the new tokens' k and v; pooled plans only."""
+        if self.pool is None:
+            raise ValueError("the fused RoPE store runs on a pooled plan")
+        ws_ptr = self.workspace.data_ptr() if self.workspace is not None else None
+        ws_len = self.workspace.numel() if self.workspace is not None else 0
+        call("yattn_decode_run_pooled_rope", items_dev.data_ptr(), rows_dev.data_ptr(), self.work.data_ptr(),
+             self.n_work, self.n_parts, self.n_groups, self.n_heads, self.n_kv_heads, self.head_dim, self.kv_dim,
+             self.pool[0], self.pool[1], rope_kind, n_rope_dims, theta, ws_ptr, ws_len, _stream(stream))
+
     def run(self, items_dev: torch.Tensor, stream=None) -> None:
         ws_ptr = self.workspace.data_ptr() if self.workspace is not None else None
         ws_len = self.workspace.numel() if self.workspace is not None else 0
@@ -204,6 +217,18 @@ def make_items(entries: Sequence[tuple], device=None) -> torch.Tensor:
 
 
 ROPE_LLAMA, ROPE_QWEN, ROPE_MROPE = 0, 1, 2
+
+
+def make_new_rows(entries: Sequence[tuple], device=None) -> torch.Tensor:
+    """Device array of YattnDecodeNewRow from (k, v) tensors: each item's new token (fp32, n_kv_heads*head_dim)."""
+    arr = (YattnDecodeNewRow * len(entries))()
+    for i, (k, v) in enumerate(entries):
+        _need(k, torch.float32, "k")
+        _need(v, torch.float32, "v")
+        arr[i].k = k.data_ptr()
+        arr[i].v = v.data_ptr()
+    raw = bytearray(C.string_at(arr, C.sizeof(arr)))
+    return torch.frombuffer(raw, dtype=torch.uint8).to(device or "cuda")
 
 
 def make_rope_items(entries: Sequence[tuple], device=None) -> torch.Tensor:

@@ -209,6 +209,41 @@ __host__ __device__ __forceinline__ uint16_t engine_f32_to_f16(float f) {
     return static_cast<uint16_t>(sign | (static_cast<uint32_t>(e) << 10) | (man >> 13));
 }
 
+// RoPE rotation of the pair (a, b) of inverse frequency inv_freq at position pos, in the
+// reference's fp32 operation order (matvec.c:890-939): angle = one fp32 multiply,
+// a*c - b*s and a*s + b*c without FMA contraction.  Shared by the RoPE store and the
+// decode with the fused store, so both give the same bits.
+__device__ __forceinline__ void rope_sincos(float inv_freq, uint32_t pos, float& s, float& c) {
+    sincosf(__fmul_rn(inv_freq, static_cast<float>(pos)), &s, &c);
+}
+__device__ __forceinline__ void rope_apply(float& a, float& b, float s, float c) {
+    const float ra = __fsub_rn(__fmul_rn(a, c), __fmul_rn(b, s));
+    const float rb = __fadd_rn(__fmul_rn(a, s), __fmul_rn(b, c));
+    a = ra;
+    b = rb;
+}
+__device__ __forceinline__ void rope_rotate(float& a, float& b, float inv_freq, uint32_t pos) {
+    float s, c;
+    rope_sincos(inv_freq, pos, s, c);
+    rope_apply(a, b, s, c);
+}
+
+// Element indices (e0, e1) of RoPE pair j inside a head: kind 0 (2j, 2j+1), kind 1
+// (j, j + hd/2), kind 2 (j, j + n_dims/2).
+__host__ __device__ __forceinline__ void rope_pair(uint32_t kind, uint32_t hd, uint32_t n_dims, uint32_t j,
+                                                   uint32_t& e0, uint32_t& e1) {
+    if (kind == 0) {
+        e0 = 2 * j;
+        e1 = 2 * j + 1;
+    } else if (kind == 1) {
+        e0 = j;
+        e1 = j + hd / 2;
+    } else {
+        e0 = j;
+        e1 = j + n_dims / 2;
+    }
+}
+
 // fp16 bits -> fp32, exact (hardware conversion).
 __device__ __forceinline__ float h2f(uint16_t h) { return __half2float(__ushort_as_half(h)); }
 

@@ -86,6 +86,20 @@ struct DecodeParams {
     float* out_o;                     // partial_only: [n_heads][HD]
 };
 
+// The fused RoPE + KV store of yattn_decode_run_pooled_rope: per item the new
+// token's k and v (fp32, rows[item]); q is read unrotated.  inv_freq[j] =
+// theta^(-2j/d), the reference's powf values (computed on the host).
+constexpr int kRopeMaxPairs = 128;
+struct DecodeRope {
+    const YattnDecodeNewRow* rows;
+    uint64_t pool_rows;                   // rows of the pool: the new rows are written inside it only
+    uint32_t kind, n_dims;                // rope kind (0 llama, 1 qwen, 2 M-RoPE), rotated dims
+    float inv_freq[kRopeMaxPairs];
+};
+
+// Threads of k_decode: NCW consumer warps, the producer, and (ROPE) the RoPE warp.
+template <int HD, bool ROPE> constexpr int decode_threads() { return DecodeCfg<HD>::THREADS + (ROPE ? 32 : 0); }
+
 __host__ __device__ __forceinline__ void group_of(uint32_t kvh, uint32_t n_heads, uint32_t n_kv, uint32_t& first,
                                                   uint32_t& cnt) {
     // heads hh with hh*n_kv/n_heads == kvh: ceil(kvh*n_heads/n_kv) .. ceil((kvh+1)*n_heads/n_kv)-1
@@ -151,13 +165,14 @@ __device__ __forceinline__ uint32_t first_unit_from(const YattnDecodeWork* work,
 // One unit of a CTA: entry u of the plan, or split u of the single-query form.
 struct DecodeUnit {
     YattnDecodeItem it;
-    uint32_t kg, t0, t1, n_splits, split, part_base, group;
+    uint32_t kg, t0, t1, n_splits, split, part_base, group, item;
 };
 __device__ __forceinline__ DecodeUnit unit_of(const DecodeParams& p, uint32_t u, uint32_t HC) {
     DecodeUnit x;
     if (p.work) {
         const YattnDecodeWork w = p.work[u];
         x.it = p.items[w.item];
+        x.item = w.item;
         x.kg = w.kv_head / HC;
         x.t0 = w.t_begin;
         x.t1 = w.t_end;
@@ -167,6 +182,7 @@ __device__ __forceinline__ DecodeUnit unit_of(const DecodeParams& p, uint32_t u,
         x.group = w.group;
     } else {
         x.it = p.item0;
+        x.item = 0;
         x.kg = u / p.n_splits0;
         x.split = u % p.n_splits0;
         x.n_splits = p.n_splits0;
@@ -199,10 +215,141 @@ template <int DPL> __device__ __forceinline__ void ldcg_vec(const float* src, fl
     }
 }
 
+// The fused RoPE store's two pieces, kept out of line: they run once per unit,
+// and inlined they would raise the register pressure of the tile loop.
+//
+// One warp: query heads [0, nq) of a q slot (nq * HD floats in shared memory, the
+// unit's q as read) rotated by RoPE at pos in place.  Each lane takes pairs
+// j = lane + 32k, one sincos per pair for all heads, with rope_rotate's
+// operations, so the values equal those of the RoPE store.
+template <int HD>
+__device__ __noinline__ void rope_q_slot(float* slot, uint32_t nq, const float* s_freq, uint32_t kind,
+                                         uint32_t n_dims, uint32_t pos, uint32_t lane) {
+    const uint32_t half = (kind == 2 ? n_dims : static_cast<uint32_t>(HD)) / 2;
+    for (uint32_t j = lane; j < half; j += 32) {
+        float sn, cs;
+        rope_sincos(s_freq[j], pos, sn, cs);
+        uint32_t e0, e1;
+        rope_pair(kind, HD, n_dims, j, e0, e1);
+        for (uint32_t h = 0; h < nq; ++h) {
+            float a = slot[h * HD + e0], b = slot[h * HD + e1];
+            rope_apply(a, b, sn, cs);
+            slot[h * HD + e0] = a;
+            slot[h * HD + e1] = b;
+        }
+    }
+}
+
+// One warp: the new token's row of kv heads [kv0, kv0 + nh) -- k rotated, k and v
+// rounded with the engine's f32_to_f16 -- into cache row pos, then a proxy fence,
+// so that tensor copies ordered after it read the new values.
+// kn_g / vn_g: the new row's fp32 k and v of those heads (16-byte aligned), first
+// copied into stage (2 * nh * HD floats of shared memory) with all of a lane's
+// loads in flight, so the warp waits out one memory latency, not one per pair.
+template <int HD>
+__device__ __noinline__ void rope_new_rows(const YattnDecodeItem& it, const float* kn_g, const float* vn_g,
+                                           float* stage, uint32_t kv0, uint32_t nh, uint32_t kv_dim,
+                                           const float* s_freq, uint32_t kind, uint32_t n_dims, uint32_t lane) {
+    {
+        constexpr uint32_t kMax = DecodeCfg<HD>::HC_TM_MAX * HD / 4;   // float4 of k (and of v) at most
+        constexpr uint32_t kPer = (kMax + 31) / 32;
+        const uint32_t n4 = nh * HD / 4;
+        float4 xk[kPer], xv[kPer];
+#pragma unroll
+        for (uint32_t m = 0; m < kPer; ++m) {
+            const uint32_t c = lane + 32 * m;
+            if (c < n4) {
+                xk[m] = __ldg(reinterpret_cast<const float4*>(kn_g) + c);
+                xv[m] = __ldg(reinterpret_cast<const float4*>(vn_g) + c);
+            }
+        }
+#pragma unroll
+        for (uint32_t m = 0; m < kPer; ++m) {
+            const uint32_t c = lane + 32 * m;
+            if (c < n4) {
+                reinterpret_cast<float4*>(stage)[c] = xk[m];
+                reinterpret_cast<float4*>(stage)[n4 + c] = xv[m];
+            }
+        }
+        __syncwarp();
+    }
+    const float* kn = stage;
+    const float* vn = stage + nh * HD;
+    const uint32_t nd = kind == 2 ? n_dims : static_cast<uint32_t>(HD);
+    const size_t row = static_cast<size_t>(it.pos) * kv_dim + static_cast<size_t>(kv0) * HD;
+    uint16_t* kg = const_cast<uint16_t*>(it.k) + row;
+    uint16_t* vg = const_cast<uint16_t*>(it.v) + row;
+    for (uint32_t w = lane; w < nh * (nd / 2); w += 32) {
+        const uint32_t h = w / (nd / 2), j = w % (nd / 2);
+        uint32_t e0, e1;
+        rope_pair(kind, HD, n_dims, j, e0, e1);
+        float a = kn[h * HD + e0], b = kn[h * HD + e1];
+        rope_rotate(a, b, s_freq[j], it.pos);
+        kg[h * HD + e0] = engine_f32_to_f16(a);
+        kg[h * HD + e1] = engine_f32_to_f16(b);
+    }
+    for (uint32_t w = lane; w < nh * HD; w += 32) {
+        if (w % HD >= nd) kg[w] = engine_f32_to_f16(kn[w]);   // past M-RoPE's dims
+        vg[w] = engine_f32_to_f16(vn[w]);
+    }
+    asm volatile("fence.proxy.async.global;" ::: "memory");
+}
+
+// What the copies of a unit rely on, checked on the device (items live there).
+template <bool TM>
+__device__ __forceinline__ bool item_bad(const DecodeParams& p, const YattnDecodeItem& it) {
+    const uint64_t ka = reinterpret_cast<uint64_t>(it.k), va = reinterpret_cast<uint64_t>(it.v);
+    bool bad = ((reinterpret_cast<uintptr_t>(it.q) | reinterpret_cast<uintptr_t>(it.gate)) & 15u) != 0;
+    if (TM)
+        bad = bad || ka < p.kmap_base || va < p.vmap_base || (ka - p.kmap_base) % p.row_bytes != 0 ||
+              (va - p.vmap_base) % p.row_bytes != 0;
+    return bad;
+}
+
+// The unit that ends at its item's position holds the item's new row (the last split).
+__device__ __forceinline__ bool unit_has_new_row(const DecodeUnit& un) {
+    return un.t0 < un.t1 && un.t1 == un.it.pos + 1;
+}
+
+__device__ __forceinline__ void st_release_cta(uint32_t* p, uint32_t v) {
+    asm volatile("st.release.cta.shared.u32 [%0], %1;" ::"r"(smem_u32(p)), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint32_t ld_acquire_cta(const uint32_t* p) {
+    uint32_t v;
+    asm volatile("ld.acquire.cta.shared.u32 %0, [%1];" : "=r"(v) : "r"(smem_u32(p)) : "memory");
+    return v;
+}
+
+// Warp-uniform bounded wait until the shared counter *cnt reaches target (acquire).
+// On timeout: records code in *status, sets the abort flag and returns false.
+__device__ __forceinline__ bool warp_wait_count(const uint32_t* cnt, uint32_t target, int* status, int code,
+                                                volatile int* abort_flag) {
+    bool ok = true;
+    if (static_cast<int>(ld_acquire_cta(cnt) - target) < 0) {
+        const unsigned long long t0 = globaltimer_ns();
+        for (uint32_t it = 0;; ++it) {
+            if (static_cast<int>(ld_acquire_cta(cnt) - target) >= 0) break;
+            if ((it & 63u) == 63u) {
+                if (*abort_flag) {
+                    ok = false;
+                    break;
+                }
+                if (globaltimer_ns() - t0 > kWaitLimitNs) {
+                    if (status) atomicCAS(status, 0, code);
+                    *abort_flag = 1;
+                    ok = false;
+                    break;
+                }
+            }
+        }
+    }
+    return __all_sync(0xffffffffu, ok);
+}
+
 // Shared-memory layout of k_decode<HD, G, TM>: the ring of NST stages, (TM) one
 // q slot per stage, the ring's barriers, one unit descriptor per stage, the
 // consumer warps' P^T staging, their (m, l) for the merge, and flags.
-template <int HD, int G, bool TM> struct DecodeSmem {
+template <int HD, int G, bool TM, bool ROPE = false> struct DecodeSmem {
     using C = DecodeCfg<HD>;
     static constexpr int STAGE = TM ? C::STAGE_TM : C::STAGE_ROW;
     static constexpr int QSLOT = TM ? C::HC_TM_MAX * G * HD * 4 : 0;   // q of a unit's query heads, fp32
@@ -213,9 +360,14 @@ template <int HD, int G, bool TM> struct DecodeSmem {
     static constexpr int OFF_PT = OFF_DESC + C::NST * DESC;
     static constexpr int OFF_ML = OFF_PT + C::NCW * C::PT_BYTES;
     static constexpr int OFF_FLAGS = OFF_ML + C::NCW * G * 2 * 4;
-    static constexpr int BYTES = OFF_FLAGS + 16 + (TM ? 1024 : 0);   // + alignment slack of the ring
+    static constexpr int OFF_FREQ = OFF_FLAGS + 16;                  // ROPE: inverse frequencies
+    // ROPE: u32 counters [0] new rows written (RoPE warp), [1] first-tile stages claimed (producer)
+    static constexpr int OFF_ROWS = OFF_FREQ + (ROPE ? kRopeMaxPairs * 4 : 0);
+    static constexpr int OFF_RSTAGE = OFF_ROWS + (ROPE ? 16 : 0);     // ROPE: the new row's k and v, fp32
+    static constexpr int BYTES = OFF_RSTAGE + (ROPE ? 2 * C::HC_TM_MAX * HD * 4 : 0) + (TM ? 1024 : 0);   // + ring alignment slack
     static_assert(2 * 16 * C::NCW * HD * 2 >= C::NCW * G * HD * 4, "the warps' merge fits in one ring stage");
     static_assert(BYTES <= 232448, "shared memory of one CTA");
+    static_assert(OFF_RSTAGE % 16 == 0, "16-byte stores into the row staging area");
 };
 
 // Warp NCW is the producer; consumer warp w owns kv head kg*HC + (w % HC) of
@@ -238,12 +390,24 @@ template <int HD, int G, bool TM> struct DecodeSmem {
 // the unit from the slot, so none of the unit's setup waits on global memory,
 // and they merge in the stage of the unit's last tile, which they release only
 // after the merge: the producer keeps the other stages streaming meanwhile.
-template <int HD, int G, bool TM>
-__global__ void __launch_bounds__(DecodeCfg<HD>::THREADS, 1)
+//
+// ROPE = true (tensor-copy kernels only): one more warp, the RoPE warp.  For the
+// unit that ends at the item's position -- the last split of each (item, head
+// group) -- it rotates the new token's k, rounds k and v with the engine's
+// f32_to_f16 and writes them into cache row pos; the producer copies the tile
+// that holds that row only after it.  For every unit it reads the unit's q heads
+// unrotated and writes them rotated into the q slot of the unit's first stage,
+// whose full barrier then takes its arrive as a second one.  That is
+// engine.c:1052-1072 fused into the attention; the producer only waits on a
+// counter before a unit's last tile, and the consumers run the same code as
+// without it.
+template <int HD, int G, bool TM, bool ROPE = false>
+__global__ void __launch_bounds__(decode_threads<HD, ROPE>(), 1)
     k_decode(const __grid_constant__ CUtensorMap kmap, const __grid_constant__ CUtensorMap vmap,
-             const DecodeParams p) {
+             const DecodeParams p, const __grid_constant__ DecodeRope rope) {
     using C = DecodeCfg<HD>;
-    using L = DecodeSmem<HD, G, TM>;
+    using L = DecodeSmem<HD, G, TM, ROPE>;
+    static_assert(!ROPE || TM, "the fused RoPE store runs in the tensor-copy kernels");
     constexpr int NCW = C::NCW;
     constexpr int KS = HD / 16;                                       // k-steps (QK) and m-tiles (PV)
     constexpr int DPL = HD / 32;                                      // dims per lane in the merges
@@ -290,11 +454,20 @@ __global__ void __launch_bounds__(DecodeCfg<HD>::THREADS, 1)
     }
     if (threadIdx.x == 0) {
         for (int s = 0; s < C::NST; ++s) {
-            mbar_init(&full[s], 1);
+            mbar_init(&full[s], ROPE ? 2 : 1);   // ROPE: + the RoPE warp (first tiles) or the producer again
             mbar_init(&empty[s], NCW);
+        }
+        if (ROPE) {
+            reinterpret_cast<volatile uint32_t*>(smem + L::OFF_ROWS)[0] = 0u;
+            reinterpret_cast<volatile uint32_t*>(smem + L::OFF_ROWS)[1] = 0u;
         }
         abort_flag[0] = 0;
         fence_mbar_init();
+    }
+    float* s_freq = reinterpret_cast<float*>(smem + L::OFF_FREQ);
+    if constexpr (ROPE) {
+        for (uint32_t j = threadIdx.x; j < static_cast<uint32_t>(kRopeMaxPairs); j += blockDim.x)
+            s_freq[j] = rope.inv_freq[j];
     }
     __syncthreads();
     const uint32_t u_begin = s_range[0], u_end = s_range[1];
@@ -310,16 +483,13 @@ __global__ void __launch_bounds__(DecodeCfg<HD>::THREADS, 1)
         }
         uint32_t gi = 0;   // tiles issued so far
         bool ok = true;
+        uint32_t nrow = 0;   // ROPE: new rows this CTA's units hold, up to the current unit
         for (uint32_t u = u_begin; u < u_end && ok; ++u) {
             const DecodeUnit un = unit_of(p, u, HC);
             const uint32_t ntiles = max(1u, (un.t1 - un.t0 + TOK - 1) / TOK);
+            const bool has_row = ROPE && unit_has_new_row(un);
             {   // items live on the device: check what the copies below rely on
-                const uint64_t ka = reinterpret_cast<uint64_t>(un.it.k), va = reinterpret_cast<uint64_t>(un.it.v);
-                bool bad = ((reinterpret_cast<uintptr_t>(un.it.q) | reinterpret_cast<uintptr_t>(un.it.gate)) & 15u) != 0;
-                if (TM)
-                    bad = bad || ka < p.kmap_base || va < p.vmap_base || (ka - p.kmap_base) % p.row_bytes != 0 ||
-                          (va - p.vmap_base) % p.row_bytes != 0;
-                if (bad) {
+                if (item_bad<TM>(p, un.it)) {
                     if (lane == 0) {
                         atomicCAS(p.status, 0, ST_DECODE_BAD_ITEM);
                         *abort_flag = 1;
@@ -351,6 +521,20 @@ __global__ void __launch_bounds__(DecodeCfg<HD>::THREADS, 1)
                 const uint32_t nrows = tile0 < un.t1 ? min(TOK, un.t1 - tile0) : 0u;
                 uint8_t* kdst = stages + s * STAGEB;
                 uint8_t* vdst = kdst + TILEB;
+                if constexpr (ROPE) {
+                    // a first tile's stage is free: the RoPE warp may fill its q slot and arrive
+                    if (i == 0 && lane == 0) st_release_cta(reinterpret_cast<uint32_t*>(smem + L::OFF_ROWS) + 1, gi + 1);
+                    // the new row lies in the unit's last tile: the RoPE warp has written it before that
+                    // tile is copied
+                    if (has_row && i + 1 == ntiles) {
+                        if (!warp_wait_count(reinterpret_cast<const uint32_t*>(smem + L::OFF_ROWS), nrow + 1,
+                                             p.status, ST_DECODE_FULL_TIMEOUT, abort_flag)) {
+                            ok = false;
+                            break;
+                        }
+                        ++nrow;
+                    }
+                }
                 if (i == 0 && lane == 0) {
                     *desc_at(s) = un;   // published by the arrive on full[s] below
                     if (un.it.gate) bulk_prefetch_l2(un.it.gate + static_cast<size_t>(qa) * HD, qbytes);
@@ -358,9 +542,10 @@ __global__ void __launch_bounds__(DecodeCfg<HD>::THREADS, 1)
                 if constexpr (TM) {
                     // whole boxes of TOK rows (rows past the unit are masked; past the map, zero-filled)
                     if (lane == 0) {
-                        mbar_arrive_expect_tx(&full[s], STAGEB + (i == 0 ? qbytes : 0u));
-                        if (i == 0)
+                        mbar_arrive_expect_tx(&full[s], STAGEB + (i == 0 && !ROPE ? qbytes : 0u));
+                        if (i == 0 && !ROPE)
                             bulk_g2s(qslots + s * L::QSLOT, un.it.q + static_cast<size_t>(qa) * HD, qbytes, &full[s]);
+                        if (ROPE && i > 0) mbar_arrive(&full[s]);   // a first tile's second arrive: the RoPE warp
                         for (uint32_t c = 0; c < HC * (HD / 64); ++c) {   // HC heads, 64 dims per box
                             const int32_t x = static_cast<int32_t>(un.kg * HC * HD + c * 64);
                             tma_load_2d(kdst + c * TOK * 128, &kmap, x, krow0 + static_cast<int32_t>(tile0), &full[s]);
@@ -385,6 +570,78 @@ __global__ void __launch_bounds__(DecodeCfg<HD>::THREADS, 1)
             mbar_wait_bounded(&full[g % C::NST], (g / C::NST) & 1u, p.status, ST_DECODE_FULL_TIMEOUT, &dummy);
         }
         return;
+    }
+
+    if constexpr (ROPE) {
+        if (warp == NCW + 1) {
+            // ================= RoPE warp =================
+            // Per unit, in the producer's order: once the producer has claimed the stage of the
+            // unit's first tile, the unit's q heads rotated into that stage's q slot and the first
+            // tile's second arrive; then the new row (if the unit holds it) written into the cache
+            // and counted in rows_done, which the producer waits for before it copies the unit's
+            // last tile.  Its global loads wait here, not in the producer.
+            uint32_t* rows_done = reinterpret_cast<uint32_t*>(smem + L::OFF_ROWS);
+            const uint32_t* claimed = rows_done + 1;
+            uint32_t gi = 0, nrow = 0;
+            for (uint32_t u = u_begin; u < u_end; ++u) {
+                const DecodeUnit un = unit_of(p, u, HC);
+                const uint32_t ntiles = max(1u, (un.t1 - un.t0 + TOK - 1) / TOK);
+                if (item_bad<TM>(p, un.it)) break;   // the producer reports it and stops
+                // the unit's q heads [qa, qa + nq), read before the wait below (all of a lane's
+                // loads in flight), so that their latency passes while the ring still streams
+                uint32_t qa, qn, qb, qm;
+                group_of(un.kg * HC, p.n_heads, p.n_kv, qa, qn);
+                group_of(un.kg * HC + HC - 1, p.n_heads, p.n_kv, qb, qm);
+                const uint32_t nq = qb + qm - qa, nq4 = nq * HD / 4;
+                constexpr uint32_t kQPer = (C::HC_TM_MAX * G * HD / 4 + 31) / 32;
+                const float4* q4 = reinterpret_cast<const float4*>(un.it.q + static_cast<size_t>(qa) * HD);
+                float4 xq[kQPer];
+    #pragma unroll
+                for (uint32_t m = 0; m < kQPer; ++m)
+                    if (lane + 32 * m < nq4) xq[m] = __ldg(q4 + lane + 32 * m);
+                // Wait until the producer has claimed the stage of the unit's first tile: it waited for
+                // that stage's release, so full[s] is in this tile's phase and stays there until the
+                // arrive below.  (A parity wait on empty[s] could not tell this tile's phase from one
+                // two uses earlier: this warp runs up to whole units ahead of the ring.)
+                const int s = gi % C::NST;
+                if (!warp_wait_count(claimed, gi + 1, p.status, ST_DECODE_EMPTY_TIMEOUT, abort_flag)) break;
+                float* slot = reinterpret_cast<float*>(qslots + s * L::QSLOT);
+    #pragma unroll
+                for (uint32_t m = 0; m < kQPer; ++m)
+                    if (lane + 32 * m < nq4) reinterpret_cast<float4*>(slot)[lane + 32 * m] = xq[m];
+                __syncwarp();
+                rope_q_slot<HD>(slot, nq, s_freq, rope.kind, rope.n_dims, un.it.pos, lane);
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&full[s]);
+                if (unit_has_new_row(un)) {
+                    // the rows written lie inside the pool
+                    const uint64_t kr = (reinterpret_cast<uint64_t>(un.it.k) - p.kmap_base) / p.row_bytes;
+                    const uint64_t vr = (reinterpret_cast<uint64_t>(un.it.v) - p.vmap_base) / p.row_bytes;
+                    if (kr + un.it.pos >= rope.pool_rows || vr + un.it.pos >= rope.pool_rows) {
+                        if (lane == 0) {
+                            atomicCAS(p.status, 0, ST_DECODE_BAD_ITEM);
+                            *abort_flag = 1;
+                        }
+                        break;
+                    }
+                    const YattnDecodeNewRow nr = rope.rows[un.item];
+                    if (((reinterpret_cast<uintptr_t>(nr.k) | reinterpret_cast<uintptr_t>(nr.v)) & 15u) != 0) {
+                        if (lane == 0) {
+                            atomicCAS(p.status, 0, ST_DECODE_BAD_ITEM);
+                            *abort_flag = 1;
+                        }
+                        break;
+                    }
+                    const size_t h0 = static_cast<size_t>(un.kg) * HC * HD;
+                    rope_new_rows<HD>(un.it, nr.k + h0, nr.v + h0, reinterpret_cast<float*>(smem + L::OFF_RSTAGE),
+                                      un.kg * HC, HC, p.kv_dim, s_freq, rope.kind, rope.n_dims, lane);
+                    __syncwarp();
+                    if (lane == 0) st_release_cta(rows_done, ++nrow);
+                }
+                gi += ntiles;
+            }
+            return;
+        }
     }
 
     // ================= consumers =================
@@ -892,10 +1149,10 @@ __global__ void k_merge_partials(float* out, const float* ml, const float* o, ui
 }
 
 // ------------------------------------------------------------------ dispatch
-template <int HD, int G, bool TM>
-int launch_t(const DecodeParams& p, const CUtensorMap& km, const CUtensorMap& vm, uint32_t grid, cudaStream_t st,
-             char* err, size_t errlen) {
-    const size_t smem = DecodeSmem<HD, G, TM>::BYTES;
+template <int HD, int G, bool TM, bool ROPE>
+int launch_t(const DecodeParams& p, const CUtensorMap& km, const CUtensorMap& vm, const DecodeRope& rope,
+             uint32_t grid, cudaStream_t st, char* err, size_t errlen) {
+    const size_t smem = DecodeSmem<HD, G, TM, ROPE>::BYTES;
     if (TM && p.hc > static_cast<uint32_t>(DecodeCfg<HD>::HC_TM_MAX)) {
         set_err(err, errlen, "decode: %u kv heads per CTA with tensor copies (max %d)", p.hc, DecodeCfg<HD>::HC_TM_MAX);
         return -1;
@@ -904,7 +1161,7 @@ int launch_t(const DecodeParams& p, const CUtensorMap& km, const CUtensorMap& vm
     int dev = 0;
     cudaGetDevice(&dev);
     if (dev >= 0 && dev < 64 && !attr_done[dev]) {
-        cudaError_t e = cudaFuncSetAttribute(k_decode<HD, G, TM>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        cudaError_t e = cudaFuncSetAttribute(k_decode<HD, G, TM, ROPE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                              static_cast<int>(smem));
         if (e != cudaSuccess) {
             set_err(err, errlen, "decode: smem attribute: %s", cudaGetErrorString(e));
@@ -912,46 +1169,59 @@ int launch_t(const DecodeParams& p, const CUtensorMap& km, const CUtensorMap& vm
         }
         attr_done[dev] = true;
     }
-    k_decode<HD, G, TM><<<grid, DecodeCfg<HD>::THREADS, smem, st>>>(km, vm, p);
+    k_decode<HD, G, TM, ROPE><<<grid, decode_threads<HD, ROPE>(), smem, st>>>(km, vm, p, rope);
     YATTN_CHECK_LAUNCH(err, errlen, "decode");
     return 0;
 }
 
-template <int HD, bool TM>
-int launch_hd(const DecodeParams& p, const CUtensorMap& km, const CUtensorMap& vm, uint32_t gmax, uint32_t grid,
-              cudaStream_t st, char* err, size_t errlen) {
+template <int HD, bool TM, bool ROPE>
+int launch_hd(const DecodeParams& p, const CUtensorMap& km, const CUtensorMap& vm, const DecodeRope& rope,
+              uint32_t gmax, uint32_t grid, cudaStream_t st, char* err, size_t errlen) {
     switch (gmax) {
-        case 1: return launch_t<HD, 1, TM>(p, km, vm, grid, st, err, errlen);
-        case 2: return launch_t<HD, 2, TM>(p, km, vm, grid, st, err, errlen);
-        case 3: return launch_t<HD, 3, TM>(p, km, vm, grid, st, err, errlen);
-        case 4: return launch_t<HD, 4, TM>(p, km, vm, grid, st, err, errlen);
-        case 5: return launch_t<HD, 5, TM>(p, km, vm, grid, st, err, errlen);
-        case 6: return launch_t<HD, 6, TM>(p, km, vm, grid, st, err, errlen);
-        case 7: return launch_t<HD, 7, TM>(p, km, vm, grid, st, err, errlen);
-        case 8: return launch_t<HD, 8, TM>(p, km, vm, grid, st, err, errlen);
+        case 1: return launch_t<HD, 1, TM, ROPE>(p, km, vm, rope, grid, st, err, errlen);
+        case 2: return launch_t<HD, 2, TM, ROPE>(p, km, vm, rope, grid, st, err, errlen);
+        case 3: return launch_t<HD, 3, TM, ROPE>(p, km, vm, rope, grid, st, err, errlen);
+        case 4: return launch_t<HD, 4, TM, ROPE>(p, km, vm, rope, grid, st, err, errlen);
+        case 5: return launch_t<HD, 5, TM, ROPE>(p, km, vm, rope, grid, st, err, errlen);
+        case 6: return launch_t<HD, 6, TM, ROPE>(p, km, vm, rope, grid, st, err, errlen);
+        case 7: return launch_t<HD, 7, TM, ROPE>(p, km, vm, rope, grid, st, err, errlen);
+        case 8: return launch_t<HD, 8, TM, ROPE>(p, km, vm, rope, grid, st, err, errlen);
         default: set_err(err, errlen, "decode: %u query heads per kv head (max 8)", gmax); return -1;
     }
 }
 
 // tm: tensor-copy kernels (p.hc must be 1, km / vm valid); otherwise the row-copy kernels.
+// rope (tensor-copy kernels only): the fused RoPE + KV store variant.
 int launch_decode(const DecodeParams& p, bool tm, const CUtensorMap* km, const CUtensorMap* vm, uint32_t head_dim,
-                  uint32_t grid, cudaStream_t st, char* err, size_t errlen) {
+                  uint32_t grid, cudaStream_t st, char* err, size_t errlen, const DecodeRope* rope = nullptr) {
     const uint32_t gmax = (p.n_heads + p.n_kv - 1) / p.n_kv;
     static const CUtensorMap none{};
+    static const DecodeRope no_rope{};
     const CUtensorMap& k = km ? *km : none;
     const CUtensorMap& v = vm ? *vm : none;
-    if (tm) {
+    if (rope) {
+        if (!tm) {
+            set_err(err, errlen, "decode: the fused RoPE store needs the pooled (tensor-copy) path");
+            return -1;
+        }
         switch (head_dim) {
-            case 64: return launch_hd<64, true>(p, k, v, gmax, grid, st, err, errlen);
-            case 128: return launch_hd<128, true>(p, k, v, gmax, grid, st, err, errlen);
-            case 256: return launch_hd<256, true>(p, k, v, gmax, grid, st, err, errlen);
+            case 64: return launch_hd<64, true, true>(p, k, v, *rope, gmax, grid, st, err, errlen);
+            case 128: return launch_hd<128, true, true>(p, k, v, *rope, gmax, grid, st, err, errlen);
+            case 256: return launch_hd<256, true, true>(p, k, v, *rope, gmax, grid, st, err, errlen);
+            default: break;
+        }
+    } else if (tm) {
+        switch (head_dim) {
+            case 64: return launch_hd<64, true, false>(p, k, v, no_rope, gmax, grid, st, err, errlen);
+            case 128: return launch_hd<128, true, false>(p, k, v, no_rope, gmax, grid, st, err, errlen);
+            case 256: return launch_hd<256, true, false>(p, k, v, no_rope, gmax, grid, st, err, errlen);
             default: break;
         }
     } else {
         switch (head_dim) {
-            case 64: return launch_hd<64, false>(p, k, v, gmax, grid, st, err, errlen);
-            case 128: return launch_hd<128, false>(p, k, v, gmax, grid, st, err, errlen);
-            case 256: return launch_hd<256, false>(p, k, v, gmax, grid, st, err, errlen);
+            case 64: return launch_hd<64, false, false>(p, k, v, no_rope, gmax, grid, st, err, errlen);
+            case 128: return launch_hd<128, false, false>(p, k, v, no_rope, gmax, grid, st, err, errlen);
+            case 256: return launch_hd<256, false, false>(p, k, v, no_rope, gmax, grid, st, err, errlen);
             default: break;
         }
     }
@@ -1405,7 +1675,7 @@ namespace {
 int decode_run_impl(const YattnDecodeItem* items_dev, const YattnDecodeWork* work_dev, uint32_t n_work,
                     uint32_t n_parts, uint32_t n_groups, uint32_t n_heads, uint32_t n_kv_heads, uint32_t head_dim,
                     uint32_t kv_dim, const void* pool, size_t pool_bytes, void* workspace, size_t ws_bytes,
-                    void* stream, char* err, size_t errlen) {
+                    void* stream, char* err, size_t errlen, const DecodeRope* rope = nullptr) {
     if (check_geom(n_heads, n_kv_heads, head_dim, kv_dim, err, errlen)) return -1;
     if (n_work == 0) return 0;
     if (!items_dev || !work_dev) {
@@ -1448,6 +1718,12 @@ int decode_run_impl(const YattnDecodeItem* items_dev, const YattnDecodeWork* wor
     if (encode_kv_map(&map, pool, kv_dim, rows, box_rows, err, errlen)) return -1;
     p.kmap_base = p.vmap_base = reinterpret_cast<uint64_t>(pool);
     p.row_bytes = kv_dim * 2;
+    if (rope) {
+        DecodeRope r = *rope;
+        r.pool_rows = rows;
+        return launch_decode(p, true, &map, &map, head_dim, n_work, static_cast<cudaStream_t>(stream), err, errlen,
+                             &r);
+    }
     return launch_decode(p, true, &map, &map, head_dim, n_work, static_cast<cudaStream_t>(stream), err, errlen);
 }
 }  // namespace
@@ -1471,6 +1747,36 @@ extern "C" int yattn_decode_run_pooled(const YattnDecodeItem* items_dev, const Y
     }
     return decode_run_impl(items_dev, work_dev, n_work, n_parts, n_groups, n_heads, n_kv_heads, head_dim, kv_dim,
                            pool, pool_bytes, workspace, ws_bytes, stream, err, errlen);
+}
+
+extern "C" int yattn_decode_run_pooled_rope(const YattnDecodeItem* items_dev, const YattnDecodeNewRow* rows_dev,
+                                            const YattnDecodeWork* work_dev, uint32_t n_work, uint32_t n_parts,
+                                            uint32_t n_groups, uint32_t n_heads, uint32_t n_kv_heads,
+                                            uint32_t head_dim, uint32_t kv_dim, const void* pool, size_t pool_bytes,
+                                            int rope_kind, uint32_t n_rope_dims, float theta, void* workspace,
+                                            size_t ws_bytes, void* stream, char* err, size_t errlen) {
+    if (!pool || !rows_dev) {
+        set_err(err, errlen, "decode_run_pooled_rope: null pool or rows");
+        return -1;
+    }
+    if (rope_kind < 0 || rope_kind > 2) {
+        set_err(err, errlen, "decode_run_pooled_rope: rope_kind %d (0 llama, 1 qwen, 2 mrope)", rope_kind);
+        return -1;
+    }
+    const uint32_t nd = rope_kind == 2 ? n_rope_dims : head_dim;
+    if (nd == 0 || (nd & 1) || nd > head_dim || nd / 2 > static_cast<uint32_t>(kRopeMaxPairs)) {
+        set_err(err, errlen, "decode_run_pooled_rope: %u rotated dims for head_dim %u", nd, head_dim);
+        return -1;
+    }
+    DecodeRope rope{};
+    rope.rows = rows_dev;
+    rope.kind = static_cast<uint32_t>(rope_kind);
+    rope.n_dims = nd;
+    // the reference's expression, in the same fp32 operation order (matvec.c:895, 912, 929)
+    for (uint32_t j = 0; j < nd / 2; ++j)
+        rope.inv_freq[j] = powf(theta, -2.0f * static_cast<float>(j) / static_cast<float>(nd));
+    return decode_run_impl(items_dev, work_dev, n_work, n_parts, n_groups, n_heads, n_kv_heads, head_dim, kv_dim,
+                           pool, pool_bytes, workspace, ws_bytes, stream, err, errlen, &rope);
 }
 
 extern "C" size_t yattn_decode_partial_workspace_bytes(uint32_t n_tokens, uint32_t n_heads, uint32_t n_kv_heads,

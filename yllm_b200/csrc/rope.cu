@@ -46,32 +46,6 @@ struct RopeParams {
     float inv_freq[kMaxPairs];       // theta^(-2j/n_dims), the reference's powf values
 };
 
-// Rotates the pair (a, b) of pair index j at position pos.
-__device__ __forceinline__ void rotate(float& a, float& b, float inv_freq, uint32_t pos) {
-    const float ang = __fmul_rn(inv_freq, static_cast<float>(pos));
-    float s, c;
-    sincosf(ang, &s, &c);
-    const float ra = __fsub_rn(__fmul_rn(a, c), __fmul_rn(b, s));
-    const float rb = __fadd_rn(__fmul_rn(a, s), __fmul_rn(b, c));
-    a = ra;
-    b = rb;
-}
-
-// Element indices of pair j inside a head for the rope kind.
-__device__ __forceinline__ void pair_of(uint32_t kind, uint32_t hd, uint32_t n_dims, uint32_t j, uint32_t& e0,
-                                        uint32_t& e1) {
-    if (kind == 0) {
-        e0 = 2 * j;
-        e1 = 2 * j + 1;
-    } else if (kind == 1) {
-        e0 = j;
-        e1 = j + hd / 2;
-    } else {
-        e0 = j;
-        e1 = j + n_dims / 2;
-    }
-}
-
 // Row `blockIdx.y` of the launch: the item, or row b of the batch form.
 __device__ __forceinline__ YattnRopeItem item_of(const RopeParams& p) {
     YattnRopeItem it;
@@ -108,19 +82,19 @@ __global__ void __launch_bounds__(256) k_rope_store(const RopeParams p) {
         if (u < nq) {
             const uint32_t h = u / pairs, j = u % pairs;
             uint32_t e0, e1;
-            pair_of(p.kind, p.hd, p.n_dims, j, e0, e1);
+            rope_pair(p.kind, p.hd, p.n_dims, j, e0, e1);
             float* qh = it.q + static_cast<size_t>(h) * p.hd;
             float a = qh[e0], b = qh[e1];
-            rotate(a, b, s_freq[j], it.pos);
+            rope_rotate(a, b, s_freq[j], it.pos);
             qh[e0] = a;
             qh[e1] = b;
         } else if (u < nq + nk) {
             const uint32_t w = u - nq, h = w / pairs, j = w % pairs;
             uint32_t e0, e1;
-            pair_of(p.kind, p.hd, p.n_dims, j, e0, e1);
+            rope_pair(p.kind, p.hd, p.n_dims, j, e0, e1);
             const float* kh = it.k + static_cast<size_t>(h) * p.hd;
             float a = kh[e0], b = kh[e1];
-            rotate(a, b, s_freq[j], it.pos);
+            rope_rotate(a, b, s_freq[j], it.pos);
             krow[h * p.hd + e0] = engine_f32_to_f16(a);
             krow[h * p.hd + e1] = engine_f32_to_f16(b);
         } else if (u < nq + nk + nr) {
@@ -182,9 +156,9 @@ __global__ void __launch_bounds__(128) k_qknorm_rope_store(const RopeParams p) {
     for (uint32_t u = t; u < pairs + (hd - p.n_dims); u += 128) {
         if (u < pairs) {
             uint32_t e0, e1;
-            pair_of(p.kind, hd, p.n_dims, u, e0, e1);
+            rope_pair(p.kind, hd, p.n_dims, u, e0, e1);
             float a = s_x[e0], b = s_x[e1];
-            rotate(a, b, s_freq[u], it.pos);
+            rope_rotate(a, b, s_freq[u], it.pos);
             if (is_q) {
                 qh[e0] = a;
                 qh[e1] = b;
