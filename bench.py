@@ -47,7 +47,7 @@ def load_peaks() -> tuple[dict, str]:
 # capture report null.
 # dram__bytes_read.sum + dram__bytes_write.sum of one launch of each workload's dominant kernel, from the ncu
 # captures summarised under profiles/ (same workloads; --layers-reduced steps have the same per-launch bytes)
-NCU_TRAFFIC = {"decode": 1226090496, "prefill": 25237504, "gated_prefill": 168607744, "gated_decode": 274070272,
+NCU_TRAFFIC = {"decode": 1225510144, "prefill": 25237504, "gated_prefill": 168607744, "gated_decode": 274070272,
                "long_decode": 541052160, "gdn_inputs": 225114112, "rope_store": 1590784,
                "gdn_decode": 78914048, "gdn_prefill_state": 257715456}
 
