@@ -1147,7 +1147,7 @@ def run_gemv(args, fmt: str = "q4k") -> None:
     ach = step_bytes / (per_call / 1e3) / 1e9
     roof = {"bound": "hbm", "achieved": round(ach, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
             "frac": round(ach / peaks["hbm_gbs"], 4), "traffic": None,
-            "kernel": "k_gemv_f16<4,1,2>" if f16 else "k_gemv_q4k_t1<4,KS>",
+            "kernel": "k_gemv_f16<4,1,2>" if f16 else "k_gemv_q4k_tc<1,KS,2> (mma.sync)",
             "peak_source": src, "bytes_per_step": step_bytes,
             "note": "224 launches per step in one graph; achieved = weight bytes / step device time"}
     e2e = None

@@ -60,7 +60,11 @@ def q4k_dequant_f64(w, out, in_):
     return y.reshape(out, in_)
 
 
-@pytest.mark.parametrize("out,in_,B", [(4096, 4096, 1), (1000, 512, 3), (14336, 4096, 4), (96, 2048, 9)])
+@pytest.mark.parametrize("out,in_,B", [(4096, 4096, 1), (1000, 512, 3), (14336, 4096, 4), (96, 2048, 9),
+                                      # one token: the shared-memory-fed kernel (rows of 1-2 blocks leave some
+                                      # k-chunks empty; a ragged last 16-row tile), and rows too long for one
+                                      # CTA's shared memory (the register-fed fallback)
+                                      (4096, 14336, 1), (1000, 512, 1), (37, 256, 1), (64, 18432, 1)])
 def test_gemv_q4k_matches_reference(dev, out, in_, B):
     from yllm_b200 import attn
 

@@ -11,11 +11,12 @@
 //
 // Here both read each weight byte once per launch, which is the bound (HBM):
 //   Q4_K: a 256-weight block is 144 B (d, dmin fp16; 12 B of 6-bit scales and
-//         mins; 128 B of nibbles).  Lane l of a warp takes nibble bytes
-//         4l..4l+3 of every block of a row: low nibbles of group 2(l/8), high
-//         nibbles of group 2(l/8)+1.  Per group it forms sum(nib*x) and sum(x)
-//         and adds d*sc*sum(nib*x) - dmin*mn*sum(x), the reference's
-//         per-weight expression summed in another order.
+//         mins; 128 B of nibbles).  One token: k_gemv_q4k_tc, the nibbles and
+//         x on the tensor cores (below).  A few tokens: k_gemv_q4k, lane l of a
+//         warp takes nibble bytes 4l..4l+3 of every block of a row: low nibbles
+//         of group 2(l/8), high nibbles of group 2(l/8)+1.  Per group both form
+//         sum(nib*x) and sum(x) and add d*sc*sum(nib*x) - dmin*mn*sum(x), the
+//         reference's per-weight expression summed in another order.
 //   fp16: lane l takes 8 consecutive weights (16 B) per 256-weight stripe.
 // A CTA works on R rows at once so each x value a lane loads serves R weights
 // (x would otherwise cost 8x the weight bytes in L1 traffic), and on NT tokens
@@ -72,6 +73,17 @@ __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
     return v;
+}
+
+__device__ __forceinline__ uint32_t h2_u32(__half2 h) { return *reinterpret_cast<uint32_t*>(&h); }
+
+// D(16x8 f32) += A(16x16 f16, row) * B(16x8 f16, col)
+__device__ __forceinline__ void mma_f16_16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
 
 // Sums acc[r][t] over the CTA's warps and writes y.  red: kWarps * R * NT floats of shared memory.
@@ -181,115 +193,182 @@ __global__ void __launch_bounds__(kWarps * 32) k_gemv_q4k(float* __restrict__ y,
     reduce_store<R, NT>(acc, red, y, row0, out, nt);
 }
 
-// Single-token Q4_K GEMV.  A warp step covers 4 blocks of R rows: lane l takes nibble bytes 16(l%8)..+15 of
-// block 4*step + l/8, i.e. elements e0..e0+15 (e0 = 16*(l%2)) of the pair p = (l%8)/2: group 2p from the low
-// nibbles, group 2p+1 from the high ones.  Four nibbles become bytes 0x80|n with one LOP3, and each byte
-// becomes the float 1 + n/128 with one byte permute (into byte 2 of 1.0f), so
-//   sum(n*x) = 128 * (sum((1 + n/128) * x) - sum(x)),
-// one FFMA per weight; sum(x) per group is shared by the R rows.  Each group's scale and min are decoded once
-// per block by one lane and passed to the two lanes that use them.
-// The CTA's 8 warps are KS k-slices (steps ks, ks + KS, ...) of 8/KS row groups of R rows, KS chosen so every
-// warp has a step even when a row has few blocks; the slices meet in shared memory.
-template <int R, int KS>
-__global__ void __launch_bounds__(kWarps * 32) k_gemv_q4k_t1(float* __restrict__ y, const uint8_t* __restrict__ w,
+// Single-token Q4_K GEMV on the tensor cores (mma.sync m16n8k16, fp16 in, fp32 accumulate).
+//
+// A (16 weight rows x 16 k) holds nibbles n as the fp16 subnormals n * 2^-24: the nibble bits ANDed out of a
+// 32-bit word of two weights' bytes are that half2 as is, exactly, one instruction per two weights.
+// B (16 k x 8 columns) holds x: per 256-weight block x is scaled by a power of two s (the block's largest |x|
+// goes to [2^14, 2^15)) and split into fp16 hi + lo (about 22 significant bits).  Column 2q + h of one
+// accumulator belongs to group q of a set of four (h: hi, lo); a k-step of group q has B zero outside its two
+// columns.  So after a set's 8 k-steps (4 groups x 2) lane (g, t) holds, for rows g and g + 8, the hi and lo
+// halves of sum(n x s) 2^-24 of group t of the set, and applies that group's d*sc and dmin*mn itself:
+//   y += (d*sc * sum(n x) - dmin*mn * sum(x)), the reference's per-weight expression summed in another order.
+// The k order inside a group: lane t takes bytes [8t, 8t + 8) of the group's 32-byte nibble chunk; of its
+// word of bytes b0..b3, k = 2t, 2t+1, 2t+8, 2t+9 are bytes b0, b2, b1, b3 (so a word ANDed with 0x000F000F
+// is the (2t, 2t+1) pair, shifted by 8 the (2t+8, 2t+9) pair; by 4 and 12 the high nibbles); B follows it.
+// Rows: warp w of the CTA takes MT 16-row tiles of row group w / KS and the blocks w % KS, + KS, ... of them,
+// U blocks per step with all their loads in flight; the k-slices meet in shared memory.
+template <int MT, int KS, int U>
+__global__ void __launch_bounds__(kWarps * 32) k_gemv_q4k_tc(float* __restrict__ y, const uint8_t* __restrict__ w,
                                                             const float* __restrict__ x, uint32_t out, uint32_t in) {
     constexpr int RG = kWarps / KS;                   // row groups per CTA
-    __shared__ float red[kWarps * R];
+    constexpr int ROWS = 16 * MT;                     // rows per row group
+    __shared__ float red[kWarps * ROWS];
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int g = lane >> 2, t = lane & 3;
     const int rg = warp / KS, ks = warp % KS;
-    const uint32_t row0 = (blockIdx.x * RG + rg) * R;
+    const uint32_t row0 = (blockIdx.x * RG + rg) * ROWS;
     const uint32_t nb = in / 256;
     const size_t row_bytes = static_cast<size_t>(nb) * kQ4kBlock;
-    const int k = lane & 7, sub = lane >> 3;          // chunk of the block, block of the step
-    const int p = k >> 1, e0 = 16 * (k & 1);
-    const int glo = 2 * p, ghi = glo + 1;
-    const int src_lo = (lane & ~7) | glo, src_hi = (lane & ~7) | ghi;   // lanes holding my groups' scales
-    float acc[R];
+    const uint8_t* rp[MT][2];                         // rows g and g + 8 of each tile (clamped: a padded tile
+#pragma unroll                                        // reads a real row and is not stored)
+    for (int m = 0; m < MT; ++m)
 #pragma unroll
-    for (int r = 0; r < R; ++r) acc[r] = 0.f;
-    const uint8_t* rows[R];
+        for (int r = 0; r < 2; ++r) rp[m][r] = w + static_cast<size_t>(min(row0 + 16 * m + 8 * r + g, out - 1)) * row_bytes;
+    float yacc[MT][2];
 #pragma unroll
-    for (int r = 0; r < R; ++r) rows[r] = w + static_cast<size_t>(min(row0 + r, out - 1)) * row_bytes;
-    const uint32_t nsteps = (nb + 3) / 4;
-    uint4 hA[R], qA[R];
-    auto load = [&](uint32_t st, uint4 (&H)[R], uint4 (&Q)[R]) {
-        const uint32_t bb = min(st * 4 + sub, nb - 1);
-#pragma unroll
-        for (int r = 0; r < R; ++r) {
-            const uint8_t* blk = rows[r] + static_cast<size_t>(bb) * kQ4kBlock;
-            H[r] = ldg_nc16(blk);
-            Q[r] = ldg_nc16(blk + 16 + 16 * k);
-        }
+    for (int m = 0; m < MT; ++m) yacc[m][0] = yacc[m][1] = 0.f;
+    const uint32_t zero = 0u;
+
+    // U blocks per step: all their loads are issued before any of them is used
+    struct Blk {
+        float xv[2][8];
+        uint4 hd[MT][2];
+        uint2 qw[MT][2][4];                       // [tile][row][chunk]: bytes 8t..8t+7 of the 32-byte chunk
     };
-    auto compute = [&](uint32_t st, const uint4 (&H)[R], const uint4 (&Q)[R]) {
-        const uint32_t b = st * 4 + sub;
-        const bool valid = b < nb;
-        const uint32_t bb = valid ? b : nb - 1;
-        float xl[16], xh[16];
-        const float* xb = x + static_cast<size_t>(bb) * 256;
+    auto load = [&](uint32_t b, Blk& k) {
+        // this lane's x (its groups g/2 and 4 + g/2, elements 8t..8t+7), the headers, the nibble words
 #pragma unroll
-        for (int i = 0; i < 16; i += 4) {
-            const float4 a = *reinterpret_cast<const float4*>(xb + glo * 32 + e0 + i);
-            const float4 c = *reinterpret_cast<const float4*>(xb + ghi * 32 + e0 + i);
-            xl[i] = a.x; xl[i + 1] = a.y; xl[i + 2] = a.z; xl[i + 3] = a.w;
-            xh[i] = c.x; xh[i + 1] = c.y; xh[i + 2] = c.z; xh[i + 3] = c.w;
-        }
-        float sxl = 0.f, sxh = 0.f;
-#pragma unroll
-        for (int i = 0; i < 16; ++i) {
-            sxl += xl[i];
-            sxh += xh[i];
+        for (int S = 0; S < 2; ++S) {
+            const int G = 4 * S + (g >> 1);
+            const float* xp = x + static_cast<size_t>(b) * 256 + 64 * (G >> 1) + 32 * (G & 1) + 8 * t;
+            const float4 a = *reinterpret_cast<const float4*>(xp);
+            const float4 c = *reinterpret_cast<const float4*>(xp + 4);
+            k.xv[S][0] = a.x; k.xv[S][1] = a.y; k.xv[S][2] = a.z; k.xv[S][3] = a.w;
+            k.xv[S][4] = c.x; k.xv[S][5] = c.y; k.xv[S][6] = c.z; k.xv[S][7] = c.w;
         }
 #pragma unroll
-        for (int r = 0; r < R; ++r) {
-            // my lane decodes group k of this block; the lanes of groups glo / ghi pass theirs over
-            float sc, mn;
-            scale_min(H[r], k, sc, mn);
-            const float d = half_lo(H[r].x), dmin = half_hi(H[r].x);
-            const float dk = d * sc, mk = dmin * mn;
-            const float d_lo = __shfl_sync(0xffffffffu, dk, src_lo), m_lo = __shfl_sync(0xffffffffu, mk, src_lo);
-            const float d_hi = __shfl_sync(0xffffffffu, dk, src_hi), m_hi = __shfl_sync(0xffffffffu, mk, src_hi);
-            const uint32_t q[4] = {Q[r].x, Q[r].y, Q[r].z, Q[r].w};
-            float sl[4], sh[4];   // four partial sums each: short FMA chains
+        for (int m = 0; m < MT; ++m)
 #pragma unroll
-            for (int j = 0; j < 4; ++j) {
-                sl[j] = 0.f;
-                sh[j] = 0.f;
-                // the word's 4 low / 4 high nibbles as bytes 0x80|n: byte 2 of the float 1.0f (0x3F800000) is
-                // 0x80, so placing 0x80|n there by one byte permute gives 1 + n/128 exactly
-                const uint32_t lob = (q[j] & 0x0F0F0F0Fu) | 0x80808080u;
-                const uint32_t hib = ((q[j] >> 4) & 0x0F0F0F0Fu) | 0x80808080u;
+            for (int r = 0; r < 2; ++r) {
+                const uint8_t* blk = rp[m][r] + static_cast<size_t>(b) * kQ4kBlock;
+                k.hd[m][r] = ldg_nc16(blk);
 #pragma unroll
-                for (int i = 0; i < 4; ++i) {
-                    const uint32_t sel = 0x7044u | (static_cast<uint32_t>(i) << 8);   // bytes [0, 0, b_i, 0x3F]
-                    const float fl = __uint_as_float(__byte_perm(lob, 0x3F000000u, sel));
-                    const float fh = __uint_as_float(__byte_perm(hib, 0x3F000000u, sel));
-                    sl[j] = fmaf(fl, xl[4 * j + i], sl[j]);
-                    sh[j] = fmaf(fh, xh[4 * j + i], sh[j]);
+                for (int j = 0; j < 4; ++j) {
+                    uint2 v;
+                    asm volatile("ld.global.nc.v2.u32 {%0,%1}, [%2];" : "=r"(v.x), "=r"(v.y)
+                                 : "l"(blk + 16 + 32 * j + 8 * t));
+                    k.qw[m][r][j] = v;
                 }
             }
-            const float nl = 128.f * (((sl[0] + sl[1]) + (sl[2] + sl[3])) - sxl);   // sum(n*x), low group
-            const float nh = 128.f * (((sh[0] + sh[1]) + (sh[2] + sh[3])) - sxh);
-            const float v = (d_lo * nl - m_lo * sxl) + (d_hi * nh - m_hi * sxh);
-            acc[r] += valid ? v : 0.f;
+    };
+    auto compute = [&](const Blk& k) {
+        // ---- the block's scale: 2^(14 - floor(log2 max|x|)), a power of two (exact) ----
+        float mx = 0.f;
+#pragma unroll
+        for (int S = 0; S < 2; ++S)
+#pragma unroll
+            for (int i = 0; i < 8; ++i) mx = fmaxf(mx, fabsf(k.xv[S][i]));
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+        const int ex = static_cast<int>((__float_as_uint(mx) >> 23) & 0xFFu);   // biased exponent of max|x|
+        const int se = mx > 0.f ? min(max(268 - ex, 1), 253) : 127;   // biased: 127 + 14 - (ex - 127)
+        const float sc_x = __uint_as_float(static_cast<uint32_t>(se) << 23);
+        const float unsc = __uint_as_float(static_cast<uint32_t>(254 - se) << 23);   // 1 / sc_x, exact
+        // ---- B fragments: x * s as hi (even g) or lo (odd g) halves, this lane's two groups; sums of x * s ----
+        uint32_t bf[2][2][2];                         // [set][sub-step][reg]
+        float sxg[2];
+#pragma unroll
+        for (int S = 0; S < 2; ++S) {
+            float part[8], sx = 0.f;
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                const float xs = k.xv[S][i] * sc_x;
+                const float hi = __half2float(__float2half_rn(xs));
+                part[i] = (g & 1) ? xs - hi : hi;
+                sx += xs;
+            }
+#pragma unroll
+            for (int s2 = 0; s2 < 2; ++s2) {
+                const float* q = part + 4 * s2;
+                bf[S][s2][0] = h2_u32(__floats2half2_rn(q[0], q[2]));   // k = 2t (byte 0), 2t + 1 (byte 2)
+                bf[S][s2][1] = h2_u32(__floats2half2_rn(q[1], q[3]));   // k = 2t + 8 (byte 1), 2t + 9 (byte 3)
+            }
+            sx += __shfl_xor_sync(0xffffffffu, sx, 1);
+            sx += __shfl_xor_sync(0xffffffffu, sx, 2);
+            sxg[S] = sx;                              // sum of x * s over group 4S + g/2
+        }
+        // group 4S + t's sum, from a lane whose g / 2 = t
+        const float sxt[2] = {__shfl_sync(0xffffffffu, sxg[0], 8 * t), __shfl_sync(0xffffffffu, sxg[1], 8 * t)};
+        // ---- per tile: two sets of 4 groups, 8 k-steps each, the two sets' chains interleaved ----
+#pragma unroll
+        for (int m = 0; m < MT; ++m) {
+            float c[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+#pragma unroll
+            for (int jj = 0; jj < 2; ++jj) {              // chunk j = 2S + jj: groups 2j (low) and 2j + 1 (high)
+#pragma unroll
+                for (int hn = 0; hn < 2; ++hn) {
+                    const int q = 2 * jj + hn;            // group within the set
+                    const bool mine = (g >> 1) == q;
+#pragma unroll
+                    for (int s2 = 0; s2 < 2; ++s2) {
+#pragma unroll
+                        for (int S = 0; S < 2; ++S) {
+                            const int j = 2 * S + jj;
+                            const uint32_t w0 = s2 ? k.qw[m][0][j].y : k.qw[m][0][j].x;   // row g
+                            const uint32_t w1 = s2 ? k.qw[m][1][j].y : k.qw[m][1][j].x;   // row g + 8
+                            const int sh = 4 * hn;
+                            uint32_t a[4];
+                            a[0] = (w0 >> sh) & 0x000F000Fu;
+                            a[1] = (w1 >> sh) & 0x000F000Fu;
+                            a[2] = (w0 >> (sh + 8)) & 0x000F000Fu;
+                            a[3] = (w1 >> (sh + 8)) & 0x000F000Fu;
+                            const uint32_t b0 = mine ? bf[S][s2][0] : zero, b1 = mine ? bf[S][s2][1] : zero;
+                            mma_f16_16816(c[S], a, b0, b1);
+                        }
+                    }
+                }
+            }
+            // lane (g, t): group 4S + t, rows g (c0 hi, c1 lo) and g + 8 (c2, c3)
+#pragma unroll
+            for (int S = 0; S < 2; ++S) {
+                const int G = 4 * S + t;
+#pragma unroll
+                for (int r = 0; r < 2; ++r) {
+                    float scv, mnv;
+                    scale_min(k.hd[m][r], G, scv, mnv);
+                    const float d = half_lo(k.hd[m][r].x), dmin = half_hi(k.hd[m][r].x);
+                    const float snx = (r ? c[S][2] + c[S][3] : c[S][0] + c[S][1]) * 16777216.0f;   // sum(n x s)
+                    yacc[m][r] += (d * scv * snx - dmin * mnv * sxt[S]) * unsc;
+                }
+            }
         }
     };
-    for (uint32_t st = ks; st < nsteps; st += KS) {
-        load(st, hA, qA);
-        compute(st, hA, qA);
-    }
+    for (uint32_t b0 = ks; b0 < nb; b0 += U * KS) {
+        Blk blk[U];
 #pragma unroll
-    for (int r = 0; r < R; ++r) {
-        const float v = warp_sum(acc[r]);
-        if (lane == 0) red[warp * R + r] = v;
+        for (int u = 0; u < U; ++u) load(min(b0 + u * KS, nb - 1), blk[u]);   // past the row: a repeat, unused
+#pragma unroll
+        for (int u = 0; u < U; ++u)
+            if (b0 + u * KS < nb) compute(blk[u]);
     }
+    // ---- lanes t = 0..3 of a row, then the CTA's k-slices ----
+#pragma unroll
+    for (int m = 0; m < MT; ++m)
+#pragma unroll
+        for (int r = 0; r < 2; ++r) {
+            float v = yacc[m][r];
+            v += __shfl_xor_sync(0xffffffffu, v, 1);
+            v += __shfl_xor_sync(0xffffffffu, v, 2);
+            if (t == 0) red[warp * ROWS + 16 * m + 8 * r + g] = v;
+        }
     __syncthreads();
-    if (threadIdx.x < RG * R) {
-        const int g = threadIdx.x / R, r = threadIdx.x % R;
+    for (int i = threadIdx.x; i < RG * ROWS; i += kWarps * 32) {
+        const int grp = i / ROWS, rr = i % ROWS;
         float v = 0.f;
 #pragma unroll
-        for (int kk = 0; kk < KS; ++kk) v += red[(g * KS + kk) * R + r];
-        const uint32_t row = (blockIdx.x * RG + g) * R + r;
+        for (int kk = 0; kk < KS; ++kk) v += red[(grp * KS + kk) * ROWS + rr];
+        const uint32_t row = (blockIdx.x * RG + grp) * ROWS + rr;
         if (row < out) y[row] = v;
     }
 }
@@ -377,31 +456,30 @@ __global__ void __launch_bounds__(kWarps * 32) k_gemv_f16_any(float* __restrict_
 constexpr int kR = 4;   // rows per CTA
 constexpr int kNT = 4;  // tokens per pass over the weights
 
-constexpr int kR1 = 4;  // rows per warp of the single-token Q4_K kernel
-
-template <int KS>
-void launch_q4k_t1(float* y, const uint8_t* w, const float* x, uint32_t out, uint32_t in, cudaStream_t st) {
-    constexpr uint32_t rows_per_cta = (kWarps / KS) * kR1;
-    k_gemv_q4k_t1<kR1, KS><<<(out + rows_per_cta - 1) / rows_per_cta, kWarps * 32, 0, st>>>(y, w, x, out, in);
+template <int MT, int KS>
+void launch_q4k_tc(float* y, const uint8_t* w, const float* x, uint32_t out, uint32_t in, cudaStream_t st) {
+    constexpr uint32_t rows_per_cta = (kWarps / KS) * 16 * MT;
+    k_gemv_q4k_tc<MT, KS, 2><<<(out + rows_per_cta - 1) / rows_per_cta, kWarps * 32, 0, st>>>(y, w, x, out, in);
+}
+template <int MT>
+void launch_q4k_tc_ks(float* y, const uint8_t* w, const float* x, uint32_t out, uint32_t in, cudaStream_t st) {
+    const uint32_t nb = in / 256;   // k-slices so that every warp has a few blocks and the grid spreads
+    if (nb >= 16)
+        launch_q4k_tc<MT, 8>(y, w, x, out, in, st);
+    else if (nb >= 8)
+        launch_q4k_tc<MT, 4>(y, w, x, out, in, st);
+    else if (nb >= 2)
+        launch_q4k_tc<MT, 2>(y, w, x, out, in, st);
+    else
+        launch_q4k_tc<MT, 1>(y, w, x, out, in, st);
 }
 
 template <int NT>
 void launch_q4k(float* y, const uint8_t* w, const float* x, uint32_t out, uint32_t in, uint32_t nt, cudaStream_t st) {
-    if (NT == 1) {
-        // as many k-slices as a row has steps (up to the CTA's 8 warps): the fewest rows per CTA, so even a
-        // matrix of 1024 rows spreads over every SM
-        const uint32_t nsteps = (in / 256 + 3) / 4;   // 4-block steps per row
-        if (nsteps >= 8)
-            launch_q4k_t1<8>(y, w, x, out, in, st);
-        else if (nsteps >= 4)
-            launch_q4k_t1<4>(y, w, x, out, in, st);
-        else if (nsteps >= 2)
-            launch_q4k_t1<2>(y, w, x, out, in, st);
-        else
-            launch_q4k_t1<1>(y, w, x, out, in, st);
-    } else {
+    if (NT == 1)
+        launch_q4k_tc_ks<1>(y, w, x, out, in, st);
+    else
         k_gemv_q4k<kR, NT, 1><<<(out + kR - 1) / kR, kWarps * 32, 0, st>>>(y, w, x, out, in, nt);
-    }
 }
 template <int NT>
 void launch_f16(float* y, const uint16_t* w, const float* x, uint32_t out, uint32_t in, uint32_t nt, cudaStream_t st) {
