@@ -157,6 +157,24 @@ __global__ void __launch_bounds__(kPThreads, 1)
     const uint32_t kmax = qpos0 + rows_valid - 1;
     const uint32_t nkb = kmax / BN + 1;
 
+    // The softmax warps' share of the fp32 Q tile (one batch of loads in flight per thread), issued before the
+    // barrier and TMEM setup below so that the loads' latency passes meanwhile.
+    constexpr int C4 = HD / 4;
+    constexpr int QITER = BM * C4 / 256;
+    static_assert(QITER <= 32, "Q loads in one batch");
+    float4 qv[QITER];
+    if (warp < 8) {
+#pragma unroll
+        for (int i = 0; i < QITER; ++i) {
+            const int idx = threadIdx.x + i * 256;
+            const uint32_t b = row0 + idx / C4;
+            qv[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (b < p.B)
+                qv[i] = __ldcs(reinterpret_cast<const float4*>(p.q + static_cast<size_t>(b) * p.q_stride +
+                                                               static_cast<size_t>(hh) * HD + (idx % C4) * 4));
+        }
+    }
+
     if (threadIdx.x == 0) {
         for (int s = 0; s < KST; ++s) {
             mbar_init(&bars->k_full[s], 1);
@@ -284,19 +302,7 @@ __global__ void __launch_bounds__(kPThreads, 1)
         //      tile is not an fp16 value, Q_lo = fp16(q - Q_hi) (TMEM); 256 threads, one batch
         //      of loads in flight each ----
         {
-            constexpr int C4 = HD / 4;
-            constexpr int QITER = BM * C4 / 256;
-            static_assert(QITER <= 32, "Q loads in one batch");
-            float4 v[QITER];
-#pragma unroll
-            for (int i = 0; i < QITER; ++i) {
-                const int idx = threadIdx.x + i * 256;
-                const uint32_t b = row0 + idx / C4;
-                v[i] = make_float4(0.f, 0.f, 0.f, 0.f);
-                if (b < p.B)
-                    v[i] = __ldcs(reinterpret_cast<const float4*>(p.q + static_cast<size_t>(b) * p.q_stride +
-                                                                  static_cast<size_t>(hh) * HD + (idx % C4) * 4));
-            }
+            const float4* v = qv;   // loaded before the setup
             // hi and lo halves of this thread's q, packed (4 registers per float4 loaded)
             uint2 qh[QITER], ql[QITER];
             bool any_lo = false;
@@ -510,7 +516,9 @@ __global__ void __launch_bounds__(kPThreads, 1)
                         bulk_commit_group();
                     }
                 }
-                if (lane == 0) bulk_wait_group<0>();   // every staged store has landed
+                // the boxes have been read before the CTA (and its shared memory) goes; the stores' global writes
+                // complete with the grid
+                if (lane == 0) bulk_wait_group_read<0>();
             } else {
                 const uint32_t b = row0 + r;
 #pragma unroll 1
