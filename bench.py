@@ -47,9 +47,10 @@ def load_peaks() -> tuple[dict, str]:
 # capture report null.
 # dram__bytes_read.sum + dram__bytes_write.sum of one launch of each workload's dominant kernel, from the ncu
 # captures summarised under profiles/ (same workloads; --layers-reduced steps have the same per-launch bytes)
-NCU_TRAFFIC = {"decode": 1225510144, "prefill": 25237504, "gated_prefill": 168607744, "gated_decode": 274070272,
+NCU_TRAFFIC = {"decode": 1225510144, "prefill": 25232128, "gated_prefill": 168607744, "gated_decode": 274070272,
                "long_decode": 541052160, "gdn_inputs": 225114112, "rope_store": 1590784,
-               "gdn_decode": 78914048, "gdn_prefill_state": 257715456}
+               "gdn_decode": 78914048, "gdn_prefill_state": 257715456, "fused_decode": 1226680832,
+               "gemv_q4k_gate": 33069568}
 
 
 class ClockSampler:
@@ -1070,7 +1071,8 @@ def run_fused_decode(args) -> None:
     step_bytes = n_layers * (keys * kd * 2 * 2 + n * (H * hd * 4 * 2 + kd * 4 * 2))
     peaks, src = load_peaks()
     roof = {"bound": "hbm", "achieved": round(step_bytes / (ms_f / 1e3) / 1e9, 1), "peak": peaks["hbm_gbs"],
-            "unit": "GB/s", "frac": round(step_bytes / (ms_f / 1e3) / 1e9 / peaks["hbm_gbs"], 4), "traffic": None,
+            "unit": "GB/s", "frac": round(step_bytes / (ms_f / 1e3) / 1e9 / peaks["hbm_gbs"], 4),
+            "traffic": None if (args.seqs or args.layers or world > 1) else NCU_TRAFFIC["fused_decode"],
             "kernel": "k_decode<128,4,TM,ROPE> (pooled tensor copies, RoPE + store fused)", "peak_source": src,
             "bytes_per_step": step_bytes}
     if rank == 0:
@@ -1146,10 +1148,12 @@ def run_gemv(args, fmt: str = "q4k") -> None:
     peaks, src = load_peaks()
     ach = step_bytes / (per_call / 1e3) / 1e9
     roof = {"bound": "hbm", "achieved": round(ach, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
-            "frac": round(ach / peaks["hbm_gbs"], 4), "traffic": None,
+            "frac": round(ach / peaks["hbm_gbs"], 4),
+            "traffic": None if (f16 or args.layers) else NCU_TRAFFIC["gemv_q4k_gate"],
             "kernel": "k_gemv_f16<4,1,2>" if f16 else "k_gemv_q4k_tc<1,KS,2> (mma.sync)",
             "peak_source": src, "bytes_per_step": step_bytes,
-            "note": "224 launches per step in one graph; achieved = weight bytes / step device time"}
+            "note": ("224 launches per step in one graph; achieved = weight bytes / step device time"
+                     + ("" if f16 else "; traffic: one 14336 x 4096 launch (gate / up), 33,030,144 B of weights"))}
     e2e = None
     if not args.no_e2e:
         hx = torch.empty(H, dtype=torch.float32, pin_memory=True)
