@@ -274,32 +274,66 @@ __global__ void __launch_bounds__(256) k_gdn_chunk_prep(const ChunkParams p) {
     }
     __syncthreads();
 
-    // ---- T = (I + A)^-1 by forward substitution, one column per thread (threads 0-63) ----
-    // Column c: x_t = -sum_{i<t} A[t][i] x_i for t > c, x_c = 1, x_t = 0 for t < c.  A[t][i]
-    // is zero for i >= t, so each row sums over whole float4 groups; every thread reads the
-    // same A element at the same time (broadcast).
+    // ---- T = (I + A)^-1, blocked by 16 (L = I + A is unit lower triangular) ----
+    // T_ii = L_ii^-1: the four diagonal blocks by forward substitution, one column per thread (threads 0-63);
+    // then the blocks below, by distance d = i - j from the diagonal: T_ij = -T_ii sum_{j<=k<i} A_ik T_kj,
+    // every thread on the 16x16 products.  The blocks above the diagonal are zero.
+    float* Xs = Tm + kC * LA;                     // [3][16][16] scratch, still inside the consumed K/Q area
     if (tid < kC) {
-        const int c = tid;
-        float x[kC];
+        const int o = tid & ~15, c = tid & 15;
+        float x[16];
 #pragma unroll
-        for (int t = 0; t < kC; ++t) x[t] = (t == c) ? 1.f : 0.f;
+        for (int t = 0; t < 16; ++t) x[t] = (t == c) ? 1.f : 0.f;
 #pragma unroll
-        for (int t = 1; t < kC; ++t) {
-            float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
+        for (int t = 1; t < 16; ++t) {
+            float s0 = 0.f, s1 = 0.f;
 #pragma unroll
-            for (int i4 = 0; i4 < (t + 3) / 4; ++i4) {
-                const float4 a = *reinterpret_cast<const float4*>(Am + t * LA + 4 * i4);
-                s0 = fmaf(a.x, x[4 * i4], s0);
-                s1 = fmaf(a.y, x[4 * i4 + 1], s1);
-                s2 = fmaf(a.z, x[4 * i4 + 2], s2);
-                s3 = fmaf(a.w, x[4 * i4 + 3], s3);
+            for (int i = 0; i < t; ++i) {
+                if (i & 1)
+                    s1 = fmaf(Am[(o + t) * LA + o + i], x[i], s1);
+                else
+                    s0 = fmaf(Am[(o + t) * LA + o + i], x[i], s0);
             }
-            if (t > c) x[t] = -((s0 + s1) + (s2 + s3));
+            if (t > c) x[t] = -(s0 + s1);
         }
 #pragma unroll
-        for (int t = 0; t < kC; ++t) Tm[t * LA + c] = x[t];
+        for (int t = 0; t < 16; ++t) Tm[(o + t) * LA + o + c] = x[t];
+    } else {
+        for (int e = tid - kC; e < 6 * 256; e += 256 - kC) {   // the 6 blocks above the diagonal
+            const int blk = e >> 8, r = (e >> 4) & 15, c = e & 15;
+            const int bi = blk < 3 ? 0 : blk < 5 ? 1 : 2, bj = blk < 3 ? blk + 1 : blk < 5 ? blk - 1 : 3;
+            Tm[(16 * bi + r) * LA + 16 * bj + c] = 0.f;
+        }
     }
     __syncthreads();
+#pragma unroll 1
+    for (int d = 1; d < 4; ++d) {
+        const int nb = 4 - d;                     // blocks (j + d, j), j < nb
+        for (int e = tid; e < nb * 256; e += 256) {
+            const int j = e >> 8, r = (e >> 4) & 15, c = e & 15, i = j + d;
+            float s0 = 0.f, s1 = 0.f;
+            for (int k = j; k < i; ++k) {
+#pragma unroll
+                for (int m = 0; m < 16; m += 2) {
+                    s0 = fmaf(Am[(16 * i + r) * LA + 16 * k + m], Tm[(16 * k + m) * LA + 16 * j + c], s0);
+                    s1 = fmaf(Am[(16 * i + r) * LA + 16 * k + m + 1], Tm[(16 * k + m + 1) * LA + 16 * j + c], s1);
+                }
+            }
+            Xs[e] = s0 + s1;
+        }
+        __syncthreads();
+        for (int e = tid; e < nb * 256; e += 256) {
+            const int j = e >> 8, r = (e >> 4) & 15, c = e & 15, i = j + d;
+            float s0 = 0.f, s1 = 0.f;
+#pragma unroll
+            for (int m = 0; m < 16; m += 2) {
+                s0 = fmaf(Tm[(16 * i + r) * LA + 16 * i + m], Xs[(j << 8) + m * 16 + c], s0);
+                s1 = fmaf(Tm[(16 * i + r) * LA + 16 * i + m + 1], Xs[(j << 8) + (m + 1) * 16 + c], s1);
+            }
+            Tm[(16 * i + r) * LA + 16 * j + c] = -(s0 + s1);
+        }
+        __syncthreads();
+    }
 
     // ---- T, P -> fp16 hi/lo scratch ----
     __half* dst = p.tp + (sc * p.n_vheads + h) * kTpHalves;
