@@ -829,7 +829,8 @@ def _long_decode(args, rank, world, local, dist, sub=False):
     n = d.ctx[0]
     k0, k1 = ydist.split_range(n, world, rank)
     H, hd = c.n_heads, c.head_dim
-    peer = world > 1 and args.exchange == "peer"
+    peer = world > 1 and args.exchange in ("peer", "peer2")
+    fused = peer and args.exchange == "peer"
     ex = (ydist.PeerExchange if peer else ydist.PartialExchange)(H, hd, device=f"cuda:{local}")
     out = d.out[0, 0]
     kv, vv = d.k_view(0, 0), d.v_view(0, 0)
@@ -841,9 +842,9 @@ def _long_decode(args, rank, world, local, dist, sub=False):
         # launches on the current stream, so the step (NCCL included) can be graph-captured
         if world == 1:
             attn.attn_decode(out, d.q[0, 0], kv, vv, n - 1, H, c.n_kv_heads, hd, c.kv_dim)
-        elif peer:   # two launches: the shard's split decode, then merge + exchange + merge in one kernel
+        elif fused:   # two launches: the shard's split decode, then merge + exchange + merge in one kernel
             ex.decode(out, d.q[0, 0], kv, vv, k0, k1, c.n_kv_heads, c.kv_dim)
-        else:
+        else:         # the shard's partial decode, then the exchange (peer memory or NCCL) as its own call
             partial()
             ex.run(out)
 
@@ -880,15 +881,17 @@ def _long_decode(args, rank, world, local, dist, sub=False):
     roof = {"bound": "hbm", "achieved": round(ach, 1), "peak": peaks["hbm_gbs"] * world, "unit": "GB/s",
             "frac": round(ach / (peaks["hbm_gbs"] * world), 4),
             "traffic": NCU_TRAFFIC["long_decode"] if world == 1 else None,
-            "kernel": "k_decode<128,4,TM>" + ((" + k_merge_splits<EX> (split merge + exchange + merge)" if peer
+            "kernel": "k_decode<128,4,TM>" + ((" + k_merge_splits<EX> (split merge + exchange + merge)" if fused
+                                               else " + k_merge_splits, then k_exchange_merge" if peer
                                                else " + NCCL all-gather + merge")
                                               if world > 1 else " + k_merge_splits"),
             "peak_source": src + f" x{world} GPUs"}
     cfg_d = {"workload": c.name, "ctx": n, "n_heads": H, "n_kv_heads": c.n_kv_heads, "head_dim": hd,
              "kv_bytes": nbytes,
              "parallelism": (f"split-KV x{world}, " + (
-                 "(m,l,o) pushed into every GPU over NVLink + LSE merge, one kernel"
-                 if peer else "NCCL all-gather of (m,l,o) + LSE merge")) if world > 1 else "one GPU",
+                 "(m,l,o) pushed into every GPU over NVLink + LSE merge, one kernel" if fused
+                 else "(m,l,o) pushed into every GPU over NVLink + LSE merge, its own launch" if peer
+                 else "NCCL all-gather of (m,l,o) + LSE merge")) if world > 1 else "one GPU",
              "launch": "CUDA graph replay of the step (partial decode, exchange, merge)",
              "l2": "KV 537 MB > L2"}
     if peer:
@@ -1426,8 +1429,9 @@ def main() -> None:
     ap.add_argument("--weak", action="store_true",
                     help="decode at N>1: every rank serves a whole 64-sequence batch (default: the 64 sharded)")
     ap.add_argument("--no-long", action="store_true", help="decode: skip the config-4 long_decode sub-object")
-    ap.add_argument("--exchange", choices=["peer", "nccl"], default="peer",
-                    help="long_decode at N>1: split-KV exchange over peer memory (one kernel) or NCCL all-gather")
+    ap.add_argument("--exchange", choices=["peer", "peer2", "nccl"], default="peer",
+                    help="long_decode at N>1: split-KV exchange over peer memory fused into the split merge (peer), "
+                         "over peer memory as its own launch after the partial decode (peer2), or NCCL all-gather")
     args = ap.parse_args()
     if args.warmup < 3:
         log("warmup raised to 3 (timing rule)")
