@@ -29,9 +29,9 @@
 // double-precision difference, e^Gamma and e^(Gamma_63 - Gamma) exp in double.
 //
 // Two kernels:
-//   k_gdn_chunk_prep   (chunk, v-head, seq): everything that does not depend on
-//                      S -- Gamma, T and P -- plus fp16 hi/lo copies of K and Q.
-//                      Fully parallel.
+//   k_gdn_chunk_prep   (chunk, k-head, seq): everything that does not depend on
+//                      S -- Gamma, T and P of each v-head on the k-head -- plus
+//                      fp16 hi/lo copies of K and Q.  Fully parallel.
 //   k_gdn_chunk_state  (32 state rows, v-head, seq): walks the chunks in order
 //                      with its 32 x 128 slice of S in fp32 registers; every
 //                      contraction is mma.sync m16n8k16 with both operands split
@@ -136,24 +136,36 @@ __device__ __forceinline__ void cp16(void* dst_smem, const void* src, bool valid
 }
 
 // ------------------------------------------------------------------ prep
-// smem: Kh Kl Qh Ql [64][LDH] halves (T aliases Kh.. once K/Q are done), A and P
-// [64][LA] fp32, gates then Gamma [64] double, beta [64] fp32.
-constexpr int kPrepSmem = 4 * kC * LDH * 2 + 2 * kC * LA * 4 + kC * 8 + kC * 4;
+// One CTA per (chunk, k-head, sequence).  K K^T and Q K^T depend only on the
+// k-head, so they are contracted once, lower triangles only (10 of the 16
+// 16x16 output tiles each), and every v-head that reads this k-head
+// (h = kh, kh + num_k_heads, ...) then applies its own gates and betas.
+// smem: Kh Kl Qh Ql [64][LDH] halves, raw K K^T and Q K^T [64][LA] fp32,
+// then per half of the CTA: Gamma [64] double, beta [64] fp32.  Once the
+// contractions are done, the two halves (128 threads each) take the v-heads
+// in turn, each half with its own A, T [64][LA] and block scratch [3][16][16]
+// in the space of the consumed K/Q tiles (grown to fit both halves).
+constexpr int kPrepHalfFloats = 2 * kC * LA + 3 * 256;
+constexpr int kPrepAlias = std::max(4 * kC * LDH * 2, 2 * kPrepHalfFloats * 4);
+constexpr int kPrepSmem = kPrepAlias + 2 * kC * LA * 4 + 2 * kC * 8 + 2 * kC * 4;
+static_assert(2 * (kPrepSmem + 1024) <= 233472, "two prep CTAs per SM");
 
-__global__ void __launch_bounds__(256) k_gdn_chunk_prep(const ChunkParams p) {
+// lower-triangular 16x16 output tile r (0..9) -> (m-tile, n-tile)
+__device__ __forceinline__ void tri_tile(int r, int& mt, int& nt) {
+    mt = r >= 6 ? 3 : r >= 3 ? 2 : r >= 1 ? 1 : 0;
+    nt = r - mt * (mt + 1) / 2;
+}
+
+__global__ void __launch_bounds__(256, 2) k_gdn_chunk_prep(const ChunkParams p) {
     extern __shared__ __align__(16) uint8_t smp[];
     __half* Kh = reinterpret_cast<__half*>(smp);
     __half* Kl = Kh + kC * LDH;
     __half* Qh = Kl + kC * LDH;
     __half* Ql = Qh + kC * LDH;
-    float* Am = reinterpret_cast<float*>(Ql + kC * LDH);
-    float* Pm = Am + kC * LA;
-    double* G = reinterpret_cast<double*>(Pm + kC * LA);   // 8-byte aligned: every array above is
-    float* Bt = reinterpret_cast<float*>(G + kC);
-    float* Tm = reinterpret_cast<float*>(Kh);           // [64][LA], after K/Q are consumed
+    float* KK = reinterpret_cast<float*>(smp + kPrepAlias);   // raw k_t . k_i   (i <= t)
+    float* QK = KK + kC * LA;                              // raw q_t . k_i   (i <= t)
 
-    const uint32_t ch = blockIdx.x, h = blockIdx.y, sq = blockIdx.z;
-    const uint32_t kh = h % p.num_k_heads;
+    const uint32_t ch = blockIdx.x, kh = blockIdx.y, sq = blockIdx.z;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const uint32_t t0 = ch * kC;
     const uint32_t nvalid = min(static_cast<uint32_t>(kC), p.T - t0);
@@ -161,7 +173,7 @@ __global__ void __launch_bounds__(256) k_gdn_chunk_prep(const ChunkParams p) {
     const size_t tok0 = static_cast<size_t>(sq) * p.T + t0;
     const size_t sc = static_cast<size_t>(sq) * p.n_chunks + ch;
 
-    // ---- K, Q -> fp16 hi/lo; gates, betas (all 16 float4 loads of a thread in flight) ----
+    // ---- K, Q -> fp16 hi/lo (all 16 float4 loads of a thread in flight) ----
     constexpr int NL = kC * kD / 4 / 256;   // float4 of K (and of Q) per thread
     float4 kvs[NL], qvs[NL];
 #pragma unroll
@@ -191,37 +203,8 @@ __global__ void __launch_bounds__(256) k_gdn_chunk_prep(const ChunkParams p) {
         *reinterpret_cast<__half2*>(Ql + t * LDH + c) = l0;
         *reinterpret_cast<__half2*>(Ql + t * LDH + c + 2) = l1;
     }
-    if (tid < kC) {
-        const bool ok = static_cast<uint32_t>(tid) < nvalid;
-        G[tid] = ok ? p.gate[(tok0 + tid) * p.n_vheads + h] : 0.f;
-        Bt[tid] = ok ? p.beta[(tok0 + tid) * p.n_vheads + h] : 0.f;
-    }
     __syncthreads();
-    // Gamma: inclusive prefix sum of the gates in double (warp 0), published for the state kernel
-    if (warp == 0) {
-        double x0 = G[lane], x1 = G[32 + lane];
-#pragma unroll
-        for (int o = 1; o < 32; o <<= 1) {
-            const double y0 = __shfl_up_sync(0xffffffffu, x0, o), y1 = __shfl_up_sync(0xffffffffu, x1, o);
-            if (lane >= o) {
-                x0 += y0;
-                x1 += y1;
-            }
-        }
-        x1 += __shfl_sync(0xffffffffu, x0, 31);
-        G[lane] = x0;
-        G[32 + lane] = x1;
-        const double glast = __shfl_sync(0xffffffffu, x1, 31);
-        float* gm = p.gam + (sc * p.n_vheads + h) * kGamFloats;
-        gm[lane] = static_cast<float>(x0);
-        gm[32 + lane] = static_cast<float>(x1);
-        gm[kC + lane] = static_cast<float>(exp(x0));
-        gm[kC + 32 + lane] = static_cast<float>(exp(x1));
-        gm[2 * kC + lane] = static_cast<float>(exp(glast - x0));
-        gm[2 * kC + 32 + lane] = static_cast<float>(exp(glast - x1));
-    }
-    // K/Q hi/lo to the scratch, once per k-head (by the v-head that equals it)
-    if (h < p.num_k_heads) {   // Kh, Kl, Qh, Ql are consecutive [64][LDH] arrays
+    {   // K/Q hi/lo to the scratch (Kh, Kl, Qh, Ql are consecutive [64][LDH] arrays)
         __half* dst = p.kq + (sc * p.num_k_heads + kh) * kKqHalves;
 #pragma unroll 4
         for (int i = tid; i < 4 * kC * (kD / 8); i += 256) {
@@ -230,122 +213,202 @@ __global__ void __launch_bounds__(256) k_gdn_chunk_prep(const ChunkParams p) {
                 *reinterpret_cast<const uint4*>(Kh + ar * LDH + c);
         }
     }
-    __syncthreads();
 
-    // ---- K K^T (warps 0-3) and Q K^T (warps 4-7), m-tile = warp & 3, all 64 columns ----
+    // ---- K K^T and Q K^T, lower-triangular tiles: 20 tiles of 16x16 over the 8 warps ----
     {
-        const int mt = warp & 3, which = warp >> 2;
-        const uint32_t ah_b = smem_u32(which ? Qh : Kh), al_b = smem_u32(which ? Ql : Kl);
         const uint32_t bh_b = smem_u32(Kh), bl_b = smem_u32(Kl);
-        float acc[8][4];
-#pragma unroll
-        for (int n = 0; n < 8; ++n) acc[n][0] = acc[n][1] = acc[n][2] = acc[n][3] = 0.f;
-#pragma unroll
-        for (int ks = 0; ks < kD / 16; ++ks) {
-            uint32_t ah[4], al[4];
-            ldsm4(a_addr(ah_b, 16 * mt, 16 * ks, LDH, lane), ah);
-            ldsm4(a_addr(al_b, 16 * mt, 16 * ks, LDH, lane), al);
-#pragma unroll
-            for (int np = 0; np < 4; ++np) {
-                uint32_t bh[4], bl[4];
-                ldsm4(bnk_addr(bh_b, 16 * np, 16 * ks, LDH, lane), bh);
-                ldsm4(bnk_addr(bl_b, 16 * np, 16 * ks, LDH, lane), bl);
-                mma3(acc[2 * np], ah, al, bh[0], bh[1], bl[0], bl[1]);
-                mma3(acc[2 * np + 1], ah, al, bh[2], bh[3], bl[2], bl[3]);
-            }
-        }
-        // A[t][i] = beta_t e^{Gamma_t - Gamma_i} kk (i < t);  P[t][i] = e^{Gamma_t - Gamma_i} qk (i <= t)
         const int g = lane >> 2, tq = lane & 3;
-#pragma unroll
-        for (int n = 0; n < 8; ++n) {
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-                const int t = 16 * mt + g + ((e >> 1) << 3), i = 8 * n + 2 * tq + (e & 1);
-                float val = 0.f;
-                if (which == 0) {
-                    if (i < t) val = Bt[t] * expf(static_cast<float>(G[t] - G[i])) * acc[n][e];
-                    Am[t * LA + i] = val;
-                } else {
-                    if (i <= t) val = expf(static_cast<float>(G[t] - G[i])) * acc[n][e];
-                    Pm[t * LA + i] = val;
-                }
-            }
-        }
-    }
-    __syncthreads();
-
-    // ---- T = (I + A)^-1, blocked by 16 (L = I + A is unit lower triangular) ----
-    // T_ii = L_ii^-1: the four diagonal blocks by forward substitution, one column per thread (threads 0-63);
-    // then the blocks below, by distance d = i - j from the diagonal: T_ij = -T_ii sum_{j<=k<i} A_ik T_kj,
-    // every thread on the 16x16 products.  The blocks above the diagonal are zero.
-    float* Xs = Tm + kC * LA;                     // [3][16][16] scratch, still inside the consumed K/Q area
-    if (tid < kC) {
-        const int o = tid & ~15, c = tid & 15;
-        float x[16];
-#pragma unroll
-        for (int t = 0; t < 16; ++t) x[t] = (t == c) ? 1.f : 0.f;
-#pragma unroll
-        for (int t = 1; t < 16; ++t) {
-            float s0 = 0.f, s1 = 0.f;
-#pragma unroll
-            for (int i = 0; i < t; ++i) {
-                if (i & 1)
-                    s1 = fmaf(Am[(o + t) * LA + o + i], x[i], s1);
-                else
-                    s0 = fmaf(Am[(o + t) * LA + o + i], x[i], s0);
-            }
-            if (t > c) x[t] = -(s0 + s1);
-        }
-#pragma unroll
-        for (int t = 0; t < 16; ++t) Tm[(o + t) * LA + o + c] = x[t];
-    } else {
-        for (int e = tid - kC; e < 6 * 256; e += 256 - kC) {   // the 6 blocks above the diagonal
-            const int blk = e >> 8, r = (e >> 4) & 15, c = e & 15;
-            const int bi = blk < 3 ? 0 : blk < 5 ? 1 : 2, bj = blk < 3 ? blk + 1 : blk < 5 ? blk - 1 : 3;
-            Tm[(16 * bi + r) * LA + 16 * bj + c] = 0.f;
-        }
-    }
-    __syncthreads();
 #pragma unroll 1
-    for (int d = 1; d < 4; ++d) {
-        const int nb = 4 - d;                     // blocks (j + d, j), j < nb
-        for (int e = tid; e < nb * 256; e += 256) {
-            const int j = e >> 8, r = (e >> 4) & 15, c = e & 15, i = j + d;
-            float s0 = 0.f, s1 = 0.f;
-            for (int k = j; k < i; ++k) {
+        for (int u = warp; u < 20; u += 8) {
+            const int which = u >= 10;
+            int mt, nt;
+            tri_tile(u - 10 * which, mt, nt);
+            const uint32_t ah_b = smem_u32(which ? Qh : Kh), al_b = smem_u32(which ? Ql : Kl);
+            float acc[2][4];
 #pragma unroll
-                for (int m = 0; m < 16; m += 2) {
-                    s0 = fmaf(Am[(16 * i + r) * LA + 16 * k + m], Tm[(16 * k + m) * LA + 16 * j + c], s0);
-                    s1 = fmaf(Am[(16 * i + r) * LA + 16 * k + m + 1], Tm[(16 * k + m + 1) * LA + 16 * j + c], s1);
+            for (int n = 0; n < 2; ++n) acc[n][0] = acc[n][1] = acc[n][2] = acc[n][3] = 0.f;
+#pragma unroll
+            for (int ks = 0; ks < kD / 16; ++ks) {
+                uint32_t ah[4], al[4], bh[4], bl[4];
+                ldsm4(a_addr(ah_b, 16 * mt, 16 * ks, LDH, lane), ah);
+                ldsm4(a_addr(al_b, 16 * mt, 16 * ks, LDH, lane), al);
+                ldsm4(bnk_addr(bh_b, 16 * nt, 16 * ks, LDH, lane), bh);
+                ldsm4(bnk_addr(bl_b, 16 * nt, 16 * ks, LDH, lane), bl);
+                mma3(acc[0], ah, al, bh[0], bh[1], bl[0], bl[1]);
+                mma3(acc[1], ah, al, bh[2], bh[3], bl[2], bl[3]);
+            }
+            float* dst = which ? QK : KK;
+#pragma unroll
+            for (int n = 0; n < 2; ++n) {
+                const int t = 16 * mt + g, i = 16 * nt + 8 * n + 2 * tq;
+                *reinterpret_cast<float2*>(dst + t * LA + i) = make_float2(acc[n][0], acc[n][1]);
+                *reinterpret_cast<float2*>(dst + (t + 8) * LA + i) = make_float2(acc[n][2], acc[n][3]);
+            }
+        }
+    }
+    __syncthreads();   // K/Q consumed: the halves' A, T and scratch may overwrite them
+
+    // ---- per v-head: half hf of the CTA takes h = kh + hf * nk, kh + 3 * nk, ... (named barrier 1 + hf) ----
+    const int hf = tid >> 7, th = tid & 127, hw = th >> 5;
+    double* G = reinterpret_cast<double*>(QK + kC * LA) + hf * kC;   // 8-byte aligned: every array above is
+    float* Bt = reinterpret_cast<float*>(reinterpret_cast<double*>(QK + kC * LA) + 2 * kC) + hf * kC;
+    float* Am = reinterpret_cast<float*>(smp) + hf * kPrepHalfFloats;   // [64][LA]
+    float* Tm = Am + kC * LA;                                           // [64][LA]
+    float* Xs = Tm + kC * LA;                                           // [3][16][16]
+    auto half_sync = [&]() {
+        if (hf == 0)
+            asm volatile("bar.sync 1, 128;" ::: "memory");
+        else
+            asm volatile("bar.sync 2, 128;" ::: "memory");
+    };
+#pragma unroll 1
+    for (uint32_t h = kh + hf * p.num_k_heads; h < p.n_vheads; h += 2 * p.num_k_heads) {
+        // Gamma: inclusive prefix sum of the gates in double (warp 0 of the half), published for the state
+        // kernel; the betas by warp 1
+        if (hw == 0) {
+            const bool ok0 = static_cast<uint32_t>(lane) < nvalid, ok1 = static_cast<uint32_t>(32 + lane) < nvalid;
+            double x0 = ok0 ? p.gate[(tok0 + lane) * p.n_vheads + h] : 0.f;
+            double x1 = ok1 ? p.gate[(tok0 + 32 + lane) * p.n_vheads + h] : 0.f;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const double y0 = __shfl_up_sync(0xffffffffu, x0, o), y1 = __shfl_up_sync(0xffffffffu, x1, o);
+                if (lane >= o) {
+                    x0 += y0;
+                    x1 += y1;
                 }
             }
-            Xs[e] = s0 + s1;
-        }
-        __syncthreads();
-        for (int e = tid; e < nb * 256; e += 256) {
-            const int j = e >> 8, r = (e >> 4) & 15, c = e & 15, i = j + d;
-            float s0 = 0.f, s1 = 0.f;
+            x1 += __shfl_sync(0xffffffffu, x0, 31);
+            G[lane] = x0;
+            G[32 + lane] = x1;
+            const double glast = __shfl_sync(0xffffffffu, x1, 31);
+            float* gm = p.gam + (sc * p.n_vheads + h) * kGamFloats;
+            gm[lane] = static_cast<float>(x0);
+            gm[32 + lane] = static_cast<float>(x1);
+            gm[kC + lane] = static_cast<float>(exp(x0));
+            gm[kC + 32 + lane] = static_cast<float>(exp(x1));
+            gm[2 * kC + lane] = static_cast<float>(exp(glast - x0));
+            gm[2 * kC + 32 + lane] = static_cast<float>(exp(glast - x1));
+        } else if (hw == 1) {
 #pragma unroll
-            for (int m = 0; m < 16; m += 2) {
-                s0 = fmaf(Tm[(16 * i + r) * LA + 16 * i + m], Xs[(j << 8) + m * 16 + c], s0);
-                s1 = fmaf(Tm[(16 * i + r) * LA + 16 * i + m + 1], Xs[(j << 8) + (m + 1) * 16 + c], s1);
+            for (int j = 0; j < 2; ++j) {
+                const int t = 32 * j + lane;
+                Bt[t] = static_cast<uint32_t>(t) < nvalid ? p.beta[(tok0 + t) * p.n_vheads + h] : 0.f;
             }
-            Tm[(16 * i + r) * LA + 16 * j + c] = -(s0 + s1);
         }
-        __syncthreads();
-    }
+        half_sync();
 
-    // ---- T, P -> fp16 hi/lo scratch ----
-    __half* dst = p.tp + (sc * p.n_vheads + h) * kTpHalves;
-    for (int i = tid; i < kC * kC / 2; i += 256) {
-        const int t = i / (kC / 2), c = (i % (kC / 2)) * 2;
-        __half2 th, tl, ph, pl;
-        split2(Tm[t * LA + c], Tm[t * LA + c + 1], th, tl);
-        split2(Pm[t * LA + c], Pm[t * LA + c + 1], ph, pl);
-        *reinterpret_cast<__half2*>(dst + 0 * kC * kC + t * kC + c) = th;
-        *reinterpret_cast<__half2*>(dst + 1 * kC * kC + t * kC + c) = tl;
-        *reinterpret_cast<__half2*>(dst + 2 * kC * kC + t * kC + c) = ph;
-        *reinterpret_cast<__half2*>(dst + 3 * kC * kC + t * kC + c) = pl;
+        // A[t][i] = beta_t e^{Gamma_t - Gamma_i} kk (i < t) -> smem;  P[t][i] = e^{Gamma_t - Gamma_i} qk (i <= t)
+        // -> fp16 hi/lo scratch.  32 threads per row, two columns each.
+        __half* tp = p.tp + (sc * p.n_vheads + h) * kTpHalves;
+#pragma unroll 4
+        for (int e = th; e < kC * kC / 2; e += 128) {
+            const int t = e / (kC / 2), i = (e % (kC / 2)) * 2;
+            const double gt = G[t];
+            const double2 gi = *reinterpret_cast<const double2*>(G + i);
+            const float2 kk = *reinterpret_cast<const float2*>(KK + t * LA + i);
+            const float2 qk = *reinterpret_cast<const float2*>(QK + t * LA + i);
+            const float bt = Bt[t];
+            const float d0 = (i <= t) ? expf(static_cast<float>(gt - gi.x)) : 0.f;
+            const float d1 = (i + 1 <= t) ? expf(static_cast<float>(gt - gi.y)) : 0.f;
+            const float a[2] = {(i < t) ? bt * d0 * kk.x : 0.f, (i + 1 < t) ? bt * d1 * kk.y : 0.f};
+            const float pv[2] = {(i <= t) ? d0 * qk.x : 0.f, (i + 1 <= t) ? d1 * qk.y : 0.f};
+            *reinterpret_cast<float2*>(Am + t * LA + i) = make_float2(a[0], a[1]);
+            __half2 ph, pl;
+            split2(pv[0], pv[1], ph, pl);
+            *reinterpret_cast<__half2*>(tp + 2 * kC * kC + t * kC + i) = ph;
+            *reinterpret_cast<__half2*>(tp + 3 * kC * kC + t * kC + i) = pl;
+        }
+        half_sync();
+
+        // ---- T = (I + A)^-1, blocked by 16 (L = I + A is unit lower triangular) ----
+        // T_ii = L_ii^-1: the four diagonal blocks by forward substitution, one column per thread (threads 0-63 of the half);
+        // then the blocks below, by distance d = i - j from the diagonal: T_ij = -T_ii sum_{j<=k<i} A_ik T_kj,
+        // every thread of the half on the 16x16 products, four columns of a row each (float4 operands).
+        // The blocks above the diagonal are zero.
+        if (th < kC) {
+            const int o = th & ~15, c = th & 15;
+            float x[16];
+#pragma unroll
+            for (int t = 0; t < 16; ++t) x[t] = (t == c) ? 1.f : 0.f;
+#pragma unroll
+            for (int t = 1; t < 16; ++t) {
+                float s0 = 0.f, s1 = 0.f;
+#pragma unroll
+                for (int i = 0; i < t; ++i) {
+                    if (i & 1)
+                        s1 = fmaf(Am[(o + t) * LA + o + i], x[i], s1);
+                    else
+                        s0 = fmaf(Am[(o + t) * LA + o + i], x[i], s0);
+                }
+                if (t > c) x[t] = -(s0 + s1);
+            }
+#pragma unroll
+            for (int t = 0; t < 16; ++t) Tm[(o + t) * LA + o + c] = x[t];
+        } else {
+            for (int e = th - kC; e < 6 * 256; e += 128 - kC) {   // the 6 blocks above the diagonal
+                const int blk = e >> 8, r = (e >> 4) & 15, c = e & 15;
+                const int bi = blk < 3 ? 0 : blk < 5 ? 1 : 2, bj = blk < 3 ? blk + 1 : blk < 5 ? blk - 1 : 3;
+                Tm[(16 * bi + r) * LA + 16 * bj + c] = 0.f;
+            }
+        }
+        half_sync();
+#pragma unroll 1
+        for (int d = 1; d < 4; ++d) {
+            const int nb = 4 - d;                     // blocks (j + d, j), j < nb; a thread: 4 columns of a row
+            for (int e = th; e < nb * 64; e += 128) {
+                const int j = e >> 6, r = (e >> 2) & 15, c = (e & 3) * 4, i = j + d;
+                float4 s = make_float4(0.f, 0.f, 0.f, 0.f);
+                for (int k = j; k < i; ++k) {
+                    const float* arow = Am + (16 * i + r) * LA + 16 * k;
+#pragma unroll
+                    for (int m4 = 0; m4 < 16; m4 += 4) {
+                        const float4 a4 = *reinterpret_cast<const float4*>(arow + m4);
+                        const float av[4] = {a4.x, a4.y, a4.z, a4.w};
+#pragma unroll
+                        for (int mm = 0; mm < 4; ++mm) {
+                            const float4 tv =
+                                *reinterpret_cast<const float4*>(Tm + (16 * k + m4 + mm) * LA + 16 * j + c);
+                            s.x = fmaf(av[mm], tv.x, s.x);
+                            s.y = fmaf(av[mm], tv.y, s.y);
+                            s.z = fmaf(av[mm], tv.z, s.z);
+                            s.w = fmaf(av[mm], tv.w, s.w);
+                        }
+                    }
+                }
+                *reinterpret_cast<float4*>(Xs + (j << 8) + r * 16 + c) = s;
+            }
+            half_sync();
+            for (int e = th; e < nb * 64; e += 128) {
+                const int j = e >> 6, r = (e >> 2) & 15, c = (e & 3) * 4, i = j + d;
+                const float* trow = Tm + (16 * i + r) * LA + 16 * i;
+                float4 s = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+                for (int m4 = 0; m4 < 16; m4 += 4) {
+                    const float4 a4 = *reinterpret_cast<const float4*>(trow + m4);
+                    const float av[4] = {a4.x, a4.y, a4.z, a4.w};
+#pragma unroll
+                    for (int mm = 0; mm < 4; ++mm) {
+                        const float4 xv = *reinterpret_cast<const float4*>(Xs + (j << 8) + (m4 + mm) * 16 + c);
+                        s.x = fmaf(av[mm], xv.x, s.x);
+                        s.y = fmaf(av[mm], xv.y, s.y);
+                        s.z = fmaf(av[mm], xv.z, s.z);
+                        s.w = fmaf(av[mm], xv.w, s.w);
+                    }
+                }
+                *reinterpret_cast<float4*>(Tm + (16 * i + r) * LA + 16 * j + c) = make_float4(-s.x, -s.y, -s.z, -s.w);
+            }
+            half_sync();
+        }
+
+        // ---- T -> fp16 hi/lo scratch ----
+        for (int e = th; e < kC * kC / 2; e += 128) {
+            const int t = e / (kC / 2), c = (e % (kC / 2)) * 2;
+            __half2 thi, tl;
+            split2(Tm[t * LA + c], Tm[t * LA + c + 1], thi, tl);
+            *reinterpret_cast<__half2*>(tp + 0 * kC * kC + t * kC + c) = thi;
+            *reinterpret_cast<__half2*>(tp + 1 * kC * kC + t * kC + c) = tl;
+        }
+        half_sync();   // G, Bt, Am, Tm are rewritten for the half's next v-head
     }
 }
 
@@ -684,7 +747,7 @@ int gdn_prefill_chunked(float* S, float* out, const float* q, const float* k, co
     p.n_chunks = n_chunks;
     p.num_k_heads = num_k_heads;
     p.n_vheads = n_vheads;
-    k_gdn_chunk_prep<<<dim3(n_chunks, n_vheads, n_seqs), 256, kPrepSmem, st>>>(p);
+    k_gdn_chunk_prep<<<dim3(n_chunks, num_k_heads, n_seqs), 256, kPrepSmem, st>>>(p);
     YATTN_CHECK_LAUNCH(err, errlen, "gdn_prefill chunk prep");
     k_gdn_chunk_state<<<dim3(kD / kR, n_vheads, n_seqs), 256, kStateSmem, st>>>(p);
     YATTN_CHECK_LAUNCH(err, errlen, "gdn_prefill chunk state");
