@@ -50,7 +50,7 @@ def load_peaks() -> tuple[dict, str]:
 NCU_TRAFFIC = {"decode": 1225510144, "prefill": 25232128, "gated_prefill": 168607744, "gated_decode": 274070272,
                "long_decode": 541052160, "gdn_inputs": 225114112, "rope_store": 1590784,
                "gdn_decode": 78914048, "gdn_prefill_state": 257715456, "fused_decode": 1226680832,
-               "gemv_q4k_gate": 33069568}
+               "gemv_q4k_gate_up": 66100423}
 
 
 class ClockSampler:
@@ -1127,9 +1127,10 @@ def run_gemv(args, fmt: str = "q4k") -> None:
     brackets attention with these GEMVs): per layer q, k, v, o (4096/1024 x
     4096), gate and up (14336 x 4096) and down (4096 x 14336), 218 M weights:
     123 MB as Q4_K (fmt "q4k"), 436 MB as fp16 (fmt "f16"); 32 layers, each
-    with its own weights (far above L2).  One step = 224 launches replayed as
-    a CUDA graph.  Bound: HBM on the weight bytes.  Weak scaling: each rank
-    streams its own copy."""
+    with its own weights (far above L2).  Q4_K runs q/k/v and gate/up, which
+    read the same x, as one launch each (128 launches per step); fp16 runs the
+    224 matrices one by one.  The step is replayed as a CUDA graph.  Bound:
+    HBM on the weight bytes.  Weak scaling: each rank streams its own copy."""
     import ctypes as C
 
     import torch
@@ -1167,10 +1168,24 @@ def run_gemv(args, fmt: str = "q4k") -> None:
             mats.append((wbuf[off:off + n].view(torch.int16) if f16 else wbuf[off:off + n], o, i))
             off += n
     gemv = attn.gemv_f16 if f16 else attn.gemv_q4k
+    # Q4_K: the matrices that read the same x go in one launch (q, k, v; gate, up), 4 launches per layer
+    if f16:
+        calls = [(lambda w=w, o=o, i=i: gemv(ys[o], w, xs[i], o, i, 1)) for w, o, i in mats]
+    else:
+        yq = {o: torch.empty(o, device=dev) for o in (1024, 4096, 14336)}   # second outputs of a group
+        calls = []
+        for l in range(L):
+            q, k, v, o_, gt, up, dn = mats[7 * l:7 * l + 7]
+            calls.append(lambda q=q, k=k, v=v: attn.gemv_q4k_multi([ys[4096], ys[1024], yq[1024]], [q[0], k[0], v[0]],
+                                                                  [4096, 1024, 1024], xs[H], H))
+            calls.append(lambda o_=o_: gemv(ys[4096], o_[0], xs[H], 4096, H, 1))
+            calls.append(lambda gt=gt, up=up: attn.gemv_q4k_multi([ys[14336], yq[14336]], [gt[0], up[0]],
+                                                                 [14336, 14336], xs[H], H))
+            calls.append(lambda dn=dn: gemv(ys[4096], dn[0], xs[14336], 4096, 14336, 1))
 
     def step():
-        for w, o, i in mats:
-            gemv(ys[o], w, xs[i], o, i, 1)
+        for c in calls:
+            c()
 
     ms, per_call, clk = _timed(step, args, stream, world, dist, local, graph=True)
     step_bytes = L * per_layer
@@ -1178,11 +1193,11 @@ def run_gemv(args, fmt: str = "q4k") -> None:
     ach = step_bytes / (per_call / 1e3) / 1e9
     roof = {"bound": "hbm", "achieved": round(ach, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
             "frac": round(ach / peaks["hbm_gbs"], 4),
-            "traffic": None if (f16 or args.layers) else NCU_TRAFFIC["gemv_q4k_gate"],
-            "kernel": "k_gemv_f16<4,1,2>" if f16 else "k_gemv_q4k_tc<1,KS,2> (mma.sync)",
+            "traffic": None if (f16 or args.layers) else NCU_TRAFFIC["gemv_q4k_gate_up"],
+            "kernel": "k_gemv_f16<4,1,2>" if f16 else "k_gemv_q4k_tc(_multi)<1,KS,2> (mma.sync)",
             "peak_source": src, "bytes_per_step": step_bytes,
-            "note": ("224 launches per step in one graph; achieved = weight bytes / step device time"
-                     + ("" if f16 else "; traffic: one 14336 x 4096 launch (gate / up), 33,030,144 B of weights"))}
+            "note": (f"{len(calls)} launches per step in one graph; achieved = weight bytes / step device time"
+                     + ("" if f16 else "; traffic: one gate + up launch (two 14336 x 4096), 66,060,288 B of weights"))}
     e2e = None
     if not args.no_e2e:
         hx = torch.empty(H, dtype=torch.float32, pin_memory=True)
@@ -1197,7 +1212,9 @@ def run_gemv(args, fmt: str = "q4k") -> None:
         ems, _, _ = _timed(e2e_step, args, stream, world, dist, local)
         e2e = {"value": round(world / (ems / 1e3), 2), "unit": "tok/s", "h2d_bytes_per_step": H * 4 * world,
                "d2h_bytes_per_step": H * 4 * world,
-               "path": f"yattn_gemv_{fmt} per matrix per step (no graph), pinned x in, y back"}
+               "path": (f"yattn_gemv_{fmt} per matrix" if f16 else
+                        "yattn_gemv_q4k_multi for q/k/v and gate/up, yattn_gemv_q4k for o and down")
+                       + " per step (no graph), pinned x in, y back"}
     cpu = None
     if rank == 0 and not args.no_cpu_baseline:
         import numpy as np
@@ -1231,7 +1248,7 @@ def run_gemv(args, fmt: str = "q4k") -> None:
                       "weight_bytes_per_step": step_bytes, "parallelism": f"replicas x{world}",
                       "launch": "CUDA graph replay of the step",
                       "l2": f"weights per step {step_bytes / 1e9:.1f} GB > L2"},
-                     roof, args.steps * len(mats), clk, e2e, cpu=cpu, scaling="weak")
+                     roof, args.steps * len(calls), clk, e2e, cpu=cpu, scaling="weak")
         line["dtype"] = f"{name} weights, f32 x and accumulation"
         print(json.dumps(line), flush=True)
     if world > 1:

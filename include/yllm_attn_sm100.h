@@ -455,6 +455,15 @@ int yattn_gemv_q4k(float* y, const uint8_t* w, const float* x, uint32_t out, uin
                    void* stream, char* err, size_t errlen);
 int yattn_gemv_f16(float* y, const uint16_t* w, const float* x, uint32_t out, uint32_t in, uint32_t B,
                    void* stream, char* err, size_t errlen);
+/* One token through n (1..4) Q4_K matrices that read the same x, in one launch:
+ * y[i][0..out[i]) = W_i x for the engine's q, k, v (or gate, up) projections,
+ * which cuda_fwd.c:94-168 issues as separate cuda_k_gemv_q4k calls on the same
+ * normalised hidden state.  y, w and out are host arrays of n entries; every
+ * W_i is [out[i]][in], in % 256 == 0, 16-byte aligned, as is x.  Each y[i]
+ * equals yattn_gemv_q4k(y[i], w[i], x, out[i], in, 1) bit for bit.  Returns 0
+ * or -1 + err. */
+int yattn_gemv_q4k_multi(uint32_t n, float* const* y, const uint8_t* const* w, const uint32_t* out,
+                         const float* x, uint32_t in, void* stream, char* err, size_t errlen);
 
 /* Drop-ins with the reference's names and signatures (cuda_kernels.h; kernels
  * cuda_kernels.cu:36-249), legacy default stream.  The f16 pair accepts the

@@ -61,9 +61,8 @@ def q4k_dequant_f64(w, out, in_):
 
 
 @pytest.mark.parametrize("out,in_,B", [(4096, 4096, 1), (1000, 512, 3), (14336, 4096, 4), (96, 2048, 9),
-                                      # one token: the shared-memory-fed kernel (rows of 1-2 blocks leave some
-                                      # k-chunks empty; a ragged last 16-row tile), and rows too long for one
-                                      # CTA's shared memory (the register-fed fallback)
+                                      # one token: the tensor-core kernel at every k-slice count (rows of 56,
+                                      # 2 and 1 blocks), a ragged last 16-row tile, and a 72-block row
                                       (4096, 14336, 1), (1000, 512, 1), (37, 256, 1), (64, 18432, 1)])
 def test_gemv_q4k_matches_reference(dev, out, in_, B):
     from yllm_b200 import attn
@@ -122,3 +121,41 @@ def test_gemv_dropins_match(dev):
         assert getattr(lib, name_m)(*args_m, err, 256) == 0, err.value
         torch.cuda.synchronize()
         assert torch.equal(yb[0], y1[0]) and torch.equal(yc, ya), name_v
+
+
+@pytest.mark.parametrize("outs,in_", [((4096, 1024, 1024), 4096), ((14336, 14336), 4096), ((37, 1000, 16, 999), 512),
+                                      ((100,), 256), ((64, 48), 2048)])
+def test_gemv_q4k_multi_matches_single_and_reference(dev, outs, in_):
+    """One launch over matrices that share x (q/k/v, gate/up): every output equals the single-matrix call bit for
+    bit, and the oracle within the GEMV tolerance."""
+    from yllm_b200 import attn
+
+    rng = np.random.default_rng(sum(outs) + in_)
+    ws = [q4k_weights(rng, o, in_) for o in outs]
+    x = rng.standard_normal(in_).astype(np.float32)
+    tx = torch.from_numpy(x).to(dev)
+    tws = [torch.from_numpy(w).to(dev) for w in ws]
+    ys = [torch.full((o,), float("nan"), device=dev) for o in outs]
+    ones = [torch.zeros(o, device=dev) for o in outs]
+    attn.gemv_q4k_multi(ys, tws, outs, tx, in_)
+    for y1, tw, o in zip(ones, tws, outs):
+        attn.gemv_q4k(y1, tw, tx, o, in_, 1)
+    torch.cuda.synchronize()
+    for i, o in enumerate(outs):
+        assert torch.equal(ys[i], ones[i]), f"matrix {i} ({o} x {in_}) differs from the single call"
+        want = np.zeros(o, np.float32)
+        _ref_lib().orc_gemv_q4k(want, ws[i], x, o, in_, 1)
+        exact = q4k_dequant_f64(ws[i], o, in_) @ x.astype(np.float64)
+        oracle.assert_close(ys[i].cpu().numpy(), want, tol=TOL, what=f"q4k multi {i}: {o}x{in_}", exact=exact)
+
+
+def test_gemv_q4k_multi_rejects_bad_args(dev):
+    from yllm_b200 import attn
+
+    x = torch.zeros(256, device=dev)
+    w = torch.zeros(144 * 4, dtype=torch.uint8, device=dev)
+    y = torch.zeros(4, device=dev)
+    with pytest.raises(ValueError):
+        attn.gemv_q4k_multi([y] * 5, [w] * 5, [4] * 5, x, 256)   # more than four matrices
+    with pytest.raises(RuntimeError):
+        attn.gemv_q4k_multi([y], [w], [4], x, 100)               # in not a multiple of 256

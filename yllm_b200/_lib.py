@@ -139,6 +139,7 @@ PROTOS = {
     "yattn_sess_kv_save": (C.c_int, [vp, u32, u32, u32, u32, C.c_char_p, vp, *E]),
     "yattn_sess_kv_load": (C.c_int, [vp, u32, u32, u32, C.c_char_p, C.POINTER(u32), vp, *E]),
     "yattn_gemv_q4k": (C.c_int, [vp, vp, vp, u32, u32, u32, vp, *E]),
+    "yattn_gemv_q4k_multi": (C.c_int, [u32, vp, vp, vp, vp, u32, vp, *E]),
     "yattn_gemv_f16": (C.c_int, [vp, vp, vp, u32, u32, u32, vp, *E]),
     "cuda_k_gemv_q4k": (C.c_int, [vp, vp, vp, u32, u32, *E]),
     "cuda_k_gemm_q4k": (C.c_int, [vp, vp, vp, u32, u32, u32, *E]),

@@ -373,6 +373,24 @@ def gemv_q4k(y: torch.Tensor, w: torch.Tensor, x: torch.Tensor, out: int, in_: i
     call("yattn_gemv_q4k", y.data_ptr(), w.data_ptr(), x.data_ptr(), out, in_, B, _stream(stream))
 
 
+def gemv_q4k_multi(ys, ws, outs, x: torch.Tensor, in_: int, stream=None) -> None:
+    """One token through up to four Q4_K matrices that read the same x, in one launch: ys[i][:outs[i]] =
+    W_i . x, each bit-identical to gemv_q4k(ys[i], ws[i], x, outs[i], in_) (the engine's q/k/v or gate/up
+    calls of cuda_fwd.c:94-168 fused)."""
+    n = len(ws)
+    if not (1 <= n <= 4) or len(ys) != n or len(outs) != n:
+        raise ValueError("gemv_q4k_multi: 1 to 4 matrices, with as many outputs and row counts")
+    _need(x, torch.float32, "x")
+    for y, w, o in zip(ys, ws, outs):
+        _need(y, torch.float32, "y")
+        if w.dtype != torch.uint8 or not w.is_cuda or w.numel() < o * (in_ // 256) * 144:
+            raise ValueError("w must be a CUDA uint8 tensor of out * in/256 Q4_K blocks")
+    yp = (C.c_void_p * n)(*[y.data_ptr() for y in ys])
+    wp = (C.c_void_p * n)(*[w.data_ptr() for w in ws])
+    op = (C.c_uint32 * n)(*[int(o) for o in outs])
+    call("yattn_gemv_q4k_multi", n, yp, wp, op, x.data_ptr(), in_, _stream(stream))
+
+
 def gemv_f16(y: torch.Tensor, w: torch.Tensor, x: torch.Tensor, out: int, in_: int, B: int = 1,
              stream=None) -> None:
     """y[B][out] = fp16 W[out][in] . x[B][in] in fp32 (matvec.c:111-122 per token)."""

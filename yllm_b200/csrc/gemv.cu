@@ -208,16 +208,17 @@ __global__ void __launch_bounds__(kWarps * 32) k_gemv_q4k(float* __restrict__ y,
 // is the (2t, 2t+1) pair, shifted by 8 the (2t+8, 2t+9) pair; by 4 and 12 the high nibbles); B follows it.
 // Rows: warp w of the CTA takes MT 16-row tiles of row group w / KS and the blocks w % KS, + KS, ... of them,
 // U blocks per step with all their loads in flight; the k-slices meet in shared memory.
+// The CTA body: row tile cta of one matrix (the single-matrix kernel passes blockIdx.x).
 template <int MT, int KS, int U>
-__global__ void __launch_bounds__(kWarps * 32) k_gemv_q4k_tc(float* __restrict__ y, const uint8_t* __restrict__ w,
-                                                            const float* __restrict__ x, uint32_t out, uint32_t in) {
+__device__ __forceinline__ void gemv_q4k_tc_cta(float* __restrict__ y, const uint8_t* __restrict__ w,
+                                                const float* __restrict__ x, uint32_t out, uint32_t in, uint32_t cta) {
     constexpr int RG = kWarps / KS;                   // row groups per CTA
     constexpr int ROWS = 16 * MT;                     // rows per row group
     __shared__ float red[kWarps * ROWS];
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int g = lane >> 2, t = lane & 3;
     const int rg = warp / KS, ks = warp % KS;
-    const uint32_t row0 = (blockIdx.x * RG + rg) * ROWS;
+    const uint32_t row0 = (cta * RG + rg) * ROWS;
     const uint32_t nb = in / 256;
     const size_t row_bytes = static_cast<size_t>(nb) * kQ4kBlock;
     const uint8_t* rp[MT][2];                         // rows g and g + 8 of each tile (clamped: a padded tile
@@ -368,9 +369,36 @@ __global__ void __launch_bounds__(kWarps * 32) k_gemv_q4k_tc(float* __restrict__
         float v = 0.f;
 #pragma unroll
         for (int kk = 0; kk < KS; ++kk) v += red[(grp * KS + kk) * ROWS + rr];
-        const uint32_t row = (blockIdx.x * RG + grp) * ROWS + rr;
+        const uint32_t row = (cta * RG + grp) * ROWS + rr;
         if (row < out) y[row] = v;
     }
+}
+
+template <int MT, int KS, int U>
+__global__ void __launch_bounds__(kWarps * 32) k_gemv_q4k_tc(float* __restrict__ y, const uint8_t* __restrict__ w,
+                                                            const float* __restrict__ x, uint32_t out, uint32_t in) {
+    gemv_q4k_tc_cta<MT, KS, U>(y, w, x, out, in, blockIdx.x);
+}
+
+// Up to kMaxSegs matrices that read the same x (the engine's q/k/v, or gate/up) in one launch: CTAs
+// [cta0[s], cta0[s + 1]) take matrix s.
+constexpr int kMaxSegs = 4;
+struct Q4kSegs {
+    const uint8_t* w[kMaxSegs];
+    float* y[kMaxSegs];
+    uint32_t out[kMaxSegs];
+    uint32_t cta0[kMaxSegs + 1];
+    uint32_t n;
+};
+
+template <int MT, int KS, int U>
+__global__ void __launch_bounds__(kWarps * 32) k_gemv_q4k_tc_multi(const __grid_constant__ Q4kSegs sg,
+                                                                  const float* __restrict__ x, uint32_t in) {
+    uint32_t s = 0;
+#pragma unroll
+    for (int i = 1; i < kMaxSegs; ++i)
+        if (i < static_cast<int>(sg.n) && blockIdx.x >= sg.cta0[i]) s = i;
+    gemv_q4k_tc_cta<MT, KS, U>(sg.y[s], sg.w[s], x, sg.out[s], in, blockIdx.x - sg.cta0[s]);
 }
 
 // fp16 weights [out][in], in % 8 == 0 and 16-byte aligned rows and x.  One CTA per R rows; warp w takes
@@ -461,6 +489,13 @@ void launch_q4k_tc(float* y, const uint8_t* w, const float* x, uint32_t out, uin
     constexpr uint32_t rows_per_cta = (kWarps / KS) * 16 * MT;
     k_gemv_q4k_tc<MT, KS, 2><<<(out + rows_per_cta - 1) / rows_per_cta, kWarps * 32, 0, st>>>(y, w, x, out, in);
 }
+template <int MT, int KS>
+void launch_q4k_tc_multi(Q4kSegs sg, const float* x, uint32_t in, cudaStream_t st) {
+    constexpr uint32_t rows_per_cta = (kWarps / KS) * 16 * MT;
+    sg.cta0[0] = 0;
+    for (uint32_t i = 0; i < sg.n; ++i) sg.cta0[i + 1] = sg.cta0[i] + (sg.out[i] + rows_per_cta - 1) / rows_per_cta;
+    k_gemv_q4k_tc_multi<MT, KS, 2><<<sg.cta0[sg.n], kWarps * 32, 0, st>>>(sg, x, in);
+}
 template <int MT>
 void launch_q4k_tc_ks(float* y, const uint8_t* w, const float* x, uint32_t out, uint32_t in, cudaStream_t st) {
     const uint32_t nb = in / 256;   // k-slices so that every warp has a few blocks and the grid spreads
@@ -510,6 +545,41 @@ int gemv_q4k(float* y, const uint8_t* w, const float* x, uint32_t out, uint32_t 
     return 0;
 }
 
+int gemv_q4k_multi(uint32_t n, float* const* y, const uint8_t* const* w, const uint32_t* out, const float* x,
+                   uint32_t in, cudaStream_t st, char* err, size_t errlen) {
+    if (n == 0 || n > static_cast<uint32_t>(kMaxSegs) || !y || !w || !out || !x || in == 0 || (in % 256) != 0) {
+        set_err(err, errlen, "gemv_q4k_multi: bad args (n=%u, 1..%d matrices; in=%u, a multiple of 256)", n, kMaxSegs,
+                in);
+        return -1;
+    }
+    if (reinterpret_cast<uintptr_t>(x) & 15) {
+        set_err(err, errlen, "gemv_q4k_multi: x must be 16-byte aligned");
+        return -1;
+    }
+    Q4kSegs sg{};
+    sg.n = n;
+    for (uint32_t i = 0; i < n; ++i) {
+        if (!y[i] || !w[i] || out[i] == 0 || (reinterpret_cast<uintptr_t>(w[i]) & 15)) {
+            set_err(err, errlen, "gemv_q4k_multi: matrix %u: null pointer, out = 0 or w not 16-byte aligned", i);
+            return -1;
+        }
+        sg.w[i] = w[i];
+        sg.y[i] = y[i];
+        sg.out[i] = out[i];
+    }
+    const uint32_t nb = in / 256;   // the single-matrix kernel's k-slice choice
+    if (nb >= 16)
+        launch_q4k_tc_multi<1, 8>(sg, x, in, st);
+    else if (nb >= 8)
+        launch_q4k_tc_multi<1, 4>(sg, x, in, st);
+    else if (nb >= 2)
+        launch_q4k_tc_multi<1, 2>(sg, x, in, st);
+    else
+        launch_q4k_tc_multi<1, 1>(sg, x, in, st);
+    YATTN_CHECK_LAUNCH(err, errlen, "gemv_q4k_multi");
+    return 0;
+}
+
 int gemv_f16(float* y, const uint16_t* w, const float* x, uint32_t out, uint32_t in, uint32_t B, cudaStream_t st,
              char* err, size_t errlen, const char* who) {
     if (!y || !w || !x || out == 0 || in == 0 || B == 0) {
@@ -540,6 +610,11 @@ using namespace yattn;
 extern "C" int yattn_gemv_q4k(float* y, const uint8_t* w, const float* x, uint32_t out, uint32_t in, uint32_t B,
                               void* stream, char* err, size_t errlen) {
     return gemv_q4k(y, w, x, out, in, B, static_cast<cudaStream_t>(stream), err, errlen, "gemv_q4k");
+}
+
+extern "C" int yattn_gemv_q4k_multi(uint32_t n, float* const* y, const uint8_t* const* w, const uint32_t* out,
+                                    const float* x, uint32_t in, void* stream, char* err, size_t errlen) {
+    return gemv_q4k_multi(n, y, w, out, x, in, static_cast<cudaStream_t>(stream), err, errlen);
 }
 
 extern "C" int yattn_gemv_f16(float* y, const uint16_t* w, const float* x, uint32_t out, uint32_t in, uint32_t B,
