@@ -63,7 +63,9 @@ def q4k_dequant_f64(w, out, in_):
 @pytest.mark.parametrize("out,in_,B", [(4096, 4096, 1), (1000, 512, 3), (14336, 4096, 4), (96, 2048, 9),
                                       # one token: the tensor-core kernel at every k-slice count (rows of 56,
                                       # 2 and 1 blocks), a ragged last 16-row tile, and a 72-block row
-                                      (4096, 14336, 1), (1000, 512, 1), (37, 256, 1), (64, 18432, 1)])
+                                      (4096, 14336, 1), (1000, 512, 1), (37, 256, 1), (64, 18432, 1),
+                                      # tall matrices take 32-row tiles (ragged last tile in the second)
+                                      (14336, 4096, 1), (9500, 4096, 1)])
 def test_gemv_q4k_matches_reference(dev, out, in_, B):
     from yllm_b200 import attn
 

@@ -489,17 +489,30 @@ void launch_q4k_tc(float* y, const uint8_t* w, const float* x, uint32_t out, uin
     constexpr uint32_t rows_per_cta = (kWarps / KS) * 16 * MT;
     k_gemv_q4k_tc<MT, KS, 2><<<(out + rows_per_cta - 1) / rows_per_cta, kWarps * 32, 0, st>>>(y, w, x, out, in);
 }
-template <int MT, int KS>
+template <int MT, int KS, int U>
 void launch_q4k_tc_multi(Q4kSegs sg, const float* x, uint32_t in, cudaStream_t st) {
     constexpr uint32_t rows_per_cta = (kWarps / KS) * 16 * MT;
     sg.cta0[0] = 0;
     for (uint32_t i = 0; i < sg.n; ++i) sg.cta0[i + 1] = sg.cta0[i] + (sg.out[i] + rows_per_cta - 1) / rows_per_cta;
-    k_gemv_q4k_tc_multi<MT, KS, 2><<<sg.cta0[sg.n], kWarps * 32, 0, st>>>(sg, x, in);
+    k_gemv_q4k_tc_multi<MT, KS, U><<<sg.cta0[sg.n], kWarps * 32, 0, st>>>(sg, x, in);
+}
+// Two 16-row tiles per warp (x work shared by 32 rows, one block's loads in flight: 100 registers, two CTAs per
+// SM) when the grid still has two 32-row CTAs per SM; each row's sums are the same either way.
+bool q4k_tall(uint32_t rows, uint32_t nb) {
+    static int n_sm[64] = {};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return false;
+    if (n_sm[dev] == 0 && (cudaDeviceGetAttribute(&n_sm[dev], cudaDevAttrMultiProcessorCount, dev) != cudaSuccess ||
+                           n_sm[dev] <= 0))
+        n_sm[dev] = 1 << 20;   // unknown: never tall
+    return nb >= 16 && rows / 32 >= 2u * static_cast<uint32_t>(n_sm[dev]);
 }
 template <int MT>
 void launch_q4k_tc_ks(float* y, const uint8_t* w, const float* x, uint32_t out, uint32_t in, cudaStream_t st) {
     const uint32_t nb = in / 256;   // k-slices so that every warp has a few blocks and the grid spreads
-    if (nb >= 16)
+    if (MT == 1 && q4k_tall(out, nb))
+        k_gemv_q4k_tc<2, 8, 1><<<(out + 31) / 32, kWarps * 32, 0, st>>>(y, w, x, out, in);
+    else if (nb >= 16)
         launch_q4k_tc<MT, 8>(y, w, x, out, in, st);
     else if (nb >= 8)
         launch_q4k_tc<MT, 4>(y, w, x, out, in, st);
@@ -568,14 +581,18 @@ int gemv_q4k_multi(uint32_t n, float* const* y, const uint8_t* const* w, const u
         sg.out[i] = out[i];
     }
     const uint32_t nb = in / 256;   // the single-matrix kernel's k-slice choice
-    if (nb >= 16)
-        launch_q4k_tc_multi<1, 8>(sg, x, in, st);
+    uint32_t rows = 0;
+    for (uint32_t i = 0; i < n; ++i) rows += out[i];
+    if (q4k_tall(rows, nb))
+        launch_q4k_tc_multi<2, 8, 1>(sg, x, in, st);
+    else if (nb >= 16)
+        launch_q4k_tc_multi<1, 8, 2>(sg, x, in, st);
     else if (nb >= 8)
-        launch_q4k_tc_multi<1, 4>(sg, x, in, st);
+        launch_q4k_tc_multi<1, 4, 2>(sg, x, in, st);
     else if (nb >= 2)
-        launch_q4k_tc_multi<1, 2>(sg, x, in, st);
+        launch_q4k_tc_multi<1, 2, 2>(sg, x, in, st);
     else
-        launch_q4k_tc_multi<1, 1>(sg, x, in, st);
+        launch_q4k_tc_multi<1, 1, 2>(sg, x, in, st);
     YATTN_CHECK_LAUNCH(err, errlen, "gemv_q4k_multi");
     return 0;
 }
