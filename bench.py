@@ -50,7 +50,7 @@ def load_peaks() -> tuple[dict, str]:
 NCU_TRAFFIC = {"decode": 1225510144, "prefill": 25232128, "gated_prefill": 168607744, "gated_decode": 274070272,
                "long_decode": 541052160, "gdn_inputs": 225114112, "rope_store": 1590784,
                "gdn_decode": 78914048, "gdn_prefill_state": 257715456, "fused_decode": 1226680832,
-               "gemv_q4k_gate_up": 66100423}
+               "gemv_q4k_gate_up": 66095388}
 
 
 class ClockSampler:
@@ -1194,7 +1194,7 @@ def run_gemv(args, fmt: str = "q4k") -> None:
     roof = {"bound": "hbm", "achieved": round(ach, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
             "frac": round(ach / peaks["hbm_gbs"], 4),
             "traffic": None if (f16 or args.layers) else NCU_TRAFFIC["gemv_q4k_gate_up"],
-            "kernel": "k_gemv_f16<4,1,2>" if f16 else "k_gemv_q4k_tc(_multi)<1,KS,2> (mma.sync)",
+            "kernel": "k_gemv_f16<4,1,2>" if f16 else "k_gemv_q4k_tc(_multi)<MT,KS,U> (mma.sync)",
             "peak_source": src, "bytes_per_step": step_bytes,
             "note": (f"{len(calls)} launches per step in one graph; achieved = weight bytes / step device time"
                      + ("" if f16 else "; traffic: one gate + up launch (two 14336 x 4096), 66,060,288 B of weights"))}
